@@ -1,0 +1,126 @@
+/*
+ * CPU oracle for the VOLTA-ZK prover hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the shipped library links or calls
+ * this code; it is the checker that the CUDA backend is compared against in
+ * tests/, in __graft_entry__.smoke() and in the cpu_baseline leg of bench.py.
+ *
+ * Every function restates the reference's CPU semantics (okrame/volta-zk,
+ * Rust crates) and cites the file:line it follows.  Parity is pinned by the
+ * reference's own published golden vectors (tests/test_oracle_golden.py).
+ */
+#ifndef VOLTA_ORACLE_H
+#define VOLTA_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    uint64_t c0, c1;
+} ofp2;
+
+/* ---- Goldilocks / Fp2 (rust/volta-field/src/lib.rs:10-210) ---- */
+uint64_t or_fp_add(uint64_t a, uint64_t b);
+uint64_t or_fp_sub(uint64_t a, uint64_t b);
+uint64_t or_fp_mul(uint64_t a, uint64_t b);
+uint64_t or_fp_pow(uint64_t a, uint64_t e);
+uint64_t or_fp_inv(uint64_t a);
+ofp2 or_fp2_add(ofp2 a, ofp2 b);
+ofp2 or_fp2_sub(ofp2 a, ofp2 b);
+ofp2 or_fp2_mul(ofp2 a, ofp2 b);
+ofp2 or_fp2_inv(ofp2 a);
+void or_fp_mul_batch(const uint64_t* a, const uint64_t* b, uint64_t* out, size_t n);
+
+/* ---- FpStream = rand_chacha 0.3.1 ChaCha8Rng (rust/volta-field/src/lib.rs:222-268) ---- */
+typedef struct {
+    uint32_t key[8];
+    uint64_t stream;
+    uint64_t block;
+    uint32_t words[16];
+    uint32_t idx; /* next u64 index in words (0..8) */
+} or_stream;
+
+void or_stream_init(or_stream* s, const uint8_t seed[32], uint64_t domain);
+uint64_t or_stream_next_u64(or_stream* s);
+uint64_t or_stream_next_fp(or_stream* s);
+ofp2 or_stream_next_fp2(or_stream* s);
+uint64_t or_stream_next_bits(or_stream* s, unsigned width);
+/* rows x count Fp, row r from FpStream(seed, base+r) */
+void or_chacha_fp_rows(const uint8_t seed[32], uint64_t base, size_t rows, size_t count,
+                       uint64_t* out);
+/* rows x padded Fp2, first count from next_fp2, rest zero */
+void or_chacha_fp2_rows_padded(const uint8_t seed[32], uint64_t base, size_t rows,
+                               size_t count, size_t padded, ofp2* out);
+
+/* ---- sumcheck primitives ---- */
+void or_product_round(const ofp2* a, const ofp2* b, size_t pairs, ofp2 out[2]);
+void or_triple_product_round(const ofp2* a, const ofp2* b, const ofp2* c, size_t pairs,
+                             ofp2 out[3]);
+void or_logup_general_round(const ofp2* p0, const ofp2* p1, const ofp2* q0, const ofp2* q1,
+                            const ofp2* suffix, size_t pairs, ofp2 out[4]);
+void or_fold_rows(const ofp2* in, size_t rows, size_t len, ofp2 r, ofp2* out);
+void or_logup_tree(const uint64_t* leaf, const uint32_t* mult, size_t n, uint64_t alpha1,
+                   int neg_mult, ofp2* p, ofp2* q);
+void or_materialize_leaves(const uint64_t* leaf, const uint32_t* mult, size_t n,
+                           uint64_t alpha1, int neg_mult, ofp2* p, ofp2* q);
+void or_suffix_eq(const ofp2* point, size_t len, ofp2* out);
+void or_eq_rows(const ofp2* points, size_t rows, size_t dims, ofp2* out);
+void or_eq_vec(const ofp2* point, size_t len, ofp2* out);
+void or_aux_round(const ofp2* q0, const ofp2* q1, const ofp2* suffix, const ofp2* columns,
+                  const ofp2* eq_rows, const uint32_t* claim_cols, const ofp2* weights,
+                  size_t column_count, size_t claim_count, size_t vector_len, ofp2 lambda,
+                  ofp2 cpref, ofp2 point, ofp2 out[3]);
+void or_matrix_fold(const void* input, const ofp2* weights, size_t rows, size_t stride,
+                    size_t column_offset, size_t cols, size_t out_pad, int kind, int axis,
+                    ofp2* out);
+
+/* Full protocol drivers (clear sinks).  Messages are written flat. */
+/* Triple-product sumcheck (hadamard.rs:186-260, clear variant):
+ * rounds*3 messages, challenges from FpStream(chal_seed, u64::MAX).next_fp2()
+ * after each message; returns the three final openings in finals[3]. */
+void or_triple_sumcheck(ofp2* a, ofp2* b, ofp2* c, size_t n, const uint8_t chal_seed[32],
+                        ofp2* messages, ofp2* finals);
+/* logup_prove (logup.rs:1760-1771) over i16 queries/table; writes the
+ * proof in a flat layout: alpha, then per side root_p, root_q, then per layer
+ * [rounds x (h0,h2)], p0,p1,q0,q1.  Returns number of Fp2 written. */
+size_t or_logup_prove(const int16_t* f, size_t n_f, const int16_t* table, size_t n_t,
+                      const uint32_t* mult, const uint8_t chal_seed[32], uint64_t chal_domain,
+                      ofp2* out, size_t out_cap);
+
+/* ---- NTT (rust/volta-pcs/src/ntt.rs:9-70) ---- */
+void or_ntt_batch(const uint64_t* in, size_t rows, size_t msg_len, size_t n, uint64_t* out);
+void or_ntt_fp2_batch(const ofp2* in, size_t rows, size_t msg_len, size_t n, ofp2* out);
+
+/* ---- BLAKE3 (third-party blake3 1.8.5, restated from the published spec) ---- */
+void or_blake3(const uint8_t* data, size_t len, uint8_t out[32]);
+/* Column leaves (ligero.rs:351-359, 595-616) and merkle levels (merkle.rs:27-36) */
+void or_hash_fp_columns(const uint64_t* m, size_t rows, size_t cols, uint8_t* leaves);
+void or_hash_fp2_columns(const ofp2* m, size_t rows, size_t cols, uint8_t* leaves);
+void or_merkle_tree(const uint8_t* leaves, size_t n, uint8_t* tree); /* (2n-1)*32 bytes */
+void or_merkle_paths(const uint8_t* tree, size_t leaves, const uint32_t* idx, size_t q,
+                     uint8_t* paths);
+
+/* ---- PCS rows ---- */
+void or_pcs_messages(const int16_t* w, const uint64_t* pads, size_t rows, size_t cols,
+                     size_t pad, size_t code_len, uint64_t* out);
+void or_pcs_combine_rows(const int16_t* w, const uint64_t* pads, const ofp2* coeffs,
+                         size_t rows, size_t cols, size_t pad, size_t combos, ofp2* out);
+
+/* ---- GEMM + requant + MAC corrections (rust/volta-gpt2/src/gemm.rs:19-154) ---- */
+void or_gemm_i64(const int16_t* a, const int16_t* b, int64_t* out, size_t m, size_t k,
+                 size_t n);
+void or_gemm_requant_auth(const int16_t* a, const int16_t* b, const uint64_t* masks,
+                          int16_t* out, uint64_t* corr, size_t m, size_t k, size_t n,
+                          uint32_t shift);
+
+/* ---- FNV-1a style checksums used by the reference p7 recipes ---- */
+uint64_t or_fnv_u64(uint64_t h, const uint64_t* v, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

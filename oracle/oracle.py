@@ -1,0 +1,376 @@
+"""NumPy glue over the C oracle (``oracle/_build/liboracle.so``).
+
+TEST INFRASTRUCTURE ONLY: imported by ``tests/``, ``__graft_entry__.smoke()``
+and the ``cpu_baseline`` leg of ``bench.py`` as the checker.  The shipped
+library never imports it.
+
+Fp2 vectors are ``numpy.uint64`` arrays of shape ``(n, 2)`` (c0, c1), the
+same 16-byte ``Fp2Repr`` layout the reference seam uses
+(rust/volta-accel/src/lib.rs:394-399).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+P = 0xFFFFFFFF00000001
+
+_lib = None
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        _lib = C.CDLL(LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+class Fp2C(C.Structure):
+    _fields_ = [("c0", C.c_uint64), ("c1", C.c_uint64)]
+
+
+class Stream(C.Structure):
+    _fields_ = [
+        ("key", C.c_uint32 * 8),
+        ("stream", C.c_uint64),
+        ("block", C.c_uint64),
+        ("words", C.c_uint32 * 16),
+        ("idx", C.c_uint32),
+    ]
+
+
+_vp = C.c_void_p
+_sz = C.c_size_t
+_u64 = C.c_uint64
+
+
+def _declare(L):
+    L.or_fp_mul.restype = _u64
+    L.or_fp_mul.argtypes = [_u64, _u64]
+    L.or_fp_add.restype = _u64
+    L.or_fp_add.argtypes = [_u64, _u64]
+    L.or_fp_sub.restype = _u64
+    L.or_fp_sub.argtypes = [_u64, _u64]
+    L.or_fp_pow.restype = _u64
+    L.or_fp_pow.argtypes = [_u64, _u64]
+    L.or_fp_inv.restype = _u64
+    L.or_fp_inv.argtypes = [_u64]
+    L.or_fp2_mul.restype = Fp2C
+    L.or_fp2_mul.argtypes = [Fp2C, Fp2C]
+    L.or_fp2_inv.restype = Fp2C
+    L.or_fp2_inv.argtypes = [Fp2C]
+    L.or_fp_mul_batch.argtypes = [_vp, _vp, _vp, _sz]
+    L.or_stream_init.argtypes = [C.POINTER(Stream), C.c_char_p, _u64]
+    L.or_stream_next_u64.restype = _u64
+    L.or_stream_next_u64.argtypes = [C.POINTER(Stream)]
+    L.or_stream_next_fp.restype = _u64
+    L.or_stream_next_fp.argtypes = [C.POINTER(Stream)]
+    L.or_stream_next_fp2.restype = Fp2C
+    L.or_stream_next_fp2.argtypes = [C.POINTER(Stream)]
+    L.or_stream_next_bits.restype = _u64
+    L.or_stream_next_bits.argtypes = [C.POINTER(Stream), C.c_uint]
+    L.or_chacha_fp_rows.argtypes = [C.c_char_p, _u64, _sz, _sz, _vp]
+    L.or_chacha_fp2_rows_padded.argtypes = [C.c_char_p, _u64, _sz, _sz, _sz, _vp]
+    L.or_product_round.argtypes = [_vp, _vp, _sz, _vp]
+    L.or_triple_product_round.argtypes = [_vp, _vp, _vp, _sz, _vp]
+    L.or_logup_general_round.argtypes = [_vp, _vp, _vp, _vp, _vp, _sz, _vp]
+    L.or_fold_rows.argtypes = [_vp, _sz, _sz, Fp2C, _vp]
+    L.or_logup_tree.argtypes = [_vp, _vp, _sz, _u64, C.c_int, _vp, _vp]
+    L.or_materialize_leaves.argtypes = [_vp, _vp, _sz, _u64, C.c_int, _vp, _vp]
+    L.or_suffix_eq.argtypes = [_vp, _sz, _vp]
+    L.or_eq_rows.argtypes = [_vp, _sz, _sz, _vp]
+    L.or_eq_vec.argtypes = [_vp, _sz, _vp]
+    L.or_aux_round.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz,
+                               Fp2C, Fp2C, Fp2C, _vp]
+    L.or_matrix_fold.argtypes = [_vp, _vp, _sz, _sz, _sz, _sz, _sz, C.c_int, C.c_int, _vp]
+    L.or_triple_sumcheck.argtypes = [_vp, _vp, _vp, _sz, C.c_char_p, _vp, _vp]
+    L.or_logup_prove.restype = _sz
+    L.or_logup_prove.argtypes = [_vp, _sz, _vp, _sz, _vp, C.c_char_p, _u64, _vp, _sz]
+    L.or_ntt_batch.argtypes = [_vp, _sz, _sz, _sz, _vp]
+    L.or_ntt_fp2_batch.argtypes = [_vp, _sz, _sz, _sz, _vp]
+    L.or_blake3.argtypes = [_vp, _sz, _vp]
+    L.or_hash_fp_columns.argtypes = [_vp, _sz, _sz, _vp]
+    L.or_hash_fp2_columns.argtypes = [_vp, _sz, _sz, _vp]
+    L.or_merkle_tree.argtypes = [_vp, _sz, _vp]
+    L.or_merkle_paths.argtypes = [_vp, _sz, _vp, _sz, _vp]
+    L.or_pcs_messages.argtypes = [_vp, _vp, _sz, _sz, _sz, _sz, _vp]
+    L.or_pcs_combine_rows.argtypes = [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp]
+    L.or_gemm_i64.argtypes = [_vp, _vp, _vp, _sz, _sz, _sz]
+    L.or_gemm_requant_auth.argtypes = [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, C.c_uint32]
+    L.or_fnv_u64.restype = _u64
+    L.or_fnv_u64.argtypes = [_u64, _vp, _sz]
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data_as(_vp)
+
+
+def fp2(x) -> Fp2C:
+    return Fp2C(int(x[0]) % P, int(x[1]) % P)
+
+
+def fp2_tuple(v: Fp2C):
+    return (v.c0, v.c1)
+
+
+def fp2_array(n: int) -> np.ndarray:
+    return np.zeros((n, 2), dtype=np.uint64)
+
+
+# ---- field ----------------------------------------------------------------
+
+def fp_mul(a: int, b: int) -> int:
+    return lib().or_fp_mul(a, b)
+
+
+def fp2_mul(a, b):
+    return fp2_tuple(lib().or_fp2_mul(fp2(a), fp2(b)))
+
+
+def fp2_inv(a):
+    return fp2_tuple(lib().or_fp2_inv(fp2(a)))
+
+
+def fp_mul_batch(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.uint64)
+    b = np.ascontiguousarray(b, dtype=np.uint64)
+    out = np.empty_like(a)
+    lib().or_fp_mul_batch(_p(a), _p(b), _p(out), a.size)
+    return out
+
+
+# ---- FpStream ---------------------------------------------------------------
+
+class FpStream:
+    """rust/volta-field/src/lib.rs:222-268 (FpStream::domain_separated)."""
+
+    def __init__(self, seed: bytes, domain: int):
+        assert len(seed) == 32
+        self._s = Stream()
+        lib().or_stream_init(C.byref(self._s), seed, domain & 0xFFFFFFFFFFFFFFFF)
+
+    def next_u64(self) -> int:
+        return lib().or_stream_next_u64(C.byref(self._s))
+
+    def next_fp(self) -> int:
+        return lib().or_stream_next_fp(C.byref(self._s))
+
+    def next_fp2(self):
+        return fp2_tuple(lib().or_stream_next_fp2(C.byref(self._s)))
+
+    def next_bits(self, width: int) -> int:
+        return lib().or_stream_next_bits(C.byref(self._s), width)
+
+
+def chacha_fp_rows(seed: bytes, base: int, rows: int, count: int) -> np.ndarray:
+    out = np.zeros((rows, count), dtype=np.uint64)
+    lib().or_chacha_fp_rows(seed, base, rows, count, _p(out))
+    return out
+
+
+def chacha_fp2_rows_padded(seed: bytes, base: int, rows: int, count: int, padded: int):
+    out = np.zeros((rows * padded, 2), dtype=np.uint64)
+    lib().or_chacha_fp2_rows_padded(seed, base, rows, count, padded, _p(out))
+    return out
+
+
+# ---- sumcheck -----------------------------------------------------------------
+
+def product_round(a, b, pairs):
+    out = fp2_array(2)
+    lib().or_product_round(_p(a), _p(b), pairs, _p(out))
+    return out
+
+
+def triple_product_round(a, b, c, pairs):
+    out = fp2_array(3)
+    lib().or_triple_product_round(_p(a), _p(b), _p(c), pairs, _p(out))
+    return out
+
+
+def logup_general_round(p0, p1, q0, q1, suffix, pairs):
+    out = fp2_array(4)
+    lib().or_logup_general_round(_p(p0), _p(p1), _p(q0), _p(q1), _p(suffix), pairs, _p(out))
+    return out
+
+
+def fold_rows(x, rows, length, r):
+    out = fp2_array(rows * (length // 2))
+    lib().or_fold_rows(_p(x), rows, length, fp2(r), _p(out))
+    return out
+
+
+def logup_tree(leaf: np.ndarray, mult, n: int, alpha1: int, neg_mult: bool):
+    p = fp2_array(n - 1)
+    q = fp2_array(n - 1)
+    mp = _p(mult) if mult is not None else None
+    lib().or_logup_tree(_p(leaf), mp, n, alpha1, int(neg_mult), _p(p), _p(q))
+    return p, q
+
+
+def materialize_leaves(leaf, mult, n, alpha1, neg_mult):
+    p = fp2_array(n)
+    q = fp2_array(n)
+    mp = _p(mult) if mult is not None else None
+    lib().or_materialize_leaves(_p(leaf), mp, n, alpha1, int(neg_mult), _p(p), _p(q))
+    return p, q
+
+
+def suffix_eq(point: np.ndarray):
+    L = point.shape[0]
+    out = fp2_array((1 << L) - 1)
+    lib().or_suffix_eq(_p(point), L, _p(out))
+    return out
+
+
+def eq_rows(points: np.ndarray, rows: int, dims: int):
+    out = fp2_array(rows << dims)
+    lib().or_eq_rows(_p(points), rows, dims, _p(out))
+    return out
+
+
+def aux_round(q0, q1, suffix, columns, eq, claim_cols, weights, column_count, claim_count,
+              vector_len, lam, cpref, point):
+    out = fp2_array(3)
+    lib().or_aux_round(_p(q0), _p(q1), _p(suffix), _p(columns),
+                       _p(eq) if eq is not None else None,
+                       _p(claim_cols) if claim_cols is not None else None,
+                       _p(weights) if weights is not None else None,
+                       column_count, claim_count, vector_len,
+                       fp2(lam), fp2(cpref), fp2(point), _p(out))
+    return out
+
+
+def matrix_fold(inp, weights, rows, stride, column_offset, cols, out_pad, kind, axis):
+    out = fp2_array(out_pad)
+    lib().or_matrix_fold(_p(inp), _p(weights), rows, stride, column_offset, cols, out_pad,
+                         kind, axis, _p(out))
+    return out
+
+
+def triple_sumcheck(a, b, c, chal_seed: bytes):
+    a = a.copy(); b = b.copy(); c = c.copy()
+    n = a.shape[0]
+    rounds = n.bit_length() - 1
+    msgs = fp2_array(3 * rounds)
+    finals = fp2_array(3)
+    lib().or_triple_sumcheck(_p(a), _p(b), _p(c), n, chal_seed, _p(msgs), _p(finals))
+    return msgs, finals
+
+
+def logup_prove_words(n_f: int, n_t: int) -> int:
+    def side(n):
+        d = n.bit_length() - 1
+        return 2 + sum(2 * l + 4 for l in range(d))
+    return 1 + side(n_f) + side(n_t)
+
+
+def logup_prove(f: np.ndarray, table: np.ndarray, mult: np.ndarray, chal_seed: bytes,
+                chal_domain: int):
+    f = np.ascontiguousarray(f, dtype=np.int16)
+    table = np.ascontiguousarray(table, dtype=np.int16)
+    mult = np.ascontiguousarray(mult, dtype=np.uint32)
+    cap = logup_prove_words(f.size, table.size)
+    out = fp2_array(cap)
+    w = lib().or_logup_prove(_p(f), f.size, _p(table), table.size, _p(mult), chal_seed,
+                             chal_domain, _p(out), cap)
+    assert w == cap, (w, cap)
+    return out
+
+
+# ---- PCS ------------------------------------------------------------------------
+
+def ntt_batch(msgs: np.ndarray, rows: int, msg_len: int, n: int) -> np.ndarray:
+    msgs = np.ascontiguousarray(msgs, dtype=np.uint64)
+    out = np.zeros(rows * n, dtype=np.uint64)
+    lib().or_ntt_batch(_p(msgs), rows, msg_len, n, _p(out))
+    return out
+
+
+def ntt_fp2_batch(msgs: np.ndarray, rows: int, msg_len: int, n: int) -> np.ndarray:
+    msgs = np.ascontiguousarray(msgs, dtype=np.uint64)
+    out = fp2_array(rows * n)
+    lib().or_ntt_fp2_batch(_p(msgs), rows, msg_len, n, _p(out))
+    return out
+
+
+def blake3(data: bytes) -> bytes:
+    buf = np.frombuffer(data, dtype=np.uint8).copy() if data else np.zeros(1, np.uint8)
+    out = np.zeros(32, dtype=np.uint8)
+    lib().or_blake3(_p(buf), len(data), _p(out))
+    return out.tobytes()
+
+
+def hash_fp_columns(m: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    m = np.ascontiguousarray(m, dtype=np.uint64)
+    out = np.zeros((cols, 32), dtype=np.uint8)
+    lib().or_hash_fp_columns(_p(m), rows, cols, _p(out))
+    return out
+
+
+def hash_fp2_columns(m: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    m = np.ascontiguousarray(m, dtype=np.uint64)
+    out = np.zeros((cols, 32), dtype=np.uint8)
+    lib().or_hash_fp2_columns(_p(m), rows, cols, _p(out))
+    return out
+
+
+def merkle_tree(leaves: np.ndarray) -> np.ndarray:
+    n = leaves.shape[0]
+    tree = np.zeros((2 * n - 1, 32), dtype=np.uint8)
+    lib().or_merkle_tree(_p(np.ascontiguousarray(leaves)), n, _p(tree))
+    return tree
+
+
+def merkle_paths(tree: np.ndarray, leaves: int, idx: np.ndarray) -> np.ndarray:
+    bits = leaves.bit_length() - 1
+    idx = np.ascontiguousarray(idx, dtype=np.uint32)
+    out = np.zeros((idx.size * bits, 32), dtype=np.uint8)
+    lib().or_merkle_paths(_p(tree), leaves, _p(idx), idx.size, _p(out))
+    return out
+
+
+def pcs_messages(w, pads, rows, cols, pad, code_len):
+    out = np.zeros(rows * code_len, dtype=np.uint64)
+    lib().or_pcs_messages(_p(w), _p(pads) if pad else None, rows, cols, pad, code_len, _p(out))
+    return out
+
+
+def pcs_combine_rows(w, pads, coeffs, rows, cols, pad, combos):
+    out = fp2_array(combos * (cols + pad))
+    lib().or_pcs_combine_rows(_p(w), _p(pads) if pad else None, _p(coeffs), rows, cols, pad,
+                              combos, _p(out))
+    return out
+
+
+def gemm_i64(a, b, m, k, n):
+    out = np.zeros(m * n, dtype=np.int64)
+    lib().or_gemm_i64(_p(a), _p(b), _p(out), m, k, n)
+    return out
+
+
+def gemm_requant_auth(a, b, masks, m, k, n, shift):
+    out = np.zeros(m * n, dtype=np.int16)
+    corr = np.zeros(m * n, dtype=np.uint64)
+    lib().or_gemm_requant_auth(_p(a), _p(b), _p(masks), _p(out), _p(corr), m, k, n, shift)
+    return out, corr
+
+
+def fnv_u64(values: np.ndarray, h: int = 0xCBF29CE484222325) -> int:
+    v = np.ascontiguousarray(values, dtype=np.uint64).reshape(-1)
+    return lib().or_fnv_u64(h, _p(v), v.size)
