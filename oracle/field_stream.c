@@ -184,6 +184,12 @@ void or_chacha_fp2_rows_padded(const uint8_t seed[32], uint64_t base, size_t row
     }
 }
 
+void or_stream_fill_u64(const uint8_t seed[32], uint64_t domain, size_t n, uint64_t* out) {
+    or_stream st;
+    or_stream_init(&st, seed, domain);
+    for (size_t i = 0; i < n; ++i) out[i] = or_stream_next_u64(&st);
+}
+
 uint64_t or_fnv_u64(uint64_t h, const uint64_t* v, size_t n) {
     for (size_t i = 0; i < n; ++i) {
         h ^= v[i];

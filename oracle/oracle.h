@@ -49,6 +49,7 @@ uint64_t or_stream_next_u64(or_stream* s);
 uint64_t or_stream_next_fp(or_stream* s);
 ofp2 or_stream_next_fp2(or_stream* s);
 uint64_t or_stream_next_bits(or_stream* s, unsigned width);
+void or_stream_fill_u64(const uint8_t seed[32], uint64_t domain, size_t n, uint64_t* out);
 /* rows x count Fp, row r from FpStream(seed, base+r) */
 void or_chacha_fp_rows(const uint8_t seed[32], uint64_t base, size_t rows, size_t count,
                        uint64_t* out);

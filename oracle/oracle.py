@@ -83,6 +83,7 @@ def _declare(L):
     L.or_stream_next_fp2.argtypes = [C.POINTER(Stream)]
     L.or_stream_next_bits.restype = _u64
     L.or_stream_next_bits.argtypes = [C.POINTER(Stream), C.c_uint]
+    L.or_stream_fill_u64.argtypes = [C.c_char_p, _u64, _sz, _vp]
     L.or_chacha_fp_rows.argtypes = [C.c_char_p, _u64, _sz, _sz, _vp]
     L.or_chacha_fp2_rows_padded.argtypes = [C.c_char_p, _u64, _sz, _sz, _sz, _vp]
     L.or_product_round.argtypes = [_vp, _vp, _sz, _vp]
@@ -175,6 +176,12 @@ class FpStream:
 
     def next_bits(self, width: int) -> int:
         return lib().or_stream_next_bits(C.byref(self._s), width)
+
+
+def stream_u64(seed: bytes, domain: int, n: int) -> np.ndarray:
+    out = np.zeros(n, dtype=np.uint64)
+    lib().or_stream_fill_u64(seed, domain & 0xFFFFFFFFFFFFFFFF, n, _p(out))
+    return out
 
 
 def chacha_fp_rows(seed: bytes, base: int, rows: int, count: int) -> np.ndarray:

@@ -268,3 +268,22 @@ def test_fused_epilogue_golden(oracle, m, k, n, out_ck, corr_ck):
     out, corr = oracle.gemm_requant_auth(a, b, masks, m, k, n, 8)
     assert oracle.fnv_u64(out.view(np.uint16).astype(np.uint64)) == out_ck
     assert oracle.fnv_u64(corr) == corr_ck
+
+
+def test_oracle_matches_reference_chacha_header(oracle):
+    """Diff the oracle's FpStream against the reference's own host-compilable
+    header cuda/volta_chacha8_fp.cuh (built into oracle/_ref by oracle/Makefile
+    when the reference tree is present)."""
+    import ctypes as C
+    import os
+
+    path = os.path.join(os.path.dirname(oracle.LIB_PATH), "..", "_ref", "libref_chacha.so")
+    if not os.path.exists(path):
+        pytest.skip("reference cross-check library not built (reference tree absent)")
+    ref = C.CDLL(path)
+    ref.ref_chacha_fp_rows.argtypes = [C.c_char_p, C.c_uint64, C.c_size_t, C.c_size_t, C.c_void_p]
+    for seed, base, rows, count in [(bytes(range(32)), 0x0123456789ABCDEF, 3, 10),
+                                    (bytes([0xA5] * 32), 2**64 - 5, 4, 1000)]:
+        out = np.zeros(rows * count, dtype=np.uint64)
+        ref.ref_chacha_fp_rows(seed, base, rows, count, out.ctypes.data_as(C.c_void_p))
+        assert np.array_equal(out.reshape(rows, count), oracle.chacha_fp_rows(seed, base, rows, count))

@@ -1,0 +1,311 @@
+"""ctypes bindings of the C ABI and of the host mirror.
+
+``CudaBackend`` exposes every ``volta_cuda_*`` entry point of
+``libvolta_cuda_backend.so`` with argument types parsed from
+``include/volta_cuda_backend.h`` (the declarations the reference's Rust FFI
+binds, rust/volta-accel/src/cuda.rs:121-974), and checks return codes the way
+the seam does (``AccelError`` carrying ``volta_cuda_last_error``).
+
+``Prover`` drives the resident protocol callers implemented in
+``libvolta_accel.so`` (triple-product sumcheck, LogUp prove).
+
+Nothing here falls back to the CPU: a missing library, a missing symbol, an
+ABI mismatch or a host without a CUDA device raises ``AccelError``.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+from typing import Dict
+
+import numpy as np
+
+from .build import HERE, library_path
+
+ROOT = os.path.dirname(HERE)
+HEADER = os.path.join(ROOT, "include", "volta_cuda_backend.h")
+ABI_VERSION = 37
+P = 0xFFFFFFFF00000001
+
+
+class AccelError(RuntimeError):
+    pass
+
+
+class Fp2(C.Structure):
+    """Fp2Repr {c0, c1} (rust/volta-accel/src/lib.rs:394-399)."""
+
+    _fields_ = [("c0", C.c_uint64), ("c1", C.c_uint64)]
+
+    def tuple(self):
+        return (self.c0, self.c1)
+
+
+def fp2(v) -> Fp2:
+    return Fp2(int(v[0]), int(v[1]))
+
+
+class RawStats(C.Structure):
+    _fields_ = (
+        [("calls", C.c_uint64 * 7), ("kernel_ns", C.c_uint64 * 7)]
+        + [(n, C.c_uint64) for n in (
+            "h2d_bytes d2h_bytes d2d_bytes device_zeroed_bytes device_generated_bytes h2d_ns d2h_ns "
+            "resident_h2d_host_calls resident_d2h_host_calls resident_h2d_host_call_ns "
+            "resident_d2h_host_call_ns synchronizations synchronization_ns sync_host_output "
+            "sync_upload_lifetime sync_timing_flush sync_profiling_legacy sync_allocator_flush "
+            "allocation_calls resident_alloc_requests resident_reuse_hits resident_free_requests "
+            "physical_free_calls live_device_bytes peak_device_bytes pinned_allocation_calls "
+            "pinned_alloc_requests pinned_reuse_hits pinned_free_requests pinned_physical_free_calls "
+            "pinned_host_write_calls pinned_host_write_bytes live_pinned_bytes peak_pinned_bytes "
+            "x4c_arena_reset_calls x4c_arena_reset_bytes x4c_kernel_launches x4c_control_peek_calls "
+            "x4c_control_peek_pending timing_records timing_elapsed_query_attempts "
+            "timing_elapsed_no_write timing_event_queries timing_event_api_calls "
+            "timing_pending_high_water timing_flush_count coarse_timing_scopes coarse_timing_ns"
+        ).split()]
+        + [("timing_mode", C.c_uint32), ("reserved", C.c_uint32)]
+    )
+
+
+assert C.sizeof(RawStats) == 504
+
+_CTYPES = {
+    "void*": C.c_void_p, "void**": C.POINTER(C.c_void_p), "const void*": C.c_void_p,
+    "uint64_t": C.c_uint64, "size_t": C.c_size_t, "int": C.c_int, "uint32_t": C.c_uint32,
+    "int32_t": C.c_int32, "uint8_t": C.c_uint8, "const uint8_t*": C.c_void_p, "uint8_t*": C.c_void_p,
+    "const int16_t*": C.c_void_p, "int16_t*": C.c_void_p, "const uint64_t*": C.c_void_p,
+    "uint64_t*": C.c_void_p, "int64_t*": C.c_void_p, "const uint32_t*": C.c_void_p,
+    "const uint16_t*": C.c_void_p, "size_t*": C.c_void_p, "int*": C.c_void_p,
+    "vz_fp2": Fp2, "vz_fp2*": C.c_void_p, "const vz_fp2*": C.c_void_p,
+    "vz_raw_stats*": C.c_void_p, "vz_raw_pinned_stats*": C.c_void_p,
+    "vz_raw_control_state*": C.c_void_p, "const vz_attention_wires_args*": C.c_void_p,
+}
+_RESTYPES = {"int": C.c_int, "uint32_t": C.c_uint32, "void": None, "const char*": C.c_char_p}
+
+
+def parse_header(path: str = HEADER) -> Dict[str, tuple]:
+    """name -> (restype, [argtypes]) for every declaration in the header."""
+    text = re.sub(r"/\*.*?\*/", "", open(path).read(), flags=re.S)
+    out = {}
+    for ret, name, args in re.findall(
+            r"\b(int|uint32_t|void|const char\*) (volta_cuda_\w+)\(([^;]*?)\);", text, re.S):
+        types = []
+        args = " ".join(args.split())
+        if args and args != "void":
+            for a in args.split(","):
+                a = a.strip()
+                m = re.match(r"(.*?)(\w+)$", a)
+                t = m.group(1).replace(" *", "*").strip()
+                types.append(_CTYPES[t])
+        out[name] = (_RESTYPES[ret], types)
+    return out
+
+
+_cuda_lib = None
+_host_lib = None
+
+
+def load_cuda_library(path: str | None = None):
+    """dlopen + ABI check + eager symbol resolution (cuda.rs:1119-1170)."""
+    global _cuda_lib
+    if _cuda_lib is not None and path is None:
+        return _cuda_lib
+    path = path or os.environ.get("VOLTA_CUDA_LIBRARY") or library_path()
+    if not os.path.exists(path):
+        raise AccelError(f"LibraryLoad: {path} not found (build with volta_zk_b200.build_all())")
+    lib = C.CDLL(path, mode=os.RTLD_NOW | os.RTLD_LOCAL)
+    for name, (res, args) in parse_header().items():
+        try:
+            fn = getattr(lib, name)
+        except AttributeError as e:
+            raise AccelError(f"MissingSymbol: {name}") from e
+        fn.restype = res
+        fn.argtypes = args
+    # measurement extensions (include/volta_b200_ext.h)
+    lib.volta_b200_timing_mark.argtypes = [C.c_void_p, C.c_int]
+    lib.volta_b200_timing_elapsed.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_float)]
+    lib.volta_b200_launch_count.argtypes = [C.c_void_p, C.POINTER(C.c_uint64)]
+    if lib.volta_cuda_abi_version() != ABI_VERSION:
+        raise AccelError(f"AbiMismatch: expected {ABI_VERSION}, found {lib.volta_cuda_abi_version()}")
+    _cuda_lib = lib
+    return lib
+
+
+def load_host_library():
+    global _host_lib
+    if _host_lib is None:
+        path = library_path("libvolta_accel.so")
+        if not os.path.exists(path):
+            raise AccelError(f"LibraryLoad: {path} not found (build with volta_zk_b200.build_all())")
+        L = C.CDLL(path)
+        vp, sz, u64 = C.c_void_p, C.c_size_t, C.c_uint64
+        L.vzh_open.restype = vp
+        L.vzh_open.argtypes = [C.c_char_p, C.c_int, C.c_char_p, sz]
+        L.vzh_close.argtypes = [vp]
+        L.vzh_context.restype = vp
+        L.vzh_context.argtypes = [vp]
+        L.vzh_stats.argtypes = [vp, vp, C.c_char_p, sz]
+        L.vzh_reset_stats.argtypes = [vp, C.c_char_p, sz]
+        L.vzh_triple_sumcheck.argtypes = [vp, u64, u64, u64, sz, C.c_char_p, vp, vp, C.c_char_p, sz]
+        L.vzh_logup_prove.argtypes = [vp, u64, sz, u64, sz, u64, C.c_char_p, u64, vp, sz,
+                                      C.POINTER(C.c_size_t), C.c_char_p, sz]
+        L.vzh_fpstream_u64.argtypes = [C.c_char_p, u64, sz, vp]
+        _host_lib = L
+    return _host_lib
+
+
+def _ptr(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class CudaBackend:
+    """One resident context of libvolta_cuda_backend.so (policy 0 deferred
+    events, 1 wall-only counters; None keeps the synchronous event mode)."""
+
+    def __init__(self, policy: int | None = 0, ctx=None, lib=None):
+        self.lib = lib or load_cuda_library()
+        self._owned = ctx is None
+        if ctx is None:
+            raw = C.c_void_p()
+            rc = self.lib.volta_cuda_create(C.byref(raw))
+            if rc != 0:
+                msg = self.lib.volta_cuda_last_error(raw).decode() if raw.value else "create failed"
+                if raw.value:
+                    self.lib.volta_cuda_destroy(raw)
+                raise AccelError(f"Cuda: {msg}")
+            self.ctx = raw
+            if policy is not None:
+                self.check(self.lib.volta_cuda_set_resident_timing_policy(self.ctx, policy),
+                           "set_resident_timing_policy")
+        else:
+            self.ctx = C.c_void_p(ctx)
+
+    def close(self):
+        if self._owned and self.ctx:
+            self.lib.volta_cuda_destroy(self.ctx)
+            self.ctx = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def last_error(self) -> str:
+        return self.lib.volta_cuda_last_error(self.ctx).decode()
+
+    def check(self, rc: int, what: str):
+        if rc != 0:
+            raise AccelError(f"Cuda: {what}: {self.last_error()} (rc={rc})")
+
+    def call(self, name: str, *args):
+        fn = getattr(self.lib, "volta_cuda_" + name)
+        self.check(fn(self.ctx, *args), name)
+
+    # ---- arena -----------------------------------------------------------------
+    def alloc(self, nbytes: int) -> int:
+        out = C.c_uint64()
+        self.check(self.lib.volta_cuda_resident_alloc(self.ctx, max(int(nbytes), 16), C.byref(out)),
+                   "resident_alloc")
+        return out.value
+
+    def free(self, buf: int):
+        self.check(self.lib.volta_cuda_resident_free(self.ctx, buf), "resident_free")
+
+    def upload(self, buf: int, array: np.ndarray, offset_bytes: int = 0):
+        a = np.ascontiguousarray(array)
+        self.check(self.lib.volta_cuda_resident_upload(self.ctx, buf, offset_bytes, _ptr(a), a.nbytes),
+                   "resident_upload")
+
+    def download(self, buf: int, nbytes: int, dtype=np.uint64, offset_bytes: int = 0) -> np.ndarray:
+        out = np.zeros(nbytes // np.dtype(dtype).itemsize, dtype=dtype)
+        self.check(self.lib.volta_cuda_resident_download(self.ctx, buf, offset_bytes, _ptr(out), nbytes),
+                   "resident_download")
+        return out
+
+    def upload_new(self, array: np.ndarray) -> int:
+        a = np.ascontiguousarray(array)
+        buf = self.alloc(a.nbytes)
+        self.upload(buf, a)
+        return buf
+
+    def download_fp2(self, buf: int, n: int, offset: int = 0) -> np.ndarray:
+        return self.download(buf, 16 * n, offset_bytes=16 * offset).reshape(n, 2)
+
+    def stats(self) -> RawStats:
+        s = RawStats()
+        self.check(self.lib.volta_cuda_get_stats(self.ctx, C.byref(s)), "get_stats")
+        return s
+
+    # ---- measurement extensions ---------------------------------------------
+    def mark(self, slot: int):
+        self.check(self.lib.volta_b200_timing_mark(self.ctx, slot), "timing_mark")
+
+    def elapsed_ms(self, start: int, end: int) -> float:
+        ms = C.c_float()
+        self.check(self.lib.volta_b200_timing_elapsed(self.ctx, start, end, C.byref(ms)), "timing_elapsed")
+        return ms.value
+
+    def launches(self) -> int:
+        n = C.c_uint64()
+        self.check(self.lib.volta_b200_launch_count(self.ctx, C.byref(n)), "launch_count")
+        return n.value
+
+
+def fpstream_u64(seed: bytes, domain: int, n: int) -> np.ndarray:
+    """Raw u64 draws of FpStream(seed, domain) (rust/volta-field/src/lib.rs:231-267)."""
+    out = np.zeros(n, dtype=np.uint64)
+    load_host_library().vzh_fpstream_u64(seed, domain & (2**64 - 1), n, _ptr(out))
+    return out
+
+
+class Prover:
+    """Resident protocol drivers of libvolta_accel.so on their own context."""
+
+    def __init__(self, policy: int = 1):
+        self.host = load_host_library()
+        load_cuda_library()  # same dlopen handle as the host library's
+        err = C.create_string_buffer(1024)
+        self.h = self.host.vzh_open(library_path().encode(), policy, err, 1024)
+        if not self.h:
+            raise AccelError(err.value.decode())
+        self.backend = CudaBackend(ctx=self.host.vzh_context(self.h))
+
+    def close(self):
+        if self.h:
+            self.host.vzh_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _err(self, rc, err):
+        if rc != 0:
+            raise AccelError(err.value.decode())
+
+    def triple_sumcheck(self, a: int, b: int, c: int, n: int, seed: bytes):
+        rounds = n.bit_length() - 1
+        msgs = np.zeros((3 * rounds, 2), dtype=np.uint64)
+        finals = np.zeros((3, 2), dtype=np.uint64)
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_triple_sumcheck(self.h, a, b, c, n, seed, _ptr(msgs), _ptr(finals), err, 1024)
+        self._err(rc, err)
+        return msgs, finals
+
+    def logup_prove(self, f_col: int, n_f: int, t_col: int, n_t: int, mult: int, seed: bytes,
+                    domain: int, cap: int):
+        out = np.zeros((cap, 2), dtype=np.uint64)
+        written = C.c_size_t()
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_logup_prove(self.h, f_col, n_f, t_col, n_t, mult, seed, domain, _ptr(out), cap,
+                                       C.byref(written), err, 1024)
+        self._err(rc, err)
+        return out[: written.value]
+
+    def stats(self) -> RawStats:
+        return self.backend.stats()

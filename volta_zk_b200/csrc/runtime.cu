@@ -1,0 +1,1290 @@
+// Context, arena, pinned pool, measurement observer and their C ABI.
+//
+// Reference semantics (okrame/volta-zk cuda/volta_cuda_backend.cu):
+//   ids / arena / regions       182-330, 3733-3960
+//   errors                      355-403
+//   timing modes and stats      42-124, 1035-1270, 3213-3420
+//   pinned pool                 194-203, 3570-3730
+#include "runtime.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <new>
+
+namespace vzb {
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+
+static void drop_active_record(Context* c) noexcept {
+    if (!c) return;
+    if (c->coarse_work) c->poisoned = true;
+    if (c->active_record != kRingSize) {
+        c->ring[c->active_record].mask = 0;
+        c->ring[c->active_record].committed = false;
+    }
+    c->active_record = kRingSize;
+    c->coarse = false;
+    c->coarse_inner = false;
+    c->counter_active = false;
+    c->coarse_work = false;
+    c->coarse_op = -1;
+}
+
+int fail_message(Context* c, const char* message) noexcept {
+    drop_active_record(c);
+    if (c) {
+        try {
+            c->error = message;
+        } catch (...) {
+        }
+    }
+    return -1;
+}
+
+int fail_cuda(Context* c, const char* what, cudaError_t e) noexcept {
+    drop_active_record(c);
+    if (c) {
+        try {
+            c->error = std::string(what) + ": " + cudaGetErrorString(e);
+        } catch (...) {
+        }
+    }
+    return e == cudaSuccess ? -1 : static_cast<int>(e);
+}
+
+int reject(Context* c, const char* message) noexcept {
+    if (c) {
+        try {
+            c->error = message;
+        } catch (...) {
+        }
+    }
+    return -1;
+}
+
+// ---------------------------------------------------------------------------
+// arena
+// ---------------------------------------------------------------------------
+
+static uint64_t make_id(size_t slot, uint32_t gen) {
+    return (static_cast<uint64_t>(gen) << 32) | static_cast<uint64_t>(slot + 1);
+}
+
+Slot* find_slot(Context* c, uint64_t id) {
+    if (!c || !id) return nullptr;
+    const uint64_t enc = id & kSlotMask;
+    const uint32_t gen = static_cast<uint32_t>(id >> 32);
+    if (!enc || !gen) return nullptr;
+    const size_t slot = static_cast<size_t>(enc - 1);
+    if (slot >= c->slots.size()) return nullptr;
+    Slot& s = c->slots[slot];
+    return (s.active && s.generation == gen) ? &s : nullptr;
+}
+
+int region(Context* c, uint64_t id, size_t offset, size_t bytes, void** out) {
+    Slot* s = find_slot(c, id);
+    if (!s) return fail_message(c, "unknown resident buffer id");
+    if (offset > s->logical || bytes > s->logical - offset)
+        return fail_message(c, "resident buffer region is out of bounds");
+    *out = static_cast<unsigned char*>(s->ptr) + offset;
+    return 0;
+}
+
+int region_elems(Context* c, uint64_t id, size_t offset, size_t count, size_t elem, void** out) {
+    size_t ob = 0, nb = 0;
+    if (!mul_ok(offset, elem, &ob) || !mul_ok(count, elem, &nb))
+        return fail_message(c, "resident geometry overflows size_t");
+    return region(c, id, ob, nb, out);
+}
+
+int strided_region(Context* c, uint64_t id, size_t offset, size_t stride, size_t row_bytes,
+                   size_t rows, void** out, size_t* span) {
+    if (!rows || !row_bytes || stride < row_bytes)
+        return fail_message(c, "invalid resident strided-row geometry");
+    size_t prefix = 0;
+    if (!mul_ok(rows - 1, stride, &prefix) || !add_ok(prefix, row_bytes, span))
+        return fail_message(c, "resident strided-row geometry overflows size_t");
+    return region(c, id, offset, *span, out);
+}
+
+int sync_stream_raw(Context* c) {
+    const auto t0 = std::chrono::steady_clock::now();
+    const cudaError_t e = cudaStreamSynchronize(c->stream);
+    const auto t1 = std::chrono::steady_clock::now();
+    if (e != cudaSuccess) return fail_cuda(c, "cudaStreamSynchronize", e);
+    c->counter_pending = false;
+    c->outstanding = 0;
+    ++c->stats.synchronizations;
+    c->stats.synchronization_ns +=
+        std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count();
+    return 0;
+}
+
+static uint64_t& sync_counter(RawStats& s, Sync r) {
+    switch (r) {
+        case Sync::HostOutput: return s.sync_host_output;
+        case Sync::UploadLifetime: return s.sync_upload_lifetime;
+        case Sync::TimingFlush: return s.sync_timing_flush;
+        case Sync::AllocatorFlush: return s.sync_allocator_flush;
+        case Sync::ProfilingLegacy: break;
+    }
+    return s.sync_profiling_legacy;
+}
+
+int sync_stream(Context* c, Sync reason) {
+    if (sync_stream_raw(c)) return -1;
+    ++sync_counter(c->stats, reason);
+    return 0;
+}
+
+static int flush_ring(Context* c, Sync reason);
+
+static int sync_for_reclaim(Context* c) {
+    if (c->mode == kTimingDeferred && c->ring_pending) return flush_ring(c, Sync::AllocatorFlush);
+    return sync_stream(c, Sync::AllocatorFlush);
+}
+
+int ensure_ws(Context* c, int slot, size_t bytes) {
+    if (slot < 0 || slot >= kWsCount) return fail_message(c, "invalid workspace slot");
+    Workspace& w = c->ws[slot];
+    if (w.capacity >= bytes) return 0;
+    if (c->coarse) {
+        const std::string m = "workspace slot " + std::to_string(slot) + " growth from " +
+                              std::to_string(w.capacity) + " to " + std::to_string(bytes) +
+                              " bytes is forbidden inside a coarse timing scope";
+        return reject(c, m.c_str());
+    }
+    // grow geometrically so repeated shapes settle quickly
+    size_t want = std::max(bytes, w.capacity + w.capacity / 2);
+    want = (want + 255) & ~size_t{255};
+    if (w.ptr) {
+        if (sync_for_reclaim(c)) return -1;
+        VZB_CUDA(c, cudaFree(w.ptr));
+        ++c->stats.physical_free_calls;
+        c->stats.live_device_bytes -= w.capacity;
+        w = Workspace{};
+    }
+    VZB_CUDA(c, cudaMalloc(&w.ptr, want));
+    w.capacity = want;
+    ++c->stats.allocation_calls;
+    c->stats.live_device_bytes += want;
+    c->stats.peak_device_bytes = std::max(c->stats.peak_device_bytes, c->stats.live_device_bytes);
+    if (slot == kWsCounter) VZB_CUDA(c, cudaMemsetAsync(w.ptr, 0, want, c->stream));
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+// measurement observer
+// ---------------------------------------------------------------------------
+
+static cudaError_t ev_record(Context* c, cudaEvent_t e) {
+    ++c->stats.timing_event_api_calls;
+    return cudaEventRecord(e, c->stream);
+}
+
+static int elapsed_once(Context* c, cudaEvent_t a, cudaEvent_t b, uint64_t* out, bool* ok) {
+    ++c->stats.timing_elapsed_query_attempts;
+    if (c->inject_no_write) {
+        --c->inject_no_write;
+        ++c->stats.timing_elapsed_no_write;
+        *ok = false;
+        return 0;
+    }
+    float ms = -1.0f;
+    ++c->stats.timing_event_api_calls;
+    const cudaError_t e = cudaEventElapsedTime(&ms, a, b);
+    if (e != cudaSuccess) return fail_cuda(c, "cudaEventElapsedTime", e);
+    if (std::isfinite(ms) && ms >= 0.0f) {
+        *out = static_cast<uint64_t>(ms * 1.0e6f);
+        ++c->stats.timing_event_queries;
+        *ok = true;
+    } else {
+        ++c->stats.timing_elapsed_no_write;
+        *ok = false;
+    }
+    return 0;
+}
+
+static int elapsed(Context* c, cudaEvent_t a, cudaEvent_t b, uint64_t* out) {
+    for (int i = 0; i < 4; ++i) {
+        bool ok = false;
+        if (elapsed_once(c, a, b, out, &ok)) return -1;
+        if (ok) return 0;
+    }
+    return fail_message(c, "cudaEventElapsedTime returned success without a duration after bounded retries");
+}
+
+static uint8_t full_mask(RecordKind k) { return k == RecordKind::Primitive ? 0x0f : 0x03; }
+
+static int flush_ring(Context* c, Sync reason) {
+    if (c->mode != kTimingDeferred || !c->ring_pending) return 0;
+    if (sync_stream(c, reason)) return -1;
+    ++c->stats.timing_flush_count;
+    for (size_t k = 0; k < c->ring_pending; ++k) {
+        Record& r = c->ring[(c->ring_head + k) % kRingSize];
+        if (!r.committed || r.mask != full_mask(r.kind))
+            return fail_message(c, "invalid deferred timing record");
+        if (r.kind == RecordKind::Primitive) {
+            if (r.h2d && elapsed(c, r.ev[0], r.ev[1], &r.ns[0])) return -1;
+            if (elapsed(c, r.ev[1], r.ev[2], &r.ns[1])) return -1;
+            if (r.d2h && elapsed(c, r.ev[2], r.ev[3], &r.ns[2])) return -1;
+        } else if (r.kind == RecordKind::Coarse) {
+            if (elapsed(c, r.ev[0], r.ev[1], &r.ns[1])) return -1;
+        } else {
+            if (elapsed(c, r.ev[0], r.ev[1], &r.ns[0])) return -1;
+        }
+    }
+    for (size_t k = 0; k < c->ring_pending; ++k) {
+        Record& r = c->ring[(c->ring_head + k) % kRingSize];
+        RawStats& s = c->stats;
+        if (r.kind == RecordKind::Primitive) {
+            ++s.calls[r.op];
+            s.h2d_bytes += r.h2d;
+            s.d2h_bytes += r.d2h;
+            s.d2d_bytes += r.d2d;
+            s.device_zeroed_bytes += r.zeroed;
+            s.device_generated_bytes += r.generated;
+            if (r.h2d) s.h2d_ns += r.ns[0];
+            s.kernel_ns[r.op] += r.ns[1];
+            if (r.d2h) s.d2h_ns += r.ns[2];
+        } else if (r.kind == RecordKind::Coarse) {
+            s.kernel_ns[r.op] += r.ns[1];
+            s.coarse_timing_ns += r.ns[1];
+        } else if (r.kind == RecordKind::Upload) {
+            s.h2d_bytes += r.h2d;
+            s.h2d_ns += r.ns[0];
+        } else {
+            s.d2h_bytes += r.d2h;
+            s.d2h_ns += r.ns[0];
+        }
+        r.committed = false;
+        r.mask = 0;
+    }
+    c->ring_head = (c->ring_head + c->ring_pending) % kRingSize;
+    c->ring_pending = 0;
+    return 0;
+}
+
+static int discard_ring(Context* c, Sync reason) {
+    if (c->mode != kTimingDeferred || !c->ring_pending) return 0;
+    if (sync_stream(c, reason)) return -1;
+    for (size_t k = 0; k < c->ring_pending; ++k) {
+        Record& r = c->ring[(c->ring_head + k) % kRingSize];
+        r.committed = false;
+        r.mask = 0;
+    }
+    c->ring_head = (c->ring_head + c->ring_pending) % kRingSize;
+    c->ring_pending = 0;
+    return 0;
+}
+
+static int ring_open(Context* c, RecordKind kind, int events) {
+    if (c->active_record != kRingSize) return fail_message(c, "nested deferred timing record");
+    if (c->ring_pending == kRingSize && flush_ring(c, Sync::TimingFlush)) return -1;
+    const size_t slot = (c->ring_head + c->ring_pending) % kRingSize;
+    Record& r = c->ring[slot];
+    if (r.committed) return fail_message(c, "deferred timing ring would overwrite a committed record");
+    for (int i = 0; i < events; ++i) {
+        if (!r.ev[i]) {
+            ++c->stats.timing_event_api_calls;
+            VZB_CUDA(c, cudaEventCreate(&r.ev[i]));
+        }
+    }
+    r.kind = kind;
+    r.op = -1;
+    r.mask = 0;
+    r.h2d = r.d2h = r.d2d = r.zeroed = r.generated = 0;
+    r.ns[0] = r.ns[1] = r.ns[2] = 0;
+    VZB_CUDA(c, ev_record(c, r.ev[0]));
+    r.mask |= 1;
+    c->active_record = slot;
+    return 0;
+}
+
+static int ring_commit(Context* c) {
+    if (c->active_record == kRingSize) return fail_message(c, "no active deferred timing record");
+    Record& r = c->ring[c->active_record];
+    if (r.committed || r.mask != full_mask(r.kind))
+        return fail_message(c, "deferred timing commit has incomplete event markers");
+    r.committed = true;
+    c->active_record = kRingSize;
+    ++c->ring_pending;
+    ++c->stats.timing_records;
+    c->stats.timing_pending_high_water =
+        std::max<uint64_t>(c->stats.timing_pending_high_water, c->ring_pending);
+    return 0;
+}
+
+int op_begin(Context* c) {
+    c->phase_ns[0] = c->phase_ns[1] = c->phase_ns[2] = 0;
+    if (c->coarse) {
+        if (c->coarse_inner) return reject(c, "nested primitive timing inside a coarse timing scope");
+        c->coarse_inner = true;
+        return 0;
+    }
+    switch (c->mode) {
+        case kTimingCounters:
+            if (c->counter_active) return reject(c, "nested counter-only timing record");
+            c->counter_active = true;
+            return 0;
+        case kTimingDeferred:
+            return ring_open(c, RecordKind::Primitive, 4);
+        case kTimingEvents:
+            VZB_CUDA(c, ev_record(c, c->sync_ev[0]));
+            return 0;
+        default:
+            c->phase_start = std::chrono::steady_clock::now();
+            return 0;
+    }
+}
+
+static int host_phase(Context* c, int phase) {
+    if (sync_stream_raw(c)) return -1;
+    const auto t = std::chrono::steady_clock::now();
+    c->phase_ns[phase] =
+        std::chrono::duration_cast<std::chrono::nanoseconds>(t - c->phase_start).count();
+    c->phase_start = t;
+    return 0;
+}
+
+int op_mark(Context* c, int which) {
+    if (which != 1 && which != 2) return fail_message(c, "invalid timing event");
+    if (c->coarse) {
+        if (!c->coarse_inner) return fail_message(c, "coarse timing marker without an active primitive");
+        return 0;
+    }
+    switch (c->mode) {
+        case kTimingCounters:
+            if (!c->counter_active) return fail_message(c, "counter-only timing marker without active operation");
+            return 0;
+        case kTimingDeferred: {
+            if (c->active_record == kRingSize) return fail_message(c, "deferred timing marker without active record");
+            Record& r = c->ring[c->active_record];
+            VZB_CUDA(c, ev_record(c, r.ev[which]));
+            r.mask |= static_cast<uint8_t>(1u << which);
+            return 0;
+        }
+        case kTimingEvents:
+            VZB_CUDA(c, ev_record(c, c->sync_ev[which]));
+            return 0;
+        default:
+            return host_phase(c, which - 1);
+    }
+}
+
+int op_finish(Context* c, int op, uint64_t h2d, uint64_t d2h, uint64_t d2d, uint64_t zeroed,
+              uint64_t generated) {
+    ++c->outstanding;
+    RawStats& s = c->stats;
+    if (c->coarse) {
+        if (!c->coarse_inner) return fail_message(c, "coarse timing finish without an active primitive");
+        if (op != c->coarse_op)
+            return fail_message(c, "coarse timing scope received a different operation kind");
+        if (h2d || d2h) {
+            if (sync_stream(c, d2h ? Sync::HostOutput : Sync::UploadLifetime)) return -1;
+            return fail_message(c, "host transfer is forbidden inside a coarse timing scope");
+        }
+        ++s.calls[op];
+        s.d2d_bytes += d2d;
+        s.device_zeroed_bytes += zeroed;
+        s.device_generated_bytes += generated;
+        c->coarse_work = true;
+        if (c->mode == kTimingCounters) c->counter_pending = true;
+        c->coarse_inner = false;
+        return 0;
+    }
+    uint64_t ns0 = 0, ns1 = 0, ns2 = 0;
+    if (c->mode == kTimingCounters) {
+        if (!c->counter_active) return fail_message(c, "counter-only finish without active operation");
+        c->counter_active = false;
+        c->counter_pending = true;
+        if (d2h && sync_stream(c, Sync::HostOutput)) return -1;
+        ++s.calls[op];
+        s.h2d_bytes += h2d;
+        s.d2h_bytes += d2h;
+        s.d2d_bytes += d2d;
+        s.device_zeroed_bytes += zeroed;
+        s.device_generated_bytes += generated;
+        return 0;
+    }
+    if (c->mode == kTimingDeferred) {
+        if (c->active_record == kRingSize) return fail_message(c, "deferred finish without active record");
+        Record& r = c->ring[c->active_record];
+        VZB_CUDA(c, ev_record(c, r.ev[3]));
+        r.mask |= 1u << 3;
+        r.kind = RecordKind::Primitive;
+        r.op = op;
+        r.h2d = h2d;
+        r.d2h = d2h;
+        r.d2d = d2d;
+        r.zeroed = zeroed;
+        r.generated = generated;
+        if (ring_commit(c)) return -1;
+        return d2h ? flush_ring(c, Sync::HostOutput) : 0;
+    }
+    if (c->mode == kTimingEvents) {
+        VZB_CUDA(c, ev_record(c, c->sync_ev[3]));
+        const Sync why = d2h ? Sync::HostOutput : (h2d ? Sync::UploadLifetime : Sync::ProfilingLegacy);
+        if (sync_stream(c, why)) return -1;
+        if (elapsed(c, c->sync_ev[0], c->sync_ev[1], &ns0) ||
+            elapsed(c, c->sync_ev[1], c->sync_ev[2], &ns1) ||
+            elapsed(c, c->sync_ev[2], c->sync_ev[3], &ns2))
+            return -1;
+    } else {
+        if (host_phase(c, 2)) return -1;
+        if (h2d) ++s.sync_upload_lifetime;
+        if (d2h) ++s.sync_host_output;
+        s.sync_profiling_legacy += 3 - (h2d ? 1 : 0) - (d2h ? 1 : 0);
+        ns0 = c->phase_ns[0];
+        ns1 = c->phase_ns[1];
+        ns2 = c->phase_ns[2];
+    }
+    ++s.calls[op];
+    s.h2d_bytes += h2d;
+    s.d2h_bytes += d2h;
+    s.d2d_bytes += d2d;
+    s.device_zeroed_bytes += zeroed;
+    s.device_generated_bytes += generated;
+    if (h2d) s.h2d_ns += ns0;
+    s.kernel_ns[op] += ns1;
+    if (d2h) s.d2h_ns += ns2;
+    return 0;
+}
+
+int xfer_begin(Context* c) {
+    if (c->coarse) return reject(c, "host transfer is forbidden inside a coarse timing scope");
+    switch (c->mode) {
+        case kTimingCounters:
+            if (c->counter_active) return reject(c, "nested counter-only timing record");
+            c->counter_active = true;
+            return 0;
+        case kTimingDeferred:
+            return ring_open(c, RecordKind::Upload, 2);
+        case kTimingEvents:
+            VZB_CUDA(c, ev_record(c, c->sync_ev[0]));
+            return 0;
+        default:
+            c->phase_start = std::chrono::steady_clock::now();
+            return 0;
+    }
+}
+
+int xfer_finish(Context* c, size_t bytes, bool h2d) {
+    ++c->outstanding;
+    uint64_t ns = 0;
+    if (c->mode == kTimingCounters) {
+        if (!c->counter_active) return fail_message(c, "counter-only transfer finish without active transfer");
+        c->counter_active = false;
+        c->counter_pending = true;
+        if (!h2d && sync_stream(c, Sync::HostOutput)) return -1;
+        if (h2d) c->stats.h2d_bytes += bytes;
+        else c->stats.d2h_bytes += bytes;
+        return 0;
+    }
+    if (c->mode == kTimingDeferred) {
+        if (c->active_record == kRingSize) return fail_message(c, "deferred transfer finish without active record");
+        Record& r = c->ring[c->active_record];
+        VZB_CUDA(c, ev_record(c, r.ev[1]));
+        r.mask |= 1u << 1;
+        r.kind = h2d ? RecordKind::Upload : RecordKind::Download;
+        r.h2d = h2d ? bytes : 0;
+        r.d2h = h2d ? 0 : bytes;
+        if (ring_commit(c)) return -1;
+        return h2d ? 0 : flush_ring(c, Sync::HostOutput);
+    }
+    if (c->mode == kTimingEvents) {
+        VZB_CUDA(c, ev_record(c, c->sync_ev[1]));
+        if (sync_stream(c, h2d ? Sync::UploadLifetime : Sync::HostOutput)) return -1;
+        if (elapsed(c, c->sync_ev[0], c->sync_ev[1], &ns)) return -1;
+    } else {
+        if (sync_stream(c, h2d ? Sync::UploadLifetime : Sync::HostOutput)) return -1;
+        ns = std::chrono::duration_cast<std::chrono::nanoseconds>(
+                 std::chrono::steady_clock::now() - c->phase_start).count();
+    }
+    if (h2d) {
+        c->stats.h2d_bytes += bytes;
+        c->stats.h2d_ns += ns;
+    } else {
+        c->stats.d2h_bytes += bytes;
+        c->stats.d2h_ns += ns;
+    }
+    return 0;
+}
+
+static int probe_timing(Context* c) {
+    VZB_CUDA(c, ev_record(c, c->sync_ev[0]));
+    VZB_CUDA(c, ev_record(c, c->sync_ev[1]));
+    VZB_CUDA(c, cudaStreamSynchronize(c->stream));
+    float ms = -1.0f;
+    ++c->stats.timing_event_api_calls;
+    const cudaError_t e = cudaEventElapsedTime(&ms, c->sync_ev[0], c->sync_ev[1]);
+    if (e == cudaSuccess && ms >= 0.0f) {
+        c->mode = kTimingEvents;
+    } else {
+        (void)cudaGetLastError();
+        c->mode = kTimingHostBarrier;
+    }
+    c->stats.timing_mode = c->mode;
+    return 0;
+}
+
+// ---- pinned pool helpers ----------------------------------------------------
+
+static PinnedSlot* find_pinned(Context* c, uint64_t id) {
+    if (!c || !id) return nullptr;
+    const uint64_t enc = id & kSlotMask;
+    const uint32_t gen = static_cast<uint32_t>(id >> 32);
+    if (!enc || !gen) return nullptr;
+    const size_t slot = static_cast<size_t>(enc - 1);
+    if (slot >= c->pinned.size()) return nullptr;
+    PinnedSlot& p = c->pinned[slot];
+    return (p.active && p.generation == gen) ? &p : nullptr;
+}
+
+static int pinned_ready(Context* c, PinnedSlot* p, bool* ready) {
+    if (!p->in_flight) {
+        *ready = true;
+        return 0;
+    }
+    const cudaError_t st = cudaEventQuery(p->ready);
+    if (st == cudaSuccess) {
+        p->in_flight = false;
+        *ready = true;
+        return 0;
+    }
+    if (st == cudaErrorNotReady) {
+        *ready = false;
+        return 0;
+    }
+    return fail_cuda(c, "cudaEventQuery(pinned ready)", st);
+}
+
+static int trim_resident(Context* c) {
+    bool any = false;
+    for (size_t s : c->free_slots)
+        if (!c->slots[s].active && c->slots[s].ptr) any = true;
+    if (!any) return 0;
+    if (sync_for_reclaim(c)) return -1;
+    for (size_t s : c->free_slots) {
+        Slot& b = c->slots[s];
+        if (b.active || !b.ptr) continue;
+        VZB_CUDA(c, cudaFree(b.ptr));
+        ++c->stats.physical_free_calls;
+        c->stats.live_device_bytes -= b.capacity;
+        b.ptr = nullptr;
+        b.capacity = 0;
+        b.logical = 0;
+    }
+    return 0;
+}
+
+static int trim_pinned(Context* c) {
+    bool any = false;
+    for (size_t s : c->free_pinned)
+        if (!c->pinned[s].active && c->pinned[s].ptr) any = true;
+    if (!any) return 0;
+    if (sync_for_reclaim(c)) return -1;
+    for (size_t s : c->free_pinned) {
+        PinnedSlot& b = c->pinned[s];
+        if (b.active || !b.ptr) continue;
+        const uint32_t gen = b.generation;
+        const size_t cap = b.capacity;
+        if (b.ready) VZB_CUDA(c, cudaEventDestroy(b.ready));
+        VZB_CUDA(c, cudaFreeHost(b.ptr));
+        ++c->stats.pinned_physical_free_calls;
+        c->stats.live_pinned_bytes -= cap;
+        b = PinnedSlot{};
+        b.generation = gen;
+    }
+    return 0;
+}
+
+}  // namespace vzb
+
+using namespace vzb;
+
+// ===========================================================================
+// C ABI: context
+// ===========================================================================
+
+extern "C" uint32_t volta_cuda_abi_version(void) { return kAbiVersion; }
+
+extern "C" int volta_cuda_create(void** out) {
+    if (!out) return -1;
+    *out = nullptr;
+    Context* c = new (std::nothrow) Context;
+    if (!c) return -1;
+    *out = c;
+    try {
+        int count = 0;
+        cudaError_t e = cudaGetDeviceCount(&count);
+        if (e != cudaSuccess) return fail_cuda(c, "cudaGetDeviceCount", e);
+        if (count < 1) return fail_message(c, "no CUDA device is available");
+        VZB_CUDA(c, cudaGetDevice(&c->device));
+        cudaDeviceProp prop{};
+        VZB_CUDA(c, cudaGetDeviceProperties(&prop, c->device));
+        if (prop.major < 10)
+            return fail_message(c, "libvolta_cuda_backend (B200 build) requires an sm_100 device");
+        c->sm_count = prop.multiProcessorCount;
+        VZB_CUDA(c, cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+        for (auto& ev : c->sync_ev) {
+            ++c->stats.timing_event_api_calls;
+            VZB_CUDA(c, cudaEventCreate(&ev));
+        }
+        VZB_CUDA(c, cudaHostAlloc(&c->host_mailbox, 4096, cudaHostAllocMapped));
+        VZB_CUDA(c, cudaHostGetDevicePointer(&c->host_mailbox_dev, c->host_mailbox, 0));
+        if (ensure_ws(c, kWsCounter, 4096)) return -1;
+        if (probe_timing(c)) return -1;
+        return 0;
+    } catch (...) {
+        return fail_message(c, "CUDA context construction threw a C++ exception");
+    }
+}
+
+extern "C" void volta_cuda_destroy(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return;
+    if (c->coarse) drop_active_record(c);
+    if (c->mode == kTimingDeferred) (void)flush_ring(c, Sync::TimingFlush);
+    if (c->stream) (void)cudaStreamSynchronize(c->stream);
+    for (auto& w : c->ws)
+        if (w.ptr) cudaFree(w.ptr);
+    for (auto& s : c->slots)
+        if (s.ptr) cudaFree(s.ptr);
+    for (auto& p : c->pinned) {
+        if (p.ready) cudaEventDestroy(p.ready);
+        if (p.ptr) cudaFreeHost(p.ptr);
+    }
+    for (auto& r : c->ring)
+        for (auto e : r.ev)
+            if (e) cudaEventDestroy(e);
+    for (auto e : c->sync_ev)
+        if (e) cudaEventDestroy(e);
+    for (auto e : c->bench_ev)
+        if (e) cudaEventDestroy(e);
+    if (c->host_mailbox) cudaFreeHost(c->host_mailbox);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+extern "C" const char* volta_cuda_last_error(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    return c ? c->error.c_str() : "null CUDA context";
+}
+
+extern "C" int volta_cuda_set_resident_timing_policy(void* raw, int policy) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return -1;
+    if (c->active_record != kRingSize || c->coarse || c->counter_active || c->ring_pending ||
+        c->counter_pending)
+        return reject(c, "cannot change resident timing policy after work has started");
+    if (policy == 0) {
+        if (c->mode == kTimingEvents) c->mode = kTimingDeferred;
+    } else if (policy == 1) {
+        c->mode = kTimingCounters;
+    } else {
+        return reject(c, "unknown resident timing policy");
+    }
+    c->stats.timing_elapsed_query_attempts = 0;
+    c->stats.timing_elapsed_no_write = 0;
+    c->stats.timing_event_queries = 0;
+    c->stats.timing_event_api_calls = 0;
+    c->stats.timing_mode = c->mode;
+    return 0;
+}
+
+extern "C" int volta_cuda_test_inject_elapsed_no_write_once(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return -1;
+    if (c->active_record != kRingSize)
+        return reject(c, "cannot inject elapsed no-write during an active record");
+    c->inject_no_write = 1;
+    return 0;
+}
+
+extern "C" int volta_cuda_begin_coarse_timing(void* raw, int operation) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return -1;
+    if (c->mode != kTimingDeferred && c->mode != kTimingCounters)
+        return reject(c, "coarse timing requires a resident observation mode");
+    if (c->poisoned) return reject(c, "measurement timing is poisoned; reset stats before continuing");
+    if (operation < 0 || operation >= kOpCount) return reject(c, "invalid coarse timing operation");
+    if (c->coarse || c->active_record != kRingSize || c->counter_active)
+        return reject(c, "nested coarse timing scope");
+    if (c->mode == kTimingDeferred && ring_open(c, RecordKind::Coarse, 2)) return -1;
+    c->coarse_op = operation;
+    c->coarse = true;
+    c->coarse_inner = false;
+    c->coarse_work = false;
+    if (c->mode == kTimingDeferred) c->ring[c->active_record].op = operation;
+    return 0;
+}
+
+extern "C" int volta_cuda_end_coarse_timing(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return -1;
+    if (c->mode != kTimingDeferred && c->mode != kTimingCounters)
+        return reject(c, "coarse timing requires a resident observation mode");
+    if (!c->coarse || (c->mode == kTimingDeferred && c->active_record == kRingSize))
+        return reject(c, "no active coarse timing scope");
+    if (c->coarse_inner) return reject(c, "cannot end coarse timing during an active primitive");
+    if (c->mode == kTimingDeferred) {
+        Record& r = c->ring[c->active_record];
+        VZB_CUDA(c, ev_record(c, r.ev[1]));
+        r.mask |= 1u << 1;
+        r.kind = RecordKind::Coarse;
+        r.op = c->coarse_op;
+    }
+    c->coarse = false;
+    c->coarse_op = -1;
+    if (c->mode == kTimingDeferred && ring_commit(c)) return -1;
+    c->coarse_work = false;
+    ++c->stats.coarse_timing_scopes;
+    return 0;
+}
+
+extern "C" int volta_cuda_abort_coarse_timing(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return -1;
+    if (c->mode != kTimingDeferred && c->mode != kTimingCounters)
+        return reject(c, "coarse timing requires a resident observation mode");
+    if (c->coarse) drop_active_record(c);
+    return 0;
+}
+
+extern "C" int volta_cuda_ensure_timing_capacity(void* raw, size_t bound, size_t* before,
+                                                 size_t* after, int* flushed) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !before || !after || !flushed) return reject(c, "invalid timing-capacity output");
+    if (c->mode != kTimingDeferred && c->mode != kTimingCounters)
+        return reject(c, "timing-capacity preflight requires a resident observation mode");
+    if (c->active_record != kRingSize || c->counter_active)
+        return reject(c, "cannot preflight timing capacity during an active record");
+    if (bound > kRingSize) return reject(c, "deferred timing cohort bound exceeds ring capacity");
+    *before = c->mode == kTimingDeferred ? c->ring_pending : 0;
+    *flushed = 0;
+    if (c->mode == kTimingCounters) {
+        *after = 0;
+        return 0;
+    }
+    if (c->ring_pending > kRingSize - bound) {
+        if (flush_ring(c, Sync::TimingFlush)) return -1;
+        *flushed = 1;
+    }
+    *after = c->ring_pending;
+    return 0;
+}
+
+extern "C" int volta_cuda_flush_profiling(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return -1;
+    if (c->poisoned) return reject(c, "measurement timing is poisoned; reset stats before reading it");
+    if (c->active_record != kRingSize || c->counter_active)
+        return reject(c, "cannot flush an active timing record");
+    if (c->mode == kTimingCounters && c->counter_pending) return sync_stream(c, Sync::TimingFlush);
+    return flush_ring(c, Sync::TimingFlush);
+}
+
+extern "C" int volta_cuda_reset_stats(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return -1;
+    if (c->active_record != kRingSize || c->counter_active)
+        return reject(c, "cannot reset stats during an active timing record");
+    const bool pending = (c->mode == kTimingDeferred && c->ring_pending) ||
+                         (c->mode == kTimingCounters && c->counter_pending);
+    if (discard_ring(c, Sync::TimingFlush)) return -1;
+    if (c->mode == kTimingCounters && c->counter_pending && sync_stream(c, Sync::TimingFlush))
+        return -1;
+    if (c->poisoned && !pending && sync_stream(c, Sync::TimingFlush)) return -1;
+    const uint64_t live = c->stats.live_device_bytes, pinned = c->stats.live_pinned_bytes;
+    c->stats = RawStats{};
+    c->stats.live_device_bytes = live;
+    c->stats.peak_device_bytes = live;
+    c->stats.live_pinned_bytes = pinned;
+    c->stats.peak_pinned_bytes = pinned;
+    c->stats.timing_mode = c->mode;
+    c->poisoned = false;
+    c->coarse_work = false;
+    c->counter_active = false;
+    c->counter_pending = false;
+    return 0;
+}
+
+extern "C" int volta_cuda_get_stats(void* raw, RawStats* out) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !out) return -1;
+    if (c->poisoned) return reject(c, "measurement timing is poisoned; reset stats before reading it");
+    if (c->active_record != kRingSize || c->counter_active)
+        return reject(c, "cannot read stats during an active timing record");
+    if (volta_cuda_flush_profiling(raw)) return -1;
+    const RawStats& s = c->stats;
+    if (s.sync_host_output + s.sync_upload_lifetime + s.sync_timing_flush + s.sync_profiling_legacy +
+            s.sync_allocator_flush != s.synchronizations)
+        return fail_message(c, "synchronization reason accounting mismatch");
+    if (s.timing_elapsed_query_attempts != s.timing_event_queries + s.timing_elapsed_no_write)
+        return fail_message(c, "elapsed timing query accounting mismatch");
+    if (c->mode == kTimingCounters) {
+        uint64_t k = 0;
+        for (uint64_t v : s.kernel_ns) k += v;
+        if (s.timing_records || s.timing_elapsed_query_attempts || s.timing_elapsed_no_write ||
+            s.timing_event_queries || s.timing_event_api_calls || s.timing_pending_high_water ||
+            s.timing_flush_count || s.h2d_ns || s.d2h_ns || s.coarse_timing_ns || k)
+            return fail_message(c, "wall-only counter mode emitted CUDA-event attribution");
+    }
+    *out = s;
+    return 0;
+}
+
+extern "C" int volta_cuda_memory_breakdown(void* raw, uint64_t* workspace, uint64_t* resident,
+                                           uint64_t* cached) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !workspace || !resident || !cached) return fail_message(c, "invalid memory-breakdown output");
+    uint64_t w = 0, r = 0, k = 0;
+    for (const auto& x : c->ws) w += x.capacity;
+    for (const auto& s : c->slots) {
+        if (!s.ptr) continue;
+        (s.active ? r : k) += s.capacity;
+    }
+    if (w + r + k != c->stats.live_device_bytes) return fail_message(c, "device-memory accounting mismatch");
+    *workspace = w;
+    *resident = r;
+    *cached = k;
+    return 0;
+}
+
+extern "C" int volta_cuda_trim_resident_cache(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return fail_message(c, "invalid resident-cache trim context");
+    if (c->coarse) return reject(c, "resident-cache trim is forbidden inside a coarse timing scope");
+    return trim_resident(c);
+}
+
+extern "C" int volta_cuda_pinned_memory_stats(void* raw, RawPinnedMemoryStats* out) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !out) return fail_message(c, "invalid pinned-memory stats output");
+    RawPinnedMemoryStats r{};
+    for (auto& p : c->pinned) {
+        if (!p.ptr) continue;
+        bool ready = false;
+        if (pinned_ready(c, &p, &ready)) return -1;
+        if (p.active) {
+            r.active_bytes += p.capacity;
+            ++r.active_allocations;
+        } else {
+            r.cached_bytes += p.capacity;
+            ++r.cached_allocations;
+        }
+        if (!ready) ++r.in_flight_allocations;
+    }
+    if (r.active_bytes + r.cached_bytes != c->stats.live_pinned_bytes)
+        return fail_message(c, "pinned-memory accounting mismatch");
+    r.physical_allocation_calls = c->stats.pinned_allocation_calls;
+    r.allocation_requests = c->stats.pinned_alloc_requests;
+    r.reuse_hits = c->stats.pinned_reuse_hits;
+    r.free_requests = c->stats.pinned_free_requests;
+    r.physical_free_calls = c->stats.pinned_physical_free_calls;
+    r.host_write_calls = c->stats.pinned_host_write_calls;
+    r.host_write_bytes = c->stats.pinned_host_write_bytes;
+    r.peak_bytes = c->stats.peak_pinned_bytes;
+    *out = r;
+    return 0;
+}
+
+extern "C" int volta_cuda_x4c_control_state(void* raw, RawX4cControlState* out) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !out) return fail_message(c, "invalid X4c control-state output");
+    ++c->stats.x4c_control_peek_calls;
+    const cudaError_t st = cudaStreamQuery(c->stream);
+    uint32_t state = 0;
+    if (st == cudaSuccess) {
+        c->outstanding = 0;
+        c->counter_pending = false;
+        for (auto& p : c->pinned) p.in_flight = false;
+    } else if (st == cudaErrorNotReady) {
+        state = 1;
+        ++c->stats.x4c_control_peek_pending;
+    } else {
+        return fail_cuda(c, "cudaStreamQuery(X4c control state)", st);
+    }
+    RawX4cControlState r{};
+    r.stream_state = state;
+    r.flags = (c->coarse ? 1u : 0u) | ((c->active_record != kRingSize || c->counter_active) ? 2u : 0u) |
+              (c->poisoned ? 4u : 0u);
+    r.outstanding_cuda_operations = c->outstanding;
+    r.pending_timing_records = c->ring_pending;
+    for (const auto& w : c->ws) r.workspace_device_bytes += w.capacity;
+    for (const auto& s : c->slots) {
+        if (!s.ptr) continue;
+        if (s.active) {
+            ++r.active_device_allocations;
+            r.active_device_bytes += s.capacity;
+        } else {
+            ++r.cached_device_allocations;
+            r.cached_device_bytes += s.capacity;
+        }
+    }
+    for (const auto& p : c->pinned) {
+        if (!p.ptr) continue;
+        if (p.active) {
+            ++r.active_pinned_allocations;
+            r.active_pinned_bytes += p.capacity;
+        } else {
+            ++r.cached_pinned_allocations;
+            r.cached_pinned_bytes += p.capacity;
+        }
+        if (p.in_flight) ++r.in_flight_pinned_allocations;
+    }
+    if (r.workspace_device_bytes + r.active_device_bytes + r.cached_device_bytes !=
+        c->stats.live_device_bytes)
+        return fail_message(c, "X4c control-state device ownership mismatch");
+    if (r.active_pinned_bytes + r.cached_pinned_bytes != c->stats.live_pinned_bytes)
+        return fail_message(c, "X4c control-state pinned ownership mismatch");
+    *out = r;
+    return 0;
+}
+
+// ===========================================================================
+// C ABI: pinned pool
+// ===========================================================================
+
+extern "C" int volta_cuda_pinned_alloc(void* raw, size_t bytes, uint64_t* out_id) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !bytes || !out_id) return fail_message(c, "invalid pinned allocation");
+    if (c->coarse) return reject(c, "pinned allocation is forbidden inside a coarse timing scope");
+    try {
+        ++c->stats.pinned_alloc_requests;
+        // best fit among cached, ready allocations (ties to the lowest slot)
+        size_t best_pos = SIZE_MAX, best_slot = SIZE_MAX, best_cap = SIZE_MAX;
+        for (size_t pos = 0; pos < c->free_pinned.size(); ++pos) {
+            const size_t s = c->free_pinned[pos];
+            PinnedSlot& p = c->pinned[s];
+            bool ready = false;
+            if (p.ptr && pinned_ready(c, &p, &ready)) return -1;
+            if (p.active || !p.ptr || !ready || p.generation == kGenerationMax || p.capacity < bytes)
+                continue;
+            if (p.capacity < best_cap || (p.capacity == best_cap && s < best_slot)) {
+                best_pos = pos;
+                best_cap = p.capacity;
+                best_slot = s;
+            }
+        }
+        if (best_pos != SIZE_MAX) {
+            c->free_pinned[best_pos] = c->free_pinned.back();
+            c->free_pinned.pop_back();
+            PinnedSlot& p = c->pinned[best_slot];
+            ++p.generation;
+            p.logical = bytes;
+            p.active = true;
+            ++c->stats.pinned_reuse_hits;
+            *out_id = make_id(best_slot, p.generation);
+            return 0;
+        }
+        void* ptr = nullptr;
+        cudaError_t st = cudaMallocHost(&ptr, bytes);
+        if (st != cudaSuccess) return fail_cuda(c, "cudaMallocHost(&pinned, bytes)", st);
+        cudaEvent_t ready = nullptr;
+        st = cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
+        if (st != cudaSuccess) {
+            (void)cudaFreeHost(ptr);
+            return fail_cuda(c, "cudaEventCreateWithFlags(pinned ready)", st);
+        }
+        ++c->stats.pinned_allocation_calls;
+        c->stats.live_pinned_bytes += bytes;
+        c->stats.peak_pinned_bytes = std::max(c->stats.peak_pinned_bytes, c->stats.live_pinned_bytes);
+        size_t slot = SIZE_MAX;
+        for (size_t pos = 0; pos < c->free_pinned.size(); ++pos) {
+            const size_t s = c->free_pinned[pos];
+            const PinnedSlot& p = c->pinned[s];
+            if (!p.active && !p.ptr && p.generation != kGenerationMax) {
+                slot = s;
+                c->free_pinned[pos] = c->free_pinned.back();
+                c->free_pinned.pop_back();
+                break;
+            }
+        }
+        if (slot == SIZE_MAX) {
+            if (c->pinned.size() >= kSlotMask) return fail_message(c, "pinned slot id space exhausted");
+            c->pinned.emplace_back();
+            slot = c->pinned.size() - 1;
+        }
+        PinnedSlot& p = c->pinned[slot];
+        ++p.generation;
+        p.ptr = ptr;
+        p.capacity = bytes;
+        p.logical = bytes;
+        p.ready = ready;
+        p.active = true;
+        p.in_flight = false;
+        *out_id = make_id(slot, p.generation);
+        return 0;
+    } catch (...) {
+        return fail_message(c, "pinned allocation threw a C++ exception");
+    }
+}
+
+extern "C" int volta_cuda_pinned_write(void* raw, uint64_t id, size_t offset, const void* src,
+                                       size_t bytes) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !src || !bytes) return fail_message(c, "invalid pinned write");
+    PinnedSlot* p = find_pinned(c, id);
+    if (!p) return fail_message(c, "unknown pinned buffer id");
+    if (offset > p->logical || bytes > p->logical - offset)
+        return fail_message(c, "pinned buffer region is out of bounds");
+    bool ready = false;
+    if (pinned_ready(c, p, &ready)) return -1;
+    if (!ready) return reject(c, "pinned buffer is still consumed by an outstanding H2D");
+    std::memcpy(static_cast<unsigned char*>(p->ptr) + offset, src, bytes);
+    ++c->stats.pinned_host_write_calls;
+    c->stats.pinned_host_write_bytes += bytes;
+    return 0;
+}
+
+extern "C" int volta_cuda_pinned_wait_ready(void* raw, uint64_t id) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !id) return fail_message(c, "invalid pinned wait");
+    if (c->coarse || c->coarse_inner || c->counter_active || c->active_record != kRingSize)
+        return reject(c, "pinned wait inside an active timing scope");
+    PinnedSlot* p = find_pinned(c, id);
+    if (!p) return fail_message(c, "unknown pinned buffer id");
+    bool ready = false;
+    if (pinned_ready(c, p, &ready)) return -1;
+    if (ready) return 0;
+    const auto t0 = std::chrono::steady_clock::now();
+    const cudaError_t st = cudaEventSynchronize(p->ready);
+    const auto t1 = std::chrono::steady_clock::now();
+    if (st != cudaSuccess) return fail_cuda(c, "cudaEventSynchronize(pinned ready)", st);
+    p->in_flight = false;
+    ++c->stats.synchronizations;
+    ++c->stats.sync_upload_lifetime;
+    c->stats.synchronization_ns += std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count();
+    return 0;
+}
+
+extern "C" int volta_cuda_pinned_free(void* raw, uint64_t id) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !id) return fail_message(c, "invalid pinned free");
+    if (c->coarse) return reject(c, "pinned free is forbidden inside a coarse timing scope");
+    PinnedSlot* p = find_pinned(c, id);
+    if (!p) return fail_message(c, "unknown or stale pinned buffer id");
+    ++c->stats.pinned_free_requests;
+    c->free_pinned.push_back(static_cast<size_t>((id & kSlotMask) - 1));
+    p->logical = 0;
+    p->active = false;
+    return 0;
+}
+
+extern "C" int volta_cuda_trim_pinned_cache(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return fail_message(c, "invalid pinned-cache trim context");
+    if (c->coarse) return reject(c, "pinned-cache trim is forbidden inside a coarse timing scope");
+    return trim_pinned(c);
+}
+
+// ===========================================================================
+// C ABI: resident arena
+// ===========================================================================
+
+extern "C" int volta_cuda_resident_alloc(void* raw, size_t bytes, uint64_t* out_id) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !bytes || !out_id) return fail_message(c, "invalid resident allocation");
+    if (c->coarse) return reject(c, "resident allocation is forbidden inside a coarse timing scope");
+    try {
+        ++c->stats.resident_alloc_requests;
+        size_t best_pos = SIZE_MAX, best_slot = SIZE_MAX, best_cap = SIZE_MAX;
+        for (size_t pos = 0; pos < c->free_slots.size(); ++pos) {
+            const size_t s = c->free_slots[pos];
+            const Slot& b = c->slots[s];
+            if (b.active || !b.ptr || b.generation == kGenerationMax || b.capacity < bytes) continue;
+            if (b.capacity < best_cap || (b.capacity == best_cap && s < best_slot)) {
+                best_pos = pos;
+                best_cap = b.capacity;
+                best_slot = s;
+            }
+        }
+        if (best_pos != SIZE_MAX) {
+            c->free_slots[best_pos] = c->free_slots.back();
+            c->free_slots.pop_back();
+            Slot& b = c->slots[best_slot];
+            ++b.generation;
+            b.logical = bytes;
+            b.active = true;
+            ++c->stats.resident_reuse_hits;
+            *out_id = make_id(best_slot, b.generation);
+            return 0;
+        }
+        void* ptr = nullptr;
+        cudaError_t e = cudaMalloc(&ptr, bytes);
+        if (e == cudaErrorMemoryAllocation) {
+            (void)cudaGetLastError();
+            if (trim_resident(c)) return -1;
+            e = cudaMalloc(&ptr, bytes);
+        }
+        if (e != cudaSuccess) return fail_cuda(c, "cudaMalloc(&resident, bytes)", e);
+        ++c->stats.allocation_calls;
+        c->stats.live_device_bytes += bytes;
+        c->stats.peak_device_bytes = std::max(c->stats.peak_device_bytes, c->stats.live_device_bytes);
+        size_t slot = SIZE_MAX;
+        for (size_t pos = 0; pos < c->free_slots.size(); ++pos) {
+            const size_t s = c->free_slots[pos];
+            const Slot& b = c->slots[s];
+            if (!b.active && !b.ptr && b.generation != kGenerationMax) {
+                slot = s;
+                c->free_slots[pos] = c->free_slots.back();
+                c->free_slots.pop_back();
+                break;
+            }
+        }
+        if (slot == SIZE_MAX) {
+            if (c->slots.size() >= kSlotMask) {
+                cudaFree(ptr);
+                return fail_message(c, "resident slot id space exhausted");
+            }
+            c->slots.emplace_back();
+            slot = c->slots.size() - 1;
+        }
+        Slot& b = c->slots[slot];
+        ++b.generation;
+        b.ptr = ptr;
+        b.capacity = bytes;
+        b.logical = bytes;
+        b.active = true;
+        *out_id = make_id(slot, b.generation);
+        return 0;
+    } catch (...) {
+        return fail_message(c, "resident allocation threw a C++ exception");
+    }
+}
+
+extern "C" int volta_cuda_resident_free(void* raw, uint64_t id) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !id) return fail_message(c, "invalid resident free");
+    if (c->coarse) return reject(c, "resident free is forbidden inside a coarse timing scope");
+    ++c->stats.resident_free_requests;
+    Slot* b = find_slot(c, id);
+    if (!b) return fail_message(c, "unknown or stale resident buffer id");
+    try {
+        c->free_slots.push_back(static_cast<size_t>((id & kSlotMask) - 1));
+    } catch (...) {
+        return fail_message(c, "resident free threw a C++ exception");
+    }
+    b->logical = 0;
+    b->active = false;
+    return 0;
+}
+
+extern "C" int volta_cuda_resident_upload(void* raw, uint64_t id, size_t offset, const void* src,
+                                          size_t bytes) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !src || !bytes) return fail_message(c, "invalid resident upload");
+    void* dst = nullptr;
+    if (region(c, id, offset, bytes, &dst)) return -1;
+    if (xfer_begin(c)) return -1;
+    const auto t0 = std::chrono::steady_clock::now();
+    const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->stream);
+    const auto t1 = std::chrono::steady_clock::now();
+    if (e != cudaSuccess) return fail_cuda(c, "cudaMemcpyAsync(resident H2D)", e);
+    ++c->stats.resident_h2d_host_calls;
+    c->stats.resident_h2d_host_call_ns +=
+        std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count();
+    return xfer_finish(c, bytes, true);
+}
+
+extern "C" int volta_cuda_resident_download(void* raw, uint64_t id, size_t offset, void* dst,
+                                            size_t bytes) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !dst || !bytes) return fail_message(c, "invalid resident download");
+    void* src = nullptr;
+    if (region(c, id, offset, bytes, &src)) return -1;
+    if (xfer_begin(c)) return -1;
+    const auto t0 = std::chrono::steady_clock::now();
+    const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c->stream);
+    const auto t1 = std::chrono::steady_clock::now();
+    if (e != cudaSuccess) return fail_cuda(c, "cudaMemcpyAsync(resident D2H)", e);
+    ++c->stats.resident_d2h_host_calls;
+    c->stats.resident_d2h_host_call_ns +=
+        std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count();
+    return xfer_finish(c, bytes, false);
+}
+
+extern "C" int volta_cuda_resident_zero(void* raw, uint64_t id, size_t offset, size_t bytes) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !bytes) return fail_message(c, "invalid resident zero");
+    void* dst = nullptr;
+    if (region(c, id, offset, bytes, &dst)) return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    VZB_CUDA(c, cudaMemsetAsync(dst, 0, bytes, c->stream));
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsRows, 0, 0, 0, bytes, 0);
+}
+
+static int copy_rows(Context* c, uint64_t src_id, size_t src_off, size_t src_stride,
+                     uint64_t dst_id, size_t dst_off, size_t dst_stride, size_t rows,
+                     size_t row_bytes, int op) {
+    if (!c) return fail_message(c, "invalid resident D2D copy context");
+    void *src = nullptr, *dst = nullptr;
+    size_t src_span = 0, dst_span = 0;
+    if (strided_region(c, src_id, src_off, src_stride, row_bytes, rows, &src, &src_span) ||
+        strided_region(c, dst_id, dst_off, dst_stride, row_bytes, rows, &dst, &dst_span))
+        return -1;
+    if (src_id == dst_id) {
+        size_t se = 0, de = 0;
+        if (!add_ok(src_off, src_span, &se) || !add_ok(dst_off, dst_span, &de))
+            return fail_message(c, "resident D2D copy envelope overflows size_t");
+        if (src_off < de && dst_off < se)
+            return fail_message(c, "resident D2D copy source and destination overlap");
+    }
+    size_t total = 0;
+    if (!mul_ok(rows, row_bytes, &total)) return fail_message(c, "resident D2D byte count overflows size_t");
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    VZB_CUDA(c, cudaMemcpy2DAsync(dst, dst_stride, src, src_stride, row_bytes, rows,
+                                  cudaMemcpyDeviceToDevice, c->stream));
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, op, 0, 0, total, 0, 0);
+}
+
+extern "C" int volta_cuda_resident_copy_rows(void* raw, uint64_t src_id, size_t src_off,
+                                             size_t src_stride, uint64_t dst_id, size_t dst_off,
+                                             size_t dst_stride, size_t rows, size_t row_bytes) {
+    return copy_rows(static_cast<Context*>(raw), src_id, src_off, src_stride, dst_id, dst_off,
+                     dst_stride, rows, row_bytes, kOpPcsRows);
+}
+
+extern "C" int volta_cuda_resident_mailbox_copy_rows(void* raw, uint64_t src_id, size_t src_off,
+                                                     size_t src_stride, uint64_t dst_id,
+                                                     size_t dst_off, size_t dst_stride,
+                                                     size_t rows, size_t row_bytes) {
+    return copy_rows(static_cast<Context*>(raw), src_id, src_off, src_stride, dst_id, dst_off,
+                     dst_stride, rows, row_bytes, kOpMailbox);
+}
+
+// ===========================================================================
+// Extensions (include/volta_b200_ext.h): measurement markers, launch count
+// ===========================================================================
+
+extern "C" int volta_b200_timing_mark(void* raw, int slot) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || slot < 0 || slot >= 8) return fail_message(c, "invalid timing marker slot");
+    if (!c->bench_ev[slot]) VZB_CUDA(c, cudaEventCreate(&c->bench_ev[slot]));
+    VZB_CUDA(c, cudaEventRecord(c->bench_ev[slot], c->stream));
+    return 0;
+}
+
+extern "C" int volta_b200_timing_elapsed(void* raw, int start, int end, float* ms) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !ms || start < 0 || start >= 8 || end < 0 || end >= 8 || !c->bench_ev[start] ||
+        !c->bench_ev[end])
+        return fail_message(c, "invalid timing marker pair");
+    VZB_CUDA(c, cudaEventSynchronize(c->bench_ev[end]));
+    VZB_CUDA(c, cudaEventElapsedTime(ms, c->bench_ev[start], c->bench_ev[end]));
+    return 0;
+}
+
+extern "C" int volta_b200_launch_count(void* raw, uint64_t* launches) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !launches) return fail_message(c, "invalid launch-count output");
+    *launches = c->launches;
+    return 0;
+}

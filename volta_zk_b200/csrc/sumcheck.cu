@@ -1,0 +1,1111 @@
+// Sumcheck round engine: product / triple-product / LogUp round messages,
+// multilinear folds, eq tables and the small Fp2 vector primitives of the
+// seam.
+//
+// Reference entry points (okrame/volta-zk cuda/volta_cuda_backend.cu):
+//   fp2_product_round{,_into,_scaled_into}_device   4827-4893
+//   fp2_triple_product_round{,_into}_device         5106-5153
+//   logup_general_round{,_device,_into_device}      6655-6769
+//   logup_fold4{,_device}                           6771-6808
+//   fp2_deinterleave_device                         6810-6831
+//   logup_suffix_eq_device                          6833-6860
+//   fp2_fold_rows_device                            6862-6882
+//   logup_eq_rows_device                            6884-6918
+//   logup_aux_round{,_into}_device                  7008-7062
+//   fp2_dot_device, fp2_dot_scaled_pair_into_device, fp2_pair_sum_device
+//                                                   4715-4746, 5001-5069
+//   claim_reduce_f_two_into_device, x4d_link_eq_accumulate_device 4895-4999
+//   fp2_add_inplace / mobius_inverse / affine_eq_weights 7101-7149
+//   fp2_row_dots_device, fp2_powers_device          4049-4126
+//   reserve_*_workspace                             4748-4785
+// CPU semantics: rust/volta-proto/src/logup.rs:284-500, hadamard.rs:222-240,
+// sumcheck_clear.rs:33-45, mle.rs:7-30.
+#include "reduce.cuh"
+#include "runtime.cuh"
+
+#include <algorithm>
+
+namespace vzb {
+
+// ---------------------------------------------------------------------------
+// evaluation functors (one per message shape)
+// ---------------------------------------------------------------------------
+
+struct ProductEval {  // [g(0), g(2)] of a*b
+    const Fp2 *a, *b;
+    __device__ __forceinline__ void operator()(size_t i, Acc<2>& acc) const {
+        const Fp2 a0 = ldcs2(a + 2 * i), a1 = ldcs2(a + 2 * i + 1);
+        const Fp2 b0 = ldcs2(b + 2 * i), b1 = ldcs2(b + 2 * i + 1);
+        acc.v[0] = f2add(acc.v[0], f2mul(a0, b0));
+        acc.v[1] = f2add(acc.v[1], f2mul(f2at2(a0, a1), f2at2(b0, b1)));
+    }
+};
+
+struct TripleEval {  // [g(0), g(2), g(3)] of a*b*c
+    const Fp2 *a, *b, *c;
+    __device__ __forceinline__ void operator()(size_t i, Acc<3>& acc) const {
+        const Fp2 a0 = ldcs2(a + 2 * i), a1 = ldcs2(a + 2 * i + 1);
+        const Fp2 b0 = ldcs2(b + 2 * i), b1 = ldcs2(b + 2 * i + 1);
+        const Fp2 c0 = ldcs2(c + 2 * i), c1 = ldcs2(c + 2 * i + 1);
+        const Fp2 da = f2sub(a1, a0), db = f2sub(b1, b0), dc = f2sub(c1, c0);
+        const Fp2 a2 = f2add(a1, da), b2 = f2add(b1, db), c2 = f2add(c1, dc);
+        const Fp2 a3 = f2add(a2, da), b3 = f2add(b2, db), c3 = f2add(c2, dc);
+        acc.v[0] = f2add(acc.v[0], f2mul(f2mul(a0, b0), c0));
+        acc.v[1] = f2add(acc.v[1], f2mul(f2mul(a2, b2), c2));
+        acc.v[2] = f2add(acc.v[2], f2mul(f2mul(a3, b3), c3));
+    }
+};
+
+// RoundAcc = sum_i S[i] * (a0 d0 + b0 c0, a2 d2 + b2 c2, c0 d0, c2 d2)
+struct LogupEval {
+    const Fp2 *p0, *p1, *q0, *q1, *s;
+    __device__ __forceinline__ void operator()(size_t i, Acc<4>& acc) const {
+        const Fp2 a0 = ldcs2(p0 + 2 * i), a2 = f2at2(a0, ldcs2(p0 + 2 * i + 1));
+        const Fp2 b0 = ldcs2(p1 + 2 * i), b2 = f2at2(b0, ldcs2(p1 + 2 * i + 1));
+        const Fp2 c0 = ldcs2(q0 + 2 * i), c2 = f2at2(c0, ldcs2(q0 + 2 * i + 1));
+        const Fp2 d0 = ldcs2(q1 + 2 * i), d2 = f2at2(d0, ldcs2(q1 + 2 * i + 1));
+        const Fp2 si = ldg2(s + i);
+        acc.v[0] = f2add(acc.v[0], f2mul(si, f2add(f2mul(a0, d0), f2mul(b0, c0))));
+        acc.v[1] = f2add(acc.v[1], f2mul(si, f2add(f2mul(a2, d2), f2mul(b2, c2))));
+        acc.v[2] = f2add(acc.v[2], f2mul(si, f2mul(c0, d0)));
+        acc.v[3] = f2add(acc.v[3], f2mul(si, f2mul(c2, d2)));
+    }
+};
+
+struct DotEval {
+    const Fp2 *a, *b;
+    __device__ __forceinline__ void operator()(size_t i, Acc<1>& acc) const {
+        acc.v[0] = f2add(acc.v[0], f2mul(ldcs2(a + i), ldcs2(b + i)));
+    }
+};
+
+struct PairSumEval {  // sums of an array of (g0, g2) pairs
+    const Fp2* in;
+    __device__ __forceinline__ void operator()(size_t i, Acc<2>& acc) const {
+        acc.v[0] = f2add(acc.v[0], ldcs2(in + 2 * i));
+        acc.v[1] = f2add(acc.v[1], ldcs2(in + 2 * i + 1));
+    }
+};
+
+// Degree-3 aux-leaf round (logup.rs:740-900 per pair):
+// pq(t) = S (c_t + d_t), qq(t) = S c_t d_t, aux(t) = sum_k e_t (w0 v0_t + w1 v1_t)
+struct AuxEval {
+    const Fp2 *q0, *q1, *s, *columns, *eq, *weights;
+    const uint32_t* claim_cols;
+    size_t column_count, claim_count, vector_len;
+    __device__ __forceinline__ void operator()(size_t i, Acc<9>& acc) const {
+        const Fp2 c0 = ldg2(q0 + 2 * i), c1 = ldg2(q0 + 2 * i + 1);
+        const Fp2 d0 = ldg2(q1 + 2 * i), d1 = ldg2(q1 + 2 * i + 1);
+        const Fp2 ct[3] = {c0, f2at2(c0, c1), f2at3(c0, c1)};
+        const Fp2 dt[3] = {d0, f2at2(d0, d1), f2at3(d0, d1)};
+        const Fp2 si = ldg2(s + i);
+#pragma unroll
+        for (int t = 0; t < 3; ++t) {
+            acc.v[t] = f2add(acc.v[t], f2mul(si, f2add(ct[t], dt[t])));
+            acc.v[3 + t] = f2add(acc.v[3 + t], f2mul(si, f2mul(ct[t], dt[t])));
+        }
+        for (size_t k = 0; k < claim_count; ++k) {
+            const size_t col = claim_cols[k];
+            if (col >= column_count) continue;
+            const Fp2* v0 = columns + (2 * col) * vector_len;
+            const Fp2* v1 = columns + (2 * col + 1) * vector_len;
+            const Fp2* e = eq + k * vector_len;
+            const Fp2 w0 = ldg2(weights + 2 * k), w1 = ldg2(weights + 2 * k + 1);
+            const Fp2 x0 = ldg2(v0 + 2 * i), x1 = ldg2(v0 + 2 * i + 1);
+            const Fp2 y0 = ldg2(v1 + 2 * i), y1 = ldg2(v1 + 2 * i + 1);
+            const Fp2 e0 = ldg2(e + 2 * i), e1 = ldg2(e + 2 * i + 1);
+            const Fp2 xt[3] = {x0, f2at2(x0, x1), f2at3(x0, x1)};
+            const Fp2 yt[3] = {y0, f2at2(y0, y1), f2at3(y0, y1)};
+            const Fp2 et[3] = {e0, f2at2(e0, e1), f2at3(e0, e1)};
+#pragma unroll
+            for (int t = 0; t < 3; ++t)
+                acc.v[6 + t] = f2add(acc.v[6 + t],
+                                     f2mul(et[t], f2add(f2mul(w0, xt[t]), f2mul(w1, yt[t]))));
+        }
+    }
+};
+
+// Assemble the aux message: l(t) * cpref * (lambda pq + qq) + aux, with
+// l(0) = 1 - p, l(2) = 3p - 1, l(3) = 5p - 2.
+struct AuxEpi {
+    Fp2* out;
+    Fp2 lambda, cpref, point;
+    __device__ void operator()(const Acc<9>& a) const {
+        const Fp2 p = point;
+        const Fp2 l0 = f2sub(f2one(), p);
+        const Fp2 l2 = f2sub(f2add(f2add(p, p), p), f2one());
+        const Fp2 l3 = f2sub(f2add(f2add(f2add(p, p), f2add(p, p)), p), Fp2{2, 0});
+        const Fp2 ell[3] = {l0, l2, l3};
+        for (int t = 0; t < 3; ++t)
+            out[t] = f2add(f2mul(ell[t], f2mul(cpref, f2add(f2mul(lambda, a.v[t]), a.v[3 + t]))),
+                           a.v[6 + t]);
+    }
+};
+
+struct ScaledPairEpi {  // (scale * dot, -scale * dot)
+    Fp2* out;
+    Fp2 scale;
+    __device__ void operator()(const Acc<1>& a) const {
+        const Fp2 v = f2mul(scale, a.v[0]);
+        out[0] = v;
+        out[1] = f2neg(v);
+    }
+};
+
+template <int K, class Eval, class Epi>
+__global__ void __launch_bounds__(kReduceThreads) reduce_rounds_kernel(
+    Eval eval, size_t items, Fp2* partials, unsigned* counter, Epi epi) {
+    Acc<K> acc;
+    acc.zero();
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < items; i += stride)
+        eval(i, acc);
+    grid_finish<K>(acc, partials, counter, epi);
+}
+
+template <int K, class Eval, class Epi>
+static int launch_reduce(Context* c, const Eval& eval, size_t items, const Epi& epi,
+                         unsigned per_sm = 4) {
+    const unsigned blocks = grid_for(c, items, kReduceThreads, per_sm);
+    reduce_rounds_kernel<K, Eval, Epi><<<blocks, kReduceThreads, 0, c->stream>>>(
+        eval, items, ws<Fp2>(c, kWsPartials), ws<unsigned>(c, kWsCounter), epi);
+    VZB_LAUNCHED(c);
+    return 0;
+}
+
+// Output of a round message: a device pointer (arena mailbox) or a host
+// pointer served through the context's mapped pinned mailbox.
+struct MsgOut {
+    Fp2* dev;
+    Fp2* host;
+    size_t count;
+};
+
+static MsgOut msg_out(Context* c, Fp2* dev, Fp2* host, size_t count) {
+    if (dev) return MsgOut{dev, nullptr, count};
+    return MsgOut{static_cast<Fp2*>(c->host_mailbox_dev), host, count};
+}
+
+static int finish_msg(Context* c, int op, const MsgOut& o) {
+    if (op_mark(c, 2)) return -1;
+    if (!o.host) return op_finish(c, op, 0, 0);
+    const size_t bytes = o.count * sizeof(Fp2);
+    if (op_finish(c, op, 0, bytes)) return -1;
+    std::memcpy(o.host, c->host_mailbox, bytes);  // stream is synchronised here
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+// folds and element-wise kernels
+// ---------------------------------------------------------------------------
+
+// out[row, i] = in[row, 2i] + (in[row, 2i+1] - in[row, 2i]) r
+__global__ void fold_rows_kernel(const Fp2* __restrict__ in, Fp2* __restrict__ out, size_t rows,
+                                 size_t pairs, Fp2 r) {
+    const size_t total = rows * pairs;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t z = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; z < total; z += stride) {
+        const size_t row = z / pairs, i = z - row * pairs;
+        const Fp2* src = in + row * 2 * pairs;
+        st2(out + z, f2fold(ldcs2(src + 2 * i), ldcs2(src + 2 * i + 1), r));
+    }
+}
+
+struct Quad {
+    const Fp2* in[4];
+    Fp2* out[4];
+};
+
+__global__ void fold4_kernel(Quad q, size_t pairs, Fp2 r) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < pairs; i += stride) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            st2(q.out[k] + i, f2fold(ldcs2(q.in[k] + 2 * i), ldcs2(q.in[k] + 2 * i + 1), r));
+    }
+}
+
+__global__ void deinterleave_kernel(const Fp2* in, Fp2* even, Fp2* odd, size_t pairs) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < pairs; i += stride) {
+        st2(even + i, ldcs2(in + 2 * i));
+        st2(odd + i, ldcs2(in + 2 * i + 1));
+    }
+}
+
+__global__ void add_inplace_kernel(Fp2* t, const Fp2* a, size_t n) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        st2(t + i, f2add(ldg2(t + i), ldg2(a + i)));
+}
+
+// ---------------------------------------------------------------------------
+// eq tables
+//
+// eq(point, i) = prod_b (bit_b(i) ? point[b] : 1 - point[b]) (LSB-first,
+// mle.rs:7-20).  A table of 2^n entries is the outer product of a table over
+// the low 12 coordinates and a table over the rest, so every entry beyond
+// 2^12 costs one product.  Tables up to 2^12 are built by in-block expansion
+// in shared memory.
+// ---------------------------------------------------------------------------
+
+constexpr int kEqTileBits = 11;
+constexpr int kEqTile = 1 << kEqTileBits;
+
+// Block-wide: write eq(point[0..n), .) * scale (* *scale_dev) (n <= 11) to `out`.
+__device__ void eq_block_build(const Fp2* point, int n, Fp2 scale, const Fp2* scale_dev, Fp2* out) {
+    __shared__ Fp2 buf[kEqTile];
+    if (threadIdx.x == 0) buf[0] = scale_dev ? f2mul(scale, *scale_dev) : scale;
+    __syncthreads();
+    int size = 1;
+    for (int k = n - 1; k >= 0; --k) {
+        const Fp2 pk = point[k];
+        // expand in place from the top so sources are read before overwrite
+        Fp2 lo[kEqTile / 256], hi[kEqTile / 256];
+        int cnt = 0;
+        for (int i = threadIdx.x; i < size; i += blockDim.x, ++cnt) {
+            const Fp2 v = buf[i];
+            hi[cnt] = f2mul(v, pk);
+            lo[cnt] = f2sub(v, hi[cnt]);
+        }
+        __syncthreads();
+        cnt = 0;
+        for (int i = threadIdx.x; i < size; i += blockDim.x, ++cnt) {
+            buf[2 * i] = lo[cnt];
+            buf[2 * i + 1] = hi[cnt];
+        }
+        __syncthreads();
+        size *= 2;
+    }
+    for (int i = threadIdx.x; i < size; i += blockDim.x) out[i] = buf[i];
+    __syncthreads();
+}
+
+// One block per table: tables[t] = eq(points + t * stride_pts, n_t) with n_t <= 12.
+struct EqJob {
+    const Fp2* point;
+    int n;
+    Fp2 scale;
+    Fp2* out;
+    const Fp2* scale_dev;  // optional device-resident factor
+};
+constexpr int kMaxEqJobs = 96;
+struct EqJobs {
+    EqJob job[kMaxEqJobs];
+    int count;
+};
+
+__global__ void __launch_bounds__(256) eq_small_kernel(EqJobs jobs) {
+    const EqJob j = jobs.job[blockIdx.x];
+    eq_block_build(j.point, j.n, j.scale, j.scale_dev, j.out);
+}
+
+// out[i] = lo[i & (2^lo_bits - 1)] * hi[i >> lo_bits] (+ add[i] if add)
+__global__ void eq_outer_kernel(const Fp2* lo, int lo_bits, const Fp2* hi, size_t total, Fp2* out,
+                                const Fp2* add) {
+    const size_t mask = (size_t{1} << lo_bits) - 1;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        Fp2 v = f2mul(ldg2(lo + (i & mask)), ldg2(hi + (i >> lo_bits)));
+        if (add) v = f2add(v, ldg2(add + i));
+        st2(out + i, v);
+    }
+}
+
+// Full eq table of n coordinates (any n < 48) scaled by `scale`, written to
+// `out`; `tmp` must hold 2^12 + 2^(n-12) entries when n > 12.
+static int eq_table(Context* c, const Fp2* point, int n, Fp2 scale, Fp2* out, Fp2* tmp,
+                    const Fp2* add = nullptr, const Fp2* scale_dev = nullptr) {
+    if (n <= kEqTileBits && !add) {
+        EqJobs jobs{};
+        jobs.job[0] = EqJob{point, n, scale, out, scale_dev};
+        jobs.count = 1;
+        eq_small_kernel<<<1, 256, 0, c->stream>>>(jobs);
+        VZB_LAUNCHED(c);
+        return 0;
+    }
+    const int lo_bits = n < kEqTileBits ? n : kEqTileBits;
+    Fp2* lo = tmp;
+    Fp2* hi = tmp + kEqTile;
+    // low table unscaled; high table (recursively) carries the scale
+    EqJobs jobs{};
+    jobs.job[0] = EqJob{point, lo_bits, Fp2{1, 0}, lo, nullptr};
+    jobs.count = 1;
+    eq_small_kernel<<<1, 256, 0, c->stream>>>(jobs);
+    VZB_LAUNCHED(c);
+    const int hi_bits = n - lo_bits;
+    if (hi_bits <= kEqTileBits) {
+        jobs.job[0] = EqJob{point + lo_bits, hi_bits, scale, hi, scale_dev};
+        eq_small_kernel<<<1, 256, 0, c->stream>>>(jobs);
+        VZB_LAUNCHED(c);
+    } else {
+        if (eq_table(c, point + lo_bits, hi_bits, scale, hi, hi + (size_t{1} << hi_bits), nullptr,
+                     scale_dev))
+            return -1;
+    }
+    const size_t total = size_t{1} << n;
+    eq_outer_kernel<<<grid_for(c, total, 256), 256, 0, c->stream>>>(lo, lo_bits, hi, total, out, add);
+    VZB_LAUNCHED(c);
+    return 0;
+}
+
+// scratch entries eq_table needs for n coordinates
+static size_t eq_tmp_entries(int n) {
+    if (n <= kEqTileBits) return 0;
+    size_t t = kEqTile;
+    int rest = n - kEqTileBits;
+    t += size_t{1} << rest;
+    if (rest > kEqTileBits) t += eq_tmp_entries(rest);
+    return t;
+}
+
+// In-tile subset-sum stages (strides < 2^12) of the Mobius transform.
+__global__ void mobius_tile_kernel(Fp2* v, size_t n) {
+    __shared__ Fp2 tile[kEqTile];
+    const size_t tile_n = n < kEqTile ? n : kEqTile;
+    const size_t base = static_cast<size_t>(blockIdx.x) * tile_n;
+    for (size_t i = threadIdx.x; i < tile_n; i += blockDim.x) tile[i] = v[base + i];
+    __syncthreads();
+    for (size_t stride = 1; stride < tile_n; stride <<= 1) {
+        for (size_t i = threadIdx.x; i < tile_n / 2; i += blockDim.x) {
+            const size_t blk = i / stride, off = i - blk * stride;
+            const size_t low = blk * 2 * stride + off;
+            tile[low + stride] = f2add(tile[low + stride], tile[low]);
+        }
+        __syncthreads();
+    }
+    for (size_t i = threadIdx.x; i < tile_n; i += blockDim.x) v[base + i] = tile[i];
+}
+
+__global__ void mobius_stage_kernel(Fp2* v, size_t pairs, size_t stride) {
+    const size_t gs = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < pairs; i += gs) {
+        const size_t blk = i / stride, off = i - blk * stride;
+        const size_t low = blk * 2 * stride + off;
+        st2(v + low + stride, f2add(ldg2(v + low + stride), ldg2(v + low)));
+    }
+}
+
+// values[i] = rho * eq(point, i) + gamma * (i < source_count ? values[i] : 0)
+__global__ void affine_eq_kernel(Fp2* values, const Fp2* eqv, size_t n, size_t source_count,
+                                 Fp2 rho, Fp2 gamma) {
+    const size_t gs = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += gs) {
+        const Fp2 coef = i < source_count ? ldg2(values + i) : Fp2{0, 0};
+        st2(values + i, f2add(f2mul(rho, ldg2(eqv + i)), f2mul(gamma, coef)));
+    }
+}
+
+__global__ void powers_kernel(Fp2 base, Fp2* out, size_t count) {
+    const size_t gs = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += gs) {
+        // base^(i+1) by square-and-multiply
+        size_t e = i + 1;
+        Fp2 acc{1, 0}, b = base;
+        while (e) {
+            if (e & 1) acc = f2mul(acc, b);
+            b = f2mul(b, b);
+            e >>= 1;
+        }
+        st2(out + i, acc);
+    }
+}
+
+__global__ void __launch_bounds__(256) row_dots_kernel(const Fp2* a, size_t as, const Fp2* b,
+                                                       size_t bs, Fp2* out, size_t rows,
+                                                       size_t len) {
+    for (size_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        Acc<1> acc;
+        acc.zero();
+        for (size_t j = threadIdx.x; j < len; j += blockDim.x)
+            acc.v[0] = f2add(acc.v[0], f2mul(ldg2(a + row * as + j), ldg2(b + row * bs + j)));
+        acc = block_sum<1>(acc);
+        if (threadIdx.x == 0) out[row] = acc.v[0];
+    }
+}
+
+}  // namespace vzb
+
+using namespace vzb;
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+
+namespace {
+
+int resolve_pairs_input(Context* c, uint64_t id, size_t offset, size_t pairs, const Fp2** out) {
+    size_t n = 0;
+    if (!mul_ok(pairs, 2, &n)) return fail_message(c, "resident geometry overflows size_t");
+    void* p = nullptr;
+    if (region_elems(c, id, offset, n, sizeof(Fp2), &p)) return -1;
+    *out = static_cast<const Fp2*>(p);
+    return 0;
+}
+
+int product_round(Context* c, uint64_t a_id, size_t a_off, uint64_t b_id, size_t b_off,
+                  size_t pairs, Fp2* host, uint64_t out_id, size_t out_off, bool scaled, Fp2 scale) {
+    const Fp2 *a = nullptr, *b = nullptr;
+    if (resolve_pairs_input(c, a_id, a_off, pairs, &a) || resolve_pairs_input(c, b_id, b_off, pairs, &b))
+        return -1;
+    Fp2* dev = nullptr;
+    if (!host) {
+        void* p = nullptr;
+        if (region_elems(c, out_id, out_off, 2, sizeof(Fp2), &p)) return -1;
+        dev = static_cast<Fp2*>(p);
+    }
+    const MsgOut o = msg_out(c, dev, host, 2);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (launch_reduce<2>(c, ProductEval{a, b}, pairs, StoreEpi<2>{o.dev, scale, scaled})) return -1;
+    return finish_msg(c, kOpGemm, o);
+}
+
+int triple_round(Context* c, uint64_t a_id, size_t a_off, uint64_t b_id, size_t b_off,
+                 uint64_t c_id, size_t c_off, size_t pairs, Fp2* host, uint64_t out_id,
+                 size_t out_off) {
+    const Fp2 *a = nullptr, *b = nullptr, *cc = nullptr;
+    if (resolve_pairs_input(c, a_id, a_off, pairs, &a) || resolve_pairs_input(c, b_id, b_off, pairs, &b) ||
+        resolve_pairs_input(c, c_id, c_off, pairs, &cc))
+        return -1;
+    Fp2* dev = nullptr;
+    if (!host) {
+        void* p = nullptr;
+        if (region_elems(c, out_id, out_off, 3, sizeof(Fp2), &p)) return -1;
+        dev = static_cast<Fp2*>(p);
+    }
+    const MsgOut o = msg_out(c, dev, host, 3);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (launch_reduce<3>(c, TripleEval{a, b, cc}, pairs, StoreEpi<3>{o.dev, Fp2{1, 0}, false})) return -1;
+    return finish_msg(c, kOpGemm, o);
+}
+
+int logup_round(Context* c, const Fp2* p0, const Fp2* p1, const Fp2* q0, const Fp2* q1,
+                const Fp2* s, size_t pairs, const MsgOut& o) {
+    return launch_reduce<4>(c, LogupEval{p0, p1, q0, q1, s}, pairs,
+                            StoreEpi<4>{o.dev, Fp2{1, 0}, false});
+}
+
+int resolve_logup_inputs(Context* c, uint64_t p0_id, size_t p0_off, uint64_t p1_id, size_t p1_off,
+                         uint64_t q0_id, size_t q0_off, uint64_t q1_id, size_t q1_off,
+                         uint64_t s_id, size_t s_off, size_t pairs, const Fp2** v) {
+    void* s = nullptr;
+    if (resolve_pairs_input(c, p0_id, p0_off, pairs, &v[0]) ||
+        resolve_pairs_input(c, p1_id, p1_off, pairs, &v[1]) ||
+        resolve_pairs_input(c, q0_id, q0_off, pairs, &v[2]) ||
+        resolve_pairs_input(c, q1_id, q1_off, pairs, &v[3]) ||
+        region_elems(c, s_id, s_off, pairs, sizeof(Fp2), &s))
+        return -1;
+    v[4] = static_cast<const Fp2*>(s);
+    return 0;
+}
+
+int launch_fold_rows(Context* c, const Fp2* in, Fp2* out, size_t rows, size_t pairs, Fp2 r) {
+    const size_t total = rows * pairs;
+    fold_rows_kernel<<<grid_for(c, total, 256), 256, 0, c->stream>>>(in, out, rows, pairs, r);
+    VZB_LAUNCHED(c);
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int volta_cuda_reserve_fp2_product_round_workspace(void* raw, size_t max_pairs) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !max_pairs) return reject(c, "invalid product-round workspace reservation");
+    if (c->coarse || c->active_record != kRingSize)
+        return reject(c, "cannot reserve product-round workspace during active timing");
+    // The single-launch reduction needs only the fixed per-block partials
+    // allocated at context creation; nothing grows with max_pairs.
+    return 0;
+}
+
+extern "C" int volta_cuda_reserve_logup_round_workspace(void* raw, size_t max_pairs) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !max_pairs) return reject(c, "invalid LogUp round workspace reservation");
+    if (c->coarse || c->active_record != kRingSize)
+        return reject(c, "cannot reserve LogUp round workspace during active timing");
+    return 0;
+}
+
+extern "C" int volta_cuda_fp2_product_round_device(void* raw, uint64_t a_id, size_t a_off,
+                                                   uint64_t b_id, size_t b_off, size_t pairs,
+                                                   Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs || !output) return fail_message(c, "invalid resident product-round geometry");
+    return product_round(c, a_id, a_off, b_id, b_off, pairs, output, 0, 0, false, Fp2{1, 0});
+}
+
+extern "C" int volta_cuda_fp2_product_round_into_device(void* raw, uint64_t a_id, size_t a_off,
+                                                        uint64_t b_id, size_t b_off, size_t pairs,
+                                                        uint64_t out_id, size_t out_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs) return fail_message(c, "invalid resident product-round mailbox geometry");
+    return product_round(c, a_id, a_off, b_id, b_off, pairs, nullptr, out_id, out_off, false, Fp2{1, 0});
+}
+
+extern "C" int volta_cuda_fp2_product_round_scaled_into_device(void* raw, uint64_t a_id,
+                                                               size_t a_off, uint64_t b_id,
+                                                               size_t b_off, size_t pairs,
+                                                               Fp2 scale, uint64_t out_id,
+                                                               size_t out_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs)
+        return fail_message(c, "invalid resident scaled product-round mailbox geometry");
+    return product_round(c, a_id, a_off, b_id, b_off, pairs, nullptr, out_id, out_off, true, scale);
+}
+
+extern "C" int volta_cuda_fp2_triple_product_round_device(void* raw, uint64_t a_id, size_t a_off,
+                                                          uint64_t b_id, size_t b_off,
+                                                          uint64_t c_id, size_t c_off,
+                                                          size_t pairs, Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs || !output) return fail_message(c, "invalid resident triple-product geometry");
+    return triple_round(c, a_id, a_off, b_id, b_off, c_id, c_off, pairs, output, 0, 0);
+}
+
+extern "C" int volta_cuda_fp2_triple_product_round_into_device(void* raw, uint64_t a_id,
+                                                               size_t a_off, uint64_t b_id,
+                                                               size_t b_off, uint64_t c_id,
+                                                               size_t c_off, size_t pairs,
+                                                               uint64_t out_id, size_t out_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs) return fail_message(c, "invalid resident triple-product mailbox geometry");
+    return triple_round(c, a_id, a_off, b_id, b_off, c_id, c_off, pairs, nullptr, out_id, out_off);
+}
+
+extern "C" int volta_cuda_logup_general_round(void* raw, const Fp2* p0, const Fp2* p1,
+                                              const Fp2* q0, const Fp2* q1, const Fp2* suffix,
+                                              size_t pairs, Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !p0 || !p1 || !q0 || !q1 || !suffix || !output || !pairs) return -1;
+    const size_t vb = 2 * pairs * sizeof(Fp2), sb = pairs * sizeof(Fp2);
+    const int slots[5] = {kWsStageA, kWsStageB, kWsStageC, kWsStageD, kWsStageE};
+    for (int i = 0; i < 5; ++i)
+        if (ensure_ws(c, slots[i], i == 4 ? sb : vb)) return -1;
+    if (op_begin(c)) return -1;
+    const Fp2* src[5] = {p0, p1, q0, q1, suffix};
+    for (int i = 0; i < 5; ++i)
+        VZB_CUDA(c, cudaMemcpyAsync(c->ws[slots[i]].ptr, src[i], i == 4 ? sb : vb,
+                                    cudaMemcpyHostToDevice, c->stream));
+    if (op_mark(c, 1)) return -1;
+    const MsgOut o = msg_out(c, nullptr, output, 4);
+    if (logup_round(c, ws<Fp2>(c, kWsStageA), ws<Fp2>(c, kWsStageB), ws<Fp2>(c, kWsStageC),
+                    ws<Fp2>(c, kWsStageD), ws<Fp2>(c, kWsStageE), pairs, o))
+        return -1;
+    if (op_mark(c, 2)) return -1;
+    if (op_finish(c, kOpLogup, 4 * vb + sb, 4 * sizeof(Fp2))) return -1;
+    std::memcpy(output, c->host_mailbox, 4 * sizeof(Fp2));
+    return 0;
+}
+
+extern "C" int volta_cuda_logup_general_round_device(void* raw, uint64_t p0_id, size_t p0_off,
+                                                     uint64_t p1_id, size_t p1_off,
+                                                     uint64_t q0_id, size_t q0_off,
+                                                     uint64_t q1_id, size_t q1_off,
+                                                     uint64_t s_id, size_t s_off, size_t pairs,
+                                                     Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs || !output) return fail_message(c, "invalid resident LogUp round geometry");
+    const Fp2* v[5];
+    if (resolve_logup_inputs(c, p0_id, p0_off, p1_id, p1_off, q0_id, q0_off, q1_id, q1_off, s_id,
+                             s_off, pairs, v))
+        return -1;
+    const MsgOut o = msg_out(c, nullptr, output, 4);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (logup_round(c, v[0], v[1], v[2], v[3], v[4], pairs, o)) return -1;
+    return finish_msg(c, kOpLogup, o);
+}
+
+extern "C" int volta_cuda_logup_general_round_into_device(void* raw, uint64_t p0_id, size_t p0_off,
+                                                          uint64_t p1_id, size_t p1_off,
+                                                          uint64_t q0_id, size_t q0_off,
+                                                          uint64_t q1_id, size_t q1_off,
+                                                          uint64_t s_id, size_t s_off,
+                                                          size_t pairs, uint64_t out_id,
+                                                          size_t out_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs) return fail_message(c, "invalid resident LogUp round mailbox geometry");
+    const Fp2* v[5];
+    void* out = nullptr;
+    if (resolve_logup_inputs(c, p0_id, p0_off, p1_id, p1_off, q0_id, q0_off, q1_id, q1_off, s_id,
+                             s_off, pairs, v) ||
+        region_elems(c, out_id, out_off, 4, sizeof(Fp2), &out))
+        return -1;
+    const MsgOut o = msg_out(c, static_cast<Fp2*>(out), nullptr, 4);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (logup_round(c, v[0], v[1], v[2], v[3], v[4], pairs, o)) return -1;
+    return finish_msg(c, kOpLogup, o);
+}
+
+extern "C" int volta_cuda_logup_fold4(void* raw, const Fp2* p0, const Fp2* p1, const Fp2* q0,
+                                      const Fp2* q1, size_t pairs, Fp2 r, Fp2* o0, Fp2* o1,
+                                      Fp2* o2, Fp2* o3) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !p0 || !p1 || !q0 || !q1 || !o0 || !o1 || !o2 || !o3 || !pairs) return -1;
+    const size_t ib = 2 * pairs * sizeof(Fp2), ob = pairs * sizeof(Fp2);
+    const int in_slots[4] = {kWsStageA, kWsStageB, kWsStageC, kWsStageD};
+    const int out_slots[4] = {kWsStageE, kWsStageF, kWsStageG, kWsStageH};
+    for (int i = 0; i < 4; ++i)
+        if (ensure_ws(c, in_slots[i], ib) || ensure_ws(c, out_slots[i], ob)) return -1;
+    if (op_begin(c)) return -1;
+    const Fp2* src[4] = {p0, p1, q0, q1};
+    for (int i = 0; i < 4; ++i)
+        VZB_CUDA(c, cudaMemcpyAsync(c->ws[in_slots[i]].ptr, src[i], ib, cudaMemcpyHostToDevice, c->stream));
+    if (op_mark(c, 1)) return -1;
+    Quad q{};
+    for (int i = 0; i < 4; ++i) {
+        q.in[i] = ws<Fp2>(c, in_slots[i]);
+        q.out[i] = ws<Fp2>(c, out_slots[i]);
+    }
+    fold4_kernel<<<grid_for(c, pairs, 256), 256, 0, c->stream>>>(q, pairs, r);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    Fp2* dst[4] = {o0, o1, o2, o3};
+    for (int i = 0; i < 4; ++i)
+        VZB_CUDA(c, cudaMemcpyAsync(dst[i], q.out[i], ob, cudaMemcpyDeviceToHost, c->stream));
+    return op_finish(c, kOpLogup, 4 * ib, 4 * ob);
+}
+
+extern "C" int volta_cuda_logup_fold4_device(void* raw, uint64_t p0_id, size_t p0_off,
+                                             uint64_t p1_id, size_t p1_off, uint64_t q0_id,
+                                             size_t q0_off, uint64_t q1_id, size_t q1_off,
+                                             size_t pairs, Fp2 r, uint64_t o0_id, size_t o0_off,
+                                             uint64_t o1_id, size_t o1_off, uint64_t o2_id,
+                                             size_t o2_off, uint64_t o3_id, size_t o3_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs) return fail_message(c, "invalid resident LogUp fold geometry");
+    const uint64_t ii[4] = {p0_id, p1_id, q0_id, q1_id};
+    const size_t io[4] = {p0_off, p1_off, q0_off, q1_off};
+    const uint64_t oi[4] = {o0_id, o1_id, o2_id, o3_id};
+    const size_t oo[4] = {o0_off, o1_off, o2_off, o3_off};
+    Quad q{};
+    for (int i = 0; i < 4; ++i) {
+        void* out = nullptr;
+        if (resolve_pairs_input(c, ii[i], io[i], pairs, &q.in[i]) ||
+            region_elems(c, oi[i], oo[i], pairs, sizeof(Fp2), &out))
+            return -1;
+        q.out[i] = static_cast<Fp2*>(out);
+    }
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    fold4_kernel<<<grid_for(c, pairs, 256), 256, 0, c->stream>>>(q, pairs, r);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpLogup, 0, 0);
+}
+
+extern "C" int volta_cuda_fp2_deinterleave_device(void* raw, uint64_t in_id, size_t in_off,
+                                                  size_t pairs, uint64_t even_id, size_t even_off,
+                                                  uint64_t odd_id, size_t odd_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs) return fail_message(c, "invalid resident deinterleave geometry");
+    const Fp2* in = nullptr;
+    void *even = nullptr, *odd = nullptr;
+    if (resolve_pairs_input(c, in_id, in_off, pairs, &in) ||
+        region_elems(c, even_id, even_off, pairs, sizeof(Fp2), &even) ||
+        region_elems(c, odd_id, odd_off, pairs, sizeof(Fp2), &odd))
+        return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    deinterleave_kernel<<<grid_for(c, pairs, 256), 256, 0, c->stream>>>(
+        in, static_cast<Fp2*>(even), static_cast<Fp2*>(odd), pairs);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpLogup, 0, 0);
+}
+
+// Suffix tables: table k (2^k entries, eq over the last k coordinates) at
+// offset 2^k - 1, k = 0 .. L-1 (logup.rs:284-305).
+extern "C" int volta_cuda_logup_suffix_eq_device(void* raw, uint64_t points_id, size_t points_off,
+                                                 size_t point_len, uint64_t out_id, size_t out_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !point_len || point_len >= 63) return fail_message(c, "invalid resident suffix-eq geometry");
+    const size_t total = (size_t{1} << point_len) - 1;
+    void *pts = nullptr, *out = nullptr;
+    if (region_elems(c, points_id, points_off, point_len, sizeof(Fp2), &pts) ||
+        region_elems(c, out_id, out_off, total, sizeof(Fp2), &out))
+        return -1;
+    const Fp2* point = static_cast<const Fp2*>(pts);
+    Fp2* o = static_cast<Fp2*>(out);
+    const int L = static_cast<int>(point_len);
+    // tables with k <= 12 come from one multi-job launch; larger tables are
+    // outer products of their low 12 coordinates and the table k - 12.
+    size_t tmp_entries = 0;
+    for (int k = kEqTileBits + 1; k < L; ++k) tmp_entries += kEqTile;
+    if (tmp_entries && ensure_ws(c, kWsScratch, tmp_entries * sizeof(Fp2))) return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    EqJobs jobs{};
+    for (int k = 0; k < L && k <= kEqTileBits; ++k) {
+        jobs.job[jobs.count++] = EqJob{point + (L - k), k, Fp2{1, 0}, o + ((size_t{1} << k) - 1), nullptr};
+    }
+    Fp2* lows = ws<Fp2>(c, kWsScratch);
+    for (int k = kEqTileBits + 1; k < L; ++k) {
+        if (jobs.count == kMaxEqJobs) return fail_message(c, "suffix-eq job table overflow");
+        jobs.job[jobs.count++] =
+            EqJob{point + (L - k), kEqTileBits, Fp2{1, 0}, lows + static_cast<size_t>(k - kEqTileBits - 1) * kEqTile, nullptr};
+    }
+    eq_small_kernel<<<jobs.count, 256, 0, c->stream>>>(jobs);
+    VZB_LAUNCHED(c);
+    // bands of 12 levels so that table k - 12 is complete before table k
+    for (int band = kEqTileBits + 1; band < L; band += kEqTileBits) {
+        for (int k = band; k < L && k < band + kEqTileBits; ++k) {
+            const size_t entries = size_t{1} << k;
+            eq_outer_kernel<<<grid_for(c, entries, 256), 256, 0, c->stream>>>(
+                lows + static_cast<size_t>(k - kEqTileBits - 1) * kEqTile, kEqTileBits,
+                o + ((size_t{1} << (k - kEqTileBits)) - 1), entries, o + (entries - 1), nullptr);
+            VZB_LAUNCHED(c);
+        }
+    }
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpLogup, 0, 0);
+}
+
+extern "C" int volta_cuda_fp2_fold_rows_device(void* raw, uint64_t in_id, size_t in_off,
+                                               size_t rows, size_t len, Fp2 r, uint64_t out_id,
+                                               size_t out_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !rows || len < 2 || (len & 1)) return fail_message(c, "invalid resident row-fold geometry");
+    const size_t pairs = len / 2;
+    size_t n_in = 0, n_out = 0;
+    if (!mul_ok(rows, len, &n_in) || !mul_ok(rows, pairs, &n_out))
+        return fail_message(c, "resident row-fold geometry overflows size_t");
+    void *in = nullptr, *out = nullptr;
+    if (region_elems(c, in_id, in_off, n_in, sizeof(Fp2), &in) ||
+        region_elems(c, out_id, out_off, n_out, sizeof(Fp2), &out))
+        return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (launch_fold_rows(c, static_cast<const Fp2*>(in), static_cast<Fp2*>(out), rows, pairs, r)) return -1;
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpLogup, 0, 0);
+}
+
+extern "C" int volta_cuda_logup_eq_rows_device(void* raw, uint64_t points_id, size_t points_off,
+                                               size_t rows, size_t dims, uint64_t out_id,
+                                               size_t out_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !rows || dims >= 63 || (dims && !points_id))
+        return fail_message(c, "invalid resident eq-row geometry");
+    const size_t width = size_t{1} << dims;
+    size_t total = 0;
+    if (!mul_ok(rows, width, &total)) return fail_message(c, "resident eq-row geometry overflows size_t");
+    void *pts = nullptr, *out = nullptr;
+    if ((dims && region_elems(c, points_id, points_off, rows * dims, sizeof(Fp2), &pts)) ||
+        region_elems(c, out_id, out_off, total, sizeof(Fp2), &out))
+        return -1;
+    const Fp2* point = static_cast<const Fp2*>(pts);
+    Fp2* o = static_cast<Fp2*>(out);
+    const size_t tmp = eq_tmp_entries(static_cast<int>(dims));
+    if (tmp && ensure_ws(c, kWsScratch, tmp * sizeof(Fp2))) return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (dims <= static_cast<size_t>(kEqTileBits)) {
+        for (size_t r0 = 0; r0 < rows; r0 += kMaxEqJobs) {
+            EqJobs jobs{};
+            for (size_t r = r0; r < rows && jobs.count < kMaxEqJobs; ++r)
+                jobs.job[jobs.count++] = EqJob{point + r * dims, static_cast<int>(dims), Fp2{1, 0}, o + r * width, nullptr};
+            eq_small_kernel<<<jobs.count, 256, 0, c->stream>>>(jobs);
+            VZB_LAUNCHED(c);
+        }
+    } else {
+        for (size_t r = 0; r < rows; ++r)
+            if (eq_table(c, point + r * dims, static_cast<int>(dims), Fp2{1, 0}, o + r * width,
+                         ws<Fp2>(c, kWsScratch)))
+                return -1;
+    }
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpLogup, 0, 0);
+}
+
+namespace {
+
+int aux_round(Context* c, uint64_t q0_id, size_t q0_off, uint64_t q1_id, size_t q1_off,
+              uint64_t s_id, size_t s_off, uint64_t col_id, size_t col_off, uint64_t eq_id,
+              size_t eq_off, uint64_t cc_id, size_t cc_off, uint64_t w_id, size_t w_off,
+              size_t column_count, size_t claim_count, size_t vector_len, Fp2 lambda, Fp2 cpref,
+              Fp2 point, Fp2* host, uint64_t out_id, size_t out_off) {
+    const size_t pairs = vector_len / 2;
+    void *q0 = nullptr, *q1 = nullptr, *s = nullptr, *cols = nullptr;
+    void *eq = nullptr, *cc = nullptr, *w = nullptr;
+    size_t col_n = 0, eq_n = 0;
+    if (!mul_ok(column_count, vector_len, &col_n) || !mul_ok(col_n, 2, &col_n) ||
+        !mul_ok(claim_count, vector_len, &eq_n))
+        return fail_message(c, "resident aux-round geometry overflows size_t");
+    if (region_elems(c, q0_id, q0_off, vector_len, sizeof(Fp2), &q0) ||
+        region_elems(c, q1_id, q1_off, vector_len, sizeof(Fp2), &q1) ||
+        region_elems(c, s_id, s_off, pairs, sizeof(Fp2), &s) ||
+        region_elems(c, col_id, col_off, col_n, sizeof(Fp2), &cols))
+        return -1;
+    if (claim_count &&
+        (region_elems(c, eq_id, eq_off, eq_n, sizeof(Fp2), &eq) ||
+         region_elems(c, cc_id, cc_off, claim_count, sizeof(uint32_t), &cc) ||
+         region_elems(c, w_id, w_off, 2 * claim_count, sizeof(Fp2), &w)))
+        return -1;
+    Fp2* dev = nullptr;
+    if (!host) {
+        void* p = nullptr;
+        if (region_elems(c, out_id, out_off, 3, sizeof(Fp2), &p)) return -1;
+        dev = static_cast<Fp2*>(p);
+    }
+    const MsgOut o = msg_out(c, dev, host, 3);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    AuxEval ev{static_cast<const Fp2*>(q0), static_cast<const Fp2*>(q1), static_cast<const Fp2*>(s),
+               static_cast<const Fp2*>(cols), static_cast<const Fp2*>(eq), static_cast<const Fp2*>(w),
+               static_cast<const uint32_t*>(cc), column_count, claim_count, vector_len};
+    if (launch_reduce<9>(c, ev, pairs, AuxEpi{o.dev, lambda, cpref, point}, 2)) return -1;
+    return finish_msg(c, kOpLogup, o);
+}
+
+}  // namespace
+
+extern "C" int volta_cuda_logup_aux_round_device(
+    void* raw, uint64_t q0_id, size_t q0_off, uint64_t q1_id, size_t q1_off, uint64_t s_id,
+    size_t s_off, uint64_t col_id, size_t col_off, uint64_t eq_id, size_t eq_off, uint64_t cc_id,
+    size_t cc_off, uint64_t w_id, size_t w_off, size_t column_count, size_t claim_count,
+    size_t vector_len, Fp2 lambda, Fp2 cpref, Fp2 point, Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !output || !column_count || vector_len < 2 || (vector_len & 1))
+        return fail_message(c, "invalid resident aux-round geometry");
+    return aux_round(c, q0_id, q0_off, q1_id, q1_off, s_id, s_off, col_id, col_off, eq_id, eq_off,
+                     cc_id, cc_off, w_id, w_off, column_count, claim_count, vector_len, lambda,
+                     cpref, point, output, 0, 0);
+}
+
+extern "C" int volta_cuda_logup_aux_round_into_device(
+    void* raw, uint64_t q0_id, size_t q0_off, uint64_t q1_id, size_t q1_off, uint64_t s_id,
+    size_t s_off, uint64_t col_id, size_t col_off, uint64_t eq_id, size_t eq_off, uint64_t cc_id,
+    size_t cc_off, uint64_t w_id, size_t w_off, size_t column_count, size_t claim_count,
+    size_t vector_len, Fp2 lambda, Fp2 cpref, Fp2 point, uint64_t out_id, size_t out_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !column_count || vector_len < 2 || (vector_len & 1))
+        return fail_message(c, "invalid resident aux-round mailbox geometry");
+    return aux_round(c, q0_id, q0_off, q1_id, q1_off, s_id, s_off, col_id, col_off, eq_id, eq_off,
+                     cc_id, cc_off, w_id, w_off, column_count, claim_count, vector_len, lambda,
+                     cpref, point, nullptr, out_id, out_off);
+}
+
+extern "C" int volta_cuda_fp2_dot_device(void* raw, uint64_t a_id, size_t a_off, uint64_t b_id,
+                                         size_t b_off, size_t n, Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !n || !output) return fail_message(c, "invalid resident Fp2 dot geometry");
+    void *a = nullptr, *b = nullptr;
+    if (region_elems(c, a_id, a_off, n, sizeof(Fp2), &a) || region_elems(c, b_id, b_off, n, sizeof(Fp2), &b))
+        return -1;
+    const MsgOut o = msg_out(c, nullptr, output, 1);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (launch_reduce<1>(c, DotEval{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b)}, n,
+                         StoreEpi<1>{o.dev, Fp2{1, 0}, false}))
+        return -1;
+    return finish_msg(c, kOpGemm, o);
+}
+
+extern "C" int volta_cuda_fp2_dot_scaled_pair_into_device(void* raw, uint64_t a_id, size_t a_off,
+                                                          uint64_t b_id, size_t b_off, size_t n,
+                                                          Fp2 scale, uint64_t out_id,
+                                                          size_t out_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !n) return fail_message(c, "invalid X4d scaled-dot geometry");
+    void *a = nullptr, *b = nullptr, *out = nullptr;
+    if (region_elems(c, a_id, a_off, n, sizeof(Fp2), &a) || region_elems(c, b_id, b_off, n, sizeof(Fp2), &b) ||
+        region_elems(c, out_id, out_off, 2, sizeof(Fp2), &out))
+        return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (launch_reduce<1>(c, DotEval{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b)}, n,
+                         ScaledPairEpi{static_cast<Fp2*>(out), scale}))
+        return -1;
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpGemm, 0, 0);
+}
+
+extern "C" int volta_cuda_fp2_pair_sum_device(void* raw, uint64_t in_id, size_t in_off, size_t pairs,
+                                              Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs || !output) return fail_message(c, "invalid X4d pair-mailbox geometry");
+    size_t off = 0;
+    if (!mul_ok(in_off, 2, &off)) return fail_message(c, "X4d pair geometry overflows size_t");
+    const Fp2* in = nullptr;
+    if (resolve_pairs_input(c, in_id, off, pairs, &in)) return -1;
+    const MsgOut o = msg_out(c, nullptr, output, 2);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (launch_reduce<2>(c, PairSumEval{in}, pairs, StoreEpi<2>{o.dev, Fp2{1, 0}, false})) return -1;
+    return finish_msg(c, kOpGemm, o);
+}
+
+extern "C" int volta_cuda_claim_reduce_f_two_into_device(
+    void* raw, uint64_t points_id, size_t points_off, size_t n_vars, uint64_t out_id,
+    size_t out_off, uint64_t s1_id, size_t s1_off, uint64_t s2_id, size_t s2_off, uint64_t s3_id,
+    size_t s3_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !n_vars || n_vars > 30) return fail_message(c, "invalid ClaimReduce F geometry");
+    const size_t len = size_t{1} << n_vars;
+    void *pts = nullptr, *out = nullptr, *s1 = nullptr, *s2 = nullptr, *s3 = nullptr;
+    if (region_elems(c, points_id, points_off, 2 * n_vars + 2, sizeof(Fp2), &pts) ||
+        region_elems(c, out_id, out_off, len, sizeof(Fp2), &out) ||
+        region_elems(c, s1_id, s1_off, len, sizeof(Fp2), &s1) ||
+        region_elems(c, s2_id, s2_off, len, sizeof(Fp2), &s2) ||
+        region_elems(c, s3_id, s3_off, len, sizeof(Fp2), &s3))
+        return -1;
+    const Fp2* p = static_cast<const Fp2*>(pts);
+    // out = s1 * eq(p[0..n)) + s2 * eq(p[n..2n)); the scales p[2n], p[2n+1]
+    // stay on the device and are read inside the table kernels.
+    const size_t tmp = eq_tmp_entries(static_cast<int>(n_vars));
+    if (tmp && ensure_ws(c, kWsScratch, tmp * sizeof(Fp2))) return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    Fp2* second = static_cast<Fp2*>(s2);
+    if (eq_table(c, p + n_vars, static_cast<int>(n_vars), Fp2{1, 0}, second, ws<Fp2>(c, kWsScratch),
+                 nullptr, p + 2 * n_vars + 1))
+        return -1;
+    if (n_vars <= static_cast<size_t>(kEqTileBits)) {
+        if (eq_table(c, p, static_cast<int>(n_vars), Fp2{1, 0}, static_cast<Fp2*>(s1),
+                     ws<Fp2>(c, kWsScratch), nullptr, p + 2 * n_vars))
+            return -1;
+        add_inplace_kernel<<<1, 256, 0, c->stream>>>(static_cast<Fp2*>(s1), second, len);
+        VZB_LAUNCHED(c);
+        VZB_CUDA(c, cudaMemcpyAsync(out, s1, len * sizeof(Fp2), cudaMemcpyDeviceToDevice, c->stream));
+    } else if (eq_table(c, p, static_cast<int>(n_vars), Fp2{1, 0}, static_cast<Fp2*>(out),
+                        ws<Fp2>(c, kWsScratch), second, p + 2 * n_vars)) {
+        return -1;
+    }
+    (void)s3;
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpGemm, 0, 0);
+}
+
+extern "C" int volta_cuda_x4d_link_eq_accumulate_device(void* raw, uint64_t point_id,
+                                                        size_t point_off, size_t n_vars,
+                                                        uint64_t target_id, size_t target_off,
+                                                        uint64_t s1_id, size_t s1_off,
+                                                        uint64_t s2_id, size_t s2_off,
+                                                        int initialize) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !n_vars || n_vars > 30 || (initialize != 0 && initialize != 1))
+        return fail_message(c, "invalid X4d link-equality geometry");
+    const size_t len = size_t{1} << n_vars;
+    void *pt = nullptr, *target = nullptr, *s1 = nullptr, *s2 = nullptr;
+    if (region_elems(c, point_id, point_off, n_vars + 1, sizeof(Fp2), &pt) ||
+        region_elems(c, target_id, target_off, len, sizeof(Fp2), &target) ||
+        region_elems(c, s1_id, s1_off, len, sizeof(Fp2), &s1) ||
+        region_elems(c, s2_id, s2_off, len, sizeof(Fp2), &s2))
+        return -1;
+    const Fp2* p = static_cast<const Fp2*>(pt);
+    const size_t tmp = eq_tmp_entries(static_cast<int>(n_vars));
+    if (tmp && ensure_ws(c, kWsScratch, tmp * sizeof(Fp2))) return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    const Fp2 scale{1, 0};
+    Fp2* contrib = static_cast<Fp2*>(s1);
+    if (eq_table(c, p, static_cast<int>(n_vars), scale, contrib, ws<Fp2>(c, kWsScratch), nullptr,
+                 p + n_vars))
+        return -1;
+    if (initialize) {
+        VZB_CUDA(c, cudaMemcpyAsync(target, contrib, len * sizeof(Fp2), cudaMemcpyDeviceToDevice, c->stream));
+    } else {
+        add_inplace_kernel<<<grid_for(c, len, 256), 256, 0, c->stream>>>(static_cast<Fp2*>(target), contrib, len);
+        VZB_LAUNCHED(c);
+    }
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpGemm, 0, 0);
+}
+
+extern "C" int volta_cuda_fp2_add_inplace_device(void* raw, uint64_t t_id, size_t t_off,
+                                                 uint64_t a_id, size_t a_off, size_t n) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !n) return fail_message(c, "invalid resident Fp2 add");
+    void *t = nullptr, *a = nullptr;
+    if (region_elems(c, t_id, t_off, n, sizeof(Fp2), &t) || region_elems(c, a_id, a_off, n, sizeof(Fp2), &a))
+        return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    add_inplace_kernel<<<grid_for(c, n, 256), 256, 0, c->stream>>>(static_cast<Fp2*>(t),
+                                                                   static_cast<const Fp2*>(a), n);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsRows, 0, 0);
+}
+
+extern "C" int volta_cuda_fp2_mobius_inverse_inplace_device(void* raw, uint64_t v_id, size_t v_off,
+                                                            size_t n) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !n || (n & (n - 1))) return fail_message(c, "invalid resident Fp2 Mobius inverse");
+    void* v = nullptr;
+    if (region_elems(c, v_id, v_off, n, sizeof(Fp2), &v)) return -1;
+    Fp2* values = static_cast<Fp2*>(v);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (n > 1) {
+        const size_t tile = n < kEqTile ? n : kEqTile;
+        mobius_tile_kernel<<<static_cast<unsigned>(n / tile), 256, 0, c->stream>>>(values, n);
+        VZB_LAUNCHED(c);
+        for (size_t stride = tile; stride < n; stride <<= 1) {
+            mobius_stage_kernel<<<grid_for(c, n / 2, 256), 256, 0, c->stream>>>(values, n / 2, stride);
+            VZB_LAUNCHED(c);
+        }
+    }
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsRows, 0, 0);
+}
+
+extern "C" int volta_cuda_fp2_affine_eq_weights_inplace_device(void* raw, uint64_t v_id, size_t n,
+                                                               size_t source_count,
+                                                               uint64_t point_id, size_t point_off,
+                                                               size_t point_len, uint64_t rho_c0,
+                                                               uint64_t rho_c1, uint64_t gamma_c0,
+                                                               uint64_t gamma_c1) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !n || (n & (n - 1)) || !point_len || point_len >= 8 * sizeof(size_t) ||
+        n != (size_t{1} << point_len) || source_count > n)
+        return fail_message(c, "invalid resident Fp2 affine equality weights");
+    void *v = nullptr, *pt = nullptr;
+    if (region(c, v_id, 0, n * sizeof(Fp2), &v) ||
+        region_elems(c, point_id, point_off, point_len, sizeof(Fp2), &pt))
+        return -1;
+    const size_t tmp = eq_tmp_entries(static_cast<int>(point_len)) + n;
+    if (ensure_ws(c, kWsScratch2, tmp * sizeof(Fp2))) return -1;
+    Fp2* eqv = ws<Fp2>(c, kWsScratch2);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (eq_table(c, static_cast<const Fp2*>(pt), static_cast<int>(point_len), Fp2{1, 0}, eqv, eqv + n)) return -1;
+    affine_eq_kernel<<<grid_for(c, n, 256), 256, 0, c->stream>>>(static_cast<Fp2*>(v), eqv, n, source_count,
+                                                                 Fp2{rho_c0, rho_c1}, Fp2{gamma_c0, gamma_c1});
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsRows, 0, 0);
+}
+
+extern "C" int volta_cuda_fp2_row_dots_device(void* raw, uint64_t a_id, size_t a_off, size_t a_stride,
+                                              uint64_t b_id, size_t b_off, size_t b_stride,
+                                              uint64_t out_id, size_t out_off, size_t rows,
+                                              size_t len) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !rows || !len || a_stride < len || b_stride < len)
+        return fail_message(c, "invalid Fp2 row-dot geometry");
+    size_t aob = 0, asb = 0, bob = 0, bsb = 0, oob = 0, ob = 0, rb = 0;
+    if (!mul_ok(a_off, sizeof(Fp2), &aob) || !mul_ok(a_stride, sizeof(Fp2), &asb) ||
+        !mul_ok(b_off, sizeof(Fp2), &bob) || !mul_ok(b_stride, sizeof(Fp2), &bsb) ||
+        !mul_ok(out_off, sizeof(Fp2), &oob) || !mul_ok(len, sizeof(Fp2), &rb) ||
+        !mul_ok(rows, sizeof(Fp2), &ob))
+        return fail_message(c, "Fp2 row-dot geometry overflows size_t");
+    void *a = nullptr, *b = nullptr, *out = nullptr;
+    size_t aspan = 0, bspan = 0;
+    if (strided_region(c, a_id, aob, asb, rb, rows, &a, &aspan) ||
+        strided_region(c, b_id, bob, bsb, rb, rows, &b, &bspan) || region(c, out_id, oob, ob, &out))
+        return -1;
+    size_t oe = 0, ae = 0, be = 0;
+    if (!add_ok(oob, ob, &oe) || !add_ok(aob, aspan, &ae) || !add_ok(bob, bspan, &be))
+        return fail_message(c, "Fp2 row-dot envelope overflows size_t");
+    if ((out_id == a_id && oob < ae && aob < oe) || (out_id == b_id && oob < be && bob < oe))
+        return fail_message(c, "Fp2 row-dot output overlaps an input");
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    const unsigned blocks = static_cast<unsigned>(std::min<size_t>(rows, 65535));
+    row_dots_kernel<<<blocks, 256, 0, c->stream>>>(static_cast<const Fp2*>(a), a_stride,
+                                                   static_cast<const Fp2*>(b), b_stride,
+                                                   static_cast<Fp2*>(out), rows, len);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsRows, 0, 0);
+}
+
+extern "C" int volta_cuda_fp2_powers_device(void* raw, uint64_t base_c0, uint64_t base_c1,
+                                            uint64_t out_id, size_t out_off, size_t count) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !count || base_c0 >= kP || base_c1 >= kP) return fail_message(c, "invalid Fp2 powers input");
+    void* out = nullptr;
+    if (region_elems(c, out_id, out_off, count, sizeof(Fp2), &out)) return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    powers_kernel<<<grid_for(c, count, 256), 256, 0, c->stream>>>(Fp2{base_c0, base_c1},
+                                                                  static_cast<Fp2*>(out), count);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsRows, 0, 0, 0, 0, count * sizeof(Fp2));
+}

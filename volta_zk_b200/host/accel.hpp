@@ -1,0 +1,122 @@
+// Host side above the C ABI: a C++ restatement of the reference's Rust seam
+// `volta_accel::Backend` for the resident CUDA backend and of the protocol
+// callers on the hot path.
+//
+//   loader         rust/volta-accel/src/cuda.rs:1119-1420 (dlopen of
+//                  $VOLTA_CUDA_LIBRARY or the in-package library, ABI version
+//                  check, eager resolution of all 124 symbols)
+//   Backend        rust/volta-accel/src/lib.rs:986-1640 (cuda_resident with a
+//                  timing policy, typed device buffers, segment downloads)
+//   FpStream       rust/volta-field/src/lib.rs:222-268
+//   Transcript     rust/volta-mac/src/transcript.rs:84-103, 563-590 (private
+//                  challenge mode: FpStream(seed, u64::MAX))
+//
+// Errors are reported as AccelError exceptions carrying the backend's
+// last_error text; nothing falls back to the CPU.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#ifndef __CUDACC__
+#define __host__
+#define __device__
+#define __forceinline__ inline
+#endif
+#include "../csrc/field.cuh"
+
+namespace vzh {
+
+using vzb::Fp2;
+
+struct AccelError : std::runtime_error {
+    explicit AccelError(const std::string& m) : std::runtime_error(m) {}
+};
+
+// ---- host FpStream (ChaCha8Rng, rand_chacha 0.3.1 layout) ----------------
+class FpStream {
+   public:
+    FpStream(const uint8_t seed[32], uint64_t domain);
+    uint64_t next_u64();
+    uint64_t next_fp();
+    Fp2 next_fp2() {
+        const uint64_t a = next_fp();
+        const uint64_t b = next_fp();
+        return Fp2{a, b};
+    }
+    uint64_t next_bits(unsigned width) {
+        const uint64_t raw = next_u64();
+        return width >= 64 ? raw : raw & ((uint64_t{1} << width) - 1);
+    }
+
+   private:
+    uint32_t key_[8];
+    uint64_t stream_, counter_ = 0;
+    uint32_t words_[16];
+    unsigned idx_ = 8;
+};
+
+// ---- the loaded C ABI ------------------------------------------------------
+struct Api;  // function table, defined in accel.cpp
+
+enum class TimingPolicy { DeferredEvents = 0, WallOnlyCounters = 1 };
+
+enum Operation : int { kGemm = 0, kLogup = 1, kPcsRows = 2, kPcsNtt = 3, kPcsMerkle = 4,
+                       kAuthMasks = 5, kMailbox = 6 };
+
+class Backend {
+   public:
+    // Load the library (path, else $VOLTA_CUDA_LIBRARY, else the in-package
+    // libvolta_cuda_backend.so) and create a resident context.
+    explicit Backend(const std::string& library, TimingPolicy policy);
+    ~Backend();
+    Backend(const Backend&) = delete;
+    Backend& operator=(const Backend&) = delete;
+
+    const Api& api() const { return *api_; }
+    void* ctx() const { return ctx_; }
+    [[noreturn]] void raise(const char* what) const;
+    void check(int rc, const char* what) const {
+        if (rc != 0) raise(what);
+    }
+
+    // typed device buffers: id + element count
+    uint64_t alloc(size_t bytes);
+    void free(uint64_t id);
+    void upload(uint64_t id, size_t offset_bytes, const void* src, size_t bytes);
+    void download(uint64_t id, size_t offset_bytes, void* dst, size_t bytes);
+    // one mailbox download of several Fp2 slices (lib.rs:1523-1577)
+    std::vector<Fp2> download_fp2_segments(const std::vector<std::pair<uint64_t, size_t>>& elems);
+
+    vz_raw_stats stats();
+    void reset_stats();
+
+   private:
+    void* handle_ = nullptr;
+    Api* api_ = nullptr;
+    void* ctx_ = nullptr;
+};
+
+// ---- protocol drivers (resident) -------------------------------------------
+
+// Triple-product sumcheck over three device tables of n = 2^k Fp2 entries
+// (hadamard.rs:186-260 device calls, clear messages).  The input buffers are
+// not modified.  Returns 3*k round messages and the three final openings.
+struct TripleResult {
+    std::vector<Fp2> messages;
+    Fp2 finals[3];
+};
+TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
+                                      FpStream& tx);
+
+// LogUp (logup.rs:1760-1771, resident engine 995-1470): queries and table are
+// device columns of canonical Fp values (n_f and n_t entries, powers of two),
+// mult a device u32 column of n_t multiplicities.  Appends the flat proof
+// (alpha, per side root_p, root_q, per layer rounds (h0, h2) and splits).
+std::vector<Fp2> logup_prove_resident(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col,
+                                      size_t n_t, uint64_t mult, FpStream& chal);
+
+}  // namespace vzh

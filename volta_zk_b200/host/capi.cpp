@@ -1,0 +1,92 @@
+// C entry points of libvolta_accel.so (the host mirror) for Python/ctypes.
+// Every function returns 0 on success, -1 on failure with the message copied
+// into `err` (no exception crosses the C boundary).
+#include <cstring>
+#include <exception>
+#include <string>
+
+#include "accel.hpp"
+#include "api.hpp"
+
+using namespace vzh;
+
+namespace {
+int fail(char* err, size_t len, const char* msg) {
+    if (err && len) {
+        std::strncpy(err, msg, len - 1);
+        err[len - 1] = 0;
+    }
+    return -1;
+}
+template <class F>
+int guarded(char* err, size_t len, F&& f) {
+    try {
+        f();
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(err, len, e.what());
+    } catch (...) {
+        return fail(err, len, "unknown C++ exception");
+    }
+}
+}  // namespace
+
+extern "C" {
+
+// policy: 0 deferred CUDA events, 1 wall-only counters (lib.rs:1009-1044)
+void* vzh_open(const char* library, int policy, char* err, size_t len) {
+    try {
+        return new Backend(library ? library : "", policy ? TimingPolicy::WallOnlyCounters
+                                                          : TimingPolicy::DeferredEvents);
+    } catch (const std::exception& e) {
+        fail(err, len, e.what());
+    } catch (...) {
+        fail(err, len, "unknown C++ exception");
+    }
+    return nullptr;
+}
+
+void vzh_close(void* h) { delete static_cast<Backend*>(h); }
+
+void* vzh_context(void* h) { return static_cast<Backend*>(h)->ctx(); }
+
+int vzh_stats(void* h, vz_raw_stats* out, char* err, size_t len) {
+    return guarded(err, len, [&] { *out = static_cast<Backend*>(h)->stats(); });
+}
+
+int vzh_reset_stats(void* h, char* err, size_t len) {
+    return guarded(err, len, [&] { static_cast<Backend*>(h)->reset_stats(); });
+}
+
+// Triple-product sumcheck on three resident tables of n Fp2 entries;
+// challenges from FpStream(seed, u64::MAX) (a private Transcript).
+int vzh_triple_sumcheck(void* h, uint64_t a, uint64_t b, uint64_t c, size_t n, const uint8_t* seed,
+                        vz_fp2* messages, vz_fp2* finals, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        FpStream tx(seed, UINT64_MAX);
+        TripleResult r = triple_sumcheck_resident(*static_cast<Backend*>(h), a, b, c, n, tx);
+        std::memcpy(messages, r.messages.data(), r.messages.size() * sizeof(vz_fp2));
+        std::memcpy(finals, r.finals, sizeof(r.finals));
+    });
+}
+
+// LogUp proof over resident Fp columns; challenges from FpStream(seed, domain).
+int vzh_logup_prove(void* h, uint64_t f_col, size_t n_f, uint64_t t_col, size_t n_t, uint64_t mult,
+                    const uint8_t* seed, uint64_t domain, vz_fp2* out, size_t cap, size_t* written,
+                    char* err, size_t len) {
+    return guarded(err, len, [&] {
+        FpStream chal(seed, domain);
+        std::vector<Fp2> proof = logup_prove_resident(*static_cast<Backend*>(h), f_col, n_f, t_col, n_t, mult, chal);
+        if (proof.size() > cap) throw AccelError("logup proof buffer too small");
+        std::memcpy(out, proof.data(), proof.size() * sizeof(vz_fp2));
+        *written = proof.size();
+    });
+}
+
+// Raw u64 draws of FpStream(seed, domain) (input synthesis for benches).
+void vzh_fpstream_u64(const uint8_t* seed, uint64_t domain, size_t n, uint64_t* out) {
+    FpStream s(seed, domain);
+    for (size_t i = 0; i < n; ++i) out[i] = s.next_u64();
+}
+
+}  // extern "C"
