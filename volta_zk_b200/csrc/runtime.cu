@@ -637,6 +637,9 @@ extern "C" int volta_cuda_create(void** out) {
         VZB_CUDA(c, cudaHostAlloc(&c->host_mailbox, 4096, cudaHostAllocMapped));
         VZB_CUDA(c, cudaHostGetDevicePointer(&c->host_mailbox_dev, c->host_mailbox, 0));
         if (ensure_ws(c, kWsCounter, 4096)) return -1;
+        // per-block partials of the single-launch reductions: at most 8 blocks
+        // per SM and 9 Fp2 accumulators per block (the aux round)
+        if (ensure_ws(c, kWsPartials, static_cast<size_t>(c->sm_count) * 8 * 9 * sizeof(Fp2))) return -1;
         if (probe_timing(c)) return -1;
         return 0;
     } catch (...) {

@@ -166,7 +166,11 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_rounds_kernel(
 template <int K, class Eval, class Epi>
 static int launch_reduce(Context* c, const Eval& eval, size_t items, const Epi& epi,
                          unsigned per_sm = 4) {
-    const unsigned blocks = grid_for(c, items, kReduceThreads, per_sm);
+    static_assert(K <= 9, "partials workspace holds 9 accumulators per block");
+    // grid_for caps the grid at sm_count * per_sm <= sm_count * 8 blocks, the
+    // size of the partials workspace allocated at context creation
+    const unsigned blocks = grid_for(c, items, kReduceThreads, per_sm < 8 ? per_sm : 8);
+    if (!c->ws[kWsPartials].ptr) return fail_message(c, "reduction workspace missing");
     reduce_rounds_kernel<K, Eval, Epi><<<blocks, kReduceThreads, 0, c->stream>>>(
         eval, items, ws<Fp2>(c, kWsPartials), ws<unsigned>(c, kWsCounter), epi);
     VZB_LAUNCHED(c);
