@@ -92,7 +92,7 @@ def test_requant_and_pair_columns(be, oracle, shift):
     rows, cols, row_pad, col_pad = 5, 6, 8, 8
     acc = rng.integers(-(1 << 30), 1 << 30, size=rows * cols, dtype=np.int64)
     out = np.clip((acc + (1 << (shift - 1))) >> shift, -32768, 32767).astype(np.int16)
-    out[3] = np.int16(out[3] + 1)  # one inconsistent entry: error flag must be set
+    out[3] = np.int16((int(out[3]) + 1 + 32768) % 65536 - 32768)  # inconsistent entry: error flag must be set
     ia, io = be.upload_new(acc), be.upload_new(out)
     count = 4 if shift > 16 else 2
     ic = be.alloc(8 * count * row_pad * col_pad)
@@ -113,7 +113,11 @@ def test_requant_and_pair_columns(be, oracle, shift):
                 assert int(got[1, r, c]) == y1 % P
                 assert int(got[2, r, c]) == (y1 + (1 << 15) - (y << 16)) % (1 << 64)
                 assert int(got[3, r, c]) == y % P
-    assert int(got[0, 7, 7]) == 0 and int(got[count - 1, 7, 7]) == 0
+    # padded entries carry acc = out = 0: rem = 2^(s-1) (chained: 2^(s-17), 0, 2^15, 0)
+    if shift <= 16:
+        assert int(got[0, 7, 7]) == 1 << (shift - 1) and int(got[1, 7, 7]) == 0
+    else:
+        assert [int(got[k, 7, 7]) for k in range(4)] == [1 << (shift - 17), 0, 1 << 15, 0]
     ip = be.alloc(8 * 2 * row_pad * col_pad)
     be.call("pair_columns_device", ia, 0, io, 0, ip, 0, rows, cols, row_pad, col_pad, 5, 9, 1, 0)
     pc = be.download(ip, 16 * row_pad * col_pad).reshape(2, row_pad, col_pad)

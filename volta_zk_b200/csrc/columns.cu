@@ -157,6 +157,12 @@ __global__ void histogram_lut_kernel(const uint64_t* in, uint32_t* out, size_t n
     }
 }
 
+// out[i] = in[i % len] for elements of 2, 4, 8 or 16 bytes
+template <typename T>
+__global__ void repeat_kernel(const T* in, T* out, size_t len, size_t total) {
+    VZB_GRID_LOOP(i, total) out[i] = in[i % len];
+}
+
 __global__ void u32_add_kernel(uint32_t* t, const uint32_t* a, size_t n) {
     VZB_GRID_LOOP(i, n) t[i] += a[i];
 }
@@ -249,6 +255,10 @@ using namespace vzb;
     if (op_begin(c) || op_mark(c, 1)) return -1
 #define VZB_OP_END(c, op) \
     VZB_LAUNCHED(c); \
+    if (op_mark(c, 2)) return -1; \
+    return op_finish(c, op, 0, 0)
+// for primitives that enqueue a copy instead of a kernel
+#define VZB_OP_END_COPY(c, op) \
     if (op_mark(c, 2)) return -1; \
     return op_finish(c, op, 0, 0)
 
@@ -382,10 +392,15 @@ extern "C" int volta_cuda_repeat_vector_device(void* raw, uint64_t in_id, size_t
     if (region_elems(c, in_id, in_off, input_len, e, &in) ||
         region_elems(c, out_id, out_off, input_len * repeat, e, &out))
         return -1;
+    const size_t total = input_len * repeat;
     VZB_OP_BEGIN(c);
-    // one 2-D copy: `repeat` rows of the same source (source pitch 0)
-    VZB_CUDA(c, cudaMemcpy2DAsync(out, input_len * e, in, 0, input_len * e, repeat, cudaMemcpyDeviceToDevice,
-                                  c->stream));
+    const unsigned grid = grid_for(c, total, 256);
+    switch (e) {
+        case 2: repeat_kernel<<<grid, 256, 0, c->stream>>>(static_cast<const uint16_t*>(in), static_cast<uint16_t*>(out), input_len, total); break;
+        case 4: repeat_kernel<<<grid, 256, 0, c->stream>>>(static_cast<const uint32_t*>(in), static_cast<uint32_t*>(out), input_len, total); break;
+        case 8: repeat_kernel<<<grid, 256, 0, c->stream>>>(static_cast<const uint64_t*>(in), static_cast<uint64_t*>(out), input_len, total); break;
+        default: repeat_kernel<<<grid, 256, 0, c->stream>>>(static_cast<const ulonglong2*>(in), static_cast<ulonglong2*>(out), input_len, total); break;
+    }
     VZB_OP_END(c, kOpGemm);
 }
 
@@ -403,7 +418,7 @@ extern "C" int volta_cuda_compact_strided_rows_device(void* raw, uint64_t in_id,
     VZB_OP_BEGIN(c);
     VZB_CUDA(c, cudaMemcpy2DAsync(out, width * e, in, source_stride * e, width * e, rows,
                                   cudaMemcpyDeviceToDevice, c->stream));
-    VZB_OP_END(c, kOpGemm);
+    VZB_OP_END_COPY(c, kOpGemm);
 }
 
 extern "C" int volta_cuda_attention_above_mask_device(void* raw, uint64_t eq_id, size_t eq_off, size_t entries,

@@ -46,6 +46,8 @@ int fail_message(Context* c, const char* message) noexcept {
 
 int fail_cuda(Context* c, const char* what, cudaError_t e) noexcept {
     drop_active_record(c);
+    // consume a non-sticky error so it cannot surface again at a later launch
+    (void)cudaGetLastError();
     if (c) {
         try {
             c->error = std::string(what) + ": " + cudaGetErrorString(e);

@@ -164,7 +164,7 @@ int reject(Context* c, const char* message) noexcept;
 #define VZB_LAUNCHED(c)                                                  \
     do {                                                                 \
         ++(c)->launches;                                                 \
-        cudaError_t vzb_l_ = cudaPeekAtLastError();                      \
+        cudaError_t vzb_l_ = cudaGetLastError();                         \
         if (vzb_l_ != cudaSuccess) return ::vzb::fail_cuda((c), "kernel launch", vzb_l_); \
     } while (0)
 
