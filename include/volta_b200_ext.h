@@ -9,6 +9,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "volta_cuda_backend.h"
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -19,6 +21,40 @@ int volta_b200_timing_mark(void* ctx, int slot);
 int volta_b200_timing_elapsed(void* ctx, int start, int end, float* ms);
 /* Kernels this context has launched since it was created. */
 int volta_b200_launch_count(void* ctx, uint64_t* launches);
+
+/*
+ * Triple-product round message without any device allocation.
+ *
+ * No counterpart in the reference seam.  Every other entry point reserves
+ * its reduction workspace through the context (cudaMalloc on first use or
+ * growth).  Some callers cannot allocate: code whose HBM is owned by another
+ * framework's caching allocator (a process that budgets all device memory
+ * itself), and per-round paths that cannot afford the device-wide
+ * synchronisation cudaMalloc/cudaFree can trigger.  This variant takes plain
+ * device pointers and a stream, and keeps its reduction scratch in a fixed
+ * array compiled into the library (VOLTA_B200_NOALLOC_SCRATCH_BYTES per GPU
+ * that loads it, held until the process exits).
+ *
+ *   a, b, c  device pointers to 2*pairs Fp2 each (16-byte aligned)
+ *   output   device pointer receiving [g(0), g(2), g(3)] (3 Fp2), the same
+ *            values volta_cuda_fp2_triple_product_round_device returns
+ *   stream   cudaStream_t to enqueue on (NULL = legacy default stream)
+ * Returns 0 on success, -1 on null pointers or pairs == 0, -2
+ * (VOLTA_B200_NOALLOC_TOO_LARGE) when pairs exceeds
+ * VOLTA_B200_NOALLOC_MAX_PAIRS, or a cudaError_t value.
+ *
+ * The first call on a device resolves the scratch array's device address
+ * (once per device, with that device current); make that first call before
+ * any stream capture.  All calls share the one scratch array: calls that
+ * overlap on the GPU (concurrent streams, several host threads) race and
+ * must be serialised by the caller.  The result is final once `stream`
+ * completes.
+ */
+#define VOLTA_B200_NOALLOC_MAX_PAIRS ((size_t)22369280)  /* 21845 blocks x 1024 pairs */
+#define VOLTA_B200_NOALLOC_SCRATCH_BYTES ((size_t)1048576 + 256)
+#define VOLTA_B200_NOALLOC_TOO_LARGE (-2)
+int volta_b200_triple_product_round_noalloc(const vz_fp2* a, const vz_fp2* b, const vz_fp2* c,
+                                            size_t pairs, vz_fp2* output, void* stream);
 
 #ifdef __cplusplus
 }
