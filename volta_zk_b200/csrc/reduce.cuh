@@ -91,6 +91,26 @@ __device__ __forceinline__ void grid_finish(Acc<K> a, Fp2* partials, unsigned* c
     }
 }
 
+#ifdef __CUDACC__
+// Grid-stride evaluation into lazily reduced accumulators (sums of 128-bit
+// products, one canonical reduction per accumulator per thread), then the
+// single-launch grid reduction.  `eval(i, w)` adds item i's terms into w[K].
+template <int K, class Eval, class Epi>
+__global__ void __launch_bounds__(kReduceThreads) reduce_wide_kernel(Eval eval, size_t items, Fp2* partials,
+                                                                     unsigned* counter, Epi epi) {
+    Fp2W w[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) f2w_zero(w[k]);
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < items; i += stride)
+        eval(i, w);
+    Acc<K> acc;
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc.v[k] = f2w_reduce(w[k]);
+    grid_finish<K>(acc, partials, counter, epi);
+}
+#endif
+
 // Epilogue that stores the K sums, optionally multiplied by a scale.
 template <int K>
 struct StoreEpi {

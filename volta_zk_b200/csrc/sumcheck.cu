@@ -31,52 +31,65 @@ namespace vzb {
 // evaluation functors (one per message shape)
 // ---------------------------------------------------------------------------
 
+// The round evaluations accumulate the last product of each term lazily
+// (Fp2W: unreduced 128-bit products), so each pair pays one canonical
+// reduction per inner product only.  at2 = v1 + (v1 - v0) and
+// at3 = at2 + (v1 - v0) are formed as "weak" values (< 2^64), which the
+// products accept.
+
 struct ProductEval {  // [g(0), g(2)] of a*b
     const Fp2 *a, *b;
-    __device__ __forceinline__ void operator()(size_t i, Acc<2>& acc) const {
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
         const Fp2 a0 = ldcs2(a + 2 * i), a1 = ldcs2(a + 2 * i + 1);
         const Fp2 b0 = ldcs2(b + 2 * i), b1 = ldcs2(b + 2 * i + 1);
-        acc.v[0] = f2add(acc.v[0], f2mul(a0, b0));
-        acc.v[1] = f2add(acc.v[1], f2mul(f2at2(a0, a1), f2at2(b0, b1)));
+        f2w_mac(w[0], a0, b0);
+        f2w_mac(w[1], d2add_weak(a1, d2sub(a1, a0)), d2add_weak(b1, d2sub(b1, b0)));
     }
 };
 
 struct TripleEval {  // [g(0), g(2), g(3)] of a*b*c
     const Fp2 *a, *b, *c;
-    __device__ __forceinline__ void operator()(size_t i, Acc<3>& acc) const {
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
         const Fp2 a0 = ldcs2(a + 2 * i), a1 = ldcs2(a + 2 * i + 1);
         const Fp2 b0 = ldcs2(b + 2 * i), b1 = ldcs2(b + 2 * i + 1);
         const Fp2 c0 = ldcs2(c + 2 * i), c1 = ldcs2(c + 2 * i + 1);
-        const Fp2 da = f2sub(a1, a0), db = f2sub(b1, b0), dc = f2sub(c1, c0);
-        const Fp2 a2 = f2add(a1, da), b2 = f2add(b1, db), c2 = f2add(c1, dc);
-        const Fp2 a3 = f2add(a2, da), b3 = f2add(b2, db), c3 = f2add(c2, dc);
-        acc.v[0] = f2add(acc.v[0], f2mul(f2mul(a0, b0), c0));
-        acc.v[1] = f2add(acc.v[1], f2mul(f2mul(a2, b2), c2));
-        acc.v[2] = f2add(acc.v[2], f2mul(f2mul(a3, b3), c3));
+        const Fp2 da = d2sub(a1, a0), db = d2sub(b1, b0), dc = d2sub(c1, c0);
+        const Fp2 a2 = d2add_weak(a1, da), b2 = d2add_weak(b1, db), c2 = d2add_weak(c1, dc);
+        const Fp2 a3 = d2add_weak(a2, da), b3 = d2add_weak(b2, db), c3 = d2add_weak(c2, dc);
+        f2w_mac(w[0], d2mul(a0, b0), c0);
+        f2w_mac(w[1], d2mul(a2, b2), c2);
+        f2w_mac(w[2], d2mul(a3, b3), c3);
     }
 };
 
 // RoundAcc = sum_i S[i] * (a0 d0 + b0 c0, a2 d2 + b2 c2, c0 d0, c2 d2)
 struct LogupEval {
     const Fp2 *p0, *p1, *q0, *q1, *s;
-    __device__ __forceinline__ void operator()(size_t i, Acc<4>& acc) const {
-        const Fp2 a0 = ldcs2(p0 + 2 * i), a2 = f2at2(a0, ldcs2(p0 + 2 * i + 1));
-        const Fp2 b0 = ldcs2(p1 + 2 * i), b2 = f2at2(b0, ldcs2(p1 + 2 * i + 1));
-        const Fp2 c0 = ldcs2(q0 + 2 * i), c2 = f2at2(c0, ldcs2(q0 + 2 * i + 1));
-        const Fp2 d0 = ldcs2(q1 + 2 * i), d2 = f2at2(d0, ldcs2(q1 + 2 * i + 1));
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        const Fp2 a0 = ldcs2(p0 + 2 * i), a1 = ldcs2(p0 + 2 * i + 1);
+        const Fp2 b0 = ldcs2(p1 + 2 * i), b1 = ldcs2(p1 + 2 * i + 1);
+        const Fp2 c0 = ldcs2(q0 + 2 * i), c1 = ldcs2(q0 + 2 * i + 1);
+        const Fp2 d0 = ldcs2(q1 + 2 * i), d1 = ldcs2(q1 + 2 * i + 1);
         const Fp2 si = ldg2(s + i);
-        acc.v[0] = f2add(acc.v[0], f2mul(si, f2add(f2mul(a0, d0), f2mul(b0, c0))));
-        acc.v[1] = f2add(acc.v[1], f2mul(si, f2add(f2mul(a2, d2), f2mul(b2, c2))));
-        acc.v[2] = f2add(acc.v[2], f2mul(si, f2mul(c0, d0)));
-        acc.v[3] = f2add(acc.v[3], f2mul(si, f2mul(c2, d2)));
+        const Fp2 a2 = d2add_weak(a1, d2sub(a1, a0)), b2 = d2add_weak(b1, d2sub(b1, b0));
+        const Fp2 c2 = d2add_weak(c1, d2sub(c1, c0)), d2 = d2add_weak(d1, d2sub(d1, d0));
+        Fp2W t;
+        f2w_zero(t);
+        f2w_mac(t, a0, d0);
+        f2w_mac(t, b0, c0);
+        f2w_mac(w[0], si, f2w_reduce(t));
+        f2w_zero(t);
+        f2w_mac(t, a2, d2);
+        f2w_mac(t, b2, c2);
+        f2w_mac(w[1], si, f2w_reduce(t));
+        f2w_mac(w[2], si, d2mul(c0, d0));
+        f2w_mac(w[3], si, d2mul(c2, d2));
     }
 };
 
 struct DotEval {
     const Fp2 *a, *b;
-    __device__ __forceinline__ void operator()(size_t i, Acc<1>& acc) const {
-        acc.v[0] = f2add(acc.v[0], f2mul(ldcs2(a + i), ldcs2(b + i)));
-    }
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const { f2w_mac(w[0], ldcs2(a + i), ldcs2(b + i)); }
 };
 
 struct PairSumEval {  // sums of an array of (g0, g2) pairs
@@ -161,6 +174,18 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_rounds_kernel(
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < items; i += stride)
         eval(i, acc);
     grid_finish<K>(acc, partials, counter, epi);
+}
+
+template <int K, class Eval, class Epi>
+static int launch_reduce_wide(Context* c, const Eval& eval, size_t items, const Epi& epi,
+                              unsigned per_sm = 4) {
+    static_assert(K <= 9, "partials workspace holds 9 accumulators per block");
+    const unsigned blocks = grid_for(c, items, kReduceThreads, per_sm < 8 ? per_sm : 8);
+    if (!c->ws[kWsPartials].ptr) return fail_message(c, "reduction workspace missing");
+    reduce_wide_kernel<K, Eval, Epi><<<blocks, kReduceThreads, 0, c->stream>>>(
+        eval, items, ws<Fp2>(c, kWsPartials), ws<unsigned>(c, kWsCounter), epi);
+    VZB_LAUNCHED(c);
+    return 0;
 }
 
 template <int K, class Eval, class Epi>
@@ -460,7 +485,7 @@ int product_round(Context* c, uint64_t a_id, size_t a_off, uint64_t b_id, size_t
     }
     const MsgOut o = msg_out(c, dev, host, 2);
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    if (launch_reduce<2>(c, ProductEval{a, b}, pairs, StoreEpi<2>{o.dev, scale, scaled})) return -1;
+    if (launch_reduce_wide<2>(c, ProductEval{a, b}, pairs, StoreEpi<2>{o.dev, scale, scaled})) return -1;
     return finish_msg(c, kOpGemm, o);
 }
 
@@ -479,13 +504,13 @@ int triple_round(Context* c, uint64_t a_id, size_t a_off, uint64_t b_id, size_t 
     }
     const MsgOut o = msg_out(c, dev, host, 3);
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    if (launch_reduce<3>(c, TripleEval{a, b, cc}, pairs, StoreEpi<3>{o.dev, Fp2{1, 0}, false})) return -1;
+    if (launch_reduce_wide<3>(c, TripleEval{a, b, cc}, pairs, StoreEpi<3>{o.dev, Fp2{1, 0}, false})) return -1;
     return finish_msg(c, kOpGemm, o);
 }
 
 int logup_round(Context* c, const Fp2* p0, const Fp2* p1, const Fp2* q0, const Fp2* q1,
                 const Fp2* s, size_t pairs, const MsgOut& o) {
-    return launch_reduce<4>(c, LogupEval{p0, p1, q0, q1, s}, pairs,
+    return launch_reduce_wide<4>(c, LogupEval{p0, p1, q0, q1, s}, pairs,
                             StoreEpi<4>{o.dev, Fp2{1, 0}, false});
 }
 
@@ -892,7 +917,7 @@ extern "C" int volta_cuda_fp2_dot_device(void* raw, uint64_t a_id, size_t a_off,
         return -1;
     const MsgOut o = msg_out(c, nullptr, output, 1);
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    if (launch_reduce<1>(c, DotEval{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b)}, n,
+    if (launch_reduce_wide<1>(c, DotEval{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b)}, n,
                          StoreEpi<1>{o.dev, Fp2{1, 0}, false}))
         return -1;
     return finish_msg(c, kOpGemm, o);
@@ -909,7 +934,7 @@ extern "C" int volta_cuda_fp2_dot_scaled_pair_into_device(void* raw, uint64_t a_
         region_elems(c, out_id, out_off, 2, sizeof(Fp2), &out))
         return -1;
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    if (launch_reduce<1>(c, DotEval{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b)}, n,
+    if (launch_reduce_wide<1>(c, DotEval{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b)}, n,
                          ScaledPairEpi{static_cast<Fp2*>(out), scale}))
         return -1;
     if (op_mark(c, 2)) return -1;
