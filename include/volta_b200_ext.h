@@ -23,6 +23,24 @@ int volta_b200_timing_elapsed(void* ctx, int start, int end, float* ms);
 int volta_b200_launch_count(void* ctx, uint64_t* launches);
 
 /*
+ * Fused fold + next round message.  With r the challenge of round j, fold the
+ * current resident vectors (len entries each, len a multiple of 4, offset 0)
+ * into the output vectors (len/2 entries) exactly as
+ * volta_cuda_fp2_fold_rows_device / volta_cuda_logup_fold4_device would, and
+ * return the round j+1 message over the folded vectors exactly as
+ * volta_cuda_fp2_triple_product_round_device / volta_cuda_logup_general_round_device
+ * would (the LogUp variant reads its suffix table at (suffix_id, suffix_offset)).
+ * One pass over the data and one launch instead of two (four for three folds).
+ */
+int volta_b200_triple_fold_round_device(void* ctx, uint64_t a_id, uint64_t b_id, uint64_t c_id, size_t len,
+                                        vz_fp2 r, uint64_t a_out_id, uint64_t b_out_id, uint64_t c_out_id,
+                                        vz_fp2* output);
+int volta_b200_logup_fold_round_device(void* ctx, uint64_t p0_id, uint64_t p1_id, uint64_t q0_id,
+                                       uint64_t q1_id, size_t len, vz_fp2 r, uint64_t o0_id, uint64_t o1_id,
+                                       uint64_t o2_id, uint64_t o3_id, uint64_t suffix_id, size_t suffix_offset,
+                                       vz_fp2* output);
+
+/*
  * Triple-product round message without any device allocation.
  *
  * No counterpart in the reference seam.  Every other entry point reserves

@@ -9,11 +9,15 @@ P = 0xFFFFFFFF00000001
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module")
-def prover():
+# (timing policy, fused fold + round extensions): the reference's call
+# sequence under deferred events, and the fused drivers under both policies.
+@pytest.fixture(scope="module", params=[(0, False), (0, True), (1, True)],
+                ids=["events-unfused", "events-fused", "counters-fused"])
+def prover(request):
     from volta_zk_b200 import accel
 
-    p = accel.Prover(policy=0)
+    policy, fused = request.param
+    p = accel.Prover(policy=policy, fused=fused)
     yield p
     p.close()
 

@@ -26,6 +26,7 @@ from .build import HERE, library_path
 
 ROOT = os.path.dirname(HERE)
 HEADER = os.path.join(ROOT, "include", "volta_cuda_backend.h")
+EXT_HEADER = os.path.join(ROOT, "include", "volta_b200_ext.h")
 ABI_VERSION = 37
 P = 0xFFFFFFFF00000001
 
@@ -80,16 +81,17 @@ _CTYPES = {
     "vz_fp2": Fp2, "vz_fp2*": C.c_void_p, "const vz_fp2*": C.c_void_p,
     "vz_raw_stats*": C.c_void_p, "vz_raw_pinned_stats*": C.c_void_p,
     "vz_raw_control_state*": C.c_void_p, "const vz_attention_wires_args*": C.c_void_p,
+    "float*": C.POINTER(C.c_float),
 }
 _RESTYPES = {"int": C.c_int, "uint32_t": C.c_uint32, "void": None, "const char*": C.c_char_p}
 
 
-def parse_header(path: str = HEADER) -> Dict[str, tuple]:
+def parse_header(path: str = HEADER, prefix: str = "volta_cuda_") -> Dict[str, tuple]:
     """name -> (restype, [argtypes]) for every declaration in the header."""
     text = re.sub(r"/\*.*?\*/", "", open(path).read(), flags=re.S)
     out = {}
     for ret, name, args in re.findall(
-            r"\b(int|uint32_t|void|const char\*) (volta_cuda_\w+)\(([^;]*?)\);", text, re.S):
+            r"\b(int|uint32_t|void|const char\*) (" + prefix + r"\w+)\(([^;]*?)\);", text, re.S):
         types = []
         args = " ".join(args.split())
         if args and args != "void":
@@ -122,10 +124,11 @@ def load_cuda_library(path: str | None = None):
             raise AccelError(f"MissingSymbol: {name}") from e
         fn.restype = res
         fn.argtypes = args
-    # measurement extensions (include/volta_b200_ext.h)
-    lib.volta_b200_timing_mark.argtypes = [C.c_void_p, C.c_int]
-    lib.volta_b200_timing_elapsed.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_float)]
-    lib.volta_b200_launch_count.argtypes = [C.c_void_p, C.POINTER(C.c_uint64)]
+    # extensions (include/volta_b200_ext.h)
+    for name, (res, args) in parse_header(EXT_HEADER, "volta_b200_").items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
     if lib.volta_cuda_abi_version() != ABI_VERSION:
         raise AccelError(f"AbiMismatch: expected {ABI_VERSION}, found {lib.volta_cuda_abi_version()}")
     _cuda_lib = lib
@@ -143,6 +146,7 @@ def load_host_library():
         L.vzh_open.restype = vp
         L.vzh_open.argtypes = [C.c_char_p, C.c_int, C.c_char_p, sz]
         L.vzh_close.argtypes = [vp]
+        L.vzh_set_fused.argtypes = [vp, C.c_int]
         L.vzh_context.restype = vp
         L.vzh_context.argtypes = [vp]
         L.vzh_stats.argtypes = [vp, vp, C.c_char_p, sz]
@@ -264,7 +268,7 @@ def fpstream_u64(seed: bytes, domain: int, n: int) -> np.ndarray:
 class Prover:
     """Resident protocol drivers of libvolta_accel.so on their own context."""
 
-    def __init__(self, policy: int = 1):
+    def __init__(self, policy: int = 1, fused: bool = True):
         self.host = load_host_library()
         load_cuda_library()  # same dlopen handle as the host library's
         err = C.create_string_buffer(1024)
@@ -272,6 +276,7 @@ class Prover:
         if not self.h:
             raise AccelError(err.value.decode())
         self.backend = CudaBackend(ctx=self.host.vzh_context(self.h))
+        self.host.vzh_set_fused(self.h, 1 if fused else 0)
 
     def close(self):
         if self.h:

@@ -112,14 +112,22 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_wide_kernel(Eval eval, 
 #endif
 
 // Epilogue that stores the K sums, optionally multiplied by a scale.
+// When `flag` is set (host-bound message in the mapped mailbox) the message
+// is published by a system-scope fence followed by the sequence number.
 template <int K>
 struct StoreEpi {
     Fp2* out;
     Fp2 scale;
     bool scaled;
+    unsigned* flag;
+    unsigned seq;
     __device__ __forceinline__ void operator()(const Acc<K>& a) const {
 #pragma unroll
         for (int k = 0; k < K; ++k) out[k] = scaled ? f2mul(a.v[k], scale) : a.v[k];
+        if (flag) {
+            __threadfence_system();
+            *reinterpret_cast<volatile unsigned*>(flag) = seq;
+        }
     }
 };
 

@@ -8,8 +8,10 @@
 #include "runtime.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
+#include <cstring>
 #include <new>
 
 namespace vzb {
@@ -456,6 +458,39 @@ int op_finish(Context* c, int op, uint64_t h2d, uint64_t d2h, uint64_t d2d, uint
     return 0;
 }
 
+int op_finish_message(Context* c, int op, uint64_t d2h, uint32_t seq) {
+    if (c->coarse || c->mode != kTimingCounters) return op_finish(c, op, 0, d2h);
+    if (!c->counter_active) return fail_message(c, "counter-only finish without active operation");
+    c->counter_active = false;
+    c->counter_pending = true;
+    ++c->outstanding;
+    volatile uint32_t* flag =
+        reinterpret_cast<volatile uint32_t*>(static_cast<char*>(c->host_mailbox) + kMailboxFlagOffset);
+    const auto t0 = std::chrono::steady_clock::now();
+    uint64_t spins = 0;
+    while (*flag != seq) {
+        if ((++spins & 255) == 0) {
+            const cudaError_t q = cudaStreamQuery(c->stream);
+            if (q == cudaSuccess) {
+                if (*flag == seq) break;
+                return fail_message(c, "round message flag missing after the stream completed");
+            }
+            if (q != cudaErrorNotReady) return fail_cuda(c, "cudaStreamQuery(round message)", q);
+            if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(120))
+                return fail_message(c, "timed out waiting for a round message");
+        }
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);  // message words are read after the flag
+    const auto t1 = std::chrono::steady_clock::now();
+    RawStats& s = c->stats;
+    ++s.calls[op];
+    s.d2h_bytes += d2h;
+    ++s.synchronizations;
+    ++s.sync_host_output;
+    s.synchronization_ns += std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count();
+    return 0;
+}
+
 int xfer_begin(Context* c) {
     if (c->coarse) return reject(c, "host transfer is forbidden inside a coarse timing scope");
     switch (c->mode) {
@@ -638,6 +673,7 @@ extern "C" int volta_cuda_create(void** out) {
         }
         VZB_CUDA(c, cudaHostAlloc(&c->host_mailbox, 4096, cudaHostAllocMapped));
         VZB_CUDA(c, cudaHostGetDevicePointer(&c->host_mailbox_dev, c->host_mailbox, 0));
+        std::memset(c->host_mailbox, 0, 4096);  // the message flag starts below every sequence number
         if (ensure_ws(c, kWsCounter, 4096)) return -1;
         // per-block partials of the single-launch reductions: at most 8 blocks
         // per SM and 9 Fp2 accumulators per block (the aux round)

@@ -150,6 +150,7 @@ struct Context {
     std::chrono::steady_clock::time_point phase_start{};
     uint64_t phase_ns[3] = {};
     size_t twiddle_n = 0;
+    uint32_t mail_seq = 0;               // sequence number of host-bound messages
     uint64_t launches = 0;               // kernels launched by this context
     cudaEvent_t bench_ev[8] = {};        // measurement markers (extension ABI)
     std::string error;
@@ -206,6 +207,13 @@ int op_begin(Context* c);
 int op_mark(Context* c, int which);  // 1 = inputs staged, 2 = kernels enqueued
 int op_finish(Context* c, int op, uint64_t h2d, uint64_t d2h, uint64_t d2d = 0,
               uint64_t zeroed = 0, uint64_t generated = 0);
+// Host-bound round messages: the reducing kernel writes the message into the
+// mapped mailbox, then (after a system fence) `seq` into the flag word.
+constexpr size_t kMailboxFlagOffset = 1024;
+// Finish a primitive whose output is a message in the mapped mailbox.  In the
+// wall-only counter mode the host waits on the flag (no stream
+// synchronisation); the other modes synchronise as op_finish does.
+int op_finish_message(Context* c, int op, uint64_t d2h_bytes, uint32_t seq);
 int xfer_begin(Context* c);
 int xfer_finish(Context* c, size_t bytes, bool h2d);
 

@@ -87,6 +87,66 @@ struct LogupEval {
     }
 };
 
+// Fused fold + next round.  Round j's challenge r folds the current vectors
+// (len entries) into fresh half-length vectors and, in the same pass,
+// evaluates round j + 1 on the folded values: item i reads entries 4i..4i+3,
+// writes folded entries 2i, 2i+1 and accumulates the pair (2i, 2i+1).
+// This halves the launches per round and skips re-reading the folded
+// vectors.
+__device__ __forceinline__ void fold4_pair(const Fp2* in, Fp2* out, size_t i, Fp2 r, Fp2& x0, Fp2& x1) {
+    const Fp2 v0 = ldcs2(in + 4 * i), v1 = ldcs2(in + 4 * i + 1);
+    const Fp2 v2 = ldcs2(in + 4 * i + 2), v3 = ldcs2(in + 4 * i + 3);
+    x0 = d2fold(v0, v1, r);
+    x1 = d2fold(v2, v3, r);
+    st2(out + 2 * i, x0);
+    st2(out + 2 * i + 1, x1);
+}
+
+struct TripleFoldEval {
+    const Fp2 *a, *b, *c;
+    Fp2 *ao, *bo, *co;
+    Fp2 r;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        Fp2 a0, a1, b0, b1, c0, c1;
+        fold4_pair(a, ao, i, r, a0, a1);
+        fold4_pair(b, bo, i, r, b0, b1);
+        fold4_pair(c, co, i, r, c0, c1);
+        const Fp2 da = d2sub(a1, a0), db = d2sub(b1, b0), dc = d2sub(c1, c0);
+        const Fp2 a2 = d2add_weak(a1, da), b2 = d2add_weak(b1, db), c2 = d2add_weak(c1, dc);
+        const Fp2 a3 = d2add_weak(a2, da), b3 = d2add_weak(b2, db), c3 = d2add_weak(c2, dc);
+        f2w_mac(w[0], d2mul(a0, b0), c0);
+        f2w_mac(w[1], d2mul(a2, b2), c2);
+        f2w_mac(w[2], d2mul(a3, b3), c3);
+    }
+};
+
+struct LogupFoldEval {
+    const Fp2 *p0, *p1, *q0, *q1, *s;
+    Fp2 *o0, *o1, *o2, *o3;
+    Fp2 r;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        Fp2 a0, a1, b0, b1, c0, c1, d0, d1;
+        fold4_pair(p0, o0, i, r, a0, a1);
+        fold4_pair(p1, o1, i, r, b0, b1);
+        fold4_pair(q0, o2, i, r, c0, c1);
+        fold4_pair(q1, o3, i, r, d0, d1);
+        const Fp2 si = ldg2(s + i);
+        const Fp2 a2 = d2add_weak(a1, d2sub(a1, a0)), b2 = d2add_weak(b1, d2sub(b1, b0));
+        const Fp2 c2 = d2add_weak(c1, d2sub(c1, c0)), d2 = d2add_weak(d1, d2sub(d1, d0));
+        Fp2W t;
+        f2w_zero(t);
+        f2w_mac(t, a0, d0);
+        f2w_mac(t, b0, c0);
+        f2w_mac(w[0], si, f2w_reduce(t));
+        f2w_zero(t);
+        f2w_mac(t, a2, d2);
+        f2w_mac(t, b2, c2);
+        f2w_mac(w[1], si, f2w_reduce(t));
+        f2w_mac(w[2], si, d2mul(c0, d0));
+        f2w_mac(w[3], si, d2mul(c2, d2));
+    }
+};
+
 struct DotEval {
     const Fp2 *a, *b;
     __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const { f2w_mac(w[0], ldcs2(a + i), ldcs2(b + i)); }
@@ -208,19 +268,28 @@ struct MsgOut {
     Fp2* dev;
     Fp2* host;
     size_t count;
+    unsigned* flag;  // device address of the mailbox flag (host-bound messages)
+    unsigned seq;
 };
 
 static MsgOut msg_out(Context* c, Fp2* dev, Fp2* host, size_t count) {
-    if (dev) return MsgOut{dev, nullptr, count};
-    return MsgOut{static_cast<Fp2*>(c->host_mailbox_dev), host, count};
+    if (dev) return MsgOut{dev, nullptr, count, nullptr, 0};
+    unsigned* flag = reinterpret_cast<unsigned*>(static_cast<char*>(c->host_mailbox_dev) + kMailboxFlagOffset);
+    return MsgOut{static_cast<Fp2*>(c->host_mailbox_dev), host, count, flag, ++c->mail_seq};
 }
 
-static int finish_msg(Context* c, int op, const MsgOut& o) {
+template <int K>
+static StoreEpi<K> store_epi(const MsgOut& o, Fp2 scale = Fp2{1, 0}, bool scaled = false) {
+    return StoreEpi<K>{o.dev, scale, scaled, o.host ? o.flag : nullptr, o.seq};
+}
+
+// `flagged`: the kernel publishes the message with the mailbox flag
+static int finish_msg(Context* c, int op, const MsgOut& o, bool flagged = true) {
     if (op_mark(c, 2)) return -1;
     if (!o.host) return op_finish(c, op, 0, 0);
     const size_t bytes = o.count * sizeof(Fp2);
-    if (op_finish(c, op, 0, bytes)) return -1;
-    std::memcpy(o.host, c->host_mailbox, bytes);  // stream is synchronised here
+    if (flagged ? op_finish_message(c, op, bytes, o.seq) : op_finish(c, op, 0, bytes)) return -1;
+    std::memcpy(o.host, c->host_mailbox, bytes);  // message published (flag) or stream synchronised
     return 0;
 }
 
@@ -485,7 +554,7 @@ int product_round(Context* c, uint64_t a_id, size_t a_off, uint64_t b_id, size_t
     }
     const MsgOut o = msg_out(c, dev, host, 2);
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    if (launch_reduce_wide<2>(c, ProductEval{a, b}, pairs, StoreEpi<2>{o.dev, scale, scaled})) return -1;
+    if (launch_reduce_wide<2>(c, ProductEval{a, b}, pairs, store_epi<2>(o, scale, scaled))) return -1;
     return finish_msg(c, kOpGemm, o);
 }
 
@@ -504,14 +573,13 @@ int triple_round(Context* c, uint64_t a_id, size_t a_off, uint64_t b_id, size_t 
     }
     const MsgOut o = msg_out(c, dev, host, 3);
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    if (launch_reduce_wide<3>(c, TripleEval{a, b, cc}, pairs, StoreEpi<3>{o.dev, Fp2{1, 0}, false})) return -1;
+    if (launch_reduce_wide<3>(c, TripleEval{a, b, cc}, pairs, store_epi<3>(o))) return -1;
     return finish_msg(c, kOpGemm, o);
 }
 
 int logup_round(Context* c, const Fp2* p0, const Fp2* p1, const Fp2* q0, const Fp2* q1,
                 const Fp2* s, size_t pairs, const MsgOut& o) {
-    return launch_reduce_wide<4>(c, LogupEval{p0, p1, q0, q1, s}, pairs,
-                            StoreEpi<4>{o.dev, Fp2{1, 0}, false});
+    return launch_reduce_wide<4>(c, LogupEval{p0, p1, q0, q1, s}, pairs, store_epi<4>(o));
 }
 
 int resolve_logup_inputs(Context* c, uint64_t p0_id, size_t p0_off, uint64_t p1_id, size_t p1_off,
@@ -877,7 +945,7 @@ int aux_round(Context* c, uint64_t q0_id, size_t q0_off, uint64_t q1_id, size_t 
                static_cast<const Fp2*>(cols), static_cast<const Fp2*>(eq), static_cast<const Fp2*>(w),
                static_cast<const uint32_t*>(cc), column_count, claim_count, vector_len};
     if (launch_reduce<9>(c, ev, pairs, AuxEpi{o.dev, lambda, cpref, point}, 2)) return -1;
-    return finish_msg(c, kOpLogup, o);
+    return finish_msg(c, kOpLogup, o, false);
 }
 
 }  // namespace
@@ -918,7 +986,7 @@ extern "C" int volta_cuda_fp2_dot_device(void* raw, uint64_t a_id, size_t a_off,
     const MsgOut o = msg_out(c, nullptr, output, 1);
     if (op_begin(c) || op_mark(c, 1)) return -1;
     if (launch_reduce_wide<1>(c, DotEval{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b)}, n,
-                         StoreEpi<1>{o.dev, Fp2{1, 0}, false}))
+                         store_epi<1>(o)))
         return -1;
     return finish_msg(c, kOpGemm, o);
 }
@@ -951,7 +1019,7 @@ extern "C" int volta_cuda_fp2_pair_sum_device(void* raw, uint64_t in_id, size_t 
     if (resolve_pairs_input(c, in_id, off, pairs, &in)) return -1;
     const MsgOut o = msg_out(c, nullptr, output, 2);
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    if (launch_reduce<2>(c, PairSumEval{in}, pairs, StoreEpi<2>{o.dev, Fp2{1, 0}, false})) return -1;
+    if (launch_reduce<2>(c, PairSumEval{in}, pairs, store_epi<2>(o))) return -1;
     return finish_msg(c, kOpGemm, o);
 }
 
@@ -1137,4 +1205,51 @@ extern "C" int volta_cuda_fp2_powers_device(void* raw, uint64_t base_c0, uint64_
     VZB_LAUNCHED(c);
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpPcsRows, 0, 0, 0, 0, count * sizeof(Fp2));
+}
+
+// ===========================================================================
+// Extensions (include/volta_b200_ext.h): fused fold + next round
+// ===========================================================================
+
+extern "C" int volta_b200_triple_fold_round_device(void* raw, uint64_t a_id, uint64_t b_id, uint64_t c_id,
+                                                   size_t len, Fp2 r, uint64_t ao_id, uint64_t bo_id,
+                                                   uint64_t co_id, Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !output || len < 4 || (len & 3)) return fail_message(c, "invalid fused triple fold-round geometry");
+    void *a = nullptr, *b = nullptr, *cc = nullptr, *ao = nullptr, *bo = nullptr, *co = nullptr;
+    if (region_elems(c, a_id, 0, len, sizeof(Fp2), &a) || region_elems(c, b_id, 0, len, sizeof(Fp2), &b) ||
+        region_elems(c, c_id, 0, len, sizeof(Fp2), &cc) || region_elems(c, ao_id, 0, len / 2, sizeof(Fp2), &ao) ||
+        region_elems(c, bo_id, 0, len / 2, sizeof(Fp2), &bo) || region_elems(c, co_id, 0, len / 2, sizeof(Fp2), &co))
+        return -1;
+    const MsgOut o = msg_out(c, nullptr, output, 3);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    TripleFoldEval ev{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b), static_cast<const Fp2*>(cc),
+                      static_cast<Fp2*>(ao), static_cast<Fp2*>(bo), static_cast<Fp2*>(co), r};
+    if (launch_reduce_wide<3>(c, ev, len / 4, store_epi<3>(o))) return -1;
+    return finish_msg(c, kOpGemm, o);
+}
+
+extern "C" int volta_b200_logup_fold_round_device(void* raw, uint64_t p0_id, uint64_t p1_id, uint64_t q0_id,
+                                                  uint64_t q1_id, size_t len, Fp2 r, uint64_t o0_id,
+                                                  uint64_t o1_id, uint64_t o2_id, uint64_t o3_id,
+                                                  uint64_t s_id, size_t s_off, Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !output || len < 4 || (len & 3)) return fail_message(c, "invalid fused LogUp fold-round geometry");
+    const uint64_t ii[4] = {p0_id, p1_id, q0_id, q1_id};
+    const uint64_t oi[4] = {o0_id, o1_id, o2_id, o3_id};
+    void* in[4];
+    void* out[4];
+    void* s = nullptr;
+    for (int k = 0; k < 4; ++k)
+        if (region_elems(c, ii[k], 0, len, sizeof(Fp2), &in[k]) ||
+            region_elems(c, oi[k], 0, len / 2, sizeof(Fp2), &out[k]))
+            return -1;
+    if (region_elems(c, s_id, s_off, len / 4, sizeof(Fp2), &s)) return -1;
+    const MsgOut o = msg_out(c, nullptr, output, 4);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    LogupFoldEval ev{static_cast<const Fp2*>(in[0]), static_cast<const Fp2*>(in[1]), static_cast<const Fp2*>(in[2]),
+                     static_cast<const Fp2*>(in[3]), static_cast<const Fp2*>(s), static_cast<Fp2*>(out[0]),
+                     static_cast<Fp2*>(out[1]), static_cast<Fp2*>(out[2]), static_cast<Fp2*>(out[3]), r};
+    if (launch_reduce_wide<4>(c, ev, len / 4, store_epi<4>(o))) return -1;
+    return finish_msg(c, kOpLogup, o);
 }

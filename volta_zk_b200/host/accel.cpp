@@ -102,12 +102,20 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
                          std::to_string(version));
     }
     api_ = api.release();
+    ext_loaded_ = new ExtApi();
+    ext_loaded_->triple_fold_round = reinterpret_cast<decltype(ext_loaded_->triple_fold_round)>(
+        dlsym(handle_, "volta_b200_triple_fold_round_device"));
+    ext_loaded_->logup_fold_round = reinterpret_cast<decltype(ext_loaded_->logup_fold_round)>(
+        dlsym(handle_, "volta_b200_logup_fold_round_device"));
+    ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {
         std::string msg = ctx ? api_->volta_cuda_last_error(ctx) : "volta_cuda_create failed";
         if (ctx) api_->volta_cuda_destroy(ctx);
         delete api_;
         api_ = nullptr;
+        delete ext_loaded_;
+        ext_ = ext_loaded_ = nullptr;
         dlclose(handle_);
         handle_ = nullptr;
         throw AccelError("Cuda: " + msg);
@@ -120,7 +128,15 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
 Backend::~Backend() {
     if (api_ && ctx_) api_->volta_cuda_destroy(ctx_);
     delete api_;
+    if (ext_ != ext_loaded_) delete ext_;
+    delete ext_loaded_;
     if (handle_) dlclose(handle_);
+}
+
+void Backend::set_fused(bool on) {
+    static const ExtApi none{};
+    if (ext_ != ext_loaded_) delete ext_;
+    ext_ = on ? ext_loaded_ : new ExtApi(none);
 }
 
 void Backend::raise(const char* what) const {

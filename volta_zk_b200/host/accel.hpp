@@ -60,7 +60,8 @@ class FpStream {
 };
 
 // ---- the loaded C ABI ------------------------------------------------------
-struct Api;  // function table, defined in accel.cpp
+struct Api;     // function table, defined in api.hpp
+struct ExtApi;  // optional extensions, defined in api.hpp
 
 enum class TimingPolicy { DeferredEvents = 0, WallOnlyCounters = 1 };
 
@@ -77,6 +78,9 @@ class Backend {
     Backend& operator=(const Backend&) = delete;
 
     const Api& api() const { return *api_; }
+    const ExtApi& ext() const { return *ext_; }
+    // Use the fused fold + round extensions when the library has them.
+    void set_fused(bool on);
     void* ctx() const { return ctx_; }
     [[noreturn]] void raise(const char* what) const;
     void check(int rc, const char* what) const {
@@ -97,6 +101,8 @@ class Backend {
    private:
     void* handle_ = nullptr;
     Api* api_ = nullptr;
+    ExtApi* ext_ = nullptr;
+    ExtApi* ext_loaded_ = nullptr;
     void* ctx_ = nullptr;
 };
 

@@ -2,6 +2,7 @@
 // include/volta_cuda_backend.h).
 #pragma once
 
+#include "../../include/volta_b200_ext.h"
 #include "../../include/volta_cuda_backend.h"
 #include "abi_symbols.inc"
 
@@ -11,6 +12,14 @@ struct Api {
 #define VZH_FIELD(name) decltype(&::name) name = nullptr;
     VZH_ABI_SYMBOLS(VZH_FIELD)
 #undef VZH_FIELD
+};
+
+// Optional extension entry points (include/volta_b200_ext.h); null when the
+// loaded library is a backend without them, in which case the drivers use the
+// reference's call sequence only.
+struct ExtApi {
+    decltype(&::volta_b200_triple_fold_round_device) triple_fold_round = nullptr;
+    decltype(&::volta_b200_logup_fold_round_device) logup_fold_round = nullptr;
 };
 
 }  // namespace vzh

@@ -48,6 +48,10 @@ void* vzh_open(const char* library, int policy, char* err, size_t len) {
 
 void vzh_close(void* h) { delete static_cast<Backend*>(h); }
 
+// on != 0: use the fused fold + round extensions when the library has them
+// (the default); 0: the reference's call sequence only.
+void vzh_set_fused(void* h, int on) { static_cast<Backend*>(h)->set_fused(on != 0); }
+
 void* vzh_context(void* h) { return static_cast<Backend*>(h)->ctx(); }
 
 int vzh_stats(void* h, vz_raw_stats* out, char* err, size_t len) {

@@ -78,26 +78,49 @@ std::pair<std::vector<Fp2>, std::vector<Fp2>> layer_general_resident(
         b.check(A.volta_cuda_logup_suffix_eq_device(ctx, pts, 0, L, suffix, 0), "logup_suffix_eq_device");
     }
     size_t len = vector_len;
+    auto fold4 = [&](Fp2 r, size_t half, uint64_t* nv) {
+        b.check(A.volta_cuda_logup_fold4_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, half, r, nv[0], 0,
+                                                nv[1], 0, nv[2], 0, nv[3], 0),
+                "logup_fold4_device");
+    };
+    const auto fused = b.ext().logup_fold_round;
+    Fp2 acc[4];
+    Fp2 pending{0, 0};  // challenge of the previous round, not yet folded in
     for (size_t j = 0; j < L; ++j) {
         const size_t half = len / 2;
         const size_t soff = (size_t{1} << (L - 1 - j)) - 1;
-        Fp2 acc[4];
-        b.check(A.volta_cuda_logup_general_round_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, suffix,
-                                                        soff, half, acc),
-                "logup_general_round_device");
+        if (j == 0 || !fused) {
+            b.check(A.volta_cuda_logup_general_round_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, suffix,
+                                                            soff, half, acc),
+                    "logup_general_round_device");
+        } else {
+            // v still holds 2 * len entries: fold the previous round's
+            // challenge and evaluate this round in one pass
+            uint64_t nv[4];
+            for (int k = 0; k < 4; ++k) nv[k] = own.add(b.alloc(len * sizeof(Fp2)));
+            b.check(fused(ctx, v[0], v[1], v[2], v[3], 2 * len, pending, nv[0], nv[1], nv[2], nv[3], suffix,
+                          soff, acc),
+                    "volta_b200_logup_fold_round_device");
+            for (int k = 0; k < 4; ++k) {
+                own.release(v[k]);
+                v[k] = nv[k];
+            }
+        }
         const Fp2 h0 = f2mul(cpref, f2add(f2mul(lambda, acc[0]), acc[2]));
         const Fp2 h2 = f2mul(cpref, f2add(f2mul(lambda, acc[1]), acc[3]));
         proof.push_back(h0);
         proof.push_back(h2);
         const Fp2 r = chal.next_fp2();
-        uint64_t nv[4];
-        for (int k = 0; k < 4; ++k) nv[k] = own.add(b.alloc(half * sizeof(Fp2)));
-        b.check(A.volta_cuda_logup_fold4_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, half, r, nv[0], 0,
-                                                nv[1], 0, nv[2], 0, nv[3], 0),
-                "logup_fold4_device");
-        for (int k = 0; k < 4; ++k) {
-            own.release(v[k]);
-            v[k] = nv[k];
+        if (!fused || j + 1 == L) {
+            uint64_t nv[4];
+            for (int k = 0; k < 4; ++k) nv[k] = own.add(b.alloc(half * sizeof(Fp2)));
+            fold4(r, half, nv);
+            for (int k = 0; k < 4; ++k) {
+                own.release(v[k]);
+                v[k] = nv[k];
+            }
+        } else {
+            pending = r;
         }
         cpref = eq_step(cpref, point[j], r);
         rprime.push_back(r);
@@ -158,18 +181,29 @@ TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint6
     uint64_t cur[3] = {a, bb, c};
     bool owned = false;  // the caller's inputs are never folded in place
     size_t len = n;
+    const auto fused = b.ext().triple_fold_round;
+    Fp2 g[3];
+    if (len > 1)
+        b.check(A.volta_cuda_fp2_triple_product_round_device(ctx, cur[0], 0, cur[1], 0, cur[2], 0, len / 2, g),
+                "fp2_triple_product_round_device");
     while (len > 1) {
         const size_t pairs = len / 2;
-        Fp2 g[3];
-        b.check(A.volta_cuda_fp2_triple_product_round_device(ctx, cur[0], 0, cur[1], 0, cur[2], 0, pairs, g),
-                "fp2_triple_product_round_device");
         out.messages.insert(out.messages.end(), g, g + 3);
         const Fp2 r = tx.next_fp2();
         uint64_t nxt[3];
-        for (int k = 0; k < 3; ++k) {
-            nxt[k] = own.add(b.alloc(pairs * sizeof(Fp2)));
-            b.check(A.volta_cuda_fp2_fold_rows_device(ctx, cur[k], 0, 1, len, r, nxt[k], 0),
-                    "fp2_fold_rows_device");
+        for (int k = 0; k < 3; ++k) nxt[k] = own.add(b.alloc(pairs * sizeof(Fp2)));
+        if (fused && pairs > 1) {
+            // fold with r and produce the next round's message in one pass
+            b.check(fused(ctx, cur[0], cur[1], cur[2], len, r, nxt[0], nxt[1], nxt[2], g),
+                    "volta_b200_triple_fold_round_device");
+        } else {
+            for (int k = 0; k < 3; ++k)
+                b.check(A.volta_cuda_fp2_fold_rows_device(ctx, cur[k], 0, 1, len, r, nxt[k], 0),
+                        "fp2_fold_rows_device");
+            if (pairs > 1)
+                b.check(A.volta_cuda_fp2_triple_product_round_device(ctx, nxt[0], 0, nxt[1], 0, nxt[2], 0,
+                                                                     pairs / 2, g),
+                        "fp2_triple_product_round_device");
         }
         for (int k = 0; k < 3; ++k) {
             if (owned) own.release(cur[k]);
