@@ -39,6 +39,16 @@ int volta_b200_logup_fold_round_device(void* ctx, uint64_t p0_id, uint64_t p1_id
                                        uint64_t q1_id, size_t len, vz_fp2 r, uint64_t o0_id, uint64_t o1_id,
                                        uint64_t o2_id, uint64_t o3_id, uint64_t suffix_id, size_t suffix_offset,
                                        vz_fp2* output);
+/* The same, writing the message to the resident buffer (out_id, out_offset
+ * in Fp2 elements) instead of the host, with no synchronisation, like the
+ * reference's *_into_device rounds. */
+int volta_b200_triple_fold_round_into_device(void* ctx, uint64_t a_id, uint64_t b_id, uint64_t c_id, size_t len,
+                                             vz_fp2 r, uint64_t a_out_id, uint64_t b_out_id, uint64_t c_out_id,
+                                             uint64_t out_id, size_t out_offset);
+int volta_b200_logup_fold_round_into_device(void* ctx, uint64_t p0_id, uint64_t p1_id, uint64_t q0_id,
+                                            uint64_t q1_id, size_t len, vz_fp2 r, uint64_t o0_id, uint64_t o1_id,
+                                            uint64_t o2_id, uint64_t o3_id, uint64_t suffix_id,
+                                            size_t suffix_offset, uint64_t out_id, size_t out_offset);
 
 /*
  * Triple-product round message without any device allocation.

@@ -9,15 +9,18 @@ P = 0xFFFFFFFF00000001
 pytestmark = pytest.mark.gpu
 
 
-# (timing policy, fused fold + round extensions): the reference's call
-# sequence under deferred events, and the fused drivers under both policies.
-@pytest.fixture(scope="module", params=[(0, False), (0, True), (1, True)],
-                ids=["events-unfused", "events-fused", "counters-fused"])
+# (timing policy, fused fold + round extensions, scheduled drivers): the
+# reference's round-by-round call sequence under deferred events, the fused
+# round-by-round drivers under both policies, and the scheduled drivers
+# (challenges first, one message download) with and without fusion.
+@pytest.fixture(scope="module",
+                params=[(0, False, False), (0, True, False), (1, True, False), (1, False, True), (1, True, True)],
+                ids=["events-unfused", "events-fused", "counters-fused", "scheduled-unfused", "scheduled-fused"])
 def prover(request):
     from volta_zk_b200 import accel
 
-    policy, fused = request.param
-    p = accel.Prover(policy=policy, fused=fused)
+    policy, fused, scheduled = request.param
+    p = accel.Prover(policy=policy, fused=fused, scheduled=scheduled)
     yield p
     p.close()
 

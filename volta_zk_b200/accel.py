@@ -147,6 +147,7 @@ def load_host_library():
         L.vzh_open.argtypes = [C.c_char_p, C.c_int, C.c_char_p, sz]
         L.vzh_close.argtypes = [vp]
         L.vzh_set_fused.argtypes = [vp, C.c_int]
+        L.vzh_set_scheduled.argtypes = [vp, C.c_int]
         L.vzh_context.restype = vp
         L.vzh_context.argtypes = [vp]
         L.vzh_stats.argtypes = [vp, vp, C.c_char_p, sz]
@@ -268,7 +269,7 @@ def fpstream_u64(seed: bytes, domain: int, n: int) -> np.ndarray:
 class Prover:
     """Resident protocol drivers of libvolta_accel.so on their own context."""
 
-    def __init__(self, policy: int = 1, fused: bool = True):
+    def __init__(self, policy: int = 1, fused: bool = True, scheduled: bool = True):
         self.host = load_host_library()
         load_cuda_library()  # same dlopen handle as the host library's
         err = C.create_string_buffer(1024)
@@ -277,6 +278,7 @@ class Prover:
             raise AccelError(err.value.decode())
         self.backend = CudaBackend(ctx=self.host.vzh_context(self.h))
         self.host.vzh_set_fused(self.h, 1 if fused else 0)
+        self.host.vzh_set_scheduled(self.h, 1 if scheduled else 0)
 
     def close(self):
         if self.h:

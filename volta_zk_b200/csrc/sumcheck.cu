@@ -1211,17 +1211,18 @@ extern "C" int volta_cuda_fp2_powers_device(void* raw, uint64_t base_c0, uint64_
 // Extensions (include/volta_b200_ext.h): fused fold + next round
 // ===========================================================================
 
-extern "C" int volta_b200_triple_fold_round_device(void* raw, uint64_t a_id, uint64_t b_id, uint64_t c_id,
-                                                   size_t len, Fp2 r, uint64_t ao_id, uint64_t bo_id,
-                                                   uint64_t co_id, Fp2* output) {
-    Context* c = static_cast<Context*>(raw);
-    if (!c || !output || len < 4 || (len & 3)) return fail_message(c, "invalid fused triple fold-round geometry");
-    void *a = nullptr, *b = nullptr, *cc = nullptr, *ao = nullptr, *bo = nullptr, *co = nullptr;
+static int triple_fold_round(Context* c, uint64_t a_id, uint64_t b_id, uint64_t c_id, size_t len, Fp2 r,
+                             uint64_t ao_id, uint64_t bo_id, uint64_t co_id, Fp2* host, uint64_t out_id,
+                             size_t out_off) {
+    if (!c || (!host && !out_id) || len < 4 || (len & 3))
+        return fail_message(c, "invalid fused triple fold-round geometry");
+    void *a = nullptr, *b = nullptr, *cc = nullptr, *ao = nullptr, *bo = nullptr, *co = nullptr, *dev = nullptr;
     if (region_elems(c, a_id, 0, len, sizeof(Fp2), &a) || region_elems(c, b_id, 0, len, sizeof(Fp2), &b) ||
         region_elems(c, c_id, 0, len, sizeof(Fp2), &cc) || region_elems(c, ao_id, 0, len / 2, sizeof(Fp2), &ao) ||
         region_elems(c, bo_id, 0, len / 2, sizeof(Fp2), &bo) || region_elems(c, co_id, 0, len / 2, sizeof(Fp2), &co))
         return -1;
-    const MsgOut o = msg_out(c, nullptr, output, 3);
+    if (!host && region_elems(c, out_id, out_off, 3, sizeof(Fp2), &dev)) return -1;
+    const MsgOut o = msg_out(c, static_cast<Fp2*>(dev), host, 3);
     if (op_begin(c) || op_mark(c, 1)) return -1;
     TripleFoldEval ev{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b), static_cast<const Fp2*>(cc),
                       static_cast<Fp2*>(ao), static_cast<Fp2*>(bo), static_cast<Fp2*>(co), r};
@@ -1229,27 +1230,59 @@ extern "C" int volta_b200_triple_fold_round_device(void* raw, uint64_t a_id, uin
     return finish_msg(c, kOpGemm, o);
 }
 
-extern "C" int volta_b200_logup_fold_round_device(void* raw, uint64_t p0_id, uint64_t p1_id, uint64_t q0_id,
-                                                  uint64_t q1_id, size_t len, Fp2 r, uint64_t o0_id,
-                                                  uint64_t o1_id, uint64_t o2_id, uint64_t o3_id,
-                                                  uint64_t s_id, size_t s_off, Fp2* output) {
-    Context* c = static_cast<Context*>(raw);
-    if (!c || !output || len < 4 || (len & 3)) return fail_message(c, "invalid fused LogUp fold-round geometry");
-    const uint64_t ii[4] = {p0_id, p1_id, q0_id, q1_id};
-    const uint64_t oi[4] = {o0_id, o1_id, o2_id, o3_id};
+static int logup_fold_round(Context* c, const uint64_t in_ids[4], size_t len, Fp2 r, const uint64_t out_ids[4],
+                            uint64_t s_id, size_t s_off, Fp2* host, uint64_t out_id, size_t out_off) {
+    if (!c || (!host && !out_id) || len < 4 || (len & 3))
+        return fail_message(c, "invalid fused LogUp fold-round geometry");
     void* in[4];
     void* out[4];
-    void* s = nullptr;
+    void *s = nullptr, *dev = nullptr;
     for (int k = 0; k < 4; ++k)
-        if (region_elems(c, ii[k], 0, len, sizeof(Fp2), &in[k]) ||
-            region_elems(c, oi[k], 0, len / 2, sizeof(Fp2), &out[k]))
+        if (region_elems(c, in_ids[k], 0, len, sizeof(Fp2), &in[k]) ||
+            region_elems(c, out_ids[k], 0, len / 2, sizeof(Fp2), &out[k]))
             return -1;
     if (region_elems(c, s_id, s_off, len / 4, sizeof(Fp2), &s)) return -1;
-    const MsgOut o = msg_out(c, nullptr, output, 4);
+    if (!host && region_elems(c, out_id, out_off, 4, sizeof(Fp2), &dev)) return -1;
+    const MsgOut o = msg_out(c, static_cast<Fp2*>(dev), host, 4);
     if (op_begin(c) || op_mark(c, 1)) return -1;
     LogupFoldEval ev{static_cast<const Fp2*>(in[0]), static_cast<const Fp2*>(in[1]), static_cast<const Fp2*>(in[2]),
                      static_cast<const Fp2*>(in[3]), static_cast<const Fp2*>(s), static_cast<Fp2*>(out[0]),
                      static_cast<Fp2*>(out[1]), static_cast<Fp2*>(out[2]), static_cast<Fp2*>(out[3]), r};
     if (launch_reduce_wide<4>(c, ev, len / 4, store_epi<4>(o))) return -1;
     return finish_msg(c, kOpLogup, o);
+}
+
+extern "C" int volta_b200_triple_fold_round_device(void* raw, uint64_t a_id, uint64_t b_id, uint64_t c_id,
+                                                   size_t len, Fp2 r, uint64_t ao_id, uint64_t bo_id,
+                                                   uint64_t co_id, Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!output) return fail_message(c, "invalid fused triple fold-round geometry");
+    return triple_fold_round(c, a_id, b_id, c_id, len, r, ao_id, bo_id, co_id, output, 0, 0);
+}
+
+extern "C" int volta_b200_triple_fold_round_into_device(void* raw, uint64_t a_id, uint64_t b_id, uint64_t c_id,
+                                                        size_t len, Fp2 r, uint64_t ao_id, uint64_t bo_id,
+                                                        uint64_t co_id, uint64_t out_id, size_t out_offset) {
+    return triple_fold_round(static_cast<Context*>(raw), a_id, b_id, c_id, len, r, ao_id, bo_id, co_id, nullptr,
+                             out_id, out_offset);
+}
+
+extern "C" int volta_b200_logup_fold_round_device(void* raw, uint64_t p0_id, uint64_t p1_id, uint64_t q0_id,
+                                                  uint64_t q1_id, size_t len, Fp2 r, uint64_t o0_id,
+                                                  uint64_t o1_id, uint64_t o2_id, uint64_t o3_id,
+                                                  uint64_t s_id, size_t s_off, Fp2* output) {
+    Context* c = static_cast<Context*>(raw);
+    if (!output) return fail_message(c, "invalid fused LogUp fold-round geometry");
+    const uint64_t in[4] = {p0_id, p1_id, q0_id, q1_id}, out[4] = {o0_id, o1_id, o2_id, o3_id};
+    return logup_fold_round(c, in, len, r, out, s_id, s_off, output, 0, 0);
+}
+
+extern "C" int volta_b200_logup_fold_round_into_device(void* raw, uint64_t p0_id, uint64_t p1_id, uint64_t q0_id,
+                                                       uint64_t q1_id, size_t len, Fp2 r, uint64_t o0_id,
+                                                       uint64_t o1_id, uint64_t o2_id, uint64_t o3_id,
+                                                       uint64_t s_id, size_t s_off, uint64_t out_id,
+                                                       size_t out_offset) {
+    const uint64_t in[4] = {p0_id, p1_id, q0_id, q1_id}, out[4] = {o0_id, o1_id, o2_id, o3_id};
+    return logup_fold_round(static_cast<Context*>(raw), in, len, r, out, s_id, s_off, nullptr, out_id,
+                            out_offset);
 }

@@ -81,6 +81,12 @@ class Backend {
     const ExtApi& ext() const { return *ext_; }
     // Use the fused fold + round extensions when the library has them.
     void set_fused(bool on);
+    // Scheduled drivers: draw every challenge first, enqueue all rounds with
+    // device-side message slots and download the messages once (valid for
+    // the clear / private-transcript sinks, whose challenges do not depend on
+    // the messages).  Off: the reference's round-by-round call sequence.
+    void set_scheduled(bool on) { scheduled_ = on; }
+    bool scheduled() const { return scheduled_; }
     void* ctx() const { return ctx_; }
     [[noreturn]] void raise(const char* what) const;
     void check(int rc, const char* what) const {
@@ -103,6 +109,7 @@ class Backend {
     Api* api_ = nullptr;
     ExtApi* ext_ = nullptr;
     ExtApi* ext_loaded_ = nullptr;
+    bool scheduled_ = false;
     void* ctx_ = nullptr;
 };
 

@@ -20,6 +20,8 @@ struct Api {
 struct ExtApi {
     decltype(&::volta_b200_triple_fold_round_device) triple_fold_round = nullptr;
     decltype(&::volta_b200_logup_fold_round_device) logup_fold_round = nullptr;
+    decltype(&::volta_b200_triple_fold_round_into_device) triple_fold_round_into = nullptr;
+    decltype(&::volta_b200_logup_fold_round_into_device) logup_fold_round_into = nullptr;
 };
 
 }  // namespace vzh

@@ -52,6 +52,10 @@ void vzh_close(void* h) { delete static_cast<Backend*>(h); }
 // (the default); 0: the reference's call sequence only.
 void vzh_set_fused(void* h, int on) { static_cast<Backend*>(h)->set_fused(on != 0); }
 
+// on != 0: scheduled drivers (challenges first, one message download per
+// protocol); 0: one synchronised message per round, as the reference calls.
+void vzh_set_scheduled(void* h, int on) { static_cast<Backend*>(h)->set_scheduled(on != 0); }
+
 void* vzh_context(void* h) { return static_cast<Backend*>(h)->ctx(); }
 
 int vzh_stats(void* h, vz_raw_stats* out, char* err, size_t len) {

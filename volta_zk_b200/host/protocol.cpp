@@ -9,44 +9,15 @@
 
 #include "api.hpp"
 #include "accel.hpp"
+#include "protocol.hpp"
 
 namespace vzh {
 
 
 using vzb::f2add;
 using vzb::f2mul;
-using vzb::f2sub;
 
 namespace {
-
-// eq(p, r) = 2pr - p - r + 1 (logup.rs:466-468)
-Fp2 eq_step(Fp2 cpref, Fp2 p, Fp2 r) {
-    const Fp2 pr = f2mul(p, r);
-    return f2mul(cpref, f2add(f2sub(f2sub(f2add(pr, pr), p), r), Fp2{1, 0}));
-}
-
-// RAII list of arena ids freed on scope exit (mirrors the Rust guards).
-struct Owned {
-    Backend& b;
-    std::vector<uint64_t> ids;
-    explicit Owned(Backend& be) : b(be) {}
-    uint64_t add(uint64_t id) {
-        ids.push_back(id);
-        return id;
-    }
-    void release(uint64_t id) {
-        for (auto& x : ids)
-            if (x == id) {
-                x = 0;
-                b.free(id);
-                return;
-            }
-    }
-    ~Owned() {
-        for (uint64_t id : ids)
-            if (id) b.api().volta_cuda_resident_free(b.ctx(), id);
-    }
-};
 
 // layer_general_resident: children at (tree_p, tree_q)[child_offset ..
 // child_offset + child_len), claim point of length L = log2(child_len) - 1.
@@ -172,8 +143,9 @@ void prove_frac_tree_resident(Backend& b, uint64_t leaf, uint64_t mult, size_t n
 
 }  // namespace
 
-TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
-                                      FpStream& tx) {
+namespace {
+
+TripleResult triple_sumcheck_rounds(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n, FpStream& tx) {
     const Api& A = b.api();
     void* ctx = b.ctx();
     TripleResult out;
@@ -217,8 +189,18 @@ TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint6
     return out;
 }
 
+}  // namespace
+
+using SideProver = void (*)(Backend&, uint64_t, uint64_t, size_t, uint64_t, FpStream&, std::vector<Fp2>&);
+
+TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
+                                      FpStream& tx) {
+    return b.scheduled() ? triple_sumcheck_scheduled(b, a, bb, c, n, tx) : triple_sumcheck_rounds(b, a, bb, c, n, tx);
+}
+
 std::vector<Fp2> logup_prove_resident(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col,
                                       size_t n_t, uint64_t mult, FpStream& chal) {
+    const SideProver side_prover = b.scheduled() ? prove_frac_tree_scheduled : prove_frac_tree_resident;
     const Api& A = b.api();
     void* ctx = b.ctx();
     std::vector<Fp2> proof;
@@ -234,7 +216,7 @@ std::vector<Fp2> logup_prove_resident(Backend& b, uint64_t f_col, size_t n_f, ui
         const uint64_t leaf = side.add(b.alloc(n_f * sizeof(uint64_t)));
         b.check(A.volta_cuda_pack_lookup_leaf_device(ctx, f_col, 0, shifts, 0, leaf, 0, 1, n_f, alpha.c0),
                 "pack_lookup_leaf_device");
-        prove_frac_tree_resident(b, leaf, 0, n_f, alpha.c1, chal, proof);
+        side_prover(b, leaf, 0, n_f, alpha.c1, chal, proof);
     }
     // table side: numerators -mult
     {
@@ -242,7 +224,7 @@ std::vector<Fp2> logup_prove_resident(Backend& b, uint64_t f_col, size_t n_f, ui
         const uint64_t leaf = side.add(b.alloc(n_t * sizeof(uint64_t)));
         b.check(A.volta_cuda_pack_lookup_leaf_device(ctx, t_col, 0, shifts, 0, leaf, 0, 1, n_t, alpha.c0),
                 "pack_lookup_leaf_device");
-        prove_frac_tree_resident(b, leaf, mult, n_t, alpha.c1, chal, proof);
+        side_prover(b, leaf, mult, n_t, alpha.c1, chal, proof);
     }
     return proof;
 }

@@ -1,0 +1,49 @@
+// Helpers shared by the protocol drivers (protocol.cpp, scheduled.cpp).
+#pragma once
+
+#include <vector>
+
+#include "accel.hpp"
+#include "api.hpp"
+
+namespace vzh {
+
+using vzb::f2add;
+using vzb::f2mul;
+using vzb::f2sub;
+
+// eq(p, r) = 2pr - p - r + 1 (logup.rs:466-468)
+inline Fp2 eq_step(Fp2 cpref, Fp2 p, Fp2 r) {
+    const Fp2 pr = f2mul(p, r);
+    return f2mul(cpref, f2add(f2sub(f2sub(f2add(pr, pr), p), r), Fp2{1, 0}));
+}
+
+// RAII list of arena ids freed on scope exit (mirrors the Rust guards).
+struct Owned {
+    Backend& b;
+    std::vector<uint64_t> ids;
+    explicit Owned(Backend& be) : b(be) {}
+    uint64_t add(uint64_t id) {
+        ids.push_back(id);
+        return id;
+    }
+    void release(uint64_t id) {
+        for (auto& x : ids)
+            if (x == id) {
+                x = 0;
+                b.free(id);
+                return;
+            }
+    }
+    ~Owned() {
+        for (uint64_t id : ids)
+            if (id) b.api().volta_cuda_resident_free(b.ctx(), id);
+    }
+};
+
+void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t n, uint64_t alpha1,
+                               FpStream& chal, std::vector<Fp2>& proof);
+TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
+                                       FpStream& tx);
+
+}  // namespace vzh

@@ -1,0 +1,220 @@
+// Scheduled protocol drivers.
+//
+// In the clear sink (logup.rs:1601-1622) and the private transcript
+// (transcript.rs:84-103: FpStream(seed, u64::MAX)) every challenge is the next
+// draw of a seeded stream that never absorbs a message.  The challenge
+// sequence, every claim point and every suffix-eq table are therefore known
+// before the first kernel runs.  These drivers draw them first, in the exact
+// order of the round-by-round callers (hadamard.rs:186-260, logup.rs:995-1470),
+// enqueue every round on the context's stream with its message written to a
+// device slot (the *_into_device entry points), and bring all messages home in
+// one download.  The host then forms the proof words (h0, h2 = cpref (lambda pq
+// + qq), logup.rs:452-453) exactly as the round-by-round driver does.
+//
+// Nothing waits on the GPU between rounds, so the GPU runs the rounds back to
+// back instead of idling for a host round trip per round.
+#include <cstring>
+
+#include "protocol.hpp"
+
+namespace vzh {
+
+namespace {
+
+// Layout of one side's message buffer: roots, then per layer l its l round
+// accumulators (4 Fp2 each) followed by its 4 split values.
+size_t layer_msg_offset(size_t l) { return 2 + 2 * l * (l - 1) + 4 * l; }
+
+}  // namespace
+
+TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
+                                       FpStream& tx) {
+    const Api& A = b.api();
+    const ExtApi& X = b.ext();
+    void* ctx = b.ctx();
+    size_t k = 0;
+    while ((size_t{1} << k) < n) ++k;
+    if ((size_t{1} << k) != n) throw AccelError("triple sumcheck needs a power-of-two table length");
+    std::vector<Fp2> r(k);
+    for (auto& x : r) x = tx.next_fp2();
+    Owned own(b);
+    // slots: 3 per round message, then the 3 final openings
+    const uint64_t msgs = own.add(b.alloc((3 * k + 3) * sizeof(Fp2)));
+    uint64_t cur[3] = {a, bb, c};
+    bool owned = false;
+    if (k)
+        b.check(A.volta_cuda_fp2_triple_product_round_into_device(ctx, a, 0, bb, 0, c, 0, n / 2, msgs, 0),
+                "fp2_triple_product_round_into_device");
+    size_t len = n;
+    for (size_t j = 0; j < k; ++j) {
+        const size_t pairs = len / 2;
+        if (pairs == 1) {  // last fold: the openings land in their slots
+            for (int t = 0; t < 3; ++t)
+                b.check(A.volta_cuda_fp2_fold_rows_device(ctx, cur[t], 0, 1, 2, r[j], msgs, 3 * k + t),
+                        "fp2_fold_rows_device");
+            break;
+        }
+        uint64_t nxt[3];
+        for (int t = 0; t < 3; ++t) nxt[t] = own.add(b.alloc(pairs * sizeof(Fp2)));
+        if (X.triple_fold_round_into) {
+            b.check(X.triple_fold_round_into(ctx, cur[0], cur[1], cur[2], len, r[j], nxt[0], nxt[1], nxt[2], msgs,
+                                             3 * (j + 1)),
+                    "volta_b200_triple_fold_round_into_device");
+        } else {
+            for (int t = 0; t < 3; ++t)
+                b.check(A.volta_cuda_fp2_fold_rows_device(ctx, cur[t], 0, 1, len, r[j], nxt[t], 0),
+                        "fp2_fold_rows_device");
+            b.check(A.volta_cuda_fp2_triple_product_round_into_device(ctx, nxt[0], 0, nxt[1], 0, nxt[2], 0,
+                                                                      pairs / 2, msgs, 3 * (j + 1)),
+                    "fp2_triple_product_round_into_device");
+        }
+        for (int t = 0; t < 3; ++t) {
+            if (owned) own.release(cur[t]);
+            cur[t] = nxt[t];
+        }
+        owned = true;
+        len = pairs;
+    }
+    if (!k)  // a single entry: the openings are the inputs
+        for (int t = 0; t < 3; ++t)
+            b.check(A.volta_cuda_resident_copy_rows(ctx, cur[t], 0, sizeof(Fp2), msgs, t * sizeof(Fp2),
+                                                    sizeof(Fp2), 1, sizeof(Fp2)),
+                    "resident_copy_rows");
+    std::vector<Fp2> host(3 * k + 3);
+    b.download(msgs, 0, host.data(), host.size() * sizeof(Fp2));
+    TripleResult out;
+    out.messages.assign(host.begin(), host.begin() + 3 * k);
+    for (int t = 0; t < 3; ++t) out.finals[t] = host[3 * k + t];
+    return out;
+}
+
+void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t n, uint64_t alpha1,
+                               FpStream& chal, std::vector<Fp2>& proof) {
+    const Api& A = b.api();
+    const ExtApi& X = b.ext();
+    void* ctx = b.ctx();
+    size_t depth = 0;
+    while ((size_t{1} << depth) < n) ++depth;
+    // ---- every challenge of this side, in the round-by-round order:
+    // per layer l: lambda, l round challenges, the split challenge t.
+    std::vector<Fp2> lambda(depth), t(depth);
+    std::vector<std::vector<Fp2>> r(depth), point(depth);
+    for (size_t l = 0; l < depth; ++l) {
+        lambda[l] = chal.next_fp2();
+        r[l].resize(l);
+        for (auto& x : r[l]) x = chal.next_fp2();
+        t[l] = chal.next_fp2();
+        if (l + 1 < depth) {  // claim point of the next layer: (t, r')
+            point[l + 1].push_back(t[l]);
+            point[l + 1].insert(point[l + 1].end(), r[l].begin(), r[l].end());
+        }
+    }
+    Owned own(b);
+    // all claim points in one upload: point l at offset l(l-1)/2
+    const size_t pts_total = depth * (depth - 1) / 2;
+    uint64_t pts = 0;
+    if (pts_total) {
+        std::vector<Fp2> flat;
+        flat.reserve(pts_total);
+        for (size_t l = 0; l < depth; ++l) flat.insert(flat.end(), point[l].begin(), point[l].end());
+        pts = own.add(b.alloc(pts_total * sizeof(Fp2)));
+        b.upload(pts, 0, flat.data(), pts_total * sizeof(Fp2));
+    }
+    const size_t msg_total = layer_msg_offset(depth);
+    const uint64_t msgs = own.add(b.alloc(msg_total * sizeof(Fp2)));
+    // ---- the fraction tree and its root
+    const uint64_t tp = own.add(b.alloc((n > 1 ? n - 1 : 1) * sizeof(Fp2)));
+    const uint64_t tq = own.add(b.alloc((n > 1 ? n - 1 : 1) * sizeof(Fp2)));
+    b.check(A.volta_cuda_logup_tree_device(ctx, leaf, 0, mult, 0, n, alpha1, mult ? 1 : 0, tp, 0, tq, 0),
+            "logup_tree_device");
+    b.check(A.volta_cuda_resident_copy_rows(ctx, tp, 0, sizeof(Fp2), msgs, 0, sizeof(Fp2), 1, sizeof(Fp2)),
+            "resident_copy_rows");
+    b.check(A.volta_cuda_resident_copy_rows(ctx, tq, 0, sizeof(Fp2), msgs, sizeof(Fp2), sizeof(Fp2), 1,
+                                            sizeof(Fp2)),
+            "resident_copy_rows");
+    // ---- layers, all enqueued without a host wait
+    for (size_t l = 0; l < depth; ++l) {
+        Owned layer(b);
+        const size_t L = l, vector_len = size_t{1} << l, child_len = size_t{2} << l;
+        const size_t moff = layer_msg_offset(l), split = moff + 4 * L;
+        uint64_t src_p = tp, src_q = tq;
+        size_t child_off = child_len - 1;
+        if (l + 1 == depth) {
+            src_p = layer.add(b.alloc(n * sizeof(Fp2)));
+            src_q = layer.add(b.alloc(n * sizeof(Fp2)));
+            b.check(A.volta_cuda_logup_materialize_leaves_device(ctx, leaf, 0, mult, 0, n, alpha1, mult ? 1 : 0,
+                                                                 src_p, 0, src_q, 0),
+                    "logup_materialize_leaves_device");
+            child_off = 0;
+        }
+        if (L == 0) {  // no rounds: the split values are the two children
+            b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_p, child_off, 1, msgs, split, msgs, split + 1),
+                    "fp2_deinterleave_device");
+            b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_q, child_off, 1, msgs, split + 2, msgs,
+                                                         split + 3),
+                    "fp2_deinterleave_device");
+            continue;
+        }
+        uint64_t v[4];
+        for (auto& x : v) x = layer.add(b.alloc(vector_len * sizeof(Fp2)));
+        b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_p, child_off, vector_len, v[0], 0, v[1], 0),
+                "fp2_deinterleave_device");
+        b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_q, child_off, vector_len, v[2], 0, v[3], 0),
+                "fp2_deinterleave_device");
+        const uint64_t suffix = layer.add(b.alloc(((size_t{1} << L) - 1) * sizeof(Fp2)));
+        b.check(A.volta_cuda_logup_suffix_eq_device(ctx, pts, L * (L - 1) / 2, L, suffix, 0),
+                "logup_suffix_eq_device");
+        size_t len = vector_len;
+        b.check(A.volta_cuda_logup_general_round_into_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, suffix,
+                                                             (size_t{1} << (L - 1)) - 1, len / 2, msgs, moff),
+                "logup_general_round_into_device");
+        for (size_t j = 0; j < L; ++j) {
+            const size_t half = len / 2;
+            if (half == 1) {  // last fold: the split values land in their slots
+                b.check(A.volta_cuda_logup_fold4_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, 1, r[l][j], msgs,
+                                                        split, msgs, split + 1, msgs, split + 2, msgs, split + 3),
+                        "logup_fold4_device");
+                break;
+            }
+            uint64_t nv[4];
+            for (auto& x : nv) x = layer.add(b.alloc(half * sizeof(Fp2)));
+            const size_t soff = (size_t{1} << (L - 2 - j)) - 1;  // suffix table of round j + 1
+            if (X.logup_fold_round_into) {
+                b.check(X.logup_fold_round_into(ctx, v[0], v[1], v[2], v[3], len, r[l][j], nv[0], nv[1], nv[2],
+                                                nv[3], suffix, soff, msgs, moff + 4 * (j + 1)),
+                        "volta_b200_logup_fold_round_into_device");
+            } else {
+                b.check(A.volta_cuda_logup_fold4_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, half, r[l][j],
+                                                        nv[0], 0, nv[1], 0, nv[2], 0, nv[3], 0),
+                        "logup_fold4_device");
+                b.check(A.volta_cuda_logup_general_round_into_device(ctx, nv[0], 0, nv[1], 0, nv[2], 0, nv[3], 0,
+                                                                     suffix, soff, half / 2, msgs,
+                                                                     moff + 4 * (j + 1)),
+                        "logup_general_round_into_device");
+            }
+            for (int k = 0; k < 4; ++k) {
+                layer.release(v[k]);
+                v[k] = nv[k];
+            }
+            len = half;
+        }
+    }
+    // ---- one download, then the proof words in the round-by-round order
+    std::vector<Fp2> m(msg_total);
+    b.download(msgs, 0, m.data(), msg_total * sizeof(Fp2));
+    proof.push_back(m[0]);
+    proof.push_back(m[1]);
+    for (size_t l = 0; l < depth; ++l) {
+        const size_t moff = layer_msg_offset(l);
+        Fp2 cpref{1, 0};
+        for (size_t j = 0; j < l; ++j) {
+            const Fp2* acc = &m[moff + 4 * j];
+            proof.push_back(f2mul(cpref, f2add(f2mul(lambda[l], acc[0]), acc[2])));
+            proof.push_back(f2mul(cpref, f2add(f2mul(lambda[l], acc[1]), acc[3])));
+            cpref = eq_step(cpref, point[l][j], r[l][j]);
+        }
+        for (int k = 0; k < 4; ++k) proof.push_back(m[moff + 4 * l + k]);
+    }
+}
+
+}  // namespace vzh
