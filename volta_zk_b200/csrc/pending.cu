@@ -72,58 +72,3 @@ extern "C" int volta_cuda_attention_proof_wires_device(void* ctx, const vz_atten
     return pending(ctx, "volta_cuda_attention_proof_wires_device");
 }
 
-extern "C" int volta_cuda_ntt_fp(void* ctx, const uint64_t* msg, size_t msg_len, size_t n, uint64_t* out) {
-    return pending(ctx, "volta_cuda_ntt_fp");
-}
-
-extern "C" int volta_cuda_ntt_fp_batch(void* ctx, const uint64_t* messages, size_t rows, size_t msg_len, size_t n, uint64_t* out) {
-    return pending(ctx, "volta_cuda_ntt_fp_batch");
-}
-
-extern "C" int volta_cuda_ntt_fp2(void* ctx, const Fp2* msg, size_t msg_len, size_t n, Fp2* out) {
-    return pending(ctx, "volta_cuda_ntt_fp2");
-}
-
-extern "C" int volta_cuda_ntt_fp_batch_device(void* ctx, uint64_t input_id, size_t input_offset, size_t rows, size_t n, uint64_t output_id, size_t output_offset) {
-    return pending(ctx, "volta_cuda_ntt_fp_batch_device");
-}
-
-extern "C" int volta_cuda_ntt_fp2_batch_device(void* ctx, uint64_t input_id, size_t input_offset, size_t rows, size_t n, uint64_t output_id, size_t output_offset) {
-    return pending(ctx, "volta_cuda_ntt_fp2_batch_device");
-}
-
-extern "C" int volta_cuda_pcs_messages_device(void* ctx, uint64_t weights_id, size_t weights_offset, uint64_t pads_id, size_t pads_offset, size_t rows, size_t cols, size_t pad, size_t code_len, uint64_t output_id, size_t output_offset) {
-    return pending(ctx, "volta_cuda_pcs_messages_device");
-}
-
-extern "C" int volta_cuda_pcs_combine_rows_device(void* ctx, uint64_t weights_id, size_t weights_offset, uint64_t pads_id, size_t pads_offset, uint64_t coeffs_id, size_t coeffs_offset, size_t rows, size_t cols, size_t pad, size_t combinations, uint64_t output_id, size_t output_offset) {
-    return pending(ctx, "volta_cuda_pcs_combine_rows_device");
-}
-
-extern "C" int volta_cuda_hash_fp_tree_device(void* ctx, uint64_t matrix_id, size_t matrix_offset, size_t rows, size_t cols, uint64_t tree_id, size_t tree_offset_bytes) {
-    return pending(ctx, "volta_cuda_hash_fp_tree_device");
-}
-
-extern "C" int volta_cuda_hash_fp2_tree_device(void* ctx, uint64_t matrix_id, size_t matrix_offset, size_t rows, size_t cols, uint64_t tree_id, size_t tree_offset_bytes) {
-    return pending(ctx, "volta_cuda_hash_fp2_tree_device");
-}
-
-extern "C" int volta_cuda_merkle_paths_device(void* ctx, uint64_t tree_id, size_t tree_offset_bytes, size_t leaves, uint64_t indices_id, size_t indices_offset, size_t queries, uint64_t paths_id, size_t paths_offset_bytes) {
-    return pending(ctx, "volta_cuda_merkle_paths_device");
-}
-
-extern "C" int volta_cuda_pcs_gather_columns_device(void* ctx, uint64_t matrix_id, size_t matrix_offset, size_t rows, size_t cols, uint64_t indices_id, size_t indices_offset, size_t queries, uint64_t output_id, size_t output_offset, int fp2) {
-    return pending(ctx, "volta_cuda_pcs_gather_columns_device");
-}
-
-extern "C" int volta_cuda_pcs_combine_rows(void* ctx, const int16_t* weights, const uint64_t* pads, const Fp2* coeffs, size_t rows, size_t cols, size_t pad, size_t combinations, Fp2* out) {
-    return pending(ctx, "volta_cuda_pcs_combine_rows");
-}
-
-extern "C" int volta_cuda_pcs_gather_columns(void* ctx, const uint64_t* matrix, size_t rows, size_t cols, const uint32_t* indices, size_t queries, uint64_t* out) {
-    return pending(ctx, "volta_cuda_pcs_gather_columns");
-}
-
-extern "C" int volta_cuda_hash_fp_columns(void* ctx, const uint64_t* matrix, size_t rows, size_t cols, uint8_t* leaves) {
-    return pending(ctx, "volta_cuda_hash_fp_columns");
-}
