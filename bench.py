@@ -37,6 +37,7 @@ SUMCHECK_SEED = bytes([0x51] * 32)
 TRANSCRIPT_SEED = bytes([0x5A] * 32)
 LOGUP_SEED = bytes([0x4C] * 32)
 LOGUP_DOMAIN = 0x1004
+LIGERO_ROW_SEED = bytes([0x11] * 32)
 
 
 def parse():
@@ -48,6 +49,11 @@ def parse():
     ap.add_argument("--log2-sumcheck", type=int, default=24)
     ap.add_argument("--log2-queries", type=int, default=24)
     ap.add_argument("--log2-table", type=int, default=16)
+    ap.add_argument("--ligero-rows", type=int, default=8192)
+    ap.add_argument("--ligero-log2-msg", type=int, default=14)
+    ap.add_argument("--ligero-log2-code", type=int, default=16)
+    ap.add_argument("--ligero-queries", type=int, default=128)
+    ap.add_argument("--no-ligero", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -169,6 +175,68 @@ def cpu_sample(log2_sample: int, log2_table: int, steps: int = 1):
 # B200 arm
 # ---------------------------------------------------------------------------
 
+def ligero_leg(args, prover, be, peaks):
+    """Ligero commitment of rows x 2^msg seeded Fp message
+    rows, RS-encoded to 2^code columns (rate 1/4 at the defaults), BLAKE3
+    column Merkle tree and 128 column openings, through the host API (one
+    call per commitment; the message rows are generated on the device by the
+    ChaCha8 row kernel, the root, columns and paths come back to the host)."""
+    rows, msg, code, q = args.ligero_rows, 1 << args.ligero_log2_msg, 1 << args.ligero_log2_code, args.ligero_queries
+
+    def step():
+        return prover.ligero_commit_open(LIGERO_ROW_SEED, rows, msg, code, q, TRANSCRIPT_SEED)
+
+    for _ in range(max(1, args.warmup)):
+        out = step()
+    be.mark(6)
+    for _ in range(args.steps):
+        out = step()
+    be.mark(7)
+    commit_s = be.elapsed_ms(6, 7) / 1e3 / args.steps
+    # dominant kernels alone on a resident codeword (in place, inputs >> L2)
+    buf = be.alloc(8 * rows * code)
+    be.call("chacha8_prover_secret_fp_rows_device", buf, 0, LIGERO_ROW_SEED, 0, rows, code)
+    tree = be.alloc(32 * (2 * code - 1))
+    reps = 5
+    be.call("ntt_fp_batch_device", buf, 0, rows, code, buf, 0)
+    be.mark(8)
+    for _ in range(reps):
+        be.call("ntt_fp_batch_device", buf, 0, rows, code, buf, 0)
+    be.mark(9)
+    be.call("hash_fp_tree_device", buf, 0, rows, code, tree, 0)
+    be.mark(10)
+    for _ in range(reps):
+        be.call("hash_fp_tree_device", buf, 0, rows, code, tree, 0)
+    be.mark(11)
+    ntt_ms = be.elapsed_ms(8, 9) / reps
+    hash_ms = be.elapsed_ms(10, 11) / reps
+    be.free(buf)
+    be.free(tree)
+    data = 8 * rows * code
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    butterflies = rows * (code // 2) * args.ligero_log2_code
+    chunks = (rows * 8 + 1023) // 1024
+    compressions = code * (chunks * 16 + chunks - 1) + (code - 1)
+    return {
+        "workload": f"config 2: Ligero commit {rows} rows x 2^{args.ligero_log2_msg} msg -> 2^{args.ligero_log2_code} "
+                    f"code, BLAKE3 column Merkle, {q} openings",
+        "value": round(commit_s, 6), "unit": "s/commitment", "higher_is_better": False,
+        "root": out[0].hex(),
+        "kernels": {
+            "ntt_fp_batch": {"avg_launch_ms": round(ntt_ms, 4),
+                             "hbm_gbs": round(2 * data / (ntt_ms / 1e3) / 1e9, 1),
+                             "frac_of_hbm_peak": round(2 * data / (ntt_ms / 1e3) / 1e9 / hbm, 4),
+                             "butterflies_per_s": round(butterflies / (ntt_ms / 1e3), 1),
+                             "algorithmic_bytes": 2 * data},
+            "hash_fp_tree": {"avg_launch_ms": round(hash_ms, 4),
+                             "hbm_gbs": round(data / (hash_ms / 1e3) / 1e9, 1),
+                             "frac_of_hbm_peak": round(data / (hash_ms / 1e3) / 1e9 / hbm, 4),
+                             "blake3_compressions_per_s": round(compressions / (hash_ms / 1e3), 1),
+                             "algorithmic_bytes": data},
+        },
+    }
+
+
 def run_b200(args, rank, world, local_rank):
     import torch
 
@@ -238,21 +306,27 @@ def run_b200(args, rank, world, local_rank):
     # ---- e2e through the C ABI with host buffers ---------------------------
     e2e = None
     if not args.no_e2e:
-        host_tables = [be.download_fp2(t, n) for t in tables]
-        pinned = [torch.from_numpy(x).pin_memory() for x in host_tables]
-        fcol_h = torch.from_numpy(embed_i16(f)).pin_memory()
-        tcol_h = torch.from_numpy(embed_i16(table)).pin_memory()
+        # the user's tables are Fp columns (8 B per entry); they are lifted to
+        # Fp2 on the device (base_broadcast_fp2_device) after the upload
+        host_cols = [np.ascontiguousarray(be.download_fp2(t, n)[:, 0]) for t in tables]
+        pinned = [torch.from_numpy(x.view(np.int64)).pin_memory() for x in host_cols]
+        fcol_h = torch.from_numpy(embed_i16(f).view(np.int64)).pin_memory()
+        tcol_h = torch.from_numpy(embed_i16(table).view(np.int64)).pin_memory()
         mult_h = torch.from_numpy(mult.astype(np.int32)).pin_memory()
-        bufs = [be.alloc(16 * n) for _ in range(3)] + [be.alloc(8 * n_f), be.alloc(8 * n_t), be.alloc(4 * n_t)]
-        h2d = 3 * 16 * n + 8 * n_f + 8 * n_t + 4 * n_t
+        ups = [be.alloc(8 * n) for _ in range(3)] + [be.alloc(8 * n_f), be.alloc(8 * n_t), be.alloc(4 * n_t)]
+        lifted = [be.alloc(16 * n) for _ in range(3)]
+        bufs = ups + lifted
+        h2d = 3 * 8 * n + 8 * n_f + 8 * n_t + 4 * n_t
         d2h = 16 * (3 * args.log2_sumcheck + 3) + 16 * cap
 
         def e2e_step():
-            for buf, t in zip(bufs, pinned + [fcol_h, tcol_h, mult_h]):
+            for buf, t in zip(ups, pinned + [fcol_h, tcol_h, mult_h]):
                 be.check(be.lib.volta_cuda_resident_upload(be.ctx, buf, 0, t.data_ptr(),
                                                            t.numel() * t.element_size()), "upload")
-            prover.triple_sumcheck(bufs[0], bufs[1], bufs[2], n, TRANSCRIPT_SEED)
-            prover.logup_prove(bufs[3], n_f, bufs[4], n_t, bufs[5], LOGUP_SEED, LOGUP_DOMAIN, cap)
+            for col, tid in zip(ups[:3], lifted):
+                be.call("base_broadcast_fp2_device", col, 0, tid, 0, n, 1, 2)
+            prover.triple_sumcheck(lifted[0], lifted[1], lifted[2], n, TRANSCRIPT_SEED)
+            prover.logup_prove(ups[3], n_f, ups[4], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN, cap)
 
         e2e_step()
         barrier()
@@ -292,6 +366,8 @@ def run_b200(args, rank, world, local_rank):
                 "frac": round(achieved / peak, 4), "traffic": None, "algorithmic_bytes": alg_bytes,
                 "avg_launch_ms": round(kern_ms, 4)}
 
+    ligero = None if args.no_ligero else ligero_leg(args, prover, be, peaks)
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         log2_sample = max(10, min(20, args.log2_sumcheck) - 0)
@@ -315,6 +391,7 @@ def run_b200(args, rank, world, local_rank):
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "gpu_launches": launches,
             "clocks": clocks.summary(),
             "proof_check": {"messages": int(msgs.shape[0]), "proof_words": int(proof.shape[0])},
+            "ligero": ligero,
         }
         print(json.dumps(line), flush=True)
     prover.close()

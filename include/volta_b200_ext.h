@@ -15,7 +15,7 @@
 extern "C" {
 #endif
 
-/* Record timing marker `slot` (0..7) on the context's stream. */
+/* Record timing marker `slot` (0..15) on the context's stream. */
 int volta_b200_timing_mark(void* ctx, int slot);
 /* Wait for marker `end` and return the device time between two markers. */
 int volta_b200_timing_elapsed(void* ctx, int start, int end, float* ms);

@@ -381,3 +381,21 @@ def gemm_requant_auth(a, b, masks, m, k, n, shift):
 def fnv_u64(values: np.ndarray, h: int = 0xCBF29CE484222325) -> int:
     v = np.ascontiguousarray(values, dtype=np.uint64).reshape(-1)
     return lib().or_fnv_u64(h, _p(v), v.size)
+
+
+def ligero_commit_open(row_seed: bytes, rows: int, msg_len: int, code_len: int, queries: int, chal_seed: bytes):
+    """Resident Ligero commitment + openings on the CPU
+    (rust/volta-pcs/src/ligero.rs:465-505 commit, 1440-1480 openings):
+    message row r = FpStream(row_seed, r) x msg_len, zero-padded to code_len,
+    forward NTT per row, BLAKE3 column leaves, Merkle tree; query j =
+    challenge_fp2().c0 mod code_len from FpStream(chal_seed, u64::MAX).
+    Returns (root bytes, indices, columns [queries x rows], paths)."""
+    msgs = chacha_fp_rows(row_seed, 0, rows, msg_len)
+    code = ntt_batch(msgs, rows, msg_len, code_len).reshape(rows, code_len)
+    tree = merkle_tree(hash_fp_columns(code, rows, code_len))
+    tx = FpStream(chal_seed, 2**64 - 1)
+    idx = np.array([tx.next_fp2()[0] % code_len for _ in range(queries)], dtype=np.uint32)
+    cols = np.ascontiguousarray(code[:, idx].T)
+    bits = code_len.bit_length() - 1
+    paths = merkle_paths(tree, code_len, idx).reshape(queries, bits, 32) if bits else np.zeros((queries, 0, 32), np.uint8)
+    return tree[-1].tobytes(), idx, cols, paths

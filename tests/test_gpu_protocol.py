@@ -92,3 +92,14 @@ def test_logup_roots_cross_check(prover, oracle):
     assert ((x[0] + y[0]) % P, (x[1] + y[1]) % P) == (0, 0)
     for i in ids:
         be.free(i)
+
+
+@pytest.mark.parametrize("rows,msg_len,code_len,queries", [(1, 1, 2, 1), (8, 16, 64, 5), (64, 256, 1024, 32),
+                                                           (256, 4096, 16384, 128)])
+def test_ligero_commit_open_matches_oracle(prover, oracle, rows, msg_len, code_len, queries):
+    row_seed, chal_seed = bytes([0x11] * 32), bytes([0x5A] * 32)
+    got = prover.ligero_commit_open(row_seed, rows, msg_len, code_len, queries, chal_seed)
+    exp = oracle.ligero_commit_open(row_seed, rows, msg_len, code_len, queries, chal_seed)
+    assert got[0] == exp[0]
+    for g, e in zip(got[1:], exp[1:]):
+        assert np.array_equal(g, e)

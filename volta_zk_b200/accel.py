@@ -155,6 +155,8 @@ def load_host_library():
         L.vzh_triple_sumcheck.argtypes = [vp, u64, u64, u64, sz, C.c_char_p, vp, vp, C.c_char_p, sz]
         L.vzh_logup_prove.argtypes = [vp, u64, sz, u64, sz, u64, C.c_char_p, u64, vp, sz,
                                       C.POINTER(C.c_size_t), C.c_char_p, sz]
+        L.vzh_ligero_commit_open.argtypes = [vp, C.c_char_p, sz, sz, sz, sz, C.c_char_p, vp, vp, vp, vp,
+                                             C.c_char_p, sz]
         L.vzh_fpstream_u64.argtypes = [C.c_char_p, u64, sz, vp]
         _host_lib = L
     return _host_lib
@@ -313,6 +315,21 @@ class Prover:
                                        C.byref(written), err, 1024)
         self._err(rc, err)
         return out[: written.value]
+
+    def ligero_commit_open(self, row_seed: bytes, rows: int, msg_len: int, code_len: int, queries: int,
+                           chal_seed: bytes):
+        """Commit seeded message rows and open `queries` columns: (root bytes,
+        indices, columns [queries x rows], paths [queries x log2(code_len) x 32])."""
+        bits = code_len.bit_length() - 1
+        root = np.zeros(32, dtype=np.uint8)
+        idx = np.zeros(queries, dtype=np.uint32)
+        cols = np.zeros((queries, rows), dtype=np.uint64)
+        paths = np.zeros((queries, bits, 32), dtype=np.uint8)
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_ligero_commit_open(self.h, row_seed, rows, msg_len, code_len, queries, chal_seed,
+                                              _ptr(root), _ptr(idx), _ptr(cols), _ptr(paths), err, 1024)
+        self._err(rc, err)
+        return root.tobytes(), idx, cols, paths
 
     def stats(self) -> RawStats:
         return self.backend.stats()

@@ -1307,7 +1307,7 @@ extern "C" int volta_cuda_resident_mailbox_copy_rows(void* raw, uint64_t src_id,
 
 extern "C" int volta_b200_timing_mark(void* raw, int slot) {
     Context* c = static_cast<Context*>(raw);
-    if (!c || slot < 0 || slot >= 8) return fail_message(c, "invalid timing marker slot");
+    if (!c || slot < 0 || slot >= kTimingMarkers) return fail_message(c, "invalid timing marker slot");
     if (!c->bench_ev[slot]) VZB_CUDA(c, cudaEventCreate(&c->bench_ev[slot]));
     VZB_CUDA(c, cudaEventRecord(c->bench_ev[slot], c->stream));
     return 0;
@@ -1315,7 +1315,7 @@ extern "C" int volta_b200_timing_mark(void* raw, int slot) {
 
 extern "C" int volta_b200_timing_elapsed(void* raw, int start, int end, float* ms) {
     Context* c = static_cast<Context*>(raw);
-    if (!c || !ms || start < 0 || start >= 8 || end < 0 || end >= 8 || !c->bench_ev[start] ||
+    if (!c || !ms || start < 0 || start >= kTimingMarkers || end < 0 || end >= kTimingMarkers || !c->bench_ev[start] ||
         !c->bench_ev[end])
         return fail_message(c, "invalid timing marker pair");
     VZB_CUDA(c, cudaEventSynchronize(c->bench_ev[end]));

@@ -94,6 +94,8 @@ struct Record {
 };
 
 // Grow-only private workspace (never visible through the arena).
+constexpr int kTimingMarkers = 16;  // measurement marker slots (extension ABI)
+
 struct Workspace {
     void* ptr = nullptr;
     size_t capacity = 0;
@@ -152,7 +154,7 @@ struct Context {
     size_t twiddle_n = 0;
     uint32_t mail_seq = 0;               // sequence number of host-bound messages
     uint64_t launches = 0;               // kernels launched by this context
-    cudaEvent_t bench_ev[8] = {};        // measurement markers (extension ABI)
+    cudaEvent_t bench_ev[kTimingMarkers] = {};        // measurement markers (extension ABI)
     std::string error;
 };
 

@@ -132,4 +132,18 @@ TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint6
 std::vector<Fp2> logup_prove_resident(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col,
                                       size_t n_t, uint64_t mult, FpStream& chal);
 
+// Ligero commitment of `rows` seeded Fp message rows (FpStream(row_seed, r),
+// msg_len words each) zero-padded to code_len, and `queries` column openings
+// at challenge_fp2().c0 mod code_len drawn from `tx` (ligero.rs:465-505,
+// 1440-1480).  Columns are query-major (queries x rows); paths hold
+// log2(code_len) sibling hashes per query, leaf level first.
+struct LigeroOpening {
+    uint8_t root[32];
+    std::vector<uint32_t> indices;
+    std::vector<uint64_t> columns;
+    std::vector<uint8_t> paths;
+};
+LigeroOpening ligero_commit_open_resident(Backend& b, const uint8_t row_seed[32], size_t rows, size_t msg_len,
+                                          size_t code_len, size_t queries, FpStream& tx);
+
 }  // namespace vzh

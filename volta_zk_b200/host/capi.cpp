@@ -91,6 +91,23 @@ int vzh_logup_prove(void* h, uint64_t f_col, size_t n_f, uint64_t t_col, size_t 
     });
 }
 
+// Ligero commitment + openings (see accel.hpp); challenges from
+// FpStream(chal_seed, u64::MAX).  columns: queries x rows u64, paths:
+// queries x log2(code_len) x 32 bytes.
+int vzh_ligero_commit_open(void* h, const uint8_t* row_seed, size_t rows, size_t msg_len, size_t code_len,
+                           size_t queries, const uint8_t* chal_seed, uint8_t* root, uint32_t* indices,
+                           uint64_t* columns, uint8_t* paths, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        FpStream tx(chal_seed, UINT64_MAX);
+        LigeroOpening o = ligero_commit_open_resident(*static_cast<Backend*>(h), row_seed, rows, msg_len, code_len,
+                                                      queries, tx);
+        std::memcpy(root, o.root, 32);
+        std::memcpy(indices, o.indices.data(), o.indices.size() * sizeof(uint32_t));
+        std::memcpy(columns, o.columns.data(), o.columns.size() * sizeof(uint64_t));
+        std::memcpy(paths, o.paths.data(), o.paths.size());
+    });
+}
+
 // Raw u64 draws of FpStream(seed, domain) (input synthesis for benches).
 void vzh_fpstream_u64(const uint8_t* seed, uint64_t domain, size_t n, uint64_t* out) {
     FpStream s(seed, domain);
