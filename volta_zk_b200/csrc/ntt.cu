@@ -10,13 +10,16 @@
 //   * n <= 2^11: one CTA holds whole rows in shared memory (the bit
 //     reversal happens on the load), runs every stage there and writes the
 //     rows back: one read and one write of the data.
-//   * 2^12 <= n <= 2^22: the six-step split n = n1 * n2 (n1, n2 <= 2^11).
-//     Pass 1 runs the n2 column DFTs of length n1 on tiles of T adjacent
-//     columns, applies w^(j2 k1) and stores the tile transposed; pass 2 runs
-//     the n1 row DFTs of length n2 and stores X[k1 + n1 k2].  Every global
-//     access moves T consecutive elements (128 B for Fp).  Rows go through
-//     in chunks whose transposed intermediate stays in L2, so HBM sees one
-//     read of the input and one write of the output.
+//   * 2^12 <= n <= 2^16 (the Ligero code lengths): the six-step split
+//     n = n1 * n2 (n1, n2 in 64..256).  Pass 1 runs the n2 column DFTs of
+//     length n1, applies w^(j2 k1) and stores the result transposed; pass 2
+//     runs the n1 row DFTs of length n2 and stores X[k1 + n1 k2].  Each
+//     length-m DFT is m = RA x RB in registers (radix-8/16 sub-DFTs whose
+//     twiddles are powers of two, i.e. shifts) with a single shared-memory
+//     exchange; every global access covers 16 adjacent elements (128 B for
+//     Fp).  Rows go through in chunks whose transposed intermediate stays in
+//     L2, so HBM sees one read of the input and one write of the output.
+//   * 2^17 <= n <= 2^22: the same split with shared-memory radix-2 sub-DFTs.
 //   * larger n: the per-stage global algorithm (correct, not tuned).
 #include "runtime.cuh"
 
@@ -27,18 +30,153 @@ constexpr int kNttThreads = 256;
 constexpr int kSmallMaxBits = 11;
 constexpr size_t kNttChunkBytes = size_t{48} << 20;  // transposed intermediate kept in L2
 
+// x * 2^s mod p for 0 <= s < 192 (2 has order 192: 2^96 = -1).  With s a
+// compile-time constant after unrolling this is a few funnel shifts and one
+// reduction of the 160-bit shifted value.
+__device__ __forceinline__ uint64_t mul_pow2(uint64_t x, int s) {
+    const bool neg = s >= 96;
+    s = neg ? s - 96 : s;
+    if (s == 0) return neg ? dsub(0, x) : x;
+    const int q = s >> 5, r = s & 31;
+    const uint32_t x0 = lo32(x), x1 = hi32(x);
+    const uint32_t l0 = r ? x0 << r : x0;
+    const uint32_t l1 = r ? __funnelshift_l(x0, x1, r) : x1;
+    const uint32_t l2 = r ? x1 >> (32 - r) : 0;
+    W5 w;
+    w.w[0] = q == 0 ? l0 : 0;
+    w.w[1] = q == 0 ? l1 : (q == 1 ? l0 : 0);
+    w.w[2] = q == 0 ? l2 : (q == 1 ? l1 : l0);
+    w.w[3] = q == 1 ? l2 : (q == 2 ? l1 : 0);
+    w.w[4] = q == 2 ? l2 : 0;
+    const uint64_t y = wreduce(w);
+    return neg ? dsub(0, y) : y;
+}
+
 struct FpOps {
     using T = uint64_t;
     static __device__ __forceinline__ T add(T a, T b) { return fadd(a, b); }
     static __device__ __forceinline__ T sub(T a, T b) { return fsub(a, b); }
     static __device__ __forceinline__ T mulb(T a, uint64_t w) { return fmul(a, w); }
+    static __device__ __forceinline__ T mulp2(T a, int s) { return mul_pow2(a, s); }
 };
 struct Fp2Ops {
     using T = Fp2;
     static __device__ __forceinline__ T add(T a, T b) { return f2add(a, b); }
     static __device__ __forceinline__ T sub(T a, T b) { return f2sub(a, b); }
     static __device__ __forceinline__ T mulb(T a, uint64_t w) { return Fp2{fmul(a.c0, w), fmul(a.c1, w)}; }
+    static __device__ __forceinline__ T mulp2(T a, int s) { return Fp2{mul_pow2(a.c0, s), mul_pow2(a.c1, s)}; }
 };
+
+// Register DFT of R <= 16 values, natural order in and out (radix-2 DIT on
+// the bit-reversed registers).  The R-th roots of unity of the reference's
+// generator are powers of two: w_2 = 2^96, w_4 = 2^48, w_8 = 2^120,
+// w_16 = 2^156 (w_R = 7^((p-1)/R)), so every twiddle is a shift.
+constexpr int ilog2c(int r) { return r <= 1 ? 0 : 1 + ilog2c(r >> 1); }
+constexpr int root_exp(int r) { return r == 2 ? 96 : r == 4 ? 48 : r == 8 ? 120 : 156; }
+
+template <class Ops, int R>
+__device__ __forceinline__ void reg_dft(typename Ops::T (&v)[R]) {
+    using T = typename Ops::T;
+    constexpr int kLog = ilog2c(R);
+    constexpr int kE = root_exp(R);
+    T a[R];
+    // (flat loops with intrinsic index arithmetic unroll completely, so the
+    // arrays stay in registers)
+#pragma unroll
+    for (int i = 0; i < R; ++i) a[__brev(i) >> (32 - kLog)] = v[i];
+#pragma unroll
+    for (int lg = 0; lg < kLog; ++lg) {
+#pragma unroll
+        for (int b = 0; b < R / 2; ++b) {
+            const int k = b & ((1 << lg) - 1);
+            const int i0 = ((b >> lg) << (lg + 1)) + k, i1 = i0 + (1 << lg);
+            const T u = a[i0];
+            const T w = k == 0 ? a[i1] : Ops::mulp2(a[i1], (kE * k * (R >> (lg + 1))) % 192);
+            a[i0] = Ops::add(u, w);
+            a[i1] = Ops::sub(u, w);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < R; ++i) v[i] = a[i];
+}
+
+// One six-step pass over 16 sequences of length m = RA * RB per CTA, all
+// arithmetic in registers with one shared-memory exchange:
+//   step A (16 RB threads): DFT_RA over x[t + RB u] (u < RA), times w_m^(t k)
+//   step B (16 RA threads): DFT_RB over t, giving X[k + RA k'].
+// kCols: the sequences are 16 adjacent columns j2 of the n1 x n2 view (pass
+// 1: length n1, output times w_n^(j2 k1), stored transposed as
+// Y[k1][j2]); otherwise 16 adjacent rows k1 of Y (pass 2: length n2, output
+// X[k1 + n1 k2]).  Every global access covers 16 adjacent elements.
+template <class Ops, int RA, int RB, bool kCols>
+__global__ void __launch_bounds__(16 * (RA > RB ? RA : RB)) ntt_pass_kernel(const typename Ops::T* in,
+                                                                           typename Ops::T* out, int bits1,
+                                                                           int bits2, const uint64_t* tw) {
+    using T = typename Ops::T;
+    constexpr int M = RA * RB;
+    constexpr int kPitchT = RA + 1;              // odd: conflict-free 8-byte accesses
+    constexpr int kPitchSeq = RB * kPitchT + 1;  // odd
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T* S = reinterpret_cast<T*>(smem_raw);
+    uint64_t* twm = reinterpret_cast<uint64_t*>(S + 16 * kPitchSeq);  // w_m^i, i < m
+    const int n1 = 1 << bits1, n2 = 1 << bits2;
+    const int bits = bits1 + bits2;
+    const size_t n = size_t{1} << bits;
+    const int seq_len_bits = kCols ? bits1 : bits2;  // = log2 M
+    const int tiles = (kCols ? n2 : n1) / 16;
+    const size_t row = blockIdx.x / tiles;
+    const int base = (blockIdx.x - static_cast<int>(row * tiles)) * 16;
+    const T* src = in + row * n;
+    T* dst = out + row * n;
+    for (int i = threadIdx.x; i < M; i += blockDim.x) {
+        const size_t e = static_cast<size_t>(i) << (bits - seq_len_bits);
+        twm[i] = e < n / 2 ? __ldg(tw + e) : dsub(0, __ldg(tw + (e - n / 2)));
+    }
+    __syncthreads();
+    // ---- step A
+    if (threadIdx.x < 16 * RB) {
+        int seq, t;
+        if (kCols) {
+            seq = threadIdx.x & 15;
+            t = threadIdx.x >> 4;
+        } else {
+            t = threadIdx.x % RB;
+            seq = threadIdx.x / RB;
+        }
+        T v[RA];
+#pragma unroll
+        for (int u = 0; u < RA; ++u) {
+            const int j = t + RB * u;
+            v[u] = kCols ? src[static_cast<size_t>(j) * n2 + base + seq] : src[static_cast<size_t>(base + seq) * n2 + j];
+        }
+        reg_dft<Ops, RA>(v);
+        T* srow = S + seq * kPitchSeq + t * kPitchT;
+        srow[0] = v[0];
+#pragma unroll
+        for (int k = 1; k < RA; ++k) srow[k] = Ops::mulb(v[k], twm[t * k]);
+    }
+    __syncthreads();
+    // ---- step B
+    if (threadIdx.x < 16 * RA) {
+        const int seq = threadIdx.x & 15, k = threadIdx.x >> 4;
+        T v[RB];
+#pragma unroll
+        for (int t = 0; t < RB; ++t) v[t] = S[seq * kPitchSeq + t * kPitchT + k];
+        reg_dft<Ops, RB>(v);
+#pragma unroll
+        for (int kp = 0; kp < RB; ++kp) {
+            const int kk = k + RA * kp;  // output index within the sequence
+            if (kCols) {
+                const size_t j2 = base + seq;
+                const size_t e = j2 * static_cast<size_t>(kk);  // < n
+                const uint64_t w = e < n / 2 ? __ldg(tw + e) : dsub(0, __ldg(tw + (e - n / 2)));
+                dst[static_cast<size_t>(kk) * n2 + j2] = e ? Ops::mulb(v[kp], w) : v[kp];
+            } else {
+                dst[base + seq + static_cast<size_t>(n1) * kk] = v[kp];
+            }
+        }
+    }
+}
 
 __device__ __forceinline__ unsigned brev_bits(unsigned i, int bits) { return bits ? __brev(i) >> (32 - bits) : 0; }
 
@@ -196,6 +334,32 @@ int ensure_twiddles(Context* c, size_t n) {
     return 0;
 }
 
+template <class Ops, int RA, int RB, bool kCols>
+int launch_pass_rr(Context* c, const typename Ops::T* in, typename Ops::T* out, int bits1, int bits2, size_t rows,
+                   const uint64_t* tw) {
+    using T = typename Ops::T;
+    constexpr int kPitchSeq = RB * (RA + 1) + 1;
+    const size_t smem = 16 * kPitchSeq * sizeof(T) + RA * RB * sizeof(uint64_t);
+    auto k = ntt_pass_kernel<Ops, RA, RB, kCols>;
+    VZB_CUDA(c, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    const size_t tiles = (size_t{1} << (kCols ? bits2 : bits1)) / 16;
+    k<<<static_cast<unsigned>(rows * tiles), 16 * (RA > RB ? RA : RB), smem, c->stream>>>(in, out, bits1, bits2, tw);
+    VZB_LAUNCHED(c);
+    return 0;
+}
+
+// Sequence length 2^len_bits (6..8) split into register radices RA x RB.
+template <class Ops, bool kCols>
+int launch_pass(Context* c, const typename Ops::T* in, typename Ops::T* out, int bits1, int bits2, size_t rows,
+                int len_bits, const uint64_t* tw) {
+    switch (len_bits) {
+        case 6: return launch_pass_rr<Ops, 8, 8, kCols>(c, in, out, bits1, bits2, rows, tw);
+        case 7: return launch_pass_rr<Ops, 16, 8, kCols>(c, in, out, bits1, bits2, rows, tw);
+        case 8: return launch_pass_rr<Ops, 16, 16, kCols>(c, in, out, bits1, bits2, rows, tw);
+        default: return fail_message(c, "internal: unsupported NTT pass length");
+    }
+}
+
 template <class Ops>
 int launch_ntt(Context* c, const typename Ops::T* in, typename Ops::T* out, size_t rows, size_t n) {
     using T = typename Ops::T;
@@ -215,6 +379,21 @@ int launch_ntt(Context* c, const typename Ops::T* in, typename Ops::T* out, size
             k<<<static_cast<unsigned>(nb), kNttThreads, smem, c->stream>>>(in + r0 * n, out + r0 * n, rows - r0,
                                                                            bits, rpc, tw);
             VZB_LAUNCHED(c);
+        }
+        return 0;
+    }
+    if (bits >= 12 && bits <= 16) {
+        // register six-step: n1 = 2^ceil(bits/2), n2 = 2^floor(bits/2), each 64..256
+        const int bits2 = bits / 2, bits1 = bits - bits2;
+        size_t chunk = kNttChunkBytes / (n * sizeof(T));
+        if (chunk < 1) chunk = 1;
+        if (chunk > rows) chunk = rows;
+        if (ensure_ws(c, kWsScratch2, chunk * n * sizeof(T))) return -1;
+        T* y = ws<T>(c, kWsScratch2);
+        for (size_t r0 = 0; r0 < rows; r0 += chunk) {
+            const size_t nr = rows - r0 < chunk ? rows - r0 : chunk;
+            if (launch_pass<Ops, true>(c, in + r0 * n, y, bits1, bits2, nr, bits1, tw)) return -1;
+            if (launch_pass<Ops, false>(c, y, out + r0 * n, bits1, bits2, nr, bits2, tw)) return -1;
         }
         return 0;
     }

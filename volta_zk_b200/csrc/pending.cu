@@ -12,22 +12,6 @@ int pending(void* raw, const char* what) {
 }
 }  // namespace
 
-extern "C" int volta_cuda_gemm_i64(void* ctx, const int16_t* a, const int16_t* b, int64_t* out, size_t m, size_t k, size_t n) {
-    return pending(ctx, "volta_cuda_gemm_i64");
-}
-
-extern "C" int volta_cuda_gemm_i64_device(void* ctx, uint64_t a_id, size_t a_offset, uint64_t b_id, size_t b_offset, uint64_t out_id, size_t out_offset, size_t m, size_t k, size_t n) {
-    return pending(ctx, "volta_cuda_gemm_i64_device");
-}
-
-extern "C" int volta_cuda_gemm_requant_auth(void* ctx, const int16_t* a, const int16_t* b, const uint64_t* masks, int16_t* out, uint64_t* corr, size_t m, size_t k, size_t n, uint32_t shift) {
-    return pending(ctx, "volta_cuda_gemm_requant_auth");
-}
-
-extern "C" int volta_cuda_gemm_requant_auth_device(void* ctx, uint64_t a_id, size_t a_offset, uint64_t b_id, size_t b_offset, uint64_t masks_id, size_t masks_offset, uint64_t out_id, size_t out_offset, uint64_t corr_id, size_t corr_offset, size_t m, size_t k, size_t n, uint32_t shift) {
-    return pending(ctx, "volta_cuda_gemm_requant_auth_device");
-}
-
 extern "C" int volta_cuda_fixed_embed_device(void* ctx, uint64_t tokens_id, size_t tokens_offset, uint64_t wte_id, size_t wte_offset, uint64_t wpe_id, size_t wpe_offset, uint64_t acc_id, size_t acc_offset, uint64_t out_id, size_t out_offset, uint64_t error_id, size_t error_offset, size_t rows, size_t d, size_t vocab, size_t positions, size_t pos0, int32_t shift) {
     return pending(ctx, "volta_cuda_fixed_embed_device");
 }

@@ -116,7 +116,8 @@ enum WorkspaceSlot : int {
     kWsStageH = 11,
     kWsScratch = 12,   // miscellaneous scratch
     kWsScratch2 = 13,
-    kWsCount = 14,
+    kWsGemm = 14,      // byte planes of the GEMM operands
+    kWsCount = 15,
 };
 
 struct Context {
