@@ -121,6 +121,30 @@ void or_gemm_requant_auth(const int16_t* a, const int16_t* b, const uint64_t* ma
 /* ---- FNV-1a style checksums used by the reference p7 recipes ---- */
 uint64_t or_fnv_u64(uint64_t h, const uint64_t* v, size_t n);
 
+/* ---- int16 fixed-point forward primitives (fixed.c; backend.cu:1442-1740) ---- */
+void or_fixed_embed(const uint32_t* tokens, const int16_t* wte, const int16_t* wpe, int64_t* acc_out,
+                    int16_t* out, uint32_t* err, size_t rows, size_t d, size_t vocab, size_t positions,
+                    size_t pos0, int32_t shift);
+void or_fixed_layer_norm(const int16_t* input, const int16_t* gain, const int16_t* bias, const int16_t* lut,
+                         int64_t* means, int64_t* vars, int64_t* rin, int16_t* rout, int64_t* accs, int16_t* outs,
+                         uint32_t* err, size_t rows, size_t d, uint32_t var_shift, uint32_t norm_shift);
+void or_fixed_gemm(const int16_t* input, const int16_t* w, const int16_t* bias, const int16_t* residual,
+                   int64_t* accs, int16_t* req, int16_t* res_out, uint32_t* err, size_t m, size_t k, size_t n,
+                   uint32_t shift);
+void or_fixed_qkv_split(const int16_t* qkv, int16_t* q, int16_t* k, int16_t* v, size_t rows, size_t d);
+void or_fixed_attention_scores(const int16_t* q, const int16_t* k, int64_t* accs, int16_t* outs, uint32_t* err,
+                               size_t rows, size_t seq, size_t pos0, size_t heads, size_t head_dim,
+                               uint32_t shift);
+void or_fixed_softmax(const int16_t* scores, const int16_t* exp_lut, const int16_t* recip_lut, int16_t* row_shifts,
+                      int16_t* exp_out, int64_t* denoms, int16_t* recips, int16_t* weights, uint32_t* err,
+                      size_t rows, size_t pos0, size_t heads, uint32_t recip_den_shift, uint32_t recip_log2,
+                      uint32_t norm_shift, int use_row_shift);
+void or_fixed_av(const int16_t* weights, const int16_t* values, int64_t* accs, int16_t* outs, uint32_t* err,
+                 size_t rows, size_t seq, size_t pos0, size_t d, size_t heads, uint32_t shift);
+void or_fixed_lookup(const int16_t* input, const int16_t* lut, int16_t* out, size_t n);
+void or_fixed_requant_i16(const int16_t* input, int16_t* out, uint32_t* err, size_t n, uint32_t shift);
+void or_fixed_logits(const int16_t* input, const int16_t* w, int64_t* out, size_t rows, size_t d, size_t vocab);
+
 #ifdef __cplusplus
 }
 #endif

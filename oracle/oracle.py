@@ -399,3 +399,127 @@ def ligero_commit_open(row_seed: bytes, rows: int, msg_len: int, code_len: int, 
     bits = code_len.bit_length() - 1
     paths = merkle_paths(tree, code_len, idx).reshape(queries, bits, 32) if bits else np.zeros((queries, 0, 32), np.uint8)
     return tree[-1].tobytes(), idx, cols, paths
+
+
+# ---- int16 fixed-point forward primitives (fixed.c) -----------------------------
+
+def _opt(a):
+    return _p(a) if a is not None else None
+
+
+_FIXED_ARGS = {
+    "or_fixed_embed": [_vp] * 6 + [_sz] * 5 + [C.c_int32],
+    "or_fixed_layer_norm": [_vp] * 11 + [_sz, _sz, C.c_uint32, C.c_uint32],
+    "or_fixed_gemm": [_vp] * 8 + [_sz] * 3 + [C.c_uint32],
+    "or_fixed_qkv_split": [_vp] * 4 + [_sz] * 2,
+    "or_fixed_attention_scores": [_vp] * 5 + [_sz] * 5 + [C.c_uint32],
+    "or_fixed_softmax": [_vp] * 9 + [_sz] * 3 + [C.c_uint32] * 3 + [C.c_int],
+    "or_fixed_av": [_vp] * 5 + [_sz] * 5 + [C.c_uint32],
+    "or_fixed_lookup": [_vp] * 3 + [_sz],
+    "or_fixed_requant_i16": [_vp] * 3 + [_sz, C.c_uint32],
+    "or_fixed_logits": [_vp] * 3 + [_sz] * 3,
+}
+
+
+def _fx():
+    L = lib()
+    if not getattr(L, "_fixed_declared", False):
+        for name, args in _FIXED_ARGS.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = None
+        L._fixed_declared = True
+    return L
+
+
+def fixed_embed(tokens, wte, wpe, rows, d, vocab, positions, pos0, shift):
+    acc = np.zeros(rows * d, np.int64)
+    out = np.zeros(rows * d, np.int16)
+    err = np.zeros(1, np.uint32)
+    _fx().or_fixed_embed(_p(tokens), _p(wte), _p(wpe), _p(acc), _p(out), _p(err), rows, d, vocab, positions, pos0,
+                         C.c_int32(shift))
+    return acc, out, int(err[0])
+
+
+def fixed_layer_norm(x, gain, bias, lut, rows, d, var_shift, norm_shift):
+    means, vars_, rin = (np.zeros(rows, np.int64) for _ in range(3))
+    rout = np.zeros(rows, np.int16)
+    acc = np.zeros(rows * d, np.int64)
+    out = np.zeros(rows * d, np.int16)
+    err = np.zeros(1, np.uint32)
+    _fx().or_fixed_layer_norm(_p(x), _p(gain), _p(bias), _p(lut), _p(means), _p(vars_), _p(rin), _p(rout), _p(acc),
+                              _p(out), _p(err), rows, d, C.c_uint32(var_shift), C.c_uint32(norm_shift))
+    return means, vars_, rin, rout, acc, out, int(err[0])
+
+
+def fixed_gemm(x, w, bias, residual, m, k, n, shift):
+    acc = np.zeros(m * n, np.int64)
+    req = np.zeros(m * n, np.int16)
+    res_out = np.zeros(m * n, np.int16) if residual is not None else None
+    err = np.zeros(1, np.uint32)
+    _fx().or_fixed_gemm(_p(x), _p(w), _opt(bias), _opt(residual), _p(acc), _p(req), _opt(res_out), _p(err), m, k, n,
+                        C.c_uint32(shift))
+    return acc, req, res_out, int(err[0])
+
+
+def fixed_qkv_split(qkv, rows, d):
+    q, k, v = (np.zeros(rows * d, np.int16) for _ in range(3))
+    _fx().or_fixed_qkv_split(_p(qkv), _p(q), _p(k), _p(v), rows, d)
+    return q, k, v
+
+
+def packed_len(rows, pos0, heads):
+    return heads * (rows * pos0 + rows * (rows + 1) // 2)
+
+
+def fixed_attention_scores(q, k, rows, seq, pos0, heads, head_dim, shift):
+    n = packed_len(rows, pos0, heads)
+    acc = np.zeros(n, np.int64)
+    out = np.zeros(n, np.int16)
+    err = np.zeros(1, np.uint32)
+    _fx().or_fixed_attention_scores(_p(q), _p(k), _p(acc), _p(out), _p(err), rows, seq, pos0, heads, head_dim,
+                                    C.c_uint32(shift))
+    return acc, out, int(err[0])
+
+
+def fixed_softmax(scores, exp_lut, recip_lut, rows, pos0, heads, recip_den_shift, recip_log2, norm_shift,
+                  use_row_shift):
+    n = packed_len(rows, pos0, heads)
+    row_shifts = np.zeros(heads * rows, np.int16)
+    exp_out = np.zeros(n, np.int16)
+    denoms = np.zeros(heads * rows, np.int64)
+    recips = np.zeros(heads * rows, np.int16)
+    weights = np.zeros(n, np.int16)
+    err = np.zeros(1, np.uint32)
+    _fx().or_fixed_softmax(_p(scores), _p(exp_lut), _p(recip_lut), _p(row_shifts), _p(exp_out), _p(denoms),
+                           _p(recips), _p(weights), _p(err), rows, pos0, heads, C.c_uint32(recip_den_shift),
+                           C.c_uint32(recip_log2), C.c_uint32(norm_shift), C.c_int(use_row_shift))
+    return row_shifts, exp_out, denoms, recips, weights, int(err[0])
+
+
+def fixed_av(weights, values, rows, seq, pos0, d, heads, shift):
+    acc = np.zeros(rows * d, np.int64)
+    out = np.zeros(rows * d, np.int16)
+    err = np.zeros(1, np.uint32)
+    _fx().or_fixed_av(_p(weights), _p(values), _p(acc), _p(out), _p(err), rows, seq, pos0, d, heads,
+                      C.c_uint32(shift))
+    return acc, out, int(err[0])
+
+
+def fixed_lookup(x, lut):
+    out = np.zeros(x.size, np.int16)
+    _fx().or_fixed_lookup(_p(x), _p(lut), _p(out), x.size)
+    return out
+
+
+def fixed_requant_i16(x, shift):
+    out = np.zeros(x.size, np.int16)
+    err = np.zeros(1, np.uint32)
+    _fx().or_fixed_requant_i16(_p(x), _p(out), _p(err), x.size, C.c_uint32(shift))
+    return out, int(err[0])
+
+
+def fixed_logits(x, w, rows, d, vocab):
+    out = np.zeros(rows * vocab, np.int64)
+    _fx().or_fixed_logits(_p(x), _p(w), _p(out), rows, d, vocab)
+    return out

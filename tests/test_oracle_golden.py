@@ -287,3 +287,24 @@ def test_oracle_matches_reference_chacha_header(oracle):
         out = np.zeros(rows * count, dtype=np.uint64)
         ref.ref_chacha_fp_rows(seed, base, rows, count, out.ctypes.data_as(C.c_void_p))
         assert np.array_equal(out.reshape(rows, count), oracle.chacha_fp_rows(seed, base, rows, count))
+
+
+# --------------------------------------------------------------------------
+# int16 fixed-point layer (scripts/gpt2_fixed.py forward_layer fixture)
+# --------------------------------------------------------------------------
+
+def test_fixed_layer_oracle_matches_reference_mirror(oracle):
+    """The oracle's forward primitives, composed as forward_layer, reproduce
+    every intermediate of the reference's NumPy mirror (digests in
+    tests/golden/fixed_layer_t8.npz, made by tests/golden/make_fixed_golden.py)."""
+    import fixed_layer as fl
+
+    g = np.load(fl.GOLDEN)
+    seed, t = (int(v) for v in g["seed_t"])
+    w, x = fl.synthetic_layer(seed, t)
+    assert fl.weights_digest(w) == str(g["weights_digest"])
+    assert fl.digest(x) == str(g["input_digest"])
+    luts = {k: g[k] for k in ("exp", "gelu", "ln_rsqrt", "softmax_recip")}
+    res = fl.forward_layer(fl.OracleOps(oracle), x, w, luts, t)
+    assert res["errors"] == [0] * len(res["errors"])
+    assert fl.check_against_golden(res) == []

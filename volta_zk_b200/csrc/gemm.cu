@@ -8,23 +8,28 @@
 namespace vzb {
 
 __global__ void split_planes_kernel(const int16_t* x, size_t rows, size_t k, size_t ld, int8_t* hi, uint8_t* lo,
-                                    size_t kp) {
-    const size_t total = rows * kp;
+                                    size_t kp, unsigned batches, size_t boff) {
+    const size_t per = rows * kp, total = per * batches;
     for (size_t z = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; z < total;
          z += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const size_t r = z / kp, c = z - r * kp;
-        const int v = c < k ? x[r * ld + c] : 0;
+        const size_t b = z / per, rem = z - b * per;
+        const size_t r = rem / kp, c = rem - r * kp;
+        const int v = c < k ? x[b * boff + r * ld + c] : 0;
         hi[z] = static_cast<int8_t>(v >> 8);
         lo[z] = static_cast<uint8_t>(v & 0xFF);
     }
 }
 
 // 32 x 32 tiles through shared memory: coalesced reads of x rows and
-// coalesced writes of plane rows.
+// coalesced writes of plane rows; blockIdx.z is the batch.
 __global__ void split_planes_t_kernel(const int16_t* x, size_t k, size_t n, size_t ld, int8_t* hi, uint8_t* lo,
-                                      size_t kp) {
+                                      size_t kp, size_t boff) {
     __shared__ int16_t t[32][33];
     const size_t k0 = static_cast<size_t>(blockIdx.x) * 32, n0 = static_cast<size_t>(blockIdx.y) * 32;
+    const size_t b = blockIdx.z;
+    x += b * boff;
+    hi += b * n * kp;
+    lo += b * n * kp;
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
         const size_t kk = k0 + r, nn = n0 + threadIdx.x;
         t[r][threadIdx.x] = (kk < k && nn < n) ? x[kk * ld + nn] : 0;
@@ -40,31 +45,41 @@ __global__ void split_planes_t_kernel(const int16_t* x, size_t k, size_t n, size
     }
 }
 
-int gemm_prepare(Context* c, const int16_t* a, size_t m, size_t k, size_t lda, const int16_t* b, size_t n,
-                 size_t ldb, bool b_nk, GemmPlanes* out) {
-    const size_t kp = (k + kGemmBK - 1) / kGemmBK * kGemmBK;
-    const size_t abytes = m * kp, bbytes = n * kp;
-    if (ensure_ws(c, kWsGemm, 2 * abytes + 2 * bbytes + 64)) return -1;
+int gemm_prepare_b(Context* c, const int16_t* b, size_t k, size_t n, size_t ldb, bool b_nk, size_t kp,
+                   unsigned batches, size_t b_boff, size_t a_bytes, GemmPlanes* out) {
+    const size_t bbytes = n * kp * batches;
+    if (ensure_ws(c, kWsGemm, 2 * a_bytes + 2 * bbytes + 64)) return -1;
     unsigned char* w = ws<unsigned char>(c, kWsGemm);
     out->a_hi = reinterpret_cast<int8_t*>(w);
-    out->a_lo = w + abytes;
-    out->b_hi = reinterpret_cast<int8_t*>(w + 2 * abytes);
-    out->b_lo = w + 2 * abytes + bbytes;
-    out->m = m;
+    out->a_lo = w + a_bytes;
+    out->b_hi = reinterpret_cast<int8_t*>(w + 2 * a_bytes);
+    out->b_lo = w + 2 * a_bytes + bbytes;
     out->n = n;
     out->kp = kp;
-    split_planes_kernel<<<grid_for(c, m * kp, 256), 256, 0, c->stream>>>(
-        a, m, k, lda, const_cast<int8_t*>(out->a_hi), const_cast<uint8_t*>(out->a_lo), kp);
-    VZB_LAUNCHED(c);
+    out->batches = batches;
+    out->b_batch = n * kp;
     if (b_nk) {
-        split_planes_kernel<<<grid_for(c, n * kp, 256), 256, 0, c->stream>>>(
-            b, n, k, ldb, const_cast<int8_t*>(out->b_hi), const_cast<uint8_t*>(out->b_lo), kp);
+        split_planes_kernel<<<grid_for(c, bbytes, 256), 256, 0, c->stream>>>(
+            b, n, k, ldb, const_cast<int8_t*>(out->b_hi), const_cast<uint8_t*>(out->b_lo), kp, batches, b_boff);
     } else {
-        const dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((n + 31) / 32));
-        if (grid.y > 65535) return fail_message(c, "GEMM column count exceeds the launch grid");
+        const dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((n + 31) / 32), batches);
+        if (grid.y > 65535 || grid.z > 65535) return fail_message(c, "GEMM column count exceeds the launch grid");
         split_planes_t_kernel<<<grid, dim3(32, 8), 0, c->stream>>>(b, k, n, ldb, const_cast<int8_t*>(out->b_hi),
-                                                                   const_cast<uint8_t*>(out->b_lo), kp);
+                                                                   const_cast<uint8_t*>(out->b_lo), kp, b_boff);
     }
+    VZB_LAUNCHED(c);
+    return 0;
+}
+
+int gemm_prepare(Context* c, const int16_t* a, size_t m, size_t k, size_t lda, const int16_t* b, size_t n,
+                 size_t ldb, bool b_nk, GemmPlanes* out, unsigned batches, size_t a_boff, size_t b_boff) {
+    const size_t kp = (k + kGemmBK - 1) / kGemmBK * kGemmBK;
+    const size_t abytes = m * kp * batches;
+    if (gemm_prepare_b(c, b, k, n, ldb, b_nk, kp, batches, b_boff, abytes, out)) return -1;
+    out->m = m;
+    out->a_batch = m * kp;
+    split_planes_kernel<<<grid_for(c, abytes, 256), 256, 0, c->stream>>>(
+        a, m, k, lda, const_cast<int8_t*>(out->a_hi), const_cast<uint8_t*>(out->a_lo), kp, batches, a_boff);
     VZB_LAUNCHED(c);
     return 0;
 }
@@ -74,7 +89,8 @@ namespace {
 struct I64Epi {
     int64_t* out;
     size_t ldo;
-    __device__ __forceinline__ void operator()(size_t i, size_t j, int64_t v) const { out[i * ldo + j] = v; }
+    __device__ __forceinline__ bool active(size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t v) const { out[i * ldo + j] = v; }
 };
 
 __device__ __forceinline__ int16_t requant_clamped(int64_t acc, uint32_t shift) {
@@ -88,7 +104,8 @@ struct RequantAuthEpi {
     uint64_t* corr;
     size_t n;
     uint32_t shift;
-    __device__ __forceinline__ void operator()(size_t i, size_t j, int64_t v) const {
+    __device__ __forceinline__ bool active(size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t v) const {
         const size_t z = i * n + j;
         const int16_t y = requant_clamped(v, shift);
         out[z] = y;

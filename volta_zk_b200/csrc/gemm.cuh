@@ -25,12 +25,16 @@ constexpr int kGemmRow = kGemmBK + 16;  // shared-memory row pitch in bytes
 constexpr int kGemmThreads = 128;
 constexpr size_t kGemmChunkK = 16384;   // int32 partials stay exact below this
 
+// Byte planes of `batches` independent products (batch z at z * a_batch /
+// z * b_batch bytes into each plane).
 struct GemmPlanes {
     const int8_t* a_hi;
     const uint8_t* a_lo;
     const int8_t* b_hi;
     const uint8_t* b_lo;
     size_t m, n, kp;
+    size_t a_batch = 0, b_batch = 0;
+    unsigned batches = 1;
 };
 
 #ifdef __CUDACC__
@@ -54,13 +58,20 @@ __device__ __forceinline__ void ldsm_x4(const void* smem, uint32_t& r0, uint32_t
                  : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])                                    \
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]))
 
-// epi(i, j, acc) is called once per output element inside [0,m) x [0,n).
+// epi(z, i, j, acc) is called once per output element of batch z inside
+// [0,m) x [0,n); tiles for which epi.active(z, m0, n0) is false are skipped.
 template <class Epi, bool kLongK>
 __global__ void __launch_bounds__(kGemmThreads) gemm_planes_kernel(GemmPlanes g, Epi epi) {
     __shared__ __align__(16) unsigned char sm[2][4][kGemmBM][kGemmRow];  // stage, plane, row, k bytes
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int wm = warp >> 1, wn = warp & 1;
     const size_t m0 = static_cast<size_t>(blockIdx.y) * kGemmBM, n0 = static_cast<size_t>(blockIdx.x) * kGemmBN;
+    const size_t bz = blockIdx.z;
+    if (!epi.active(bz, m0, n0)) return;
+    g.a_hi += bz * g.a_batch;
+    g.a_lo += bz * g.a_batch;
+    g.b_hi += bz * g.b_batch;
+    g.b_lo += bz * g.b_batch;
     const size_t ktiles = g.kp / kGemmBK;
 
     auto load = [&](int stage, size_t kt) {
@@ -174,34 +185,40 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_planes_kernel(GemmPlanes g,
                                              : 65536 * static_cast<int64_t>(acc[0][mt][nt][e]) +
                                                    256 * static_cast<int64_t>(acc[1][mt][nt][e]) +
                                                    static_cast<int64_t>(acc[2][mt][nt][e]);
-                    epi(i, j, v);
+                    epi(bz, i, j, v);
                 }
             }
 }
 #undef VZB_MMA_I8
 
-// Byte planes of a row-major matrix [rows][k] (row stride ld) into
-// hi/lo [rows][kp], zero beyond k.
+// Byte planes of `batches` row-major matrices [rows][k] (row stride ld,
+// batch b starting at x + b * boff) into hi/lo [batches][rows][kp], zero
+// beyond k.
 __global__ void split_planes_kernel(const int16_t* x, size_t rows, size_t k, size_t ld, int8_t* hi, uint8_t* lo,
-                                    size_t kp);
-// Byte planes of the transpose: x is [k][n] row-major (stride ld); planes are
-// [n][kp].
+                                    size_t kp, unsigned batches, size_t boff);
+// Byte planes of the transposes: batch b of x is [k][n] row-major (stride ld,
+// starting at x + b * boff); planes are [batches][n][kp].
 __global__ void split_planes_t_kernel(const int16_t* x, size_t k, size_t n, size_t ld, int8_t* hi, uint8_t* lo,
-                                      size_t kp);
+                                      size_t kp, size_t boff);
 
 #endif  // __CUDACC__
 
 // Split A (m x k, row-major) and B (k x n row-major, or n x k when b_nk) into
-// byte planes in the context's GEMM workspace.
+// byte planes in the context's GEMM workspace; `batches` products whose
+// operands start a_boff / b_boff elements apart.
 int gemm_prepare(Context* c, const int16_t* a, size_t m, size_t k, size_t lda, const int16_t* b, size_t n,
-                 size_t ldb, bool b_nk, GemmPlanes* out);
+                 size_t ldb, bool b_nk, GemmPlanes* out, unsigned batches = 1, size_t a_boff = 0,
+                 size_t b_boff = 0);
+// Planes for A supplied by the caller's own split (fills b only).
+int gemm_prepare_b(Context* c, const int16_t* b, size_t k, size_t n, size_t ldb, bool b_nk, size_t kp,
+                   unsigned batches, size_t b_boff, size_t a_bytes, GemmPlanes* out);
 
 #ifdef __CUDACC__
 template <class Epi>
 int gemm_launch(Context* c, const GemmPlanes& g, const Epi& epi) {
     const dim3 grid(static_cast<unsigned>((g.n + kGemmBN - 1) / kGemmBN),
-                    static_cast<unsigned>((g.m + kGemmBM - 1) / kGemmBM));
-    if (grid.y > 65535) return fail_message(c, "GEMM row count exceeds the launch grid");
+                    static_cast<unsigned>((g.m + kGemmBM - 1) / kGemmBM), g.batches);
+    if (grid.y > 65535 || grid.z > 65535) return fail_message(c, "GEMM shape exceeds the launch grid");
     if (g.kp > kGemmChunkK)
         gemm_planes_kernel<Epi, true><<<grid, kGemmThreads, 0, c->stream>>>(g, epi);
     else
