@@ -257,3 +257,151 @@ void or_fixed_logits(const int16_t* input, const int16_t* w, int64_t* out, size_
             out[row * vocab + word] = acc;
         }
 }
+
+/* ---- attention proof wires (backend.cu:2202-2470, 5278-5375) ---- */
+
+/* backend.cu fp_from_i64_device: the canonical residue of a signed value */
+static uint64_t fp_of_i64(int64_t v) {
+    const uint64_t p = 0xFFFFFFFF00000001ull;
+    if (v >= 0) return (uint64_t)v % p;
+    const uint64_t mag = (uint64_t)(-(v + 1)) + 1, r = mag % p;
+    return r == 0 ? 0 : p - r;
+}
+
+/* rect: 9 columns of head_pad x query_pad x seq_pad entries; above: the
+ * strictly-above-causal full scores; rows: 13 columns of head_pad x
+ * query_pad; qkv: 2 columns of query_pad x 4 d_pad. */
+void or_attention_wires(const or_wires_geom* g, const int16_t* q, const int16_t* k_cache, const int16_t* own_k,
+                        const int16_t* v, const int64_t* scores_acc, const int16_t* scores_q,
+                        const int16_t* row_shifts, const int16_t* exp_outputs, const int64_t* denoms,
+                        const int16_t* recips, const int16_t* weights, const int16_t* recip_lut,
+                        const int64_t* qkv_acc, uint64_t* rect, uint64_t* rows_out, uint64_t* above,
+                        uint64_t* qkv_cols, uint32_t* err) {
+    const size_t qr = g->query_rows, d = g->heads * g->head_dim;
+    const size_t per_head = qr * g->pos0 + qr * (qr + 1) / 2;
+    const int rs = g->use_row_shift;
+    /* rectangle columns */
+    const size_t sp2 = g->query_pad * g->seq_pad, rect_n = g->head_pad * sp2;
+    for (size_t z = 0; z < rect_n; ++z) {
+        const size_t head = z / sp2, rem = z % sp2, row = rem / g->seq_pad, col = rem % g->seq_pad;
+        const int64_t half_s = (int64_t)1 << (g->shift_scores - 1), half_n = (int64_t)1 << (g->shift_softmax_norm - 1);
+        int64_t norm_rem = half_n, weight = 0, score_rem = half_s;
+        int64_t score_value = rs ? -(int64_t)g->exp_pad_input : (int64_t)g->exp_pad_input;
+        int64_t score_index = score_value + ((int64_t)1 << 16);
+        int64_t exp_input = g->exp_pad_input, exp_value = 0, is_max = 0, full = 0;
+        if (head < g->heads && row < qr && col < g->seq) {
+            for (size_t l = 0; l < g->head_dim; ++l)
+                full += (int64_t)q[row * d + head * g->head_dim + l] * (int64_t)k_cache[col * d + head * g->head_dim + l];
+            const size_t width = g->pos0 + row + 1;
+            if (col < width) {
+                const size_t start = head * per_head + packed_prefix(row, g->pos0), pk = start + col;
+                const int64_t score = scores_q[pk];
+                const int64_t raw = requant_rounded(scores_acc[pk], g->shift_scores);
+                const int64_t clamped = raw < INT16_MIN ? INT16_MIN : (raw > INT16_MAX ? INT16_MAX : raw);
+                if (raw < -((int64_t)1 << 16) || raw >= ((int64_t)1 << 16) || score != clamped) *err = 1;
+                const int64_t shift_v = rs ? row_shifts[head * qr + row] : 0;
+                score_value = score;
+                score_index = raw + ((int64_t)1 << 16);
+                exp_input = rs ? shift_v - score : score;
+                if ((rs && (exp_input < 0 || exp_input > UINT16_MAX)) ||
+                    (!rs && (exp_input < INT16_MIN || exp_input > INT16_MAX)))
+                    *err = 1;
+                score_rem = scores_acc[pk] + half_s - raw * ((int64_t)1 << g->shift_scores);
+                if (score_rem < 0 || score_rem >= ((int64_t)1 << g->shift_scores)) *err = 1;
+                if (scores_acc[pk] != full) *err = 1;
+                exp_value = exp_outputs[pk];
+                weight = weights[pk];
+                const int64_t rc = recips[head * qr + row];
+                norm_rem = exp_value * rc + half_n - weight * ((int64_t)1 << g->shift_softmax_norm);
+                if (norm_rem < 0 || norm_rem >= ((int64_t)1 << g->shift_softmax_norm)) *err = 1;
+                if (rs && exp_input == 0) {
+                    int first = 1;
+                    for (size_t prior = 0; prior < col; ++prior)
+                        if ((int64_t)scores_q[start + prior] - shift_v == 0) {
+                            first = 0;
+                            break;
+                        }
+                    is_max = first;
+                }
+            } else {
+                const size_t local = col - width;
+                const size_t row_prefix = row * (qr - 1) - row * (row - 1) / 2;
+                above[head * (qr * (qr - 1) / 2) + row_prefix + local] = fp_of_i64(full);
+            }
+        }
+        rect[z] = (uint64_t)norm_rem;
+        rect[rect_n + z] = fp_of_i64(weight);
+        rect[2 * rect_n + z] = (uint64_t)score_rem;
+        rect[3 * rect_n + z] = rs ? (uint64_t)score_index : fp_of_i64(score_value);
+        rect[4 * rect_n + z] = fp_of_i64(score_value);
+        rect[5 * rect_n + z] = rs ? (uint64_t)exp_input : fp_of_i64(exp_input);
+        rect[6 * rect_n + z] = fp_of_i64(exp_value);
+        rect[7 * rect_n + z] = (uint64_t)is_max;
+        rect[8 * rect_n + z] = fp_of_i64(full);
+    }
+    /* row columns */
+    const size_t row_n = g->head_pad * g->query_pad;
+    for (size_t z = 0; z < row_n; ++z) {
+        const size_t head = z / g->query_pad, row = z % g->query_pad;
+        int64_t denom = 0, rin = 0, rc = g->recip_pad_output, shift_v = 0;
+        int real = 0;
+        if (head < g->heads && row < qr) {
+            real = 1;
+            denom = denoms[head * qr + row];
+            rin = denom >> g->recip_den_shift;
+            rc = recips[head * qr + row];
+            shift_v = rs ? row_shifts[head * qr + row] : 0;
+            if (recip_value(rin, recip_lut, g->recip_den_shift, g->recip_log2, rs, err) != rc) *err = 1;
+            if (rs) {
+                const size_t start = head * per_head + packed_prefix(row, g->pos0), width = g->pos0 + row + 1;
+                int found = 0;
+                for (size_t c = 0; c < width; ++c)
+                    if (scores_q[start + c] == shift_v) {
+                        found = 1;
+                        break;
+                    }
+                if (!found || width > g->seq) *err = 1;
+            }
+        }
+        rows_out[z] = fp_of_i64(denom);
+        rows_out[row_n + z] = (uint64_t)rin;
+        rows_out[2 * row_n + z] = fp_of_i64(rc);
+        rows_out[3 * row_n + z] = fp_of_i64(shift_v);
+        const uint32_t ds = g->recip_den_shift;
+        const int64_t r_in = real ? rin : 256;
+        const int64_t r_den = real ? denom : ((int64_t)256 << ds);
+        const int64_t r_q = real ? rc : recip_value(256, recip_lut, ds, g->recip_log2, 1, err);
+        const int64_t denom_low = r_den - (r_in << ds);
+        const int64_t divisor = (r_in << ds) + ((int64_t)1 << (ds - 1));
+        const int64_t numer = ((int64_t)1 << g->recip_log2) + divisor / 2;
+        const int64_t remainder = numer - r_q * divisor;
+        const int64_t slack = divisor - 1 - remainder;
+        if (denom_low < 0 || denom_low >= ((int64_t)1 << ds) || r_in < 0 || r_in >= ((int64_t)1 << 18) || r_q < 0 ||
+            r_q >= ((int64_t)1 << 15) || remainder < 0 || remainder >= divisor || remainder >= ((int64_t)1 << 24) ||
+            slack < 0 || slack >= ((int64_t)1 << 24))
+            *err = 1;
+        rows_out[4 * row_n + z] = (uint64_t)denom_low;
+        rows_out[5 * row_n + z] = (uint64_t)(r_in & 0xffff);
+        rows_out[6 * row_n + z] = (uint64_t)(r_in >> 16);
+        rows_out[7 * row_n + z] = (uint64_t)r_q;
+        rows_out[8 * row_n + z] = (uint64_t)(remainder & 0xffff);
+        rows_out[9 * row_n + z] = (uint64_t)(remainder >> 16);
+        rows_out[10 * row_n + z] = (uint64_t)(slack & 0xffff);
+        rows_out[11 * row_n + z] = (uint64_t)(slack >> 16);
+        rows_out[12 * row_n + z] = (uint64_t)divisor;
+    }
+    /* QKV requant columns */
+    const size_t width = 4 * g->d_pad, qkv_n = g->query_pad * width;
+    for (size_t z = 0; z < qkv_n; ++z) {
+        const size_t row = z / width, col = z % width, third = col / g->d_pad, rest = col % g->d_pad;
+        const int64_t half = (int64_t)1 << (g->shift_qkv - 1);
+        int64_t rem = half, out = 0;
+        if (row < qr && third < 3 && rest < d) {
+            out = third == 0 ? q[row * d + rest] : (third == 1 ? own_k[row * d + rest] : v[row * d + rest]);
+            rem = qkv_acc[row * 3 * d + third * d + rest] + half - out * ((int64_t)1 << g->shift_qkv);
+            if (rem < 0 || rem >= ((int64_t)1 << g->shift_qkv)) *err = 1;
+        }
+        qkv_cols[z] = (uint64_t)rem;
+        qkv_cols[qkv_n + z] = fp_of_i64(out);
+    }
+}

@@ -144,6 +144,18 @@ void or_fixed_av(const int16_t* weights, const int16_t* values, int64_t* accs, i
 void or_fixed_lookup(const int16_t* input, const int16_t* lut, int16_t* out, size_t n);
 void or_fixed_requant_i16(const int16_t* input, int16_t* out, uint32_t* err, size_t n, uint32_t shift);
 void or_fixed_logits(const int16_t* input, const int16_t* w, int64_t* out, size_t rows, size_t d, size_t vocab);
+/* attention proof wires (backend.cu:2202-2470) */
+typedef struct {
+    size_t query_rows, seq, pos0, heads, head_pad, head_dim, query_pad, seq_pad, d_pad;
+    uint32_t shift_scores, shift_softmax_norm, shift_qkv, recip_den_shift, recip_log2;
+    int32_t exp_pad_input, recip_pad_output, use_row_shift;
+} or_wires_geom;
+void or_attention_wires(const or_wires_geom* g, const int16_t* q, const int16_t* k_cache, const int16_t* own_k,
+                        const int16_t* v, const int64_t* scores_acc, const int16_t* scores_q,
+                        const int16_t* row_shifts, const int16_t* exp_outputs, const int64_t* denoms,
+                        const int16_t* recips, const int16_t* weights, const int16_t* recip_lut,
+                        const int64_t* qkv_acc, uint64_t* rect, uint64_t* rows_out, uint64_t* above,
+                        uint64_t* qkv_cols, uint32_t* err);
 
 #ifdef __cplusplus
 }

@@ -523,3 +523,32 @@ def fixed_logits(x, w, rows, d, vocab):
     out = np.zeros(rows * vocab, np.int64)
     _fx().or_fixed_logits(_p(x), _p(w), _p(out), rows, d, vocab)
     return out
+
+
+class WiresGeom(C.Structure):
+    _fields_ = [(n, C.c_size_t) for n in ("query_rows", "seq", "pos0", "heads", "head_pad", "head_dim", "query_pad",
+                                          "seq_pad", "d_pad")] + \
+               [(n, C.c_uint32) for n in ("shift_scores", "shift_softmax_norm", "shift_qkv", "recip_den_shift",
+                                          "recip_log2")] + \
+               [(n, C.c_int32) for n in ("exp_pad_input", "recip_pad_output", "use_row_shift")]
+
+
+def attention_wires(geom: dict, q, k_cache, own_k, v, scores_acc, scores_q, row_shifts, exp_outputs, denoms, recips,
+                    weights, recip_lut, qkv_acc):
+    """Attention proof-wire columns (backend.cu:2202-2470): returns
+    (rect [9 x entries], rows [13 x head_pad query_pad], above, qkv
+    [2 x query_pad 4 d_pad], error)."""
+    g = WiresGeom(**geom)
+    qr = g.query_rows
+    rect = np.zeros(9 * g.head_pad * g.query_pad * g.seq_pad, np.uint64)
+    rows = np.zeros(13 * g.head_pad * g.query_pad, np.uint64)
+    above = np.zeros(max(1, g.heads * qr * (qr - 1) // 2), np.uint64)
+    qkv = np.zeros(2 * g.query_pad * 4 * g.d_pad, np.uint64)
+    err = np.zeros(1, np.uint32)
+    L = lib()
+    L.or_attention_wires.argtypes = [C.POINTER(WiresGeom)] + [_vp] * 18
+    L.or_attention_wires.restype = None
+    L.or_attention_wires(C.byref(g), *[_p(a) for a in (q, k_cache, own_k, v, scores_acc, scores_q, row_shifts,
+                                                       exp_outputs, denoms, recips, weights, recip_lut, qkv_acc,
+                                                       rect, rows, above, qkv, err)])
+    return rect, rows, above, qkv, int(err[0])
