@@ -18,6 +18,7 @@ Prints one JSON line on rank 0.
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -241,6 +242,7 @@ def run_b200(args, rank, world, local_rank):
     import torch
 
     from volta_zk_b200 import accel, build_all
+    from volta_zk_b200.sharded import ShardedProver, torch_all_gather
 
     if not os.path.exists(os.path.join(ROOT, "volta_zk_b200", "libvolta_cuda_backend.so")):
         if rank == 0:
@@ -257,6 +259,8 @@ def run_b200(args, rank, world, local_rank):
     be = prover.backend
     n = 1 << args.log2_sumcheck
     n_f, n_t = 1 << args.log2_queries, 1 << args.log2_table
+    if world & (world - 1) or n % world or n_f % world or n_t % (2 * world):
+        raise SystemExit("the GPU count must be a power of two that divides the tables")
 
     # ---- inputs resident in HBM (generated on the device through the ABI) ----
     tables = []
@@ -268,12 +272,32 @@ def run_b200(args, rank, world, local_rank):
         tables.append(tid)
     be.free(col)
     f, table, mult = logup_inputs(args.log2_queries, args.log2_table, accel.fpstream_u64)
-    f_col, t_col, m_col = be.upload_new(embed_i16(f)), be.upload_new(embed_i16(table)), be.upload_new(mult)
     cap = proof_words(n_f, n_t)
+    if world == 1:
+        shard_tables = tables
+        f_col, t_col, m_col = be.upload_new(embed_i16(f)), be.upload_new(embed_i16(table)), be.upload_new(mult)
+    else:
+        # this rank's slices: entries [rank n / world, (rank + 1) n / world) of every table and column
+        nl = n // world
+        shard_tables = []
+        for tid in tables:
+            sl = be.alloc(16 * nl)
+            be.call("resident_copy_rows", tid, 16 * nl * rank, 16 * nl, sl, 0, 16 * nl, 1, 16 * nl)
+            shard_tables.append(sl)
+        fs, ts = slice(rank * n_f // world, (rank + 1) * n_f // world), slice(rank * n_t // world,
+                                                                              (rank + 1) * n_t // world)
+        f_col = be.upload_new(np.ascontiguousarray(embed_i16(f)[fs]))
+        t_col = be.upload_new(np.ascontiguousarray(embed_i16(table)[ts]))
+        m_col = be.upload_new(np.ascontiguousarray(mult[ts]))
+        sharded = ShardedProver(prover, rank, world, torch_all_gather(torch.device("cuda", local_rank)))
 
     def step():
-        msgs, finals = prover.triple_sumcheck(tables[0], tables[1], tables[2], n, TRANSCRIPT_SEED)
-        proof = prover.logup_prove(f_col, n_f, t_col, n_t, m_col, LOGUP_SEED, LOGUP_DOMAIN, cap)
+        if world == 1:
+            msgs, finals = prover.triple_sumcheck(tables[0], tables[1], tables[2], n, TRANSCRIPT_SEED)
+            proof = prover.logup_prove(f_col, n_f, t_col, n_t, m_col, LOGUP_SEED, LOGUP_DOMAIN, cap)
+        else:
+            msgs, finals = sharded.triple_sumcheck(*shard_tables, n, TRANSCRIPT_SEED)
+            proof = sharded.logup_prove(f_col, n_f, t_col, n_t, m_col, LOGUP_SEED, LOGUP_DOMAIN)
         return msgs, finals, proof
 
     def barrier():
@@ -307,26 +331,32 @@ def run_b200(args, rank, world, local_rank):
     e2e = None
     if not args.no_e2e:
         # the user's tables are Fp columns (8 B per entry); they are lifted to
-        # Fp2 on the device (base_broadcast_fp2_device) after the upload
-        host_cols = [np.ascontiguousarray(be.download_fp2(t, n)[:, 0]) for t in tables]
+        # Fp2 on the device (base_broadcast_fp2_device) after the upload.  With
+        # N GPUs every rank uploads only its slices.
+        nl, nfl, ntl = n // world, n_f // world, n_t // world
+        host_cols = [np.ascontiguousarray(be.download_fp2(t, n)[rank * nl:(rank + 1) * nl, 0]) for t in tables]
         pinned = [torch.from_numpy(x.view(np.int64)).pin_memory() for x in host_cols]
-        fcol_h = torch.from_numpy(embed_i16(f).view(np.int64)).pin_memory()
-        tcol_h = torch.from_numpy(embed_i16(table).view(np.int64)).pin_memory()
-        mult_h = torch.from_numpy(mult.astype(np.int32)).pin_memory()
-        ups = [be.alloc(8 * n) for _ in range(3)] + [be.alloc(8 * n_f), be.alloc(8 * n_t), be.alloc(4 * n_t)]
-        lifted = [be.alloc(16 * n) for _ in range(3)]
+        fcol_h = torch.from_numpy(np.ascontiguousarray(embed_i16(f)[rank * nfl:(rank + 1) * nfl]).view(np.int64)).pin_memory()
+        tcol_h = torch.from_numpy(np.ascontiguousarray(embed_i16(table)[rank * ntl:(rank + 1) * ntl]).view(np.int64)).pin_memory()
+        mult_h = torch.from_numpy(np.ascontiguousarray(mult[rank * ntl:(rank + 1) * ntl]).astype(np.int32)).pin_memory()
+        ups = [be.alloc(8 * nl) for _ in range(3)] + [be.alloc(8 * nfl), be.alloc(8 * ntl), be.alloc(4 * ntl)]
+        lifted = [be.alloc(16 * nl) for _ in range(3)]
         bufs = ups + lifted
-        h2d = 3 * 8 * n + 8 * n_f + 8 * n_t + 4 * n_t
-        d2h = 16 * (3 * args.log2_sumcheck + 3) + 16 * cap
+        h2d = 3 * 8 * n + 8 * n_f + 8 * n_t + 4 * n_t  # whole job
+        d2h = (16 * (3 * args.log2_sumcheck + 3) + 16 * cap) * world
 
         def e2e_step():
             for buf, t in zip(ups, pinned + [fcol_h, tcol_h, mult_h]):
                 be.check(be.lib.volta_cuda_resident_upload(be.ctx, buf, 0, t.data_ptr(),
                                                            t.numel() * t.element_size()), "upload")
             for col, tid in zip(ups[:3], lifted):
-                be.call("base_broadcast_fp2_device", col, 0, tid, 0, n, 1, 2)
-            prover.triple_sumcheck(lifted[0], lifted[1], lifted[2], n, TRANSCRIPT_SEED)
-            prover.logup_prove(ups[3], n_f, ups[4], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN, cap)
+                be.call("base_broadcast_fp2_device", col, 0, tid, 0, nl, 1, 2)
+            if world == 1:
+                prover.triple_sumcheck(lifted[0], lifted[1], lifted[2], n, TRANSCRIPT_SEED)
+                prover.logup_prove(ups[3], n_f, ups[4], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN, cap)
+            else:
+                sharded.triple_sumcheck(lifted[0], lifted[1], lifted[2], n, TRANSCRIPT_SEED)
+                sharded.logup_prove(ups[3], n_f, ups[4], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN)
 
         e2e_step()
         barrier()
@@ -336,7 +366,7 @@ def run_b200(args, rank, world, local_rank):
         be.mark(3)
         e2e_s = max_over_ranks(be.elapsed_ms(2, 3) / 1e3 / args.steps)
         barrier()
-        e2e = {"value": e2e_s / world, "unit": "s/proof", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        e2e = {"value": e2e_s, "unit": "s/proof", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
         for b in bufs:
             be.free(b)
 
@@ -366,10 +396,12 @@ def run_b200(args, rank, world, local_rank):
                 "frac": round(achieved / peak, 4), "traffic": None, "algorithmic_bytes": alg_bytes,
                 "avg_launch_ms": round(kern_ms, 4)}
 
-    ligero = None if args.no_ligero else ligero_leg(args, prover, be, peaks)
+    # the Ligero commitment is measured on one GPU (its row split across GPUs
+    # is not part of this bench)
+    ligero = None if (args.no_ligero or world > 1) else ligero_leg(args, prover, be, peaks)
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         log2_sample = max(10, min(20, args.log2_sumcheck) - 0)
         ts = cpu_sample(log2_sample, args.log2_table)
         scale = (1 << args.log2_sumcheck) / (1 << log2_sample)
@@ -379,18 +411,23 @@ def run_b200(args, rank, world, local_rank):
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(step_s / world, 6), "unit": "s/proof", "n_gpus": world,
+            "metric": METRIC, "value": round(step_s, 6), "unit": "s/proof", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3),
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "Fp2 (u64 Goldilocks)",
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "Fp2 (u64 Goldilocks)",
             "data": "synthetic (seeded FpStream tables and GELU-LUT queries)",
             "config": {"workload": f"config 1: triple-product sumcheck 3 x 2^{args.log2_sumcheck} Fp2, "
                                    f"{args.log2_sumcheck} rounds + LogUp 2^{args.log2_queries} queries "
                                    f"vs 2^{args.log2_table} table",
-                       "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (805 MB tables)",
+                       "parallelism": f"one proof sharded over {world} GPU(s) (top index bits; one NCCL "
+                                      f"all-gather per sumcheck)" if world > 1 else "one proof on one GPU",
+                       "l2": "inputs larger than L2 (805 MB tables)",
                        "timing_policy": "wall-only counters"},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "gpu_launches": launches,
             "clocks": clocks.summary(),
-            "proof_check": {"messages": int(msgs.shape[0]), "proof_words": int(proof.shape[0])},
+            "proof_check": {"messages": int(msgs.shape[0]), "proof_words": int(proof.shape[0]),
+                            "sha256": hashlib.sha256(np.ascontiguousarray(msgs).tobytes() +
+                                                     np.ascontiguousarray(finals).tobytes() +
+                                                     np.ascontiguousarray(proof).tobytes()).hexdigest()},
             "ligero": ligero,
         }
         print(json.dumps(line), flush=True)

@@ -25,3 +25,11 @@ def oracle():
 
     o.build()
     return o
+
+
+@pytest.fixture(scope="session")
+def package_built():
+    """Both shared libraries of the package, built in place (incremental)."""
+    from volta_zk_b200 import build_all
+
+    build_all()

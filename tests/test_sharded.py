@@ -1,0 +1,117 @@
+"""Sharded single proof (volta_zk_b200/sharded.py) on the CPU: shard work
+emulated with the oracle, combined by the product's host logic, compared
+with the oracle's one-process proof; and the same across two gloo ranks
+through torch.distributed (the multi-GPU path's host side)."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import sharded_emulation as em
+from volta_zk_b200 import sharded as sh
+
+P = 0xFFFFFFFF00000001
+pytestmark = pytest.mark.usefixtures("package_built")
+
+
+def tables(oracle, n):
+    seed = bytes([0x51] * 32)
+    out = []
+    for t in range(3):
+        x = np.zeros((n, 2), dtype=np.uint64)
+        x[:, 0] = oracle.chacha_fp_rows(seed, t, 1, n)[0]
+        out.append(x)
+    out[2][:, 1] = oracle.chacha_fp_rows(seed, 7, 1, n)[0]
+    return out
+
+
+@pytest.mark.parametrize("log2n,G", [(1, 2), (5, 2), (8, 4), (10, 8)])
+def test_triple_finish(oracle, log2n, G):
+    n = 1 << log2n
+    a, b, c = tables(oracle, n)
+    seed = bytes([0x5A] * 32)
+    parts = []
+    for g in range(G):
+        sl = slice(g * n // G, (g + 1) * n // G)
+        parts.append(em.triple_local(oracle, a[sl], b[sl], c[sl], seed))
+    msgs, finals = sh.triple_finish([np.concatenate(p) for p in parts], n, seed)
+    em_msgs, em_finals = oracle.triple_sumcheck(a, b, c, seed)
+    assert np.array_equal(msgs, em_msgs)
+    assert np.array_equal(finals, em_finals)
+
+
+def lookup_case(log2f, log2t, seed):
+    rng = np.random.default_rng(seed)
+    table = rng.integers(-32768, 32768, size=1 << log2t, dtype=np.int64).astype(np.int16)
+    idx = rng.integers(0, 1 << log2t, size=1 << log2f)
+    return table[idx], table, np.bincount(idx, minlength=1 << log2t).astype(np.uint32)
+
+
+@pytest.mark.parametrize("log2f,log2t,G", [(2, 2, 2), (6, 4, 2), (9, 5, 4), (10, 4, 8)])
+def test_logup_finish(oracle, log2f, log2t, G):
+    f, table, mult = lookup_case(log2f, log2t, log2f * 10 + G)
+    seed, domain = bytes([0x4C] * 32), 0x1004
+    nf, nt = 1 << log2f, 1 << log2t
+    fe, te = em.embed_i16(f), em.embed_i16(table)
+    s = G.bit_length() - 1
+    parts = []
+    for g in range(G):
+        w, _ = em.logup_local(oracle, fe[g * nf // G:(g + 1) * nf // G], te[g * nt // G:(g + 1) * nt // G],
+                              mult[g * nt // G:(g + 1) * nt // G], s, seed, domain)
+        parts.append(w)
+    got = sh.logup_finish(parts, nf, nt, seed, domain)
+    exp = oracle.logup_prove(f, table, mult, seed, domain)
+    assert got.shape == exp.shape
+    assert np.array_equal(got, exp)
+
+
+def _rank(rank, world, port, q):
+    import torch.distributed as dist
+
+    from oracle import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        gather = sh.torch_all_gather()
+        f, table, mult = lookup_case(8, 4, 3)
+        nf, nt = f.size, table.size
+        fe, te = em.embed_i16(f), em.embed_i16(table)
+        seed, domain = bytes([0x4C] * 32), 0x1004
+        w, _ = em.logup_local(oracle, fe[rank * nf // world:(rank + 1) * nf // world],
+                              te[rank * nt // world:(rank + 1) * nt // world],
+                              mult[rank * nt // world:(rank + 1) * nt // world], world.bit_length() - 1, seed,
+                              domain)
+        proof = sh.logup_finish(gather(w), nf, nt, seed, domain)
+        ok = np.array_equal(proof, oracle.logup_prove(f, table, mult, seed, domain))
+        a, b, c = tables(oracle, 64)
+        sl = slice(rank * 64 // world, (rank + 1) * 64 // world)
+        m, fin = em.triple_local(oracle, a[sl], b[sl], c[sl], bytes([0x5A] * 32))
+        parts = gather(np.concatenate([m, fin]))
+        msgs, _ = sh.triple_finish(parts, 64, bytes([0x5A] * 32))
+        em_msgs, _ = oracle.triple_sumcheck(a, b, c, bytes([0x5A] * 32))
+        ok = ok and np.array_equal(msgs, em_msgs)
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks():
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    results = dict(q.get(timeout=5) for _ in range(2))
+    assert results == {0: True, 1: True}
+    assert all(p.exitcode == 0 for p in procs)

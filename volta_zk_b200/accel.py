@@ -157,6 +157,9 @@ def load_host_library():
                                       C.POINTER(C.c_size_t), C.c_char_p, sz]
         L.vzh_ligero_commit_open.argtypes = [vp, C.c_char_p, sz, sz, sz, sz, C.c_char_p, vp, vp, vp, vp,
                                              C.c_char_p, sz]
+        L.vzh_logup_local.argtypes = [vp, u64, sz, u64, sz, u64, sz, C.c_char_p, u64, vp, sz,
+                                      C.POINTER(C.c_size_t), C.c_char_p, sz]
+        L.vzh_fpstream_fp2.argtypes = [C.c_char_p, u64, sz, vp]
         L.vzh_fpstream_u64.argtypes = [C.c_char_p, u64, sz, vp]
         _host_lib = L
     return _host_lib
@@ -261,6 +264,13 @@ class CudaBackend:
         return n.value
 
 
+def fpstream_fp2(seed: bytes, domain: int, n: int) -> np.ndarray:
+    """The first n Fp2 draws of FpStream(seed, domain), shape (n, 2)."""
+    out = np.zeros((n, 2), dtype=np.uint64)
+    load_host_library().vzh_fpstream_fp2(seed, domain, n, _ptr(out))
+    return out
+
+
 def fpstream_u64(seed: bytes, domain: int, n: int) -> np.ndarray:
     """Raw u64 draws of FpStream(seed, domain) (rust/volta-field/src/lib.rs:231-267)."""
     out = np.zeros(n, dtype=np.uint64)
@@ -330,6 +340,18 @@ class Prover:
                                               _ptr(root), _ptr(idx), _ptr(cols), _ptr(paths), err, 1024)
         self._err(rc, err)
         return root.tobytes(), idx, cols, paths
+
+    def logup_local(self, f_col: int, n_f_local: int, t_col: int, n_t_local: int, mult: int, shard_bits: int,
+                    seed: bytes, domain: int) -> np.ndarray:
+        """This shard's share of a LogUp proof (see vzh_logup_local): Fp2 words."""
+        cap = 1 + 2 * (2 + sum(4 * (l - shard_bits) + 4 for l in range(shard_bits, 64)))
+        out = np.zeros((cap, 2), dtype=np.uint64)
+        written = C.c_size_t()
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_logup_local(self.h, f_col, n_f_local, t_col, n_t_local, mult, shard_bits, seed, domain,
+                                       _ptr(out), cap, C.byref(written), err, 1024)
+        self._err(rc, err)
+        return out[: written.value]
 
     def stats(self) -> RawStats:
         return self.backend.stats()

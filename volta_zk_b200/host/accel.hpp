@@ -132,6 +132,15 @@ TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint6
 std::vector<Fp2> logup_prove_resident(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col,
                                       size_t n_t, uint64_t mult, FpStream& chal);
 
+// Completion of a proof sharded over G = 2^s shards (sharded.cpp): `parts`
+// holds every shard's local output in shard order (triple: the messages of
+// its own rounds then its 3 final values; LogUp: vzh_logup_local's words).
+// The challenges are redrawn from the stream; the result equals the
+// one-device proof.
+TripleResult triple_finish(const Fp2* parts, size_t shards, size_t n, FpStream& tx);
+std::vector<Fp2> logup_finish(const Fp2* parts, size_t shards, size_t words_per_shard, size_t n_f, size_t n_t,
+                              FpStream& chal);
+
 // Ligero commitment of `rows` seeded Fp message rows (FpStream(row_seed, r),
 // msg_len words each) zero-padded to code_len, and `queries` column openings
 // at challenge_fp2().c0 mod code_len drawn from `tx` (ligero.rs:465-505,

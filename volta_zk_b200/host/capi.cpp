@@ -7,6 +7,7 @@
 
 #include "accel.hpp"
 #include "api.hpp"
+#include "protocol.hpp"
 
 using namespace vzh;
 
@@ -106,6 +107,79 @@ int vzh_ligero_commit_open(void* h, const uint8_t* row_seed, size_t rows, size_t
         std::memcpy(columns, o.columns.data(), o.columns.size() * sizeof(uint64_t));
         std::memcpy(paths, o.paths.data(), o.paths.size());
     });
+}
+
+// One shard's share of a LogUp proof (both sides, see frac_side_local):
+// leaves are this shard's slices of the query / table columns (n_f_local,
+// n_t_local entries), shard_bits = log2(shards).  Output (Fp2 words): alpha,
+// then per side root_p, root_q and per global layer l >= shard_bits the
+// 4 (l - shard_bits) local round accumulators followed by 4 left-over values.
+int vzh_logup_local(void* h, uint64_t f_col, size_t n_f_local, uint64_t t_col, size_t n_t_local, uint64_t mult,
+                    size_t shard_bits, const uint8_t* seed, uint64_t domain, vz_fp2* out, size_t cap,
+                    size_t* written, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        Backend& b = *static_cast<Backend*>(h);
+        const Api& A = b.api();
+        FpStream chal(seed, domain);
+        std::vector<Fp2> words;
+        const Fp2 alpha = chal.next_fp2();
+        words.push_back(alpha);
+        const uint32_t zero_shift = 0;
+        Owned own(b);
+        const uint64_t shifts = own.add(b.alloc(sizeof(uint32_t)));
+        b.upload(shifts, 0, &zero_shift, sizeof(zero_shift));
+        const uint64_t cols[2] = {f_col, t_col};
+        const size_t ns[2] = {n_f_local, n_t_local};
+        for (int side = 0; side < 2; ++side) {
+            Owned so(b);
+            const uint64_t leaf = so.add(b.alloc(ns[side] * sizeof(uint64_t)));
+            b.check(A.volta_cuda_pack_lookup_leaf_device(b.ctx(), cols[side], 0, shifts, 0, leaf, 0, 1, ns[side],
+                                                         alpha.c0),
+                    "pack_lookup_leaf_device");
+            size_t local_depth = 0;
+            while ((size_t{1} << local_depth) < ns[side]) ++local_depth;
+            const SideSchedule sch = draw_side_schedule(chal, local_depth + shard_bits);
+            const LocalSide loc = frac_side_local(b, leaf, side ? mult : 0, ns[side], alpha.c1, shard_bits, sch);
+            words.push_back(loc.root_p);
+            words.push_back(loc.root_q);
+            for (size_t i = 0; i < loc.accs.size(); ++i) {
+                words.insert(words.end(), loc.accs[i].begin(), loc.accs[i].end());
+                words.insert(words.end(), loc.leftover[i].begin(), loc.leftover[i].end());
+            }
+        }
+        if (words.size() > cap) throw AccelError("local LogUp buffer too small");
+        std::memcpy(out, words.data(), words.size() * sizeof(vz_fp2));
+        *written = words.size();
+    });
+}
+
+// Sharded-proof completion (see accel.hpp); no device involved.
+int vzh_triple_finish(const vz_fp2* parts, size_t shards, size_t n, const uint8_t* seed, vz_fp2* messages,
+                      vz_fp2* finals, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        FpStream tx(seed, UINT64_MAX);
+        TripleResult r = triple_finish(parts, shards, n, tx);
+        std::memcpy(messages, r.messages.data(), r.messages.size() * sizeof(vz_fp2));
+        std::memcpy(finals, r.finals, sizeof(r.finals));
+    });
+}
+
+int vzh_logup_finish(const vz_fp2* parts, size_t shards, size_t words_per_shard, size_t n_f, size_t n_t,
+                     const uint8_t* seed, uint64_t domain, vz_fp2* out, size_t cap, size_t* written, char* err,
+                     size_t len) {
+    return guarded(err, len, [&] {
+        FpStream chal(seed, domain);
+        std::vector<Fp2> proof = logup_finish(parts, shards, words_per_shard, n_f, n_t, chal);
+        if (proof.size() > cap) throw AccelError("logup proof buffer too small");
+        std::memcpy(out, proof.data(), proof.size() * sizeof(vz_fp2));
+        *written = proof.size();
+    });
+}
+
+// The first n Fp2 draws of FpStream(seed, domain) (challenge schedules).
+void vzh_fpstream_fp2(const uint8_t* seed, uint64_t domain, size_t n, vz_fp2* out) {
+    FpStream s(seed, domain);
+    for (size_t i = 0; i < n; ++i) out[i] = s.next_fp2();
 }
 
 // Raw u64 draws of FpStream(seed, domain) (input synthesis for benches).

@@ -43,6 +43,27 @@ struct Owned {
 
 void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t n, uint64_t alpha1,
                                FpStream& chal, std::vector<Fp2>& proof);
+
+// Every challenge of one fraction-tree side in the round-by-round order: per
+// layer l the batching lambda, l round challenges and the split challenge t;
+// point[l] is layer l's claim point (t, r' of layer l - 1).
+struct SideSchedule {
+    std::vector<Fp2> lambda, t;
+    std::vector<std::vector<Fp2>> r, point;
+};
+SideSchedule draw_side_schedule(FpStream& chal, size_t depth);
+
+// One shard's part of a side (scheduled.cpp): its subtree root and, per
+// global layer l >= shard_bits, the raw accumulators of the first
+// l - shard_bits rounds and the four left-over vector values.
+struct LocalSide {
+    size_t shard_bits = 0;
+    Fp2 root_p, root_q;
+    std::vector<std::vector<Fp2>> accs;      // [l - shard_bits][4 (l - shard_bits)]
+    std::vector<std::vector<Fp2>> leftover;  // [l - shard_bits][4]
+};
+LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_local, uint64_t alpha1,
+                          size_t shard_bits, const SideSchedule& sch);
 TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
                                        FpStream& tx);
 

@@ -19,14 +19,6 @@
 
 namespace vzh {
 
-namespace {
-
-// Layout of one side's message buffer: roots, then per layer l its l round
-// accumulators (4 Fp2 each) followed by its 4 split values.
-size_t layer_msg_offset(size_t l) { return 2 + 2 * l * (l - 1) + 4 * l; }
-
-}  // namespace
-
 TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
                                        FpStream& tx) {
     const Api& A = b.api();
@@ -88,66 +80,94 @@ TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint
     return out;
 }
 
-void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t n, uint64_t alpha1,
-                               FpStream& chal, std::vector<Fp2>& proof) {
+SideSchedule draw_side_schedule(FpStream& chal, size_t depth) {
+    SideSchedule s;
+    s.lambda.resize(depth);
+    s.t.resize(depth);
+    s.r.resize(depth);
+    s.point.resize(depth);
+    for (size_t l = 0; l < depth; ++l) {
+        s.lambda[l] = chal.next_fp2();
+        s.r[l].resize(l);
+        for (auto& x : s.r[l]) x = chal.next_fp2();
+        s.t[l] = chal.next_fp2();
+        if (l + 1 < depth) {  // claim point of the next layer: (t, r')
+            s.point[l + 1].push_back(s.t[l]);
+            s.point[l + 1].insert(s.point[l + 1].end(), s.r[l].begin(), s.r[l].end());
+        }
+    }
+    return s;
+}
+
+// One shard of a fraction-tree side.  The shard holds leaves
+// [g n_local, (g+1) n_local) of a side of depth log2(n_local) + shard_bits;
+// its subtree is the slice of every global level below level shard_bits.
+// For every global layer l >= shard_bits it runs the first l - shard_bits
+// rounds on its slice (the rounds that only fold the shard's own index bits)
+// with the suffix-eq tables of the truncated claim point, so each round
+// accumulator is this shard's share of the global one up to the factor
+// eq(top bits of the point, g), and keeps the four vector values left over.
+// With shard_bits = 0 these are the whole rounds and the splits.
+LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_local, uint64_t alpha1,
+                          size_t shard_bits, const SideSchedule& sch) {
     const Api& A = b.api();
     const ExtApi& X = b.ext();
     void* ctx = b.ctx();
-    size_t depth = 0;
-    while ((size_t{1} << depth) < n) ++depth;
-    // ---- every challenge of this side, in the round-by-round order:
-    // per layer l: lambda, l round challenges, the split challenge t.
-    std::vector<Fp2> lambda(depth), t(depth);
-    std::vector<std::vector<Fp2>> r(depth), point(depth);
-    for (size_t l = 0; l < depth; ++l) {
-        lambda[l] = chal.next_fp2();
-        r[l].resize(l);
-        for (auto& x : r[l]) x = chal.next_fp2();
-        t[l] = chal.next_fp2();
-        if (l + 1 < depth) {  // claim point of the next layer: (t, r')
-            point[l + 1].push_back(t[l]);
-            point[l + 1].insert(point[l + 1].end(), r[l].begin(), r[l].end());
-        }
-    }
+    size_t local_depth = 0;
+    while ((size_t{1} << local_depth) < n_local) ++local_depth;
+    if ((size_t{1} << local_depth) != n_local || !local_depth)
+        throw AccelError("fraction-tree shards need a power-of-two length of at least 2");
+    const size_t depth = local_depth + shard_bits;
+    LocalSide out;
+    out.shard_bits = shard_bits;
     Owned own(b);
-    // all claim points in one upload: point l at offset l(l-1)/2
-    const size_t pts_total = depth * (depth - 1) / 2;
-    uint64_t pts = 0;
-    if (pts_total) {
-        std::vector<Fp2> flat;
-        flat.reserve(pts_total);
-        for (size_t l = 0; l < depth; ++l) flat.insert(flat.end(), point[l].begin(), point[l].end());
-        pts = own.add(b.alloc(pts_total * sizeof(Fp2)));
-        b.upload(pts, 0, flat.data(), pts_total * sizeof(Fp2));
+    // truncated claim points of the sharded layers in one upload
+    std::vector<size_t> pts_off(depth, 0);
+    std::vector<Fp2> flat;
+    for (size_t l = shard_bits; l < depth; ++l) {
+        pts_off[l] = flat.size();
+        const size_t Lp = l - shard_bits;
+        flat.insert(flat.end(), sch.point[l].begin(), sch.point[l].begin() + Lp);
     }
-    const size_t msg_total = layer_msg_offset(depth);
+    uint64_t pts = 0;
+    if (!flat.empty()) {
+        pts = own.add(b.alloc(flat.size() * sizeof(Fp2)));
+        b.upload(pts, 0, flat.data(), flat.size() * sizeof(Fp2));
+    }
+    // message slots: local root, then per sharded layer its local round
+    // accumulators (4 Fp2 each) and its 4 left-over values
+    std::vector<size_t> moff(depth, 0);
+    size_t msg_total = 2;
+    for (size_t l = shard_bits; l < depth; ++l) {
+        moff[l] = msg_total;
+        msg_total += 4 * (l - shard_bits) + 4;
+    }
     const uint64_t msgs = own.add(b.alloc(msg_total * sizeof(Fp2)));
-    // ---- the fraction tree and its root
-    const uint64_t tp = own.add(b.alloc((n > 1 ? n - 1 : 1) * sizeof(Fp2)));
-    const uint64_t tq = own.add(b.alloc((n > 1 ? n - 1 : 1) * sizeof(Fp2)));
-    b.check(A.volta_cuda_logup_tree_device(ctx, leaf, 0, mult, 0, n, alpha1, mult ? 1 : 0, tp, 0, tq, 0),
+    const uint64_t tp = own.add(b.alloc((n_local - 1) * sizeof(Fp2)));
+    const uint64_t tq = own.add(b.alloc((n_local - 1) * sizeof(Fp2)));
+    b.check(A.volta_cuda_logup_tree_device(ctx, leaf, 0, mult, 0, n_local, alpha1, mult ? 1 : 0, tp, 0, tq, 0),
             "logup_tree_device");
     b.check(A.volta_cuda_resident_copy_rows(ctx, tp, 0, sizeof(Fp2), msgs, 0, sizeof(Fp2), 1, sizeof(Fp2)),
             "resident_copy_rows");
     b.check(A.volta_cuda_resident_copy_rows(ctx, tq, 0, sizeof(Fp2), msgs, sizeof(Fp2), sizeof(Fp2), 1,
                                             sizeof(Fp2)),
             "resident_copy_rows");
-    // ---- layers, all enqueued without a host wait
-    for (size_t l = 0; l < depth; ++l) {
+    for (size_t l = shard_bits; l < depth; ++l) {
         Owned layer(b);
-        const size_t L = l, vector_len = size_t{1} << l, child_len = size_t{2} << l;
-        const size_t moff = layer_msg_offset(l), split = moff + 4 * L;
+        const size_t L = l - shard_bits;  // local rounds
+        const size_t vector_len = size_t{1} << L, child_len = size_t{2} << L;
+        const size_t split = moff[l] + 4 * L;
         uint64_t src_p = tp, src_q = tq;
         size_t child_off = child_len - 1;
         if (l + 1 == depth) {
-            src_p = layer.add(b.alloc(n * sizeof(Fp2)));
-            src_q = layer.add(b.alloc(n * sizeof(Fp2)));
-            b.check(A.volta_cuda_logup_materialize_leaves_device(ctx, leaf, 0, mult, 0, n, alpha1, mult ? 1 : 0,
-                                                                 src_p, 0, src_q, 0),
+            src_p = layer.add(b.alloc(n_local * sizeof(Fp2)));
+            src_q = layer.add(b.alloc(n_local * sizeof(Fp2)));
+            b.check(A.volta_cuda_logup_materialize_leaves_device(ctx, leaf, 0, mult, 0, n_local, alpha1,
+                                                                 mult ? 1 : 0, src_p, 0, src_q, 0),
                     "logup_materialize_leaves_device");
             child_off = 0;
         }
-        if (L == 0) {  // no rounds: the split values are the two children
+        if (L == 0) {  // no local rounds: the four values are the two child pairs
             b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_p, child_off, 1, msgs, split, msgs, split + 1),
                     "fp2_deinterleave_device");
             b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_q, child_off, 1, msgs, split + 2, msgs,
@@ -162,17 +182,17 @@ void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t 
         b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_q, child_off, vector_len, v[2], 0, v[3], 0),
                 "fp2_deinterleave_device");
         const uint64_t suffix = layer.add(b.alloc(((size_t{1} << L) - 1) * sizeof(Fp2)));
-        b.check(A.volta_cuda_logup_suffix_eq_device(ctx, pts, L * (L - 1) / 2, L, suffix, 0),
-                "logup_suffix_eq_device");
+        b.check(A.volta_cuda_logup_suffix_eq_device(ctx, pts, pts_off[l], L, suffix, 0), "logup_suffix_eq_device");
         size_t len = vector_len;
         b.check(A.volta_cuda_logup_general_round_into_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, suffix,
-                                                             (size_t{1} << (L - 1)) - 1, len / 2, msgs, moff),
+                                                             (size_t{1} << (L - 1)) - 1, len / 2, msgs, moff[l]),
                 "logup_general_round_into_device");
         for (size_t j = 0; j < L; ++j) {
+            const Fp2 rj = sch.r[l][j];
             const size_t half = len / 2;
-            if (half == 1) {  // last fold: the split values land in their slots
-                b.check(A.volta_cuda_logup_fold4_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, 1, r[l][j], msgs,
-                                                        split, msgs, split + 1, msgs, split + 2, msgs, split + 3),
+            if (half == 1) {  // last local fold: the left-over values land in their slots
+                b.check(A.volta_cuda_logup_fold4_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, 1, rj, msgs, split,
+                                                        msgs, split + 1, msgs, split + 2, msgs, split + 3),
                         "logup_fold4_device");
                 break;
             }
@@ -180,16 +200,16 @@ void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t 
             for (auto& x : nv) x = layer.add(b.alloc(half * sizeof(Fp2)));
             const size_t soff = (size_t{1} << (L - 2 - j)) - 1;  // suffix table of round j + 1
             if (X.logup_fold_round_into) {
-                b.check(X.logup_fold_round_into(ctx, v[0], v[1], v[2], v[3], len, r[l][j], nv[0], nv[1], nv[2],
-                                                nv[3], suffix, soff, msgs, moff + 4 * (j + 1)),
+                b.check(X.logup_fold_round_into(ctx, v[0], v[1], v[2], v[3], len, rj, nv[0], nv[1], nv[2], nv[3],
+                                                suffix, soff, msgs, moff[l] + 4 * (j + 1)),
                         "volta_b200_logup_fold_round_into_device");
             } else {
-                b.check(A.volta_cuda_logup_fold4_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, half, r[l][j],
-                                                        nv[0], 0, nv[1], 0, nv[2], 0, nv[3], 0),
+                b.check(A.volta_cuda_logup_fold4_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, half, rj, nv[0], 0,
+                                                        nv[1], 0, nv[2], 0, nv[3], 0),
                         "logup_fold4_device");
                 b.check(A.volta_cuda_logup_general_round_into_device(ctx, nv[0], 0, nv[1], 0, nv[2], 0, nv[3], 0,
                                                                      suffix, soff, half / 2, msgs,
-                                                                     moff + 4 * (j + 1)),
+                                                                     moff[l] + 4 * (j + 1)),
                         "logup_general_round_into_device");
             }
             for (int k = 0; k < 4; ++k) {
@@ -199,21 +219,36 @@ void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t 
             len = half;
         }
     }
-    // ---- one download, then the proof words in the round-by-round order
     std::vector<Fp2> m(msg_total);
     b.download(msgs, 0, m.data(), msg_total * sizeof(Fp2));
-    proof.push_back(m[0]);
-    proof.push_back(m[1]);
+    out.root_p = m[0];
+    out.root_q = m[1];
+    for (size_t l = shard_bits; l < depth; ++l) {
+        const size_t L = l - shard_bits;
+        out.accs.emplace_back(m.begin() + moff[l], m.begin() + moff[l] + 4 * L);
+        out.leftover.emplace_back(m.begin() + moff[l] + 4 * L, m.begin() + moff[l] + 4 * L + 4);
+    }
+    return out;
+}
+
+void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t n, uint64_t alpha1,
+                               FpStream& chal, std::vector<Fp2>& proof) {
+    size_t depth = 0;
+    while ((size_t{1} << depth) < n) ++depth;
+    const SideSchedule sch = draw_side_schedule(chal, depth);
+    const LocalSide loc = frac_side_local(b, leaf, mult, n, alpha1, 0, sch);
+    // proof words in the round-by-round order (h0, h2 = cpref (lambda pq + qq))
+    proof.push_back(loc.root_p);
+    proof.push_back(loc.root_q);
     for (size_t l = 0; l < depth; ++l) {
-        const size_t moff = layer_msg_offset(l);
         Fp2 cpref{1, 0};
         for (size_t j = 0; j < l; ++j) {
-            const Fp2* acc = &m[moff + 4 * j];
-            proof.push_back(f2mul(cpref, f2add(f2mul(lambda[l], acc[0]), acc[2])));
-            proof.push_back(f2mul(cpref, f2add(f2mul(lambda[l], acc[1]), acc[3])));
-            cpref = eq_step(cpref, point[l][j], r[l][j]);
+            const Fp2* acc = &loc.accs[l][4 * j];
+            proof.push_back(f2mul(cpref, f2add(f2mul(sch.lambda[l], acc[0]), acc[2])));
+            proof.push_back(f2mul(cpref, f2add(f2mul(sch.lambda[l], acc[1]), acc[3])));
+            cpref = eq_step(cpref, sch.point[l][j], sch.r[l][j]);
         }
-        for (int k = 0; k < 4; ++k) proof.push_back(m[moff + 4 * l + k]);
+        for (int k = 0; k < 4; ++k) proof.push_back(loc.leftover[l][k]);
     }
 }
 
