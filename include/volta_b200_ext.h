@@ -51,6 +51,41 @@ int volta_b200_logup_fold_round_into_device(void* ctx, uint64_t p0_id, uint64_t 
                                             size_t suffix_offset, uint64_t out_id, size_t out_offset);
 
 /*
+ * Whole small sumchecks in one CTA each, with the challenges in device memory
+ * (known in advance in the clear sink / private transcript).
+ *
+ * A LogUp layer job runs all `rounds` (<= 11) rounds of a layer sumcheck on
+ * vectors of 2^rounds entries: either four resident vectors (v_id[k] at
+ * v_offset[k]) or, when il_p_id != 0, the interleaved children
+ * (p, q)[il_offset .. il_offset + 2^(rounds+1)) of a fraction-tree level.
+ * Its suffix-eq tables come from the `rounds` claim-point coordinates at
+ * (point_id, point_offset); round j folds with the challenge at
+ * (r_id, r_offset + j).  Output at (out_id, out_offset): per round the four
+ * raw accumulators of volta_cuda_logup_general_round_device, then the four
+ * final values (p0, p1, q0, q1).  Jobs are independent (one CTA each).
+ */
+typedef struct vzb_layer_job {
+    uint64_t v_id[4];
+    size_t v_offset[4];
+    uint64_t il_p_id, il_q_id;
+    size_t il_offset;
+    size_t rounds;
+    uint64_t point_id;
+    size_t point_offset;
+    uint64_t r_id;
+    size_t r_offset;
+    uint64_t out_id;
+    size_t out_offset;
+} vzb_layer_job;
+int volta_b200_logup_layers_device(void* ctx, const vzb_layer_job* jobs, size_t count);
+
+/* All rounds of a triple-product sumcheck on three resident tables of len
+ * (<= 2^11, a power of two) entries; challenges at (r_id, r_offset).  Output:
+ * 3 messages per round, then the 3 final values. */
+int volta_b200_triple_tail_device(void* ctx, uint64_t a_id, uint64_t b_id, uint64_t c_id, size_t len,
+                                  uint64_t r_id, size_t r_offset, uint64_t out_id, size_t out_offset);
+
+/*
  * Triple-product round message without any device allocation.
  *
  * No counterpart in the reference seam.  Every other entry point reserves

@@ -22,6 +22,8 @@ struct ExtApi {
     decltype(&::volta_b200_logup_fold_round_device) logup_fold_round = nullptr;
     decltype(&::volta_b200_triple_fold_round_into_device) triple_fold_round_into = nullptr;
     decltype(&::volta_b200_logup_fold_round_into_device) logup_fold_round_into = nullptr;
+    decltype(&::volta_b200_logup_layers_device) logup_layers = nullptr;
+    decltype(&::volta_b200_triple_tail_device) triple_tail = nullptr;
 };
 
 }  // namespace vzh

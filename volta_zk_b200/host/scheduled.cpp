@@ -19,6 +19,9 @@
 
 namespace vzh {
 
+// Vectors at most this long finish in one CTA (volta_b200_*_tail / layers).
+constexpr size_t kTailLen = 2048;
+
 TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
                                        FpStream& tx) {
     const Api& A = b.api();
@@ -32,23 +35,36 @@ TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint
     Owned own(b);
     // slots: 3 per round message, then the 3 final openings
     const uint64_t msgs = own.add(b.alloc((3 * k + 3) * sizeof(Fp2)));
+    uint64_t rdev = 0;
+    if (X.triple_tail && k) {
+        rdev = own.add(b.alloc(k * sizeof(Fp2)));
+        b.upload(rdev, 0, r.data(), k * sizeof(Fp2));
+    }
     uint64_t cur[3] = {a, bb, c};
     bool owned = false;
-    if (k)
+    size_t len = n, j = 0;
+    // large rounds: one pass each (fold of the previous round fused with the next round)
+    if (k && (!X.triple_tail || n > kTailLen))
         b.check(A.volta_cuda_fp2_triple_product_round_into_device(ctx, a, 0, bb, 0, c, 0, n / 2, msgs, 0),
                 "fp2_triple_product_round_into_device");
-    size_t len = n;
-    for (size_t j = 0; j < k; ++j) {
+    while (j < k && (!X.triple_tail || len > kTailLen)) {
         const size_t pairs = len / 2;
         if (pairs == 1) {  // last fold: the openings land in their slots
             for (int t = 0; t < 3; ++t)
                 b.check(A.volta_cuda_fp2_fold_rows_device(ctx, cur[t], 0, 1, 2, r[j], msgs, 3 * k + t),
                         "fp2_fold_rows_device");
+            ++j;
+            len = 1;
             break;
         }
         uint64_t nxt[3];
         for (int t = 0; t < 3; ++t) nxt[t] = own.add(b.alloc(pairs * sizeof(Fp2)));
-        if (X.triple_fold_round_into) {
+        const bool to_tail = X.triple_tail && pairs <= kTailLen;
+        if (to_tail) {  // the remaining rounds run in the tail
+            for (int t = 0; t < 3; ++t)
+                b.check(A.volta_cuda_fp2_fold_rows_device(ctx, cur[t], 0, 1, len, r[j], nxt[t], 0),
+                        "fp2_fold_rows_device");
+        } else if (X.triple_fold_round_into) {
             b.check(X.triple_fold_round_into(ctx, cur[0], cur[1], cur[2], len, r[j], nxt[0], nxt[1], nxt[2], msgs,
                                              3 * (j + 1)),
                     "volta_b200_triple_fold_round_into_device");
@@ -66,12 +82,17 @@ TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint
         }
         owned = true;
         len = pairs;
+        ++j;
     }
-    if (!k)  // a single entry: the openings are the inputs
+    if (X.triple_tail && len <= kTailLen && (j < k || k == 0)) {
+        // rounds j..k-1 and the openings in one CTA
+        b.check(X.triple_tail(ctx, cur[0], cur[1], cur[2], len, rdev, j, msgs, 3 * j), "volta_b200_triple_tail_device");
+    } else if (!k) {  // a single entry: the openings are the inputs
         for (int t = 0; t < 3; ++t)
             b.check(A.volta_cuda_resident_copy_rows(ctx, cur[t], 0, sizeof(Fp2), msgs, t * sizeof(Fp2),
                                                     sizeof(Fp2), 1, sizeof(Fp2)),
                     "resident_copy_rows");
+    }
     std::vector<Fp2> host(3 * k + 3);
     b.download(msgs, 0, host.data(), host.size() * sizeof(Fp2));
     TripleResult out;
@@ -152,6 +173,22 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
     b.check(A.volta_cuda_resident_copy_rows(ctx, tq, 0, sizeof(Fp2), msgs, sizeof(Fp2), sizeof(Fp2), 1,
                                             sizeof(Fp2)),
             "resident_copy_rows");
+    // round challenges of the local rounds, for the one-CTA layer jobs
+    const bool jobs_on = X.logup_layers != nullptr;
+    std::vector<size_t> r_off(depth, 0);
+    uint64_t rbuf = 0;
+    if (jobs_on) {
+        std::vector<Fp2> rflat;
+        for (size_t l = shard_bits; l < depth; ++l) {
+            r_off[l] = rflat.size();
+            rflat.insert(rflat.end(), sch.r[l].begin(), sch.r[l].begin() + (l - shard_bits));
+        }
+        if (!rflat.empty()) {
+            rbuf = own.add(b.alloc(rflat.size() * sizeof(Fp2)));
+            b.upload(rbuf, 0, rflat.data(), rflat.size() * sizeof(Fp2));
+        }
+    }
+    std::vector<vzb_layer_job> jobs;  // launched together after every large round is enqueued
     for (size_t l = shard_bits; l < depth; ++l) {
         Owned layer(b);
         const size_t L = l - shard_bits;  // local rounds
@@ -159,13 +196,30 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
         const size_t split = moff[l] + 4 * L;
         uint64_t src_p = tp, src_q = tq;
         size_t child_off = child_len - 1;
-        if (l + 1 == depth) {
-            src_p = layer.add(b.alloc(n_local * sizeof(Fp2)));
-            src_q = layer.add(b.alloc(n_local * sizeof(Fp2)));
+        const bool small = jobs_on && vector_len <= kTailLen;
+        if (l + 1 == depth) {  // the leaf layer's children are the materialised leaves
+            Owned& keep = small ? own : layer;  // a job reads them after this loop
+            src_p = keep.add(b.alloc(n_local * sizeof(Fp2)));
+            src_q = keep.add(b.alloc(n_local * sizeof(Fp2)));
             b.check(A.volta_cuda_logup_materialize_leaves_device(ctx, leaf, 0, mult, 0, n_local, alpha1,
                                                                  mult ? 1 : 0, src_p, 0, src_q, 0),
                     "logup_materialize_leaves_device");
             child_off = 0;
+        }
+        if (small) {  // the whole layer in one CTA: deinterleave on load, all rounds, splits
+            vzb_layer_job jb{};
+            jb.il_p_id = src_p;
+            jb.il_q_id = src_q;
+            jb.il_offset = child_off;
+            jb.rounds = L;
+            jb.point_id = pts;
+            jb.point_offset = pts_off[l];
+            jb.r_id = rbuf;
+            jb.r_offset = r_off[l];
+            jb.out_id = msgs;
+            jb.out_offset = moff[l];
+            jobs.push_back(jb);
+            continue;
         }
         if (L == 0) {  // no local rounds: the four values are the two child pairs
             b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_p, child_off, 1, msgs, split, msgs, split + 1),
@@ -190,15 +244,34 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
         for (size_t j = 0; j < L; ++j) {
             const Fp2 rj = sch.r[l][j];
             const size_t half = len / 2;
-            if (half == 1) {  // last local fold: the left-over values land in their slots
+            if (half == 1) {  // last fold: the left-over values land in their slots
                 b.check(A.volta_cuda_logup_fold4_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, 1, rj, msgs, split,
                                                         msgs, split + 1, msgs, split + 2, msgs, split + 3),
                         "logup_fold4_device");
                 break;
             }
+            const bool to_job = jobs_on && half <= kTailLen;
+            Owned& keep = to_job ? own : layer;  // the job reads the folded vectors later
             uint64_t nv[4];
-            for (auto& x : nv) x = layer.add(b.alloc(half * sizeof(Fp2)));
+            for (auto& x : nv) x = keep.add(b.alloc(half * sizeof(Fp2)));
             const size_t soff = (size_t{1} << (L - 2 - j)) - 1;  // suffix table of round j + 1
+            if (to_job) {
+                b.check(A.volta_cuda_logup_fold4_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, half, rj, nv[0], 0,
+                                                        nv[1], 0, nv[2], 0, nv[3], 0),
+                        "logup_fold4_device");
+                // rounds j + 1 .. L - 1 and the splits in one CTA
+                vzb_layer_job jb{};
+                for (int k = 0; k < 4; ++k) jb.v_id[k] = nv[k];
+                jb.rounds = L - (j + 1);
+                jb.point_id = pts;
+                jb.point_offset = pts_off[l] + j + 1;
+                jb.r_id = rbuf;
+                jb.r_offset = r_off[l] + j + 1;
+                jb.out_id = msgs;
+                jb.out_offset = moff[l] + 4 * (j + 1);
+                jobs.push_back(jb);
+                break;
+            }
             if (X.logup_fold_round_into) {
                 b.check(X.logup_fold_round_into(ctx, v[0], v[1], v[2], v[3], len, rj, nv[0], nv[1], nv[2], nv[3],
                                                 suffix, soff, msgs, moff[l] + 4 * (j + 1)),
@@ -219,6 +292,7 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
             len = half;
         }
     }
+    if (!jobs.empty()) b.check(X.logup_layers(ctx, jobs.data(), jobs.size()), "volta_b200_logup_layers_device");
     std::vector<Fp2> m(msg_total);
     b.download(msgs, 0, m.data(), msg_total * sizeof(Fp2));
     out.root_p = m[0];
