@@ -51,6 +51,24 @@ int volta_b200_logup_fold_round_into_device(void* ctx, uint64_t p0_id, uint64_t 
                                             size_t suffix_offset, uint64_t out_id, size_t out_offset);
 
 /*
+ * LogUp layer rounds read straight from a fraction-tree level: the layer's
+ * vectors p0, p1, q0, q1 (vector_len entries each) are the even/odd children
+ * p[child_offset + 2k], p[child_offset + 2k + 1], q[...] of the level.
+ * round_il: round 0 (as volta_cuda_logup_general_round_into_device on the
+ * deinterleaved vectors); fold_round_il: fold with r into the four resident
+ * half-length vectors o0..o3 and the next round's message (as
+ * volta_b200_logup_fold_round_into_device), suffix table at
+ * (suffix_id, suffix_offset).
+ */
+int volta_b200_logup_round_il_into_device(void* ctx, uint64_t p_id, uint64_t q_id, size_t child_offset,
+                                          size_t vector_len, uint64_t suffix_id, size_t suffix_offset,
+                                          uint64_t out_id, size_t out_offset);
+int volta_b200_logup_fold_round_il_into_device(void* ctx, uint64_t p_id, uint64_t q_id, size_t child_offset,
+                                               size_t vector_len, vz_fp2 r, uint64_t o0_id, uint64_t o1_id,
+                                               uint64_t o2_id, uint64_t o3_id, uint64_t suffix_id,
+                                               size_t suffix_offset, uint64_t out_id, size_t out_offset);
+
+/*
  * Whole small sumchecks in one CTA each, with the challenges in device memory
  * (known in advance in the clear sink / private transcript).
  *

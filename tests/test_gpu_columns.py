@@ -194,3 +194,20 @@ def test_small_vector_ops(be, oracle):
         assert np.array_equal(d[c * 16:(c + 1) * 16, 0], np.concatenate([col[0::2], col[1::2]]))
     for b in (ix, im, out, bc, rep, cp, ic, dout):
         be.free(b)
+
+
+def test_chacha_rows_with_rejected_draw(be, oracle):
+    """FpStream([0x11;32], 2215) draws a raw value >= p at index 45451 (found by a
+    CPU scan of the oracle stream); the fast row kernel flags that row and the
+    fix-up regenerates it with the rejection applied."""
+    seed = bytes([0x11] * 32)
+    raw = oracle.stream_u64(seed, 2215, 45460)
+    assert raw[45451] >= np.uint64(0xFFFFFFFF00000001)
+    rows, count, base = 16, 65536, 2208
+    out = be.alloc(8 * rows * count)
+    be.call("chacha8_prover_secret_fp_rows_device", out, 0, seed, base, rows, count)
+    got = be.download(out, 8 * rows * count).reshape(rows, count)
+    exp = oracle.chacha_fp_rows(seed, base, rows, count)
+    assert np.array_equal(got, exp)
+    assert got[2215 - base, 45451] == raw[45452]
+    be.free(out)

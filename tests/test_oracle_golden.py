@@ -308,3 +308,14 @@ def test_fixed_layer_oracle_matches_reference_mirror(oracle):
     res = fl.forward_layer(fl.OracleOps(oracle), x, w, luts, t)
     assert res["errors"] == [0] * len(res["errors"])
     assert fl.check_against_golden(res) == []
+
+
+def test_oracle_stream_skips_rejected_draw(oracle):
+    """FpStream rejection sampling (lib.rs:255-262): the raw draw >= p at index
+    45451 of FpStream([0x11;32], 2215) is skipped."""
+    seed = bytes([0x11] * 32)
+    raw = oracle.stream_u64(seed, 2215, 45460)
+    assert raw[45451] >= np.uint64(P)
+    rows = oracle.chacha_fp_rows(seed, 2215, 1, 45455)[0]
+    assert np.array_equal(rows[:45451], raw[:45451])
+    assert np.array_equal(rows[45451:], raw[45452:45456])

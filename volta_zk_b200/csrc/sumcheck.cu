@@ -147,6 +147,72 @@ struct LogupFoldEval {
     }
 };
 
+// The same two evaluations read straight from interleaved fraction-tree
+// children (p0 = P[2k], p1 = P[2k+1], q0 = Q[2k], q1 = Q[2k+1]): the
+// deinterleave pass of the reference's layer setup (logup.rs:1335-1360)
+// becomes part of the first round's loads.
+struct LogupEvalIL {
+    const Fp2 *P, *Q, *s;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        const Fp2 a0 = ldcs2(P + 4 * i), b0 = ldcs2(P + 4 * i + 1), a1 = ldcs2(P + 4 * i + 2), b1 = ldcs2(P + 4 * i + 3);
+        const Fp2 c0 = ldcs2(Q + 4 * i), d0 = ldcs2(Q + 4 * i + 1), c1 = ldcs2(Q + 4 * i + 2), d1 = ldcs2(Q + 4 * i + 3);
+        const Fp2 si = ldg2(s + i);
+        const Fp2 a2 = d2add_weak(a1, d2sub(a1, a0)), b2 = d2add_weak(b1, d2sub(b1, b0));
+        const Fp2 c2 = d2add_weak(c1, d2sub(c1, c0)), d2 = d2add_weak(d1, d2sub(d1, d0));
+        Fp2W t;
+        f2w_zero(t);
+        f2w_mac(t, a0, d0);
+        f2w_mac(t, b0, c0);
+        f2w_mac(w[0], si, f2w_reduce(t));
+        f2w_zero(t);
+        f2w_mac(t, a2, d2);
+        f2w_mac(t, b2, c2);
+        f2w_mac(w[1], si, f2w_reduce(t));
+        f2w_mac(w[2], si, d2mul(c0, d0));
+        f2w_mac(w[3], si, d2mul(c2, d2));
+    }
+};
+
+struct LogupFoldEvalIL {
+    const Fp2 *P, *Q, *s;
+    Fp2 *o0, *o1, *o2, *o3;
+    Fp2 r;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        Fp2 x[8], y[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            x[k] = ldcs2(P + 8 * i + k);
+            y[k] = ldcs2(Q + 8 * i + k);
+        }
+        const Fp2 a0 = d2fold(x[0], x[2], r), a1 = d2fold(x[4], x[6], r);
+        const Fp2 b0 = d2fold(x[1], x[3], r), b1 = d2fold(x[5], x[7], r);
+        const Fp2 c0 = d2fold(y[0], y[2], r), c1 = d2fold(y[4], y[6], r);
+        const Fp2 d0 = d2fold(y[1], y[3], r), d1 = d2fold(y[5], y[7], r);
+        st2(o0 + 2 * i, a0);
+        st2(o0 + 2 * i + 1, a1);
+        st2(o1 + 2 * i, b0);
+        st2(o1 + 2 * i + 1, b1);
+        st2(o2 + 2 * i, c0);
+        st2(o2 + 2 * i + 1, c1);
+        st2(o3 + 2 * i, d0);
+        st2(o3 + 2 * i + 1, d1);
+        const Fp2 si = ldg2(s + i);
+        const Fp2 a2 = d2add_weak(a1, d2sub(a1, a0)), b2 = d2add_weak(b1, d2sub(b1, b0));
+        const Fp2 c2 = d2add_weak(c1, d2sub(c1, c0)), d2 = d2add_weak(d1, d2sub(d1, d0));
+        Fp2W t;
+        f2w_zero(t);
+        f2w_mac(t, a0, d0);
+        f2w_mac(t, b0, c0);
+        f2w_mac(w[0], si, f2w_reduce(t));
+        f2w_zero(t);
+        f2w_mac(t, a2, d2);
+        f2w_mac(t, b2, c2);
+        f2w_mac(w[1], si, f2w_reduce(t));
+        f2w_mac(w[2], si, d2mul(c0, d0));
+        f2w_mac(w[3], si, d2mul(c2, d2));
+    }
+};
+
 struct DotEval {
     const Fp2 *a, *b;
     __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const { f2w_mac(w[0], ldcs2(a + i), ldcs2(b + i)); }
@@ -407,6 +473,30 @@ __global__ void eq_outer_kernel(const Fp2* lo, int lo_bits, const Fp2* hi, size_
         Fp2 v = f2mul(ldg2(lo + (i & mask)), ldg2(hi + (i >> lo_bits)));
         if (add) v = f2add(v, ldg2(add + i));
         st2(out + i, v);
+    }
+}
+
+// Several outer-product tables in one launch: table t has 2^bits[t] entries,
+// out_t[i] = lo_t[i & (2^11 - 1)] * hi_t[i >> 11].  The tables are laid out
+// back to back in the launch's index space (first[t] = sum of earlier sizes).
+constexpr int kMaxOuterTables = 12;
+struct OuterTables {
+    const Fp2* lo[kMaxOuterTables];
+    const Fp2* hi[kMaxOuterTables];
+    Fp2* out[kMaxOuterTables];
+    size_t first[kMaxOuterTables + 1];
+    int count;
+};
+
+__global__ void eq_outer_multi_kernel(OuterTables t) {
+    const size_t total = t.first[t.count];
+    const size_t mask = kEqTile - 1;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t z = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; z < total; z += stride) {
+        int k = 0;
+        while (z >= t.first[k + 1]) ++k;
+        const size_t i = z - t.first[k];
+        st2(t.out[k] + i, f2mul(ldg2(t.lo[k] + (i & mask)), ldg2(t.hi[k] + (i >> kEqTileBits))));
     }
 }
 
@@ -840,15 +930,21 @@ extern "C" int volta_cuda_logup_suffix_eq_device(void* raw, uint64_t points_id, 
     }
     eq_small_kernel<<<jobs.count, 256, 0, c->stream>>>(jobs);
     VZB_LAUNCHED(c);
-    // bands of 12 levels so that table k - 12 is complete before table k
+    // one launch per band of 11 tables: table k is the outer product of its
+    // low 11 coordinates and table k - 11, which an earlier band (or the
+    // small-table launch) completed
     for (int band = kEqTileBits + 1; band < L; band += kEqTileBits) {
+        OuterTables t{};
         for (int k = band; k < L && k < band + kEqTileBits; ++k) {
             const size_t entries = size_t{1} << k;
-            eq_outer_kernel<<<grid_for(c, entries, 256), 256, 0, c->stream>>>(
-                lows + static_cast<size_t>(k - kEqTileBits - 1) * kEqTile, kEqTileBits,
-                o + ((size_t{1} << (k - kEqTileBits)) - 1), entries, o + (entries - 1), nullptr);
-            VZB_LAUNCHED(c);
+            t.lo[t.count] = lows + static_cast<size_t>(k - kEqTileBits - 1) * kEqTile;
+            t.hi[t.count] = o + ((size_t{1} << (k - kEqTileBits)) - 1);
+            t.out[t.count] = o + (entries - 1);
+            t.first[t.count + 1] = t.first[t.count] + entries;
+            ++t.count;
         }
+        eq_outer_multi_kernel<<<grid_for(c, t.first[t.count], 256), 256, 0, c->stream>>>(t);
+        VZB_LAUNCHED(c);
     }
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpLogup, 0, 0);
@@ -1285,4 +1381,53 @@ extern "C" int volta_b200_logup_fold_round_into_device(void* raw, uint64_t p0_id
     const uint64_t in[4] = {p0_id, p1_id, q0_id, q1_id}, out[4] = {o0_id, o1_id, o2_id, o3_id};
     return logup_fold_round(static_cast<Context*>(raw), in, len, r, out, s_id, s_off, nullptr, out_id,
                             out_offset);
+}
+
+// ===========================================================================
+// Extensions: LogUp layer rounds straight from interleaved tree children
+// ===========================================================================
+
+extern "C" int volta_b200_logup_round_il_into_device(void* raw, uint64_t p_id, uint64_t q_id, size_t child_offset,
+                                                     size_t vector_len, uint64_t s_id, size_t s_off, uint64_t out_id,
+                                                     size_t out_offset) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || vector_len < 2 || (vector_len & 1)) return fail_message(c, "invalid interleaved LogUp round geometry");
+    void *P = nullptr, *Q = nullptr, *S = nullptr, *dev = nullptr;
+    if (region_elems(c, p_id, child_offset, 2 * vector_len, sizeof(Fp2), &P) ||
+        region_elems(c, q_id, child_offset, 2 * vector_len, sizeof(Fp2), &Q) ||
+        region_elems(c, s_id, s_off, vector_len / 2, sizeof(Fp2), &S) ||
+        region_elems(c, out_id, out_offset, 4, sizeof(Fp2), &dev))
+        return -1;
+    const MsgOut o = msg_out(c, static_cast<Fp2*>(dev), nullptr, 4);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    LogupEvalIL ev{static_cast<const Fp2*>(P), static_cast<const Fp2*>(Q), static_cast<const Fp2*>(S)};
+    if (launch_reduce_wide<4>(c, ev, vector_len / 2, store_epi<4>(o))) return -1;
+    return finish_msg(c, kOpLogup, o);
+}
+
+extern "C" int volta_b200_logup_fold_round_il_into_device(void* raw, uint64_t p_id, uint64_t q_id,
+                                                          size_t child_offset, size_t vector_len, Fp2 r,
+                                                          uint64_t o0_id, uint64_t o1_id, uint64_t o2_id,
+                                                          uint64_t o3_id, uint64_t s_id, size_t s_off,
+                                                          uint64_t out_id, size_t out_offset) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || vector_len < 4 || (vector_len & 3))
+        return fail_message(c, "invalid interleaved LogUp fold-round geometry");
+    void *P = nullptr, *Q = nullptr, *S = nullptr, *dev = nullptr;
+    void* o[4];
+    const uint64_t oid[4] = {o0_id, o1_id, o2_id, o3_id};
+    if (region_elems(c, p_id, child_offset, 2 * vector_len, sizeof(Fp2), &P) ||
+        region_elems(c, q_id, child_offset, 2 * vector_len, sizeof(Fp2), &Q) ||
+        region_elems(c, s_id, s_off, vector_len / 4, sizeof(Fp2), &S) ||
+        region_elems(c, out_id, out_offset, 4, sizeof(Fp2), &dev))
+        return -1;
+    for (int k = 0; k < 4; ++k)
+        if (region_elems(c, oid[k], 0, vector_len / 2, sizeof(Fp2), &o[k])) return -1;
+    const MsgOut m = msg_out(c, static_cast<Fp2*>(dev), nullptr, 4);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    LogupFoldEvalIL ev{static_cast<const Fp2*>(P), static_cast<const Fp2*>(Q), static_cast<const Fp2*>(S),
+                       static_cast<Fp2*>(o[0]), static_cast<Fp2*>(o[1]), static_cast<Fp2*>(o[2]),
+                       static_cast<Fp2*>(o[3]), r};
+    if (launch_reduce_wide<4>(c, ev, vector_len / 4, store_epi<4>(m))) return -1;
+    return finish_msg(c, kOpLogup, m);
 }

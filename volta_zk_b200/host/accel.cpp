@@ -115,6 +115,10 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         dlsym(handle_, "volta_b200_logup_layers_device"));
     ext_loaded_->triple_tail = reinterpret_cast<decltype(ext_loaded_->triple_tail)>(
         dlsym(handle_, "volta_b200_triple_tail_device"));
+    ext_loaded_->logup_round_il = reinterpret_cast<decltype(ext_loaded_->logup_round_il)>(
+        dlsym(handle_, "volta_b200_logup_round_il_into_device"));
+    ext_loaded_->logup_fold_round_il = reinterpret_cast<decltype(ext_loaded_->logup_fold_round_il)>(
+        dlsym(handle_, "volta_b200_logup_fold_round_il_into_device"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

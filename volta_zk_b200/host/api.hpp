@@ -24,6 +24,8 @@ struct ExtApi {
     decltype(&::volta_b200_logup_fold_round_into_device) logup_fold_round_into = nullptr;
     decltype(&::volta_b200_logup_layers_device) logup_layers = nullptr;
     decltype(&::volta_b200_triple_tail_device) triple_tail = nullptr;
+    decltype(&::volta_b200_logup_round_il_into_device) logup_round_il = nullptr;
+    decltype(&::volta_b200_logup_fold_round_il_into_device) logup_fold_round_il = nullptr;
 };
 
 }  // namespace vzh

@@ -229,19 +229,51 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
                     "fp2_deinterleave_device");
             continue;
         }
-        uint64_t v[4];
-        for (auto& x : v) x = layer.add(b.alloc(vector_len * sizeof(Fp2)));
-        b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_p, child_off, vector_len, v[0], 0, v[1], 0),
-                "fp2_deinterleave_device");
-        b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_q, child_off, vector_len, v[2], 0, v[3], 0),
-                "fp2_deinterleave_device");
         const uint64_t suffix = layer.add(b.alloc(((size_t{1} << L) - 1) * sizeof(Fp2)));
         b.check(A.volta_cuda_logup_suffix_eq_device(ctx, pts, pts_off[l], L, suffix, 0), "logup_suffix_eq_device");
         size_t len = vector_len;
-        b.check(A.volta_cuda_logup_general_round_into_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, suffix,
-                                                             (size_t{1} << (L - 1)) - 1, len / 2, msgs, moff[l]),
-                "logup_general_round_into_device");
-        for (size_t j = 0; j < L; ++j) {
+        uint64_t v[4];
+        size_t j_first = 0;
+        if (X.logup_round_il && X.logup_fold_round_il && vector_len >= 4) {
+            // rounds 0 and 1 read the interleaved children directly (no deinterleave pass)
+            b.check(X.logup_round_il(ctx, src_p, src_q, child_off, vector_len, suffix, (size_t{1} << (L - 1)) - 1,
+                                     msgs, moff[l]),
+                    "volta_b200_logup_round_il_into_device");
+            const size_t half = len / 2;
+            const bool to_job = jobs_on && half <= kTailLen;
+            Owned& keep = to_job ? own : layer;
+            for (auto& x : v) x = keep.add(b.alloc(half * sizeof(Fp2)));
+            // (when the rest goes to a job, the job rewrites this round-1 message)
+            b.check(X.logup_fold_round_il(ctx, src_p, src_q, child_off, vector_len, sch.r[l][0], v[0], v[1], v[2],
+                                          v[3], suffix, (size_t{1} << (L - 2)) - 1, msgs, moff[l] + 4),
+                    "volta_b200_logup_fold_round_il_into_device");
+            len = half;
+            j_first = 1;
+            if (to_job) {
+                vzb_layer_job jb{};
+                for (int k = 0; k < 4; ++k) jb.v_id[k] = v[k];
+                jb.rounds = L - 1;
+                jb.point_id = pts;
+                jb.point_offset = pts_off[l] + 1;
+                jb.r_id = rbuf;
+                jb.r_offset = r_off[l] + 1;
+                jb.out_id = msgs;
+                jb.out_offset = moff[l] + 4;
+                jobs.push_back(jb);
+                continue;
+            }
+        } else {
+            for (auto& x : v) x = layer.add(b.alloc(vector_len * sizeof(Fp2)));
+            b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_p, child_off, vector_len, v[0], 0, v[1], 0),
+                    "fp2_deinterleave_device");
+            b.check(A.volta_cuda_fp2_deinterleave_device(ctx, src_q, child_off, vector_len, v[2], 0, v[3], 0),
+                    "fp2_deinterleave_device");
+            b.check(A.volta_cuda_logup_general_round_into_device(ctx, v[0], 0, v[1], 0, v[2], 0, v[3], 0, suffix,
+                                                                 (size_t{1} << (L - 1)) - 1, len / 2, msgs,
+                                                                 moff[l]),
+                    "logup_general_round_into_device");
+        }
+        for (size_t j = j_first; j < L; ++j) {
             const Fp2 rj = sch.r[l][j];
             const size_t half = len / 2;
             if (half == 1) {  // last fold: the left-over values land in their slots
