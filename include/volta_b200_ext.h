@@ -69,6 +69,27 @@ int volta_b200_logup_fold_round_il_into_device(void* ctx, uint64_t p_id, uint64_
                                                size_t suffix_offset, uint64_t out_id, size_t out_offset);
 
 /*
+ * Column commitments of row-sharded matrices (one Ligero commitment over
+ * several GPUs).  A column's BLAKE3 tree over rows = 128 * 2^k is a perfect
+ * binary tree of 1 KiB chunks, so a slab of 128 * 2^j aligned rows is one of
+ * its subtrees.
+ * hash_fp_column_cvs: per column of a rows x cols Fp slab, the non-root
+ *   chaining value of that subtree (first chunk's global index chunk_base),
+ *   32 bytes per column.
+ * merkle_from_cvs: column leaves from the `shards` subtree values per column
+ *   ([shards][cols] x 32 B, top-to-bottom slab order) merged left to right
+ *   with ROOT on the final merge, then the Merkle tree over them (layout of
+ *   volta_cuda_hash_fp_tree_device).
+ * merkle_levels: the levels above `leaves` leaves already stored at level 0.
+ */
+int volta_b200_hash_fp_column_cvs_device(void* ctx, uint64_t matrix_id, size_t matrix_offset, size_t rows,
+                                         size_t cols, uint64_t chunk_base, uint64_t out_id,
+                                         size_t out_offset_bytes);
+int volta_b200_merkle_from_cvs_device(void* ctx, uint64_t cvs_id, size_t cvs_offset_bytes, size_t shards,
+                                      size_t cols, uint64_t tree_id, size_t tree_offset_bytes);
+int volta_b200_merkle_levels_device(void* ctx, uint64_t tree_id, size_t tree_offset_bytes, size_t leaves);
+
+/*
  * Whole small sumchecks in one CTA each, with the challenges in device memory
  * (known in advance in the clear sink / private transcript).
  *

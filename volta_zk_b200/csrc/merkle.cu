@@ -119,11 +119,12 @@ __device__ __forceinline__ uint64_t column_word(const uint64_t* m, size_t cols, 
     return __ldcs(m + 2 * (row * cols + col) + (w & 1));
 }
 
-// Chaining value of chunk `chunk` of a column of `words` u64 words; with
-// `root` set (single-chunk column) the last block carries the ROOT flag.
+// Chaining value of chunk `chunk` of a column of `words` u64 words, compressed
+// with chunk counter `counter`; with `root` set (single-chunk column) the last
+// block carries the ROOT flag (and counter 0).
 template <int WPV>
 __device__ __forceinline__ H32 chunk_cv(const uint64_t* m, size_t cols, size_t col, size_t words, size_t chunk,
-                                        bool root) {
+                                        uint64_t counter, bool root) {
     const size_t w0 = chunk * 128;
     const size_t take = words - w0 < 128 ? words - w0 : 128;
     const int blocks = static_cast<int>((take + 7) / 8);
@@ -142,7 +143,7 @@ __device__ __forceinline__ H32 chunk_cv(const uint64_t* m, size_t cols, size_t c
         }
         const bool last = b + 1 == blocks;
         const uint32_t flags = (b == 0 ? kChunkStart : 0) | (last ? kChunkEnd : 0) | (last && root ? kRoot : 0);
-        h = compress(cv, blk, root ? 0 : chunk, static_cast<uint32_t>(bw * 8), flags);
+        h = compress(cv, blk, root ? 0 : counter, static_cast<uint32_t>(bw * 8), flags);
 #pragma unroll
         for (int i = 0; i < 8; ++i) cv[i] = h.w[i];
     }
@@ -160,11 +161,15 @@ __device__ __host__ __forceinline__ size_t level_offset(size_t leaves, int l) {
 }
 
 // One CTA: 32 adjacent columns.  Leaves (and, when `build` is set, the Merkle
-// levels above them up to the CTA's subtree root) go to `tree`.
+// levels above them up to the CTA's subtree root) go to `tree`.  With `root`
+// clear the result per column is the non-root chaining value of the chunk
+// subtree whose first chunk has global index chunk_base (a row slab of a
+// taller column).
 template <int WPV>
 __global__ void __launch_bounds__(kColsPerCta * kHashWarps) column_leaves_kernel(const uint64_t* m, size_t rows,
                                                                                   size_t cols, H32* tree,
-                                                                                  H32* scratch, int build) {
+                                                                                  H32* scratch, int build,
+                                                                                  uint64_t chunk_base, int root) {
     extern __shared__ H32 cvs_flat[];  // [min(chunks, 64) or 1][32] chunk CVs, then the subtree nodes
     auto cvs = [&](size_t ch, int ln) -> H32& { return cvs_flat[ch * kColsPerCta + ln]; };
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -177,7 +182,7 @@ __global__ void __launch_bounds__(kColsPerCta * kHashWarps) column_leaves_kernel
     // chunk chaining values, warps striding over the chunks
     if (lane < ncols) {
         for (size_t ch = warp; ch < chunks; ch += kHashWarps) {
-            const H32 h = chunk_cv<WPV>(m, cols, col, words, ch, chunks == 1);
+            const H32 h = chunk_cv<WPV>(m, cols, col, words, ch, chunk_base + ch, chunks == 1 && root);
             if (in_smem)
                 cvs(ch, lane) = h;
             else
@@ -196,7 +201,7 @@ __global__ void __launch_bounds__(kColsPerCta * kHashWarps) column_leaves_kernel
             H32 mine[kMaxSmemChunks / 2 / kHashWarps];
             int nm = 0;
             for (size_t p = warp; p < pairs; p += kHashWarps)
-                mine[nm++] = parent_cv(cvs(2 * p, lane), cvs(2 * p + 1, lane), count == 2 ? kRoot : 0);
+                mine[nm++] = parent_cv(cvs(2 * p, lane), cvs(2 * p + 1, lane), count == 2 && root ? kRoot : 0);
             H32 carry{};
             const bool odd = count & 1;
             if (odd && warp == 0) carry = cvs(count - 1, lane);
@@ -226,7 +231,7 @@ __global__ void __launch_bounds__(kColsPerCta * kHashWarps) column_leaves_kernel
         H32 cv = scratch[(chunks - 1) * cols + col];
         while (depth) {
             --depth;
-            cv = parent_cv(stack[depth], cv, depth == 0 ? kRoot : 0);
+            cv = parent_cv(stack[depth], cv, depth == 0 && root ? kRoot : 0);
         }
         leaf = cv;
     }
@@ -308,7 +313,8 @@ __global__ void merkle_paths_kernel(const H32* tree, const uint32_t* idx, H32* p
     }
 }
 
-int column_leaves(Context* c, const void* matrix, size_t rows, size_t cols, bool fp2, H32* tree, bool build) {
+int column_leaves(Context* c, const void* matrix, size_t rows, size_t cols, bool fp2, H32* tree, bool build,
+                  uint64_t chunk_base = 0, bool root = true) {
     const size_t words = rows * (fp2 ? 2 : 1);
     const size_t chunks = (words + 127) / 128;
     H32* scratch = nullptr;
@@ -322,20 +328,19 @@ int column_leaves(Context* c, const void* matrix, size_t rows, size_t cols, bool
     const size_t smem = smem_chunks * kColsPerCta * sizeof(H32);
     auto k = fp2 ? column_leaves_kernel<2> : column_leaves_kernel<1>;
     VZB_CUDA(c, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    k<<<blocks, kColsPerCta * kHashWarps, smem, c->stream>>>(m, rows, cols, tree, scratch, build ? 1 : 0);
+    k<<<blocks, kColsPerCta * kHashWarps, smem, c->stream>>>(m, rows, cols, tree, scratch, build ? 1 : 0,
+                                                             chunk_base, root ? 1 : 0);
     VZB_LAUNCHED(c);
     return 0;
 }
 
-int hash_tree(Context* c, const void* matrix, size_t rows, size_t cols, bool fp2, H32* tree) {
-    if (column_leaves(c, matrix, rows, cols, fp2, tree, true)) return -1;
-    if (cols <= kColsPerCta) return 0;
-    // subtree roots of the column CTAs sit at level log2(32) = 5
-    int level = 5;
-    size_t len = cols >> level;
+// Merkle levels above `level` (whose nodes are already in `tree`).
+int merkle_up(Context* c, H32* tree, size_t leaves, int level) {
+    size_t len = leaves >> level;
+    if (len <= 1) return 0;
     constexpr size_t kTopNodes = 2048;  // 64 KiB of shared memory
     while (len > kTopNodes) {
-        const size_t off = level_offset(cols, level);
+        const size_t off = level_offset(leaves, level);
         merkle_level_kernel<<<grid_for(c, len / 2, 256), 256, 0, c->stream>>>(tree + off, tree + off + len, len / 2);
         VZB_LAUNCHED(c);
         len /= 2;
@@ -344,9 +349,33 @@ int hash_tree(Context* c, const void* matrix, size_t rows, size_t cols, bool fp2
     const size_t smem = len * sizeof(H32);
     VZB_CUDA(c, cudaFuncSetAttribute(merkle_top_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
-    merkle_top_kernel<<<1, 1024, smem, c->stream>>>(tree, cols, level);
+    merkle_top_kernel<<<1, 1024, smem, c->stream>>>(tree, leaves, level);
     VZB_LAUNCHED(c);
     return 0;
+}
+
+int hash_tree(Context* c, const void* matrix, size_t rows, size_t cols, bool fp2, H32* tree) {
+    if (column_leaves(c, matrix, rows, cols, fp2, tree, true)) return -1;
+    if (cols <= kColsPerCta) return 0;
+    // subtree roots of the column CTAs sit at level log2(32) = 5
+    return merkle_up(c, tree, cols, 5);
+}
+
+// Column leaves from `shards` subtree chaining values per column
+// (in[g * cols + col]), merged pairwise left to right with ROOT on the final
+// merge: the BLAKE3 tree of a column whose chunk tree splits into `shards`
+// aligned complete subtrees.
+constexpr int kMaxCvShards = 64;
+
+__global__ void cvs_merge_kernel(const H32* in, int shards, size_t cols, H32* leaves) {
+    for (size_t col = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; col < cols;
+         col += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        H32 cv[kMaxCvShards];
+        for (int g = 0; g < shards; ++g) cv[g] = in[static_cast<size_t>(g) * cols + col];
+        for (int n = shards; n > 1; n >>= 1)
+            for (int i = 0; i < n / 2; ++i) cv[i] = parent_cv(cv[2 * i], cv[2 * i + 1], n == 2 ? kRoot : 0);
+        leaves[col] = cv[0];
+    }
 }
 
 bool pow2(size_t n) { return n && !(n & (n - 1)); }
@@ -416,6 +445,60 @@ extern "C" int volta_cuda_merkle_paths_device(void* raw, uint64_t tree_id, size_
         static_cast<const H32*>(tree), static_cast<const uint32_t*>(idx), static_cast<H32*>(paths), leaves, queries,
         bits);
     VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsMerkle, 0, 0);
+}
+
+// ===========================================================================
+// Extensions: column trees of row-sharded matrices
+// ===========================================================================
+
+extern "C" int volta_b200_hash_fp_column_cvs_device(void* raw, uint64_t matrix_id, size_t matrix_offset, size_t rows,
+                                                    size_t cols, uint64_t chunk_base, uint64_t out_id,
+                                                    size_t out_offset_bytes) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !cols || !rows || rows % 128 || !pow2(rows / 128))
+        return fail_message(c, "column chaining values need rows = 128 * 2^k");
+    void *matrix = nullptr, *out = nullptr;
+    if (region_elems(c, matrix_id, matrix_offset, rows * cols, sizeof(uint64_t), &matrix) ||
+        region(c, out_id, out_offset_bytes, cols * sizeof(H32), &out))
+        return -1;
+    if (reinterpret_cast<uintptr_t>(out) % alignof(H32)) return fail_message(c, "chaining-value output is not 4-byte aligned");
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (column_leaves(c, matrix, rows, cols, false, static_cast<H32*>(out), false, chunk_base, false)) return -1;
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsMerkle, 0, 0);
+}
+
+extern "C" int volta_b200_merkle_from_cvs_device(void* raw, uint64_t cvs_id, size_t cvs_offset_bytes, size_t shards,
+                                                 size_t cols, uint64_t tree_id, size_t tree_offset_bytes) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || shards < 2 || shards > static_cast<size_t>(kMaxCvShards) || !pow2(shards) || !pow2(cols))
+        return fail_message(c, "invalid sharded column-tree geometry");
+    void *in = nullptr, *tree = nullptr;
+    if (region(c, cvs_id, cvs_offset_bytes, shards * cols * sizeof(H32), &in) ||
+        region(c, tree_id, tree_offset_bytes, (2 * cols - 1) * sizeof(H32), &tree))
+        return -1;
+    if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(tree)) % alignof(H32))
+        return fail_message(c, "Merkle buffers are not 4-byte aligned");
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    cvs_merge_kernel<<<grid_for(c, cols, 128), 128, 0, c->stream>>>(static_cast<const H32*>(in),
+                                                                    static_cast<int>(shards), cols,
+                                                                    static_cast<H32*>(tree));
+    VZB_LAUNCHED(c);
+    if (merkle_up(c, static_cast<H32*>(tree), cols, 0)) return -1;
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsMerkle, 0, 0);
+}
+
+extern "C" int volta_b200_merkle_levels_device(void* raw, uint64_t tree_id, size_t tree_offset_bytes, size_t leaves) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pow2(leaves)) return fail_message(c, "invalid Merkle level geometry");
+    void* tree = nullptr;
+    if (region(c, tree_id, tree_offset_bytes, (2 * leaves - 1) * sizeof(H32), &tree)) return -1;
+    if (reinterpret_cast<uintptr_t>(tree) % alignof(H32)) return fail_message(c, "Merkle tree is not 4-byte aligned");
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (merkle_up(c, static_cast<H32*>(tree), leaves, 0)) return -1;
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpPcsMerkle, 0, 0);
 }

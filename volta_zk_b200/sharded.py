@@ -114,3 +114,154 @@ class ShardedProver:
         local = self.prover.logup_local(f_col, n_f // self.world, t_col, n_t // self.world, mult, self.s, seed,
                                         domain)
         return logup_finish(self.gather(local), n_f, n_t, seed, domain)
+
+
+# ---------------------------------------------------------------------------
+# Ligero commitment over G GPUs (rust/volta-pcs/src/ligero.rs:465-505 commit,
+# 1440-1480 openings).  Shard g encodes rows [g R/G, (g+1) R/G): its ChaCha8
+# message rows, zero padding and row NTTs are local.  A column's BLAKE3 tree
+# over R = 128 * 2^k rows is a perfect tree of 1 KiB chunks, so shard g's rows
+# are one aligned subtree of it: the shard hashes each column's subtree to a
+# 32-byte chaining value, and one all-to-all hands shard s the values of its
+# slab of code_len / G columns.  Shard s merges them into its column leaves,
+# builds the Merkle subtree of its slab and all-gathers its slab root; the
+# top log2 G levels are hashed on one device from the G roots.  Openings: each
+# shard gathers its rows of the queried columns and the paths inside its slab.
+# ---------------------------------------------------------------------------
+
+H = 32  # bytes per hash
+
+
+def ligero_shard_encode(be, row_seed: bytes, row0: int, rows_local: int, msg_len: int, code_len: int):
+    """Phase 1 (per shard): resident codeword rows and their column chaining
+    values (numpy [code_len, 32] uint8)."""
+    msgs = be.alloc(8 * rows_local * msg_len)
+    be.call("chacha8_prover_secret_fp_rows_device", msgs, 0, row_seed, row0, rows_local, msg_len)
+    code = be.alloc(8 * rows_local * code_len)
+    if msg_len < code_len:
+        be.call("resident_zero", code, 0, 8 * rows_local * code_len)
+    be.call("resident_copy_rows", msgs, 0, 8 * msg_len, code, 0, 8 * code_len, rows_local, 8 * msg_len)
+    be.free(msgs)
+    be.call("ntt_fp_batch_device", code, 0, rows_local, code_len, code, 0)
+    cvs = be.alloc(H * code_len)
+    be.check(be.lib.volta_b200_hash_fp_column_cvs_device(be.ctx, code, 0, rows_local, code_len, row0 // 128, cvs, 0),
+             "hash_fp_column_cvs_device")
+    host = be.download(cvs, H * code_len, dtype=np.uint8).reshape(code_len, H)
+    be.free(cvs)
+    return code, host
+
+
+def ligero_shard_tree(be, recv: np.ndarray, shards: int, slab: int):
+    """Phase 2 (per shard): the Merkle tree of this shard's column slab from
+    the received chaining values ([shards, slab, 32]); returns (tree id, slab
+    root bytes)."""
+    buf = be.upload_new(np.ascontiguousarray(recv, dtype=np.uint8))
+    tree = be.alloc(H * (2 * slab - 1))
+    be.check(be.lib.volta_b200_merkle_from_cvs_device(be.ctx, buf, 0, shards, slab, tree, 0), "merkle_from_cvs_device")
+    be.free(buf)
+    root = be.download(tree, H, dtype=np.uint8, offset_bytes=H * (2 * slab - 2))
+    return tree, root
+
+
+def ligero_top_tree(be, roots: np.ndarray) -> np.ndarray:
+    """The Merkle levels above the G slab roots ([G, 32]): full top tree
+    [(2G - 1), 32], global root last."""
+    G = roots.shape[0]
+    tree = be.alloc(H * (2 * G - 1))
+    be.upload(tree, np.ascontiguousarray(roots, dtype=np.uint8))
+    be.check(be.lib.volta_b200_merkle_levels_device(be.ctx, tree, 0, G), "merkle_levels_device")
+    out = be.download(tree, H * (2 * G - 1), dtype=np.uint8).reshape(2 * G - 1, H)
+    be.free(tree)
+    return out
+
+
+def ligero_shard_open(be, code: int, rows_local: int, code_len: int, tree: int, slab: int, shard: int,
+                      idx: np.ndarray):
+    """Phase 3 (per shard): this shard's rows of the queried columns
+    ([q, rows_local]) and, for the queries inside its slab, their paths up to
+    the slab root ([q, log2 slab, 32]; zeros for other queries)."""
+    q = idx.size
+    ids = be.upload_new(idx.astype(np.uint32))
+    cols = be.alloc(8 * q * rows_local)
+    be.call("pcs_gather_columns_device", code, 0, rows_local, code_len, ids, 0, q, cols, 0, 0)
+    columns = be.download(cols, 8 * q * rows_local).reshape(q, rows_local)
+    bits = slab.bit_length() - 1
+    local = np.where(idx // slab == shard, idx % slab, slab).astype(np.uint32)  # out of range -> zero path
+    paths = np.zeros((q, bits, H), dtype=np.uint8)
+    if bits:
+        lid = be.upload_new(local)
+        pid = be.alloc(H * q * bits)
+        be.call("merkle_paths_device", tree, 0, slab, lid, 0, q, pid, 0)
+        paths = be.download(pid, H * q * bits, dtype=np.uint8).reshape(q, bits, H)
+        be.free(lid)
+        be.free(pid)
+    be.free(ids)
+    be.free(cols)
+    return columns, paths
+
+
+def ligero_assemble(parts_cols, parts_paths, top: np.ndarray, idx: np.ndarray, slab: int):
+    """Openings from every shard's phase-3 output and the top tree: columns
+    [q, R] (rows in shard order) and full paths [q, log2 code_len, 32]."""
+    G = len(parts_cols)
+    columns = np.concatenate(parts_cols, axis=1)
+    owner = idx // slab
+    local = np.stack([parts_paths[int(o)][k] for k, o in enumerate(owner)])
+    top_bits = G.bit_length() - 1
+    top_paths = np.zeros((idx.size, top_bits, H), dtype=np.uint8)
+    for k, o in enumerate(owner):
+        node, off, width = int(o), 0, G
+        for lv in range(top_bits):
+            top_paths[k, lv] = top[off + (node ^ 1)]
+            off += width
+            width //= 2
+            node >>= 1
+    return columns, np.concatenate([local, top_paths], axis=1)
+
+
+def ligero_query_indices(chal_seed: bytes, queries: int, code_len: int) -> np.ndarray:
+    """challenge_fp2().c0 mod code_len from FpStream(seed, u64::MAX) (ligero.rs:1444)."""
+    from .accel import fpstream_fp2
+
+    return (fpstream_fp2(chal_seed, 2**64 - 1, queries)[:, 0] % np.uint64(code_len)).astype(np.uint32)
+
+
+def torch_all_to_all(device=None):
+    """All-to-all of uint8 arrays [G, ...]: block s goes to rank s; returns
+    the blocks received from every rank, in rank order."""
+    import torch
+    import torch.distributed as dist
+
+    def exchange(x: np.ndarray) -> np.ndarray:
+        t = torch.from_numpy(np.ascontiguousarray(x).reshape(-1))
+        if device is not None:
+            t = t.to(device)
+        out = torch.empty_like(t)
+        dist.all_to_all_single(out, t)
+        return out.cpu().numpy().reshape(x.shape)
+
+    return exchange
+
+
+def ligero_commit_open_sharded(be, rank: int, world: int, all_gather: AllGather, all_to_all, row_seed: bytes,
+                               rows: int, msg_len: int, code_len: int, queries: int, chal_seed: bytes):
+    """One Ligero commitment + openings over `world` GPUs; every rank returns
+    (root bytes, indices, columns [q, rows], paths [q, log2 code_len, 32]),
+    equal to the one-GPU result."""
+    if rows % (128 * world) or (rows // 128) & (rows // 128 - 1) or code_len % world:
+        raise ValueError("sharded Ligero needs rows = 128 * 2^k divisible by 128 * world")
+    rl, slab = rows // world, code_len // world
+    code, cvs = ligero_shard_encode(be, row_seed, rank * rl, rl, msg_len, code_len)
+    recv = all_to_all(cvs.reshape(world, slab, H))
+    tree, root = ligero_shard_tree(be, recv, world, slab)
+    roots = np.stack(all_gather(np.frombuffer(root.tobytes(), dtype=np.uint64).copy()))
+    top = ligero_top_tree(be, roots.view(np.uint8).reshape(world, H))
+    idx = ligero_query_indices(chal_seed, queries, code_len)
+    cols, paths = ligero_shard_open(be, code, rl, code_len, tree, slab, rank, idx)
+    all_cols = all_gather(cols)
+    all_paths = [p.view(np.uint8).reshape(paths.shape)
+                 for p in all_gather(np.ascontiguousarray(paths).view(np.uint64))]
+    be.free(code)
+    be.free(tree)
+    columns, full_paths = ligero_assemble(all_cols, all_paths, top, idx, slab)
+    return top[-1].tobytes(), idx, columns, full_paths
