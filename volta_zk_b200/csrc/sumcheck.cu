@@ -663,7 +663,7 @@ int triple_round(Context* c, uint64_t a_id, size_t a_off, uint64_t b_id, size_t 
     }
     const MsgOut o = msg_out(c, dev, host, 3);
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    if (launch_reduce_wide<3>(c, TripleEval{a, b, cc}, pairs, store_epi<3>(o))) return -1;
+    if (launch_reduce_wide<3>(c, TripleEval{a, b, cc}, pairs, store_epi<3>(o), 8)) return -1;
     return finish_msg(c, kOpGemm, o);
 }
 
@@ -1322,7 +1322,7 @@ static int triple_fold_round(Context* c, uint64_t a_id, uint64_t b_id, uint64_t 
     if (op_begin(c) || op_mark(c, 1)) return -1;
     TripleFoldEval ev{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b), static_cast<const Fp2*>(cc),
                       static_cast<Fp2*>(ao), static_cast<Fp2*>(bo), static_cast<Fp2*>(co), r};
-    if (launch_reduce_wide<3>(c, ev, len / 4, store_epi<3>(o))) return -1;
+    if (launch_reduce_wide<3>(c, ev, len / 4, store_epi<3>(o), 8)) return -1;
     return finish_msg(c, kOpGemm, o);
 }
 
