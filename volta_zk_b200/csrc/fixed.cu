@@ -238,7 +238,7 @@ struct FixedGemmEpi {
     uint32_t* error;
     size_t n;
     uint32_t shift;
-    __device__ __forceinline__ bool active(size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ bool active(size_t, size_t, size_t, size_t) const { return true; }
     __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t acc) const {
         if (bias) acc += static_cast<int64_t>(bias[j]) << shift;
         const size_t z = i * n + j;
@@ -262,7 +262,10 @@ struct ScoresEpi {
     uint32_t* error;
     size_t rows, pos0, per_head;
     uint32_t shift;
-    __device__ __forceinline__ bool active(size_t, size_t m0, size_t n0) const { return n0 <= pos0 + m0 + kGemmBM - 1; }
+    // tiles entirely above the causal diagonal produce nothing
+    __device__ __forceinline__ bool active(size_t, size_t m0, size_t n0, size_t tile_rows) const {
+        return n0 <= pos0 + m0 + tile_rows - 1;
+    }
     __device__ __forceinline__ void operator()(size_t h, size_t i, size_t j, int64_t acc) const {
         if (j > pos0 + i) return;
         const size_t p = h * per_head + packed_prefix(i, pos0) + j;
@@ -280,7 +283,7 @@ struct AvEpi {
     uint32_t* error;
     size_t d, head_dim;
     uint32_t shift;
-    __device__ __forceinline__ bool active(size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ bool active(size_t, size_t, size_t, size_t) const { return true; }
     __device__ __forceinline__ void operator()(size_t h, size_t i, size_t j, int64_t acc) const {
         const size_t z = i * d + h * head_dim + j;
         accs[z] = acc;
@@ -293,23 +296,37 @@ struct AvEpi {
 struct LogitsEpi {
     int64_t* out;
     size_t vocab;
-    __device__ __forceinline__ bool active(size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ bool active(size_t, size_t, size_t, size_t) const { return true; }
     __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t v) const { out[i * vocab + j] = v; }
 };
 
-// Byte planes of the packed causal attention weights as dense rows
-// [heads][rows][kp] (zero beyond each row's width pos0 + row + 1).
+// Byte planes of the packed causal attention weights as dense rows (rpad per
+// head, zero beyond each row's width pos0 + row + 1 and beyond `rows`); one
+// thread per 16-byte chunk of the planes.
 __global__ void causal_planes_kernel(const int16_t* w, size_t rows, size_t pos0, size_t heads, size_t kp,
-                                     int8_t* hi, uint8_t* lo) {
+                                     size_t rpad, int8_t* hi, uint8_t* lo) {
     const size_t per_head = rows * pos0 + rows * (rows + 1) / 2;
-    const size_t total = heads * rows * kp;
+    const size_t per = rpad * kp / 16, total = heads * per;
     for (size_t z = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; z < total;
          z += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const size_t h = z / (rows * kp), rem = z - h * rows * kp;
-        const size_t i = rem / kp, j = rem - i * kp;
-        const int v = j < pos0 + i + 1 ? w[h * per_head + packed_prefix(i, pos0) + j] : 0;
-        hi[z] = static_cast<int8_t>(v >> 8);
-        lo[z] = static_cast<uint8_t>(v & 0xFF);
+        const size_t h = z / per, q = z - h * per;
+        const size_t slice = q / (rpad * 4), rem = q - slice * rpad * 4;
+        const size_t i = (rem >> 5) * 8 + (rem & 7), j0 = slice * 64 + ((rem >> 3) & 3) * 16;
+        uint32_t hv[4] = {0, 0, 0, 0}, lv[4] = {0, 0, 0, 0};
+        if (i < rows) {
+            const int16_t* src = w + h * per_head + packed_prefix(i, pos0);
+            const size_t width = pos0 + i + 1;
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+                const size_t j = j0 + t;
+                const uint32_t v = j < width ? static_cast<uint16_t>(src[j]) : 0u;
+                hv[t >> 2] |= (v >> 8) << (8 * (t & 3));
+                lv[t >> 2] |= (v & 0xFFu) << (8 * (t & 3));
+            }
+        }
+        const size_t off = h * rpad * kp + q * 16;
+        *reinterpret_cast<uint4*>(hi + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(lo + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
     }
 }
 
@@ -515,14 +532,16 @@ extern "C" int volta_cuda_fixed_av_device(void* raw, uint64_t weights_id, size_t
     // per head: dense causal weights (rows x width) times V_h (width x head_dim, stride d)
     const size_t width = pos0 + rows;
     const size_t kp = (width + kGemmBK - 1) / kGemmBK * kGemmBK;
+    const size_t mpad = plane_rows(rows);
     GemmPlanes g;
     if (gemm_prepare_b(c, values, width, head_dim, d, false, kp, static_cast<unsigned>(heads), head_dim,
-                       heads * rows * kp, &g))
+                       heads * mpad * kp, &g))
         return -1;
     g.m = rows;
-    g.a_batch = rows * kp;
-    causal_planes_kernel<<<grid_for(c, heads * rows * kp, 256), 256, 0, c->stream>>>(
-        w, rows, pos0, heads, kp, const_cast<int8_t*>(g.a_hi), const_cast<uint8_t*>(g.a_lo));
+    g.mpad = mpad;
+    g.a_batch = mpad * kp;
+    causal_planes_kernel<<<grid_for(c, heads * mpad * kp / 16, 256), 256, 0, c->stream>>>(
+        w, rows, pos0, heads, kp, mpad, const_cast<int8_t*>(g.a_hi), const_cast<uint8_t*>(g.a_lo));
     VZB_LAUNCHED(c);
     if (gemm_launch(c, g, AvEpi{acc, out, err, d, head_dim, shift})) return -1;
     if (op_mark(c, 2)) return -1;

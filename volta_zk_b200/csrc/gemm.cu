@@ -7,29 +7,44 @@
 
 namespace vzb {
 
+// One thread per 16-byte core-matrix row of the output planes (consecutive
+// threads write consecutive 16-byte chunks).
 __global__ void split_planes_kernel(const int16_t* x, size_t rows, size_t k, size_t ld, int8_t* hi, uint8_t* lo,
-                                    size_t kp, unsigned batches, size_t boff) {
-    const size_t per = rows * kp, total = per * batches;
+                                    size_t kp, size_t rpad, unsigned batches, size_t boff) {
+    const size_t per = rpad * kp / 16, total = per * batches;
     for (size_t z = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; z < total;
          z += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const size_t b = z / per, rem = z - b * per;
-        const size_t r = rem / kp, c = rem - r * kp;
-        const int v = c < k ? x[b * boff + r * ld + c] : 0;
-        hi[z] = static_cast<int8_t>(v >> 8);
-        lo[z] = static_cast<uint8_t>(v & 0xFF);
+        const size_t b = z / per, q = z - b * per;
+        // q -> (k-slice, row group, 16-byte chunk, row in group), the order of plane_off
+        const size_t slice = q / (rpad * 4), rem = q - slice * rpad * 4;
+        const size_t r = (rem >> 5) * 8 + (rem & 7), k0 = slice * 64 + ((rem >> 3) & 3) * 16;
+        uint32_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
+        if (r < rows) {
+            const int16_t* src = x + b * boff + r * ld;
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+                const size_t kk = k0 + t;
+                const uint32_t v = kk < k ? static_cast<uint16_t>(src[kk]) : 0u;
+                h[t >> 2] |= (v >> 8) << (8 * (t & 3));
+                l[t >> 2] |= (v & 0xFFu) << (8 * (t & 3));
+            }
+        }
+        const size_t off = b * rpad * kp + q * 16;
+        *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
     }
 }
 
-// 32 x 32 tiles through shared memory: coalesced reads of x rows and
-// coalesced writes of plane rows; blockIdx.z is the batch.
+// 32 x 32 tiles through shared memory: coalesced reads of x rows; blockIdx.z
+// is the batch; rows n..npad of the planes are written as zeros.
 __global__ void split_planes_t_kernel(const int16_t* x, size_t k, size_t n, size_t ld, int8_t* hi, uint8_t* lo,
-                                      size_t kp, size_t boff) {
+                                      size_t kp, size_t npad, size_t boff) {
     __shared__ int16_t t[32][33];
     const size_t k0 = static_cast<size_t>(blockIdx.x) * 32, n0 = static_cast<size_t>(blockIdx.y) * 32;
     const size_t b = blockIdx.z;
     x += b * boff;
-    hi += b * n * kp;
-    lo += b * n * kp;
+    hi += b * npad * kp;
+    lo += b * npad * kp;
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
         const size_t kk = k0 + r, nn = n0 + threadIdx.x;
         t[r][threadIdx.x] = (kk < k && nn < n) ? x[kk * ld + nn] : 0;
@@ -37,17 +52,19 @@ __global__ void split_planes_t_kernel(const int16_t* x, size_t k, size_t n, size
     __syncthreads();
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
         const size_t nn = n0 + r, kk = k0 + threadIdx.x;
-        if (nn < n && kk < kp) {
+        if (nn < npad && kk < kp) {
             const int v = t[threadIdx.x][r];
-            hi[nn * kp + kk] = static_cast<int8_t>(v >> 8);
-            lo[nn * kp + kk] = static_cast<uint8_t>(v & 0xFF);
+            const size_t o = plane_off(nn, kk, npad);
+            hi[o] = static_cast<int8_t>(v >> 8);
+            lo[o] = static_cast<uint8_t>(v & 0xFF);
         }
     }
 }
 
 int gemm_prepare_b(Context* c, const int16_t* b, size_t k, size_t n, size_t ldb, bool b_nk, size_t kp,
                    unsigned batches, size_t b_boff, size_t a_bytes, GemmPlanes* out) {
-    const size_t bbytes = n * kp * batches;
+    const size_t npad = plane_rows(n);
+    const size_t bbytes = npad * kp * batches;
     if (ensure_ws(c, kWsGemm, 2 * a_bytes + 2 * bbytes + 64)) return -1;
     unsigned char* w = ws<unsigned char>(c, kWsGemm);
     out->a_hi = reinterpret_cast<int8_t*>(w);
@@ -55,17 +72,18 @@ int gemm_prepare_b(Context* c, const int16_t* b, size_t k, size_t n, size_t ldb,
     out->b_hi = reinterpret_cast<int8_t*>(w + 2 * a_bytes);
     out->b_lo = w + 2 * a_bytes + bbytes;
     out->n = n;
+    out->npad = npad;
     out->kp = kp;
     out->batches = batches;
-    out->b_batch = n * kp;
+    out->b_batch = npad * kp;
     if (b_nk) {
-        split_planes_kernel<<<grid_for(c, bbytes, 256), 256, 0, c->stream>>>(
-            b, n, k, ldb, const_cast<int8_t*>(out->b_hi), const_cast<uint8_t*>(out->b_lo), kp, batches, b_boff);
+        split_planes_kernel<<<grid_for(c, bbytes / 16, 256), 256, 0, c->stream>>>(
+            b, n, k, ldb, const_cast<int8_t*>(out->b_hi), const_cast<uint8_t*>(out->b_lo), kp, npad, batches, b_boff);
     } else {
-        const dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((n + 31) / 32), batches);
+        const dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>(npad / 32), batches);
         if (grid.y > 65535 || grid.z > 65535) return fail_message(c, "GEMM column count exceeds the launch grid");
         split_planes_t_kernel<<<grid, dim3(32, 8), 0, c->stream>>>(b, k, n, ldb, const_cast<int8_t*>(out->b_hi),
-                                                                   const_cast<uint8_t*>(out->b_lo), kp, b_boff);
+                                                                   const_cast<uint8_t*>(out->b_lo), kp, npad, b_boff);
     }
     VZB_LAUNCHED(c);
     return 0;
@@ -74,12 +92,14 @@ int gemm_prepare_b(Context* c, const int16_t* b, size_t k, size_t n, size_t ldb,
 int gemm_prepare(Context* c, const int16_t* a, size_t m, size_t k, size_t lda, const int16_t* b, size_t n,
                  size_t ldb, bool b_nk, GemmPlanes* out, unsigned batches, size_t a_boff, size_t b_boff) {
     const size_t kp = (k + kGemmBK - 1) / kGemmBK * kGemmBK;
-    const size_t abytes = m * kp * batches;
+    const size_t mpad = plane_rows(m);
+    const size_t abytes = mpad * kp * batches;
     if (gemm_prepare_b(c, b, k, n, ldb, b_nk, kp, batches, b_boff, abytes, out)) return -1;
     out->m = m;
-    out->a_batch = m * kp;
-    split_planes_kernel<<<grid_for(c, abytes, 256), 256, 0, c->stream>>>(
-        a, m, k, lda, const_cast<int8_t*>(out->a_hi), const_cast<uint8_t*>(out->a_lo), kp, batches, a_boff);
+    out->mpad = mpad;
+    out->a_batch = mpad * kp;
+    split_planes_kernel<<<grid_for(c, abytes / 16, 256), 256, 0, c->stream>>>(
+        a, m, k, lda, const_cast<int8_t*>(out->a_hi), const_cast<uint8_t*>(out->a_lo), kp, mpad, batches, a_boff);
     VZB_LAUNCHED(c);
     return 0;
 }
@@ -89,7 +109,7 @@ namespace {
 struct I64Epi {
     int64_t* out;
     size_t ldo;
-    __device__ __forceinline__ bool active(size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ bool active(size_t, size_t, size_t, size_t) const { return true; }
     __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t v) const { out[i * ldo + j] = v; }
 };
 
@@ -104,7 +124,7 @@ struct RequantAuthEpi {
     uint64_t* corr;
     size_t n;
     uint32_t shift;
-    __device__ __forceinline__ bool active(size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ bool active(size_t, size_t, size_t, size_t) const { return true; }
     __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t v) const {
         const size_t z = i * n + j;
         const int16_t y = requant_clamped(v, shift);

@@ -10,10 +10,21 @@
 // reference's scalar i64 loop (cuda/volta_cuda_backend.cu:1412-1440,
 // rust/volta-gpt2/src/gemm.rs:40-60) bit for bit.
 //
-// Layout: the operands are first split into byte planes, A as [m][Kp] and B
-// as [n][Kp] (k contiguous, zero-padded to Kp = 64-multiple), then a CTA
-// computes a 64 x 64 tile with 4 warps (32 x 32 each) from a 2-stage cp.async
-// pipeline of 64-byte k slices (rows padded to 80 B: conflict-free ldmatrix).
+// Layout: the operands are first split into byte planes, A with m rows and B
+// with n rows, each row holding its k bytes zero-padded to Kp (a multiple of
+// 64) and the row count padded to a multiple of 128.  A plane is stored as
+// Kp / 64 k-slices; inside a slice, rows come in groups of 8 and each group
+// holds four 8 x 16-byte core matrices (see plane_off).  A 128-row slab of one
+// k-slice is therefore one contiguous 8 KiB block that a single bulk copy
+// moves into shared memory already in the tensor core's canonical K-major
+// layout.
+//
+// gemm_tc_kernel (K <= 16384) computes a 128 x 64 tile per CTA on the 5th
+// generation tensor cores: one lane streams the tiles with cp.async.bulk into
+// a 4-stage mbarrier ring, one lane issues tcgen05.mma kind::i8 into three
+// int32 accumulators in tensor memory, and all four warps run the epilogue
+// from tensor memory.  gemm_planes_kernel (longer K) is the mma.sync form
+// with 64 x 64 tiles, which flushes int32 partials into int64 registers.
 #pragma once
 
 #include "runtime.cuh"
@@ -24,15 +35,23 @@ constexpr int kGemmBM = 64, kGemmBN = 64, kGemmBK = 64;
 constexpr int kGemmRow = kGemmBK + 16;  // shared-memory row pitch in bytes
 constexpr int kGemmThreads = 128;
 constexpr size_t kGemmChunkK = 16384;   // int32 partials stay exact below this
+constexpr size_t kPlaneRowAlign = 128;  // plane row counts are padded to this
+
+// Byte offset of element (r, k) in a plane of `rpad` rows.
+__host__ __device__ __forceinline__ size_t plane_off(size_t r, size_t k, size_t rpad) {
+    return (k >> 6) * (rpad << 6) + ((r >> 3) << 9) + (((k & 63) >> 4) << 7) + ((r & 7) << 4) + (k & 15);
+}
+inline size_t plane_rows(size_t rows) { return (rows + kPlaneRowAlign - 1) / kPlaneRowAlign * kPlaneRowAlign; }
 
 // Byte planes of `batches` independent products (batch z at z * a_batch /
-// z * b_batch bytes into each plane).
+// z * b_batch bytes into each plane; a_batch = mpad * kp, b_batch = npad * kp).
 struct GemmPlanes {
     const int8_t* a_hi;
     const uint8_t* a_lo;
     const int8_t* b_hi;
     const uint8_t* b_lo;
     size_t m, n, kp;
+    size_t mpad = 0, npad = 0;  // plane row counts (multiples of kPlaneRowAlign)
     size_t a_batch = 0, b_batch = 0;
     unsigned batches = 1;
 };
@@ -59,7 +78,8 @@ __device__ __forceinline__ void ldsm_x4(const void* smem, uint32_t& r0, uint32_t
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]))
 
 // epi(z, i, j, acc) is called once per output element of batch z inside
-// [0,m) x [0,n); tiles for which epi.active(z, m0, n0) is false are skipped.
+// [0,m) x [0,n); tiles for which epi.active(z, m0, n0, tile_rows) is false
+// are skipped.
 template <class Epi, bool kLongK>
 __global__ void __launch_bounds__(kGemmThreads) gemm_planes_kernel(GemmPlanes g, Epi epi) {
     __shared__ __align__(16) unsigned char sm[2][4][kGemmBM][kGemmRow];  // stage, plane, row, k bytes
@@ -67,7 +87,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_planes_kernel(GemmPlanes g,
     const int wm = warp >> 1, wn = warp & 1;
     const size_t m0 = static_cast<size_t>(blockIdx.y) * kGemmBM, n0 = static_cast<size_t>(blockIdx.x) * kGemmBN;
     const size_t bz = blockIdx.z;
-    if (!epi.active(bz, m0, n0)) return;
+    if (!epi.active(bz, m0, n0, kGemmBM)) return;
     g.a_hi += bz * g.a_batch;
     g.a_lo += bz * g.a_batch;
     g.b_hi += bz * g.b_batch;
@@ -88,7 +108,8 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_planes_kernel(GemmPlanes g,
                                : plane == 1 ? static_cast<const void*>(g.a_lo)
                                : plane == 2 ? static_cast<const void*>(g.b_hi)
                                             : static_cast<const void*>(g.b_lo);
-            const unsigned char* src = static_cast<const unsigned char*>(base) + rr * g.kp + k0 + c * 16;
+            const unsigned char* src =
+                static_cast<const unsigned char*>(base) + plane_off(rr, k0 + c * 16, is_a ? g.mpad : g.npad);
             cp_async16(&sm[stage][plane][r][c * 16], src, valid);
         }
         asm volatile("cp.async.commit_group;\n" ::);
@@ -191,15 +212,233 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_planes_kernel(GemmPlanes g,
 }
 #undef VZB_MMA_I8
 
+// ---- tcgen05 form -----------------------------------------------------------
+
+constexpr int kTcBM = 128, kTcBN = 64, kTcStages = 4, kTcThreads = 128;
+constexpr uint32_t kTcTileA = kTcBM * kGemmBK;                    // one A plane tile (8 KiB)
+constexpr uint32_t kTcTileB = kTcBN * kGemmBK;                    // one B plane tile (4 KiB)
+constexpr uint32_t kTcStageBytes = 2 * kTcTileA + 2 * kTcTileB;   // hi + lo of A and B
+constexpr size_t kTcSmem = static_cast<size_t>(kTcStages) * kTcStageBytes;
+constexpr uint32_t kTcTmemCols = 256;                             // 3 x 64 int32 columns used
+constexpr unsigned long long kTcWaitNs = 2000000000ull;           // bound of every pipeline wait
+constexpr int kTcPitch = 17;                                      // epilogue transpose row pitch (int64)
+static_assert(kTcThreads / 32 * 32 * kTcPitch * 8 <= kTcSmem, "epilogue transpose fits the stage ring");
+
+__device__ __forceinline__ uint32_t tc_smem(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long tc_clock() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait for the completion of phase `parity` of an mbarrier.
+__device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity) {
+    const unsigned long long t0 = tc_clock();
+    for (;;) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (tc_clock() - t0 > kTcWaitNs) return false;
+    }
+}
+
+// Shared-memory matrix descriptor, no swizzle (version 1 = tcgen05): start,
+// leading-dimension (K direction) and stride-dimension (M/N direction) byte
+// offsets between 8 x 16-byte core matrices.
+__device__ __forceinline__ uint64_t tc_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return static_cast<uint64_t>((addr >> 4) & 0x3FFF) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32) | (uint64_t{1} << 46);
+}
+
+// Instruction descriptor of kind::i8 with s32 accumulation, both operands
+// K-major, M = kTcBM, N = kTcBN; the flags select signed (1) or unsigned (0)
+// bytes.
+__host__ __device__ constexpr uint32_t tc_idesc(uint32_t a_signed, uint32_t b_signed) {
+    return (2u << 4) | (a_signed << 7) | (b_signed << 10) | (static_cast<uint32_t>(kTcBN >> 3) << 17) |
+           (static_cast<uint32_t>(kTcBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+// One 128 x 64 output tile of batch blockIdx.z.  Requires g.kp <= kGemmChunkK
+// (int32 accumulators stay exact).  A pipeline wait that runs out of time
+// records 1 in *fault, skips the epilogue and releases tensor memory.
+template <class Epi>
+__global__ void __launch_bounds__(kTcThreads) gemm_tc_kernel(GemmPlanes g, Epi epi, unsigned* fault) {
+    extern __shared__ __align__(128) unsigned char tc_ring[];
+    __shared__ __align__(8) uint64_t full_bar[kTcStages], empty_bar[kTcStages], done_bar;
+    __shared__ uint32_t tmem_base;
+    __shared__ int failed;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t m0 = static_cast<size_t>(blockIdx.y) * kTcBM, n0 = static_cast<size_t>(blockIdx.x) * kTcBN;
+    const size_t bz = blockIdx.z;
+    if (!epi.active(bz, m0, n0, kTcBM)) return;
+    const size_t ktiles = g.kp / kGemmBK;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(tc_smem(&tmem_base)),
+                     "r"(kTcTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+    }
+    if (tid == 32) {
+        for (int s = 0; s < kTcStages; ++s) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_smem(&full_bar[s])));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_smem(&empty_bar[s])));
+        }
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_smem(&done_bar)));
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::);
+        failed = 0;
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::);
+    const uint32_t tmem = tmem_base;
+    const uint32_t ring = tc_smem(tc_ring);
+    bool ok = true;
+
+    if (tid == 0) {
+        // producer: the 128-row (64-row) slab of each plane for k-slice kt is
+        // one contiguous block at kt * rpad * 64 + row0 * 64
+        const unsigned char* src[4] = {
+            reinterpret_cast<const unsigned char*>(g.a_hi) + bz * g.a_batch + m0 * kGemmBK,
+            g.a_lo + bz * g.a_batch + m0 * kGemmBK,
+            reinterpret_cast<const unsigned char*>(g.b_hi) + bz * g.b_batch + n0 * kGemmBK,
+            g.b_lo + bz * g.b_batch + n0 * kGemmBK};
+        const size_t step_a = g.mpad * kGemmBK, step_b = g.npad * kGemmBK;
+        for (size_t kt = 0; kt < ktiles; ++kt) {
+            const int s = static_cast<int>(kt % kTcStages);
+            if (kt >= static_cast<size_t>(kTcStages) &&
+                !tc_wait(tc_smem(&empty_bar[s]), static_cast<uint32_t>((kt / kTcStages - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            const uint32_t bar = tc_smem(&full_bar[s]);
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(kTcStageBytes)
+                         : "memory");
+            const uint32_t dst = ring + s * kTcStageBytes;
+            const uint32_t off[4] = {0, kTcTileA, 2 * kTcTileA, 2 * kTcTileA + kTcTileB};
+            const uint32_t bytes[4] = {kTcTileA, kTcTileA, kTcTileB, kTcTileB};
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const unsigned char* from = src[p] + kt * (p < 2 ? step_a : step_b);
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                        dst + off[p]),
+                    "l"(from), "r"(bytes[p]), "r"(bar)
+                    : "memory");
+            }
+        }
+    } else if (tid == 32) {
+        // MMA issuer: per 64-byte k-slice, two K = 32 steps of the three
+        // partial products (hh, hl + lh, ll)
+        constexpr uint32_t lbo = 128;                       // next 16-byte k chunk
+        constexpr uint32_t sbo = 8 * kGemmBK;               // next group of 8 rows
+        for (size_t kt = 0; kt < ktiles; ++kt) {
+            const int s = static_cast<int>(kt % kTcStages);
+            if (!tc_wait(tc_smem(&full_bar[s]), static_cast<uint32_t>((kt / kTcStages) & 1))) {
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;\n" ::);
+            const uint32_t a_hi = ring + s * kTcStageBytes, a_lo = a_hi + kTcTileA;
+            const uint32_t b_hi = a_hi + 2 * kTcTileA, b_lo = b_hi + kTcTileB;
+#pragma unroll
+            for (int ks = 0; ks < kGemmBK / 32; ++ks) {
+                const uint32_t ko = ks * 2 * lbo;
+                const uint32_t acc = (kt > 0 || ks > 0) ? 1u : 0u;
+                const uint64_t dah = tc_desc(a_hi + ko, lbo, sbo), dal = tc_desc(a_lo + ko, lbo, sbo);
+                const uint64_t dbh = tc_desc(b_hi + ko, lbo, sbo), dbl = tc_desc(b_lo + ko, lbo, sbo);
+                tc_mma(tmem, dah, dbh, tc_idesc(1, 1), acc);
+                tc_mma(tmem + kTcBN, dah, dbl, tc_idesc(1, 0), acc);
+                tc_mma(tmem + kTcBN, dal, dbh, tc_idesc(0, 1), 1u);
+                tc_mma(tmem + 2 * kTcBN, dal, dbl, tc_idesc(0, 0), acc);
+            }
+            tc_commit(tc_smem(&empty_bar[s]));
+        }
+        // completes once every MMA issued above has finished
+        tc_commit(tc_smem(&done_bar));
+    }
+    __syncwarp();
+    if (!tc_wait(tc_smem(&done_bar), 0)) ok = false;
+    if (!ok) failed = 1;
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::);
+    if (failed) {
+        if (tid == 0) {
+            *reinterpret_cast<volatile unsigned*>(fault) = 1u;
+            __threadfence_system();
+        }
+    } else {
+        // warp w reads accumulator rows 32w..32w+31 (its tensor-memory lane
+        // quarter), 16 columns at a time, and transposes them through the
+        // (now idle) stage ring so that each store covers 16 consecutive
+        // columns of two rows
+        int64_t* tr = reinterpret_cast<int64_t*>(tc_ring) + warp * 32 * kTcPitch;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+#pragma unroll 1
+        for (int cc = 0; cc < kTcBN; cc += 16) {
+            uint32_t hh[16], mid[16], ll[16];
+            tc_ld16(lane_base + cc, hh);
+            tc_ld16(lane_base + kTcBN + cc, mid);
+            tc_ld16(lane_base + 2 * kTcBN + cc, ll);
+            asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                tr[lane * kTcPitch + j] = 65536 * static_cast<int64_t>(static_cast<int32_t>(hh[j])) +
+                                          256 * static_cast<int64_t>(static_cast<int32_t>(mid[j])) +
+                                          static_cast<int64_t>(static_cast<int32_t>(ll[j]));
+            __syncwarp();
+#pragma unroll 4
+            for (int r2 = 0; r2 < 16; ++r2) {
+                const int row = 2 * r2 + (lane >> 4), col = lane & 15;
+                const size_t i = m0 + warp * 32 + row, j = n0 + cc + col;
+                if (i < g.m && j < g.n) epi(bz, i, j, tr[row * kTcPitch + col]);
+            }
+            __syncwarp();
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::);
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTcTmemCols));
+}
+
 // Byte planes of `batches` row-major matrices [rows][k] (row stride ld,
-// batch b starting at x + b * boff) into hi/lo [batches][rows][kp], zero
-// beyond k.
+// batch b starting at x + b * boff) into planes of rpad rows, zero beyond k
+// and beyond `rows`.
 __global__ void split_planes_kernel(const int16_t* x, size_t rows, size_t k, size_t ld, int8_t* hi, uint8_t* lo,
-                                    size_t kp, unsigned batches, size_t boff);
+                                    size_t kp, size_t rpad, unsigned batches, size_t boff);
 // Byte planes of the transposes: batch b of x is [k][n] row-major (stride ld,
-// starting at x + b * boff); planes are [batches][n][kp].
+// starting at x + b * boff); planes have npad rows (one per column of x).
 __global__ void split_planes_t_kernel(const int16_t* x, size_t k, size_t n, size_t ld, int8_t* hi, uint8_t* lo,
-                                      size_t kp, size_t boff);
+                                      size_t kp, size_t npad, size_t boff);
 
 #endif  // __CUDACC__
 
@@ -216,13 +455,19 @@ int gemm_prepare_b(Context* c, const int16_t* b, size_t k, size_t n, size_t ldb,
 #ifdef __CUDACC__
 template <class Epi>
 int gemm_launch(Context* c, const GemmPlanes& g, const Epi& epi) {
-    const dim3 grid(static_cast<unsigned>((g.n + kGemmBN - 1) / kGemmBN),
-                    static_cast<unsigned>((g.m + kGemmBM - 1) / kGemmBM), g.batches);
-    if (grid.y > 65535 || grid.z > 65535) return fail_message(c, "GEMM shape exceeds the launch grid");
-    if (g.kp > kGemmChunkK)
+    if (g.kp <= kGemmChunkK) {
+        const dim3 grid(static_cast<unsigned>((g.n + kTcBN - 1) / kTcBN),
+                        static_cast<unsigned>((g.m + kTcBM - 1) / kTcBM), g.batches);
+        if (grid.y > 65535 || grid.z > 65535) return fail_message(c, "GEMM shape exceeds the launch grid");
+        VZB_CUDA(c, cudaFuncSetAttribute(gemm_tc_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kTcSmem)));
+        gemm_tc_kernel<Epi><<<grid, kTcThreads, kTcSmem, c->stream>>>(g, epi, device_fault_word(c));
+    } else {
+        const dim3 grid(static_cast<unsigned>((g.n + kGemmBN - 1) / kGemmBN),
+                        static_cast<unsigned>((g.m + kGemmBM - 1) / kGemmBM), g.batches);
+        if (grid.y > 65535 || grid.z > 65535) return fail_message(c, "GEMM shape exceeds the launch grid");
         gemm_planes_kernel<Epi, true><<<grid, kGemmThreads, 0, c->stream>>>(g, epi);
-    else
-        gemm_planes_kernel<Epi, false><<<grid, kGemmThreads, 0, c->stream>>>(g, epi);
+    }
     VZB_LAUNCHED(c);
     return 0;
 }

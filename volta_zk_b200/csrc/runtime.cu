@@ -119,6 +119,12 @@ int sync_stream_raw(Context* c) {
     const cudaError_t e = cudaStreamSynchronize(c->stream);
     const auto t1 = std::chrono::steady_clock::now();
     if (e != cudaSuccess) return fail_cuda(c, "cudaStreamSynchronize", e);
+    volatile unsigned* fault =
+        reinterpret_cast<volatile unsigned*>(static_cast<char*>(c->host_mailbox) + kMailboxFaultOffset);
+    if (*fault) {
+        *fault = 0;
+        return fail_message(c, "a tensor-core pipeline wait timed out; the results of the last operation are invalid");
+    }
     c->counter_pending = false;
     c->outstanding = 0;
     ++c->stats.synchronizations;

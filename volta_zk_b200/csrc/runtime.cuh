@@ -213,6 +213,12 @@ int op_finish(Context* c, int op, uint64_t h2d, uint64_t d2h, uint64_t d2d = 0,
 // Host-bound round messages: the reducing kernel writes the message into the
 // mapped mailbox, then (after a system fence) `seq` into the flag word.
 constexpr size_t kMailboxFlagOffset = 1024;
+// Word of the mailbox in which a kernel whose bounded wait ran out of time
+// records a nonzero code; every stream synchronisation checks and clears it.
+constexpr size_t kMailboxFaultOffset = 2048;
+inline unsigned* device_fault_word(Context* c) {
+    return reinterpret_cast<unsigned*>(static_cast<char*>(c->host_mailbox_dev) + kMailboxFaultOffset);
+}
 // Finish a primitive whose output is a message in the mapped mailbox.  In the
 // wall-only counter mode the host waits on the flag (no stream
 // synchronisation); the other modes synchronise as op_finish does.
