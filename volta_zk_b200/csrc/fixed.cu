@@ -239,6 +239,7 @@ struct FixedGemmEpi {
     size_t n;
     uint32_t shift;
     __device__ __forceinline__ bool active(size_t, size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ size_t k_end(size_t, size_t, size_t, size_t kp) const { return kp; }
     __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t acc) const {
         if (bias) acc += static_cast<int64_t>(bias[j]) << shift;
         const size_t z = i * n + j;
@@ -266,6 +267,7 @@ struct ScoresEpi {
     __device__ __forceinline__ bool active(size_t, size_t m0, size_t n0, size_t tile_rows) const {
         return n0 <= pos0 + m0 + tile_rows - 1;
     }
+    __device__ __forceinline__ size_t k_end(size_t, size_t, size_t, size_t kp) const { return kp; }
     __device__ __forceinline__ void operator()(size_t h, size_t i, size_t j, int64_t acc) const {
         if (j > pos0 + i) return;
         const size_t p = h * per_head + packed_prefix(i, pos0) + j;
@@ -281,9 +283,14 @@ struct AvEpi {
     int64_t* accs;
     int16_t* outs;
     uint32_t* error;
-    size_t d, head_dim;
+    size_t d, head_dim, pos0;
     uint32_t shift;
     __device__ __forceinline__ bool active(size_t, size_t, size_t, size_t) const { return true; }
+    // weight rows m0 .. m0 + tile_rows - 1 are zero from key pos0 + m0 + tile_rows on
+    __device__ __forceinline__ size_t k_end(size_t, size_t m0, size_t tile_rows, size_t kp) const {
+        const size_t w = (pos0 + m0 + tile_rows + kGemmBK - 1) / kGemmBK * kGemmBK;
+        return w < kp ? w : kp;
+    }
     __device__ __forceinline__ void operator()(size_t h, size_t i, size_t j, int64_t acc) const {
         const size_t z = i * d + h * head_dim + j;
         accs[z] = acc;
@@ -297,6 +304,7 @@ struct LogitsEpi {
     int64_t* out;
     size_t vocab;
     __device__ __forceinline__ bool active(size_t, size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ size_t k_end(size_t, size_t, size_t, size_t kp) const { return kp; }
     __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t v) const { out[i * vocab + j] = v; }
 };
 
@@ -543,7 +551,7 @@ extern "C" int volta_cuda_fixed_av_device(void* raw, uint64_t weights_id, size_t
     causal_planes_kernel<<<grid_for(c, heads * mpad * kp / 16, 256), 256, 0, c->stream>>>(
         w, rows, pos0, heads, kp, mpad, const_cast<int8_t*>(g.a_hi), const_cast<uint8_t*>(g.a_lo));
     VZB_LAUNCHED(c);
-    if (gemm_launch(c, g, AvEpi{acc, out, err, d, head_dim, shift})) return -1;
+    if (gemm_launch(c, g, AvEpi{acc, out, err, d, head_dim, pos0, shift})) return -1;
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpGemm, 0, 0);
 }

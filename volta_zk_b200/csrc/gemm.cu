@@ -7,8 +7,22 @@
 
 namespace vzb {
 
+// Packs 16 int16 values into the 16 high bytes and 16 low bytes of one
+// core-matrix row of each plane.
+__device__ __forceinline__ void pack16(const uint32_t (&v)[16], int8_t* hi, uint8_t* lo) {
+    uint32_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+        h[t >> 2] |= (v[t] >> 8) << (8 * (t & 3));
+        l[t >> 2] |= (v[t] & 0xFFu) << (8 * (t & 3));
+    }
+    *reinterpret_cast<uint4*>(hi) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 // One thread per 16-byte core-matrix row of the output planes (consecutive
-// threads write consecutive 16-byte chunks).
+// threads write consecutive 16-byte chunks); a row's 16 values are read as
+// two 16-byte vectors when the source allows it.
 __global__ void split_planes_kernel(const int16_t* x, size_t rows, size_t k, size_t ld, int8_t* hi, uint8_t* lo,
                                     size_t kp, size_t rpad, unsigned batches, size_t boff) {
     const size_t per = rpad * kp / 16, total = per * batches;
@@ -18,46 +32,45 @@ __global__ void split_planes_kernel(const int16_t* x, size_t rows, size_t k, siz
         // q -> (k-slice, row group, 16-byte chunk, row in group), the order of plane_off
         const size_t slice = q / (rpad * 4), rem = q - slice * rpad * 4;
         const size_t r = (rem >> 5) * 8 + (rem & 7), k0 = slice * 64 + ((rem >> 3) & 3) * 16;
-        uint32_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
-        if (r < rows) {
-            const int16_t* src = x + b * boff + r * ld;
+        uint32_t v[16];
+        const int16_t* src = x + b * boff + r * ld + k0;
+        if (r < rows && k0 + 16 <= k && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+            const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(src)), w1 = __ldg(reinterpret_cast<const uint4*>(src) + 1);
+            const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-            for (int t = 0; t < 16; ++t) {
-                const size_t kk = k0 + t;
-                const uint32_t v = kk < k ? static_cast<uint16_t>(src[kk]) : 0u;
-                h[t >> 2] |= (v >> 8) << (8 * (t & 3));
-                l[t >> 2] |= (v & 0xFFu) << (8 * (t & 3));
+            for (int t = 0; t < 8; ++t) {
+                v[2 * t] = w[t] & 0xFFFFu;
+                v[2 * t + 1] = w[t] >> 16;
             }
+        } else {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = (r < rows && k0 + t < k) ? static_cast<uint16_t>(src[t]) : 0u;
         }
         const size_t off = b * rpad * kp + q * 16;
-        *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+        pack16(v, hi + off, lo + off);
     }
 }
 
-// 32 x 32 tiles through shared memory: coalesced reads of x rows; blockIdx.z
-// is the batch; rows n..npad of the planes are written as zeros.
+// Transposing split: plane row nn holds column nn of x ([k][n] row-major,
+// stride ld, batch b at x + b * boff).  One thread per 16-byte core-matrix
+// row (16 consecutive k of one column); the 32 threads of a warp take 32
+// consecutive columns, so each of the 16 reads is one coalesced 64-byte
+// access and each plane store covers four 128-byte row groups.  Rows n..npad
+// are written as zeros.
 __global__ void split_planes_t_kernel(const int16_t* x, size_t k, size_t n, size_t ld, int8_t* hi, uint8_t* lo,
-                                      size_t kp, size_t npad, size_t boff) {
-    __shared__ int16_t t[32][33];
-    const size_t k0 = static_cast<size_t>(blockIdx.x) * 32, n0 = static_cast<size_t>(blockIdx.y) * 32;
-    const size_t b = blockIdx.z;
-    x += b * boff;
-    hi += b * npad * kp;
-    lo += b * npad * kp;
-    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-        const size_t kk = k0 + r, nn = n0 + threadIdx.x;
-        t[r][threadIdx.x] = (kk < k && nn < n) ? x[kk * ld + nn] : 0;
-    }
-    __syncthreads();
-    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-        const size_t nn = n0 + r, kk = k0 + threadIdx.x;
-        if (nn < npad && kk < kp) {
-            const int v = t[threadIdx.x][r];
-            const size_t o = plane_off(nn, kk, npad);
-            hi[o] = static_cast<int8_t>(v >> 8);
-            lo[o] = static_cast<uint8_t>(v & 0xFF);
-        }
+                                      size_t kp, size_t npad, unsigned batches, size_t boff) {
+    const size_t chunks = kp / 16, per = npad * chunks, total = per * batches;
+    for (size_t z = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; z < total;
+         z += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t b = z / per, q = z - b * per;
+        const size_t nb = q / (32 * chunks), rem = q - nb * 32 * chunks;
+        const size_t kc = rem >> 5, nn = nb * 32 + (rem & 31), k0 = kc * 16;
+        const int16_t* src = x + b * boff + nn;
+        uint32_t v[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) v[t] = (nn < n && k0 + t < k) ? static_cast<uint16_t>(src[(k0 + t) * ld]) : 0u;
+        const size_t off = b * npad * kp + plane_off(nn, k0, npad);
+        pack16(v, hi + off, lo + off);
     }
 }
 
@@ -80,10 +93,8 @@ int gemm_prepare_b(Context* c, const int16_t* b, size_t k, size_t n, size_t ldb,
         split_planes_kernel<<<grid_for(c, bbytes / 16, 256), 256, 0, c->stream>>>(
             b, n, k, ldb, const_cast<int8_t*>(out->b_hi), const_cast<uint8_t*>(out->b_lo), kp, npad, batches, b_boff);
     } else {
-        const dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>(npad / 32), batches);
-        if (grid.y > 65535 || grid.z > 65535) return fail_message(c, "GEMM column count exceeds the launch grid");
-        split_planes_t_kernel<<<grid, dim3(32, 8), 0, c->stream>>>(b, k, n, ldb, const_cast<int8_t*>(out->b_hi),
-                                                                   const_cast<uint8_t*>(out->b_lo), kp, npad, b_boff);
+        split_planes_t_kernel<<<grid_for(c, bbytes / 16, 256), 256, 0, c->stream>>>(
+            b, k, n, ldb, const_cast<int8_t*>(out->b_hi), const_cast<uint8_t*>(out->b_lo), kp, npad, batches, b_boff);
     }
     VZB_LAUNCHED(c);
     return 0;
@@ -110,6 +121,7 @@ struct I64Epi {
     int64_t* out;
     size_t ldo;
     __device__ __forceinline__ bool active(size_t, size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ size_t k_end(size_t, size_t, size_t, size_t kp) const { return kp; }
     __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t v) const { out[i * ldo + j] = v; }
 };
 
@@ -125,6 +137,7 @@ struct RequantAuthEpi {
     size_t n;
     uint32_t shift;
     __device__ __forceinline__ bool active(size_t, size_t, size_t, size_t) const { return true; }
+    __device__ __forceinline__ size_t k_end(size_t, size_t, size_t, size_t kp) const { return kp; }
     __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t v) const {
         const size_t z = i * n + j;
         const int16_t y = requant_clamped(v, shift);

@@ -19,11 +19,12 @@
 // moves into shared memory already in the tensor core's canonical K-major
 // layout.
 //
-// gemm_tc_kernel (K <= 16384) computes a 128 x 64 tile per CTA on the 5th
-// generation tensor cores: one lane streams the tiles with cp.async.bulk into
-// a 4-stage mbarrier ring, one lane issues tcgen05.mma kind::i8 into three
-// int32 accumulators in tensor memory, and all four warps run the epilogue
-// from tensor memory.  gemm_planes_kernel (longer K) is the mma.sync form
+// gemm_tc_kernel (K <= 16384) is a persistent kernel on the 5th generation
+// tensor cores, one CTA per SM walking 128 x 128 output tiles: one lane
+// streams the slabs with cp.async.bulk into a 5-stage mbarrier ring, one lane
+// issues tcgen05.mma kind::i8 into three int32 accumulators in tensor memory,
+// and eight epilogue warps empty tensor memory into registers right after
+// each tile so that the next tile's MMAs overlap the stores.  gemm_planes_kernel (longer K) is the mma.sync form
 // with 64 x 64 tiles, which flushes int32 partials into int64 registers.
 #pragma once
 
@@ -214,15 +215,18 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_planes_kernel(GemmPlanes g,
 
 // ---- tcgen05 form -----------------------------------------------------------
 
-constexpr int kTcBM = 128, kTcBN = 64, kTcStages = 4, kTcThreads = 128;
+constexpr int kTcBM = 128, kTcBN = 128, kTcStages = 5;
+constexpr int kTcEpiWarps = 8, kTcThreads = 64 + 32 * kTcEpiWarps;  // producer, MMA, epilogue warps
+constexpr int kTcEpiCols = kTcBN / (kTcEpiWarps / 4);             // columns per epilogue warp
 constexpr uint32_t kTcTileA = kTcBM * kGemmBK;                    // one A plane tile (8 KiB)
-constexpr uint32_t kTcTileB = kTcBN * kGemmBK;                    // one B plane tile (4 KiB)
+constexpr uint32_t kTcTileB = kTcBN * kGemmBK;                    // one B plane tile (8 KiB)
 constexpr uint32_t kTcStageBytes = 2 * kTcTileA + 2 * kTcTileB;   // hi + lo of A and B
-constexpr size_t kTcSmem = static_cast<size_t>(kTcStages) * kTcStageBytes;
-constexpr uint32_t kTcTmemCols = 256;                             // 3 x 64 int32 columns used
-constexpr unsigned long long kTcWaitNs = 2000000000ull;           // bound of every pipeline wait
 constexpr int kTcPitch = 17;                                      // epilogue transpose row pitch (int64)
-static_assert(kTcThreads / 32 * 32 * kTcPitch * 8 <= kTcSmem, "epilogue transpose fits the stage ring");
+constexpr size_t kTcTransBytes = static_cast<size_t>(kTcEpiWarps) * 32 * kTcPitch * 8;
+constexpr size_t kTcSmem = static_cast<size_t>(kTcStages) * kTcStageBytes + kTcTransBytes;
+constexpr uint32_t kTcTmemCols = 512;                             // hh, mid, ll: 3 x kTcBN columns
+constexpr unsigned long long kTcWaitNs = 2000000000ull;           // bound of every pipeline wait
+static_assert(kTcSmem <= 227 * 1024, "stage ring + transpose buffer fit one CTA");
 
 __device__ __forceinline__ uint32_t tc_smem(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -234,8 +238,10 @@ __device__ __forceinline__ unsigned long long tc_clock() {
     return t;
 }
 
-// Bounded wait for the completion of phase `parity` of an mbarrier.
-__device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait for the completion of phase `parity` of an mbarrier; gives up
+// at once when another role of the CTA has already failed (unless `failed`
+// is null).
+__device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity, const volatile int* failed) {
     const unsigned long long t0 = tc_clock();
     for (;;) {
         uint32_t done;
@@ -247,8 +253,12 @@ __device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity) {
             : "r"(bar), "r"(parity)
             : "memory");
         if (done) return true;
-        if (tc_clock() - t0 > kTcWaitNs) return false;
+        if ((failed && *failed) || tc_clock() - t0 > kTcWaitNs) return false;
     }
+}
+
+__device__ __forceinline__ void tc_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
 
 // Shared-memory matrix descriptor, no swizzle (version 1 = tcgen05): start,
@@ -288,32 +298,58 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 
-// One 128 x 64 output tile of batch blockIdx.z.  Requires g.kp <= kGemmChunkK
-// (int32 accumulators stay exact).  A pipeline wait that runs out of time
-// records 1 in *fault, skips the epilogue and releases tensor memory.
-template <class Epi>
-__global__ void __launch_bounds__(kTcThreads) gemm_tc_kernel(GemmPlanes g, Epi epi, unsigned* fault) {
-    extern __shared__ __align__(128) unsigned char tc_ring[];
-    __shared__ __align__(8) uint64_t full_bar[kTcStages], empty_bar[kTcStages], done_bar;
-    __shared__ uint32_t tmem_base;
-    __shared__ int failed;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const size_t m0 = static_cast<size_t>(blockIdx.y) * kTcBM, n0 = static_cast<size_t>(blockIdx.x) * kTcBN;
-    const size_t bz = blockIdx.z;
-    if (!epi.active(bz, m0, n0, kTcBM)) return;
-    const size_t ktiles = g.kp / kGemmBK;
+// Tile t of the product, batches slowest.  Inside a batch the tiles of the
+// smaller operand vary fastest, so that consecutive tiles (running on
+// neighbouring SMs at the same time) share a slab of the larger operand.
+struct TcTile {
+    size_t m0, n0, bz;
+};
+__device__ __forceinline__ TcTile tc_tile(size_t t, size_t tiles_n, size_t tiles_m, bool m_fast) {
+    const size_t per = tiles_n * tiles_m, bz = t / per, r = t - bz * per;
+    if (m_fast) {
+        const size_t tx = r / tiles_m;
+        return TcTile{(r - tx * tiles_m) * kTcBM, tx * kTcBN, bz};
+    }
+    const size_t ty = r / tiles_n;
+    return TcTile{ty * kTcBM, (r - ty * tiles_n) * kTcBN, bz};
+}
 
-    if (warp == 0) {
+// Persistent GEMM: CTA b handles tiles b, b + gridDim.x, ... (those with
+// epi.active).  Warp 0 streams the 128-row slabs of each k-slice with
+// cp.async.bulk into a kTcStages ring; warp 1 issues the tcgen05.mma of each
+// tile into the three accumulators in tensor memory; warps 2..9 move each
+// finished tile into registers, release tensor memory for the next tile and
+// run the epilogue while it accumulates.  Only k-slices below
+// epi.k_end(z, m0, tile_rows, kp) are read (all-zero slices of causal
+// operands are skipped).  Requires g.kp <= kGemmChunkK (int32 accumulators
+// stay exact).  A wait that runs out of time records 1 in *fault; the CTA
+// then stops issuing work, waits (bounded) for its MMAs and releases tensor
+// memory.
+template <class Epi>
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(GemmPlanes g, Epi epi, unsigned* fault) {
+    extern __shared__ __align__(128) unsigned char tc_ring[];
+    __shared__ __align__(8) uint64_t full_bar[kTcStages], empty_bar[kTcStages];
+    __shared__ __align__(8) uint64_t acc_full, acc_empty, drain_bar;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int failed;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t tiles_n = (g.n + kTcBN - 1) / kTcBN, tiles_m = (g.m + kTcBM - 1) / kTcBM;
+    const size_t tiles = tiles_n * tiles_m * g.batches;
+    const bool m_fast = g.n > g.m;
+
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(tc_smem(&tmem_base)),
                      "r"(kTcTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
     }
-    if (tid == 32) {
+    if (tid == 0) {
         for (int s = 0; s < kTcStages; ++s) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_smem(&full_bar[s])));
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_smem(&empty_bar[s])));
         }
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_smem(&done_bar)));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_smem(&acc_full)));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(tc_smem(&acc_empty)), "r"(kTcEpiWarps));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_smem(&drain_bar)));
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::);
         failed = 0;
     }
@@ -321,112 +357,169 @@ __global__ void __launch_bounds__(kTcThreads) gemm_tc_kernel(GemmPlanes g, Epi e
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::);
     const uint32_t tmem = tmem_base;
     const uint32_t ring = tc_smem(tc_ring);
-    bool ok = true;
 
-    if (tid == 0) {
-        // producer: the 128-row (64-row) slab of each plane for k-slice kt is
-        // one contiguous block at kt * rpad * 64 + row0 * 64
-        const unsigned char* src[4] = {
-            reinterpret_cast<const unsigned char*>(g.a_hi) + bz * g.a_batch + m0 * kGemmBK,
-            g.a_lo + bz * g.a_batch + m0 * kGemmBK,
-            reinterpret_cast<const unsigned char*>(g.b_hi) + bz * g.b_batch + n0 * kGemmBK,
-            g.b_lo + bz * g.b_batch + n0 * kGemmBK};
-        const size_t step_a = g.mpad * kGemmBK, step_b = g.npad * kGemmBK;
-        for (size_t kt = 0; kt < ktiles; ++kt) {
-            const int s = static_cast<int>(kt % kTcStages);
-            if (kt >= static_cast<size_t>(kTcStages) &&
-                !tc_wait(tc_smem(&empty_bar[s]), static_cast<uint32_t>((kt / kTcStages - 1) & 1))) {
-                ok = false;
-                break;
-            }
-            const uint32_t bar = tc_smem(&full_bar[s]);
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(kTcStageBytes)
-                         : "memory");
-            const uint32_t dst = ring + s * kTcStageBytes;
-            const uint32_t off[4] = {0, kTcTileA, 2 * kTcTileA, 2 * kTcTileA + kTcTileB};
-            const uint32_t bytes[4] = {kTcTileA, kTcTileA, kTcTileB, kTcTileB};
+    if (warp == 0) {
+        if (lane == 0) {
+            // producer: the slab of each plane for k-slice kt is one
+            // contiguous block at kt * rpad * 64 + row0 * 64
+            const size_t step_a = g.mpad * kGemmBK, step_b = g.npad * kGemmBK;
+            size_t slice = 0;  // k-slices streamed so far (all tiles)
+            for (size_t t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
+                const TcTile tl = tc_tile(t, tiles_n, tiles_m, m_fast);
+                if (!epi.active(tl.bz, tl.m0, tl.n0, kTcBM)) continue;
+                const size_t kts = epi.k_end(tl.bz, tl.m0, kTcBM, g.kp) / kGemmBK;
+                const unsigned char* src[4] = {
+                    reinterpret_cast<const unsigned char*>(g.a_hi) + tl.bz * g.a_batch + tl.m0 * kGemmBK,
+                    g.a_lo + tl.bz * g.a_batch + tl.m0 * kGemmBK,
+                    reinterpret_cast<const unsigned char*>(g.b_hi) + tl.bz * g.b_batch + tl.n0 * kGemmBK,
+                    g.b_lo + tl.bz * g.b_batch + tl.n0 * kGemmBK};
+                for (size_t kt = 0; kt < kts; ++kt, ++slice) {
+                    const int s = static_cast<int>(slice % kTcStages);
+                    if (slice >= static_cast<size_t>(kTcStages) &&
+                        !tc_wait(tc_smem(&empty_bar[s]), static_cast<uint32_t>((slice / kTcStages - 1) & 1),
+                                 &failed)) {
+                        failed = 1;
+                        break;
+                    }
+                    const uint32_t bar = tc_smem(&full_bar[s]);
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar),
+                                 "r"(kTcStageBytes)
+                                 : "memory");
+                    const uint32_t dst = ring + s * kTcStageBytes;
+                    const uint32_t off[4] = {0, kTcTileA, 2 * kTcTileA, 2 * kTcTileA + kTcTileB};
+                    const uint32_t bytes[4] = {kTcTileA, kTcTileA, kTcTileB, kTcTileB};
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                const unsigned char* from = src[p] + kt * (p < 2 ? step_a : step_b);
-                asm volatile(
-                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                        dst + off[p]),
-                    "l"(from), "r"(bytes[p]), "r"(bar)
-                    : "memory");
+                    for (int p = 0; p < 4; ++p) {
+                        const unsigned char* from = src[p] + kt * (p < 2 ? step_a : step_b);
+                        asm volatile(
+                            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::
+                                "r"(dst + off[p]),
+                            "l"(from), "r"(bytes[p]), "r"(bar)
+                            : "memory");
+                    }
+                }
+            }
+            if (failed) {
+                // copies still in flight land before the CTA can exit
+                for (size_t q = slice > static_cast<size_t>(kTcStages) ? slice - kTcStages : 0; q < slice; ++q)
+                    tc_wait(tc_smem(&full_bar[q % kTcStages]), static_cast<uint32_t>((q / kTcStages) & 1), nullptr);
             }
         }
-    } else if (tid == 32) {
-        // MMA issuer: per 64-byte k-slice, two K = 32 steps of the three
-        // partial products (hh, hl + lh, ll)
-        constexpr uint32_t lbo = 128;                       // next 16-byte k chunk
-        constexpr uint32_t sbo = 8 * kGemmBK;               // next group of 8 rows
-        for (size_t kt = 0; kt < ktiles; ++kt) {
-            const int s = static_cast<int>(kt % kTcStages);
-            if (!tc_wait(tc_smem(&full_bar[s]), static_cast<uint32_t>((kt / kTcStages) & 1))) {
-                ok = false;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer: per 64-byte k-slice, two K = 32 steps of the three
+            // partial products (hh, hl + lh, ll); tile j starts once the
+            // epilogue has taken tile j - 1 out of tensor memory
+            constexpr uint32_t lbo = 128;             // next 16-byte k chunk
+            constexpr uint32_t sbo = 8 * kGemmBK;     // next group of 8 rows
+            size_t slice = 0, j = 0;
+            for (size_t t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
+                const TcTile tl = tc_tile(t, tiles_n, tiles_m, m_fast);
+                if (!epi.active(tl.bz, tl.m0, tl.n0, kTcBM)) continue;
+                const size_t kts = epi.k_end(tl.bz, tl.m0, kTcBM, g.kp) / kGemmBK;
+                if (j >= 1 && !tc_wait(tc_smem(&acc_empty), static_cast<uint32_t>((j - 1) & 1), &failed)) {
+                    failed = 1;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;\n" ::);
+                const uint32_t d = tmem;
+                bool ok = true;
+                for (size_t kt = 0; kt < kts; ++kt, ++slice) {
+                    const int s = static_cast<int>(slice % kTcStages);
+                    if (!tc_wait(tc_smem(&full_bar[s]), static_cast<uint32_t>((slice / kTcStages) & 1), &failed)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;\n" ::);
+                    const uint32_t a_hi = ring + s * kTcStageBytes, a_lo = a_hi + kTcTileA;
+                    const uint32_t b_hi = a_hi + 2 * kTcTileA, b_lo = b_hi + kTcTileB;
+#pragma unroll
+                    for (int ks = 0; ks < kGemmBK / 32; ++ks) {
+                        const uint32_t ko = ks * 2 * lbo;
+                        const uint32_t acc = (kt > 0 || ks > 0) ? 1u : 0u;
+                        const uint64_t dah = tc_desc(a_hi + ko, lbo, sbo), dal = tc_desc(a_lo + ko, lbo, sbo);
+                        const uint64_t dbh = tc_desc(b_hi + ko, lbo, sbo), dbl = tc_desc(b_lo + ko, lbo, sbo);
+                        tc_mma(d, dah, dbh, tc_idesc(1, 1), acc);
+                        tc_mma(d + kTcBN, dah, dbl, tc_idesc(1, 0), acc);
+                        tc_mma(d + kTcBN, dal, dbh, tc_idesc(0, 1), 1u);
+                        tc_mma(d + 2 * kTcBN, dal, dbl, tc_idesc(0, 0), acc);
+                    }
+                    tc_commit(tc_smem(&empty_bar[s]));
+                }
+                if (!ok) {
+                    failed = 1;
+                    break;
+                }
+                tc_commit(tc_smem(&acc_full));
+                ++j;
+            }
+            // completes once every MMA issued above has finished
+            tc_commit(tc_smem(&drain_bar));
+        }
+    } else {
+        // epilogue warps: warp w owns accumulator rows 32 (w % 4) .. + 31
+        // (its tensor-memory lane quarter) and half of the columns.  It
+        // pulls its 32 x 64 block into registers (combined into int64),
+        // hands tensor memory back to the MMA warp, then stores the block 16
+        // columns at a time through a private transpose buffer so that each
+        // store covers 16 consecutive columns of two rows.
+        const int quarter = warp & 3, col0 = ((warp - 2) >> 2) * kTcEpiCols;
+        int64_t* tr = reinterpret_cast<int64_t*>(tc_ring + static_cast<size_t>(kTcStages) * kTcStageBytes) +
+                      (warp - 2) * 32 * kTcPitch;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col0;
+        size_t j = 0;
+        for (size_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+            const TcTile tl = tc_tile(t, tiles_n, tiles_m, m_fast);
+            if (!epi.active(tl.bz, tl.m0, tl.n0, kTcBM)) continue;
+            if (!tc_wait(tc_smem(&acc_full), static_cast<uint32_t>(j & 1), &failed)) {
+                failed = 1;
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::);
-            const uint32_t a_hi = ring + s * kTcStageBytes, a_lo = a_hi + kTcTileA;
-            const uint32_t b_hi = a_hi + 2 * kTcTileA, b_lo = b_hi + kTcTileB;
+            int64_t v[kTcEpiCols];
 #pragma unroll
-            for (int ks = 0; ks < kGemmBK / 32; ++ks) {
-                const uint32_t ko = ks * 2 * lbo;
-                const uint32_t acc = (kt > 0 || ks > 0) ? 1u : 0u;
-                const uint64_t dah = tc_desc(a_hi + ko, lbo, sbo), dal = tc_desc(a_lo + ko, lbo, sbo);
-                const uint64_t dbh = tc_desc(b_hi + ko, lbo, sbo), dbl = tc_desc(b_lo + ko, lbo, sbo);
-                tc_mma(tmem, dah, dbh, tc_idesc(1, 1), acc);
-                tc_mma(tmem + kTcBN, dah, dbl, tc_idesc(1, 0), acc);
-                tc_mma(tmem + kTcBN, dal, dbh, tc_idesc(0, 1), 1u);
-                tc_mma(tmem + 2 * kTcBN, dal, dbl, tc_idesc(0, 0), acc);
+            for (int cc = 0; cc < kTcEpiCols; cc += 16) {
+                uint32_t hh[16], mid[16], ll[16];
+                tc_ld16(lane_base + cc, hh);
+                tc_ld16(lane_base + kTcBN + cc, mid);
+                tc_ld16(lane_base + 2 * kTcBN + cc, ll);
+                asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::);
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                    v[cc + q] = 65536 * static_cast<int64_t>(static_cast<int32_t>(hh[q])) +
+                                256 * static_cast<int64_t>(static_cast<int32_t>(mid[q])) +
+                                static_cast<int64_t>(static_cast<int32_t>(ll[q]));
             }
-            tc_commit(tc_smem(&empty_bar[s]));
+            asm volatile("tcgen05.fence::before_thread_sync;\n" ::);
+            __syncwarp();
+            if (lane == 0) tc_arrive(tc_smem(&acc_empty));
+#pragma unroll
+            for (int cc = 0; cc < kTcEpiCols; cc += 16) {
+#pragma unroll
+                for (int q = 0; q < 16; ++q) tr[lane * kTcPitch + q] = v[cc + q];
+                __syncwarp();
+#pragma unroll 4
+                for (int r2 = 0; r2 < 16; ++r2) {
+                    const int row = 2 * r2 + (lane >> 4), col = lane & 15;
+                    const size_t i = tl.m0 + quarter * 32 + row, jj = tl.n0 + col0 + cc + col;
+                    if (i < g.m && jj < g.n) epi(tl.bz, i, jj, tr[row * kTcPitch + col]);
+                }
+                __syncwarp();
+            }
+            ++j;
         }
-        // completes once every MMA issued above has finished
-        tc_commit(tc_smem(&done_bar));
     }
     __syncwarp();
-    if (!tc_wait(tc_smem(&done_bar), 0)) ok = false;
-    if (!ok) failed = 1;
+    // every MMA this CTA issued has finished before tensor memory is released
+    if (!tc_wait(tc_smem(&drain_bar), 0, nullptr)) failed = 1;
     __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;\n" ::);
-    if (failed) {
-        if (tid == 0) {
-            *reinterpret_cast<volatile unsigned*>(fault) = 1u;
-            __threadfence_system();
-        }
-    } else {
-        // warp w reads accumulator rows 32w..32w+31 (its tensor-memory lane
-        // quarter), 16 columns at a time, and transposes them through the
-        // (now idle) stage ring so that each store covers 16 consecutive
-        // columns of two rows
-        int64_t* tr = reinterpret_cast<int64_t*>(tc_ring) + warp * 32 * kTcPitch;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-#pragma unroll 1
-        for (int cc = 0; cc < kTcBN; cc += 16) {
-            uint32_t hh[16], mid[16], ll[16];
-            tc_ld16(lane_base + cc, hh);
-            tc_ld16(lane_base + kTcBN + cc, mid);
-            tc_ld16(lane_base + 2 * kTcBN + cc, ll);
-            asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::);
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                tr[lane * kTcPitch + j] = 65536 * static_cast<int64_t>(static_cast<int32_t>(hh[j])) +
-                                          256 * static_cast<int64_t>(static_cast<int32_t>(mid[j])) +
-                                          static_cast<int64_t>(static_cast<int32_t>(ll[j]));
-            __syncwarp();
-#pragma unroll 4
-            for (int r2 = 0; r2 < 16; ++r2) {
-                const int row = 2 * r2 + (lane >> 4), col = lane & 15;
-                const size_t i = m0 + warp * 32 + row, j = n0 + cc + col;
-                if (i < g.m && j < g.n) epi(bz, i, j, tr[row * kTcPitch + col]);
-            }
-            __syncwarp();
-        }
+    if (failed && tid == 0) {
+        *reinterpret_cast<volatile unsigned*>(fault) = 1u;
+        __threadfence_system();
     }
     asm volatile("tcgen05.fence::before_thread_sync;\n" ::);
     __syncthreads();
-    if (warp == 0)
+    if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTcTmemCols));
 }
 
@@ -438,7 +531,7 @@ __global__ void split_planes_kernel(const int16_t* x, size_t rows, size_t k, siz
 // Byte planes of the transposes: batch b of x is [k][n] row-major (stride ld,
 // starting at x + b * boff); planes have npad rows (one per column of x).
 __global__ void split_planes_t_kernel(const int16_t* x, size_t k, size_t n, size_t ld, int8_t* hi, uint8_t* lo,
-                                      size_t kp, size_t npad, size_t boff);
+                                      size_t kp, size_t npad, unsigned batches, size_t boff);
 
 #endif  // __CUDACC__
 
@@ -456,12 +549,11 @@ int gemm_prepare_b(Context* c, const int16_t* b, size_t k, size_t n, size_t ldb,
 template <class Epi>
 int gemm_launch(Context* c, const GemmPlanes& g, const Epi& epi) {
     if (g.kp <= kGemmChunkK) {
-        const dim3 grid(static_cast<unsigned>((g.n + kTcBN - 1) / kTcBN),
-                        static_cast<unsigned>((g.m + kTcBM - 1) / kTcBM), g.batches);
-        if (grid.y > 65535 || grid.z > 65535) return fail_message(c, "GEMM shape exceeds the launch grid");
+        const size_t tiles = (g.n + kTcBN - 1) / kTcBN * ((g.m + kTcBM - 1) / kTcBM) * g.batches;
+        const unsigned ctas = static_cast<unsigned>(tiles < static_cast<size_t>(c->sm_count) ? tiles : c->sm_count);
         VZB_CUDA(c, cudaFuncSetAttribute(gemm_tc_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kTcSmem)));
-        gemm_tc_kernel<Epi><<<grid, kTcThreads, kTcSmem, c->stream>>>(g, epi, device_fault_word(c));
+        gemm_tc_kernel<Epi><<<ctas, kTcThreads, kTcSmem, c->stream>>>(g, epi, device_fault_word(c));
     } else {
         const dim3 grid(static_cast<unsigned>((g.n + kGemmBN - 1) / kGemmBN),
                         static_cast<unsigned>((g.m + kGemmBM - 1) / kGemmBM), g.batches);
