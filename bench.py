@@ -55,6 +55,7 @@ def parse():
     ap.add_argument("--ligero-log2-code", type=int, default=16)
     ap.add_argument("--ligero-queries", type=int, default=128)
     ap.add_argument("--no-ligero", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -250,6 +251,47 @@ def ligero_leg(args, prover, be, peaks, rank=0, world=1, comm=None):
     }
 
 
+# GPT-2 small at 1024 tokens: QKV, attention projection, MLP up and down, logits (m, k, n)
+GEMM_SHAPES = [(1024, 768, 2304), (1024, 768, 768), (1024, 768, 3072), (1024, 3072, 768), (1024, 768, 50257)]
+
+
+def gemm_leg(args, be, peaks):
+    """Witness GEMMs (exact int16 x int16 -> int64) of one GPT-2 small layer
+    plus the logits, each through the reference's resident entry point
+    volta_cuda_gemm_i64_device (byte-plane split + tcgen05 kernel).  The
+    tensor-core work is 4 int8 products per int16 MAC; the peak is twice the
+    measured dense bf16 rate (B200's dense int8 rate is twice its bf16
+    rate)."""
+    rng = np.random.default_rng(7)
+    reps = max(3, args.steps)
+    out, total_ms, total_ops = {}, 0.0, 0.0
+    for m, k, n in GEMM_SHAPES:
+        a = be.upload_new(rng.integers(-32768, 32768, m * k, dtype=np.int16))
+        b = be.upload_new(rng.integers(-32768, 32768, k * n, dtype=np.int16))
+        o = be.alloc(8 * m * n)
+        for _ in range(max(1, args.warmup)):
+            be.call("gemm_i64_device", a, 0, b, 0, o, 0, m, k, n)
+        be.mark(12)
+        for _ in range(reps):
+            be.call("gemm_i64_device", a, 0, b, 0, o, 0, m, k, n)
+        be.mark(13)
+        ms = be.elapsed_ms(12, 13) / reps
+        ops = 8.0 * m * k * n
+        out[f"{m}x{k}x{n}"] = {"ms": round(ms, 4), "int8_tops": round(ops / (ms / 1e3) / 1e12, 1)}
+        total_ms += ms
+        total_ops += ops
+        for x in (a, b, o):
+            be.free(x)
+    peak = 2 * peaks.get("bf16_tflops", 1590.0)
+    achieved = total_ops / (total_ms / 1e3) / 1e12
+    return {"workload": "GPT-2 small layer GEMMs + logits at 1024 tokens, exact int16 -> int64",
+            "kernel": "gemm_tc_kernel (tcgen05.mma kind::i8, TMEM accumulators) + byte-plane split",
+            "shapes": out, "total_ms": round(total_ms, 4),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                         "unit": "int8 TOP/s", "frac": round(achieved / peak, 4),
+                         "peak_source": "2 x measured bf16 dense" if "bf16_tflops" in peaks else "2 x fallback bf16"}}
+
+
 def run_b200(args, rank, world, local_rank):
     import torch
 
@@ -418,6 +460,10 @@ def run_b200(args, rank, world, local_rank):
         if world > 1:
             ligero["value"] = round(max_over_ranks(ligero["value"]), 6)
 
+    gemm = None
+    if world == 1 and not args.no_gemm:
+        gemm = gemm_leg(args, be, peaks)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         log2_sample = max(10, min(20, args.log2_sumcheck) - 0)
@@ -447,6 +493,7 @@ def run_b200(args, rank, world, local_rank):
                                                      np.ascontiguousarray(finals).tobytes() +
                                                      np.ascontiguousarray(proof).tobytes()).hexdigest()},
             "ligero": ligero,
+            "witness_gemm": gemm,
         }
         print(json.dumps(line), flush=True)
     prover.close()
