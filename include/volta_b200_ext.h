@@ -118,6 +118,38 @@ typedef struct vzb_layer_job {
 } vzb_layer_job;
 int volta_b200_logup_layers_device(void* ctx, const vzb_layer_job* jobs, size_t count);
 
+/*
+ * Batched LogUp layer rounds.  In the clear sink / private transcript every
+ * layer's claim point and challenges are known in advance, so the round
+ * steps of different fraction-tree layers are independent; this call runs
+ * `count` (<= 24) of them in one launch, each exactly one of these calls:
+ *   kind 0: volta_b200_logup_round_il_into_device (in_id[0] = P, in_id[1] = Q,
+ *           the interleaved children at in_offset[0]; len = vector length);
+ *   kind 1: volta_b200_logup_fold_round_il_into_device (the same inputs, fold
+ *           with r into out_id[k] at out_offset[k], len / 2 entries each);
+ *   kind 2: volta_b200_logup_fold_round_into_device (the four vectors in_id[k]
+ *           at in_offset[k], len entries each, folded into out_id[k]);
+ *   kind 3: volta_cuda_logup_fold4_device (the fold of kind 2, no round).
+ * Kinds 0-2 read the suffix-eq table at (s_id, s_offset) and write the four
+ * raw accumulators at (msg_id, msg_offset).  r = (c0, c1) of the challenge.
+ * Outputs of different jobs must not overlap each other or any input.
+ */
+typedef struct vzb_round_job {
+    uint32_t kind;
+    uint32_t reserved;
+    uint64_t in_id[4];
+    size_t in_offset[4];
+    size_t len;
+    uint64_t r[2];
+    uint64_t out_id[4];
+    size_t out_offset[4];
+    uint64_t s_id;
+    size_t s_offset;
+    uint64_t msg_id;
+    size_t msg_offset;
+} vzb_round_job;
+int volta_b200_logup_round_batch_device(void* ctx, const vzb_round_job* jobs, size_t count);
+
 /* All rounds of a triple-product sumcheck on three resident tables of len
  * (<= 2^11, a power of two) entries; challenges at (r_id, r_offset).  Output:
  * 3 messages per round, then the 3 final values. */

@@ -1,0 +1,156 @@
+"""Cross-layer LogUp round batches (volta_b200_logup_round_batch_device)
+against the oracle's fold and round functions: every job of a batch must
+equal its single-layer call (round on interleaved children, fold + round on
+interleaved children, fold + round, fold only), whatever else shares the
+launch."""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+P = 0xFFFFFFFF00000001
+pytestmark = pytest.mark.gpu
+
+
+class RoundJob(C.Structure):
+    """include/volta_b200_ext.h: vzb_round_job."""
+
+    _fields_ = [("kind", C.c_uint32), ("reserved", C.c_uint32), ("in_id", C.c_uint64 * 4),
+                ("in_offset", C.c_size_t * 4), ("len", C.c_size_t), ("r", C.c_uint64 * 2),
+                ("out_id", C.c_uint64 * 4), ("out_offset", C.c_size_t * 4), ("s_id", C.c_uint64),
+                ("s_offset", C.c_size_t), ("msg_id", C.c_uint64), ("msg_offset", C.c_size_t)]
+
+
+@pytest.fixture(scope="module")
+def be():
+    from volta_zk_b200 import accel
+
+    b = accel.CudaBackend(policy=1)
+    yield b
+    b.close()
+
+
+def rand_fp2(rng, n):
+    return rng.integers(0, P, size=(n, 2), dtype=np.uint64)
+
+
+def run_batch(be, jobs):
+    arr = (RoundJob * len(jobs))(*jobs)
+    return be.lib.volta_b200_logup_round_batch_device(be.ctx, C.cast(arr, C.c_void_p), len(jobs))
+
+
+class Case:
+    """One job with its inputs, outputs and the oracle's expectation."""
+
+    def __init__(self, be, oracle, rng, kind, length, msg_id, msg_slot):
+        self.kind, self.length = kind, length
+        il = kind <= 1
+        fold = kind != 0
+        self.r = tuple(int(x) for x in rand_fp2(rng, 1)[0])
+        pairs = length // 4 if fold else length // 2
+        s_off = int(rng.integers(0, 5))
+        self.suffix = rand_fp2(rng, s_off + pairs)
+        self.ids = []
+        job = RoundJob()
+        job.kind, job.len = kind, length
+        job.r[0], job.r[1] = self.r
+        if il:
+            child_off = int(rng.integers(0, 3))
+            self.P = rand_fp2(rng, child_off + 2 * length)
+            self.Q = rand_fp2(rng, child_off + 2 * length)
+            job.in_id[0], job.in_id[1] = be.upload_new(self.P), be.upload_new(self.Q)
+            job.in_offset[0] = child_off
+            self.ids += [job.in_id[0], job.in_id[1]]
+            ch_p, ch_q = self.P[child_off:], self.Q[child_off:]
+            # deinterleaved p0, p1, q0, q1
+            v = [np.ascontiguousarray(x) for x in (ch_p[0::2], ch_p[1::2], ch_q[0::2], ch_q[1::2])]
+        else:
+            v = [rand_fp2(rng, length) for _ in range(4)]
+            for k in range(4):
+                off = int(rng.integers(0, 3))
+                job.in_id[k] = be.upload_new(np.concatenate([rand_fp2(rng, off), v[k]]))
+                job.in_offset[k] = off
+                self.ids.append(job.in_id[k])
+        if fold:
+            self.folded = [oracle.fold_rows(x, 1, length, self.r) for x in v]
+            self.out_off = []
+            for k in range(4):
+                off = int(rng.integers(0, 3))
+                job.out_id[k] = be.alloc(16 * (off + length // 2))
+                job.out_offset[k] = off
+                self.ids.append(job.out_id[k])
+                self.out_off.append(off)
+            after = self.folded
+        else:
+            after = v
+        self.expect_msg = None
+        if kind != 3:
+            job.s_id = be.upload_new(self.suffix)
+            job.s_offset = s_off
+            self.ids.append(job.s_id)
+            job.msg_id, job.msg_offset = msg_id, 4 * msg_slot
+            self.expect_msg = oracle.logup_general_round(*after, self.suffix[s_off:], pairs)
+        self.job, self.msg_slot = job, msg_slot
+
+    def check(self, be, msgs):
+        if self.kind != 0:
+            for k in range(4):
+                got = be.download_fp2(self.job.out_id[k], self.length // 2, offset=self.out_off[k])
+                assert np.array_equal(got, self.folded[k]), (self.kind, self.length, k)
+        if self.expect_msg is not None:
+            assert np.array_equal(msgs[4 * self.msg_slot: 4 * self.msg_slot + 4], self.expect_msg), \
+                (self.kind, self.length)
+
+    def free(self, be):
+        for i in self.ids:
+            be.free(i)
+
+
+@pytest.mark.parametrize("spec", [
+    [(0, 2)], [(1, 4)], [(2, 4)], [(3, 4)],
+    [(0, 1 << 12), (1, 1 << 14), (2, 1 << 13), (3, 1 << 12), (2, 1 << 16), (0, 8)],
+    [(2, 1 << 20), (2, 4096), (1, 1 << 18), (0, 1 << 17), (3, 1 << 15)] + [(2, 64)] * 10,
+], ids=["round-il", "fold-round-il", "fold-round", "fold", "mixed-6", "mixed-15"])
+def test_round_batch_matches_single_layer_calls(be, oracle, spec):
+    rng = np.random.default_rng(len(spec) * 1000 + spec[0][1])
+    msg_id = be.alloc(16 * 4 * len(spec))
+    cases = [Case(be, oracle, rng, kind, length, msg_id, j) for j, (kind, length) in enumerate(spec)]
+    assert run_batch(be, [c.job for c in cases]) == 0, be.last_error()
+    msgs = be.download_fp2(msg_id, 4 * len(spec))
+    for c in cases:
+        c.check(be, msgs)
+    # repeated launches reuse the per-job counters
+    assert run_batch(be, [c.job for c in cases]) == 0, be.last_error()
+    assert np.array_equal(be.download_fp2(msg_id, 4 * len(spec)), msgs)
+    for c in cases:
+        c.free(be)
+    be.free(msg_id)
+
+
+def test_round_batch_rejects_bad_jobs(be):
+    ids = [be.alloc(16 * 64) for _ in range(10)]
+    job = RoundJob()
+    job.kind, job.len = 2, 16
+    for k in range(4):
+        job.in_id[k], job.out_id[k] = ids[k], ids[4 + k]
+    job.s_id, job.msg_id = ids[8], ids[9]
+    assert run_batch(be, [job]) == 0, be.last_error()
+    bad = RoundJob.from_buffer_copy(job)
+    bad.kind = 4
+    assert run_batch(be, [bad]) == -1 and "kind" in be.last_error()
+    bad = RoundJob.from_buffer_copy(job)
+    bad.len = 6
+    assert run_batch(be, [bad]) == -1 and "length" in be.last_error()
+    bad = RoundJob.from_buffer_copy(job)
+    bad.len = 256  # beyond the buffers
+    assert run_batch(be, [bad]) == -1
+    bad = RoundJob.from_buffer_copy(job)
+    bad.r[0] = P
+    assert run_batch(be, [bad]) == -1 and "canonical" in be.last_error()
+    assert run_batch(be, [job] * 25) == -1 and "24" in be.last_error()
+    assert run_batch(be, []) == -1
+    # the context stays usable
+    assert run_batch(be, [job]) == 0, be.last_error()
+    for i in ids:
+        be.free(i)

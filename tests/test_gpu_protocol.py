@@ -9,18 +9,21 @@ P = 0xFFFFFFFF00000001
 pytestmark = pytest.mark.gpu
 
 
-# (timing policy, fused fold + round extensions, scheduled drivers): the
-# reference's round-by-round call sequence under deferred events, the fused
-# round-by-round drivers under both policies, and the scheduled drivers
-# (challenges first, one message download) with and without fusion.
+# (timing policy, fused fold + round extensions, scheduled drivers, cross-layer
+# batches): the reference's round-by-round call sequence under deferred
+# events, the fused round-by-round drivers under both policies, and the
+# scheduled drivers (challenges first, one message download) without fusion,
+# with fusion layer after layer, and with the cross-layer round batches.
 @pytest.fixture(scope="module",
-                params=[(0, False, False), (0, True, False), (1, True, False), (1, False, True), (1, True, True)],
-                ids=["events-unfused", "events-fused", "counters-fused", "scheduled-unfused", "scheduled-fused"])
+                params=[(0, False, False, False), (0, True, False, False), (1, True, False, False),
+                        (1, False, True, False), (1, True, True, False), (1, True, True, True)],
+                ids=["events-unfused", "events-fused", "counters-fused", "scheduled-unfused", "scheduled-fused",
+                     "scheduled-batched"])
 def prover(request):
     from volta_zk_b200 import accel
 
-    policy, fused, scheduled = request.param
-    p = accel.Prover(policy=policy, fused=fused, scheduled=scheduled)
+    policy, fused, scheduled, batched = request.param
+    p = accel.Prover(policy=policy, fused=fused, scheduled=scheduled, batched=batched)
     yield p
     p.close()
 
@@ -53,7 +56,7 @@ def test_triple_sumcheck_matches_oracle(prover, oracle, log2n):
         be.free(i)
 
 
-@pytest.mark.parametrize("log2f,log2t", [(1, 1), (4, 3), (10, 8), (14, 10)])
+@pytest.mark.parametrize("log2f,log2t", [(1, 1), (4, 3), (10, 8), (14, 10), (16, 13)])
 def test_logup_prove_matches_oracle(prover, oracle, log2f, log2t):
     nf, nt = 1 << log2f, 1 << log2t
     rng = np.random.default_rng(log2f * 100 + log2t)

@@ -81,7 +81,7 @@ _CTYPES = {
     "vz_fp2": Fp2, "vz_fp2*": C.c_void_p, "const vz_fp2*": C.c_void_p,
     "vz_raw_stats*": C.c_void_p, "vz_raw_pinned_stats*": C.c_void_p,
     "vz_raw_control_state*": C.c_void_p, "const vz_attention_wires_args*": C.c_void_p,
-    "float*": C.POINTER(C.c_float), "const vzb_layer_job*": C.c_void_p,
+    "float*": C.POINTER(C.c_float), "const vzb_layer_job*": C.c_void_p, "const vzb_round_job*": C.c_void_p,
 }
 _RESTYPES = {"int": C.c_int, "uint32_t": C.c_uint32, "void": None, "const char*": C.c_char_p}
 
@@ -148,6 +148,7 @@ def load_host_library():
         L.vzh_close.argtypes = [vp]
         L.vzh_set_fused.argtypes = [vp, C.c_int]
         L.vzh_set_scheduled.argtypes = [vp, C.c_int]
+        L.vzh_set_batched.argtypes = [vp, C.c_int]
         L.vzh_context.restype = vp
         L.vzh_context.argtypes = [vp]
         L.vzh_stats.argtypes = [vp, vp, C.c_char_p, sz]
@@ -281,7 +282,7 @@ def fpstream_u64(seed: bytes, domain: int, n: int) -> np.ndarray:
 class Prover:
     """Resident protocol drivers of libvolta_accel.so on their own context."""
 
-    def __init__(self, policy: int = 1, fused: bool = True, scheduled: bool = True):
+    def __init__(self, policy: int = 1, fused: bool = True, scheduled: bool = True, batched: bool = True):
         self.host = load_host_library()
         load_cuda_library()  # same dlopen handle as the host library's
         err = C.create_string_buffer(1024)
@@ -291,6 +292,7 @@ class Prover:
         self.backend = CudaBackend(ctx=self.host.vzh_context(self.h))
         self.host.vzh_set_fused(self.h, 1 if fused else 0)
         self.host.vzh_set_scheduled(self.h, 1 if scheduled else 0)
+        self.host.vzh_set_batched(self.h, 1 if batched else 0)
 
     def close(self):
         if self.h:

@@ -1431,3 +1431,191 @@ extern "C" int volta_b200_logup_fold_round_il_into_device(void* raw, uint64_t p_
     if (launch_reduce_wide<4>(c, ev, vector_len / 4, store_epi<4>(m))) return -1;
     return finish_msg(c, kOpLogup, m);
 }
+
+// ===========================================================================
+// Extension: round steps of several fraction-tree layers in one launch
+// ===========================================================================
+
+namespace {
+
+constexpr int kBatchJobs = 24;
+constexpr unsigned kBatchCounterBase = 64;  // per-job counters in the counter workspace
+
+enum BatchKind : uint32_t { kBatchRoundIL = 0, kBatchFoldRoundIL = 1, kBatchFoldRound = 2, kBatchFold = 3 };
+
+struct BatchJob {
+    uint32_t kind;
+    uint32_t block0, blocks;  // CTA range [block0, block0 + blocks)
+    size_t items;
+    const Fp2 *in0, *in1, *in2, *in3;
+    Fp2 *out0, *out1, *out2, *out3;
+    const Fp2* s;
+    Fp2 r;
+    Fp2* msg;
+};
+
+struct RoundBatch {
+    BatchJob job[kBatchJobs];
+    uint32_t count;
+};
+
+// Grid reduction over the `blocks` CTAs of one job (bidx = this CTA's index
+// within the job): the same last-CTA-finishes scheme as grid_finish.
+template <int K, class Epi>
+__device__ __forceinline__ void job_finish(Acc<K> a, Fp2* partials, unsigned* counter, unsigned blocks,
+                                           unsigned bidx, const Epi& epi) {
+    a = block_sum<K>(a);
+    if (blocks == 1) {
+        if (threadIdx.x == 0) epi(a);
+        return;
+    }
+    __shared__ bool last;
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) st2(partials + static_cast<size_t>(bidx) * K + k, a.v[k]);
+        __threadfence();
+        last = atomicAdd(counter, 1u) == blocks - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    Acc<K> t;
+    t.zero();
+    for (unsigned b = threadIdx.x; b < blocks; b += blockDim.x) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const ulonglong2 v = __ldcg(reinterpret_cast<const ulonglong2*>(partials + static_cast<size_t>(b) * K + k));
+            t.v[k] = f2add(t.v[k], Fp2{v.x, v.y});
+        }
+    }
+    t = block_sum<K>(t);
+    if (threadIdx.x == 0) {
+        epi(t);
+        *counter = 0;
+    }
+}
+
+struct MsgStoreEpi {
+    Fp2* out;
+    __device__ __forceinline__ void operator()(const Acc<4>& a) const {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) out[k] = a.v[k];
+    }
+};
+
+// CTA b runs the job whose range holds b: a grid-stride loop over that
+// job's items with the job's own CTA count as the stride, then the job's
+// grid reduction.  Fold-only jobs skip the reduction.
+__global__ void __launch_bounds__(kReduceThreads) logup_round_batch_kernel(const __grid_constant__ RoundBatch batch,
+                                                                          Fp2* partials, unsigned* counters) {
+    unsigned j = 0;
+    while (j + 1 < batch.count && blockIdx.x >= batch.job[j + 1].block0) ++j;
+    const BatchJob& jb = batch.job[j];
+    const unsigned bidx = blockIdx.x - jb.block0;
+    const size_t stride = static_cast<size_t>(jb.blocks) * blockDim.x;
+    const size_t first = static_cast<size_t>(bidx) * blockDim.x + threadIdx.x;
+    if (jb.kind == kBatchFold) {
+        for (size_t i = first; i < jb.items; i += stride) {
+            Fp2 x0, x1;
+            fold4_pair(jb.in0, jb.out0, i, jb.r, x0, x1);
+            fold4_pair(jb.in1, jb.out1, i, jb.r, x0, x1);
+            fold4_pair(jb.in2, jb.out2, i, jb.r, x0, x1);
+            fold4_pair(jb.in3, jb.out3, i, jb.r, x0, x1);
+        }
+        return;
+    }
+    Fp2W w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) f2w_zero(w[k]);
+    if (jb.kind == kBatchRoundIL) {
+        const LogupEvalIL ev{jb.in0, jb.in1, jb.s};
+        for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+    } else if (jb.kind == kBatchFoldRoundIL) {
+        const LogupFoldEvalIL ev{jb.in0, jb.in1, jb.s, jb.out0, jb.out1, jb.out2, jb.out3, jb.r};
+        for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+    } else {
+        const LogupFoldEval ev{jb.in0, jb.in1, jb.in2, jb.in3, jb.s, jb.out0, jb.out1, jb.out2, jb.out3, jb.r};
+        for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+    }
+    Acc<4> acc;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc.v[k] = f2w_reduce(w[k]);
+    job_finish<4>(acc, partials + static_cast<size_t>(jb.block0) * 4, counters + j, jb.blocks, bidx,
+                  MsgStoreEpi{jb.msg});
+}
+
+}  // namespace
+
+extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_job* jobs, size_t count) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !jobs || !count || count > static_cast<size_t>(kBatchJobs))
+        return fail_message(c, "invalid LogUp round batch (1 to 24 jobs)");
+    RoundBatch batch{};
+    batch.count = static_cast<uint32_t>(count);
+    size_t total = 0;
+    for (size_t j = 0; j < count; ++j) {
+        const vzb_round_job& q = jobs[j];
+        BatchJob& d = batch.job[j];
+        const size_t len = q.len;
+        d.kind = q.kind;
+        if (q.kind > kBatchFold) return fail_message(c, "invalid LogUp round batch job kind");
+        const bool il = q.kind <= kBatchFoldRoundIL, fold = q.kind != kBatchRoundIL;
+        if (len < (fold ? 4u : 2u) || (len & (fold ? 3 : 1)))
+            return fail_message(c, "invalid LogUp round batch job length");
+        if (q.r[0] >= kP || q.r[1] >= kP) return fail_message(c, "LogUp round batch challenge is not canonical");
+        d.r = Fp2{q.r[0], q.r[1]};
+        void* p[4] = {nullptr, nullptr, nullptr, nullptr};
+        if (il) {
+            for (int k = 0; k < 2; ++k)
+                if (region_elems(c, q.in_id[k], q.in_offset[0], 2 * len, sizeof(Fp2), &p[k])) return -1;
+        } else {
+            for (int k = 0; k < 4; ++k)
+                if (region_elems(c, q.in_id[k], q.in_offset[k], len, sizeof(Fp2), &p[k])) return -1;
+        }
+        d.in0 = static_cast<const Fp2*>(p[0]);
+        d.in1 = static_cast<const Fp2*>(p[1]);
+        d.in2 = static_cast<const Fp2*>(p[2]);
+        d.in3 = static_cast<const Fp2*>(p[3]);
+        if (fold) {
+            void* o[4];
+            for (int k = 0; k < 4; ++k)
+                if (region_elems(c, q.out_id[k], q.out_offset[k], len / 2, sizeof(Fp2), &o[k])) return -1;
+            d.out0 = static_cast<Fp2*>(o[0]);
+            d.out1 = static_cast<Fp2*>(o[1]);
+            d.out2 = static_cast<Fp2*>(o[2]);
+            d.out3 = static_cast<Fp2*>(o[3]);
+        }
+        d.items = fold ? len / 4 : len / 2;
+        if (q.kind != kBatchFold) {
+            void *sv = nullptr, *mv = nullptr;
+            if (region_elems(c, q.s_id, q.s_offset, d.items, sizeof(Fp2), &sv) ||
+                region_elems(c, q.msg_id, q.msg_offset, 4, sizeof(Fp2), &mv))
+                return -1;
+            d.s = static_cast<const Fp2*>(sv);
+            d.msg = static_cast<Fp2*>(mv);
+        }
+        total += d.items;
+    }
+    // CTAs in proportion to the items (at least one per job, at most one
+    // per kReduceThreads items), about 4 per SM in all
+    const size_t target = static_cast<size_t>(c->sm_count) * 4;
+    uint32_t next = 0;
+    for (size_t j = 0; j < count; ++j) {
+        BatchJob& d = batch.job[j];
+        const size_t need = (d.items + kReduceThreads - 1) / kReduceThreads;
+        size_t share = (target * d.items + total - 1) / total;
+        if (share < 1) share = 1;
+        d.block0 = next;
+        d.blocks = static_cast<uint32_t>(need < share ? need : share);
+        next += d.blocks;
+    }
+    // partials: 4 Fp2 per CTA within the workspace (SMs x 8 CTAs x 9 Fp2)
+    if (static_cast<size_t>(next) * 4 > static_cast<size_t>(c->sm_count) * 8 * 9)
+        return fail_message(c, "LogUp round batch exceeds the reduction workspace");
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    logup_round_batch_kernel<<<next, kReduceThreads, 0, c->stream>>>(batch, ws<Fp2>(c, kWsPartials),
+                                                                     ws<unsigned>(c, kWsCounter) + kBatchCounterBase);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpLogup, 0, 0);
+}

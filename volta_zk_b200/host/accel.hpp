@@ -87,6 +87,11 @@ class Backend {
     // the messages).  Off: the reference's round-by-round call sequence.
     void set_scheduled(bool on) { scheduled_ = on; }
     bool scheduled() const { return scheduled_; }
+    // Scheduled LogUp sides: run the round steps of all large layers as
+    // cross-layer batches (volta_b200_logup_round_batch_device) when the
+    // library has it.  Off: layer after layer.
+    void set_batched(bool on) { batched_ = on; }
+    bool batched() const { return batched_; }
     void* ctx() const { return ctx_; }
     [[noreturn]] void raise(const char* what) const;
     void check(int rc, const char* what) const {
@@ -110,6 +115,7 @@ class Backend {
     ExtApi* ext_ = nullptr;
     ExtApi* ext_loaded_ = nullptr;
     bool scheduled_ = false;
+    bool batched_ = true;
     void* ctx_ = nullptr;
 };
 

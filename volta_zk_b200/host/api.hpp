@@ -26,6 +26,7 @@ struct ExtApi {
     decltype(&::volta_b200_triple_tail_device) triple_tail = nullptr;
     decltype(&::volta_b200_logup_round_il_into_device) logup_round_il = nullptr;
     decltype(&::volta_b200_logup_fold_round_il_into_device) logup_fold_round_il = nullptr;
+    decltype(&::volta_b200_logup_round_batch_device) logup_round_batch = nullptr;
 };
 
 }  // namespace vzh

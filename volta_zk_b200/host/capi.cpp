@@ -57,6 +57,10 @@ void vzh_set_fused(void* h, int on) { static_cast<Backend*>(h)->set_fused(on != 
 // protocol); 0: one synchronised message per round, as the reference calls.
 void vzh_set_scheduled(void* h, int on) { static_cast<Backend*>(h)->set_scheduled(on != 0); }
 
+// on != 0 (default): scheduled LogUp sides run the round steps of their large
+// layers as cross-layer batches; 0: layer after layer.
+void vzh_set_batched(void* h, int on) { static_cast<Backend*>(h)->set_batched(on != 0); }
+
 void* vzh_context(void* h) { return static_cast<Backend*>(h)->ctx(); }
 
 int vzh_stats(void* h, vz_raw_stats* out, char* err, size_t len) {

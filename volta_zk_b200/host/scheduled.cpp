@@ -13,6 +13,7 @@
 //
 // Nothing waits on the GPU between rounds, so the GPU runs the rounds back to
 // back instead of idling for a host round trip per round.
+#include <algorithm>
 #include <cstring>
 
 #include "protocol.hpp"
@@ -21,6 +22,8 @@ namespace vzh {
 
 // Vectors at most this long finish in one CTA (volta_b200_*_tail / layers).
 constexpr size_t kTailLen = 2048;
+// Jobs per volta_b200_logup_round_batch_device call.
+constexpr size_t kRoundBatchMax = 24;
 
 TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
                                        FpStream& tx) {
@@ -189,6 +192,23 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
         }
     }
     std::vector<vzb_layer_job> jobs;  // launched together after every large round is enqueued
+    // Cross-layer batches: with every claim point and challenge known, the
+    // large layers are independent, so step t of every layer runs in one
+    // launch (plan[layer][t]); the buffers they use live until the end.
+    const bool batch_on = jobs_on && X.logup_round_batch && b.batched();
+    std::vector<std::vector<vzb_round_job>> plan;
+    auto tail_job = [&](const uint64_t v[4], size_t l, size_t j0) {
+        vzb_layer_job jb{};
+        for (int k = 0; k < 4; ++k) jb.v_id[k] = v[k];
+        jb.rounds = (l - shard_bits) - j0;
+        jb.point_id = pts;
+        jb.point_offset = pts_off[l] + j0;
+        jb.r_id = rbuf;
+        jb.r_offset = r_off[l] + j0;
+        jb.out_id = msgs;
+        jb.out_offset = moff[l] + 4 * j0;
+        jobs.push_back(jb);
+    };
     for (size_t l = shard_bits; l < depth; ++l) {
         Owned layer(b);
         const size_t L = l - shard_bits;  // local rounds
@@ -198,7 +218,7 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
         size_t child_off = child_len - 1;
         const bool small = jobs_on && vector_len <= kTailLen;
         if (l + 1 == depth) {  // the leaf layer's children are the materialised leaves
-            Owned& keep = small ? own : layer;  // a job reads them after this loop
+            Owned& keep = (small || batch_on) ? own : layer;  // a job or batch reads them after this loop
             src_p = keep.add(b.alloc(n_local * sizeof(Fp2)));
             src_q = keep.add(b.alloc(n_local * sizeof(Fp2)));
             b.check(A.volta_cuda_logup_materialize_leaves_device(ctx, leaf, 0, mult, 0, n_local, alpha1,
@@ -229,8 +249,68 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
                     "fp2_deinterleave_device");
             continue;
         }
-        const uint64_t suffix = layer.add(b.alloc(((size_t{1} << L) - 1) * sizeof(Fp2)));
+        const uint64_t suffix = (batch_on ? own : layer).add(b.alloc(((size_t{1} << L) - 1) * sizeof(Fp2)));
         b.check(A.volta_cuda_logup_suffix_eq_device(ctx, pts, pts_off[l], L, suffix, 0), "logup_suffix_eq_device");
+        if (batch_on) {  // vector_len > kTailLen here: L >= 12
+            std::vector<vzb_round_job> steps;
+            auto challenge = [&](vzb_round_job& q, size_t j) {
+                q.r[0] = sch.r[l][j].c0;
+                q.r[1] = sch.r[l][j].c1;
+            };
+            // round 0 and (fold 0 + round 1) on the interleaved children
+            vzb_round_job q{};
+            q.kind = 0;
+            q.in_id[0] = src_p;
+            q.in_id[1] = src_q;
+            q.in_offset[0] = child_off;
+            q.len = vector_len;
+            q.s_id = suffix;
+            q.s_offset = (size_t{1} << (L - 1)) - 1;
+            q.msg_id = msgs;
+            q.msg_offset = moff[l];
+            steps.push_back(q);
+            size_t len = vector_len / 2;
+            uint64_t v[4];
+            for (auto& x : v) x = own.add(b.alloc(len * sizeof(Fp2)));
+            q.kind = 1;
+            challenge(q, 0);
+            for (int k = 0; k < 4; ++k) q.out_id[k] = v[k];
+            q.s_offset = (size_t{1} << (L - 2)) - 1;
+            q.msg_offset = moff[l] + 4;
+            steps.push_back(q);
+            if (len <= kTailLen) {
+                tail_job(v, l, 1);  // (the job rewrites the round-1 message)
+            } else {
+                for (size_t j = 1;; ++j) {  // fold j + round j + 1
+                    const size_t half = len / 2;
+                    uint64_t nv[4];
+                    for (auto& x : nv) x = own.add(b.alloc(half * sizeof(Fp2)));
+                    vzb_round_job f{};
+                    for (int k = 0; k < 4; ++k) {
+                        f.in_id[k] = v[k];
+                        f.out_id[k] = nv[k];
+                    }
+                    f.len = len;
+                    challenge(f, j);
+                    if (half <= kTailLen) {  // fold only; rounds j + 1 .. L - 1 in one CTA
+                        f.kind = 3;
+                        steps.push_back(f);
+                        tail_job(nv, l, j + 1);
+                        break;
+                    }
+                    f.kind = 2;
+                    f.s_id = suffix;
+                    f.s_offset = (size_t{1} << (L - 2 - j)) - 1;
+                    f.msg_id = msgs;
+                    f.msg_offset = moff[l] + 4 * (j + 1);
+                    steps.push_back(f);
+                    for (int k = 0; k < 4; ++k) v[k] = nv[k];
+                    len = half;
+                }
+            }
+            plan.push_back(std::move(steps));
+            continue;
+        }
         size_t len = vector_len;
         uint64_t v[4];
         size_t j_first = 0;
@@ -323,6 +403,17 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
             }
             len = half;
         }
+    }
+    size_t steps_max = 0;
+    for (const auto& st : plan) steps_max = std::max(steps_max, st.size());
+    std::vector<vzb_round_job> batch;
+    for (size_t t = 0; t < steps_max; ++t) {
+        batch.clear();
+        for (const auto& st : plan)
+            if (t < st.size()) batch.push_back(st[t]);
+        for (size_t o = 0; o < batch.size(); o += kRoundBatchMax)
+            b.check(X.logup_round_batch(ctx, batch.data() + o, std::min(kRoundBatchMax, batch.size() - o)),
+                    "volta_b200_logup_round_batch_device");
     }
     if (!jobs.empty()) b.check(X.logup_layers(ctx, jobs.data(), jobs.size()), "volta_b200_logup_layers_device");
     std::vector<Fp2> m(msg_total);
