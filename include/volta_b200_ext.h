@@ -150,6 +150,22 @@ typedef struct vzb_round_job {
 } vzb_round_job;
 int volta_b200_logup_round_batch_device(void* ctx, const vzb_round_job* jobs, size_t count);
 
+/*
+ * Suffix-eq tables of several layers at once: job j writes exactly what
+ * volta_cuda_logup_suffix_eq_device(ctx, points_id, points_offset, point_len,
+ * out_id, out_offset) writes (table k = eq over the last k of the point_len
+ * coordinates, at offset 2^k - 1).  Any number of jobs; 2 + ceil(max(L - 12,
+ * 0) / 11) launches in all.  Outputs must not overlap.
+ */
+typedef struct vzb_suffix_job {
+    uint64_t points_id;
+    size_t points_offset;
+    size_t point_len;
+    uint64_t out_id;
+    size_t out_offset;
+} vzb_suffix_job;
+int volta_b200_logup_suffix_eq_batch_device(void* ctx, const vzb_suffix_job* jobs, size_t count);
+
 /* All rounds of a triple-product sumcheck on three resident tables of len
  * (<= 2^11, a power of two) entries; challenges at (r_id, r_offset).  Output:
  * 3 messages per round, then the 3 final values. */

@@ -154,3 +154,43 @@ def test_round_batch_rejects_bad_jobs(be):
     assert run_batch(be, [job]) == 0, be.last_error()
     for i in ids:
         be.free(i)
+
+
+class SuffixJob(C.Structure):
+    """include/volta_b200_ext.h: vzb_suffix_job."""
+
+    _fields_ = [("points_id", C.c_uint64), ("points_offset", C.c_size_t), ("point_len", C.c_size_t),
+                ("out_id", C.c_uint64), ("out_offset", C.c_size_t)]
+
+
+def test_suffix_eq_batch_matches_single_layer_calls(be):
+    """Every job of one batch equals volta_cuda_logup_suffix_eq_device on the
+    same point (tables of 1 to 2^23 entries, two outer-product bands)."""
+    lens = [1, 5, 11, 12, 13, 16, 23, 24]
+    rng = np.random.default_rng(11)
+    pts = rand_fp2(rng, 3 + sum(lens))
+    pid = be.upload_new(pts)
+    jobs, singles, off = [], [], 3
+    for L in lens:
+        total = (1 << L) - 1
+        out_off = int(rng.integers(0, 4))
+        batch_out, single_out = be.alloc(16 * (out_off + total)), be.alloc(16 * total)
+        jobs.append(SuffixJob(pid, off, L, batch_out, out_off))
+        be.call("logup_suffix_eq_device", pid, off, L, single_out, 0)
+        singles.append((batch_out, out_off, single_out, total))
+        off += L
+    arr = (SuffixJob * len(jobs))(*jobs)
+    assert be.lib.volta_b200_logup_suffix_eq_batch_device(be.ctx, C.cast(arr, C.c_void_p), len(jobs)) == 0, \
+        be.last_error()
+    for batch_out, out_off, single_out, total in singles:
+        assert np.array_equal(be.download_fp2(batch_out, total, offset=out_off), be.download_fp2(single_out, total))
+        be.free(batch_out)
+        be.free(single_out)
+    # a job beyond its output buffer is rejected and the context stays usable
+    small = be.alloc(16 * 7)
+    bad = (SuffixJob * 1)(SuffixJob(pid, 3, 4, small, 0))
+    assert be.lib.volta_b200_logup_suffix_eq_batch_device(be.ctx, C.cast(bad, C.c_void_p), 1) == -1
+    ok = (SuffixJob * 1)(SuffixJob(pid, 3, 3, small, 0))
+    assert be.lib.volta_b200_logup_suffix_eq_batch_device(be.ctx, C.cast(ok, C.c_void_p), 1) == 0, be.last_error()
+    be.free(small)
+    be.free(pid)

@@ -950,6 +950,120 @@ extern "C" int volta_cuda_logup_suffix_eq_device(void* raw, uint64_t points_id, 
     return op_finish(c, kOpLogup, 0, 0);
 }
 
+// Outer-product tables of several layers in one launch: table t (entries
+// 2^bits) is out_t[i] = lo_t[i & (2^11 - 1)] * hi_t[i >> 11]; its CTAs are
+// [block0, block0 + blocks), in proportion to its size.
+constexpr int kMaxOuterBatch = 256;
+struct OuterJob {
+    const Fp2* lo;
+    const Fp2* hi;
+    Fp2* out;
+    size_t entries;
+    uint32_t block0, blocks;
+};
+struct OuterBatch {
+    OuterJob t[kMaxOuterBatch];
+    int count;
+};
+
+__global__ void __launch_bounds__(256) eq_outer_batch_kernel(const __grid_constant__ OuterBatch b) {
+    int lo = 0, hi = b.count - 1;  // last table whose first CTA is <= blockIdx.x
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (b.t[mid].block0 <= blockIdx.x) lo = mid;
+        else hi = mid - 1;
+    }
+    const OuterJob& t = b.t[lo];
+    const size_t stride = static_cast<size_t>(t.blocks) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x - t.block0) * blockDim.x + threadIdx.x; i < t.entries; i += stride)
+        st2(t.out + i, f2mul(ldg2(t.lo + (i & (kEqTile - 1))), ldg2(t.hi + (i >> kEqTileBits))));
+}
+
+extern "C" int volta_b200_logup_suffix_eq_batch_device(void* raw, const vzb_suffix_job* jobs, size_t count) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !jobs || !count) return fail_message(c, "invalid suffix-eq batch");
+    std::vector<const Fp2*> pts(count);
+    std::vector<Fp2*> outs(count);
+    std::vector<size_t> low_base(count, 0);
+    size_t lows_total = 0;
+    int max_len = 0;
+    for (size_t j = 0; j < count; ++j) {
+        const vzb_suffix_job& q = jobs[j];
+        if (!q.point_len || q.point_len >= 63) return fail_message(c, "invalid resident suffix-eq geometry");
+        void *p = nullptr, *o = nullptr;
+        if (region_elems(c, q.points_id, q.points_offset, q.point_len, sizeof(Fp2), &p) ||
+            region_elems(c, q.out_id, q.out_offset, (size_t{1} << q.point_len) - 1, sizeof(Fp2), &o))
+            return -1;
+        pts[j] = static_cast<const Fp2*>(p);
+        outs[j] = static_cast<Fp2*>(o);
+        const int L = static_cast<int>(q.point_len);
+        low_base[j] = lows_total;
+        if (L > kEqTileBits + 1) lows_total += static_cast<size_t>(L - kEqTileBits - 1) * kEqTile;
+        max_len = std::max(max_len, L);
+    }
+    if (lows_total && ensure_ws(c, kWsScratch, lows_total * sizeof(Fp2))) return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    Fp2* lows = lows_total ? ws<Fp2>(c, kWsScratch) : nullptr;
+    // tables of <= 11 coordinates and the 11-coordinate low factors of the
+    // larger ones, one CTA each, kMaxEqJobs per launch
+    EqJobs small{};
+    auto flush_small = [&]() -> int {
+        if (!small.count) return 0;
+        eq_small_kernel<<<small.count, 256, 0, c->stream>>>(small);
+        VZB_LAUNCHED(c);
+        small.count = 0;
+        return 0;
+    };
+    for (size_t j = 0; j < count; ++j) {
+        const int L = static_cast<int>(jobs[j].point_len);
+        const Fp2* point = pts[j];
+        for (int k = 0; k < L; ++k) {
+            if (small.count == kMaxEqJobs && flush_small()) return -1;
+            if (k <= kEqTileBits)
+                small.job[small.count++] = EqJob{point + (L - k), k, Fp2{1, 0}, outs[j] + ((size_t{1} << k) - 1), nullptr};
+            else
+                small.job[small.count++] = EqJob{point + (L - k), kEqTileBits, Fp2{1, 0},
+                                                 lows + low_base[j] + static_cast<size_t>(k - kEqTileBits - 1) * kEqTile,
+                                                 nullptr};
+        }
+    }
+    if (flush_small()) return -1;
+    // bands of 11 table sizes across all jobs: table k is the outer product
+    // of its low factor and table k - 11 (complete after the previous band)
+    for (int band = kEqTileBits + 1; band < max_len; band += kEqTileBits) {
+        OuterBatch ob{};
+        size_t total = 0;
+        for (size_t j = 0; j < count; ++j) {
+            const int L = static_cast<int>(jobs[j].point_len);
+            for (int k = band; k < L && k < band + kEqTileBits; ++k) {
+                if (ob.count == kMaxOuterBatch) return fail_message(c, "suffix-eq batch has too many large tables");
+                OuterJob& t = ob.t[ob.count++];
+                t.lo = lows + low_base[j] + static_cast<size_t>(k - kEqTileBits - 1) * kEqTile;
+                t.hi = outs[j] + ((size_t{1} << (k - kEqTileBits)) - 1);
+                t.out = outs[j] + ((size_t{1} << k) - 1);
+                t.entries = size_t{1} << k;
+                total += t.entries;
+            }
+        }
+        if (!ob.count) continue;
+        const size_t target = static_cast<size_t>(c->sm_count) * 8;
+        uint32_t next = 0;
+        for (int i = 0; i < ob.count; ++i) {
+            OuterJob& t = ob.t[i];
+            const size_t need = (t.entries + 255) / 256;
+            size_t share = (target * t.entries + total - 1) / total;
+            if (share < 1) share = 1;
+            t.block0 = next;
+            t.blocks = static_cast<uint32_t>(std::min(need, share));
+            next += t.blocks;
+        }
+        eq_outer_batch_kernel<<<next, 256, 0, c->stream>>>(ob);
+        VZB_LAUNCHED(c);
+    }
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpLogup, 0, 0);
+}
+
 extern "C" int volta_cuda_fp2_fold_rows_device(void* raw, uint64_t in_id, size_t in_off,
                                                size_t rows, size_t len, Fp2 r, uint64_t out_id,
                                                size_t out_off) {

@@ -121,6 +121,8 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         dlsym(handle_, "volta_b200_logup_fold_round_il_into_device"));
     ext_loaded_->logup_round_batch = reinterpret_cast<decltype(ext_loaded_->logup_round_batch)>(
         dlsym(handle_, "volta_b200_logup_round_batch_device"));
+    ext_loaded_->logup_suffix_eq_batch = reinterpret_cast<decltype(ext_loaded_->logup_suffix_eq_batch)>(
+        dlsym(handle_, "volta_b200_logup_suffix_eq_batch_device"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

@@ -27,6 +27,7 @@ struct ExtApi {
     decltype(&::volta_b200_logup_round_il_into_device) logup_round_il = nullptr;
     decltype(&::volta_b200_logup_fold_round_il_into_device) logup_fold_round_il = nullptr;
     decltype(&::volta_b200_logup_round_batch_device) logup_round_batch = nullptr;
+    decltype(&::volta_b200_logup_suffix_eq_batch_device) logup_suffix_eq_batch = nullptr;
 };
 
 }  // namespace vzh

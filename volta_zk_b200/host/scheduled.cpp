@@ -197,6 +197,7 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
     // launch (plan[layer][t]); the buffers they use live until the end.
     const bool batch_on = jobs_on && X.logup_round_batch && b.batched();
     std::vector<std::vector<vzb_round_job>> plan;
+    std::vector<vzb_suffix_job> suffix_jobs;  // built together before the first batch
     auto tail_job = [&](const uint64_t v[4], size_t l, size_t j0) {
         vzb_layer_job jb{};
         for (int k = 0; k < 4; ++k) jb.v_id[k] = v[k];
@@ -250,7 +251,11 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
             continue;
         }
         const uint64_t suffix = (batch_on ? own : layer).add(b.alloc(((size_t{1} << L) - 1) * sizeof(Fp2)));
-        b.check(A.volta_cuda_logup_suffix_eq_device(ctx, pts, pts_off[l], L, suffix, 0), "logup_suffix_eq_device");
+        if (batch_on && X.logup_suffix_eq_batch)
+            suffix_jobs.push_back(vzb_suffix_job{pts, pts_off[l], L, suffix, 0});
+        else
+            b.check(A.volta_cuda_logup_suffix_eq_device(ctx, pts, pts_off[l], L, suffix, 0),
+                    "logup_suffix_eq_device");
         if (batch_on) {  // vector_len > kTailLen here: L >= 12
             std::vector<vzb_round_job> steps;
             auto challenge = [&](vzb_round_job& q, size_t j) {
@@ -404,6 +409,9 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
             len = half;
         }
     }
+    if (!suffix_jobs.empty())
+        b.check(X.logup_suffix_eq_batch(ctx, suffix_jobs.data(), suffix_jobs.size()),
+                "volta_b200_logup_suffix_eq_batch_device");
     size_t steps_max = 0;
     for (const auto& st : plan) steps_max = std::max(steps_max, st.size());
     std::vector<vzb_round_job> batch;
