@@ -132,11 +132,17 @@ int volta_b200_logup_layers_device(void* ctx, const vzb_layer_job* jobs, size_t 
  *   kind 3: volta_cuda_logup_fold4_device (the fold of kind 2, no round).
  * Kinds 0-2 read the suffix-eq table at (s_id, s_offset) and write the four
  * raw accumulators at (msg_id, msg_offset).  r = (c0, c1) of the challenge.
+ * flags bit 0 (VZB_ROUND_P_ONE): every numerator entry (P, or the p0 and p1
+ * vectors) equals 1, as in the leaf layer of a side without multiplicities
+ * (logup materialize_leaves).  The numerators are then neither read nor
+ * written, except that kind 3 writes ones into out_id[0] and out_id[1]; the
+ * results equal those of the same job on all-one numerators.
  * Outputs of different jobs must not overlap each other or any input.
  */
+#define VZB_ROUND_P_ONE 1u
 typedef struct vzb_round_job {
     uint32_t kind;
-    uint32_t reserved;
+    uint32_t flags;
     uint64_t in_id[4];
     size_t in_offset[4];
     size_t len;

@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 class RoundJob(C.Structure):
     """include/volta_b200_ext.h: vzb_round_job."""
 
-    _fields_ = [("kind", C.c_uint32), ("reserved", C.c_uint32), ("in_id", C.c_uint64 * 4),
+    _fields_ = [("kind", C.c_uint32), ("flags", C.c_uint32), ("in_id", C.c_uint64 * 4),
                 ("in_offset", C.c_size_t * 4), ("len", C.c_size_t), ("r", C.c_uint64 * 2),
                 ("out_id", C.c_uint64 * 4), ("out_offset", C.c_size_t * 4), ("s_id", C.c_uint64),
                 ("s_offset", C.c_size_t), ("msg_id", C.c_uint64), ("msg_offset", C.c_size_t)]
@@ -43,8 +43,8 @@ def run_batch(be, jobs):
 class Case:
     """One job with its inputs, outputs and the oracle's expectation."""
 
-    def __init__(self, be, oracle, rng, kind, length, msg_id, msg_slot):
-        self.kind, self.length = kind, length
+    def __init__(self, be, oracle, rng, kind, length, msg_id, msg_slot, p_one=False):
+        self.kind, self.length, self.p_one = kind, length, p_one
         il = kind <= 1
         fold = kind != 0
         self.r = tuple(int(x) for x in rand_fp2(rng, 1)[0])
@@ -54,20 +54,26 @@ class Case:
         self.ids = []
         job = RoundJob()
         job.kind, job.len = kind, length
+        job.flags = 1 if p_one else 0
         job.r[0], job.r[1] = self.r
+        ones = lambda n: np.tile(np.array([[1, 0]], dtype=np.uint64), (n, 1))  # noqa: E731
         if il:
             child_off = int(rng.integers(0, 3))
-            self.P = rand_fp2(rng, child_off + 2 * length)
+            self.P = ones(child_off + 2 * length) if p_one else rand_fp2(rng, child_off + 2 * length)
             self.Q = rand_fp2(rng, child_off + 2 * length)
-            job.in_id[0], job.in_id[1] = be.upload_new(self.P), be.upload_new(self.Q)
+            # with all-one numerators P is not read: no buffer is passed
+            job.in_id[0] = 0 if p_one else be.upload_new(self.P)
+            job.in_id[1] = be.upload_new(self.Q)
             job.in_offset[0] = child_off
-            self.ids += [job.in_id[0], job.in_id[1]]
+            self.ids += [x for x in (job.in_id[0], job.in_id[1]) if x]
             ch_p, ch_q = self.P[child_off:], self.Q[child_off:]
             # deinterleaved p0, p1, q0, q1
             v = [np.ascontiguousarray(x) for x in (ch_p[0::2], ch_p[1::2], ch_q[0::2], ch_q[1::2])]
         else:
-            v = [rand_fp2(rng, length) for _ in range(4)]
+            v = [ones(length) if (p_one and k < 2) else rand_fp2(rng, length) for k in range(4)]
             for k in range(4):
+                if p_one and k < 2:
+                    continue
                 off = int(rng.integers(0, 3))
                 job.in_id[k] = be.upload_new(np.concatenate([rand_fp2(rng, off), v[k]]))
                 job.in_offset[k] = off
@@ -77,10 +83,12 @@ class Case:
             self.out_off = []
             for k in range(4):
                 off = int(rng.integers(0, 3))
+                self.out_off.append(off)
+                if p_one and k < 2 and kind != 3:  # numerator outputs are not written
+                    continue
                 job.out_id[k] = be.alloc(16 * (off + length // 2))
                 job.out_offset[k] = off
                 self.ids.append(job.out_id[k])
-                self.out_off.append(off)
             after = self.folded
         else:
             after = v
@@ -96,6 +104,8 @@ class Case:
     def check(self, be, msgs):
         if self.kind != 0:
             for k in range(4):
+                if self.p_one and k < 2 and self.kind != 3:
+                    continue
                 got = be.download_fp2(self.job.out_id[k], self.length // 2, offset=self.out_off[k])
                 assert np.array_equal(got, self.folded[k]), (self.kind, self.length, k)
         if self.expect_msg is not None:
@@ -128,6 +138,27 @@ def test_round_batch_matches_single_layer_calls(be, oracle, spec):
     be.free(msg_id)
 
 
+@pytest.mark.parametrize("spec", [
+    [(0, 2)], [(1, 4)], [(2, 4)], [(3, 4)],
+    [(0, 1 << 16), (1, 1 << 15), (2, 1 << 14), (3, 1 << 12), (2, 1 << 18)],
+], ids=["round-il", "fold-round-il", "fold-round", "fold", "mixed-5"])
+def test_round_batch_all_one_numerators(be, oracle, spec):
+    """flags = VZB_ROUND_P_ONE: the same results as on all-one numerators,
+    without reading them (kind 3 writes the folded ones)."""
+    rng = np.random.default_rng(len(spec) * 77 + spec[0][1])
+    msg_id = be.alloc(16 * 4 * (len(spec) + 1))
+    cases = [Case(be, oracle, rng, kind, length, msg_id, j, p_one=True) for j, (kind, length) in enumerate(spec)]
+    # an ordinary job shares the launch
+    cases.append(Case(be, oracle, rng, 2, 4096, msg_id, len(spec)))
+    assert run_batch(be, [c.job for c in cases]) == 0, be.last_error()
+    msgs = be.download_fp2(msg_id, 4 * (len(spec) + 1))
+    for c in cases:
+        c.check(be, msgs)
+    for c in cases:
+        c.free(be)
+    be.free(msg_id)
+
+
 def test_round_batch_rejects_bad_jobs(be):
     ids = [be.alloc(16 * 64) for _ in range(10)]
     job = RoundJob()
@@ -139,6 +170,9 @@ def test_round_batch_rejects_bad_jobs(be):
     bad = RoundJob.from_buffer_copy(job)
     bad.kind = 4
     assert run_batch(be, [bad]) == -1 and "kind" in be.last_error()
+    bad = RoundJob.from_buffer_copy(job)
+    bad.flags = 2
+    assert run_batch(be, [bad]) == -1 and "flags" in be.last_error()
     bad = RoundJob.from_buffer_copy(job)
     bad.len = 6
     assert run_batch(be, [bad]) == -1 and "length" in be.last_error()

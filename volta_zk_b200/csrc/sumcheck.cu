@@ -1550,6 +1550,60 @@ extern "C" int volta_b200_logup_fold_round_il_into_device(void* raw, uint64_t p_
 // Extension: round steps of several fraction-tree layers in one launch
 // ===========================================================================
 
+// Round terms when every numerator entry is 1 (a = b = 1 at every point):
+// a d + b c = c + d, so the two inner products per point disappear.
+// c0, c1, d0, d1 canonical.
+__device__ __forceinline__ void q_round_terms(Fp2 c0, Fp2 c1, Fp2 d0, Fp2 d1, Fp2 si, Fp2W* w) {
+    const Fp2 t0 = d2add(c0, d0), t1 = d2add(c1, d1);
+    const Fp2 t2 = d2add_weak(t1, d2sub(t1, t0));  // (c2 + d2) = 2 (c1 + d1) - (c0 + d0)
+    const Fp2 c2 = d2add_weak(c1, d2sub(c1, c0)), d2 = d2add_weak(d1, d2sub(d1, d0));
+    f2w_mac(w[0], si, t0);
+    f2w_mac(w[1], si, t2);
+    f2w_mac(w[2], si, d2mul(c0, d0));
+    f2w_mac(w[3], si, d2mul(c2, d2));
+}
+
+// kind 0 with all-one numerators: only the Q children are read
+struct QEvalIL {
+    const Fp2 *Q, *s;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        const Fp2 c0 = ldcs2(Q + 4 * i), d0 = ldcs2(Q + 4 * i + 1), c1 = ldcs2(Q + 4 * i + 2), d1 = ldcs2(Q + 4 * i + 3);
+        q_round_terms(c0, c1, d0, d1, ldg2(s + i), w);
+    }
+};
+
+// kind 1 with all-one numerators: folds and writes q0, q1 only
+struct QFoldEvalIL {
+    const Fp2 *Q, *s;
+    Fp2 *o2, *o3;
+    Fp2 r;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        Fp2 y[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[k] = ldcs2(Q + 8 * i + k);
+        const Fp2 c0 = d2fold(y[0], y[2], r), c1 = d2fold(y[4], y[6], r);
+        const Fp2 d0 = d2fold(y[1], y[3], r), d1 = d2fold(y[5], y[7], r);
+        st2(o2 + 2 * i, c0);
+        st2(o2 + 2 * i + 1, c1);
+        st2(o3 + 2 * i, d0);
+        st2(o3 + 2 * i + 1, d1);
+        q_round_terms(c0, c1, d0, d1, ldg2(s + i), w);
+    }
+};
+
+// kind 2 with all-one numerators
+struct QFoldEval {
+    const Fp2 *q0, *q1, *s;
+    Fp2 *o2, *o3;
+    Fp2 r;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        Fp2 c0, c1, d0, d1;
+        fold4_pair(q0, o2, i, r, c0, c1);
+        fold4_pair(q1, o3, i, r, d0, d1);
+        q_round_terms(c0, c1, d0, d1, ldg2(s + i), w);
+    }
+};
+
 namespace {
 
 constexpr int kBatchJobs = 24;
@@ -1559,6 +1613,7 @@ enum BatchKind : uint32_t { kBatchRoundIL = 0, kBatchFoldRoundIL = 1, kBatchFold
 
 struct BatchJob {
     uint32_t kind;
+    uint32_t p_one;           // numerators all 1: not read, not written (kind 3 writes ones)
     uint32_t block0, blocks;  // CTA range [block0, block0 + blocks)
     size_t items;
     const Fp2 *in0, *in1, *in2, *in3;
@@ -1631,8 +1686,16 @@ __global__ void __launch_bounds__(kReduceThreads) logup_round_batch_kernel(const
     if (jb.kind == kBatchFold) {
         for (size_t i = first; i < jb.items; i += stride) {
             Fp2 x0, x1;
-            fold4_pair(jb.in0, jb.out0, i, jb.r, x0, x1);
-            fold4_pair(jb.in1, jb.out1, i, jb.r, x0, x1);
+            if (jb.p_one) {
+                const Fp2 one{1, 0};
+                st2(jb.out0 + 2 * i, one);
+                st2(jb.out0 + 2 * i + 1, one);
+                st2(jb.out1 + 2 * i, one);
+                st2(jb.out1 + 2 * i + 1, one);
+            } else {
+                fold4_pair(jb.in0, jb.out0, i, jb.r, x0, x1);
+                fold4_pair(jb.in1, jb.out1, i, jb.r, x0, x1);
+            }
             fold4_pair(jb.in2, jb.out2, i, jb.r, x0, x1);
             fold4_pair(jb.in3, jb.out3, i, jb.r, x0, x1);
         }
@@ -1641,7 +1704,18 @@ __global__ void __launch_bounds__(kReduceThreads) logup_round_batch_kernel(const
     Fp2W w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) f2w_zero(w[k]);
-    if (jb.kind == kBatchRoundIL) {
+    if (jb.p_one) {
+        if (jb.kind == kBatchRoundIL) {
+            const QEvalIL ev{jb.in1, jb.s};
+            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+        } else if (jb.kind == kBatchFoldRoundIL) {
+            const QFoldEvalIL ev{jb.in1, jb.s, jb.out2, jb.out3, jb.r};
+            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+        } else {
+            const QFoldEval ev{jb.in2, jb.in3, jb.s, jb.out2, jb.out3, jb.r};
+            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+        }
+    } else if (jb.kind == kBatchRoundIL) {
         const LogupEvalIL ev{jb.in0, jb.in1, jb.s};
         for (size_t i = first; i < jb.items; i += stride) ev(i, w);
     } else if (jb.kind == kBatchFoldRoundIL) {
@@ -1673,17 +1747,21 @@ extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_jo
         const size_t len = q.len;
         d.kind = q.kind;
         if (q.kind > kBatchFold) return fail_message(c, "invalid LogUp round batch job kind");
+        if (q.flags & ~VZB_ROUND_P_ONE) return fail_message(c, "invalid LogUp round batch job flags");
+        const bool one = (q.flags & VZB_ROUND_P_ONE) != 0;
+        d.p_one = one ? 1u : 0u;
         const bool il = q.kind <= kBatchFoldRoundIL, fold = q.kind != kBatchRoundIL;
         if (len < (fold ? 4u : 2u) || (len & (fold ? 3 : 1)))
             return fail_message(c, "invalid LogUp round batch job length");
         if (q.r[0] >= kP || q.r[1] >= kP) return fail_message(c, "LogUp round batch challenge is not canonical");
         d.r = Fp2{q.r[0], q.r[1]};
         void* p[4] = {nullptr, nullptr, nullptr, nullptr};
+        // with all-one numerators P (kinds 0, 1) or p0, p1 (kinds 2, 3) are not read
         if (il) {
-            for (int k = 0; k < 2; ++k)
+            for (int k = one ? 1 : 0; k < 2; ++k)
                 if (region_elems(c, q.in_id[k], q.in_offset[0], 2 * len, sizeof(Fp2), &p[k])) return -1;
         } else {
-            for (int k = 0; k < 4; ++k)
+            for (int k = one ? 2 : 0; k < 4; ++k)
                 if (region_elems(c, q.in_id[k], q.in_offset[k], len, sizeof(Fp2), &p[k])) return -1;
         }
         d.in0 = static_cast<const Fp2*>(p[0]);
@@ -1691,8 +1769,10 @@ extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_jo
         d.in2 = static_cast<const Fp2*>(p[2]);
         d.in3 = static_cast<const Fp2*>(p[3]);
         if (fold) {
-            void* o[4];
-            for (int k = 0; k < 4; ++k)
+            void* o[4] = {nullptr, nullptr, nullptr, nullptr};
+            // the numerator outputs are written only by kind 3 (ones)
+            const int k0 = (one && q.kind != kBatchFold) ? 2 : 0;
+            for (int k = k0; k < 4; ++k)
                 if (region_elems(c, q.out_id[k], q.out_offset[k], len / 2, sizeof(Fp2), &o[k])) return -1;
             d.out0 = static_cast<Fp2*>(o[0]);
             d.out1 = static_cast<Fp2*>(o[1]);

@@ -257,6 +257,11 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
             b.check(A.volta_cuda_logup_suffix_eq_device(ctx, pts, pts_off[l], L, suffix, 0),
                     "logup_suffix_eq_device");
         if (batch_on) {  // vector_len > kTailLen here: L >= 12
+            // the leaf layer of a side without multiplicities has all-one
+            // numerators (materialize_leaves): its jobs skip them, except
+            // that the fold feeding the one-CTA tail writes the ones
+            const uint32_t flags =
+                (l + 1 == depth && !mult && vector_len / 2 > kTailLen) ? VZB_ROUND_P_ONE : 0u;
             std::vector<vzb_round_job> steps;
             auto challenge = [&](vzb_round_job& q, size_t j) {
                 q.r[0] = sch.r[l][j].c0;
@@ -265,6 +270,7 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
             // round 0 and (fold 0 + round 1) on the interleaved children
             vzb_round_job q{};
             q.kind = 0;
+            q.flags = flags;
             q.in_id[0] = src_p;
             q.in_id[1] = src_q;
             q.in_offset[0] = child_off;
@@ -275,8 +281,8 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
             q.msg_offset = moff[l];
             steps.push_back(q);
             size_t len = vector_len / 2;
-            uint64_t v[4];
-            for (auto& x : v) x = own.add(b.alloc(len * sizeof(Fp2)));
+            uint64_t v[4] = {0, 0, 0, 0};
+            for (int k = flags ? 2 : 0; k < 4; ++k) v[k] = own.add(b.alloc(len * sizeof(Fp2)));
             q.kind = 1;
             challenge(q, 0);
             for (int k = 0; k < 4; ++k) q.out_id[k] = v[k];
@@ -288,16 +294,18 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
             } else {
                 for (size_t j = 1;; ++j) {  // fold j + round j + 1
                     const size_t half = len / 2;
-                    uint64_t nv[4];
-                    for (auto& x : nv) x = own.add(b.alloc(half * sizeof(Fp2)));
+                    const bool last = half <= kTailLen;  // fold only, then the one-CTA tail
+                    uint64_t nv[4] = {0, 0, 0, 0};
+                    for (int k = (flags && !last) ? 2 : 0; k < 4; ++k) nv[k] = own.add(b.alloc(half * sizeof(Fp2)));
                     vzb_round_job f{};
+                    f.flags = flags;
                     for (int k = 0; k < 4; ++k) {
                         f.in_id[k] = v[k];
                         f.out_id[k] = nv[k];
                     }
                     f.len = len;
                     challenge(f, j);
-                    if (half <= kTailLen) {  // fold only; rounds j + 1 .. L - 1 in one CTA
+                    if (last) {  // fold only; rounds j + 1 .. L - 1 in one CTA
                         f.kind = 3;
                         steps.push_back(f);
                         tail_job(nv, l, j + 1);
