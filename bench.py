@@ -4,8 +4,9 @@ on B200 through the drop-in C ABI.
 
 One step = one config-1 proof:
   * triple-product sumcheck over three 2^24-entry tables (uniform Fp from
-    FpStream([0x51;32], t), lifted to Fp2), 24 rounds, challenges from a
-    private transcript FpStream([0x5A;32], u64::MAX);
+    FpStream([0x51;32], t), i.e. Fp2 tables with c1 = 0, held as Fp columns),
+    24 rounds, challenges from a private transcript FpStream([0x5A;32],
+    u64::MAX);
   * LogUp lookup argument of 2^24 queries into the 2^16-entry int16 GELU
     table (queries idx_i = FpStream([0x4C;32], 1).next_bits(16), f_i =
     table[idx_i], mult = histogram), challenges FpStream([0x4C;32], 0x1004).
@@ -292,6 +293,61 @@ def gemm_leg(args, be, peaks):
                          "peak_source": "2 x measured bf16 dense" if "bf16_tflops" in peaks else "2 x fallback bf16"}}
 
 
+class RoundJob(__import__("ctypes").Structure):
+    """include/volta_b200_ext.h: vzb_round_job."""
+
+    _C = __import__("ctypes")
+    _fields_ = [("kind", _C.c_uint32), ("flags", _C.c_uint32), ("in_id", _C.c_uint64 * 4),
+                ("in_offset", _C.c_size_t * 4), ("len", _C.c_size_t), ("r", _C.c_uint64 * 2),
+                ("out_id", _C.c_uint64 * 4), ("out_offset", _C.c_size_t * 4), ("s_id", _C.c_uint64),
+                ("s_offset", _C.c_size_t), ("msg_id", _C.c_uint64), ("msg_offset", _C.c_size_t)]
+
+
+def logup_step0_replica(be, log2_queries: int, reps: int = 10):
+    """The proof's largest launch, replicated on seeded data of the same
+    shapes: step 0 of the query side's cross-layer round batch, i.e. round 0
+    on the interleaved children of every layer with more than 2^11 entries
+    per vector (layer L: 2 x 2^L children of P and Q, a 2^(L-1)-entry suffix
+    table); the leaf layer's numerators are all 1 and not read.  Returns
+    (average launch ms, algorithmic bytes per launch, jobs)."""
+    import ctypes as C
+
+    jobs, bufs, nbytes = [], [], 0
+    msg = be.alloc(16 * 4 * 32)
+    bufs.append(msg)
+    for L in range(12, log2_queries):
+        vlen = 1 << L
+        leaf = L == log2_queries - 1
+        q = be.alloc(16 * 2 * vlen)
+        be.call("chacha8_prover_secret_fp_rows_device", q, 0, SUMCHECK_SEED, 100 + L, 1, 4 * vlen)
+        p = 0
+        if not leaf:
+            p = be.alloc(16 * 2 * vlen)
+            be.call("chacha8_prover_secret_fp_rows_device", p, 0, SUMCHECK_SEED, 200 + L, 1, 4 * vlen)
+        s = be.alloc(16 * (vlen // 2))
+        be.call("chacha8_prover_secret_fp_rows_device", s, 0, SUMCHECK_SEED, 300 + L, 1, vlen)
+        bufs += [x for x in (p, q, s) if x]
+        j = RoundJob()
+        j.kind, j.flags, j.len = 0, 1 if leaf else 0, vlen
+        j.in_id[0], j.in_id[1] = p, q
+        j.s_id, j.msg_id, j.msg_offset = s, msg, 4 * len(jobs)
+        jobs.append(j)
+        nbytes += (0 if leaf else 32 * vlen) + 32 * vlen + 16 * (vlen // 2)
+    arr = (RoundJob * len(jobs))(*jobs)
+    call = lambda: be.check(be.lib.volta_b200_logup_round_batch_device(be.ctx, C.cast(arr, C.c_void_p), len(jobs)),
+                            "logup_round_batch")  # noqa: E731
+    for _ in range(3):
+        call()
+    be.mark(4)
+    for _ in range(reps):
+        call()
+    be.mark(5)
+    ms = be.elapsed_ms(4, 5) / reps
+    for x in bufs:
+        be.free(x)
+    return ms, nbytes, len(jobs)
+
+
 def run_b200(args, rank, world, local_rank):
     import torch
 
@@ -317,14 +373,13 @@ def run_b200(args, rank, world, local_rank):
         raise SystemExit("the GPU count must be a power of two that divides the tables")
 
     # ---- inputs resident in HBM (generated on the device through the ABI) ----
+    # the tables are Fp values (FpStream rows): kept as Fp columns, proved
+    # without lifting them to Fp2 (volta_b200_triple_*_fp rounds)
     tables = []
-    col = be.alloc(8 * n)
     for t in range(3):
+        col = be.alloc(8 * n)
         be.call("chacha8_prover_secret_fp_rows_device", col, 0, SUMCHECK_SEED, t, 1, n)
-        tid = be.alloc(16 * n)
-        be.call("base_broadcast_fp2_device", col, 0, tid, 0, n, 1, 2)
-        tables.append(tid)
-    be.free(col)
+        tables.append(col)
     f, table, mult = logup_inputs(args.log2_queries, args.log2_table, accel.fpstream_u64)
     cap = proof_words(n_f, n_t)
     if world == 1:
@@ -335,8 +390,8 @@ def run_b200(args, rank, world, local_rank):
         nl = n // world
         shard_tables = []
         for tid in tables:
-            sl = be.alloc(16 * nl)
-            be.call("resident_copy_rows", tid, 16 * nl * rank, 16 * nl, sl, 0, 16 * nl, 1, 16 * nl)
+            sl = be.alloc(8 * nl)
+            be.call("resident_copy_rows", tid, 8 * nl * rank, 8 * nl, sl, 0, 8 * nl, 1, 8 * nl)
             shard_tables.append(sl)
         fs, ts = slice(rank * n_f // world, (rank + 1) * n_f // world), slice(rank * n_t // world,
                                                                               (rank + 1) * n_t // world)
@@ -347,10 +402,10 @@ def run_b200(args, rank, world, local_rank):
 
     def step():
         if world == 1:
-            msgs, finals = prover.triple_sumcheck(tables[0], tables[1], tables[2], n, TRANSCRIPT_SEED)
+            msgs, finals = prover.triple_sumcheck_fp(tables[0], tables[1], tables[2], n, TRANSCRIPT_SEED)
             proof = prover.logup_prove(f_col, n_f, t_col, n_t, m_col, LOGUP_SEED, LOGUP_DOMAIN, cap)
         else:
-            msgs, finals = sharded.triple_sumcheck(*shard_tables, n, TRANSCRIPT_SEED)
+            msgs, finals = sharded.triple_sumcheck(*shard_tables, n, TRANSCRIPT_SEED, base=True)
             proof = sharded.logup_prove(f_col, n_f, t_col, n_t, m_col, LOGUP_SEED, LOGUP_DOMAIN)
         return msgs, finals, proof
 
@@ -384,18 +439,16 @@ def run_b200(args, rank, world, local_rank):
     # ---- e2e through the C ABI with host buffers ---------------------------
     e2e = None
     if not args.no_e2e:
-        # the user's tables are Fp columns (8 B per entry); they are lifted to
-        # Fp2 on the device (base_broadcast_fp2_device) after the upload.  With
-        # N GPUs every rank uploads only its slices.
+        # the user's tables are Fp columns (8 B per entry), uploaded as such and
+        # proved without a lift.  With N GPUs every rank uploads only its slices.
         nl, nfl, ntl = n // world, n_f // world, n_t // world
-        host_cols = [np.ascontiguousarray(be.download_fp2(t, n)[rank * nl:(rank + 1) * nl, 0]) for t in tables]
+        host_cols = [np.ascontiguousarray(be.download(t, 8 * n)[rank * nl:(rank + 1) * nl]) for t in tables]
         pinned = [torch.from_numpy(x.view(np.int64)).pin_memory() for x in host_cols]
         fcol_h = torch.from_numpy(np.ascontiguousarray(embed_i16(f)[rank * nfl:(rank + 1) * nfl]).view(np.int64)).pin_memory()
         tcol_h = torch.from_numpy(np.ascontiguousarray(embed_i16(table)[rank * ntl:(rank + 1) * ntl]).view(np.int64)).pin_memory()
         mult_h = torch.from_numpy(np.ascontiguousarray(mult[rank * ntl:(rank + 1) * ntl]).astype(np.int32)).pin_memory()
         ups = [be.alloc(8 * nl) for _ in range(3)] + [be.alloc(8 * nfl), be.alloc(8 * ntl), be.alloc(4 * ntl)]
-        lifted = [be.alloc(16 * nl) for _ in range(3)]
-        bufs = ups + lifted
+        bufs = ups
         h2d = 3 * 8 * n + 8 * n_f + 8 * n_t + 4 * n_t  # whole job
         d2h = (16 * (3 * args.log2_sumcheck + 3) + 16 * cap) * world
 
@@ -403,13 +456,11 @@ def run_b200(args, rank, world, local_rank):
             for buf, t in zip(ups, pinned + [fcol_h, tcol_h, mult_h]):
                 be.check(be.lib.volta_cuda_resident_upload(be.ctx, buf, 0, t.data_ptr(),
                                                            t.numel() * t.element_size()), "upload")
-            for col, tid in zip(ups[:3], lifted):
-                be.call("base_broadcast_fp2_device", col, 0, tid, 0, nl, 1, 2)
             if world == 1:
-                prover.triple_sumcheck(lifted[0], lifted[1], lifted[2], n, TRANSCRIPT_SEED)
+                prover.triple_sumcheck_fp(ups[0], ups[1], ups[2], n, TRANSCRIPT_SEED)
                 prover.logup_prove(ups[3], n_f, ups[4], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN, cap)
             else:
-                sharded.triple_sumcheck(lifted[0], lifted[1], lifted[2], n, TRANSCRIPT_SEED)
+                sharded.triple_sumcheck(ups[0], ups[1], ups[2], n, TRANSCRIPT_SEED, base=True)
                 sharded.logup_prove(ups[3], n_f, ups[4], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN)
 
         e2e_step()
@@ -424,31 +475,50 @@ def run_b200(args, rank, world, local_rank):
         for b in bufs:
             be.free(b)
 
-    # ---- roofline of the dominant kernel: triple-product round at full size ----
-    reps = 20
-    g = np.zeros((3, 2), dtype=np.uint64)
-    gp = g.ctypes.data_as(__import__("ctypes").c_void_p)
-    mbox = be.alloc(48)
-    for _ in range(3):
-        be.call("fp2_triple_product_round_into_device", tables[0], 0, tables[1], 0, tables[2], 0, n // 2, mbox, 0)
-    be.mark(4)
-    for _ in range(reps):
-        be.call("fp2_triple_product_round_into_device", tables[0], 0, tables[1], 0, tables[2], 0, n // 2, mbox, 0)
-    be.mark(5)
-    kern_ms = be.elapsed_ms(4, 5) / reps
-    be.free(mbox)
-    alg_bytes = 3 * 16 * n
+    # ---- roofline of the dominant kernel ----------------------------------
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except Exception:
         pass
     peak = peaks.get("hbm_gbs", 6650.0)
-    achieved = alg_bytes / (kern_ms / 1e3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "fp2_triple_product_round (2^23 pairs)", "achieved": round(achieved, 1),
-                "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": None, "algorithmic_bytes": alg_bytes,
-                "avg_launch_ms": round(kern_ms, 4)}
+    batch_ms, batch_bytes, batch_jobs = logup_step0_replica(be, args.log2_queries)
+    achieved = batch_bytes / (batch_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm",
+                "kernel": f"logup_round_batch_kernel: step 0 of the 2^{args.log2_queries}-query side "
+                          f"({batch_jobs} layers in one launch, the proof's largest launch)",
+                "achieved": round(achieved, 1), "peak": peak,
+                "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": None, "algorithmic_bytes": batch_bytes,
+                "avg_launch_ms": round(batch_ms, 4)}
+    # the triple-product round kernels, at full size (three 2^24 tables)
+    mbox = be.alloc(48)
+    lifted = [be.alloc(16 * n) for _ in range(3)]
+    for col, tid in zip(tables, lifted):
+        be.call("base_broadcast_fp2_device", col, 0, tid, 0, n, 1, 2)
+    fp_round = be.lib.volta_b200_triple_round_fp_into_device
+    runs = {
+        "triple_round_fp (2^23 pairs, Fp columns: the proof's round 0)":
+            (lambda: be.check(fp_round(be.ctx, *tables, n // 2, mbox, 0), "triple_round_fp"), 3 * 8 * n),
+        "fp2_triple_product_round (2^23 pairs, Fp2 tables: the reference entry point)":
+            (lambda: be.call("fp2_triple_product_round_into_device", lifted[0], 0, lifted[1], 0, lifted[2], 0,
+                             n // 2, mbox, 0), 3 * 16 * n),
+    }
+    kernels = {}
+    for name, (call, nbytes) in runs.items():
+        for _ in range(3):
+            call()
+        be.mark(4)
+        for _ in range(20):
+            call()
+        be.mark(5)
+        kms = be.elapsed_ms(4, 5) / 20
+        kernels[name] = {"avg_launch_ms": round(kms, 4), "algorithmic_bytes": nbytes,
+                         "hbm_gbs": round(nbytes / (kms / 1e3) / 1e9, 1),
+                         "frac": round(nbytes / (kms / 1e3) / 1e9 / peak, 4)}
+    roofline["other_kernels"] = kernels
+    for x in lifted + [mbox]:
+        be.free(x)
 
     ligero = None
     if not args.no_ligero:
@@ -484,7 +554,7 @@ def run_b200(args, rank, world, local_rank):
                                    f"vs 2^{args.log2_table} table",
                        "parallelism": f"one proof sharded over {world} GPU(s) (top index bits; one NCCL "
                                       f"all-gather per sumcheck)" if world > 1 else "one proof on one GPU",
-                       "l2": "inputs larger than L2 (805 MB tables)",
+                       "l2": "inputs larger than L2 (402 MB of Fp tables, 134 MB of queries)",
                        "timing_policy": "wall-only counters"},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "gpu_launches": launches,
             "clocks": clocks.summary(),

@@ -212,6 +212,23 @@ int volta_b200_triple_tail_device(void* ctx, uint64_t a_id, uint64_t b_id, uint6
 int volta_b200_triple_product_round_noalloc(const vz_fp2* a, const vz_fp2* b, const vz_fp2* c,
                                             size_t pairs, vz_fp2* output, void* stream);
 
+/*
+ * Triple-product rounds on base-field tables: a, b, c are Fp columns (u64,
+ * canonical), i.e. Fp2 tables whose c1 is 0 (such as FpStream rows).
+ *   triple_round_fp: volta_cuda_fp2_triple_product_round_into_device on the
+ *     2 * pairs entries of each column (the message's c1 parts are 0);
+ *   triple_fold_round_fp: the fold of each column with r into Fp2 tables of
+ *     len / 2 entries (ao, bo, co) and the next round's message on them, as
+ *     volta_b200_triple_fold_round_into_device on the lifted tables.
+ * Reading 8 bytes per entry and multiplying in Fp, they are exact drop-ins
+ * for the first two rounds of a sumcheck whose tables are base-field values.
+ */
+int volta_b200_triple_round_fp_into_device(void* ctx, uint64_t a_id, uint64_t b_id, uint64_t c_id, size_t pairs,
+                                           uint64_t out_id, size_t out_offset);
+int volta_b200_triple_fold_round_fp_into_device(void* ctx, uint64_t a_id, uint64_t b_id, uint64_t c_id, size_t len,
+                                                vz_fp2 r, uint64_t ao_id, uint64_t bo_id, uint64_t co_id,
+                                                uint64_t out_id, size_t out_offset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,29 @@ def test_triple_sumcheck_matches_oracle(prover, oracle, log2n):
         be.free(i)
 
 
+@pytest.mark.parametrize("log2n", [1, 2, 3, 10, 12, 13, 16])
+def test_triple_sumcheck_fp_columns_match_oracle(prover, oracle, log2n):
+    """Fp columns (tables with c1 = 0) give the proof of the lifted tables."""
+    n = 1 << log2n
+    seed = bytes([0x51] * 32)
+    cols = [oracle.chacha_fp_rows(seed, t, 1, n)[0] for t in range(3)]
+    lifted = []
+    for col in cols:
+        x = np.zeros((n, 2), dtype=np.uint64)
+        x[:, 0] = col
+        lifted.append(x)
+    be = prover.backend
+    ids = [be.upload_new(np.ascontiguousarray(col)) for col in cols]
+    chal = bytes([0x5A] * 32)
+    msgs, finals = prover.triple_sumcheck_fp(ids[0], ids[1], ids[2], n, chal)
+    emsgs, efinals = oracle.triple_sumcheck(*lifted, chal)
+    assert np.array_equal(msgs, emsgs)
+    assert np.array_equal(finals, efinals)
+    assert np.array_equal(be.download(ids[0], 8 * n), cols[0])  # the columns are left untouched
+    for i in ids:
+        be.free(i)
+
+
 @pytest.mark.parametrize("log2f,log2t", [(1, 1), (4, 3), (10, 8), (14, 10), (16, 13)])
 def test_logup_prove_matches_oracle(prover, oracle, log2f, log2t):
     nf, nt = 1 << log2f, 1 << log2t

@@ -21,18 +21,26 @@ def prover():
     p.close()
 
 
+@pytest.mark.parametrize("base", [False, True], ids=["fp2-tables", "fp-columns"])
 @pytest.mark.parametrize("log2n,G", [(1, 2), (6, 2), (12, 4), (16, 8)])
-def test_sharded_triple(prover, oracle, log2n, G):
+def test_sharded_triple(prover, oracle, log2n, G, base):
     n = 1 << log2n
     seed = bytes([0x5A] * 32)
     rng = np.random.default_rng(log2n)
     a, b, c = (rng.integers(0, 2**64 - 2**32 + 1, size=(n, 2), dtype=np.uint64) for _ in range(3))
+    if base:  # Fp columns: tables with c1 = 0
+        for x in (a, b, c):
+            x[:, 1] = 0
     be = prover.backend
     parts = []
     for g in range(G):
         sl = slice(g * n // G, (g + 1) * n // G)
-        ids = [be.upload_new(np.ascontiguousarray(x[sl])) for x in (a, b, c)]
-        m, f = prover.triple_sumcheck(*ids, n // G, seed)
+        if base:
+            ids = [be.upload_new(np.ascontiguousarray(x[sl, 0])) for x in (a, b, c)]
+            m, f = prover.triple_sumcheck_fp(*ids, n // G, seed)
+        else:
+            ids = [be.upload_new(np.ascontiguousarray(x[sl])) for x in (a, b, c)]
+            m, f = prover.triple_sumcheck(*ids, n // G, seed)
         parts.append(np.concatenate([m, f]))
         for i in ids:
             be.free(i)

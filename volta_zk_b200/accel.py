@@ -155,6 +155,7 @@ def load_host_library():
         L.vzh_stats.argtypes = [vp, vp, C.c_char_p, sz]
         L.vzh_reset_stats.argtypes = [vp, C.c_char_p, sz]
         L.vzh_triple_sumcheck.argtypes = [vp, u64, u64, u64, sz, C.c_char_p, vp, vp, C.c_char_p, sz]
+        L.vzh_triple_sumcheck_fp.argtypes = [vp, u64, u64, u64, sz, C.c_char_p, vp, vp, C.c_char_p, sz]
         L.vzh_logup_prove.argtypes = [vp, u64, sz, u64, sz, u64, C.c_char_p, u64, vp, sz,
                                       C.POINTER(C.c_size_t), C.c_char_p, sz]
         L.vzh_ligero_commit_open.argtypes = [vp, C.c_char_p, sz, sz, sz, sz, C.c_char_p, vp, vp, vp, vp,
@@ -316,6 +317,17 @@ class Prover:
         finals = np.zeros((3, 2), dtype=np.uint64)
         err = C.create_string_buffer(1024)
         rc = self.host.vzh_triple_sumcheck(self.h, a, b, c, n, seed, _ptr(msgs), _ptr(finals), err, 1024)
+        self._err(rc, err)
+        return msgs, finals
+
+    def triple_sumcheck_fp(self, a: int, b: int, c: int, n: int, seed: bytes):
+        """The same proof on three resident columns of n canonical Fp values
+        (tables whose c1 is 0), without lifting them to Fp2 first."""
+        rounds = n.bit_length() - 1
+        msgs = np.zeros((3 * rounds, 2), dtype=np.uint64)
+        finals = np.zeros((3, 2), dtype=np.uint64)
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_triple_sumcheck_fp(self.h, a, b, c, n, seed, _ptr(msgs), _ptr(finals), err, 1024)
         self._err(rc, err)
         return msgs, finals
 

@@ -120,6 +120,59 @@ struct TripleFoldEval {
     }
 };
 
+// Round 0 of a triple product over base-field tables (Fp values, i.e. Fp2
+// values with c1 = 0): the products stay in Fp (two base products per point
+// instead of two Fp2 products) and the message has c1 = 0.
+struct TripleEvalFp {
+    const uint64_t *a, *b, *c;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        const uint64_t a0 = __ldcs(a + 2 * i), a1 = __ldcs(a + 2 * i + 1);
+        const uint64_t b0 = __ldcs(b + 2 * i), b1 = __ldcs(b + 2 * i + 1);
+        const uint64_t c0 = __ldcs(c + 2 * i), c1 = __ldcs(c + 2 * i + 1);
+        const uint64_t da = dsub(a1, a0), db = dsub(b1, b0), dc = dsub(c1, c0);
+        const uint64_t a2 = dadd_weak(a1, da), b2 = dadd_weak(b1, db), c2 = dadd_weak(c1, dc);
+        const uint64_t a3 = dadd_weak(a2, da), b3 = dadd_weak(b2, db), c3 = dadd_weak(c2, dc);
+        wadd(w[0].c0, dmul_wide(dmul(a0, b0), c0));
+        wadd(w[1].c0, dmul_wide(dmul(a2, b2), c2));
+        wadd(w[2].c0, dmul_wide(dmul(a3, b3), c3));
+    }
+};
+
+// Fold of a base-field pair with an Fp2 challenge: x0 + r (x1 - x0) =
+// (x0 + r.c0 d, r.c1 d), d = x1 - x0 in Fp.
+__device__ __forceinline__ Fp2 fold_fp(uint64_t x0, uint64_t x1, Fp2 r) {
+    const uint64_t d = dsub(x1, x0);
+    return Fp2{dadd(x0, dmul(r.c0, d)), dmul(r.c1, d)};
+}
+
+// Fold of base-field tables into Fp2 tables fused with the next round (as
+// TripleFoldEval; inputs 4i .. 4i + 3, outputs 2i, 2i + 1).
+struct TripleFoldEvalFp {
+    const uint64_t *a, *b, *c;
+    Fp2 *ao, *bo, *co;
+    Fp2 r;
+    __device__ __forceinline__ void fold(const uint64_t* in, Fp2* out, size_t i, Fp2& x0, Fp2& x1) const {
+        const uint64_t v0 = __ldcs(in + 4 * i), v1 = __ldcs(in + 4 * i + 1);
+        const uint64_t v2 = __ldcs(in + 4 * i + 2), v3 = __ldcs(in + 4 * i + 3);
+        x0 = fold_fp(v0, v1, r);
+        x1 = fold_fp(v2, v3, r);
+        st2(out + 2 * i, x0);
+        st2(out + 2 * i + 1, x1);
+    }
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        Fp2 a0, a1, b0, b1, c0, c1;
+        fold(a, ao, i, a0, a1);
+        fold(b, bo, i, b0, b1);
+        fold(c, co, i, c0, c1);
+        const Fp2 da = d2sub(a1, a0), db = d2sub(b1, b0), dc = d2sub(c1, c0);
+        const Fp2 a2 = d2add_weak(a1, da), b2 = d2add_weak(b1, db), c2 = d2add_weak(c1, dc);
+        const Fp2 a3 = d2add_weak(a2, da), b3 = d2add_weak(b2, db), c3 = d2add_weak(c2, dc);
+        f2w_mac(w[0], d2mul(a0, b0), c0);
+        f2w_mac(w[1], d2mul(a2, b2), c2);
+        f2w_mac(w[2], d2mul(a3, b3), c3);
+    }
+};
+
 struct LogupFoldEval {
     const Fp2 *p0, *p1, *q0, *q1, *s;
     Fp2 *o0, *o1, *o2, *o3;
@@ -1475,6 +1528,45 @@ extern "C" int volta_b200_triple_fold_round_into_device(void* raw, uint64_t a_id
                                                         uint64_t co_id, uint64_t out_id, size_t out_offset) {
     return triple_fold_round(static_cast<Context*>(raw), a_id, b_id, c_id, len, r, ao_id, bo_id, co_id, nullptr,
                              out_id, out_offset);
+}
+
+// Triple-product rounds on base-field tables (extensions).
+extern "C" int volta_b200_triple_round_fp_into_device(void* raw, uint64_t a_id, uint64_t b_id, uint64_t c_id,
+                                                      size_t pairs, uint64_t out_id, size_t out_offset) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !pairs) return fail_message(c, "invalid base-field triple round geometry");
+    void *a = nullptr, *b = nullptr, *cc = nullptr, *dev = nullptr;
+    if (region_elems(c, a_id, 0, 2 * pairs, sizeof(uint64_t), &a) ||
+        region_elems(c, b_id, 0, 2 * pairs, sizeof(uint64_t), &b) ||
+        region_elems(c, c_id, 0, 2 * pairs, sizeof(uint64_t), &cc) ||
+        region_elems(c, out_id, out_offset, 3, sizeof(Fp2), &dev))
+        return -1;
+    const MsgOut o = msg_out(c, static_cast<Fp2*>(dev), nullptr, 3);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    TripleEvalFp ev{static_cast<const uint64_t*>(a), static_cast<const uint64_t*>(b), static_cast<const uint64_t*>(cc)};
+    if (launch_reduce_wide<3>(c, ev, pairs, store_epi<3>(o), 8)) return -1;
+    return finish_msg(c, kOpGemm, o);
+}
+
+extern "C" int volta_b200_triple_fold_round_fp_into_device(void* raw, uint64_t a_id, uint64_t b_id, uint64_t c_id,
+                                                           size_t len, Fp2 r, uint64_t ao_id, uint64_t bo_id,
+                                                           uint64_t co_id, uint64_t out_id, size_t out_offset) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || len < 4 || (len & 3)) return fail_message(c, "invalid base-field triple fold-round geometry");
+    if (r.c0 >= kP || r.c1 >= kP) return fail_message(c, "triple fold-round challenge is not canonical");
+    void *a = nullptr, *b = nullptr, *cc = nullptr, *ao = nullptr, *bo = nullptr, *co = nullptr, *dev = nullptr;
+    if (region_elems(c, a_id, 0, len, sizeof(uint64_t), &a) || region_elems(c, b_id, 0, len, sizeof(uint64_t), &b) ||
+        region_elems(c, c_id, 0, len, sizeof(uint64_t), &cc) || region_elems(c, ao_id, 0, len / 2, sizeof(Fp2), &ao) ||
+        region_elems(c, bo_id, 0, len / 2, sizeof(Fp2), &bo) || region_elems(c, co_id, 0, len / 2, sizeof(Fp2), &co) ||
+        region_elems(c, out_id, out_offset, 3, sizeof(Fp2), &dev))
+        return -1;
+    const MsgOut o = msg_out(c, static_cast<Fp2*>(dev), nullptr, 3);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    TripleFoldEvalFp ev{static_cast<const uint64_t*>(a), static_cast<const uint64_t*>(b),
+                        static_cast<const uint64_t*>(cc), static_cast<Fp2*>(ao), static_cast<Fp2*>(bo),
+                        static_cast<Fp2*>(co), r};
+    if (launch_reduce_wide<3>(c, ev, len / 4, store_epi<3>(o), 8)) return -1;
+    return finish_msg(c, kOpGemm, o);
 }
 
 extern "C" int volta_b200_logup_fold_round_device(void* raw, uint64_t p0_id, uint64_t p1_id, uint64_t q0_id,

@@ -123,6 +123,10 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         dlsym(handle_, "volta_b200_logup_round_batch_device"));
     ext_loaded_->logup_suffix_eq_batch = reinterpret_cast<decltype(ext_loaded_->logup_suffix_eq_batch)>(
         dlsym(handle_, "volta_b200_logup_suffix_eq_batch_device"));
+    ext_loaded_->triple_round_fp = reinterpret_cast<decltype(ext_loaded_->triple_round_fp)>(
+        dlsym(handle_, "volta_b200_triple_round_fp_into_device"));
+    ext_loaded_->triple_fold_round_fp = reinterpret_cast<decltype(ext_loaded_->triple_fold_round_fp)>(
+        dlsym(handle_, "volta_b200_triple_fold_round_fp_into_device"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

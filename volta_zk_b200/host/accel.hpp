@@ -130,6 +130,12 @@ struct TripleResult {
 };
 TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
                                       FpStream& tx);
+// The same sumcheck on three device columns of n canonical Fp values (Fp2
+// tables with c1 = 0).  The scheduled driver runs rounds 0 and 1 on the base
+// columns (volta_b200_triple_*_fp extensions); otherwise the columns are
+// lifted to Fp2 (base_broadcast_fp2_device) and proved as above.  Same result.
+TripleResult triple_sumcheck_resident_fp(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
+                                         FpStream& tx);
 
 // LogUp (logup.rs:1760-1771, resident engine 995-1470): queries and table are
 // device columns of canonical Fp values (n_f and n_t entries, powers of two),

@@ -28,6 +28,8 @@ struct ExtApi {
     decltype(&::volta_b200_logup_fold_round_il_into_device) logup_fold_round_il = nullptr;
     decltype(&::volta_b200_logup_round_batch_device) logup_round_batch = nullptr;
     decltype(&::volta_b200_logup_suffix_eq_batch_device) logup_suffix_eq_batch = nullptr;
+    decltype(&::volta_b200_triple_round_fp_into_device) triple_round_fp = nullptr;
+    decltype(&::volta_b200_triple_fold_round_fp_into_device) triple_fold_round_fp = nullptr;
 };
 
 }  // namespace vzh

@@ -83,6 +83,18 @@ int vzh_triple_sumcheck(void* h, uint64_t a, uint64_t b, uint64_t c, size_t n, c
     });
 }
 
+// The same on three resident columns of n canonical Fp values (tables whose
+// c1 is 0); the messages equal those of the lifted tables.
+int vzh_triple_sumcheck_fp(void* h, uint64_t a, uint64_t b, uint64_t c, size_t n, const uint8_t* seed,
+                           vz_fp2* messages, vz_fp2* finals, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        FpStream tx(seed, UINT64_MAX);
+        TripleResult r = triple_sumcheck_resident_fp(*static_cast<Backend*>(h), a, b, c, n, tx);
+        std::memcpy(messages, r.messages.data(), r.messages.size() * sizeof(vz_fp2));
+        std::memcpy(finals, r.finals, sizeof(r.finals));
+    });
+}
+
 // LogUp proof over resident Fp columns; challenges from FpStream(seed, domain).
 int vzh_logup_prove(void* h, uint64_t f_col, size_t n_f, uint64_t t_col, size_t n_t, uint64_t mult,
                     const uint8_t* seed, uint64_t domain, vz_fp2* out, size_t cap, size_t* written,

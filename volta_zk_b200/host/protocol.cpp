@@ -198,6 +198,22 @@ TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint6
     return b.scheduled() ? triple_sumcheck_scheduled(b, a, bb, c, n, tx) : triple_sumcheck_rounds(b, a, bb, c, n, tx);
 }
 
+TripleResult triple_sumcheck_resident_fp(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
+                                         FpStream& tx) {
+    const ExtApi& X = b.ext();
+    if (b.scheduled() && X.triple_round_fp && X.triple_fold_round_fp && n >= 4)
+        return triple_sumcheck_scheduled(b, a, bb, c, n, tx, true);
+    Owned own(b);
+    uint64_t lifted[3];
+    const uint64_t cols[3] = {a, bb, c};
+    for (int t = 0; t < 3; ++t) {
+        lifted[t] = own.add(b.alloc(n * sizeof(Fp2)));
+        b.check(b.api().volta_cuda_base_broadcast_fp2_device(b.ctx(), cols[t], 0, lifted[t], 0, n, 1, 2),
+                "base_broadcast_fp2_device");
+    }
+    return triple_sumcheck_resident(b, lifted[0], lifted[1], lifted[2], n, tx);
+}
+
 std::vector<Fp2> logup_prove_resident(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col,
                                       size_t n_t, uint64_t mult, FpStream& chal) {
     const SideProver side_prover = b.scheduled() ? prove_frac_tree_scheduled : prove_frac_tree_resident;

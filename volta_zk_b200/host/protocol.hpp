@@ -65,6 +65,6 @@ struct LocalSide {
 LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_local, uint64_t alpha1,
                           size_t shard_bits, const SideSchedule& sch);
 TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
-                                       FpStream& tx);
+                                       FpStream& tx, bool base = false);
 
 }  // namespace vzh

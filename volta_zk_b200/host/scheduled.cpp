@@ -26,7 +26,7 @@ constexpr size_t kTailLen = 2048;
 constexpr size_t kRoundBatchMax = 24;
 
 TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
-                                       FpStream& tx) {
+                                       FpStream& tx, bool base) {
     const Api& A = b.api();
     const ExtApi& X = b.ext();
     void* ctx = b.ctx();
@@ -46,10 +46,24 @@ TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint
     uint64_t cur[3] = {a, bb, c};
     bool owned = false;
     size_t len = n, j = 0;
-    // large rounds: one pass each (fold of the previous round fused with the next round)
-    if (k && (!X.triple_tail || n > kTailLen))
+    if (base) {
+        // base-field columns (n >= 4): rounds 0 and 1 read them directly; the
+        // fold with r[0] writes the Fp2 tables the later rounds use (when they
+        // go to the tail, it recomputes round 1 with the same result)
+        b.check(X.triple_round_fp(ctx, a, bb, c, n / 2, msgs, 0), "volta_b200_triple_round_fp_into_device");
+        uint64_t nxt[3];
+        for (int t = 0; t < 3; ++t) nxt[t] = own.add(b.alloc((n / 2) * sizeof(Fp2)));
+        b.check(X.triple_fold_round_fp(ctx, a, bb, c, n, r[0], nxt[0], nxt[1], nxt[2], msgs, 3),
+                "volta_b200_triple_fold_round_fp_into_device");
+        for (int t = 0; t < 3; ++t) cur[t] = nxt[t];
+        owned = true;
+        len = n / 2;
+        j = 1;
+    } else if (k && (!X.triple_tail || n > kTailLen)) {
+        // large rounds: one pass each (fold of the previous round fused with the next round)
         b.check(A.volta_cuda_fp2_triple_product_round_into_device(ctx, a, 0, bb, 0, c, 0, n / 2, msgs, 0),
                 "fp2_triple_product_round_into_device");
+    }
     while (j < k && (!X.triple_tail || len > kTailLen)) {
         const size_t pairs = len / 2;
         if (pairs == 1) {  // last fold: the openings land in their slots

@@ -103,9 +103,11 @@ class ShardedProver:
         self.prover, self.rank, self.world, self.gather = prover, rank, world, all_gather
         self.s = world.bit_length() - 1
 
-    def triple_sumcheck(self, a: int, b: int, c: int, n: int, seed: bytes):
-        """a, b, c: this shard's slices (n / world entries) of the tables."""
-        msgs, finals = self.prover.triple_sumcheck(a, b, c, n // self.world, seed)
+    def triple_sumcheck(self, a: int, b: int, c: int, n: int, seed: bytes, base: bool = False):
+        """a, b, c: this shard's slices (n / world entries) of the tables;
+        base: they are Fp columns (tables whose c1 is 0) rather than Fp2."""
+        local = self.prover.triple_sumcheck_fp if base else self.prover.triple_sumcheck
+        msgs, finals = local(a, b, c, n // self.world, seed)
         parts = self.gather(np.concatenate([msgs, finals]).astype(np.uint64))
         return triple_finish(parts, n, seed)
 
