@@ -484,13 +484,17 @@ def run_b200(args, rank, world, local_rank):
     peak = peaks.get("hbm_gbs", 6650.0)
     batch_ms, batch_bytes, batch_jobs = logup_step0_replica(be, args.log2_queries)
     achieved = batch_bytes / (batch_ms / 1e3) / 1e9
+    # DRAM read + write bytes per algorithmic byte of this launch, from the ncu
+    # capture of the 2^22-query replica (profiles/logup_round_batch_step0_2p22queries.md)
+    traffic_ratio = (234.784512e6 + 4.759808e6) / 235110400
     roofline = {"bound": "hbm",
                 "kernel": f"logup_round_batch_kernel: step 0 of the 2^{args.log2_queries}-query side "
                           f"({batch_jobs} layers in one launch, the proof's largest launch)",
                 "achieved": round(achieved, 1), "peak": peak,
                 "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": None, "algorithmic_bytes": batch_bytes,
-                "avg_launch_ms": round(batch_ms, 4)}
+                "frac": round(achieved / peak, 4), "traffic": int(batch_bytes * traffic_ratio),
+                "traffic_source": "ncu capture of the 2^22-query replica, scaled by algorithmic bytes",
+                "algorithmic_bytes": batch_bytes, "avg_launch_ms": round(batch_ms, 4)}
     # the triple-product round kernels, at full size (three 2^24 tables)
     mbox = be.alloc(48)
     lifted = [be.alloc(16 * n) for _ in range(3)]
