@@ -174,9 +174,9 @@ __global__ void pack_leaf_kernel(const uint64_t* cols, const uint32_t* shifts, u
         uint64_t packed = 0;
         for (size_t c = 0; c < column_count; ++c) {
             const uint32_t s = shifts[c];
-            if (s != 0xFFFFFFFFu) packed = fadd(packed, fmul(cols[c * n + i], s < 64 ? (uint64_t{1} << s) : fpow(2, s)));
+            if (s != 0xFFFFFFFFu) packed = dadd(packed, dmul(cols[c * n + i], s < 64 ? (uint64_t{1} << s) : fpow(2, s)));
         }
-        leaf[i] = fsub(alpha0, packed);
+        leaf[i] = dsub(alpha0, packed);
     }
 }
 

@@ -17,6 +17,17 @@ namespace vzb {
 constexpr int kTreeTileBits = 11;
 constexpr int kTreeTile = 1 << kTreeTileBits;  // children per block
 
+// Parent of two fractions: p = pa qb + pb qa (one lazy sum, one reduction),
+// q = qa qb, on the carry-chain arithmetic.
+__device__ __forceinline__ void combine(Fp2 pa, Fp2 pb, Fp2 qa, Fp2 qb, Fp2& p, Fp2& q) {
+    Fp2W t;
+    f2w_zero(t);
+    f2w_mac(t, pa, qb);
+    f2w_mac(t, pb, qa);
+    p = f2w_reduce(t);
+    q = d2mul(qa, qb);
+}
+
 // Combine `levels` times starting from a child level of 2^child_bits entries.
 // first == true: children are leaves (a_i, alpha1) with numerators 1 or -mult.
 template <bool kFirst>
@@ -37,19 +48,18 @@ __global__ void __launch_bounds__(256) tree_tile_kernel(
             Fp2 pv, qv;
             if (kFirst) {
                 const uint64_t a = __ldcs(leaf + child0 + 2 * i), b = __ldcs(leaf + child0 + 2 * i + 1);
-                const uint64_t sum = fadd(a, b);
+                const uint64_t sum = dadd(a, b);
                 if (neg_mult) {
                     const uint64_t ma = __ldcs(mult + child0 + 2 * i), mb = __ldcs(mult + child0 + 2 * i + 1);
-                    pv = Fp2{fneg(fadd(fmul(ma, b), fmul(mb, a))), fneg(fmul(fadd(ma, mb), alpha1))};
+                    pv = Fp2{dsub(0, dadd(dmul(ma, b), dmul(mb, a))), dsub(0, dmul(dadd(ma, mb), alpha1))};
                 } else {
-                    pv = Fp2{sum, fadd(alpha1, alpha1)};
+                    pv = Fp2{sum, dadd(alpha1, alpha1)};
                 }
-                qv = Fp2{fadd(fmul(a, b), w7a1sq), fmul(sum, alpha1)};
+                qv = Fp2{dadd(dmul(a, b), w7a1sq), dmul(sum, alpha1)};
             } else {
                 const Fp2 pa = ldcs2(cp + child0 + 2 * i), pb = ldcs2(cp + child0 + 2 * i + 1);
                 const Fp2 qa = ldcs2(cq + child0 + 2 * i), qb = ldcs2(cq + child0 + 2 * i + 1);
-                pv = f2add(f2mul(pa, qb), f2mul(pb, qa));
-                qv = f2mul(qa, qb);
+                combine(pa, pb, qa, qb, pv, qv);
             }
             sp[i] = pv;
             sq[i] = qv;
@@ -69,8 +79,7 @@ __global__ void __launch_bounds__(256) tree_tile_kernel(
         int k = 0;
         for (size_t i = threadIdx.x; i < parents; i += blockDim.x, ++k) {
             const Fp2 pa = sp[2 * i], pb = sp[2 * i + 1], qa = sq[2 * i], qb = sq[2 * i + 1];
-            np[k] = f2add(f2mul(pa, qb), f2mul(pb, qa));
-            nq[k] = f2mul(qa, qb);
+            combine(pa, pb, qa, qb, np[k], nq[k]);
         }
         __syncthreads();
         k = 0;

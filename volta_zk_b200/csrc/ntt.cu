@@ -52,18 +52,19 @@ __device__ __forceinline__ uint64_t mul_pow2(uint64_t x, int s) {
     return neg ? dsub(0, y) : y;
 }
 
+// Butterfly arithmetic on the carry-chain forms (canonical in, canonical out).
 struct FpOps {
     using T = uint64_t;
-    static __device__ __forceinline__ T add(T a, T b) { return fadd(a, b); }
-    static __device__ __forceinline__ T sub(T a, T b) { return fsub(a, b); }
-    static __device__ __forceinline__ T mulb(T a, uint64_t w) { return fmul(a, w); }
+    static __device__ __forceinline__ T add(T a, T b) { return dadd(a, b); }
+    static __device__ __forceinline__ T sub(T a, T b) { return dsub(a, b); }
+    static __device__ __forceinline__ T mulb(T a, uint64_t w) { return dmul(a, w); }
     static __device__ __forceinline__ T mulp2(T a, int s) { return mul_pow2(a, s); }
 };
 struct Fp2Ops {
     using T = Fp2;
-    static __device__ __forceinline__ T add(T a, T b) { return f2add(a, b); }
-    static __device__ __forceinline__ T sub(T a, T b) { return f2sub(a, b); }
-    static __device__ __forceinline__ T mulb(T a, uint64_t w) { return Fp2{fmul(a.c0, w), fmul(a.c1, w)}; }
+    static __device__ __forceinline__ T add(T a, T b) { return d2add(a, b); }
+    static __device__ __forceinline__ T sub(T a, T b) { return d2sub(a, b); }
+    static __device__ __forceinline__ T mulb(T a, uint64_t w) { return Fp2{dmul(a.c0, w), dmul(a.c1, w)}; }
     static __device__ __forceinline__ T mulp2(T a, int s) { return Fp2{mul_pow2(a.c0, s), mul_pow2(a.c1, s)}; }
 };
 

@@ -472,7 +472,7 @@ constexpr int kEqTile = 1 << kEqTileBits;
 // Block-wide: write eq(point[0..n), .) * scale (* *scale_dev) (n <= 11) to `out`.
 __device__ void eq_block_build(const Fp2* point, int n, Fp2 scale, const Fp2* scale_dev, Fp2* out) {
     __shared__ Fp2 buf[kEqTile];
-    if (threadIdx.x == 0) buf[0] = scale_dev ? f2mul(scale, *scale_dev) : scale;
+    if (threadIdx.x == 0) buf[0] = scale_dev ? d2mul(scale, *scale_dev) : scale;
     __syncthreads();
     int size = 1;
     for (int k = n - 1; k >= 0; --k) {
@@ -482,8 +482,8 @@ __device__ void eq_block_build(const Fp2* point, int n, Fp2 scale, const Fp2* sc
         int cnt = 0;
         for (int i = threadIdx.x; i < size; i += blockDim.x, ++cnt) {
             const Fp2 v = buf[i];
-            hi[cnt] = f2mul(v, pk);
-            lo[cnt] = f2sub(v, hi[cnt]);
+            hi[cnt] = d2mul(v, pk);
+            lo[cnt] = d2sub(v, hi[cnt]);
         }
         __syncthreads();
         cnt = 0;
@@ -523,8 +523,8 @@ __global__ void eq_outer_kernel(const Fp2* lo, int lo_bits, const Fp2* hi, size_
     const size_t mask = (size_t{1} << lo_bits) - 1;
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
-        Fp2 v = f2mul(ldg2(lo + (i & mask)), ldg2(hi + (i >> lo_bits)));
-        if (add) v = f2add(v, ldg2(add + i));
+        Fp2 v = d2mul(ldg2(lo + (i & mask)), ldg2(hi + (i >> lo_bits)));
+        if (add) v = d2add(v, ldg2(add + i));
         st2(out + i, v);
     }
 }
@@ -549,7 +549,7 @@ __global__ void eq_outer_multi_kernel(OuterTables t) {
         int k = 0;
         while (z >= t.first[k + 1]) ++k;
         const size_t i = z - t.first[k];
-        st2(t.out[k] + i, f2mul(ldg2(t.lo[k] + (i & mask)), ldg2(t.hi[k] + (i >> kEqTileBits))));
+        st2(t.out[k] + i, d2mul(ldg2(t.lo[k] + (i & mask)), ldg2(t.hi[k] + (i >> kEqTileBits))));
     }
 }
 
@@ -1029,7 +1029,7 @@ __global__ void __launch_bounds__(256) eq_outer_batch_kernel(const __grid_consta
     const OuterJob& t = b.t[lo];
     const size_t stride = static_cast<size_t>(t.blocks) * blockDim.x;
     for (size_t i = static_cast<size_t>(blockIdx.x - t.block0) * blockDim.x + threadIdx.x; i < t.entries; i += stride)
-        st2(t.out + i, f2mul(ldg2(t.lo + (i & (kEqTile - 1))), ldg2(t.hi + (i >> kEqTileBits))));
+        st2(t.out + i, d2mul(ldg2(t.lo + (i & (kEqTile - 1))), ldg2(t.hi + (i >> kEqTileBits))));
 }
 
 extern "C" int volta_b200_logup_suffix_eq_batch_device(void* raw, const vzb_suffix_job* jobs, size_t count) {
