@@ -404,9 +404,9 @@ def run_b200(args, rank, world, local_rank):
         if world == 1:
             msgs, finals = prover.triple_sumcheck_fp(tables[0], tables[1], tables[2], n, TRANSCRIPT_SEED)
             proof = prover.logup_prove(f_col, n_f, t_col, n_t, m_col, LOGUP_SEED, LOGUP_DOMAIN, cap)
-        else:
-            msgs, finals = sharded.triple_sumcheck(*shard_tables, n, TRANSCRIPT_SEED, base=True)
-            proof = sharded.logup_prove(f_col, n_f, t_col, n_t, m_col, LOGUP_SEED, LOGUP_DOMAIN)
+        else:  # one local call (both sumchecks enqueued back to back) and one all-gather per proof
+            msgs, finals, proof = sharded.prove(*shard_tables, n, TRANSCRIPT_SEED, f_col, n_f, t_col, n_t, m_col,
+                                                LOGUP_SEED, LOGUP_DOMAIN, base=True)
         return msgs, finals, proof
 
     def barrier():
@@ -460,8 +460,8 @@ def run_b200(args, rank, world, local_rank):
                 prover.triple_sumcheck_fp(ups[0], ups[1], ups[2], n, TRANSCRIPT_SEED)
                 prover.logup_prove(ups[3], n_f, ups[4], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN, cap)
             else:
-                sharded.triple_sumcheck(ups[0], ups[1], ups[2], n, TRANSCRIPT_SEED, base=True)
-                sharded.logup_prove(ups[3], n_f, ups[4], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN)
+                sharded.prove(ups[0], ups[1], ups[2], n, TRANSCRIPT_SEED, ups[3], n_f, ups[4], n_t, ups[5],
+                              LOGUP_SEED, LOGUP_DOMAIN, base=True)
 
         e2e_step()
         barrier()

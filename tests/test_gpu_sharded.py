@@ -116,3 +116,37 @@ def test_sharded_ligero_matches_single_gpu(prover, rows, msg_len, code_len, quer
     for g in range(G):
         be.free(enc[g][0])
         be.free(trees[g])
+
+
+@pytest.mark.parametrize("log2n,log2f,log2t,G", [(6, 6, 4, 2), (14, 14, 10, 4), (16, 16, 12, 8)])
+def test_sharded_proof_local_matches_oracle(prover, oracle, log2n, log2f, log2t, G):
+    """vzh_proof_local (triple on Fp columns + both LogUp sides, one
+    download) per shard, then the two finishes, equal the one-process
+    proofs; this is ShardedProver.prove's flow with the shards taking turns."""
+    n, nf, nt = 1 << log2n, 1 << log2f, 1 << log2t
+    rng = np.random.default_rng(log2n * 7 + G)
+    cols = [rng.integers(0, 2**64 - 2**32 + 1, size=n, dtype=np.uint64) for _ in range(3)]
+    lifted = [np.stack([x, np.zeros_like(x)], axis=1) for x in cols]
+    table = rng.integers(-32768, 32768, size=nt, dtype=np.int64).astype(np.int16)
+    idx = rng.integers(0, nt, size=nf)
+    f = table[idx]
+    mult = np.bincount(idx, minlength=nt).astype(np.uint32)
+    fe, te = em.embed_i16(f), em.embed_i16(table)
+    tseed, lseed, domain = bytes([0x5A] * 32), bytes([0x4C] * 32), 0x1004
+    be = prover.backend
+    parts = []
+    for g in range(G):
+        def part(x):
+            return np.ascontiguousarray(x[g * len(x) // G:(g + 1) * len(x) // G])
+        ids = [be.upload_new(part(x)) for x in cols + [fe, te, mult]]
+        parts.append(prover.proof_local(ids[0], ids[1], ids[2], n // G, True, tseed, ids[3], nf // G, ids[4],
+                                        nt // G, ids[5], G.bit_length() - 1, lseed, domain))
+        for i in ids:
+            be.free(i)
+    kt = 3 * ((n // G).bit_length() - 1) + 3
+    msgs, finals = sh.triple_finish([p[:kt] for p in parts], n, tseed)
+    em_msgs, em_finals = oracle.triple_sumcheck(*lifted, tseed)
+    assert np.array_equal(msgs, em_msgs)
+    assert np.array_equal(finals, em_finals)
+    got = sh.logup_finish([p[kt:] for p in parts], nf, nt, lseed, domain)
+    assert np.array_equal(got, oracle.logup_prove(f, table, mult, lseed, domain))

@@ -160,6 +160,8 @@ def load_host_library():
                                       C.POINTER(C.c_size_t), C.c_char_p, sz]
         L.vzh_ligero_commit_open.argtypes = [vp, C.c_char_p, sz, sz, sz, sz, C.c_char_p, vp, vp, vp, vp,
                                              C.c_char_p, sz]
+        L.vzh_proof_local.argtypes = [vp, u64, u64, u64, sz, C.c_int, C.c_char_p, u64, sz, u64, sz, u64, sz,
+                                      C.c_char_p, u64, vp, sz, C.POINTER(C.c_size_t), C.c_char_p, sz]
         L.vzh_logup_local.argtypes = [vp, u64, sz, u64, sz, u64, sz, C.c_char_p, u64, vp, sz,
                                       C.POINTER(C.c_size_t), C.c_char_p, sz]
         L.vzh_fpstream_fp2.argtypes = [C.c_char_p, u64, sz, vp]
@@ -365,6 +367,23 @@ class Prover:
         err = C.create_string_buffer(1024)
         rc = self.host.vzh_logup_local(self.h, f_col, n_f_local, t_col, n_t_local, mult, shard_bits, seed, domain,
                                        _ptr(out), cap, C.byref(written), err, 1024)
+        self._err(rc, err)
+        return out[: written.value]
+
+    def proof_local(self, a: int, b: int, c: int, n_local: int, base: bool, triple_seed: bytes, f_col: int,
+                    n_f_local: int, t_col: int, n_t_local: int, mult: int, shard_bits: int, logup_seed: bytes,
+                    domain: int) -> np.ndarray:
+        """This shard's whole config-1 part in one call (vzh_proof_local): the
+        triple sumcheck words (3 k messages, 3 finals) then the LogUp local
+        words, with a single download for both."""
+        k = n_local.bit_length() - 1
+        cap = 3 * k + 3 + 1 + 2 * (2 + sum(4 * (l - shard_bits) + 4 for l in range(shard_bits, 64)))
+        out = np.zeros((cap, 2), dtype=np.uint64)
+        written = C.c_size_t()
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_proof_local(self.h, a, b, c, n_local, 1 if base else 0, triple_seed, f_col, n_f_local,
+                                       t_col, n_t_local, mult, shard_bits, logup_seed, domain, _ptr(out), cap,
+                                       C.byref(written), err, 1024)
         self._err(rc, err)
         return out[: written.value]
 

@@ -28,10 +28,10 @@ struct Acc {
     }
 };
 
-// Sum of `a` over the block; valid in thread 0.
+// Sum of `a` over the block (up to 1024 threads); valid in thread 0.
 template <int K>
 __device__ __forceinline__ Acc<K> block_sum(Acc<K> a) {
-    __shared__ Fp2 sm[K][kReduceThreads / 32];
+    __shared__ Fp2 sm[K][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1)

@@ -680,6 +680,8 @@ extern "C" int volta_cuda_create(void** out) {
         VZB_CUDA(c, cudaHostAlloc(&c->host_mailbox, 4096, cudaHostAllocMapped));
         VZB_CUDA(c, cudaHostGetDevicePointer(&c->host_mailbox_dev, c->host_mailbox, 0));
         std::memset(c->host_mailbox, 0, 4096);  // the message flag starts below every sequence number
+        VZB_CUDA(c, cudaHostAlloc(&c->stage, kStageSlotBytes * kStageSlots, cudaHostAllocDefault));
+        for (auto& e : c->stage_ev) VZB_CUDA(c, cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         if (ensure_ws(c, kWsCounter, 4096)) return -1;
         // per-block partials of the single-launch reductions: at most 8 blocks
         // per SM and 9 Fp2 accumulators per block (the aux round)
@@ -713,6 +715,9 @@ extern "C" void volta_cuda_destroy(void* raw) {
     for (auto e : c->bench_ev)
         if (e) cudaEventDestroy(e);
     if (c->host_mailbox) cudaFreeHost(c->host_mailbox);
+    for (auto e : c->stage_ev)
+        if (e) cudaEventDestroy(e);
+    if (c->stage) cudaFreeHost(c->stage);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -1230,7 +1235,20 @@ extern "C" int volta_cuda_resident_upload(void* raw, uint64_t id, size_t offset,
     if (region(c, id, offset, bytes, &dst)) return -1;
     if (xfer_begin(c)) return -1;
     const auto t0 = std::chrono::steady_clock::now();
-    const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->stream);
+    cudaError_t e;
+    if (bytes <= kStageSlotBytes && c->stage) {
+        // small upload through a pinned staging slot (reused once its copy is done)
+        const int slot = c->stage_next;
+        c->stage_next = (slot + 1) % kStageSlots;
+        if (c->stage_used[slot]) VZB_CUDA(c, cudaEventSynchronize(c->stage_ev[slot]));
+        char* staged = static_cast<char*>(c->stage) + static_cast<size_t>(slot) * kStageSlotBytes;
+        std::memcpy(staged, src, bytes);
+        e = cudaMemcpyAsync(dst, staged, bytes, cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess) e = cudaEventRecord(c->stage_ev[slot], c->stream);
+        c->stage_used[slot] = true;
+    } else {
+        e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->stream);
+    }
     const auto t1 = std::chrono::steady_clock::now();
     if (e != cudaSuccess) return fail_cuda(c, "cudaMemcpyAsync(resident H2D)", e);
     ++c->stats.resident_h2d_host_calls;

@@ -120,6 +120,9 @@ enum WorkspaceSlot : int {
     kWsCount = 15,
 };
 
+constexpr size_t kStageSlotBytes = size_t{64} << 10;
+constexpr int kStageSlots = 64;
+
 struct Context {
     int device = 0;
     int sm_count = 148;
@@ -156,6 +159,13 @@ struct Context {
     uint32_t mail_seq = 0;               // sequence number of host-bound messages
     uint64_t launches = 0;               // kernels launched by this context
     cudaEvent_t bench_ev[kTimingMarkers] = {};        // measurement markers (extension ABI)
+    // Pinned staging ring for small uploads: the bytes are copied at call
+    // time and the async copy never waits on queued work (a pageable source
+    // may make cudaMemcpyAsync synchronise with the stream).
+    void* stage = nullptr;
+    cudaEvent_t stage_ev[kStageSlots] = {};
+    bool stage_used[kStageSlots] = {};
+    int stage_next = 0;
     std::string error;
 };
 

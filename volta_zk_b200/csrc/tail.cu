@@ -19,8 +19,8 @@ namespace vzb {
 namespace {
 
 constexpr int kTailMaxLog = 11;
-constexpr int kTailThreads = kReduceThreads;  // 256
-constexpr int kMaxJobs = 32;
+constexpr int kTailThreads = 512;
+constexpr int kMaxJobs = 64;
 constexpr int kTailPer = (1 << kTailMaxLog) / 2 / kTailThreads;  // pairs per thread, at most
 
 struct LayerJob {

@@ -135,37 +135,44 @@ int vzh_logup_local(void* h, uint64_t f_col, size_t n_f_local, uint64_t t_col, s
                     size_t* written, char* err, size_t len) {
     return guarded(err, len, [&] {
         Backend& b = *static_cast<Backend*>(h);
-        const Api& A = b.api();
         FpStream chal(seed, domain);
-        std::vector<Fp2> words;
-        const Fp2 alpha = chal.next_fp2();
-        words.push_back(alpha);
-        const uint32_t zero_shift = 0;
         Owned own(b);
-        const uint64_t shifts = own.add(b.alloc(sizeof(uint32_t)));
-        b.upload(shifts, 0, &zero_shift, sizeof(zero_shift));
-        const uint64_t cols[2] = {f_col, t_col};
-        const size_t ns[2] = {n_f_local, n_t_local};
-        for (int side = 0; side < 2; ++side) {
-            Owned so(b);
-            const uint64_t leaf = so.add(b.alloc(ns[side] * sizeof(uint64_t)));
-            b.check(A.volta_cuda_pack_lookup_leaf_device(b.ctx(), cols[side], 0, shifts, 0, leaf, 0, 1, ns[side],
-                                                         alpha.c0),
-                    "pack_lookup_leaf_device");
-            size_t local_depth = 0;
-            while ((size_t{1} << local_depth) < ns[side]) ++local_depth;
-            const SideSchedule sch = draw_side_schedule(chal, local_depth + shard_bits);
-            const LocalSide loc = frac_side_local(b, leaf, side ? mult : 0, ns[side], alpha.c1, shard_bits, sch);
-            words.push_back(loc.root_p);
-            words.push_back(loc.root_q);
-            for (size_t i = 0; i < loc.accs.size(); ++i) {
-                words.insert(words.end(), loc.accs[i].begin(), loc.accs[i].end());
-                words.insert(words.end(), loc.leftover[i].begin(), loc.leftover[i].end());
-            }
-        }
+        const PendingLogup pl = logup_local_enqueue(b, own, f_col, n_f_local, t_col, n_t_local, mult, shard_bits, chal);
+        const std::vector<Fp2> words = logup_local_collect(b, pl);
         if (words.size() > cap) throw AccelError("local LogUp buffer too small");
         std::memcpy(out, words.data(), words.size() * sizeof(vz_fp2));
         *written = words.size();
+    });
+}
+
+// One shard's whole config-1 part in one call: the triple-product sumcheck of
+// its table slices (Fp columns when base != 0) and both LogUp sides are
+// enqueued back to back and downloaded once.  out = the triple's 3 k
+// messages and 3 finals (k = log2 n_local), then the words of
+// vzh_logup_local.  Needs the scheduled drivers.
+int vzh_proof_local(void* h, uint64_t a, uint64_t bb, uint64_t c, size_t n_local, int base,
+                    const uint8_t* triple_seed, uint64_t f_col, size_t n_f_local, uint64_t t_col, size_t n_t_local,
+                    uint64_t mult, size_t shard_bits, const uint8_t* logup_seed, uint64_t domain, vz_fp2* out,
+                    size_t cap, size_t* written, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        Backend& b = *static_cast<Backend*>(h);
+        if (!b.scheduled()) throw AccelError("vzh_proof_local needs the scheduled drivers");
+        if (base && !(b.ext().triple_round_fp && b.ext().triple_fold_round_fp && n_local >= 4))
+            throw AccelError("vzh_proof_local: base-field rounds unavailable for this table length");
+        FpStream tx(triple_seed, UINT64_MAX);
+        FpStream chal(logup_seed, domain);
+        Owned own(b);
+        size_t k = 0;
+        const uint64_t tm = triple_enqueue(b, own, a, bb, c, n_local, tx, base != 0, k);
+        const PendingLogup pl = logup_local_enqueue(b, own, f_col, n_f_local, t_col, n_t_local, mult, shard_bits, chal);
+        const TripleResult tr = triple_collect(b, tm, k);
+        const std::vector<Fp2> words = logup_local_collect(b, pl);
+        const size_t total = tr.messages.size() + 3 + words.size();
+        if (total > cap) throw AccelError("local proof buffer too small");
+        std::memcpy(out, tr.messages.data(), tr.messages.size() * sizeof(vz_fp2));
+        std::memcpy(out + tr.messages.size(), tr.finals, sizeof(tr.finals));
+        std::memcpy(out + tr.messages.size() + 3, words.data(), words.size() * sizeof(vz_fp2));
+        *written = total;
     });
 }
 

@@ -216,7 +216,8 @@ TripleResult triple_sumcheck_resident_fp(Backend& b, uint64_t a, uint64_t bb, ui
 
 std::vector<Fp2> logup_prove_resident(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col,
                                       size_t n_t, uint64_t mult, FpStream& chal) {
-    const SideProver side_prover = b.scheduled() ? prove_frac_tree_scheduled : prove_frac_tree_resident;
+    if (b.scheduled()) return logup_prove_scheduled(b, f_col, n_f, t_col, n_t, mult, chal);
+    const SideProver side_prover = prove_frac_tree_resident;
     const Api& A = b.api();
     void* ctx = b.ctx();
     std::vector<Fp2> proof;

@@ -67,4 +67,42 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
 TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
                                        FpStream& tx, bool base = false);
 
+// Enqueue / collect halves of the scheduled drivers: everything is enqueued
+// on the context's stream with device-side message slots, and the collect
+// call downloads them (the only synchronisation).  Buffers go to `own`,
+// which must outlive the collect call.  Several enqueues may precede the
+// first collect, so one proof's sumchecks run back to back on the GPU.
+uint64_t triple_enqueue(Backend& b, Owned& own, uint64_t a, uint64_t bb, uint64_t c, size_t n, FpStream& tx,
+                        bool base, size_t& k_out);
+TripleResult triple_collect(Backend& b, uint64_t msgs, size_t k);
+struct PendingSide {
+    uint64_t msgs = 0;
+    size_t msg_total = 0, depth = 0, shard_bits = 0;
+    std::vector<size_t> moff;
+    // launched by launch_side_work (suffix tables, round steps per layer, one-CTA jobs)
+    std::vector<vzb_suffix_job> suffix_jobs;
+    std::vector<std::vector<vzb_round_job>> plan;
+    std::vector<vzb_layer_job> jobs;
+};
+PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mult, size_t n_local,
+                              uint64_t alpha1, size_t shard_bits, const SideSchedule& sch);
+// Launch the batched work of several sides together: one suffix-table batch,
+// step t of every large layer of every side per launch, one launch of all
+// one-CTA jobs.
+void launch_side_work(Backend& b, const std::vector<PendingSide*>& sides);
+LocalSide frac_side_collect(Backend& b, const PendingSide& ps);
+// Both sides of a (sharded) LogUp proof: the words of vzh_logup_local.
+struct PendingLogup {
+    Fp2 alpha;
+    SideSchedule sch[2];
+    PendingSide side[2];
+};
+PendingLogup logup_local_enqueue(Backend& b, Owned& own, uint64_t f_col, size_t n_f_local, uint64_t t_col,
+                                 size_t n_t_local, uint64_t mult, size_t shard_bits, FpStream& chal);
+std::vector<Fp2> logup_local_collect(Backend& b, const PendingLogup& pl);
+// The whole LogUp proof (both sides' batches sharing launches, one download
+// per side after everything is enqueued); words as logup_prove_resident.
+std::vector<Fp2> logup_prove_scheduled(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col, size_t n_t,
+                                       uint64_t mult, FpStream& chal);
+
 }  // namespace vzh

@@ -25,17 +25,17 @@ constexpr size_t kTailLen = 2048;
 // Jobs per volta_b200_logup_round_batch_device call.
 constexpr size_t kRoundBatchMax = 24;
 
-TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
-                                       FpStream& tx, bool base) {
+uint64_t triple_enqueue(Backend& b, Owned& own, uint64_t a, uint64_t bb, uint64_t c, size_t n, FpStream& tx,
+                        bool base, size_t& k_out) {
     const Api& A = b.api();
     const ExtApi& X = b.ext();
     void* ctx = b.ctx();
     size_t k = 0;
     while ((size_t{1} << k) < n) ++k;
     if ((size_t{1} << k) != n) throw AccelError("triple sumcheck needs a power-of-two table length");
+    k_out = k;
     std::vector<Fp2> r(k);
     for (auto& x : r) x = tx.next_fp2();
-    Owned own(b);
     // slots: 3 per round message, then the 3 final openings
     const uint64_t msgs = own.add(b.alloc((3 * k + 3) * sizeof(Fp2)));
     uint64_t rdev = 0;
@@ -110,12 +110,24 @@ TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint
                                                     sizeof(Fp2), 1, sizeof(Fp2)),
                     "resident_copy_rows");
     }
+    return msgs;
+}
+
+TripleResult triple_collect(Backend& b, uint64_t msgs, size_t k) {
     std::vector<Fp2> host(3 * k + 3);
     b.download(msgs, 0, host.data(), host.size() * sizeof(Fp2));
     TripleResult out;
     out.messages.assign(host.begin(), host.begin() + 3 * k);
     for (int t = 0; t < 3; ++t) out.finals[t] = host[3 * k + t];
     return out;
+}
+
+TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n, FpStream& tx,
+                                       bool base) {
+    Owned own(b);
+    size_t k = 0;
+    const uint64_t msgs = triple_enqueue(b, own, a, bb, c, n, tx, base, k);
+    return triple_collect(b, msgs, k);
 }
 
 SideSchedule draw_side_schedule(FpStream& chal, size_t depth) {
@@ -146,8 +158,8 @@ SideSchedule draw_side_schedule(FpStream& chal, size_t depth) {
 // accumulator is this shard's share of the global one up to the factor
 // eq(top bits of the point, g), and keeps the four vector values left over.
 // With shard_bits = 0 these are the whole rounds and the splits.
-LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_local, uint64_t alpha1,
-                          size_t shard_bits, const SideSchedule& sch) {
+PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mult, size_t n_local,
+                              uint64_t alpha1, size_t shard_bits, const SideSchedule& sch) {
     const Api& A = b.api();
     const ExtApi& X = b.ext();
     void* ctx = b.ctx();
@@ -156,9 +168,6 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
     if ((size_t{1} << local_depth) != n_local || !local_depth)
         throw AccelError("fraction-tree shards need a power-of-two length of at least 2");
     const size_t depth = local_depth + shard_bits;
-    LocalSide out;
-    out.shard_bits = shard_bits;
-    Owned own(b);
     // truncated claim points of the sharded layers in one upload
     std::vector<size_t> pts_off(depth, 0);
     std::vector<Fp2> flat;
@@ -431,40 +440,115 @@ LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_loc
             len = half;
         }
     }
+    // the suffix tables, the round batches and the one-CTA jobs are launched
+    // by launch_side_work, together with those of other sides
+    PendingSide ps;
+    ps.msgs = msgs;
+    ps.msg_total = msg_total;
+    ps.depth = depth;
+    ps.shard_bits = shard_bits;
+    ps.moff = std::move(moff);
+    ps.suffix_jobs = std::move(suffix_jobs);
+    ps.plan = std::move(plan);
+    ps.jobs = std::move(jobs);
+    return ps;
+}
+
+void launch_side_work(Backend& b, const std::vector<PendingSide*>& sides) {
+    const ExtApi& X = b.ext();
+    void* ctx = b.ctx();
+    std::vector<vzb_suffix_job> suffix_jobs;
+    std::vector<vzb_layer_job> jobs;
+    size_t steps_max = 0;
+    for (const PendingSide* ps : sides) {
+        suffix_jobs.insert(suffix_jobs.end(), ps->suffix_jobs.begin(), ps->suffix_jobs.end());
+        jobs.insert(jobs.end(), ps->jobs.begin(), ps->jobs.end());
+        for (const auto& st : ps->plan) steps_max = std::max(steps_max, st.size());
+    }
     if (!suffix_jobs.empty())
         b.check(X.logup_suffix_eq_batch(ctx, suffix_jobs.data(), suffix_jobs.size()),
                 "volta_b200_logup_suffix_eq_batch_device");
-    size_t steps_max = 0;
-    for (const auto& st : plan) steps_max = std::max(steps_max, st.size());
+    // step t of every large layer of every side in one launch (chunks of kRoundBatchMax)
     std::vector<vzb_round_job> batch;
     for (size_t t = 0; t < steps_max; ++t) {
         batch.clear();
-        for (const auto& st : plan)
-            if (t < st.size()) batch.push_back(st[t]);
+        for (const PendingSide* ps : sides)
+            for (const auto& st : ps->plan)
+                if (t < st.size()) batch.push_back(st[t]);
         for (size_t o = 0; o < batch.size(); o += kRoundBatchMax)
             b.check(X.logup_round_batch(ctx, batch.data() + o, std::min(kRoundBatchMax, batch.size() - o)),
                     "volta_b200_logup_round_batch_device");
     }
     if (!jobs.empty()) b.check(X.logup_layers(ctx, jobs.data(), jobs.size()), "volta_b200_logup_layers_device");
-    std::vector<Fp2> m(msg_total);
-    b.download(msgs, 0, m.data(), msg_total * sizeof(Fp2));
+}
+
+LocalSide frac_side_collect(Backend& b, const PendingSide& ps) {
+    LocalSide out;
+    out.shard_bits = ps.shard_bits;
+    std::vector<Fp2> m(ps.msg_total);
+    b.download(ps.msgs, 0, m.data(), ps.msg_total * sizeof(Fp2));
     out.root_p = m[0];
     out.root_q = m[1];
-    for (size_t l = shard_bits; l < depth; ++l) {
-        const size_t L = l - shard_bits;
-        out.accs.emplace_back(m.begin() + moff[l], m.begin() + moff[l] + 4 * L);
-        out.leftover.emplace_back(m.begin() + moff[l] + 4 * L, m.begin() + moff[l] + 4 * L + 4);
+    for (size_t l = ps.shard_bits; l < ps.depth; ++l) {
+        const size_t L = l - ps.shard_bits;
+        out.accs.emplace_back(m.begin() + ps.moff[l], m.begin() + ps.moff[l] + 4 * L);
+        out.leftover.emplace_back(m.begin() + ps.moff[l] + 4 * L, m.begin() + ps.moff[l] + 4 * L + 4);
     }
     return out;
 }
 
-void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t n, uint64_t alpha1,
-                               FpStream& chal, std::vector<Fp2>& proof) {
-    size_t depth = 0;
-    while ((size_t{1} << depth) < n) ++depth;
-    const SideSchedule sch = draw_side_schedule(chal, depth);
-    const LocalSide loc = frac_side_local(b, leaf, mult, n, alpha1, 0, sch);
-    // proof words in the round-by-round order (h0, h2 = cpref (lambda pq + qq))
+LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_local, uint64_t alpha1,
+                          size_t shard_bits, const SideSchedule& sch) {
+    Owned own(b);
+    PendingSide ps = frac_side_enqueue(b, own, leaf, mult, n_local, alpha1, shard_bits, sch);
+    launch_side_work(b, {&ps});
+    return frac_side_collect(b, ps);
+}
+
+PendingLogup logup_local_enqueue(Backend& b, Owned& own, uint64_t f_col, size_t n_f_local, uint64_t t_col,
+                                 size_t n_t_local, uint64_t mult, size_t shard_bits, FpStream& chal) {
+    const Api& A = b.api();
+    PendingLogup pl;
+    pl.alpha = chal.next_fp2();
+    const uint32_t zero_shift = 0;
+    const uint64_t shifts = own.add(b.alloc(sizeof(uint32_t)));
+    b.upload(shifts, 0, &zero_shift, sizeof(zero_shift));
+    const uint64_t cols[2] = {f_col, t_col};
+    const size_t ns[2] = {n_f_local, n_t_local};
+    for (int side = 0; side < 2; ++side) {
+        const uint64_t leaf = own.add(b.alloc(ns[side] * sizeof(uint64_t)));
+        b.check(A.volta_cuda_pack_lookup_leaf_device(b.ctx(), cols[side], 0, shifts, 0, leaf, 0, 1, ns[side],
+                                                     pl.alpha.c0),
+                "pack_lookup_leaf_device");
+        size_t local_depth = 0;
+        while ((size_t{1} << local_depth) < ns[side]) ++local_depth;
+        pl.sch[side] = draw_side_schedule(chal, local_depth + shard_bits);
+        pl.side[side] =
+            frac_side_enqueue(b, own, leaf, side ? mult : 0, ns[side], pl.alpha.c1, shard_bits, pl.sch[side]);
+    }
+    launch_side_work(b, {&pl.side[0], &pl.side[1]});  // both sides' batches share launches
+    return pl;
+}
+
+std::vector<Fp2> logup_local_collect(Backend& b, const PendingLogup& pl) {
+    std::vector<Fp2> words;
+    words.push_back(pl.alpha);
+    for (int side = 0; side < 2; ++side) {
+        const LocalSide loc = frac_side_collect(b, pl.side[side]);
+        words.push_back(loc.root_p);
+        words.push_back(loc.root_q);
+        for (size_t i = 0; i < loc.accs.size(); ++i) {
+            words.insert(words.end(), loc.accs[i].begin(), loc.accs[i].end());
+            words.insert(words.end(), loc.leftover[i].begin(), loc.leftover[i].end());
+        }
+    }
+    return words;
+}
+
+// A whole side's proof words in the round-by-round order (h0, h2 =
+// cpref (lambda pq + qq), logup.rs:452-453) from its raw accumulators.
+static void append_side_proof(const SideSchedule& sch, const LocalSide& loc, std::vector<Fp2>& proof) {
+    const size_t depth = sch.lambda.size();
     proof.push_back(loc.root_p);
     proof.push_back(loc.root_q);
     for (size_t l = 0; l < depth; ++l) {
@@ -477,6 +561,25 @@ void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t 
         }
         for (int k = 0; k < 4; ++k) proof.push_back(loc.leftover[l][k]);
     }
+}
+
+std::vector<Fp2> logup_prove_scheduled(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col, size_t n_t,
+                                       uint64_t mult, FpStream& chal) {
+    Owned own(b);
+    const PendingLogup pl = logup_local_enqueue(b, own, f_col, n_f, t_col, n_t, mult, 0, chal);
+    std::vector<Fp2> proof;
+    proof.push_back(pl.alpha);
+    for (int side = 0; side < 2; ++side) append_side_proof(pl.sch[side], frac_side_collect(b, pl.side[side]), proof);
+    return proof;
+}
+
+void prove_frac_tree_scheduled(Backend& b, uint64_t leaf, uint64_t mult, size_t n, uint64_t alpha1,
+                               FpStream& chal, std::vector<Fp2>& proof) {
+    size_t depth = 0;
+    while ((size_t{1} << depth) < n) ++depth;
+    const SideSchedule sch = draw_side_schedule(chal, depth);
+    const LocalSide loc = frac_side_local(b, leaf, mult, n, alpha1, 0, sch);
+    append_side_proof(sch, loc, proof);
 }
 
 }  // namespace vzh

@@ -111,6 +111,20 @@ class ShardedProver:
         parts = self.gather(np.concatenate([msgs, finals]).astype(np.uint64))
         return triple_finish(parts, n, seed)
 
+    def prove(self, a: int, b: int, c: int, n: int, triple_seed: bytes, f_col: int, n_f: int, t_col: int, n_t: int,
+              mult: int, logup_seed: bytes, domain: int, base: bool = False):
+        """Both parts of a config-1 proof with one local call and one
+        all-gather: (triple messages, triple finals, LogUp proof words), equal
+        to triple_sumcheck followed by logup_prove."""
+        nl = n // self.world
+        local = self.prover.proof_local(a, b, c, nl, base, triple_seed, f_col, n_f // self.world, t_col,
+                                        n_t // self.world, mult, self.s, logup_seed, domain)
+        parts = self.gather(local)
+        kt = 3 * (nl.bit_length() - 1) + 3
+        msgs, finals = triple_finish([p[:kt] for p in parts], n, triple_seed)
+        proof = logup_finish([p[kt:] for p in parts], n_f, n_t, logup_seed, domain)
+        return msgs, finals, proof
+
     def logup_prove(self, f_col: int, n_f: int, t_col: int, n_t: int, mult: int, seed: bytes, domain: int):
         """f_col / t_col / mult: this shard's slices of the global columns."""
         local = self.prover.logup_local(f_col, n_f // self.world, t_col, n_t // self.world, mult, self.s, seed,
