@@ -229,6 +229,26 @@ int volta_b200_triple_fold_round_fp_into_device(void* ctx, uint64_t a_id, uint64
                                                 vz_fp2 r, uint64_t ao_id, uint64_t bo_id, uint64_t co_id,
                                                 uint64_t out_id, size_t out_offset);
 
+/*
+ * Asynchronous uploads: upload_async copies `bytes` from `src` (pinned host
+ * memory for a truly asynchronous copy) into (id, offset) on the context's
+ * copy stream and returns at once; wait_uploads makes the context's stream
+ * (every later kernel and download) wait for all uploads issued so far.
+ * Until then the destination must not be read, written or freed, and `src`
+ * must stay valid.  This lets a caller upload the inputs of one protocol
+ * while another protocol computes.
+ */
+int volta_b200_upload_async(void* ctx, uint64_t id, size_t offset_bytes, const void* src, size_t bytes);
+int volta_b200_wait_uploads(void* ctx);
+
+/*
+ * int16 column to canonical Fp values (v >= 0 -> v, v < 0 -> p + v), so that
+ * int16 witness columns (lookup queries and tables) travel as 2 bytes per
+ * entry and are embedded on the device.
+ */
+int volta_b200_embed_i16_device(void* ctx, uint64_t in_id, size_t in_offset, uint64_t out_id, size_t out_offset,
+                                size_t n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,93 @@
+"""Asynchronous uploads and the int16 embedding (include/volta_b200_ext.h):
+data uploaded on the copy stream is what later kernels and downloads see
+once wait_uploads has been called, and a local proof whose tables arrive
+that way equals the oracle's."""
+
+import numpy as np
+import pytest
+
+import sharded_emulation as em
+from volta_zk_b200 import sharded as sh
+
+P = 0xFFFFFFFF00000001
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def prover():
+    from volta_zk_b200 import accel
+
+    p = accel.Prover(policy=1)
+    yield p
+    p.close()
+
+
+def test_embed_i16_matches_definition(prover):
+    be = prover.backend
+    rng = np.random.default_rng(3)
+    x = np.concatenate([np.array([-32768, -1, 0, 1, 32767], dtype=np.int16),
+                        rng.integers(-32768, 32768, size=100_003, dtype=np.int64).astype(np.int16)])
+    src = be.upload_new(x)
+    dst = be.alloc(8 * x.size)
+    be.embed_i16(src, dst, x.size)
+    got = be.download(dst, 8 * x.size)
+    v = x.astype(np.int64)
+    exp = np.where(v >= 0, v.astype(np.uint64), np.uint64(P) - (-v).astype(np.uint64))
+    assert np.array_equal(got, exp)
+    # beyond the buffers: rejected, and the context stays usable
+    assert be.lib.volta_b200_embed_i16_device(be.ctx, src, 0, dst, 0, x.size + 1) == -1
+    be.embed_i16(src, dst, 5)
+    be.free(src)
+    be.free(dst)
+
+
+def test_upload_async_then_wait(prover):
+    import torch
+
+    be = prover.backend
+    rng = np.random.default_rng(4)
+    data = rng.integers(0, 2**63, size=(1 << 22), dtype=np.int64)
+    host = torch.from_numpy(data).pin_memory()
+    buf = be.alloc(8 * data.size + 64)
+    be.upload_async(buf, host.data_ptr(), 8 * data.size, 64)
+    be.wait_uploads()
+    got = be.download(buf, 8 * data.size, offset_bytes=64)
+    assert np.array_equal(got.view(np.int64), data)
+    assert be.lib.volta_b200_upload_async(be.ctx, buf, 65, host.data_ptr(), 8 * data.size) == -1  # beyond
+    be.wait_uploads()
+    be.free(buf)
+
+
+def test_proof_local_waits_for_async_tables(prover, oracle):
+    """The triple columns are still in flight on the copy stream when the
+    local call starts; its triple part waits for them."""
+    import torch
+
+    n, nf, nt = 1 << 16, 1 << 14, 1 << 10
+    rng = np.random.default_rng(9)
+    cols = [rng.integers(0, P, size=n, dtype=np.uint64) for _ in range(3)]
+    lifted = [np.stack([x, np.zeros_like(x)], axis=1) for x in cols]
+    table = rng.integers(-32768, 32768, size=nt, dtype=np.int64).astype(np.int16)
+    idx = rng.integers(0, nt, size=nf)
+    f = table[idx]
+    mult = np.bincount(idx, minlength=nt).astype(np.uint32)
+    be = prover.backend
+    f16, t16 = be.upload_new(f), be.upload_new(table)
+    fe, te = be.alloc(8 * nf), be.alloc(8 * nt)
+    be.embed_i16(f16, fe, nf)
+    be.embed_i16(t16, te, nt)
+    m = be.upload_new(mult)
+    pinned = [torch.from_numpy(x.view(np.int64)).pin_memory() for x in cols]
+    ids = [be.alloc(8 * n) for _ in range(3)]
+    for buf, t in zip(ids, pinned):
+        be.upload_async(buf, t.data_ptr(), 8 * n)
+    tseed, lseed, domain = bytes([0x5A] * 32), bytes([0x4C] * 32), 0x1004
+    words = prover.proof_local(*ids, n, True, tseed, fe, nf, te, nt, m, 0, lseed, domain)
+    k = 3 * 16 + 3
+    em_msgs, em_finals = oracle.triple_sumcheck(*lifted, tseed)
+    assert np.array_equal(words[: 3 * 16], em_msgs)
+    assert np.array_equal(words[3 * 16:k], em_finals)
+    got = sh.logup_finish([words[k:]], nf, nt, lseed, domain)
+    assert np.array_equal(got, oracle.logup_prove(f, table, mult, lseed, domain))
+    for x in ids + [f16, t16, fe, te, m]:
+        be.free(x)

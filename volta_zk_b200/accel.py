@@ -254,6 +254,21 @@ class CudaBackend:
         self.check(self.lib.volta_cuda_get_stats(self.ctx, C.byref(s)), "get_stats")
         return s
 
+    # ---- asynchronous uploads (extension) --------------------------------------
+    def upload_async(self, buf: int, src_ptr: int, nbytes: int, offset_bytes: int = 0):
+        """Copy nbytes from host address src_ptr (pinned for a truly
+        asynchronous copy) on the context's copy stream; see wait_uploads."""
+        self.check(self.lib.volta_b200_upload_async(self.ctx, buf, offset_bytes, C.c_void_p(src_ptr), nbytes),
+                   "upload_async")
+
+    def wait_uploads(self):
+        """Later work on this context waits for every upload_async so far."""
+        self.check(self.lib.volta_b200_wait_uploads(self.ctx), "wait_uploads")
+
+    def embed_i16(self, in_buf: int, out_buf: int, n: int):
+        """out[i] = int16 in[i] embedded in Fp (canonical), on the device."""
+        self.check(self.lib.volta_b200_embed_i16_device(self.ctx, in_buf, 0, out_buf, 0, n), "embed_i16")
+
     # ---- measurement extensions ---------------------------------------------
     def mark(self, slot: int):
         self.check(self.lib.volta_b200_timing_mark(self.ctx, slot), "timing_mark")

@@ -551,3 +551,35 @@ extern "C" int volta_cuda_deinterleave_base_columns_device(void* raw, uint64_t c
         static_cast<const uint64_t*>(col), static_cast<Fp2*>(out), column_count, n);
     VZB_OP_END(c, kOpLogup);
 }
+
+// ---------------------------------------------------------------------------
+// Extension: int16 column to canonical Fp (negative v -> p + v), the
+// embedding of rust/volta-gpt2 witness values, on the device
+// ---------------------------------------------------------------------------
+
+namespace vzb {
+namespace {
+__global__ void embed_i16_kernel(const int16_t* in, uint64_t* out, size_t n) {
+    VZB_GRID_LOOP(i, n) {
+        const int64_t v = in[i];
+        out[i] = v < 0 ? kP - static_cast<uint64_t>(-v) : static_cast<uint64_t>(v);
+    }
+}
+}  // namespace
+}  // namespace vzb
+
+extern "C" int volta_b200_embed_i16_device(void* raw, uint64_t in_id, size_t in_offset, uint64_t out_id,
+                                           size_t out_offset, size_t n) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !n) return fail_message(c, "invalid int16 embedding geometry");
+    void *in = nullptr, *out = nullptr;
+    if (region_elems(c, in_id, in_offset, n, sizeof(int16_t), &in) ||
+        region_elems(c, out_id, out_offset, n, sizeof(uint64_t), &out))
+        return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    embed_i16_kernel<<<grid_for(c, n, 256), 256, 0, c->stream>>>(static_cast<const int16_t*>(in),
+                                                               static_cast<uint64_t*>(out), n);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsRows, 0, 0);
+}

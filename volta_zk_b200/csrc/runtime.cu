@@ -718,6 +718,9 @@ extern "C" void volta_cuda_destroy(void* raw) {
     for (auto e : c->stage_ev)
         if (e) cudaEventDestroy(e);
     if (c->stage) cudaFreeHost(c->stage);
+    if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    if (c->copy_ev) cudaEventDestroy(c->copy_ev);
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -1351,5 +1354,30 @@ extern "C" int volta_b200_launch_count(void* raw, uint64_t* launches) {
     Context* c = static_cast<Context*>(raw);
     if (!c || !launches) return fail_message(c, "invalid launch-count output");
     *launches = c->launches;
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Extensions: asynchronous uploads (include/volta_b200_ext.h)
+// ---------------------------------------------------------------------------
+
+extern "C" int volta_b200_upload_async(void* raw, uint64_t id, size_t offset, const void* src, size_t bytes) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !src || !bytes) return fail_message(c, "invalid asynchronous upload");
+    void* dst = nullptr;
+    if (region(c, id, offset, bytes, &dst)) return -1;
+    if (!c->copy_stream) {
+        VZB_CUDA(c, cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
+        VZB_CUDA(c, cudaEventCreateWithFlags(&c->copy_ev, cudaEventDisableTiming));
+    }
+    VZB_CUDA(c, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->copy_stream));
+    VZB_CUDA(c, cudaEventRecord(c->copy_ev, c->copy_stream));
+    return 0;
+}
+
+extern "C" int volta_b200_wait_uploads(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return -1;
+    if (c->copy_ev) VZB_CUDA(c, cudaStreamWaitEvent(c->stream, c->copy_ev, 0));
     return 0;
 }

@@ -166,6 +166,10 @@ struct Context {
     cudaEvent_t stage_ev[kStageSlots] = {};
     bool stage_used[kStageSlots] = {};
     int stage_next = 0;
+    // asynchronous uploads (extension): a copy stream and the event of its
+    // last copy, which volta_b200_wait_uploads makes the compute stream wait on
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t copy_ev = nullptr;
     std::string error;
 };
 

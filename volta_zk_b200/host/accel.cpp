@@ -127,6 +127,8 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         dlsym(handle_, "volta_b200_triple_round_fp_into_device"));
     ext_loaded_->triple_fold_round_fp = reinterpret_cast<decltype(ext_loaded_->triple_fold_round_fp)>(
         dlsym(handle_, "volta_b200_triple_fold_round_fp_into_device"));
+    ext_loaded_->wait_uploads =
+        reinterpret_cast<decltype(ext_loaded_->wait_uploads)>(dlsym(handle_, "volta_b200_wait_uploads"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

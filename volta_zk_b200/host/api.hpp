@@ -30,6 +30,7 @@ struct ExtApi {
     decltype(&::volta_b200_logup_suffix_eq_batch_device) logup_suffix_eq_batch = nullptr;
     decltype(&::volta_b200_triple_round_fp_into_device) triple_round_fp = nullptr;
     decltype(&::volta_b200_triple_fold_round_fp_into_device) triple_fold_round_fp = nullptr;
+    decltype(&::volta_b200_wait_uploads) wait_uploads = nullptr;
 };
 
 }  // namespace vzh

@@ -145,10 +145,12 @@ int vzh_logup_local(void* h, uint64_t f_col, size_t n_f_local, uint64_t t_col, s
     });
 }
 
-// One shard's whole config-1 part in one call: the triple-product sumcheck of
-// its table slices (Fp columns when base != 0) and both LogUp sides are
-// enqueued back to back and downloaded once.  out = the triple's 3 k
-// messages and 3 finals (k = log2 n_local), then the words of
+// One shard's whole config-1 part in one call: both LogUp sides and then the
+// triple-product sumcheck of its table slices (Fp columns when base != 0) are
+// enqueued back to back and downloaded once; the triple part first waits for
+// the context's asynchronous uploads (volta_b200_wait_uploads), so its tables
+// may still be arriving while the LogUp part computes.  out = the triple's
+// 3 k messages and 3 finals (k = log2 n_local), then the words of
 // vzh_logup_local.  Needs the scheduled drivers.
 int vzh_proof_local(void* h, uint64_t a, uint64_t bb, uint64_t c, size_t n_local, int base,
                     const uint8_t* triple_seed, uint64_t f_col, size_t n_f_local, uint64_t t_col, size_t n_t_local,
@@ -162,11 +164,12 @@ int vzh_proof_local(void* h, uint64_t a, uint64_t bb, uint64_t c, size_t n_local
         FpStream tx(triple_seed, UINT64_MAX);
         FpStream chal(logup_seed, domain);
         Owned own(b);
+        const PendingLogup pl = logup_local_enqueue(b, own, f_col, n_f_local, t_col, n_t_local, mult, shard_bits, chal);
+        if (b.ext().wait_uploads) b.check(b.ext().wait_uploads(b.ctx()), "volta_b200_wait_uploads");
         size_t k = 0;
         const uint64_t tm = triple_enqueue(b, own, a, bb, c, n_local, tx, base != 0, k);
-        const PendingLogup pl = logup_local_enqueue(b, own, f_col, n_f_local, t_col, n_t_local, mult, shard_bits, chal);
-        const TripleResult tr = triple_collect(b, tm, k);
         const std::vector<Fp2> words = logup_local_collect(b, pl);
+        const TripleResult tr = triple_collect(b, tm, k);
         const size_t total = tr.messages.size() + 3 + words.size();
         if (total > cap) throw AccelError("local proof buffer too small");
         std::memcpy(out, tr.messages.data(), tr.messages.size() * sizeof(vz_fp2));
