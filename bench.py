@@ -300,7 +300,8 @@ class RoundJob(__import__("ctypes").Structure):
     _fields_ = [("kind", _C.c_uint32), ("flags", _C.c_uint32), ("in_id", _C.c_uint64 * 4),
                 ("in_offset", _C.c_size_t * 4), ("len", _C.c_size_t), ("r", _C.c_uint64 * 2),
                 ("out_id", _C.c_uint64 * 4), ("out_offset", _C.c_size_t * 4), ("s_id", _C.c_uint64),
-                ("s_offset", _C.c_size_t), ("msg_id", _C.c_uint64), ("msg_offset", _C.c_size_t)]
+                ("s_offset", _C.c_size_t), ("msg_id", _C.c_uint64), ("msg_offset", _C.c_size_t),
+                ("q_alpha", _C.c_uint64 * 2)]
 
 
 def logup_step0_replica(be, log2_queries: int, reps: int = 10):
@@ -308,8 +309,9 @@ def logup_step0_replica(be, log2_queries: int, reps: int = 10):
     shapes: step 0 of the query side's cross-layer round batch, i.e. round 0
     on the interleaved children of every layer with more than 2^11 entries
     per vector (layer L: 2 x 2^L children of P and Q, a 2^(L-1)-entry suffix
-    table); the leaf layer's numerators are all 1 and not read.  Returns
-    (average launch ms, algorithmic bytes per launch, jobs)."""
+    table); the leaf layer's numerators are all 1 and its children are read
+    from the 8-byte query column.  Returns (average launch ms, algorithmic
+    bytes per launch, jobs)."""
     import ctypes as C
 
     jobs, bufs, nbytes = [], [], 0
@@ -318,8 +320,8 @@ def logup_step0_replica(be, log2_queries: int, reps: int = 10):
     for L in range(12, log2_queries):
         vlen = 1 << L
         leaf = L == log2_queries - 1
-        q = be.alloc(16 * 2 * vlen)
-        be.call("chacha8_prover_secret_fp_rows_device", q, 0, SUMCHECK_SEED, 100 + L, 1, 4 * vlen)
+        q = be.alloc((8 if leaf else 16) * 2 * vlen)
+        be.call("chacha8_prover_secret_fp_rows_device", q, 0, SUMCHECK_SEED, 100 + L, 1, (2 if leaf else 4) * vlen)
         p = 0
         if not leaf:
             p = be.alloc(16 * 2 * vlen)
@@ -328,11 +330,12 @@ def logup_step0_replica(be, log2_queries: int, reps: int = 10):
         be.call("chacha8_prover_secret_fp_rows_device", s, 0, SUMCHECK_SEED, 300 + L, 1, vlen)
         bufs += [x for x in (p, q, s) if x]
         j = RoundJob()
-        j.kind, j.flags, j.len = 0, 1 if leaf else 0, vlen
+        j.kind, j.flags, j.len = 0, 3 if leaf else 0, vlen
+        j.q_alpha[0], j.q_alpha[1] = 5, 7
         j.in_id[0], j.in_id[1] = p, q
         j.s_id, j.msg_id, j.msg_offset = s, msg, 4 * len(jobs)
         jobs.append(j)
-        nbytes += (0 if leaf else 32 * vlen) + 32 * vlen + 16 * (vlen // 2)
+        nbytes += (16 * vlen if leaf else 64 * vlen) + 16 * (vlen // 2)
     arr = (RoundJob * len(jobs))(*jobs)
     call = lambda: be.check(be.lib.volta_b200_logup_round_batch_device(be.ctx, C.cast(arr, C.c_void_p), len(jobs)),
                             "logup_round_batch")  # noqa: E731

@@ -137,9 +137,15 @@ int volta_b200_logup_layers_device(void* ctx, const vzb_layer_job* jobs, size_t 
  * (logup materialize_leaves).  The numerators are then neither read nor
  * written, except that kind 3 writes ones into out_id[0] and out_id[1]; the
  * results equal those of the same job on all-one numerators.
+ * flags bit 1 (VZB_ROUND_Q_COLUMN, kinds 0 and 1 with P_ONE): the children
+ * are the leaves themselves, read from a query column: in_id[1] is that
+ * column (u64 Fp values f_j from in_offset[0]) and child j's denominator is
+ * (q_alpha[0] - f_j, q_alpha[1]) (materialize_leaves of the packed leaf
+ * alpha0 - f_j), so neither the leaves nor their denominators are stored.
  * Outputs of different jobs must not overlap each other or any input.
  */
 #define VZB_ROUND_P_ONE 1u
+#define VZB_ROUND_Q_COLUMN 2u
 typedef struct vzb_round_job {
     uint32_t kind;
     uint32_t flags;
@@ -153,8 +159,18 @@ typedef struct vzb_round_job {
     size_t s_offset;
     uint64_t msg_id;
     size_t msg_offset;
+    uint64_t q_alpha[2];
 } vzb_round_job;
 int volta_b200_logup_round_batch_device(void* ctx, const vzb_round_job* jobs, size_t count);
+
+/*
+ * volta_cuda_logup_tree_device for a side without multiplicities whose leaves
+ * are alpha0 - f_j for a single query column f (pack_lookup_leaf_device with
+ * one column at shift 0): the same tree, without the packed leaf column.
+ */
+int volta_b200_logup_tree_column_device(void* ctx, uint64_t col_id, size_t col_offset, uint64_t alpha0, size_t n,
+                                        uint64_t alpha1, uint64_t p_id, size_t p_offset, uint64_t q_id,
+                                        size_t q_offset);
 
 /*
  * Suffix-eq tables of several layers at once: job j writes exactly what

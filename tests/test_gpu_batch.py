@@ -19,7 +19,8 @@ class RoundJob(C.Structure):
     _fields_ = [("kind", C.c_uint32), ("flags", C.c_uint32), ("in_id", C.c_uint64 * 4),
                 ("in_offset", C.c_size_t * 4), ("len", C.c_size_t), ("r", C.c_uint64 * 2),
                 ("out_id", C.c_uint64 * 4), ("out_offset", C.c_size_t * 4), ("s_id", C.c_uint64),
-                ("s_offset", C.c_size_t), ("msg_id", C.c_uint64), ("msg_offset", C.c_size_t)]
+                ("s_offset", C.c_size_t), ("msg_id", C.c_uint64), ("msg_offset", C.c_size_t),
+                ("q_alpha", C.c_uint64 * 2)]
 
 
 @pytest.fixture(scope="module")
@@ -171,7 +172,7 @@ def test_round_batch_rejects_bad_jobs(be):
     bad.kind = 4
     assert run_batch(be, [bad]) == -1 and "kind" in be.last_error()
     bad = RoundJob.from_buffer_copy(job)
-    bad.flags = 2
+    bad.flags = 4
     assert run_batch(be, [bad]) == -1 and "flags" in be.last_error()
     bad = RoundJob.from_buffer_copy(job)
     bad.len = 6
@@ -228,3 +229,45 @@ def test_suffix_eq_batch_matches_single_layer_calls(be):
     assert be.lib.volta_b200_logup_suffix_eq_batch_device(be.ctx, C.cast(ok, C.c_void_p), 1) == 0, be.last_error()
     be.free(small)
     be.free(pid)
+
+
+@pytest.mark.parametrize("kind,length", [(0, 2), (1, 4), (0, 1 << 16), (1, 1 << 15), (1, 1 << 18)])
+def test_round_batch_leaf_children_from_column(be, oracle, kind, length):
+    """VZB_ROUND_Q_COLUMN: children j = (p = 1, q = (a0 - f_j, a1)) read from a
+    query column equal the same job on materialised leaves."""
+    rng = np.random.default_rng(kind * 100 + length)
+    a0, a1 = (int(x) for x in rng.integers(0, P, size=2, dtype=np.uint64))
+    off = 3
+    f = rng.integers(0, P, size=off + 2 * length, dtype=np.uint64)
+    # leaves on the host: q_j = (a0 - f_j mod p, a1)
+    qc0 = np.array([(a0 - int(v)) % P for v in f[off:]], dtype=np.uint64)
+    Q = np.stack([qc0, np.full_like(qc0, a1)], axis=1)
+    v = [np.tile(np.array([[1, 0]], dtype=np.uint64), (length, 1)) for _ in range(2)]
+    v += [np.ascontiguousarray(Q[0::2]), np.ascontiguousarray(Q[1::2])]
+    r = tuple(int(t) for t in rand_fp2(rng, 1)[0])
+    pairs = length // 4 if kind == 1 else length // 2
+    suffix = rand_fp2(rng, pairs)
+    fid, sid, msg = be.upload_new(f), be.upload_new(suffix), be.alloc(64)
+    job = RoundJob()
+    job.kind, job.len, job.flags = kind, length, 3
+    job.r[0], job.r[1] = r
+    job.q_alpha[0], job.q_alpha[1] = a0, a1
+    job.in_id[1], job.in_offset[0] = fid, off
+    job.s_id, job.msg_id = sid, msg
+    outs = []
+    if kind == 1:
+        for k in (2, 3):
+            job.out_id[k] = be.alloc(16 * (length // 2))
+            outs.append(job.out_id[k])
+    assert run_batch(be, [job]) == 0, be.last_error()
+    after = [oracle.fold_rows(t, 1, length, r) for t in v] if kind == 1 else v
+    assert np.array_equal(be.download_fp2(msg, 4), oracle.logup_general_round(*after, suffix, pairs))
+    if kind == 1:
+        for k, o in zip((2, 3), outs):
+            assert np.array_equal(be.download_fp2(o, length // 2), after[k])
+    # the flag needs all-one numerators and kind 0 or 1
+    bad = RoundJob.from_buffer_copy(job)
+    bad.flags = 2
+    assert run_batch(be, [bad]) == -1 and "numerators" in be.last_error()
+    for t in [fid, sid, msg] + outs:
+        be.free(t)

@@ -30,11 +30,12 @@ __device__ __forceinline__ void combine(Fp2 pa, Fp2 pb, Fp2 qa, Fp2 qb, Fp2& p, 
 
 // Combine `levels` times starting from a child level of 2^child_bits entries.
 // first == true: children are leaves (a_i, alpha1) with numerators 1 or -mult.
-template <bool kFirst>
+// kColumn: the leaves are alpha0 - leaf[i] (`leaf` is a query column).
+template <bool kFirst, bool kColumn = false>
 __global__ void __launch_bounds__(256) tree_tile_kernel(
     const uint64_t* __restrict__ leaf, const uint32_t* __restrict__ mult, const Fp2* cp,
     const Fp2* cq, Fp2* p, Fp2* q, int child_bits, int levels, uint64_t alpha1, uint64_t w7a1sq,
-    int neg_mult) {
+    int neg_mult, uint64_t alpha0 = 0) {
     __shared__ Fp2 sp[kTreeTile / 2], sq[kTreeTile / 2];
     const size_t tile = size_t{1} << levels;  // children handled by this block
     const size_t child0 = static_cast<size_t>(blockIdx.x) * tile;
@@ -47,7 +48,11 @@ __global__ void __launch_bounds__(256) tree_tile_kernel(
         for (size_t i = threadIdx.x; i < half; i += blockDim.x) {
             Fp2 pv, qv;
             if (kFirst) {
-                const uint64_t a = __ldcs(leaf + child0 + 2 * i), b = __ldcs(leaf + child0 + 2 * i + 1);
+                uint64_t a = __ldcs(leaf + child0 + 2 * i), b = __ldcs(leaf + child0 + 2 * i + 1);
+                if (kColumn) {
+                    a = dsub(alpha0, a);
+                    b = dsub(alpha0, b);
+                }
                 const uint64_t sum = dadd(a, b);
                 if (neg_mult) {
                     const uint64_t ma = __ldcs(mult + child0 + 2 * i), mb = __ldcs(mult + child0 + 2 * i + 1);
@@ -104,7 +109,7 @@ __global__ void materialize_leaves_kernel(const uint64_t* leaf, const uint32_t* 
 }
 
 int build_tree(Context* c, const uint64_t* leaf, const uint32_t* mult, size_t n, uint64_t alpha1,
-               int neg_mult, Fp2* p, Fp2* q) {
+               int neg_mult, Fp2* p, Fp2* q, bool column = false, uint64_t alpha0 = 0) {
     int depth = 0;
     while ((size_t{1} << depth) < n) ++depth;
     const uint64_t w7a1sq = fmul7(fmul(alpha1, alpha1));
@@ -113,7 +118,11 @@ int build_tree(Context* c, const uint64_t* leaf, const uint32_t* mult, size_t n,
     while (child_bits > 0) {
         const int levels = child_bits < kTreeTileBits ? child_bits : kTreeTileBits;
         const unsigned blocks = static_cast<unsigned>((size_t{1} << child_bits) >> levels);
-        if (first) {
+        if (first && column) {
+            tree_tile_kernel<true, true><<<blocks, 256, 0, c->stream>>>(leaf, nullptr, nullptr, nullptr, p, q,
+                                                                        child_bits, levels, alpha1, w7a1sq, 0,
+                                                                        alpha0);
+        } else if (first) {
             tree_tile_kernel<true><<<blocks, 256, 0, c->stream>>>(leaf, mult, nullptr, nullptr, p, q,
                                                                   child_bits, levels, alpha1, w7a1sq,
                                                                   neg_mult);
@@ -195,6 +204,24 @@ extern "C" int volta_cuda_logup_materialize_leaves_device(void* raw, uint64_t le
         static_cast<const uint64_t*>(leaf), static_cast<const uint32_t*>(mult), static_cast<Fp2*>(p),
         static_cast<Fp2*>(q), n, alpha1, neg_mult);
     VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpLogup, 0, 0);
+}
+
+extern "C" int volta_b200_logup_tree_column_device(void* raw, uint64_t col_id, size_t col_off, uint64_t alpha0,
+                                                   size_t n, uint64_t alpha1, uint64_t p_id, size_t p_off,
+                                                   uint64_t q_id, size_t q_off) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || n < 2 || (n & (n - 1)) || alpha0 >= kP || alpha1 >= kP)
+        return fail_message(c, "invalid resident LogUp column-tree geometry");
+    void *col = nullptr, *p = nullptr, *q = nullptr;
+    if (region_elems(c, col_id, col_off, n, sizeof(uint64_t), &col) ||
+        region_elems(c, p_id, p_off, n - 1, sizeof(Fp2), &p) || region_elems(c, q_id, q_off, n - 1, sizeof(Fp2), &q))
+        return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (build_tree(c, static_cast<const uint64_t*>(col), nullptr, n, alpha1, 0, static_cast<Fp2*>(p),
+                   static_cast<Fp2*>(q), true, alpha0))
+        return -1;
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpLogup, 0, 0);
 }

@@ -1683,6 +1683,60 @@ struct QFoldEvalIL {
     }
 };
 
+// Leaf-layer children read from the query column: child j's denominator is
+// (a0 - f_j, a1).  The product of two such values is
+// (x y + 7 a1^2, a1 (x + y)): two base products instead of an Fp2 product.
+__device__ __forceinline__ Fp2 leaf_q_mul(uint64_t x, uint64_t y, uint64_t a1, uint64_t w7a1sq) {
+    return Fp2{dadd(dmul(x, y), w7a1sq), dmul(a1, dadd(x, y))};
+}
+
+// kind 0, all-one numerators, children from the query column
+struct QColEvalIL {
+    const uint64_t* f;
+    const Fp2* s;
+    uint64_t a0, a1, w7a1sq;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        const uint64_t x0 = dsub(a0, __ldcs(f + 4 * i)), x1 = dsub(a0, __ldcs(f + 4 * i + 1));
+        const uint64_t x2 = dsub(a0, __ldcs(f + 4 * i + 2)), x3 = dsub(a0, __ldcs(f + 4 * i + 3));
+        // c = q0 = (x0, x2), d = q1 = (x1, x3); every c1 part is a1, every t c1 part 2 a1
+        const uint64_t two_a1 = dadd(a1, a1);
+        const uint64_t t0 = dadd(x0, x1), t1 = dadd(x2, x3);
+        const uint64_t t2 = dadd(t1, dsub(t1, t0));
+        const uint64_t c2 = dadd(x2, dsub(x2, x0)), d2 = dadd(x3, dsub(x3, x1));
+        const Fp2 si = ldg2(s + i);
+        f2w_mac(w[0], si, Fp2{t0, two_a1});
+        f2w_mac(w[1], si, Fp2{t2, two_a1});
+        f2w_mac(w[2], si, leaf_q_mul(x0, x1, a1, w7a1sq));
+        f2w_mac(w[3], si, leaf_q_mul(c2, d2, a1, w7a1sq));
+    }
+};
+
+// kind 1, all-one numerators, children from the query column: the folds of
+// (xa, a1), (xb, a1) are (xa + r.c0 d, a1 + r.c1 d), d = xb - xa in Fp
+struct QColFoldEvalIL {
+    const uint64_t* f;
+    const Fp2* s;
+    Fp2 *o2, *o3;
+    Fp2 r;
+    uint64_t a0, a1;
+    __device__ __forceinline__ Fp2 fold(uint64_t xa, uint64_t xb) const {
+        const uint64_t d = dsub(xb, xa);
+        return Fp2{dadd(xa, dmul(r.c0, d)), dadd(a1, dmul(r.c1, d))};
+    }
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        uint64_t x[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = dsub(a0, __ldcs(f + 8 * i + k));
+        const Fp2 c0 = fold(x[0], x[2]), c1 = fold(x[4], x[6]);
+        const Fp2 d0 = fold(x[1], x[3]), d1 = fold(x[5], x[7]);
+        st2(o2 + 2 * i, c0);
+        st2(o2 + 2 * i + 1, c1);
+        st2(o3 + 2 * i, d0);
+        st2(o3 + 2 * i + 1, d1);
+        q_round_terms(c0, c1, d0, d1, ldg2(s + i), w);
+    }
+};
+
 // kind 2 with all-one numerators
 struct QFoldEval {
     const Fp2 *q0, *q1, *s;
@@ -1706,6 +1760,9 @@ enum BatchKind : uint32_t { kBatchRoundIL = 0, kBatchFoldRoundIL = 1, kBatchFold
 struct BatchJob {
     uint32_t kind;
     uint32_t p_one;           // numerators all 1: not read, not written (kind 3 writes ones)
+    uint32_t q_col;           // children are (a0 - f_j, a1) from the column `col`
+    const uint64_t* col;
+    uint64_t a0, a1, w7a1sq;
     uint32_t block0, blocks;  // CTA range [block0, block0 + blocks)
     size_t items;
     const Fp2 *in0, *in1, *in2, *in3;
@@ -1767,7 +1824,7 @@ struct MsgStoreEpi {
 // CTA b runs the job whose range holds b: a grid-stride loop over that
 // job's items with the job's own CTA count as the stride, then the job's
 // grid reduction.  Fold-only jobs skip the reduction.
-__global__ void __launch_bounds__(kReduceThreads) logup_round_batch_kernel(const __grid_constant__ RoundBatch batch,
+__global__ void __launch_bounds__(kReduceThreads, 2) logup_round_batch_kernel(const __grid_constant__ RoundBatch batch,
                                                                           Fp2* partials, unsigned* counters) {
     unsigned j = 0;
     while (j + 1 < batch.count && blockIdx.x >= batch.job[j + 1].block0) ++j;
@@ -1796,7 +1853,15 @@ __global__ void __launch_bounds__(kReduceThreads) logup_round_batch_kernel(const
     Fp2W w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) f2w_zero(w[k]);
-    if (jb.p_one) {
+    if (jb.q_col) {
+        if (jb.kind == kBatchRoundIL) {
+            const QColEvalIL ev{jb.col, jb.s, jb.a0, jb.a1, jb.w7a1sq};
+            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+        } else {
+            const QColFoldEvalIL ev{jb.col, jb.s, jb.out2, jb.out3, jb.r, jb.a0, jb.a1};
+            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+        }
+    } else if (jb.p_one) {
         if (jb.kind == kBatchRoundIL) {
             const QEvalIL ev{jb.in1, jb.s};
             for (size_t i = first; i < jb.items; i += stride) ev(i, w);
@@ -1839,9 +1904,15 @@ extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_jo
         const size_t len = q.len;
         d.kind = q.kind;
         if (q.kind > kBatchFold) return fail_message(c, "invalid LogUp round batch job kind");
-        if (q.flags & ~VZB_ROUND_P_ONE) return fail_message(c, "invalid LogUp round batch job flags");
+        if (q.flags & ~(VZB_ROUND_P_ONE | VZB_ROUND_Q_COLUMN)) return fail_message(c, "invalid LogUp round batch job flags");
         const bool one = (q.flags & VZB_ROUND_P_ONE) != 0;
+        const bool qcol = (q.flags & VZB_ROUND_Q_COLUMN) != 0;
+        if (qcol && (!one || q.kind > kBatchFoldRoundIL))
+            return fail_message(c, "LogUp round batch: column children need all-one numerators and kind 0 or 1");
+        if (qcol && (q.q_alpha[0] >= kP || q.q_alpha[1] >= kP))
+            return fail_message(c, "LogUp round batch: leaf constants are not canonical");
         d.p_one = one ? 1u : 0u;
+        d.q_col = qcol ? 1u : 0u;
         const bool il = q.kind <= kBatchFoldRoundIL, fold = q.kind != kBatchRoundIL;
         if (len < (fold ? 4u : 2u) || (len & (fold ? 3 : 1)))
             return fail_message(c, "invalid LogUp round batch job length");
@@ -1849,7 +1920,14 @@ extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_jo
         d.r = Fp2{q.r[0], q.r[1]};
         void* p[4] = {nullptr, nullptr, nullptr, nullptr};
         // with all-one numerators P (kinds 0, 1) or p0, p1 (kinds 2, 3) are not read
-        if (il) {
+        if (qcol) {  // the query column: 2 len u64 values (the children)
+            void* col = nullptr;
+            if (region_elems(c, q.in_id[1], q.in_offset[0], 2 * len, sizeof(uint64_t), &col)) return -1;
+            d.col = static_cast<const uint64_t*>(col);
+            d.a0 = q.q_alpha[0];
+            d.a1 = q.q_alpha[1];
+            d.w7a1sq = fmul7(fmul(q.q_alpha[1], q.q_alpha[1]));
+        } else if (il) {
             for (int k = one ? 1 : 0; k < 2; ++k)
                 if (region_elems(c, q.in_id[k], q.in_offset[0], 2 * len, sizeof(Fp2), &p[k])) return -1;
         } else {

@@ -129,6 +129,8 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         dlsym(handle_, "volta_b200_triple_fold_round_fp_into_device"));
     ext_loaded_->wait_uploads =
         reinterpret_cast<decltype(ext_loaded_->wait_uploads)>(dlsym(handle_, "volta_b200_wait_uploads"));
+    ext_loaded_->logup_tree_column = reinterpret_cast<decltype(ext_loaded_->logup_tree_column)>(
+        dlsym(handle_, "volta_b200_logup_tree_column_device"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

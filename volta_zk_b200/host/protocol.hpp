@@ -84,8 +84,11 @@ struct PendingSide {
     std::vector<std::vector<vzb_round_job>> plan;
     std::vector<vzb_layer_job> jobs;
 };
+// leaf: the packed leaf column, or 0 with `col` and `alpha0` given (a side
+// without multiplicities; leaf j = alpha0 - col_j).
 PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mult, size_t n_local,
-                              uint64_t alpha1, size_t shard_bits, const SideSchedule& sch);
+                              uint64_t alpha1, size_t shard_bits, const SideSchedule& sch, uint64_t col = 0,
+                              uint64_t alpha0 = 0);
 // Launch the batched work of several sides together: one suffix-table batch,
 // step t of every large layer of every side per launch, one launch of all
 // one-CTA jobs.

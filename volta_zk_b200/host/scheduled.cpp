@@ -159,7 +159,8 @@ SideSchedule draw_side_schedule(FpStream& chal, size_t depth) {
 // eq(top bits of the point, g), and keeps the four vector values left over.
 // With shard_bits = 0 these are the whole rounds and the splits.
 PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mult, size_t n_local,
-                              uint64_t alpha1, size_t shard_bits, const SideSchedule& sch) {
+                              uint64_t alpha1, size_t shard_bits, const SideSchedule& sch, uint64_t col,
+                              uint64_t alpha0) {
     const Api& A = b.api();
     const ExtApi& X = b.ext();
     void* ctx = b.ctx();
@@ -192,8 +193,27 @@ PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mu
     const uint64_t msgs = own.add(b.alloc(msg_total * sizeof(Fp2)));
     const uint64_t tp = own.add(b.alloc((n_local - 1) * sizeof(Fp2)));
     const uint64_t tq = own.add(b.alloc((n_local - 1) * sizeof(Fp2)));
-    b.check(A.volta_cuda_logup_tree_device(ctx, leaf, 0, mult, 0, n_local, alpha1, mult ? 1 : 0, tp, 0, tq, 0),
-            "logup_tree_device");
+    // A side without multiplicities given as its query column (leaf j = alpha0
+    // - col_j) whose leaf layer runs as cross-layer batches: the tree and the
+    // leaf layer's first two steps read the column, so the packed leaves and
+    // the materialised leaf denominators are never stored.
+    const bool col_path = col && !mult && X.logup_tree_column && X.logup_round_batch && b.batched() &&
+                          X.logup_layers && n_local / 4 > kTailLen;
+    if (col_path) {
+        b.check(X.logup_tree_column(ctx, col, 0, alpha0, n_local, alpha1, tp, 0, tq, 0),
+                "volta_b200_logup_tree_column_device");
+    } else {
+        if (!leaf) {  // pack the leaf column: alpha0 - col
+            const uint32_t zero_shift = 0;
+            const uint64_t shifts = own.add(b.alloc(sizeof(uint32_t)));
+            b.upload(shifts, 0, &zero_shift, sizeof(zero_shift));
+            leaf = own.add(b.alloc(n_local * sizeof(uint64_t)));
+            b.check(A.volta_cuda_pack_lookup_leaf_device(ctx, col, 0, shifts, 0, leaf, 0, 1, n_local, alpha0),
+                    "pack_lookup_leaf_device");
+        }
+        b.check(A.volta_cuda_logup_tree_device(ctx, leaf, 0, mult, 0, n_local, alpha1, mult ? 1 : 0, tp, 0, tq, 0),
+                "logup_tree_device");
+    }
     b.check(A.volta_cuda_resident_copy_rows(ctx, tp, 0, sizeof(Fp2), msgs, 0, sizeof(Fp2), 1, sizeof(Fp2)),
             "resident_copy_rows");
     b.check(A.volta_cuda_resident_copy_rows(ctx, tq, 0, sizeof(Fp2), msgs, sizeof(Fp2), sizeof(Fp2), 1,
@@ -241,7 +261,11 @@ PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mu
         uint64_t src_p = tp, src_q = tq;
         size_t child_off = child_len - 1;
         const bool small = jobs_on && vector_len <= kTailLen;
-        if (l + 1 == depth) {  // the leaf layer's children are the materialised leaves
+        if (l + 1 == depth && col_path) {  // the leaf layer's children come from the column
+            src_p = 0;
+            src_q = col;
+            child_off = 0;
+        } else if (l + 1 == depth) {  // the leaf layer's children are the materialised leaves
             Owned& keep = (small || batch_on) ? own : layer;  // a job or batch reads them after this loop
             src_p = keep.add(b.alloc(n_local * sizeof(Fp2)));
             src_q = keep.add(b.alloc(n_local * sizeof(Fp2)));
@@ -285,6 +309,7 @@ PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mu
             // that the fold feeding the one-CTA tail writes the ones
             const uint32_t flags =
                 (l + 1 == depth && !mult && vector_len / 2 > kTailLen) ? VZB_ROUND_P_ONE : 0u;
+            const bool from_col = l + 1 == depth && col_path;  // (col_path implies flags)
             std::vector<vzb_round_job> steps;
             auto challenge = [&](vzb_round_job& q, size_t j) {
                 q.r[0] = sch.r[l][j].c0;
@@ -293,7 +318,9 @@ PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mu
             // round 0 and (fold 0 + round 1) on the interleaved children
             vzb_round_job q{};
             q.kind = 0;
-            q.flags = flags;
+            q.flags = flags | (from_col ? VZB_ROUND_Q_COLUMN : 0u);
+            q.q_alpha[0] = alpha0;
+            q.q_alpha[1] = alpha1;
             q.in_id[0] = src_p;
             q.in_id[1] = src_q;
             q.in_offset[0] = child_off;
@@ -516,15 +543,20 @@ PendingLogup logup_local_enqueue(Backend& b, Owned& own, uint64_t f_col, size_t 
     const uint64_t cols[2] = {f_col, t_col};
     const size_t ns[2] = {n_f_local, n_t_local};
     for (int side = 0; side < 2; ++side) {
-        const uint64_t leaf = own.add(b.alloc(ns[side] * sizeof(uint64_t)));
-        b.check(A.volta_cuda_pack_lookup_leaf_device(b.ctx(), cols[side], 0, shifts, 0, leaf, 0, 1, ns[side],
-                                                     pl.alpha.c0),
-                "pack_lookup_leaf_device");
+        // the side without multiplicities passes its column: frac_side_enqueue
+        // reads it directly where it can, else packs the leaves itself
+        uint64_t leaf = 0;
+        if (side == 1) {
+            leaf = own.add(b.alloc(ns[side] * sizeof(uint64_t)));
+            b.check(A.volta_cuda_pack_lookup_leaf_device(b.ctx(), cols[side], 0, shifts, 0, leaf, 0, 1, ns[side],
+                                                         pl.alpha.c0),
+                    "pack_lookup_leaf_device");
+        }
         size_t local_depth = 0;
         while ((size_t{1} << local_depth) < ns[side]) ++local_depth;
         pl.sch[side] = draw_side_schedule(chal, local_depth + shard_bits);
-        pl.side[side] =
-            frac_side_enqueue(b, own, leaf, side ? mult : 0, ns[side], pl.alpha.c1, shard_bits, pl.sch[side]);
+        pl.side[side] = frac_side_enqueue(b, own, leaf, side ? mult : 0, ns[side], pl.alpha.c1, shard_bits,
+                                          pl.sch[side], cols[side], pl.alpha.c0);
     }
     launch_side_work(b, {&pl.side[0], &pl.side[1]});  // both sides' batches share launches
     return pl;
