@@ -507,7 +507,7 @@ def run_b200(args, rank, world, local_rank):
     achieved = batch_bytes / (batch_ms / 1e3) / 1e9
     # DRAM read + write bytes per algorithmic byte of this launch, from the ncu
     # capture of the 2^22-query replica (profiles/logup_round_batch_step0_2p22queries.md)
-    traffic_ratio = (234.784512e6 + 4.759808e6) / 235110400
+    traffic_ratio = (201.150720e6 + 3.792640e6) / 201031680
     roofline = {"bound": "hbm",
                 "kernel": f"logup_round_batch_kernel: step 0 of the 2^{args.log2_queries}-query side "
                           f"({batch_jobs} layers in one launch, the proof's largest launch)",
