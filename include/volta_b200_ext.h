@@ -142,10 +142,16 @@ int volta_b200_logup_layers_device(void* ctx, const vzb_layer_job* jobs, size_t 
  * column (u64 Fp values f_j from in_offset[0]) and child j's denominator is
  * (q_alpha[0] - f_j, q_alpha[1]) (materialize_leaves of the packed leaf
  * alpha0 - f_j), so neither the leaves nor their denominators are stored.
+ * flags bit 2 (VZB_ROUND_PARENTS, kind 0 without P_ONE): out_id[0] and
+ * out_id[1] (from out_offset[0], len entries each) hold the layer's own tree
+ * level, the parents of the children: for pair i, a0 d0 + b0 c0 and c0 d0 are
+ * the parent p and q at index 2 i (p = pa qb + pb qa, q = qa qb), so they are
+ * read instead of recomputed.  Correct only when they are those parents.
  * Outputs of different jobs must not overlap each other or any input.
  */
 #define VZB_ROUND_P_ONE 1u
 #define VZB_ROUND_Q_COLUMN 2u
+#define VZB_ROUND_PARENTS 4u
 typedef struct vzb_round_job {
     uint32_t kind;
     uint32_t flags;

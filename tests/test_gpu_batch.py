@@ -172,7 +172,7 @@ def test_round_batch_rejects_bad_jobs(be):
     bad.kind = 4
     assert run_batch(be, [bad]) == -1 and "kind" in be.last_error()
     bad = RoundJob.from_buffer_copy(job)
-    bad.flags = 4
+    bad.flags = 8  # no such flag
     assert run_batch(be, [bad]) == -1 and "flags" in be.last_error()
     bad = RoundJob.from_buffer_copy(job)
     bad.len = 6
@@ -270,4 +270,46 @@ def test_round_batch_leaf_children_from_column(be, oracle, kind, length):
     bad.flags = 2
     assert run_batch(be, [bad]) == -1 and "numerators" in be.last_error()
     for t in [fid, sid, msg] + outs:
+        be.free(t)
+
+
+def _fp2_mul(x, y):
+    return ((x[0] * y[0] + 7 * x[1] * y[1]) % P, (x[0] * y[1] + x[1] * y[0]) % P)
+
+
+@pytest.mark.parametrize("length", [2, 64, 1 << 12])
+def test_round_batch_parents_shortcut(be, oracle, length):
+    """VZB_ROUND_PARENTS: round 0 with the parent level given equals round 0
+    computed from the children alone."""
+    rng = np.random.default_rng(length + 5)
+    P_ = rand_fp2(rng, 2 * length)
+    Q_ = rand_fp2(rng, 2 * length)
+    par_p, par_q = np.zeros((length, 2), dtype=np.uint64), np.zeros((length, 2), dtype=np.uint64)
+    for j in range(length):  # parent j of children (2j, 2j + 1): p = pa qb + pb qa, q = qa qb
+        pa, pb = tuple(int(t) for t in P_[2 * j]), tuple(int(t) for t in P_[2 * j + 1])
+        qa, qb = tuple(int(t) for t in Q_[2 * j]), tuple(int(t) for t in Q_[2 * j + 1])
+        x, y = _fp2_mul(pa, qb), _fp2_mul(pb, qa)
+        par_p[j] = ((x[0] + y[0]) % P, (x[1] + y[1]) % P)
+        par_q[j] = _fp2_mul(qa, qb)
+    off = 2
+    suffix = rand_fp2(rng, length // 2)
+    ids = [be.upload_new(P_), be.upload_new(Q_), be.upload_new(np.concatenate([rand_fp2(rng, off), par_p])),
+           be.upload_new(np.concatenate([rand_fp2(rng, off), par_q])), be.upload_new(suffix), be.alloc(16 * 8)]
+    plain = RoundJob()
+    plain.kind, plain.len = 0, length
+    plain.in_id[0], plain.in_id[1] = ids[0], ids[1]
+    plain.s_id, plain.msg_id = ids[4], ids[5]
+    par = RoundJob.from_buffer_copy(plain)
+    par.flags = 4
+    par.out_id[0], par.out_id[1], par.out_offset[0] = ids[2], ids[3], off
+    par.msg_offset = 4
+    assert run_batch(be, [plain, par]) == 0, be.last_error()
+    msgs = be.download_fp2(ids[5], 8)
+    assert np.array_equal(msgs[:4], msgs[4:])
+    v = [np.ascontiguousarray(x) for x in (P_[0::2], P_[1::2], Q_[0::2], Q_[1::2])]
+    assert np.array_equal(msgs[:4], oracle.logup_general_round(*v, suffix, length // 2))
+    bad = RoundJob.from_buffer_copy(par)
+    bad.flags = 5  # with all-one numerators: rejected
+    assert run_batch(be, [bad]) == -1 and "parents" in be.last_error()
+    for t in ids:
         be.free(t)

@@ -506,7 +506,7 @@ struct EqJob {
     Fp2* out;
     const Fp2* scale_dev;  // optional device-resident factor
 };
-constexpr int kMaxEqJobs = 96;
+constexpr int kMaxEqJobs = 320;
 struct EqJobs {
     EqJob job[kMaxEqJobs];
     int count;
@@ -1683,6 +1683,27 @@ struct QFoldEvalIL {
     }
 };
 
+// kind 0 with the parents given: the t = 0 terms a0 d0 + b0 c0 and c0 d0 of
+// pair i are the parent node 2 i's p and q (its tree level PP, PQ).
+struct LogupEvalILPar {
+    const Fp2 *P, *Q, *s, *PP, *PQ;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        const Fp2 a0 = ldcs2(P + 4 * i), b0 = ldcs2(P + 4 * i + 1), a1 = ldcs2(P + 4 * i + 2), b1 = ldcs2(P + 4 * i + 3);
+        const Fp2 c0 = ldcs2(Q + 4 * i), d0 = ldcs2(Q + 4 * i + 1), c1 = ldcs2(Q + 4 * i + 2), d1 = ldcs2(Q + 4 * i + 3);
+        const Fp2 si = ldg2(s + i), pp = ldcs2(PP + 2 * i), pq = ldcs2(PQ + 2 * i);
+        const Fp2 a2 = d2add_weak(a1, d2sub(a1, a0)), b2 = d2add_weak(b1, d2sub(b1, b0));
+        const Fp2 c2 = d2add_weak(c1, d2sub(c1, c0)), d2 = d2add_weak(d1, d2sub(d1, d0));
+        Fp2W t;
+        f2w_zero(t);
+        f2w_mac(t, a2, d2);
+        f2w_mac(t, b2, c2);
+        f2w_mac(w[0], si, pp);
+        f2w_mac(w[1], si, f2w_reduce(t));
+        f2w_mac(w[2], si, pq);
+        f2w_mac(w[3], si, d2mul(c2, d2));
+    }
+};
+
 // Leaf-layer children read from the query column: child j's denominator is
 // (a0 - f_j, a1).  The product of two such values is
 // (x y + 7 a1^2, a1 (x + y)): two base products instead of an Fp2 product.
@@ -1761,6 +1782,8 @@ struct BatchJob {
     uint32_t kind;
     uint32_t p_one;           // numerators all 1: not read, not written (kind 3 writes ones)
     uint32_t q_col;           // children are (a0 - f_j, a1) from the column `col`
+    uint32_t parents;         // kind 0: the parent level is given (pp, pq)
+    const Fp2 *pp, *pq;
     const uint64_t* col;
     uint64_t a0, a1, w7a1sq;
     uint32_t block0, blocks;  // CTA range [block0, block0 + blocks)
@@ -1872,6 +1895,9 @@ __global__ void __launch_bounds__(kReduceThreads, 2) logup_round_batch_kernel(co
             const QFoldEval ev{jb.in2, jb.in3, jb.s, jb.out2, jb.out3, jb.r};
             for (size_t i = first; i < jb.items; i += stride) ev(i, w);
         }
+    } else if (jb.kind == kBatchRoundIL && jb.parents) {
+        const LogupEvalILPar ev{jb.in0, jb.in1, jb.s, jb.pp, jb.pq};
+        for (size_t i = first; i < jb.items; i += stride) ev(i, w);
     } else if (jb.kind == kBatchRoundIL) {
         const LogupEvalIL ev{jb.in0, jb.in1, jb.s};
         for (size_t i = first; i < jb.items; i += stride) ev(i, w);
@@ -1904,7 +1930,10 @@ extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_jo
         const size_t len = q.len;
         d.kind = q.kind;
         if (q.kind > kBatchFold) return fail_message(c, "invalid LogUp round batch job kind");
-        if (q.flags & ~(VZB_ROUND_P_ONE | VZB_ROUND_Q_COLUMN)) return fail_message(c, "invalid LogUp round batch job flags");
+        if (q.flags & ~(VZB_ROUND_P_ONE | VZB_ROUND_Q_COLUMN | VZB_ROUND_PARENTS))
+            return fail_message(c, "invalid LogUp round batch job flags");
+        if ((q.flags & VZB_ROUND_PARENTS) && (q.kind != kBatchRoundIL || (q.flags & VZB_ROUND_P_ONE)))
+            return fail_message(c, "LogUp round batch: parents need kind 0 without all-one numerators");
         const bool one = (q.flags & VZB_ROUND_P_ONE) != 0;
         const bool qcol = (q.flags & VZB_ROUND_Q_COLUMN) != 0;
         if (qcol && (!one || q.kind > kBatchFoldRoundIL))
@@ -1950,6 +1979,15 @@ extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_jo
             d.out3 = static_cast<Fp2*>(o[3]);
         }
         d.items = fold ? len / 4 : len / 2;
+        if (q.flags & VZB_ROUND_PARENTS) {
+            void *pp = nullptr, *pq = nullptr;
+            if (region_elems(c, q.out_id[0], q.out_offset[0], len, sizeof(Fp2), &pp) ||
+                region_elems(c, q.out_id[1], q.out_offset[0], len, sizeof(Fp2), &pq))
+                return -1;
+            d.parents = 1;
+            d.pp = static_cast<const Fp2*>(pp);
+            d.pq = static_cast<const Fp2*>(pq);
+        }
         if (q.kind != kBatchFold) {
             void *sv = nullptr, *mv = nullptr;
             if (region_elems(c, q.s_id, q.s_offset, d.items, sizeof(Fp2), &sv) ||

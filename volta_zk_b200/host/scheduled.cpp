@@ -329,7 +329,15 @@ PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mu
             q.s_offset = (size_t{1} << (L - 1)) - 1;
             q.msg_id = msgs;
             q.msg_offset = moff[l];
+            if (!flags) {  // round 0's t = 0 terms are the layer's own tree level (the children's parents)
+                q.flags |= VZB_ROUND_PARENTS;
+                q.out_id[0] = tp;
+                q.out_id[1] = tq;
+                q.out_offset[0] = vector_len - 1;
+            }
             steps.push_back(q);
+            q.flags &= ~VZB_ROUND_PARENTS;
+            q.out_offset[0] = 0;
             size_t len = vector_len / 2;
             uint64_t v[4] = {0, 0, 0, 0};
             for (int k = flags ? 2 : 0; k < 4; ++k) v[k] = own.add(b.alloc(len * sizeof(Fp2)));
