@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--ligero-queries", type=int, default=128)
     ap.add_argument("--no-ligero", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
+    ap.add_argument("--lanes", type=int, choices=[1, 2], default=2,
+                    help="2: the triple sumcheck and the LogUp proof run concurrently on two contexts")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -370,6 +372,11 @@ def run_b200(args, rank, world, local_rank):
 
     prover = accel.Prover(policy=1)  # resident context, wall-only counters (no event overhead)
     be = prover.backend
+    # lanes = 2: the LogUp proof runs on a second context (its own stream and
+    # workspaces) from a second host thread, concurrently with the triple
+    # sumcheck, so each protocol's latency-bound stretches overlap the other's work
+    prover_b = accel.Prover(policy=1) if args.lanes == 2 else prover
+    be_b = prover_b.backend
     n = 1 << args.log2_sumcheck
     n_f, n_t = 1 << args.log2_queries, 1 << args.log2_table
     if world & (world - 1) or n % world or n_f % world or n_t % (2 * world):
@@ -387,7 +394,7 @@ def run_b200(args, rank, world, local_rank):
     cap = proof_words(n_f, n_t)
     if world == 1:
         shard_tables = tables
-        f_col, t_col, m_col = be.upload_new(embed_i16(f)), be.upload_new(embed_i16(table)), be.upload_new(mult)
+        f_col, t_col, m_col = be_b.upload_new(embed_i16(f)), be_b.upload_new(embed_i16(table)), be_b.upload_new(mult)
     else:
         # this rank's slices: entries [rank n / world, (rank + 1) n / world) of every table and column
         nl = n // world
@@ -398,16 +405,41 @@ def run_b200(args, rank, world, local_rank):
             shard_tables.append(sl)
         fs, ts = slice(rank * n_f // world, (rank + 1) * n_f // world), slice(rank * n_t // world,
                                                                               (rank + 1) * n_t // world)
-        f_col = be.upload_new(np.ascontiguousarray(embed_i16(f)[fs]))
-        t_col = be.upload_new(np.ascontiguousarray(embed_i16(table)[ts]))
-        m_col = be.upload_new(np.ascontiguousarray(mult[ts]))
-        sharded = ShardedProver(prover, rank, world, torch_all_gather(torch.device("cuda", local_rank)))
+        f_col = be_b.upload_new(np.ascontiguousarray(embed_i16(f)[fs]))
+        t_col = be_b.upload_new(np.ascontiguousarray(embed_i16(table)[ts]))
+        m_col = be_b.upload_new(np.ascontiguousarray(mult[ts]))
+        sharded = ShardedProver(prover, rank, world, torch_all_gather(torch.device("cuda", local_rank)),
+                                logup_prover=prover_b if args.lanes == 2 else None)
+
+    def both(run_triple, run_logup):
+        """The two protocols of a proof; on two lanes the LogUp part runs in a
+        second host thread on the second context."""
+        if args.lanes == 1:
+            return run_triple(), run_logup()
+        box = {}
+
+        def worker():
+            try:
+                box["logup"] = run_logup()
+            except BaseException as e:  # re-raised in the main thread
+                box["error"] = e
+
+        th = threading.Thread(target=worker)
+        th.start()
+        try:
+            tri = run_triple()
+        finally:
+            th.join()
+        if "error" in box:
+            raise box["error"]
+        return tri, box["logup"]
 
     def step():
         if world == 1:
-            msgs, finals = prover.triple_sumcheck_fp(tables[0], tables[1], tables[2], n, TRANSCRIPT_SEED)
-            proof = prover.logup_prove(f_col, n_f, t_col, n_t, m_col, LOGUP_SEED, LOGUP_DOMAIN, cap)
-        else:  # one local call (both sumchecks enqueued back to back) and one all-gather per proof
+            (msgs, finals), proof = both(
+                lambda: prover.triple_sumcheck_fp(tables[0], tables[1], tables[2], n, TRANSCRIPT_SEED),
+                lambda: prover_b.logup_prove(f_col, n_f, t_col, n_t, m_col, LOGUP_SEED, LOGUP_DOMAIN, cap))
+        else:  # local work of both protocols, one all-gather per proof
             msgs, finals, proof = sharded.prove(*shard_tables, n, TRANSCRIPT_SEED, f_col, n_f, t_col, n_t, m_col,
                                                 LOGUP_SEED, LOGUP_DOMAIN, base=True)
         return msgs, finals, proof
@@ -427,7 +459,7 @@ def run_b200(args, rank, world, local_rank):
     for _ in range(args.warmup):
         step()
     barrier()
-    launches0 = be.launches()
+    launches0 = be.launches() + (be_b.launches() if be_b is not be else 0)
     with ClockSampler(local_rank) as clocks:
         barrier()
         be.mark(0)
@@ -436,7 +468,7 @@ def run_b200(args, rank, world, local_rank):
         be.mark(1)
         ms = be.elapsed_ms(0, 1)
         barrier()
-    launches = be.launches() - launches0
+    launches = be.launches() + (be_b.launches() if be_b is not be else 0) - launches0
     step_s = max_over_ranks(ms / 1e3 / args.steps)
 
     # ---- e2e through the C ABI with host buffers ---------------------------
@@ -455,26 +487,31 @@ def run_b200(args, rank, world, local_rank):
         f16_h = torch.from_numpy(np.ascontiguousarray(f[rank * nfl:(rank + 1) * nfl]).astype(np.int16)).pin_memory()
         t16_h = torch.from_numpy(np.ascontiguousarray(table[rank * ntl:(rank + 1) * ntl]).astype(np.int16)).pin_memory()
         mult_h = torch.from_numpy(np.ascontiguousarray(mult[rank * ntl:(rank + 1) * ntl]).astype(np.int32)).pin_memory()
-        ups = [be.alloc(8 * nl) for _ in range(3)] + [be.alloc(2 * nfl), be.alloc(2 * ntl), be.alloc(4 * ntl),
-                                                      be.alloc(8 * nfl), be.alloc(8 * ntl)]
-        bufs = ups
+        # the triple tables on the first context, the LogUp inputs on the LogUp lane's
+        ups = [be.alloc(8 * nl) for _ in range(3)] + [be_b.alloc(2 * nfl), be_b.alloc(2 * ntl), be_b.alloc(4 * ntl),
+                                                      be_b.alloc(8 * nfl), be_b.alloc(8 * ntl)]
+        owners = [be] * 3 + [be_b] * 5
         h2d = 3 * 8 * n + 2 * n_f + 2 * n_t + 4 * n_t  # whole job
         d2h = (16 * (3 * args.log2_sumcheck + 3) + 16 * cap) * world
         last = {}
 
         def e2e_step():
             for buf, t in zip(ups[3:6], [f16_h, t16_h, mult_h]):
-                be.upload_async(buf, t.data_ptr(), t.numel() * t.element_size())
-            be.wait_uploads()
+                be_b.upload_async(buf, t.data_ptr(), t.numel() * t.element_size())
+            be_b.wait_uploads()
             for buf, t in zip(ups[:3], pinned):
                 be.upload_async(buf, t.data_ptr(), t.numel() * t.element_size())
-            be.embed_i16(ups[3], ups[6], nfl)
-            be.embed_i16(ups[4], ups[7], ntl)
+            be_b.embed_i16(ups[3], ups[6], nfl)
+            be_b.embed_i16(ups[4], ups[7], ntl)
             if world == 1:
-                last["proof"] = prover.logup_prove(ups[6], n_f, ups[7], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN, cap)
-                be.wait_uploads()
-                last["msgs"], last["finals"] = prover.triple_sumcheck_fp(ups[0], ups[1], ups[2], n, TRANSCRIPT_SEED)
-            else:  # the local call waits for the uploads before its triple part
+                def run_triple():
+                    be.wait_uploads()
+                    return prover.triple_sumcheck_fp(ups[0], ups[1], ups[2], n, TRANSCRIPT_SEED)
+
+                (last["msgs"], last["finals"]), last["proof"] = both(
+                    run_triple,
+                    lambda: prover_b.logup_prove(ups[6], n_f, ups[7], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN, cap))
+            else:  # the triple part waits for its uploads
                 last["msgs"], last["finals"], last["proof"] = sharded.prove(
                     ups[0], ups[1], ups[2], n, TRANSCRIPT_SEED, ups[6], n_f, ups[7], n_t, ups[5], LOGUP_SEED,
                     LOGUP_DOMAIN, base=True)
@@ -493,8 +530,8 @@ def run_b200(args, rank, world, local_rank):
                "inputs": "triple tables as Fp columns, lookup queries and table as int16, multiplicities as u32; "
                          "the triple tables upload while the LogUp part computes",
                "proof_matches_resident": bool(same)}
-        for b in bufs:
-            be.free(b)
+        for owner, b in zip(owners, ups):
+            owner.free(b)
 
     # ---- roofline of the dominant kernel ----------------------------------
     peaks = {}

@@ -91,3 +91,40 @@ def test_proof_local_waits_for_async_tables(prover, oracle):
     assert np.array_equal(got, oracle.logup_prove(f, table, mult, lseed, domain))
     for x in ids + [f16, t16, fe, te, m]:
         be.free(x)
+
+
+def test_two_contexts_concurrently(prover, oracle):
+    """The triple sumcheck on one context and the LogUp proof on another,
+    driven from two host threads at once (bench.py's two lanes), give the
+    oracle's proofs; repeated to let the launches interleave."""
+    from volta_zk_b200 import accel
+
+    other = accel.Prover(policy=1)
+    try:
+        n, nf, nt = 1 << 16, 1 << 15, 1 << 10
+        rng = np.random.default_rng(21)
+        cols = [rng.integers(0, P, size=n, dtype=np.uint64) for _ in range(3)]
+        lifted = [np.stack([x, np.zeros_like(x)], axis=1) for x in cols]
+        table = rng.integers(-32768, 32768, size=nt, dtype=np.int64).astype(np.int16)
+        idx = rng.integers(0, nt, size=nf)
+        f = table[idx]
+        mult = np.bincount(idx, minlength=nt).astype(np.uint32)
+        tseed, lseed, domain = bytes([0x5A] * 32), bytes([0x4C] * 32), 0x1004
+        ids = [prover.backend.upload_new(x) for x in cols]
+        be_b = other.backend
+        lids = [be_b.upload_new(em.embed_i16(f)), be_b.upload_new(em.embed_i16(table)), be_b.upload_new(mult)]
+        em_msgs, em_finals = oracle.triple_sumcheck(*lifted, tseed)
+        em_proof = oracle.logup_prove(f, table, mult, lseed, domain)
+        cap = oracle.logup_prove_words(nf, nt)
+        for _ in range(3):
+            (msgs, finals), proof = sh.concurrently(
+                lambda: prover.triple_sumcheck_fp(*ids, n, tseed),
+                lambda: other.logup_prove(lids[0], nf, lids[1], nt, lids[2], lseed, domain, cap))
+            assert np.array_equal(msgs, em_msgs) and np.array_equal(finals, em_finals)
+            assert np.array_equal(proof, em_proof)
+        for i in ids:
+            prover.backend.free(i)
+        for i in lids:
+            be_b.free(i)
+    finally:
+        other.close()

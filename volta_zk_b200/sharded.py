@@ -50,6 +50,30 @@ def torch_all_gather(device=None) -> AllGather:
     return gather
 
 
+def concurrently(first, second):
+    """Run `second` in another host thread while `first` runs in this one
+    (the library's calls release the GIL); both results, or the first error."""
+    import threading
+
+    box = {}
+
+    def worker():
+        try:
+            box["value"] = second()
+        except BaseException as e:  # re-raised below
+            box["error"] = e
+
+    th = threading.Thread(target=worker)
+    th.start()
+    try:
+        a = first()
+    finally:
+        th.join()
+    if "error" in box:
+        raise box["error"]
+    return a, box["value"]
+
+
 def _host():
     L = load_host_library()
     if not getattr(L, "_sharded_declared", False):
@@ -97,10 +121,13 @@ class ShardedProver:
     """Runs this shard's local work on its GPU through a Prover (the host
     mirror over the seam) and completes the proof after one all-gather."""
 
-    def __init__(self, prover, rank: int, world: int, all_gather: AllGather):
+    def __init__(self, prover, rank: int, world: int, all_gather: AllGather, logup_prover=None):
+        """logup_prover: a second Prover (its own context) on which prove()
+        runs the LogUp part concurrently with the triple part."""
         if world & (world - 1):
             raise ValueError("the shard count must be a power of two")
         self.prover, self.rank, self.world, self.gather = prover, rank, world, all_gather
+        self.logup_prover = logup_prover
         self.s = world.bit_length() - 1
 
     def triple_sumcheck(self, a: int, b: int, c: int, n: int, seed: bytes, base: bool = False):
@@ -117,8 +144,22 @@ class ShardedProver:
         all-gather: (triple messages, triple finals, LogUp proof words), equal
         to triple_sumcheck followed by logup_prove."""
         nl = n // self.world
-        local = self.prover.proof_local(a, b, c, nl, base, triple_seed, f_col, n_f // self.world, t_col,
-                                        n_t // self.world, mult, self.s, logup_seed, domain)
+        if self.logup_prover is None:
+            local = self.prover.proof_local(a, b, c, nl, base, triple_seed, f_col, n_f // self.world, t_col,
+                                            n_t // self.world, mult, self.s, logup_seed, domain)
+        else:
+            def triple_part():
+                self.prover.backend.wait_uploads()  # tables still arriving on the copy stream, if any
+                local_sumcheck = self.prover.triple_sumcheck_fp if base else self.prover.triple_sumcheck
+                m, f = local_sumcheck(a, b, c, nl, triple_seed)
+                return np.concatenate([m, f])
+
+            def logup_part():
+                return self.logup_prover.logup_local(f_col, n_f // self.world, t_col, n_t // self.world, mult,
+                                                     self.s, logup_seed, domain)
+
+            tri, lg = concurrently(triple_part, logup_part)
+            local = np.concatenate([tri, lg])
         parts = self.gather(local)
         kt = 3 * (nl.bit_length() - 1) + 3
         msgs, finals = triple_finish([p[:kt] for p in parts], n, triple_seed)
