@@ -357,7 +357,7 @@ def run_b200(args, rank, world, local_rank):
     import torch
 
     from volta_zk_b200 import accel, build_all
-    from volta_zk_b200.sharded import ShardedProver, torch_all_gather, torch_all_to_all
+    from volta_zk_b200.sharded import ShardedProver, concurrently, torch_all_gather, torch_all_to_all
 
     if not os.path.exists(os.path.join(ROOT, "volta_zk_b200", "libvolta_cuda_backend.so")):
         if rank == 0:
@@ -416,23 +416,7 @@ def run_b200(args, rank, world, local_rank):
         second host thread on the second context."""
         if args.lanes == 1:
             return run_triple(), run_logup()
-        box = {}
-
-        def worker():
-            try:
-                box["logup"] = run_logup()
-            except BaseException as e:  # re-raised in the main thread
-                box["error"] = e
-
-        th = threading.Thread(target=worker)
-        th.start()
-        try:
-            tri = run_triple()
-        finally:
-            th.join()
-        if "error" in box:
-            raise box["error"]
-        return tri, box["logup"]
+        return concurrently(run_triple, run_logup)
 
     def step():
         if world == 1:

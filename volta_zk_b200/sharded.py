@@ -52,13 +52,27 @@ def torch_all_gather(device=None) -> AllGather:
 
 def concurrently(first, second):
     """Run `second` in another host thread while `first` runs in this one
-    (the library's calls release the GIL); both results, or the first error."""
+    (the library's calls release the GIL); both results, or the first error.
+    The worker takes this thread's current CUDA device (a new thread starts
+    on device 0, where another GPU's contexts are invalid)."""
     import threading
 
     box = {}
+    device = None
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            device = torch.cuda.current_device()
+    except ImportError:
+        pass
 
     def worker():
         try:
+            if device is not None:
+                import torch
+
+                torch.cuda.set_device(device)
             box["value"] = second()
         except BaseException as e:  # re-raised below
             box["error"] = e
