@@ -17,6 +17,10 @@ namespace vzb {
 constexpr int kTreeTileBits = 11;
 constexpr int kTreeTile = 1 << kTreeTileBits;  // children per block
 
+__device__ __forceinline__ Fp2 shfl_idx2(Fp2 v, int src) {
+    return Fp2{__shfl_sync(0xffffffffu, v.c0, src), __shfl_sync(0xffffffffu, v.c1, src)};
+}
+
 // Parent of two fractions: p = pa qb + pb qa (one lazy sum, one reduction),
 // q = qa qb, on the carry-chain arithmetic.
 __device__ __forceinline__ void combine(Fp2 pa, Fp2 pb, Fp2 qa, Fp2 qb, Fp2& p, Fp2& q) {
@@ -73,29 +77,55 @@ __global__ void __launch_bounds__(256) tree_tile_kernel(
         }
     }
     __syncthreads();
-    // remaining combines inside the tile
-    for (int step = 1; step < levels; ++step) {
+    // remaining combines inside the tile: through shared memory while a
+    // level has more than 32 nodes (at most 2 parents per thread, kept in
+    // registers) ...
+    constexpr int kPer = kTreeTile / 4 / 256;
+    int step = 1;
+    for (; step < levels && half > 32; ++step) {
         const size_t parents = half / 2;
         const int lvl = child_bits - 1 - step;
         const size_t base = child0 >> (step + 1);
         Fp2* po = p + ((size_t{1} << lvl) - 1) + base;
         Fp2* qo = q + ((size_t{1} << lvl) - 1) + base;
-        Fp2 np[kTreeTile / 512 + 1], nq[kTreeTile / 512 + 1];
-        int k = 0;
-        for (size_t i = threadIdx.x; i < parents; i += blockDim.x, ++k) {
-            const Fp2 pa = sp[2 * i], pb = sp[2 * i + 1], qa = sq[2 * i], qb = sq[2 * i + 1];
-            combine(pa, pb, qa, qb, np[k], nq[k]);
+        Fp2 np[kPer], nq[kPer];
+#pragma unroll
+        for (int m = 0; m < kPer; ++m) {
+            const size_t i = threadIdx.x + static_cast<size_t>(m) * 256;
+            if (i < parents) combine(sp[2 * i], sp[2 * i + 1], sq[2 * i], sq[2 * i + 1], np[m], nq[m]);
         }
         __syncthreads();
-        k = 0;
-        for (size_t i = threadIdx.x; i < parents; i += blockDim.x, ++k) {
-            sp[i] = np[k];
-            sq[i] = nq[k];
-            st2(po + i, np[k]);
-            st2(qo + i, nq[k]);
+#pragma unroll
+        for (int m = 0; m < kPer; ++m) {
+            const size_t i = threadIdx.x + static_cast<size_t>(m) * 256;
+            if (i < parents) {
+                sp[i] = np[m];
+                sq[i] = nq[m];
+                st2(po + i, np[m]);
+                st2(qo + i, nq[m]);
+            }
         }
         __syncthreads();
         half = parents;
+    }
+    // ... then warp 0 alone, node j of a level in lane j, with shuffles
+    if (step < levels && threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        Fp2 pv = lane < static_cast<int>(half) ? sp[lane] : Fp2{0, 0};
+        Fp2 qv = lane < static_cast<int>(half) ? sq[lane] : Fp2{0, 0};
+        for (; step < levels; ++step) {
+            const int parents = static_cast<int>(half / 2);
+            const int lvl = child_bits - 1 - step;
+            const size_t base = child0 >> (step + 1);
+            const int a = (2 * lane) & 31, b = (2 * lane + 1) & 31;
+            const Fp2 pa = shfl_idx2(pv, a), pb = shfl_idx2(pv, b), qa = shfl_idx2(qv, a), qb = shfl_idx2(qv, b);
+            if (lane < parents) {
+                combine(pa, pb, qa, qb, pv, qv);
+                st2(p + ((size_t{1} << lvl) - 1) + base + lane, pv);
+                st2(q + ((size_t{1} << lvl) - 1) + base + lane, qv);
+            }
+            half = parents;
+        }
     }
 }
 

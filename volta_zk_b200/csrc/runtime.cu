@@ -159,6 +159,7 @@ static int sync_for_reclaim(Context* c) {
 
 int ensure_ws(Context* c, int slot, size_t bytes) {
     if (slot < 0 || slot >= kWsCount) return fail_message(c, "invalid workspace slot");
+    if (bind_device(c)) return fail_message(c, "cannot select the context's device");
     Workspace& w = c->ws[slot];
     if (w.capacity >= bytes) return 0;
     if (c->coarse) {
@@ -329,6 +330,7 @@ static int ring_commit(Context* c) {
 }
 
 int op_begin(Context* c) {
+    if (bind_device(c)) return fail_message(c, "cannot select the context's device");
     c->phase_ns[0] = c->phase_ns[1] = c->phase_ns[2] = 0;
     if (c->coarse) {
         if (c->coarse_inner) return reject(c, "nested primitive timing inside a coarse timing scope");
@@ -498,6 +500,7 @@ int op_finish_message(Context* c, int op, uint64_t d2h, uint32_t seq) {
 }
 
 int xfer_begin(Context* c) {
+    if (bind_device(c)) return fail_message(c, "cannot select the context's device");
     if (c->coarse) return reject(c, "host transfer is forbidden inside a coarse timing scope");
     switch (c->mode) {
         case kTimingCounters:
@@ -1146,6 +1149,7 @@ extern "C" int volta_cuda_resident_alloc(void* raw, size_t bytes, uint64_t* out_
     Context* c = static_cast<Context*>(raw);
     if (!c || !bytes || !out_id) return fail_message(c, "invalid resident allocation");
     if (c->coarse) return reject(c, "resident allocation is forbidden inside a coarse timing scope");
+    if (bind_device(c)) return fail_message(c, "cannot select the context's device");
     try {
         ++c->stats.resident_alloc_requests;
         size_t best_pos = SIZE_MAX, best_slot = SIZE_MAX, best_cap = SIZE_MAX;
@@ -1217,6 +1221,7 @@ extern "C" int volta_cuda_resident_free(void* raw, uint64_t id) {
     Context* c = static_cast<Context*>(raw);
     if (!c || !id) return fail_message(c, "invalid resident free");
     if (c->coarse) return reject(c, "resident free is forbidden inside a coarse timing scope");
+    if (bind_device(c)) return fail_message(c, "cannot select the context's device");
     ++c->stats.resident_free_requests;
     Slot* b = find_slot(c, id);
     if (!b) return fail_message(c, "unknown or stale resident buffer id");
@@ -1335,6 +1340,7 @@ extern "C" int volta_cuda_resident_mailbox_copy_rows(void* raw, uint64_t src_id,
 extern "C" int volta_b200_timing_mark(void* raw, int slot) {
     Context* c = static_cast<Context*>(raw);
     if (!c || slot < 0 || slot >= kTimingMarkers) return fail_message(c, "invalid timing marker slot");
+    if (bind_device(c)) return fail_message(c, "cannot select the context's device");
     if (!c->bench_ev[slot]) VZB_CUDA(c, cudaEventCreate(&c->bench_ev[slot]));
     VZB_CUDA(c, cudaEventRecord(c->bench_ev[slot], c->stream));
     return 0;
@@ -1364,6 +1370,7 @@ extern "C" int volta_b200_launch_count(void* raw, uint64_t* launches) {
 extern "C" int volta_b200_upload_async(void* raw, uint64_t id, size_t offset, const void* src, size_t bytes) {
     Context* c = static_cast<Context*>(raw);
     if (!c || !src || !bytes) return fail_message(c, "invalid asynchronous upload");
+    if (bind_device(c)) return fail_message(c, "cannot select the context's device");
     void* dst = nullptr;
     if (region(c, id, offset, bytes, &dst)) return -1;
     if (!c->copy_stream) {
@@ -1378,6 +1385,7 @@ extern "C" int volta_b200_upload_async(void* raw, uint64_t id, size_t offset, co
 extern "C" int volta_b200_wait_uploads(void* raw) {
     Context* c = static_cast<Context*>(raw);
     if (!c) return -1;
+    if (bind_device(c)) return fail_message(c, "cannot select the context's device");
     if (c->copy_ev) VZB_CUDA(c, cudaStreamWaitEvent(c->stream, c->copy_ev, 0));
     return 0;
 }

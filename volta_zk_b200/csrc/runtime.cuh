@@ -173,6 +173,14 @@ struct Context {
     std::string error;
 };
 
+// A context may be driven from any host thread: make its device the
+// calling thread's current device (a new thread starts on device 0).
+inline int bind_device(Context* c) {
+    int cur = -1;
+    if (cudaGetDevice(&cur) == cudaSuccess && cur == c->device) return 0;
+    return cudaSetDevice(c->device) == cudaSuccess ? 0 : -1;
+}
+
 // ---- errors -------------------------------------------------------------
 int fail_message(Context* c, const char* message) noexcept;
 int fail_cuda(Context* c, const char* what, cudaError_t e) noexcept;
