@@ -462,9 +462,10 @@ def run_b200(args, rank, world, local_rank):
         # columns (8 B per entry), the lookup queries and table as int16
         # witness values (2 B per entry, embedded in Fp on the device), the
         # multiplicities as u32.  The LogUp inputs are uploaded first; the
-        # triple tables then travel on the copy stream while the LogUp part
-        # computes (volta_b200_upload_async / wait_uploads).  With N GPUs
-        # every rank uploads only its slices.
+        # triple columns then stream in by chunks on the first context's copy
+        # stream while the LogUp part computes, and each chunk's on-chip
+        # triple rounds run as soon as it has landed (HostColumns in the host
+        # library).  With N GPUs every rank uploads only its slices.
         nl, nfl, ntl = n // world, n_f // world, n_t // world
         host_cols = [np.ascontiguousarray(be.download(t, 8 * n)[rank * nl:(rank + 1) * nl]) for t in tables]
         pinned = [torch.from_numpy(x.view(np.int64)).pin_memory() for x in host_cols]
@@ -479,26 +480,24 @@ def run_b200(args, rank, world, local_rank):
         d2h = (16 * (3 * args.log2_sumcheck + 3) + 16 * cap) * world
         last = {}
 
+        host_ptrs = [t.data_ptr() for t in pinned]
+
         def e2e_step():
             for buf, t in zip(ups[3:6], [f16_h, t16_h, mult_h]):
                 be_b.upload_async(buf, t.data_ptr(), t.numel() * t.element_size())
             be_b.wait_uploads()
-            for buf, t in zip(ups[:3], pinned):
-                be.upload_async(buf, t.data_ptr(), t.numel() * t.element_size())
             be_b.embed_i16(ups[3], ups[6], nfl)
             be_b.embed_i16(ups[4], ups[7], ntl)
+            # the triple columns stream in from pinned host memory chunk by
+            # chunk; each chunk's on-chip rounds run as soon as it has landed
             if world == 1:
-                def run_triple():
-                    be.wait_uploads()
-                    return prover.triple_sumcheck_fp(ups[0], ups[1], ups[2], n, TRANSCRIPT_SEED)
-
                 (last["msgs"], last["finals"]), last["proof"] = both(
-                    run_triple,
+                    lambda: prover.triple_sumcheck_fp_host(ups[0], ups[1], ups[2], host_ptrs, n, TRANSCRIPT_SEED),
                     lambda: prover_b.logup_prove(ups[6], n_f, ups[7], n_t, ups[5], LOGUP_SEED, LOGUP_DOMAIN, cap))
-            else:  # the triple part waits for its uploads
+            else:
                 last["msgs"], last["finals"], last["proof"] = sharded.prove(
                     ups[0], ups[1], ups[2], n, TRANSCRIPT_SEED, ups[6], n_f, ups[7], n_t, ups[5], LOGUP_SEED,
-                    LOGUP_DOMAIN, base=True)
+                    LOGUP_DOMAIN, base=True, host=host_ptrs)
 
         e2e_step()
         barrier()
@@ -512,7 +511,8 @@ def run_b200(args, rank, world, local_rank):
                 and np.array_equal(last["proof"], proof))
         e2e = {"value": e2e_s, "unit": "s/proof", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "inputs": "triple tables as Fp columns, lookup queries and table as int16, multiplicities as u32; "
-                         "the triple tables upload while the LogUp part computes",
+                         "the triple tables stream in by 8 MiB chunks while the LogUp part and the first 13 "
+                         "triple rounds (per landed chunk) compute",
                "proof_matches_resident": bool(same)}
         for owner, b in zip(owners, ups):
             owner.free(b)
@@ -543,8 +543,22 @@ def run_b200(args, rank, world, local_rank):
     for col, tid in zip(tables, lifted):
         be.call("base_broadcast_fp2_device", col, 0, tid, 0, n, 1, 2)
     fp_round = be.lib.volta_b200_triple_round_fp_into_device
-    runs = {
-        "triple_round_fp (2^23 pairs, Fp columns: the proof's round 0)":
+    # the on-chip pass: rounds 0 .. 12 of the proof's triple sumcheck (both
+    # kernels); algorithmic bytes: the three Fp columns read once, plus the
+    # round-7 tables (3 x 64 Fp2 per 8192-entry tile) written and read once
+    tiles = n // 8192
+    loc_r = be.upload_new(np.zeros((13, 2), dtype=np.uint64) + np.uint64(3))
+    loc_acc = be.alloc(13 * 12 * 8)
+    be.call("resident_zero", loc_acc, 0, 13 * 12 * 8)
+    loc_f = [be.alloc(16 * max(tiles, 1)) for _ in range(3)]
+    loc_fn = be.lib.volta_b200_triple_local_device
+    runs = {}
+    if tiles:
+        runs[f"triple_local (rounds 0-12 on chip, 2^{args.log2_sumcheck} Fp columns: the proof's triple pass)"] = (
+            lambda: be.check(loc_fn(be.ctx, 1, *tables, n, 0, tiles, loc_r, 0, loc_acc, *loc_f), "triple_local"),
+            3 * 8 * n + 2 * tiles * 3 * 64 * 16)
+    runs |= {
+        "triple_round_fp (2^23 pairs, Fp columns: one round of the round-by-round path)":
             (lambda: be.check(fp_round(be.ctx, *tables, n // 2, mbox, 0), "triple_round_fp"), 3 * 8 * n),
         "fp2_triple_product_round (2^23 pairs, Fp2 tables: the reference entry point)":
             (lambda: be.call("fp2_triple_product_round_into_device", lifted[0], 0, lifted[1], 0, lifted[2], 0,
@@ -563,7 +577,7 @@ def run_b200(args, rank, world, local_rank):
                          "hbm_gbs": round(nbytes / (kms / 1e3) / 1e9, 1),
                          "frac": round(nbytes / (kms / 1e3) / 1e9 / peak, 4)}
     roofline["other_kernels"] = kernels
-    for x in lifted + [mbox]:
+    for x in lifted + [mbox, loc_r, loc_acc] + loc_f:
         be.free(x)
 
     ligero = None

@@ -252,6 +252,35 @@ int volta_b200_triple_fold_round_fp_into_device(void* ctx, uint64_t a_id, uint64
                                                 uint64_t out_id, size_t out_offset);
 
 /*
+ * Thirteen triple-product rounds on chip, tile by tile.
+ *
+ * No single counterpart in the reference seam: it computes what thirteen
+ * rounds of volta_cuda_fp2_triple_product_round_into_device and
+ * volta_cuda_fp2_fold_rows_device (cuda/volta_cuda_backend.cu:5106-5153,
+ * 6862-6882) compute, for challenges known in advance.  The round pairs
+ * entries (2i, 2i + 1), so a tile of 8192 consecutive entries folds into one
+ * entry after 13 rounds; each tile runs on one CTA with its tables read once.
+ *   a, b, c   len entries (a power of two, >= 8192): Fp columns (u64,
+ *             canonical) when base != 0, else Fp2 tables;
+ *   tiles     tile0 .. tile0 + tiles - 1 of the len / 8192 tiles (a launch per
+ *             uploaded chunk is fine; all tiles must be covered before the
+ *             flush);
+ *   r         the 13 challenges of these rounds at (r_id, r_offset);
+ *   acc       156 u64 counters, zero before the first tile: each tile adds
+ *             its share of the 13 messages (3 Fp2 each) exactly (32-bit
+ *             halves, integer atomics), so the order of tiles and launches
+ *             does not matter;
+ *   fa, fb, fc  len / 8192 Fp2 each: the folded a, b, c tables (tile t's
+ *             values at entry t), i.e. the tables of round 13.
+ * volta_b200_triple_flush_device writes the 39 canonical message values
+ * (round-major, 3 per round) at (out_id, out_offset) and zeroes acc.
+ */
+int volta_b200_triple_local_device(void* ctx, int base, uint64_t a_id, uint64_t b_id, uint64_t c_id, size_t len,
+                                   size_t tile0, size_t tiles, uint64_t r_id, size_t r_offset, uint64_t acc_id,
+                                   uint64_t fa_id, uint64_t fb_id, uint64_t fc_id);
+int volta_b200_triple_flush_device(void* ctx, uint64_t acc_id, uint64_t out_id, size_t out_offset);
+
+/*
  * Asynchronous uploads: upload_async copies `bytes` from `src` (pinned host
  * memory for a truly asynchronous copy) into (id, offset) on the context's
  * copy stream and returns at once; wait_uploads makes the context's stream

@@ -33,7 +33,7 @@ def embed_i16(v):
     return np.where(v64 >= 0, v64.astype(np.uint64), np.uint64(P) - (-v64).astype(np.uint64)).astype(np.uint64)
 
 
-@pytest.mark.parametrize("log2n", [1, 2, 10, 16])
+@pytest.mark.parametrize("log2n", [1, 2, 10, 13, 16])
 def test_triple_sumcheck_matches_oracle(prover, oracle, log2n):
     n = 1 << log2n
     seed = bytes([0x51] * 32)
@@ -56,7 +56,7 @@ def test_triple_sumcheck_matches_oracle(prover, oracle, log2n):
         be.free(i)
 
 
-@pytest.mark.parametrize("log2n", [1, 2, 3, 10, 12, 13, 16])
+@pytest.mark.parametrize("log2n", [1, 2, 3, 10, 12, 13, 14, 16, 17])
 def test_triple_sumcheck_fp_columns_match_oracle(prover, oracle, log2n):
     """Fp columns (tables with c1 = 0) give the proof of the lifted tables."""
     n = 1 << log2n

@@ -93,6 +93,66 @@ def test_proof_local_waits_for_async_tables(prover, oracle):
         be.free(x)
 
 
+@pytest.mark.parametrize("log2n,chunk", [(10, 0), (13, 0), (16, 8192), (16, 3 * 8192), (17, 0), (18, 5000)])
+def test_triple_sumcheck_from_host_columns(prover, oracle, log2n, chunk):
+    """vzh_triple_sumcheck_fp_host: the columns stream in from pinned host
+    memory (by chunks, each proved on chip once landed, from 8192 entries on;
+    all at once below) and the proof is the oracle's; the device columns end
+    up holding the host columns."""
+    import torch
+
+    n = 1 << log2n
+    rng = np.random.default_rng(log2n + chunk)
+    cols = [rng.integers(0, P, size=n, dtype=np.uint64) for _ in range(3)]
+    lifted = [np.stack([x, np.zeros_like(x)], axis=1) for x in cols]
+    pinned = [torch.from_numpy(x.view(np.int64)).pin_memory() for x in cols]
+    be = prover.backend
+    ids = [be.alloc(8 * n) for _ in range(3)]
+    tseed = bytes([0x5A] * 32)
+    msgs, finals = prover.triple_sumcheck_fp_host(*ids, [t.data_ptr() for t in pinned], n, tseed, chunk)
+    emsgs, efinals = oracle.triple_sumcheck(*lifted, tseed)
+    assert np.array_equal(msgs, emsgs)
+    assert np.array_equal(finals, efinals)
+    for buf, col in zip(ids, cols):
+        assert np.array_equal(be.download(buf, 8 * n), col)
+    for x in ids:
+        be.free(x)
+
+
+def test_proof_local_from_host_columns(prover, oracle):
+    """vzh_proof_local_host: the LogUp part computes while the triple columns
+    stream in by chunks; the words equal the oracle's proofs."""
+    import torch
+
+    n, nf, nt = 1 << 16, 1 << 14, 1 << 10
+    rng = np.random.default_rng(19)
+    cols = [rng.integers(0, P, size=n, dtype=np.uint64) for _ in range(3)]
+    lifted = [np.stack([x, np.zeros_like(x)], axis=1) for x in cols]
+    table = rng.integers(-32768, 32768, size=nt, dtype=np.int64).astype(np.int16)
+    idx = rng.integers(0, nt, size=nf)
+    f = table[idx]
+    mult = np.bincount(idx, minlength=nt).astype(np.uint32)
+    be = prover.backend
+    f16, t16 = be.upload_new(f), be.upload_new(table)
+    fe, te = be.alloc(8 * nf), be.alloc(8 * nt)
+    be.embed_i16(f16, fe, nf)
+    be.embed_i16(t16, te, nt)
+    m = be.upload_new(mult)
+    pinned = [torch.from_numpy(x.view(np.int64)).pin_memory() for x in cols]
+    ids = [be.alloc(8 * n) for _ in range(3)]
+    tseed, lseed, domain = bytes([0x5A] * 32), bytes([0x4C] * 32), 0x1004
+    words = prover.proof_local(*ids, n, True, tseed, fe, nf, te, nt, m, 0, lseed, domain,
+                               host=[t.data_ptr() for t in pinned], chunk=2 * 8192)
+    k = 3 * 16 + 3
+    em_msgs, em_finals = oracle.triple_sumcheck(*lifted, tseed)
+    assert np.array_equal(words[: 3 * 16], em_msgs)
+    assert np.array_equal(words[3 * 16:k], em_finals)
+    got = sh.logup_finish([words[k:]], nf, nt, lseed, domain)
+    assert np.array_equal(got, oracle.logup_prove(f, table, mult, lseed, domain))
+    for x in ids + [f16, t16, fe, te, m]:
+        be.free(x)
+
+
 def test_two_contexts_concurrently(prover, oracle):
     """The triple sumcheck on one context and the LogUp proof on another,
     driven from two host threads at once (bench.py's two lanes), give the

@@ -125,9 +125,12 @@ def load_cuda_library(path: str | None = None):
             raise AccelError(f"MissingSymbol: {name}") from e
         fn.restype = res
         fn.argtypes = args
-    # extensions (include/volta_b200_ext.h)
+    # extensions (include/volta_b200_ext.h): optional, as for the host
+    # library, so a backend built without the newer ones still loads
     for name, (res, args) in parse_header(EXT_HEADER, "volta_b200_").items():
-        fn = getattr(lib, name)
+        fn = getattr(lib, name, None)
+        if fn is None:
+            continue
         fn.restype = res
         fn.argtypes = args
     if lib.volta_cuda_abi_version() != ABI_VERSION:
@@ -156,12 +159,17 @@ def load_host_library():
         L.vzh_reset_stats.argtypes = [vp, C.c_char_p, sz]
         L.vzh_triple_sumcheck.argtypes = [vp, u64, u64, u64, sz, C.c_char_p, vp, vp, C.c_char_p, sz]
         L.vzh_triple_sumcheck_fp.argtypes = [vp, u64, u64, u64, sz, C.c_char_p, vp, vp, C.c_char_p, sz]
+        L.vzh_triple_sumcheck_fp_host.argtypes = [vp, u64, u64, u64, vp, vp, vp, sz, sz, C.c_char_p, vp, vp,
+                                                  C.c_char_p, sz]
         L.vzh_logup_prove.argtypes = [vp, u64, sz, u64, sz, u64, C.c_char_p, u64, vp, sz,
                                       C.POINTER(C.c_size_t), C.c_char_p, sz]
         L.vzh_ligero_commit_open.argtypes = [vp, C.c_char_p, sz, sz, sz, sz, C.c_char_p, vp, vp, vp, vp,
                                              C.c_char_p, sz]
         L.vzh_proof_local.argtypes = [vp, u64, u64, u64, sz, C.c_int, C.c_char_p, u64, sz, u64, sz, u64, sz,
                                       C.c_char_p, u64, vp, sz, C.POINTER(C.c_size_t), C.c_char_p, sz]
+        L.vzh_proof_local_host.argtypes = [vp, u64, u64, u64, vp, vp, vp, sz, sz, C.c_char_p, u64, sz, u64, sz,
+                                           u64, sz, C.c_char_p, u64, vp, sz, C.POINTER(C.c_size_t), C.c_char_p,
+                                           sz]
         L.vzh_logup_local.argtypes = [vp, u64, sz, u64, sz, u64, sz, C.c_char_p, u64, vp, sz,
                                       C.POINTER(C.c_size_t), C.c_char_p, sz]
         L.vzh_fpstream_fp2.argtypes = [C.c_char_p, u64, sz, vp]
@@ -348,6 +356,20 @@ class Prover:
         self._err(rc, err)
         return msgs, finals
 
+    def triple_sumcheck_fp_host(self, a: int, b: int, c: int, host, n: int, seed: bytes, chunk: int = 0):
+        """triple_sumcheck_fp with the columns still in host memory: `host`
+        holds three host addresses (pinned, n u64 each) whose values fill the
+        device columns a, b, c chunk by chunk (chunk entries per column, 0 for
+        the default) while the first rounds prove the chunks that have landed."""
+        rounds = n.bit_length() - 1
+        msgs = np.zeros((3 * rounds, 2), dtype=np.uint64)
+        finals = np.zeros((3, 2), dtype=np.uint64)
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_triple_sumcheck_fp_host(self.h, a, b, c, host[0], host[1], host[2], n, chunk, seed,
+                                                   _ptr(msgs), _ptr(finals), err, 1024)
+        self._err(rc, err)
+        return msgs, finals
+
     def logup_prove(self, f_col: int, n_f: int, t_col: int, n_t: int, mult: int, seed: bytes,
                     domain: int, cap: int):
         out = np.zeros((cap, 2), dtype=np.uint64)
@@ -387,18 +409,28 @@ class Prover:
 
     def proof_local(self, a: int, b: int, c: int, n_local: int, base: bool, triple_seed: bytes, f_col: int,
                     n_f_local: int, t_col: int, n_t_local: int, mult: int, shard_bits: int, logup_seed: bytes,
-                    domain: int) -> np.ndarray:
+                    domain: int, host=None, chunk: int = 0) -> np.ndarray:
         """This shard's whole config-1 part in one call (vzh_proof_local): the
         triple sumcheck words (3 k messages, 3 finals) then the LogUp local
-        words, with a single download for both."""
+        words, with a single download for both.  With `host` (three host
+        addresses of pinned Fp columns, base only), the triple columns a, b, c
+        are filled from host memory chunk by chunk while the LogUp part and the
+        first triple rounds compute (vzh_proof_local_host)."""
         k = n_local.bit_length() - 1
         cap = 3 * k + 3 + 1 + 2 * (2 + sum(4 * (l - shard_bits) + 4 for l in range(shard_bits, 64)))
         out = np.zeros((cap, 2), dtype=np.uint64)
         written = C.c_size_t()
         err = C.create_string_buffer(1024)
-        rc = self.host.vzh_proof_local(self.h, a, b, c, n_local, 1 if base else 0, triple_seed, f_col, n_f_local,
-                                       t_col, n_t_local, mult, shard_bits, logup_seed, domain, _ptr(out), cap,
-                                       C.byref(written), err, 1024)
+        if host is not None:
+            if not base:
+                raise AccelError("host columns need base-field tables")
+            rc = self.host.vzh_proof_local_host(self.h, a, b, c, host[0], host[1], host[2], chunk, n_local,
+                                                triple_seed, f_col, n_f_local, t_col, n_t_local, mult, shard_bits,
+                                                logup_seed, domain, _ptr(out), cap, C.byref(written), err, 1024)
+        else:
+            rc = self.host.vzh_proof_local(self.h, a, b, c, n_local, 1 if base else 0, triple_seed, f_col,
+                                           n_f_local, t_col, n_t_local, mult, shard_bits, logup_seed, domain,
+                                           _ptr(out), cap, C.byref(written), err, 1024)
         self._err(rc, err)
         return out[: written.value]
 

@@ -683,7 +683,8 @@ extern "C" int volta_cuda_create(void** out) {
         VZB_CUDA(c, cudaHostAlloc(&c->host_mailbox, 4096, cudaHostAllocMapped));
         VZB_CUDA(c, cudaHostGetDevicePointer(&c->host_mailbox_dev, c->host_mailbox, 0));
         std::memset(c->host_mailbox, 0, 4096);  // the message flag starts below every sequence number
-        VZB_CUDA(c, cudaHostAlloc(&c->stage, kStageSlotBytes * kStageSlots, cudaHostAllocDefault));
+        VZB_CUDA(c, cudaHostAlloc(&c->stage, kStageSlotBytes * kStageSlots, cudaHostAllocMapped));
+        VZB_CUDA(c, cudaHostGetDevicePointer(&c->stage_dev, c->stage, 0));
         for (auto& e : c->stage_ev) VZB_CUDA(c, cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         if (ensure_ws(c, kWsCounter, 4096)) return -1;
         // per-block partials of the single-launch reductions: at most 8 blocks
@@ -1235,6 +1236,18 @@ extern "C" int volta_cuda_resident_free(void* raw, uint64_t id) {
     return 0;
 }
 
+// Small upload from the mapped staging ring (at most 64 KiB; 4 KiB per block).
+__global__ void stage_copy_kernel(unsigned char* __restrict__ dst, const unsigned char* __restrict__ src,
+                                  size_t bytes) {
+    const size_t lo = static_cast<size_t>(blockIdx.x) * 4096, hi = lo + 4096 < bytes ? lo + 4096 : bytes;
+    if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | lo | hi) & 15) == 0) {
+        for (size_t i = lo + 16 * threadIdx.x; i < hi; i += 16 * blockDim.x)
+            *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(src + i);
+    } else {
+        for (size_t i = lo + threadIdx.x; i < hi; i += blockDim.x) dst[i] = src[i];
+    }
+}
+
 extern "C" int volta_cuda_resident_upload(void* raw, uint64_t id, size_t offset, const void* src,
                                           size_t bytes) {
     Context* c = static_cast<Context*>(raw);
@@ -1249,9 +1262,12 @@ extern "C" int volta_cuda_resident_upload(void* raw, uint64_t id, size_t offset,
         const int slot = c->stage_next;
         c->stage_next = (slot + 1) % kStageSlots;
         if (c->stage_used[slot]) VZB_CUDA(c, cudaEventSynchronize(c->stage_ev[slot]));
-        char* staged = static_cast<char*>(c->stage) + static_cast<size_t>(slot) * kStageSlotBytes;
-        std::memcpy(staged, src, bytes);
-        e = cudaMemcpyAsync(dst, staged, bytes, cudaMemcpyHostToDevice, c->stream);
+        const size_t at = static_cast<size_t>(slot) * kStageSlotBytes;
+        std::memcpy(static_cast<char*>(c->stage) + at, src, bytes);
+        stage_copy_kernel<<<static_cast<unsigned>((bytes + 4095) / 4096), 256, 0, c->stream>>>(
+            static_cast<unsigned char*>(dst), static_cast<const unsigned char*>(c->stage_dev) + at, bytes);
+        e = cudaGetLastError();
+        ++c->launches;
         if (e == cudaSuccess) e = cudaEventRecord(c->stage_ev[slot], c->stream);
         c->stage_used[slot] = true;
     } else {
@@ -1293,6 +1309,29 @@ extern "C" int volta_cuda_resident_zero(void* raw, uint64_t id, size_t offset, s
     return op_finish(c, kOpPcsRows, 0, 0, 0, bytes, 0);
 }
 
+// Strided device-to-device rows as a kernel on the compute stream, in the
+// widest unit that every address, stride and row length allows (a copy
+// engine transfer queued behind this stream's kernels could hold up other
+// streams' uploads on the same engine).
+template <typename T>
+__global__ void copy_rows_kernel(unsigned char* __restrict__ dst, size_t dst_stride,
+                                 const unsigned char* __restrict__ src, size_t src_stride, size_t rows,
+                                 size_t row_units) {
+    const size_t total = rows * row_units, step = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += step) {
+        size_t r, u;
+        if (total <= 0xFFFFFFFFull) {
+            r = static_cast<uint32_t>(i) / static_cast<uint32_t>(row_units);
+            u = static_cast<uint32_t>(i) - static_cast<uint32_t>(r) * static_cast<uint32_t>(row_units);
+        } else {
+            r = i / row_units;
+            u = i - r * row_units;
+        }
+        *reinterpret_cast<T*>(dst + r * dst_stride + u * sizeof(T)) =
+            *reinterpret_cast<const T*>(src + r * src_stride + u * sizeof(T));
+    }
+}
+
 static int copy_rows(Context* c, uint64_t src_id, size_t src_off, size_t src_stride,
                      uint64_t dst_id, size_t dst_off, size_t dst_stride, size_t rows,
                      size_t row_bytes, int op) {
@@ -1312,8 +1351,21 @@ static int copy_rows(Context* c, uint64_t src_id, size_t src_off, size_t src_str
     size_t total = 0;
     if (!mul_ok(rows, row_bytes, &total)) return fail_message(c, "resident D2D byte count overflows size_t");
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    VZB_CUDA(c, cudaMemcpy2DAsync(dst, dst_stride, src, src_stride, row_bytes, rows,
-                                  cudaMemcpyDeviceToDevice, c->stream));
+    const uintptr_t align = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | src_stride |
+                            dst_stride | row_bytes;
+    const int unit = (align & 15) == 0 ? 16 : (align & 7) == 0 ? 8 : (align & 3) == 0 ? 4 : 1;
+    const size_t units = total / unit;
+    const unsigned grid = static_cast<unsigned>(
+        std::min<size_t>((units + 255) / 256, static_cast<size_t>(c->sm_count) * 8));
+    unsigned char* d = static_cast<unsigned char*>(dst);
+    const unsigned char* sp = static_cast<const unsigned char*>(src);
+    switch (unit) {
+        case 16: copy_rows_kernel<uint4><<<grid, 256, 0, c->stream>>>(d, dst_stride, sp, src_stride, rows, row_bytes / 16); break;
+        case 8: copy_rows_kernel<uint2><<<grid, 256, 0, c->stream>>>(d, dst_stride, sp, src_stride, rows, row_bytes / 8); break;
+        case 4: copy_rows_kernel<uint32_t><<<grid, 256, 0, c->stream>>>(d, dst_stride, sp, src_stride, rows, row_bytes / 4); break;
+        default: copy_rows_kernel<unsigned char><<<grid, 256, 0, c->stream>>>(d, dst_stride, sp, src_stride, rows, row_bytes); break;
+    }
+    VZB_LAUNCHED(c);
     if (op_mark(c, 2)) return -1;
     return op_finish(c, op, 0, 0, total, 0, 0);
 }

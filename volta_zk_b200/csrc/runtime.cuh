@@ -159,10 +159,15 @@ struct Context {
     uint32_t mail_seq = 0;               // sequence number of host-bound messages
     uint64_t launches = 0;               // kernels launched by this context
     cudaEvent_t bench_ev[kTimingMarkers] = {};        // measurement markers (extension ABI)
-    // Pinned staging ring for small uploads: the bytes are copied at call
-    // time and the async copy never waits on queued work (a pageable source
-    // may make cudaMemcpyAsync synchronise with the stream).
+    // Pinned, device-mapped staging ring for small uploads: the bytes are
+    // copied into a slot at call time and a one-block kernel on the compute
+    // stream copies the slot into device memory.  A pageable source could
+    // make cudaMemcpyAsync synchronise with the stream, and a copy-engine
+    // transfer queued behind this stream's kernels would hold up other
+    // streams' copies behind it (another context's bulk uploads share the
+    // engine), so small uploads do not use the copy engine at all.
     void* stage = nullptr;
+    void* stage_dev = nullptr;
     cudaEvent_t stage_ev[kStageSlots] = {};
     bool stage_used[kStageSlots] = {};
     int stage_next = 0;

@@ -129,8 +129,14 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         dlsym(handle_, "volta_b200_triple_fold_round_fp_into_device"));
     ext_loaded_->wait_uploads =
         reinterpret_cast<decltype(ext_loaded_->wait_uploads)>(dlsym(handle_, "volta_b200_wait_uploads"));
+    ext_loaded_->upload_async =
+        reinterpret_cast<decltype(ext_loaded_->upload_async)>(dlsym(handle_, "volta_b200_upload_async"));
     ext_loaded_->logup_tree_column = reinterpret_cast<decltype(ext_loaded_->logup_tree_column)>(
         dlsym(handle_, "volta_b200_logup_tree_column_device"));
+    ext_loaded_->triple_local = reinterpret_cast<decltype(ext_loaded_->triple_local)>(
+        dlsym(handle_, "volta_b200_triple_local_device"));
+    ext_loaded_->triple_flush = reinterpret_cast<decltype(ext_loaded_->triple_flush)>(
+        dlsym(handle_, "volta_b200_triple_flush_device"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

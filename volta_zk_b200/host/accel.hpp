@@ -134,8 +134,19 @@ TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint6
 // tables with c1 = 0).  The scheduled driver runs rounds 0 and 1 on the base
 // columns (volta_b200_triple_*_fp extensions); otherwise the columns are
 // lifted to Fp2 (base_broadcast_fp2_device) and proved as above.  Same result.
+//
+// With `host` set, the three device columns are still to be filled from host
+// memory (pinned for the transfer to overlap): the scheduled driver uploads
+// them chunk by chunk on the context's copy stream (volta_b200_upload_async)
+// and, where the on-chip rounds apply (n >= 8192), proves each chunk's tiles
+// as soon as that chunk has landed, so the first 13 rounds run under the
+// transfer; otherwise everything lands before the first round.
+struct HostColumns {
+    const uint64_t* col[3] = {nullptr, nullptr, nullptr};
+    size_t chunk = 0;  // entries per column and upload chunk (0: 2^20)
+};
 TripleResult triple_sumcheck_resident_fp(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
-                                         FpStream& tx);
+                                         FpStream& tx, const HostColumns* host = nullptr);
 
 // LogUp (logup.rs:1760-1771, resident engine 995-1470): queries and table are
 // device columns of canonical Fp values (n_f and n_t entries, powers of two),

@@ -95,6 +95,25 @@ int vzh_triple_sumcheck_fp(void* h, uint64_t a, uint64_t b, uint64_t c, size_t n
     });
 }
 
+// The same proof with the columns still in host memory (HostColumns): the
+// device columns a, b, c are filled chunk by chunk while the first rounds run.
+int vzh_triple_sumcheck_fp_host(void* h, uint64_t a, uint64_t b, uint64_t c, const uint64_t* host_a,
+                                const uint64_t* host_b, const uint64_t* host_c, size_t n, size_t chunk,
+                                const uint8_t* seed, vz_fp2* messages, vz_fp2* finals, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        if (!host_a || !host_b || !host_c) throw AccelError("null host column");
+        FpStream tx(seed, UINT64_MAX);
+        HostColumns hc;
+        hc.col[0] = host_a;
+        hc.col[1] = host_b;
+        hc.col[2] = host_c;
+        hc.chunk = chunk;
+        TripleResult r = triple_sumcheck_resident_fp(*static_cast<Backend*>(h), a, b, c, n, tx, &hc);
+        std::memcpy(messages, r.messages.data(), r.messages.size() * sizeof(vz_fp2));
+        std::memcpy(finals, r.finals, sizeof(r.finals));
+    });
+}
+
 // LogUp proof over resident Fp columns; challenges from FpStream(seed, domain).
 int vzh_logup_prove(void* h, uint64_t f_col, size_t n_f, uint64_t t_col, size_t n_t, uint64_t mult,
                     const uint8_t* seed, uint64_t domain, vz_fp2* out, size_t cap, size_t* written,
@@ -152,30 +171,57 @@ int vzh_logup_local(void* h, uint64_t f_col, size_t n_f_local, uint64_t t_col, s
 // may still be arriving while the LogUp part computes.  out = the triple's
 // 3 k messages and 3 finals (k = log2 n_local), then the words of
 // vzh_logup_local.  Needs the scheduled drivers.
+static void proof_local(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n_local, int base,
+                        const HostColumns* host, const uint8_t* triple_seed, uint64_t f_col, size_t n_f_local,
+                        uint64_t t_col, size_t n_t_local, uint64_t mult, size_t shard_bits, const uint8_t* logup_seed,
+                        uint64_t domain, vz_fp2* out, size_t cap, size_t* written) {
+    if (!b.scheduled()) throw AccelError("vzh_proof_local needs the scheduled drivers");
+    if (base && !(b.ext().triple_round_fp && b.ext().triple_fold_round_fp && n_local >= 4))
+        throw AccelError("vzh_proof_local: base-field rounds unavailable for this table length");
+    FpStream tx(triple_seed, UINT64_MAX);
+    FpStream chal(logup_seed, domain);
+    Owned own(b);
+    const PendingLogup pl = logup_local_enqueue(b, own, f_col, n_f_local, t_col, n_t_local, mult, shard_bits, chal);
+    if (b.ext().wait_uploads) b.check(b.ext().wait_uploads(b.ctx()), "volta_b200_wait_uploads");
+    size_t k = 0;
+    const uint64_t tm = triple_enqueue(b, own, a, bb, c, n_local, tx, base != 0, k, host);
+    const std::vector<Fp2> words = logup_local_collect(b, pl);
+    const TripleResult tr = triple_collect(b, tm, k);
+    const size_t total = tr.messages.size() + 3 + words.size();
+    if (total > cap) throw AccelError("local proof buffer too small");
+    std::memcpy(out, tr.messages.data(), tr.messages.size() * sizeof(vz_fp2));
+    std::memcpy(out + tr.messages.size(), tr.finals, sizeof(tr.finals));
+    std::memcpy(out + tr.messages.size() + 3, words.data(), words.size() * sizeof(vz_fp2));
+    *written = total;
+}
+
 int vzh_proof_local(void* h, uint64_t a, uint64_t bb, uint64_t c, size_t n_local, int base,
                     const uint8_t* triple_seed, uint64_t f_col, size_t n_f_local, uint64_t t_col, size_t n_t_local,
                     uint64_t mult, size_t shard_bits, const uint8_t* logup_seed, uint64_t domain, vz_fp2* out,
                     size_t cap, size_t* written, char* err, size_t len) {
     return guarded(err, len, [&] {
-        Backend& b = *static_cast<Backend*>(h);
-        if (!b.scheduled()) throw AccelError("vzh_proof_local needs the scheduled drivers");
-        if (base && !(b.ext().triple_round_fp && b.ext().triple_fold_round_fp && n_local >= 4))
-            throw AccelError("vzh_proof_local: base-field rounds unavailable for this table length");
-        FpStream tx(triple_seed, UINT64_MAX);
-        FpStream chal(logup_seed, domain);
-        Owned own(b);
-        const PendingLogup pl = logup_local_enqueue(b, own, f_col, n_f_local, t_col, n_t_local, mult, shard_bits, chal);
-        if (b.ext().wait_uploads) b.check(b.ext().wait_uploads(b.ctx()), "volta_b200_wait_uploads");
-        size_t k = 0;
-        const uint64_t tm = triple_enqueue(b, own, a, bb, c, n_local, tx, base != 0, k);
-        const std::vector<Fp2> words = logup_local_collect(b, pl);
-        const TripleResult tr = triple_collect(b, tm, k);
-        const size_t total = tr.messages.size() + 3 + words.size();
-        if (total > cap) throw AccelError("local proof buffer too small");
-        std::memcpy(out, tr.messages.data(), tr.messages.size() * sizeof(vz_fp2));
-        std::memcpy(out + tr.messages.size(), tr.finals, sizeof(tr.finals));
-        std::memcpy(out + tr.messages.size() + 3, words.data(), words.size() * sizeof(vz_fp2));
-        *written = total;
+        proof_local(*static_cast<Backend*>(h), a, bb, c, n_local, base, nullptr, triple_seed, f_col, n_f_local, t_col,
+                    n_t_local, mult, shard_bits, logup_seed, domain, out, cap, written);
+    });
+}
+
+// The same with the triple columns still in host memory (base-field columns):
+// they upload chunk by chunk on the copy stream while the LogUp part and the
+// first triple rounds compute.
+int vzh_proof_local_host(void* h, uint64_t a, uint64_t bb, uint64_t c, const uint64_t* host_a,
+                         const uint64_t* host_b, const uint64_t* host_c, size_t chunk, size_t n_local,
+                         const uint8_t* triple_seed, uint64_t f_col, size_t n_f_local, uint64_t t_col,
+                         size_t n_t_local, uint64_t mult, size_t shard_bits, const uint8_t* logup_seed,
+                         uint64_t domain, vz_fp2* out, size_t cap, size_t* written, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        if (!host_a || !host_b || !host_c) throw AccelError("null host column");
+        HostColumns hc;
+        hc.col[0] = host_a;
+        hc.col[1] = host_b;
+        hc.col[2] = host_c;
+        hc.chunk = chunk;
+        proof_local(*static_cast<Backend*>(h), a, bb, c, n_local, 1, &hc, triple_seed, f_col, n_f_local, t_col,
+                    n_t_local, mult, shard_bits, logup_seed, domain, out, cap, written);
     });
 }
 

@@ -199,13 +199,15 @@ TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint6
 }
 
 TripleResult triple_sumcheck_resident_fp(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
-                                         FpStream& tx) {
+                                         FpStream& tx, const HostColumns* host) {
     const ExtApi& X = b.ext();
     if (b.scheduled() && X.triple_round_fp && X.triple_fold_round_fp && n >= 4)
-        return triple_sumcheck_scheduled(b, a, bb, c, n, tx, true);
+        return triple_sumcheck_scheduled(b, a, bb, c, n, tx, true, host);
     Owned own(b);
     uint64_t lifted[3];
     const uint64_t cols[3] = {a, bb, c};
+    if (host)
+        for (int t = 0; t < 3; ++t) b.upload(cols[t], 0, host->col[t], n * sizeof(uint64_t));
     for (int t = 0; t < 3; ++t) {
         lifted[t] = own.add(b.alloc(n * sizeof(Fp2)));
         b.check(b.api().volta_cuda_base_broadcast_fp2_device(b.ctx(), cols[t], 0, lifted[t], 0, n, 1, 2),

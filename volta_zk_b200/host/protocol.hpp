@@ -65,15 +65,16 @@ struct LocalSide {
 LocalSide frac_side_local(Backend& b, uint64_t leaf, uint64_t mult, size_t n_local, uint64_t alpha1,
                           size_t shard_bits, const SideSchedule& sch);
 TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
-                                       FpStream& tx, bool base = false);
+                                       FpStream& tx, bool base = false, const HostColumns* host = nullptr);
 
 // Enqueue / collect halves of the scheduled drivers: everything is enqueued
 // on the context's stream with device-side message slots, and the collect
 // call downloads them (the only synchronisation).  Buffers go to `own`,
 // which must outlive the collect call.  Several enqueues may precede the
 // first collect, so one proof's sumchecks run back to back on the GPU.
+// With `host` set (base-field columns only), see HostColumns.
 uint64_t triple_enqueue(Backend& b, Owned& own, uint64_t a, uint64_t bb, uint64_t c, size_t n, FpStream& tx,
-                        bool base, size_t& k_out);
+                        bool base, size_t& k_out, const HostColumns* host = nullptr);
 TripleResult triple_collect(Backend& b, uint64_t msgs, size_t k);
 struct PendingSide {
     uint64_t msgs = 0;

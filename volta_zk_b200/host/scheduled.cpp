@@ -24,9 +24,15 @@ namespace vzh {
 constexpr size_t kTailLen = 2048;
 // Jobs per volta_b200_logup_round_batch_device call.
 constexpr size_t kRoundBatchMax = 24;
+// Entries per tile of volta_b200_triple_local_device (13 rounds per pass).
+constexpr size_t kLocalTile = 8192;
+constexpr size_t kLocalRounds = 13;
+constexpr size_t kLocalAccBytes = kLocalRounds * 3 * 4 * sizeof(uint64_t);
+// Entries per column and upload chunk when host columns stream in (3 x 8 MiB).
+constexpr size_t kDefaultUploadChunk = size_t{1} << 20;
 
 uint64_t triple_enqueue(Backend& b, Owned& own, uint64_t a, uint64_t bb, uint64_t c, size_t n, FpStream& tx,
-                        bool base, size_t& k_out) {
+                        bool base, size_t& k_out, const HostColumns* host) {
     const Api& A = b.api();
     const ExtApi& X = b.ext();
     void* ctx = b.ctx();
@@ -38,15 +44,73 @@ uint64_t triple_enqueue(Backend& b, Owned& own, uint64_t a, uint64_t bb, uint64_
     for (auto& x : r) x = tx.next_fp2();
     // slots: 3 per round message, then the 3 final openings
     const uint64_t msgs = own.add(b.alloc((3 * k + 3) * sizeof(Fp2)));
+    const bool local = X.triple_local && X.triple_flush && X.triple_tail;
     uint64_t rdev = 0;
-    if (X.triple_tail && k) {
+    if ((X.triple_tail || local) && k) {
         rdev = own.add(b.alloc(k * sizeof(Fp2)));
         b.upload(rdev, 0, r.data(), k * sizeof(Fp2));
     }
     uint64_t cur[3] = {a, bb, c};
-    bool owned = false;
+    bool owned = false, finals = false;
     size_t len = n, j = 0;
-    if (base) {
+    const bool stream_in = host && local && base && n >= kLocalTile && n > kTailLen;
+    if (host) {
+        if (!base) throw AccelError("host columns need the base-field driver");
+        if (!X.upload_async || !X.wait_uploads) throw AccelError("asynchronous uploads unavailable");
+        if (!stream_in) {  // everything lands before the first round
+            for (int t = 0; t < 3; ++t)
+                b.check(X.upload_async(ctx, cur[t], 0, host->col[t], n * sizeof(uint64_t)), "volta_b200_upload_async");
+            b.check(X.wait_uploads(ctx), "volta_b200_wait_uploads");
+        }
+    }
+    // on-chip passes: 13 rounds per launch while the tables are longer than
+    // the tail takes and hold whole tiles
+    uint64_t acc = 0;
+    while (local && len >= kLocalTile && len > kTailLen) {
+        if (!acc) {
+            acc = own.add(b.alloc(kLocalAccBytes));
+            b.check(A.volta_cuda_resident_zero(ctx, acc, 0, kLocalAccBytes), "resident_zero");
+        }
+        const size_t tiles = len / kLocalTile;
+        uint64_t nxt[3];
+        for (int t = 0; t < 3; ++t) nxt[t] = own.add(b.alloc(tiles * sizeof(Fp2)));
+        // one launch over all tiles, or (first pass over host columns) one per
+        // uploaded chunk, each waiting for its own chunk only
+        size_t per = tiles;
+        if (stream_in && j == 0) {
+            const size_t want = host->chunk ? host->chunk : kDefaultUploadChunk;
+            per = std::max<size_t>(1, want / kLocalTile);
+        }
+        for (size_t t0 = 0; t0 < tiles; t0 += per) {
+            const size_t cnt = std::min(per, tiles - t0);
+            if (stream_in && j == 0) {
+                const size_t off = t0 * kLocalTile, m = cnt * kLocalTile;
+                for (int t = 0; t < 3; ++t)
+                    b.check(X.upload_async(ctx, cur[t], off * sizeof(uint64_t), host->col[t] + off,
+                                           m * sizeof(uint64_t)),
+                            "volta_b200_upload_async");
+                b.check(X.wait_uploads(ctx), "volta_b200_wait_uploads");
+            }
+            b.check(X.triple_local(ctx, base && j == 0, cur[0], cur[1], cur[2], len, t0, cnt, rdev, j, acc,
+                                   nxt[0], nxt[1], nxt[2]),
+                    "volta_b200_triple_local_device");
+        }
+        b.check(X.triple_flush(ctx, acc, msgs, 3 * j), "volta_b200_triple_flush_device");
+        for (int t = 0; t < 3; ++t) {
+            if (owned) own.release(cur[t]);
+            cur[t] = nxt[t];
+        }
+        owned = true;
+        len = tiles;
+        j += kLocalRounds;
+    }
+    if (j) {
+        // round j's message on the folded tables, unless the tail takes them
+        if (len > kTailLen)
+            b.check(A.volta_cuda_fp2_triple_product_round_into_device(ctx, cur[0], 0, cur[1], 0, cur[2], 0, len / 2,
+                                                                      msgs, 3 * j),
+                    "fp2_triple_product_round_into_device");
+    } else if (base) {
         // base-field columns (n >= 4): rounds 0 and 1 read them directly; the
         // fold with r[0] writes the Fp2 tables the later rounds use (when they
         // go to the tail, it recomputes round 1 with the same result)
@@ -72,6 +136,7 @@ uint64_t triple_enqueue(Backend& b, Owned& own, uint64_t a, uint64_t bb, uint64_
                         "fp2_fold_rows_device");
             ++j;
             len = 1;
+            finals = true;
             break;
         }
         uint64_t nxt[3];
@@ -101,7 +166,7 @@ uint64_t triple_enqueue(Backend& b, Owned& own, uint64_t a, uint64_t bb, uint64_
         len = pairs;
         ++j;
     }
-    if (X.triple_tail && len <= kTailLen && (j < k || k == 0)) {
+    if (X.triple_tail && len <= kTailLen && !finals) {
         // rounds j..k-1 and the openings in one CTA
         b.check(X.triple_tail(ctx, cur[0], cur[1], cur[2], len, rdev, j, msgs, 3 * j), "volta_b200_triple_tail_device");
     } else if (!k) {  // a single entry: the openings are the inputs
@@ -123,10 +188,10 @@ TripleResult triple_collect(Backend& b, uint64_t msgs, size_t k) {
 }
 
 TripleResult triple_sumcheck_scheduled(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n, FpStream& tx,
-                                       bool base) {
+                                       bool base, const HostColumns* host) {
     Owned own(b);
     size_t k = 0;
-    const uint64_t msgs = triple_enqueue(b, own, a, bb, c, n, tx, base, k);
+    const uint64_t msgs = triple_enqueue(b, own, a, bb, c, n, tx, base, k, host);
     return triple_collect(b, msgs, k);
 }
 

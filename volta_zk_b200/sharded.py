@@ -153,16 +153,21 @@ class ShardedProver:
         return triple_finish(parts, n, seed)
 
     def prove(self, a: int, b: int, c: int, n: int, triple_seed: bytes, f_col: int, n_f: int, t_col: int, n_t: int,
-              mult: int, logup_seed: bytes, domain: int, base: bool = False):
+              mult: int, logup_seed: bytes, domain: int, base: bool = False, host=None, chunk: int = 0):
         """Both parts of a config-1 proof with one local call and one
         all-gather: (triple messages, triple finals, LogUp proof words), equal
-        to triple_sumcheck followed by logup_prove."""
+        to triple_sumcheck followed by logup_prove.  `host`: this shard's
+        triple columns (base only) still in pinned host memory, three
+        addresses; they fill a, b, c chunk by chunk under the first rounds."""
         nl = n // self.world
         if self.logup_prover is None:
             local = self.prover.proof_local(a, b, c, nl, base, triple_seed, f_col, n_f // self.world, t_col,
-                                            n_t // self.world, mult, self.s, logup_seed, domain)
+                                            n_t // self.world, mult, self.s, logup_seed, domain, host, chunk)
         else:
             def triple_part():
+                if host is not None:
+                    m, f = self.prover.triple_sumcheck_fp_host(a, b, c, host, nl, triple_seed, chunk)
+                    return np.concatenate([m, f])
                 self.prover.backend.wait_uploads()  # tables still arriving on the copy stream, if any
                 local_sumcheck = self.prover.triple_sumcheck_fp if base else self.prover.triple_sumcheck
                 m, f = local_sumcheck(a, b, c, nl, triple_seed)
