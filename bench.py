@@ -511,7 +511,7 @@ def run_b200(args, rank, world, local_rank):
                 and np.array_equal(last["proof"], proof))
         e2e = {"value": e2e_s, "unit": "s/proof", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "inputs": "triple tables as Fp columns, lookup queries and table as int16, multiplicities as u32; "
-                         "the triple tables stream in by 8 MiB chunks while the LogUp part and the first 13 "
+                         "the triple tables stream in by 16 MiB chunks while the LogUp part and the first 13 "
                          "triple rounds (per landed chunk) compute",
                "proof_matches_resident": bool(same)}
         for owner, b in zip(owners, ups):

@@ -143,7 +143,7 @@ TripleResult triple_sumcheck_resident(Backend& b, uint64_t a, uint64_t bb, uint6
 // transfer; otherwise everything lands before the first round.
 struct HostColumns {
     const uint64_t* col[3] = {nullptr, nullptr, nullptr};
-    size_t chunk = 0;  // entries per column and upload chunk (0: 2^20)
+    size_t chunk = 0;  // entries per column and upload chunk (0: 2^21)
 };
 TripleResult triple_sumcheck_resident_fp(Backend& b, uint64_t a, uint64_t bb, uint64_t c, size_t n,
                                          FpStream& tx, const HostColumns* host = nullptr);

@@ -28,8 +28,9 @@ constexpr size_t kRoundBatchMax = 24;
 constexpr size_t kLocalTile = 8192;
 constexpr size_t kLocalRounds = 13;
 constexpr size_t kLocalAccBytes = kLocalRounds * 3 * 4 * sizeof(uint64_t);
-// Entries per column and upload chunk when host columns stream in (3 x 8 MiB).
-constexpr size_t kDefaultUploadChunk = size_t{1} << 20;
+// Entries per column and upload chunk when host columns stream in (3 x 16 MiB;
+// 2^20 and 2^22 measured within 1 % of it on a 2^24 proof with two lanes).
+constexpr size_t kDefaultUploadChunk = size_t{1} << 21;
 
 uint64_t triple_enqueue(Backend& b, Owned& own, uint64_t a, uint64_t bb, uint64_t c, size_t n, FpStream& tx,
                         bool base, size_t& k_out, const HostColumns* host) {
