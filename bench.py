@@ -56,6 +56,7 @@ def parse():
     ap.add_argument("--ligero-log2-code", type=int, default=16)
     ap.add_argument("--ligero-queries", type=int, default=128)
     ap.add_argument("--no-ligero", action="store_true")
+    ap.add_argument("--no-ligero-zk", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--lanes", type=int, choices=[1, 2], default=2,
                     help="2: the triple sumcheck and the LogUp proof run concurrently on two contexts")
@@ -179,6 +180,43 @@ def cpu_sample(log2_sample: int, log2_table: int, steps: int = 1):
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
+
+def ligero_zk_leg(prover, reps=3):
+    """The reference's full-scale weight commitment shape (ligero.rs:59-60,
+    GPT2_FULL: 8192 rows of 2^14 int16 weights + 512 ChaCha8 pads, RS-encoded
+    to 2^15, 200 queries) committed from host weights, then the device part of
+    its zero-knowledge opening for 13 claims (ligero.rs:1187-1480): 14 Fp2
+    mask rows encoded and committed, the proximity row and 13 claim rows over
+    the whole matrix, 13 masked row dots, 200 data and mask columns with their
+    paths.  Seeded synthetic weights and claims; phases timed on the host
+    around their synchronising downloads (median of `reps`)."""
+    import torch
+
+    rows, col_bits, pad, code_bits, queries, n_claims = 8192, 14, 512, 15, 200, 13
+    rng = np.random.default_rng(0x11)
+    # the weights live in pinned host memory, as a serving process keeps them
+    w = torch.from_numpy(rng.integers(-32768, 32768, size=(rows, 1 << col_bits), dtype=np.int64)
+                         .astype(np.int16)).pin_memory().numpy()
+    claims = []
+    for g in range(n_claims):  # blocks of 2^g2 rows, aligned
+        k = g % 8
+        row0 = (g * 613 // (1 << k)) * (1 << k) % rows
+        claims.append((row0 << col_bits, rng.integers(0, P, size=(col_bits + k, 2), dtype=np.uint64)))
+    c = tuple(int(x) for x in rng.integers(0, P, size=2, dtype=np.uint64))
+    idx = rng.integers(0, 1 << code_bits, size=queries).astype(np.uint32)
+    runs = []
+    for _ in range(reps + 1):
+        o = prover.ligero_commit_open_zk(w, rows, col_bits, pad, code_bits, LIGERO_ROW_SEED, claims,
+                                         bytes([0xA5] * 32), c, idx)
+        runs.append((o["commit_ms"], o["open_ms"]))
+    runs = runs[1:]
+    commit_ms = float(np.median([r[0] for r in runs]))
+    open_ms = float(np.median([r[1] for r in runs]))
+    return {"workload": "GPT2_FULL Ligero weight commitment (8192 x 2^14 int16 + 512 pads -> 2^15) from pinned "
+                        "host weights + device part of the ZK opening (13 claims, 14 mask rows, 200 queries)",
+            "commit_ms": round(commit_ms, 3), "open_ms": round(open_ms, 3), "unit": "ms", "timing": "host, median",
+            "root": bytes(o["root"]).hex(), "mask_root": bytes(o["mask_root"]).hex()}
+
 
 def ligero_leg(args, prover, be, peaks, rank=0, world=1, comm=None):
     """Ligero commitment of rows x 2^msg seeded Fp message
@@ -594,6 +632,10 @@ def run_b200(args, rank, world, local_rank):
     if world == 1 and not args.no_gemm:
         gemm = gemm_leg(args, be, peaks)
 
+    ligero_zk = None
+    if world == 1 and not args.no_ligero and not args.no_ligero_zk:
+        ligero_zk = ligero_zk_leg(prover)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         log2_sample = max(10, min(20, args.log2_sumcheck) - 0)
@@ -622,7 +664,7 @@ def run_b200(args, rank, world, local_rank):
                             "sha256": hashlib.sha256(np.ascontiguousarray(msgs).tobytes() +
                                                      np.ascontiguousarray(finals).tobytes() +
                                                      np.ascontiguousarray(proof).tobytes()).hexdigest()},
-            "ligero": ligero,
+            "ligero": ligero, "ligero_zk": ligero_zk,
             "witness_gemm": gemm,
         }
         print(json.dumps(line), flush=True)

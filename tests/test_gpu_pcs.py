@@ -197,7 +197,8 @@ def test_pcs_messages(be, oracle, rows, cols, pad, code_len):
         be.free(i)
 
 
-@pytest.mark.parametrize("rows,cols,pad,combos", [(1, 1, 0, 1), (3, 17, 4, 2), (16, 300, 8, 5), (128, 2048, 64, 9)])
+@pytest.mark.parametrize("rows,cols,pad,combos", [(1, 1, 0, 1), (3, 17, 4, 2), (16, 300, 8, 5), (128, 2048, 64, 9),
+                                                   (1000, 64, 3, 1), (4096, 512, 0, 2)])  # row bands, ragged last
 def test_pcs_combine_rows(be, oracle, rows, cols, pad, combos):
     rng = np.random.default_rng(rows * cols + combos)
     w = rng.integers(-32768, 32768, size=rows * cols, dtype=np.int64).astype(np.int16)

@@ -172,6 +172,9 @@ def load_host_library():
                                            sz]
         L.vzh_logup_local.argtypes = [vp, u64, sz, u64, sz, u64, sz, C.c_char_p, u64, vp, sz,
                                       C.POINTER(C.c_size_t), C.c_char_p, sz]
+        L.vzh_ligero_commit_open_zk.argtypes = [vp, vp, sz, sz, sz, sz, C.c_char_p, sz, vp, vp, vp, C.c_char_p,
+                                                u64, u64, vp, sz, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                                C.c_char_p, sz]
         L.vzh_fpstream_fp2.argtypes = [C.c_char_p, u64, sz, vp]
         L.vzh_fpstream_u64.argtypes = [C.c_char_p, u64, sz, vp]
         _host_lib = L
@@ -433,6 +436,39 @@ class Prover:
                                            _ptr(out), cap, C.byref(written), err, 1024)
         self._err(rc, err)
         return out[: written.value]
+
+    def ligero_commit_open_zk(self, weights: np.ndarray, rows: int, col_bits: int, pad: int, code_bits: int,
+                              pad_seed: bytes, claims, mask_seed: bytes, c, indices):
+        """Weight-matrix commitment and the device part of its zero-knowledge
+        multi-claim opening (vzh_ligero_commit_open_zk; ligero.rs:465-505,
+        1187-1480).  weights: rows x 2^col_bits int16; claims: [(offset,
+        point [k x 2] u64)]; c: the proximity challenge (c0, c1); indices: the
+        query columns.  Returns a dict of root, mask_root, u_c, u_g, s,
+        columns, mask_columns, paths, mask_paths and the host-timed phases."""
+        w = np.ascontiguousarray(weights, dtype=np.int16)
+        n, q = len(claims), len(indices)
+        cols, msg_len = 1 << col_bits, (1 << col_bits) + pad
+        offsets = np.array([cl[0] for cl in claims], dtype=np.uint64)
+        lens = np.array([len(cl[1]) for cl in claims], dtype=np.uint64)
+        pts = np.ascontiguousarray(np.concatenate([np.asarray(cl[1], dtype=np.uint64).reshape(-1, 2)
+                                                   for cl in claims]) if claims else np.zeros((0, 2)),
+                                   dtype=np.uint64)
+        idx = np.ascontiguousarray(indices, dtype=np.uint32)
+        out = {"root": np.zeros(32, np.uint8), "mask_root": np.zeros(32, np.uint8),
+               "u_c": np.zeros((msg_len, 2), np.uint64), "u_g": np.zeros((n * msg_len, 2), np.uint64),
+               "s": np.zeros((n, 2), np.uint64), "columns": np.zeros(q * rows, np.uint64),
+               "mask_columns": np.zeros((q * (n + 1), 2), np.uint64),
+               "paths": np.zeros(q * code_bits * 32, np.uint8), "mask_paths": np.zeros(q * code_bits * 32, np.uint8)}
+        phases = np.zeros(2, np.float64)
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_ligero_commit_open_zk(
+            self.h, _ptr(w), rows, col_bits, pad, code_bits, pad_seed, n, _ptr(offsets), _ptr(lens), _ptr(pts),
+            mask_seed, int(c[0]), int(c[1]), _ptr(idx), q, _ptr(out["root"]), _ptr(out["mask_root"]),
+            _ptr(out["u_c"]), _ptr(out["u_g"]), _ptr(out["s"]), _ptr(out["columns"]), _ptr(out["mask_columns"]),
+            _ptr(out["paths"]), _ptr(out["mask_paths"]), _ptr(phases), err, 1024)
+        self._err(rc, err)
+        out["commit_ms"], out["open_ms"] = float(phases[0]), float(phases[1])
+        return out
 
     def stats(self) -> RawStats:
         return self.backend.stats()

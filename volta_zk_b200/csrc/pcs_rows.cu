@@ -7,6 +7,8 @@
 //   gather     out[q, i] = matrix[i, idx[q]] (opened columns, ligero.rs:1444)
 #include "runtime.cuh"
 
+#include <algorithm>
+
 namespace vzb {
 namespace {
 
@@ -78,11 +80,74 @@ __global__ void gather_kernel(const T* m, const uint32_t* idx, T* out, size_t ro
     }
 }
 
+// The same sums over a band of rows per grid row (blockIdx.y): partial
+// out[band][combination][j] into `part`, summed by combine_finish_kernel.
+// With few combinations there are only cols + pad columns of work, so one
+// thread per column walking every row waits out a dependent HBM load per row
+// (8192 rows: milliseconds); bands give every SM independent rows to stream.
+__global__ void combine_band_kernel(const int16_t* w, const uint64_t* pads, const Fp2* coeffs, Fp2* part,
+                                    size_t rows, size_t cols, size_t pad, size_t combinations, size_t band_rows) {
+    const size_t msg_len = cols + pad;
+    const size_t groups = (combinations + kCombos - 1) / kCombos;
+    const size_t z = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (z >= groups * msg_len) return;
+    const size_t g = z / msg_len, j = z - g * msg_len;
+    const size_t c0 = g * kCombos, band = blockIdx.y;
+    const size_t r0 = band * band_rows, r1 = min(rows, r0 + band_rows);
+    const int nc = static_cast<int>(combinations - c0 < kCombos ? combinations - c0 : kCombos);
+    Fp2W acc[kCombos];
+#pragma unroll
+    for (int k = 0; k < kCombos; ++k) f2w_zero(acc[k]);
+#pragma unroll 4
+    for (size_t r = r0; r < r1; ++r) {
+        const uint64_t x = j < cols ? from_i16(w[r * cols + j]) : pads[r * pad + (j - cols)];
+#pragma unroll
+        for (int k = 0; k < kCombos; ++k) {
+            if (k < nc) {
+                const Fp2 cf = ldg2(coeffs + (c0 + k) * rows + r);
+                wadd(acc[k].c0, dmul_wide(cf.c0, x));
+                wadd(acc[k].c1, dmul_wide(cf.c1, x));
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kCombos; ++k)
+        if (k < nc) part[(band * combinations + c0 + k) * msg_len + j] = f2w_reduce(acc[k]);
+}
+
+__global__ void combine_finish_kernel(const Fp2* part, Fp2* out, size_t bands, size_t entries) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t z = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; z < entries; z += stride) {
+        Fp2 s{0, 0};
+        for (size_t b = 0; b < bands; ++b) s = f2add(s, ldg2(part + b * entries + z));
+        st2(out + z, s);
+    }
+}
+
 int combine(Context* c, const int16_t* w, const uint64_t* pads, const Fp2* coeffs, Fp2* out, size_t rows,
             size_t cols, size_t pad, size_t combinations) {
-    const size_t items = ((combinations + kCombos - 1) / kCombos) * (cols + pad);
-    combine_kernel<<<grid_for(c, items, 256), 256, 0, c->stream>>>(w, pads, coeffs, out, rows, cols, pad,
-                                                                   combinations);
+    const size_t msg_len = cols + pad;
+    const size_t items = ((combinations + kCombos - 1) / kCombos) * msg_len;
+    // aim for about 2 x 1024 threads per SM, with bands of at least 32 rows
+    const size_t want = static_cast<size_t>(c->sm_count) * 2048;
+    size_t bands = items >= want ? 1 : (want + items - 1) / items;
+    bands = std::min<size_t>(std::min(bands, (rows + 31) / 32), 65535);
+    if (bands <= 1) {
+        combine_kernel<<<grid_for(c, items, 256), 256, 0, c->stream>>>(w, pads, coeffs, out, rows, cols, pad,
+                                                                       combinations);
+        VZB_LAUNCHED(c);
+        return 0;
+    }
+    const size_t band_rows = (rows + bands - 1) / bands;
+    bands = (rows + band_rows - 1) / band_rows;
+    const size_t entries = combinations * msg_len;
+    if (ensure_ws(c, kWsScratch, bands * entries * sizeof(Fp2))) return -1;
+    Fp2* part = ws<Fp2>(c, kWsScratch);
+    const dim3 grid(static_cast<unsigned>((items + 255) / 256), static_cast<unsigned>(bands));
+    combine_band_kernel<<<grid, 256, 0, c->stream>>>(w, pads, coeffs, part, rows, cols, pad, combinations,
+                                                     band_rows);
+    VZB_LAUNCHED(c);
+    combine_finish_kernel<<<grid_for(c, entries, 256), 256, 0, c->stream>>>(part, out, bands, entries);
     VZB_LAUNCHED(c);
     return 0;
 }

@@ -178,4 +178,43 @@ struct LigeroOpening {
 LigeroOpening ligero_commit_open_resident(Backend& b, const uint8_t row_seed[32], size_t rows, size_t msg_len,
                                           size_t code_len, size_t queries, FpStream& tx);
 
+// Weight-matrix commitment and its zero-knowledge multi-claim opening, device
+// part (rust/volta-pcs/src/ligero.rs:465-505 finish_resident_commit,
+// 1187-1480 open_multi_zk_resident).  The matrix is rows x 2^col_bits int16
+// weights; each row is (weights mod p || pad ChaCha8 words from
+// FpStream(pad_seed, r)) zero-padded to 2^code_bits, RS-encoded by the batched
+// NTT and committed by the BLAKE3 column tree.  The opening draws claims + 1
+// prover-secret Fp2 mask rows (FpStream(mask_seed, g), msg_len words, padded),
+// encodes and commits them, forms u_c = sum_r c^r row_r + mask_0 (proximity)
+// and, per claim g, u_g = sum_r eq(point[col_bits..], r - row0) row_r +
+// mask_{g+1} and s_g = <mask_{g+1}[0 .. cols), eq(point[.. col_bits])>, then
+// gathers the queried data and mask columns with their Merkle paths.  The
+// transcript values (c, the query indices) come from the caller, and the
+// VOLE-MAC bookkeeping on s_g (corrections, zero batch) stays with the
+// caller's correlation stream: it is O(claims) host work.
+struct LigeroShape {
+    size_t rows = 0, col_bits = 0, pad = 0, code_bits = 0;
+    size_t cols() const { return size_t{1} << col_bits; }
+    size_t msg_len() const { return cols() + pad; }
+    size_t code_len() const { return size_t{1} << code_bits; }
+};
+struct ZkClaim {
+    size_t offset = 0;        // first coefficient of the claimed block (aligned to its size)
+    std::vector<Fp2> point;   // LSB-first: col_bits column coordinates, then row coordinates
+};
+struct LigeroZkOpening {
+    uint8_t root[32];
+    uint8_t mask_root[32];
+    std::vector<Fp2> u_c;               // msg_len
+    std::vector<Fp2> u_g;               // claims x msg_len
+    std::vector<Fp2> s;                 // claims
+    std::vector<uint64_t> columns;      // queries x rows
+    std::vector<Fp2> mask_columns;      // queries x (claims + 1)
+    std::vector<uint8_t> paths, mask_paths;  // queries x code_bits x 32
+};
+LigeroZkOpening ligero_commit_open_zk(Backend& b, const int16_t* weights, const LigeroShape& shape,
+                                      const uint8_t pad_seed[32], const std::vector<ZkClaim>& claims,
+                                      const uint8_t mask_seed[32], Fp2 c, const std::vector<uint32_t>& indices,
+                                      double phase_ms[2] = nullptr);
+
 }  // namespace vzh

@@ -225,6 +225,44 @@ int vzh_proof_local_host(void* h, uint64_t a, uint64_t bb, uint64_t c, const uin
     });
 }
 
+// Weight-matrix commitment + zero-knowledge multi-claim opening, device part
+// (see accel.hpp).  Claim g has point_lens[g] coordinates, concatenated in
+// `points`, and offsets[g]; outputs as in LigeroZkOpening (flat arrays).
+int vzh_ligero_commit_open_zk(void* h, const int16_t* weights, size_t rows, size_t col_bits, size_t pad,
+                              size_t code_bits, const uint8_t* pad_seed, size_t claims, const uint64_t* offsets,
+                              const size_t* point_lens, const vz_fp2* points, const uint8_t* mask_seed, uint64_t c0,
+                              uint64_t c1, const uint32_t* indices, size_t queries, uint8_t* root, uint8_t* mask_root,
+                              vz_fp2* u_c, vz_fp2* u_g, vz_fp2* s, uint64_t* columns, vz_fp2* mask_columns,
+                              uint8_t* paths, uint8_t* mask_paths, double* phase_ms, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        LigeroShape sh;
+        sh.rows = rows;
+        sh.col_bits = col_bits;
+        sh.pad = pad;
+        sh.code_bits = code_bits;
+        std::vector<ZkClaim> cl(claims);
+        size_t at = 0;
+        for (size_t g = 0; g < claims; ++g) {
+            cl[g].offset = offsets[g];
+            cl[g].point.assign(points + at, points + at + point_lens[g]);
+            at += point_lens[g];
+        }
+        const std::vector<uint32_t> idx(indices, indices + queries);
+        const LigeroZkOpening o =
+            ligero_commit_open_zk(*static_cast<Backend*>(h), weights, sh, pad_seed, cl, mask_seed, Fp2{c0, c1}, idx,
+                                  phase_ms);
+        std::memcpy(root, o.root, 32);
+        std::memcpy(mask_root, o.mask_root, 32);
+        std::memcpy(u_c, o.u_c.data(), o.u_c.size() * sizeof(vz_fp2));
+        std::memcpy(u_g, o.u_g.data(), o.u_g.size() * sizeof(vz_fp2));
+        std::memcpy(s, o.s.data(), o.s.size() * sizeof(vz_fp2));
+        std::memcpy(columns, o.columns.data(), o.columns.size() * sizeof(uint64_t));
+        std::memcpy(mask_columns, o.mask_columns.data(), o.mask_columns.size() * sizeof(vz_fp2));
+        std::memcpy(paths, o.paths.data(), o.paths.size());
+        std::memcpy(mask_paths, o.mask_paths.data(), o.mask_paths.size());
+    });
+}
+
 // Sharded-proof completion (see accel.hpp); no device involved.
 int vzh_triple_finish(const vz_fp2* parts, size_t shards, size_t n, const uint8_t* seed, vz_fp2* messages,
                       vz_fp2* finals, char* err, size_t len) {
