@@ -213,7 +213,9 @@ __global__ void __launch_bounds__(kLocThreads, 2)
 #pragma unroll
                 for (int k = 0; k < 3; ++k) v[k * kLocL2 + i] = f[k][m];
         }
-#pragma unroll
+        // one copy of the pair code for the upper half (instruction-cache
+        // pressure: every inlined copy is about a thousand instructions)
+#pragma unroll 1
         for (int m = 0; m < kLocPairs; ++m) {
             const int i = threadIdx.x + m * kLocThreads;
             if (i >= pairs / 2 && i < pairs) {
@@ -278,7 +280,7 @@ __global__ void __launch_bounds__(kLocThreads) triple_local_warp_kernel(const Fp
             x0[k] = ldcs2(src + k * 64 + 2 * lane);
             x1[k] = ldcs2(src + k * 64 + 2 * lane + 1);
         }
-#pragma unroll
+#pragma unroll 1
         for (int jj = 0; jj < kRounds; ++jj) {
             const int pairs = 32 >> jj;
             const Fp2 r = ldg2(rs + kLocSmemRounds + jj);
