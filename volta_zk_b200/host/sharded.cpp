@@ -14,6 +14,12 @@
 namespace vzh {
 namespace {
 
+using vzb::fadd;
+using vzb::fmul;
+using vzb::fmul7;
+using vzb::freduce128;
+using vzb::kP;
+
 // prod_b (bit b of g ? point[b] : 1 - point[b])
 Fp2 eq_bits(const Fp2* point, size_t bits, size_t g) {
     Fp2 acc{1, 0};
@@ -37,6 +43,36 @@ std::vector<Fp2> suffix_table(const std::vector<Fp2>& point, size_t k) {
         t.swap(nxt);
     }
     return t;
+}
+
+// Unreduced sum of 128-bit products with a carry word: value = carry 2^128 +
+// lo, reduced once (2^128 = -2^32 = p - 2^32 mod p).
+struct Wide192 {
+    unsigned __int128 lo = 0;
+    uint64_t carry = 0;
+    void mac(uint64_t a, uint64_t b) {
+        const unsigned __int128 m = static_cast<unsigned __int128>(a) * b;
+        lo += m;
+        carry += lo < m;
+    }
+    uint64_t reduce() const {
+        const uint64_t r = freduce128(static_cast<uint64_t>(lo), static_cast<uint64_t>(lo >> 64));
+        return fadd(r, fmul(carry, kP - (uint64_t{1} << 32)));
+    }
+};
+
+// sum_g s[g] * a[g * stride] in Fp2 with one reduction per coordinate
+// (s7[g] = 7 s[g].c1): the shard combination of the round accumulators.
+Fp2 dot_lazy(const std::vector<Fp2>& sc, const std::vector<uint64_t>& s7, const Fp2* const* a, size_t at) {
+    Wide192 c0, c1;
+    for (size_t g = 0; g < sc.size(); ++g) {
+        const Fp2 v = a[g][at];
+        c0.mac(sc[g].c0, v.c0);
+        c0.mac(s7[g], v.c1);
+        c1.mac(sc[g].c0, v.c1);
+        c1.mac(sc[g].c1, v.c0);
+    }
+    return Fp2{c0.reduce(), c1.reduce()};
 }
 
 std::vector<Fp2> fold(const std::vector<Fp2>& v, Fp2 r) {
@@ -123,12 +159,16 @@ void side_finish(const std::vector<const Fp2*>& parts, size_t depth, size_t s, c
         } else {
             const size_t Lp = l - s;
             std::vector<Fp2> scale(G);
-            for (size_t g = 0; g < G; ++g) scale[g] = eq_bits(sch.point[l].data() + Lp, s, g);
+            std::vector<uint64_t> scale7(G);
+            std::vector<const Fp2*> base(G);
+            for (size_t g = 0; g < G; ++g) {
+                scale[g] = eq_bits(sch.point[l].data() + Lp, s, g);
+                scale7[g] = fmul7(scale[g].c1);
+                base[g] = parts[g] + off[g];
+            }
             for (size_t j = 0; j < Lp; ++j) {
-                std::array<Fp2, 4> acc{};
-                for (size_t g = 0; g < G; ++g)
-                    for (int e = 0; e < 4; ++e)
-                        acc[e] = f2add(acc[e], f2mul(scale[g], parts[g][off[g] + 4 * j + e]));
+                std::array<Fp2, 4> acc;
+                for (int e = 0; e < 4; ++e) acc[e] = dot_lazy(scale, scale7, base.data(), 4 * j + e);
                 accs.push_back(acc);
             }
             for (int e = 0; e < 4; ++e)
