@@ -36,20 +36,29 @@ __device__ __forceinline__ void combine(Fp2 pa, Fp2 pb, Fp2 qa, Fp2 qb, Fp2& p, 
 // first == true: children are leaves (a_i, alpha1) with numerators 1 or -mult.
 // kColumn: the leaves are alpha0 - leaf[i] (`leaf` is a query column).
 template <bool kFirst, bool kColumn = false>
-__global__ void __launch_bounds__(256) tree_tile_kernel(
-    const uint64_t* __restrict__ leaf, const uint32_t* __restrict__ mult, const Fp2* cp,
-    const Fp2* cq, Fp2* p, Fp2* q, int child_bits, int levels, uint64_t alpha1, uint64_t w7a1sq,
-    int neg_mult, uint64_t alpha0 = 0) {
-    __shared__ Fp2 sp[kTreeTile / 2], sq[kTreeTile / 2];
+__global__ void __launch_bounds__(256, 4) tree_tile_kernel(
+    const uint64_t* __restrict__ leaf, const uint32_t* __restrict__ mult, const Fp2* __restrict__ cp,
+    const Fp2* __restrict__ cq, Fp2* __restrict__ p, Fp2* __restrict__ q, int child_bits, int levels,
+    uint64_t alpha1, uint64_t w7a1sq, int neg_mult, uint64_t alpha0 = 0) {
+    // Two shared buffers in turn (level k in A, k + 1 in B, ...): a level
+    // reads one and writes the other, so one barrier per level suffices.
+    __shared__ Fp2 ap[kTreeTile / 2], aq[kTreeTile / 2], bp[kTreeTile / 4], bq[kTreeTile / 4];
     const size_t tile = size_t{1} << levels;  // children handled by this block
     const size_t child0 = static_cast<size_t>(blockIdx.x) * tile;
-    // first combine into shared memory, level child_bits - 1
-    size_t half = tile / 2;
+    // first combine into shared memory, level child_bits - 1; the loop is
+    // unrolled over its at most 4 parents per thread so that all of a thread's
+    // loads can be in flight before the first combine (the outputs are
+    // __restrict__, so no store orders them)
+    int half = static_cast<int>(tile / 2);
     {
         const int lvl = child_bits - 1;
         Fp2* po = p + ((size_t{1} << lvl) - 1) + child0 / 2;
         Fp2* qo = q + ((size_t{1} << lvl) - 1) + child0 / 2;
-        for (size_t i = threadIdx.x; i < half; i += blockDim.x) {
+        constexpr int kPer = kTreeTile / 2 / 256;
+#pragma unroll
+        for (int m = 0; m < kPer; ++m) {
+            const int i = threadIdx.x + m * 256;
+            if (i >= half) break;
             Fp2 pv, qv;
             if (kFirst) {
                 uint64_t a = __ldcs(leaf + child0 + 2 * i), b = __ldcs(leaf + child0 + 2 * i + 1);
@@ -70,51 +79,45 @@ __global__ void __launch_bounds__(256) tree_tile_kernel(
                 const Fp2 qa = ldcs2(cq + child0 + 2 * i), qb = ldcs2(cq + child0 + 2 * i + 1);
                 combine(pa, pb, qa, qb, pv, qv);
             }
-            sp[i] = pv;
-            sq[i] = qv;
+            ap[i] = pv;
+            aq[i] = qv;
             st2(po + i, pv);
             st2(qo + i, qv);
         }
     }
     __syncthreads();
-    // remaining combines inside the tile: through shared memory while a
-    // level has more than 32 nodes (at most 2 parents per thread, kept in
-    // registers) ...
-    constexpr int kPer = kTreeTile / 4 / 256;
+    // remaining combines inside the tile through shared memory while a level
+    // has more than 32 nodes ...
     int step = 1;
+    bool in_a = true;
     for (; step < levels && half > 32; ++step) {
-        const size_t parents = half / 2;
+        const int parents = half / 2;
         const int lvl = child_bits - 1 - step;
         const size_t base = child0 >> (step + 1);
         Fp2* po = p + ((size_t{1} << lvl) - 1) + base;
         Fp2* qo = q + ((size_t{1} << lvl) - 1) + base;
-        Fp2 np[kPer], nq[kPer];
-#pragma unroll
-        for (int m = 0; m < kPer; ++m) {
-            const size_t i = threadIdx.x + static_cast<size_t>(m) * 256;
-            if (i < parents) combine(sp[2 * i], sp[2 * i + 1], sq[2 * i], sq[2 * i + 1], np[m], nq[m]);
-        }
-        __syncthreads();
-#pragma unroll
-        for (int m = 0; m < kPer; ++m) {
-            const size_t i = threadIdx.x + static_cast<size_t>(m) * 256;
-            if (i < parents) {
-                sp[i] = np[m];
-                sq[i] = nq[m];
-                st2(po + i, np[m]);
-                st2(qo + i, nq[m]);
-            }
+        const Fp2 *sp = in_a ? ap : bp, *sq = in_a ? aq : bq;
+        Fp2 *dp = in_a ? bp : ap, *dq = in_a ? bq : aq;
+        for (int i = threadIdx.x; i < parents; i += 256) {
+            Fp2 np, nq;
+            combine(sp[2 * i], sp[2 * i + 1], sq[2 * i], sq[2 * i + 1], np, nq);
+            dp[i] = np;
+            dq[i] = nq;
+            st2(po + i, np);
+            st2(qo + i, nq);
         }
         __syncthreads();
         half = parents;
+        in_a = !in_a;
     }
     // ... then warp 0 alone, node j of a level in lane j, with shuffles
     if (step < levels && threadIdx.x < 32) {
         const int lane = threadIdx.x;
-        Fp2 pv = lane < static_cast<int>(half) ? sp[lane] : Fp2{0, 0};
-        Fp2 qv = lane < static_cast<int>(half) ? sq[lane] : Fp2{0, 0};
+        const Fp2 *sp = in_a ? ap : bp, *sq = in_a ? aq : bq;
+        Fp2 pv = lane < half ? sp[lane] : Fp2{0, 0};
+        Fp2 qv = lane < half ? sq[lane] : Fp2{0, 0};
         for (; step < levels; ++step) {
-            const int parents = static_cast<int>(half / 2);
+            const int parents = half / 2;
             const int lvl = child_bits - 1 - step;
             const size_t base = child0 >> (step + 1);
             const int a = (2 * lane) & 31, b = (2 * lane + 1) & 31;
