@@ -6,8 +6,12 @@
 // inside a slice, so the global round accumulators are sums of the shards'
 // (LogUp: weighted by eq(top coordinates of the claim point, g)), and the last
 // s rounds run here on the 2^s values the shards have left.
+#include <algorithm>
 #include <array>
+#include <atomic>
 #include <cstring>
+#include <exception>
+#include <thread>
 
 #include "protocol.hpp"
 
@@ -123,28 +127,43 @@ size_t local_side_words(size_t depth, size_t s) {
     return w;
 }
 
-// One side: parts[g] points at shard g's words for this side.
-void side_finish(const std::vector<const Fp2*>& parts, size_t depth, size_t s, const SideSchedule& sch,
-                 std::vector<Fp2>& proof) {
-    const size_t G = parts.size();
-    // top s levels of the fraction tree from the shard roots (level s)
-    std::vector<std::vector<Fp2>> lp(s + 1), lq(s + 1);
-    for (size_t g = 0; g < G; ++g) {
-        lp[s].push_back(parts[g][0]);
-        lq[s].push_back(parts[g][1]);
-    }
-    for (size_t lv = s; lv-- > 0;) {
-        const auto &cp = lp[lv + 1], &cq = lq[lv + 1];
-        for (size_t i = 0; i < cp.size() / 2; ++i) {
-            lp[lv].push_back(f2add(f2mul(cp[2 * i], cq[2 * i + 1]), f2mul(cp[2 * i + 1], cq[2 * i])));
-            lq[lv].push_back(f2mul(cq[2 * i], cq[2 * i + 1]));
+// One side: parts[g] points at shard g's words for this side.  The top s
+// levels of the fraction tree come from the shard roots; every layer's words
+// then depend only on the parts, the schedule and those levels, so the layers
+// are independent tasks (SideFinish::layer), run on a few threads by the
+// caller and concatenated in order.
+struct SideFinish {
+    std::vector<const Fp2*> parts;
+    size_t depth = 0, s = 0;
+    const SideSchedule* sch = nullptr;
+    std::vector<std::vector<Fp2>> lp, lq;  // levels 0 .. s of the tree
+    std::vector<size_t> off;               // each shard's word offset of layer l >= s
+    std::vector<std::vector<Fp2>> words;   // per layer: 2 per round, then the 4 final values
+
+    SideFinish(const std::vector<const Fp2*>& p, size_t d, size_t s_, const SideSchedule& sc)
+        : parts(p), depth(d), s(s_), sch(&sc), lp(s_ + 1), lq(s_ + 1), off(d, 0), words(d) {
+        const size_t G = parts.size();
+        for (size_t g = 0; g < G; ++g) {
+            lp[s].push_back(parts[g][0]);
+            lq[s].push_back(parts[g][1]);
+        }
+        for (size_t lv = s; lv-- > 0;) {
+            const auto &cp = lp[lv + 1], &cq = lq[lv + 1];
+            for (size_t i = 0; i < cp.size() / 2; ++i) {
+                lp[lv].push_back(f2add(f2mul(cp[2 * i], cq[2 * i + 1]), f2mul(cp[2 * i + 1], cq[2 * i])));
+                lq[lv].push_back(f2mul(cq[2 * i], cq[2 * i + 1]));
+            }
+        }
+        size_t o = 2;
+        for (size_t l = s; l < depth; ++l) {
+            off[l] = o;
+            o += 4 * (l - s) + 4;
         }
     }
-    proof.push_back(lp[0][0]);
-    proof.push_back(lq[0][0]);
-    std::vector<size_t> off(G, 2);
-    for (size_t l = 0; l < depth; ++l) {
-        const size_t L = l;
+
+    void layer(size_t l) {
+        const SideSchedule& sc = *sch;
+        const size_t G = parts.size(), L = l;
         std::vector<std::array<Fp2, 4>> accs;
         std::vector<Fp2> vec[4];
         size_t first_host_round = 0;
@@ -162,9 +181,9 @@ void side_finish(const std::vector<const Fp2*>& parts, size_t depth, size_t s, c
             std::vector<uint64_t> scale7(G);
             std::vector<const Fp2*> base(G);
             for (size_t g = 0; g < G; ++g) {
-                scale[g] = eq_bits(sch.point[l].data() + Lp, s, g);
+                scale[g] = eq_bits(sc.point[l].data() + Lp, s, g);
                 scale7[g] = fmul7(scale[g].c1);
-                base[g] = parts[g] + off[g];
+                base[g] = parts[g] + off[l];
             }
             for (size_t j = 0; j < Lp; ++j) {
                 std::array<Fp2, 4> acc;
@@ -172,26 +191,33 @@ void side_finish(const std::vector<const Fp2*>& parts, size_t depth, size_t s, c
                 accs.push_back(acc);
             }
             for (int e = 0; e < 4; ++e)
-                for (size_t g = 0; g < G; ++g) vec[e].push_back(parts[g][off[g] + 4 * Lp + e]);
-            for (size_t g = 0; g < G; ++g) off[g] += 4 * Lp + 4;
+                for (size_t g = 0; g < G; ++g) vec[e].push_back(base[g][4 * Lp + e]);
             first_host_round = Lp;
         }
         for (size_t j = first_host_round; j < L; ++j) {
             std::array<Fp2, 4> acc;
-            logup_round(vec, suffix_table(sch.point[l], L - 1 - j), acc.data());
+            logup_round(vec, suffix_table(sc.point[l], L - 1 - j), acc.data());
             accs.push_back(acc);
-            for (auto& v : vec) v = fold(v, sch.r[l][j]);
+            for (auto& v : vec) v = fold(v, sc.r[l][j]);
         }
+        std::vector<Fp2>& out = words[l];
+        out.reserve(2 * L + 4);
         Fp2 cpref{1, 0};
         for (size_t j = 0; j < L; ++j) {
             const auto& a = accs[j];
-            proof.push_back(f2mul(cpref, f2add(f2mul(sch.lambda[l], a[0]), a[2])));
-            proof.push_back(f2mul(cpref, f2add(f2mul(sch.lambda[l], a[1]), a[3])));
-            cpref = eq_step(cpref, sch.point[l][j], sch.r[l][j]);
+            out.push_back(f2mul(cpref, f2add(f2mul(sc.lambda[l], a[0]), a[2])));
+            out.push_back(f2mul(cpref, f2add(f2mul(sc.lambda[l], a[1]), a[3])));
+            cpref = eq_step(cpref, sc.point[l][j], sc.r[l][j]);
         }
-        for (auto& v : vec) proof.push_back(v[0]);
+        for (auto& v : vec) out.push_back(v[0]);
     }
-}
+
+    void append(std::vector<Fp2>& proof) const {
+        proof.push_back(lp[0][0]);
+        proof.push_back(lq[0][0]);
+        for (const auto& w : words) proof.insert(proof.end(), w.begin(), w.end());
+    }
+};
 
 }  // namespace
 
@@ -233,10 +259,37 @@ std::vector<Fp2> logup_finish(const Fp2* parts, size_t G, size_t words_per_shard
         pf[g] = parts + g * words_per_shard + 1;
         pt[g] = pf[g] + wf;
     }
+    // both schedules first, in stream order; then every layer of both sides
+    // as an independent task on a few threads (largest first), the words
+    // concatenated in protocol order
     const SideSchedule sf = draw_side_schedule(chal, df);
-    side_finish(pf, df, s, sf, proof);
     const SideSchedule st = draw_side_schedule(chal, dt);
-    side_finish(pt, dt, s, st, proof);
+    SideFinish fin[2] = {SideFinish(pf, df, s, sf), SideFinish(pt, dt, s, st)};
+    std::vector<std::pair<int, size_t>> tasks;
+    for (int side = 0; side < 2; ++side)
+        for (size_t l = 0; l < fin[side].depth; ++l) tasks.emplace_back(side, l);
+    std::sort(tasks.begin(), tasks.end(), [](const auto& a, const auto& b) { return a.second > b.second; });
+    const unsigned hw = std::thread::hardware_concurrency();
+    // three threads: all ranks of a node finish at once, and a node's host
+    // cores also serve the ranks' lane threads and NCCL
+    const size_t nthreads = std::max<size_t>(1, std::min<size_t>({size_t{3}, size_t{hw ? hw : 1u}, tasks.size()}));
+    std::atomic<size_t> next{0};
+    std::vector<std::exception_ptr> errs(nthreads);
+    auto work = [&](size_t t) {
+        try {
+            for (size_t k; (k = next.fetch_add(1)) < tasks.size();) fin[tasks[k].first].layer(tasks[k].second);
+        } catch (...) {
+            errs[t] = std::current_exception();
+        }
+    };
+    std::vector<std::thread> pool;
+    for (size_t t = 1; t < nthreads; ++t) pool.emplace_back(work, t);
+    work(0);
+    for (auto& th : pool) th.join();
+    for (const auto& e : errs)
+        if (e) std::rethrow_exception(e);
+    fin[0].append(proof);
+    fin[1].append(proof);
     return proof;
 }
 

@@ -50,14 +50,32 @@ def torch_all_gather(device=None) -> AllGather:
     return gather
 
 
-def concurrently(first, second):
-    """Run `second` in another host thread while `first` runs in this one
-    (the library's calls release the GIL); both results, or the first error.
-    The worker takes this thread's current CUDA device (a new thread starts
-    on device 0, where another GPU's contexts are invalid)."""
-    import threading
+_LANES = {}
 
-    box = {}
+
+def _lane(device):
+    """One persistent worker thread per CUDA device (created on first use,
+    bound to the device once), so a proof does not pay for a thread start."""
+    ex = _LANES.get(device)
+    if ex is None:
+        from concurrent.futures import ThreadPoolExecutor
+
+        def bind():
+            if device is not None:
+                import torch
+
+                torch.cuda.set_device(device)
+
+        ex = ThreadPoolExecutor(max_workers=1, initializer=bind, thread_name_prefix="volta-lane")
+        _LANES[device] = ex
+    return ex
+
+
+def concurrently(first, second):
+    """Run `second` on this device's lane thread while `first` runs in this
+    one (the library's calls release the GIL); both results, or the first
+    error.  The lane thread runs on this thread's current CUDA device (a new
+    thread starts on device 0, where another GPU's contexts are invalid)."""
     device = None
     try:
         import torch
@@ -66,26 +84,14 @@ def concurrently(first, second):
             device = torch.cuda.current_device()
     except ImportError:
         pass
-
-    def worker():
-        try:
-            if device is not None:
-                import torch
-
-                torch.cuda.set_device(device)
-            box["value"] = second()
-        except BaseException as e:  # re-raised below
-            box["error"] = e
-
-    th = threading.Thread(target=worker)
-    th.start()
+    fut = _lane(device).submit(second)
     try:
         a = first()
     finally:
-        th.join()
-    if "error" in box:
-        raise box["error"]
-    return a, box["value"]
+        err = fut.exception()  # waits for `second` whatever `first` did
+    if err is not None:
+        raise err
+    return a, fut.result()
 
 
 def _host():
