@@ -115,3 +115,32 @@ def test_two_gloo_ranks():
     results = dict(q.get(timeout=5) for _ in range(2))
     assert results == {0: True, 1: True}
     assert all(p.exitcode == 0 for p in procs)
+
+
+def test_concurrently_lane_semantics():
+    """sh.concurrently: both results in order, the second function on one
+    persistent lane thread, its error re-raised, and the lane finishes its
+    work even when the first function raises."""
+    import threading
+    import time
+
+    main = threading.get_ident()
+    a, b = sh.concurrently(lambda: 1, lambda: threading.get_ident())
+    assert a == 1 and b != main
+    _, b2 = sh.concurrently(lambda: 2, lambda: threading.get_ident())
+    assert b2 == b  # the same lane thread serves every call
+
+    with pytest.raises(ValueError, match="lane"):
+        sh.concurrently(lambda: 3, lambda: (_ for _ in ()).throw(ValueError("lane")))
+
+    done = []
+
+    def slow():
+        time.sleep(0.05)
+        done.append(True)
+        return 4
+
+    with pytest.raises(KeyError):
+        sh.concurrently(lambda: {}["missing"], slow)
+    assert done == [True]  # the lane's work completed before the error surfaced
+    assert sh.concurrently(lambda: 5, lambda: 6) == (5, 6)
