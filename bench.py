@@ -446,8 +446,12 @@ def run_b200(args, rank, world, local_rank):
         f_col = be_b.upload_new(np.ascontiguousarray(embed_i16(f)[fs]))
         t_col = be_b.upload_new(np.ascontiguousarray(embed_i16(table)[ts]))
         m_col = be_b.upload_new(np.ascontiguousarray(mult[ts]))
-        sharded = ShardedProver(prover, rank, world, torch_all_gather(torch.device("cuda", local_rank)),
-                                logup_prover=prover_b if args.lanes == 2 else None)
+        dev = torch.device("cuda", local_rank)
+        # on two lanes the LogUp lane gathers on its own communicator as soon
+        # as its local part is done (every rank creates the group, in order)
+        lg_gather = torch_all_gather(dev, dist.new_group(backend="nccl")) if args.lanes == 2 else None
+        sharded = ShardedProver(prover, rank, world, torch_all_gather(dev),
+                                logup_prover=prover_b if args.lanes == 2 else None, logup_gather=lg_gather)
 
     def both(run_triple, run_logup):
         """The two protocols of a proof; on two lanes the LogUp part runs in a

@@ -117,6 +117,77 @@ def test_two_gloo_ranks():
     assert all(p.exitcode == 0 for p in procs)
 
 
+class _EmuProver:
+    """Stand-in for accel.Prover inside ShardedProver: each shard's local work
+    by the oracle emulation, on arrays registered under integer ids."""
+
+    def __init__(self, oracle, store):
+        import types
+
+        self.o, self.store = oracle, store
+        self.backend = types.SimpleNamespace(wait_uploads=lambda: None)
+
+    def triple_sumcheck(self, a, b, c, n, seed):
+        return em.triple_local(self.o, self.store[a], self.store[b], self.store[c], seed)
+
+    def logup_local(self, f, nf, t, nt, mult, s, seed, domain):
+        w, _ = em.logup_local(self.o, self.store[f], self.store[t], self.store[mult], s, seed, domain)
+        return w
+
+
+def _rank_split(rank, world, port, q):
+    """ShardedProver.prove with two lanes and the LogUp gather on a second
+    communicator: the LogUp lane gathers and finishes while the triple lane
+    still works, over gloo, twice in a row."""
+    import torch.distributed as dist
+
+    from oracle import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        second = dist.new_group(backend="gloo")
+        f, table, mult = lookup_case(8, 4, 5)
+        nf, nt, n = f.size, table.size, 64
+        fe, te = em.embed_i16(f), em.embed_i16(table)
+        a, b, c = tables(oracle, n)
+        sl = lambda x, m: x[rank * m // world:(rank + 1) * m // world]  # noqa: E731
+        store = {1: sl(a, n), 2: sl(b, n), 3: sl(c, n), 4: sl(fe, nf), 5: sl(te, nt), 6: sl(mult, nt)}
+        sp = sh.ShardedProver(_EmuProver(oracle, store), rank, world, sh.torch_all_gather(),
+                              logup_prover=_EmuProver(oracle, store),
+                              logup_gather=sh.torch_all_gather(group=second))
+        tseed, lseed, domain = bytes([0x5A] * 32), bytes([0x4C] * 32), 0x1004
+        em_msgs, em_finals = oracle.triple_sumcheck(a, b, c, tseed)
+        em_proof = oracle.logup_prove(f, table, mult, lseed, domain)
+        ok = True
+        for _ in range(2):
+            msgs, finals, proof = sp.prove(1, 2, 3, n, tseed, 4, nf, 5, nt, 6, lseed, domain)
+            ok = ok and np.array_equal(msgs, em_msgs) and np.array_equal(finals, em_finals)
+            ok = ok and np.array_equal(proof, em_proof)
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_split_gathers():
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_split, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    results = dict(q.get(timeout=5) for _ in range(2))
+    assert results == {0: True, 1: True}
+    assert all(p.exitcode == 0 for p in procs)
+
+
 def test_concurrently_lane_semantics():
     """sh.concurrently: both results in order, the second function on one
     persistent lane thread, its error re-raised, and the lane finishes its

@@ -32,9 +32,10 @@ from .accel import AccelError, _ptr, load_host_library
 AllGather = Callable[[np.ndarray], List[np.ndarray]]
 
 
-def torch_all_gather(device=None) -> AllGather:
+def torch_all_gather(device=None, group=None) -> AllGather:
     """All-gather of equally shaped uint64 arrays through torch.distributed
-    (NCCL when `device` is a CUDA device, else the process group's backend)."""
+    (NCCL when `device` is a CUDA device, else the process group's backend),
+    on `group` (default: the world group)."""
     import torch
     import torch.distributed as dist
 
@@ -42,9 +43,10 @@ def torch_all_gather(device=None) -> AllGather:
         t = torch.from_numpy(np.ascontiguousarray(x).view(np.int64).reshape(-1))
         if device is not None:
             t = t.to(device)
-        out = torch.empty(dist.get_world_size() * t.numel(), dtype=torch.int64, device=t.device)
-        dist.all_gather_into_tensor(out, t)
-        parts = out.cpu().numpy().view(np.uint64).reshape(dist.get_world_size(), -1)
+        world = dist.get_world_size(group)
+        out = torch.empty(world * t.numel(), dtype=torch.int64, device=t.device)
+        dist.all_gather_into_tensor(out, t, group=group)
+        parts = out.cpu().numpy().view(np.uint64).reshape(world, -1)
         return [p.reshape(x.shape) for p in parts]
 
     return gather
@@ -141,13 +143,19 @@ class ShardedProver:
     """Runs this shard's local work on its GPU through a Prover (the host
     mirror over the seam) and completes the proof after one all-gather."""
 
-    def __init__(self, prover, rank: int, world: int, all_gather: AllGather, logup_prover=None):
+    def __init__(self, prover, rank: int, world: int, all_gather: AllGather, logup_prover=None,
+                 logup_gather: AllGather = None):
         """logup_prover: a second Prover (its own context) on which prove()
-        runs the LogUp part concurrently with the triple part."""
+        runs the LogUp part concurrently with the triple part.  logup_gather:
+        an all-gather on a second communicator; with it, the LogUp lane
+        gathers and finishes its proof as soon as its local part is done
+        (under the triple part's upload or compute) instead of joining the
+        triple part's gather."""
         if world & (world - 1):
             raise ValueError("the shard count must be a power of two")
         self.prover, self.rank, self.world, self.gather = prover, rank, world, all_gather
         self.logup_prover = logup_prover
+        self.logup_gather = logup_gather
         self.s = world.bit_length() - 1
 
     def triple_sumcheck(self, a: int, b: int, c: int, n: int, seed: bytes, base: bool = False):
@@ -161,8 +169,9 @@ class ShardedProver:
     def prove(self, a: int, b: int, c: int, n: int, triple_seed: bytes, f_col: int, n_f: int, t_col: int, n_t: int,
               mult: int, logup_seed: bytes, domain: int, base: bool = False, host=None, chunk: int = 0):
         """Both parts of a config-1 proof with one local call and one
-        all-gather: (triple messages, triple finals, LogUp proof words), equal
-        to triple_sumcheck followed by logup_prove.  `host`: this shard's
+        all-gather (two, on two communicators, with logup_gather): (triple
+        messages, triple finals, LogUp proof words), equal to triple_sumcheck
+        followed by logup_prove.  `host`: this shard's
         triple columns (base only) still in pinned host memory, three
         addresses; they fill a, b, c chunk by chunk under the first rounds."""
         nl = n // self.world
@@ -180,10 +189,17 @@ class ShardedProver:
                 return np.concatenate([m, f])
 
             def logup_part():
-                return self.logup_prover.logup_local(f_col, n_f // self.world, t_col, n_t // self.world, mult,
-                                                     self.s, logup_seed, domain)
+                local = self.logup_prover.logup_local(f_col, n_f // self.world, t_col, n_t // self.world, mult,
+                                                      self.s, logup_seed, domain)
+                if self.logup_gather is None:
+                    return local
+                # its own communicator: no ordering against the triple gather
+                return logup_finish(self.logup_gather(local), n_f, n_t, logup_seed, domain)
 
             tri, lg = concurrently(triple_part, logup_part)
+            if self.logup_gather is not None:
+                msgs, finals = triple_finish(self.gather(tri), n, triple_seed)
+                return msgs, finals, lg
             local = np.concatenate([tri, lg])
         parts = self.gather(local)
         kt = 3 * (nl.bit_length() - 1) + 3
