@@ -655,9 +655,7 @@ def run_b200(args, rank, world, local_rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3),
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "Fp2 (u64 Goldilocks)",
             "data": "synthetic (seeded FpStream tables and GELU-LUT queries)",
-            "config": {"workload": f"config 1: triple-product sumcheck 3 x 2^{args.log2_sumcheck} Fp2, "
-                                   f"{args.log2_sumcheck} rounds + LogUp 2^{args.log2_queries} queries "
-                                   f"vs 2^{args.log2_table} table",
+            "config": {"workload": workload_name(args),
                        "parallelism": f"one proof sharded over {world} GPU(s) (top index bits; one NCCL "
                                       f"all-gather per sumcheck)" if world > 1 else "one proof on one GPU",
                        "l2": "inputs larger than L2 (402 MB of Fp tables, 134 MB of queries)",
@@ -677,6 +675,12 @@ def run_b200(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def workload_name(args) -> str:
+    """The config-1 workload both arms name in `config.workload`."""
+    return (f"config 1: triple-product sumcheck 3 x 2^{args.log2_sumcheck} Fp2, {args.log2_sumcheck} rounds + "
+            f"LogUp 2^{args.log2_queries} queries vs 2^{args.log2_table} table")
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
@@ -686,10 +690,10 @@ def run_reference(args, rank):
     v = statistics.median(ts) * scale
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "s/proof", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v * 1e3, 2), "higher_is_better": False,
-            "scaling": "weak", "vs_baseline": None, "dtype": "Fp2 (u64 Goldilocks)",
+            "scaling": "strong", "vs_baseline": None, "dtype": "Fp2 (u64 Goldilocks)",
             "data": "synthetic (seeded FpStream tables and GELU-LUT queries)",
-            "config": {"workload": f"config 1: triple-product sumcheck 3 x 2^{args.log2_sumcheck} Fp2 + LogUp "
-                                   f"2^{args.log2_queries} queries vs 2^{args.log2_table} table"},
+            "config": {"workload": workload_name(args),
+                       "parallelism": "the reference's CPU algorithm on the host cores of rank 0"},
             "cpu_baseline": {"value": round(v, 4), "unit": "s/proof", "cores": os.cpu_count(), "kind": "port",
                              "sample": f"2^{log2_sample} tables/queries per step, scaled x{scale:g}; the Rust "
                                        "reference cannot be built here (no cargo), its CPU algorithm runs as the "
