@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--ligero-queries", type=int, default=128)
     ap.add_argument("--no-ligero", action="store_true")
     ap.add_argument("--no-ligero-zk", action="store_true")
+    ap.add_argument("--split-gather", action="store_true",
+                    help="N > 1, two lanes: the LogUp lane gathers on a second NCCL communicator as soon as its "
+                         "local part is done")
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--lanes", type=int, choices=[1, 2], default=2,
                     help="2: the triple sumcheck and the LogUp proof run concurrently on two contexts")
@@ -449,7 +452,8 @@ def run_b200(args, rank, world, local_rank):
         dev = torch.device("cuda", local_rank)
         # on two lanes the LogUp lane gathers on its own communicator as soon
         # as its local part is done (every rank creates the group, in order)
-        lg_gather = torch_all_gather(dev, dist.new_group(backend="nccl")) if args.lanes == 2 else None
+        lg_gather = (torch_all_gather(dev, dist.new_group(backend="nccl"))
+                     if args.lanes == 2 and args.split_gather else None)
         sharded = ShardedProver(prover, rank, world, torch_all_gather(dev),
                                 logup_prover=prover_b if args.lanes == 2 else None, logup_gather=lg_gather)
 
