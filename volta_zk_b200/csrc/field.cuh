@@ -211,9 +211,11 @@ __host__ __device__ __forceinline__ uint64_t fadd(uint64_t a, uint64_t b) {
 #ifdef __CUDA_ARCH__
     return dadd(a, b);
 #endif
+    // branch-free (masks instead of branches: random field values make
+    // every branch a coin flip for the host's predictor)
     uint64_t s = a + b;
-    s += (s < a) ? kEps : 0;  // a + b >= 2^64: fold the carry as 2^32 - 1
-    return s >= kP ? s - kP : s;
+    s += kEps & (0 - static_cast<uint64_t>(s < a));  // a + b >= 2^64: fold the carry as 2^32 - 1
+    return s - (kP & (0 - static_cast<uint64_t>(s >= kP)));
 }
 
 __host__ __device__ __forceinline__ uint64_t fsub(uint64_t a, uint64_t b) {
@@ -221,20 +223,22 @@ __host__ __device__ __forceinline__ uint64_t fsub(uint64_t a, uint64_t b) {
     return dsub(a, b);
 #endif
     const uint64_t r = a - b;
-    return a < b ? r - kEps : r;  // borrow of 2^64 is -(2^32 - 1)
+    return r - (kEps & (0 - static_cast<uint64_t>(a < b)));  // borrow of 2^64 is -(2^32 - 1)
 }
 
 __host__ __device__ __forceinline__ uint64_t fneg(uint64_t a) { return a ? kP - a : 0; }
 
 __host__ __device__ __forceinline__ uint64_t freduce128(uint64_t lo, uint64_t hi) {
+    // x = lo + 2^64 hi = lo - hh + hl (2^32 - 1) with hi = hh 2^32 + hl
+    // (2^64 = 2^32 - 1, 2^96 = -1 mod p); branch-free, as fadd
     const uint64_t hh = hi >> 32;
     const uint64_t hl = hi & kEps;
     uint64_t t = lo - hh;
-    if (lo < hh) t -= kEps;
+    t -= kEps & (0 - static_cast<uint64_t>(lo < hh));
     const uint64_t u = (hl << 32) - hl;  // hl * (2^32 - 1), never overflows
     uint64_t r = t + u;
-    if (r < t) r += kEps;
-    return r >= kP ? r - kP : r;
+    r += kEps & (0 - static_cast<uint64_t>(r < t));
+    return r - (kP & (0 - static_cast<uint64_t>(r >= kP)));
 }
 
 __host__ __device__ __forceinline__ uint64_t fmul(uint64_t a, uint64_t b) {
@@ -253,8 +257,8 @@ __host__ __device__ __forceinline__ uint64_t fmul7(uint64_t a) {
     const uint64_t lo = a << 3;
     const uint64_t hi = a >> 61;
     uint64_t s = lo + hi * kEps;
-    if (s < lo) s += kEps;
-    if (s >= kP) s -= kP;
+    s += kEps & (0 - static_cast<uint64_t>(s < lo));
+    s -= kP & (0 - static_cast<uint64_t>(s >= kP));
     return fsub(s, a);
 }
 
