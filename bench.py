@@ -158,31 +158,68 @@ class ClockSampler:
 # CPU baseline (the reference's CPU algorithm, C/OpenMP restatement)
 # ---------------------------------------------------------------------------
 
-def cpu_sample(log2_sample: int, log2_table: int, steps: int = 1):
-    """Time the oracle on a bounded sample of config 1 and scale to full size."""
+def cpu_inputs(log2_sumcheck: int, log2_queries: int, log2_table: int):
+    """Config-1 inputs for the CPU arm, at full size: the three FpStream
+    tables lifted to Fp2 and the LogUp query/table/multiplicity columns."""
+    from volta_zk_b200.accel import fpstream_fp_rows  # host ChaCha8 (input synthesis only)
+
+    n = 1 << log2_sumcheck
+    tabs = []
+    for k in range(3):
+        t = np.zeros((n, 2), dtype=np.uint64)
+        t[:, 0] = fpstream_fp_rows(SUMCHECK_SEED, k, n)
+        tabs.append(t)
+    from volta_zk_b200.accel import fpstream_u64
+
+    return tabs, logup_inputs(log2_queries, log2_table, fpstream_u64)
+
+
+def cpu_prove_times(tabs, logup, steps: int):
+    """The reference's CPU algorithm for one whole config-1 proof (the C/OpenMP
+    oracle restatement: clear triple-product sumcheck + logup_prove) on every
+    host core this process may use, timed per proof.  The thread count is set
+    explicitly (torchrun exports OMP_NUM_THREADS=1 when it starts several
+    processes).  Returns (seconds per proof, threads used, the last proof as
+    (messages, finals, LogUp words))."""
     from oracle import oracle as o  # checker / baseline only
 
     o.build()
-    n = 1 << log2_sample
-    a = np.zeros((n, 2), dtype=np.uint64)
-    b = np.zeros((n, 2), dtype=np.uint64)
-    c = np.zeros((n, 2), dtype=np.uint64)
-    for k, t in enumerate((a, b, c)):
-        t[:, 0] = o.chacha_fp_rows(SUMCHECK_SEED, k, 1, n)[0]
-
-    f, table, mult = logup_inputs(log2_sample, log2_table, o.stream_u64)
-    times = []
+    threads = o.set_threads(o.host_threads())
+    f, table, mult = logup
+    times, out = [], None
     for _ in range(steps):
         t0 = time.perf_counter()
-        o.triple_sumcheck(a, b, c, TRANSCRIPT_SEED)
-        o.logup_prove(f, table, mult, LOGUP_SEED, LOGUP_DOMAIN)
+        msgs, finals = o.triple_sumcheck(*tabs, TRANSCRIPT_SEED)
+        words = o.logup_prove(f, table, mult, LOGUP_SEED, LOGUP_DOMAIN)
         times.append(time.perf_counter() - t0)
-    return times
+        out = (msgs, finals, words)
+    return times, threads, out
 
 
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
+
+LIGERO_MASK_SEED = bytes([0xA5] * 32)
+
+
+def ligero_zk_inputs():
+    """Seeded GPT2_FULL-shaped inputs of the ZK commitment leg: 8192 x 2^14
+    int16 weights, 512 pads, code 2^15, 13 claims on aligned row blocks,
+    challenge c and 200 query indices."""
+    rows, col_bits, pad, code_bits, queries, n_claims = 8192, 14, 512, 15, 200, 13
+    rng = np.random.default_rng(0x11)
+    w = rng.integers(-32768, 32768, size=(rows, 1 << col_bits), dtype=np.int64).astype(np.int16)
+    claims = []
+    for g in range(n_claims):  # blocks of 2^k rows, aligned
+        k = g % 8
+        row0 = (g * 613 // (1 << k)) * (1 << k) % rows
+        claims.append((row0 << col_bits, rng.integers(0, P, size=(col_bits + k, 2), dtype=np.uint64)))
+    c = tuple(int(x) for x in rng.integers(0, P, size=2, dtype=np.uint64))
+    idx = rng.integers(0, 1 << code_bits, size=queries).astype(np.uint32)
+    return {"rows": rows, "col_bits": col_bits, "pad": pad, "code_bits": code_bits, "w": w, "claims": claims,
+            "c": c, "idx": idx}
+
 
 def ligero_zk_leg(prover, reps=3):
     """The reference's full-scale weight commitment shape (ligero.rs:59-60,
@@ -195,22 +232,14 @@ def ligero_zk_leg(prover, reps=3):
     around their synchronising downloads (median of `reps`)."""
     import torch
 
-    rows, col_bits, pad, code_bits, queries, n_claims = 8192, 14, 512, 15, 200, 13
-    rng = np.random.default_rng(0x11)
+    z = ligero_zk_inputs()
+    rows, col_bits, pad, code_bits = z["rows"], z["col_bits"], z["pad"], z["code_bits"]
     # the weights live in pinned host memory, as a serving process keeps them
-    w = torch.from_numpy(rng.integers(-32768, 32768, size=(rows, 1 << col_bits), dtype=np.int64)
-                         .astype(np.int16)).pin_memory().numpy()
-    claims = []
-    for g in range(n_claims):  # blocks of 2^g2 rows, aligned
-        k = g % 8
-        row0 = (g * 613 // (1 << k)) * (1 << k) % rows
-        claims.append((row0 << col_bits, rng.integers(0, P, size=(col_bits + k, 2), dtype=np.uint64)))
-    c = tuple(int(x) for x in rng.integers(0, P, size=2, dtype=np.uint64))
-    idx = rng.integers(0, 1 << code_bits, size=queries).astype(np.uint32)
+    w = torch.from_numpy(z["w"]).pin_memory().numpy()
     runs = []
     for _ in range(reps + 1):
-        o = prover.ligero_commit_open_zk(w, rows, col_bits, pad, code_bits, LIGERO_ROW_SEED, claims,
-                                         bytes([0xA5] * 32), c, idx)
+        o = prover.ligero_commit_open_zk(w, rows, col_bits, pad, code_bits, LIGERO_ROW_SEED, z["claims"],
+                                         LIGERO_MASK_SEED, z["c"], z["idx"])
         runs.append((o["commit_ms"], o["open_ms"]))
     runs = runs[1:]
     commit_ms = float(np.median([r[0] for r in runs]))
@@ -573,7 +602,7 @@ def run_b200(args, rank, world, local_rank):
     batch_ms, batch_bytes, batch_jobs = logup_step0_replica(be, args.log2_queries)
     achieved = batch_bytes / (batch_ms / 1e3) / 1e9
     # DRAM read + write bytes per algorithmic byte of this launch, from the ncu
-    # capture of the 2^22-query replica (profiles/logup_round_batch_step0_2p22queries.md)
+    # capture of the 2^22-query replica of the same launch
     traffic_ratio = (201.150720e6 + 3.792640e6) / 201031680
     roofline = {"bound": "hbm",
                 "kernel": f"logup_round_batch_kernel: step 0 of the 2^{args.log2_queries}-query side "
@@ -644,14 +673,18 @@ def run_b200(args, rank, world, local_rank):
     if world == 1 and not args.no_ligero and not args.no_ligero_zk:
         ligero_zk = ligero_zk_leg(prover)
 
-    cpu = None
+    cpu, parity = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        log2_sample = max(10, min(20, args.log2_sumcheck) - 0)
-        ts = cpu_sample(log2_sample, args.log2_table)
-        scale = (1 << args.log2_sumcheck) / (1 << log2_sample)
-        cpu = {"value": round(min(ts) * scale, 4), "unit": "s/proof", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"oracle (C/OpenMP restatement of the reference CPU prover) on 2^{log2_sample} tables "
-                         f"and 2^{log2_sample} queries, scaled x{scale:g} by entries"}
+        tabs, logup = cpu_inputs(args.log2_sumcheck, args.log2_queries, args.log2_table)
+        ts, threads, ref = cpu_prove_times(tabs, logup, steps=2)
+        del tabs
+        cpu = {"value": round(min(ts), 4), "unit": "s/proof", "cores": threads, "kind": "port",
+               "sample": f"one whole config-1 proof at full size (2^{args.log2_sumcheck} tables, "
+                         f"2^{args.log2_queries} queries), best of 2, oracle (C/OpenMP restatement of the reference "
+                         "CPU prover)"}
+        # the oracle's proof is the checker of the device proof at this size
+        parity = bool(np.array_equal(ref[0], msgs) and np.array_equal(ref[1], finals)
+                      and np.array_equal(ref[2], proof))
 
     if rank == 0:
         line = {
@@ -666,7 +699,10 @@ def run_b200(args, rank, world, local_rank):
                        "timing_policy": "wall-only counters"},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "gpu_launches": launches,
             "clocks": clocks.summary(),
-            "proof_check": {"messages": int(msgs.shape[0]), "proof_words": int(proof.shape[0]),
+            "proof_check": {"parity": parity,
+                            "parity_source": "device proof == oracle proof at the measured size" if parity is not None
+                            else "not checked in this run (the oracle runs at N = 1); compare sha256 with N = 1",
+                            "messages": int(msgs.shape[0]), "proof_words": int(proof.shape[0]),
                             "sha256": hashlib.sha256(np.ascontiguousarray(msgs).tobytes() +
                                                      np.ascontiguousarray(finals).tobytes() +
                                                      np.ascontiguousarray(proof).tobytes()).hexdigest()},
@@ -686,21 +722,24 @@ def workload_name(args) -> str:
 
 
 def run_reference(args, rank):
+    """The reference's CPU algorithm (the oracle restatement, all host
+    threads) proving the same whole config-1 proof as the B200 arm, every
+    step at full size: W untimed proofs, then K timed ones."""
     if rank != 0:
         return
-    log2_sample = 20
-    ts = cpu_sample(log2_sample, args.log2_table, steps=args.warmup + args.steps)[args.warmup:]
-    scale = (1 << args.log2_sumcheck) / (1 << log2_sample)
-    v = statistics.median(ts) * scale
+    tabs, logup = cpu_inputs(args.log2_sumcheck, args.log2_queries, args.log2_table)
+    ts, threads, _ = cpu_prove_times(tabs, logup, steps=args.warmup + args.steps)
+    ts = ts[args.warmup:]
+    v = sum(ts) / len(ts)
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "s/proof", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v * 1e3, 2), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "Fp2 (u64 Goldilocks)",
             "data": "synthetic (seeded FpStream tables and GELU-LUT queries)",
             "config": {"workload": workload_name(args),
-                       "parallelism": "the reference's CPU algorithm on the host cores of rank 0"},
-            "cpu_baseline": {"value": round(v, 4), "unit": "s/proof", "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"2^{log2_sample} tables/queries per step, scaled x{scale:g}; the Rust "
-                                       "reference cannot be built here (no cargo), its CPU algorithm runs as the "
+                       "parallelism": f"the reference's CPU algorithm on {threads} host threads of rank 0"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "s/proof", "cores": threads, "kind": "port",
+                             "sample": "the whole config-1 proof at full size every step (no extrapolation); the "
+                                       "Rust reference cannot be built here (no cargo), its CPU algorithm runs as the "
                                        "C/OpenMP oracle restatement"},
             "e2e": {"value": round(v, 4), "unit": "s/proof", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

@@ -223,7 +223,8 @@ int volta_b200_triple_tail_device(void* ctx, uint64_t a_id, uint64_t b_id, uint6
  *
  * The first call on a device resolves the scratch array's device address
  * (once per device, with that device current); make that first call before
- * any stream capture.  All calls share the one scratch array: calls that
+ * any stream capture.  The address is kept per device and driver context: a
+ * call after the context was re-created (cudaDeviceReset) resolves it again.  All calls share the one scratch array: calls that
  * overlap on the GPU (concurrent streams, several host threads) race and
  * must be serialised by the caller.  The result is final once `stream`
  * completes.

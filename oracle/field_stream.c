@@ -17,7 +17,17 @@
  */
 #include "oracle.h"
 
+#include <omp.h>
 #include <string.h>
+
+/* Thread count of every OpenMP loop in the oracle.  Set explicitly by the
+ * CPU baseline so that a launcher's OMP_NUM_THREADS (torchrun sets 1 when it
+ * starts several processes) does not silently serialise it. */
+void or_set_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+}
+
+int or_max_threads(void) { return omp_get_max_threads(); }
 
 #define P_GOLD 0xFFFFFFFF00000001ULL
 

@@ -120,6 +120,8 @@ void or_gemm_requant_auth(const int16_t* a, const int16_t* b, const uint64_t* ma
 
 /* ---- FNV-1a style checksums used by the reference p7 recipes ---- */
 uint64_t or_fnv_u64(uint64_t h, const uint64_t* v, size_t n);
+void or_set_threads(int n);
+int or_max_threads(void);
 
 /* ---- int16 fixed-point forward primitives (fixed.c; backend.cu:1442-1740) ---- */
 void or_fixed_embed(const uint32_t* tokens, const int16_t* wte, const int16_t* wpe, int64_t* acc_out,

@@ -24,8 +24,18 @@ P = 0xFFFFFFFF00000001
 _lib = None
 
 
+def reference_cuda_dir() -> str:
+    """The reference's ``cuda/`` directory, when its source tree is present:
+    ``$VOLTA_REFERENCE_DIR/cuda``, else a ``reference`` checkout beside this
+    repository.  Empty when neither exists (the GPU box has no reference)."""
+    root = os.environ.get("VOLTA_REFERENCE_DIR") or os.path.join(os.path.dirname(os.path.dirname(HERE)),
+                                                                 "reference")
+    d = os.path.join(root, "cuda")
+    return d if os.path.isdir(d) else ""
+
+
 def build() -> str:
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    subprocess.run(["make", "-s", "-C", HERE, f"REF_DIR={reference_cuda_dir()}"], check=True)
     return LIB_PATH
 
 
@@ -112,8 +122,24 @@ def _declare(L):
     L.or_pcs_combine_rows.argtypes = [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp]
     L.or_gemm_i64.argtypes = [_vp, _vp, _vp, _sz, _sz, _sz]
     L.or_gemm_requant_auth.argtypes = [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, C.c_uint32]
+    L.or_set_threads.argtypes = [C.c_int]
+    L.or_max_threads.restype = C.c_int
     L.or_fnv_u64.restype = _u64
     L.or_fnv_u64.argtypes = [_u64, _vp, _sz]
+
+
+def host_threads() -> int:
+    """Host cores this process may run on (affinity mask / cgroup cpuset)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def set_threads(n: int) -> int:
+    """Pin the oracle's OpenMP thread count; returns the count now in force."""
+    lib().or_set_threads(int(n))
+    return int(lib().or_max_threads())
 
 
 def _p(a: np.ndarray):

@@ -177,6 +177,7 @@ def load_host_library():
                                                 C.c_char_p, sz]
         L.vzh_fpstream_fp2.argtypes = [C.c_char_p, u64, sz, vp]
         L.vzh_fpstream_u64.argtypes = [C.c_char_p, u64, sz, vp]
+        L.vzh_fpstream_fp.argtypes = [C.c_char_p, u64, sz, vp]
         _host_lib = L
     return _host_lib
 
@@ -299,6 +300,15 @@ def fpstream_fp2(seed: bytes, domain: int, n: int) -> np.ndarray:
     """The first n Fp2 draws of FpStream(seed, domain), shape (n, 2)."""
     out = np.zeros((n, 2), dtype=np.uint64)
     load_host_library().vzh_fpstream_fp2(seed, domain, n, _ptr(out))
+    return out
+
+
+def fpstream_fp_rows(seed: bytes, domain: int, n: int) -> np.ndarray:
+    """The first n Fp draws of FpStream(seed, domain) (next_fp, rejection
+    exact): the values chacha8_prover_secret_fp_rows_device writes for row
+    `domain`."""
+    out = np.zeros(n, dtype=np.uint64)
+    load_host_library().vzh_fpstream_fp(seed, domain & (2**64 - 1), n, _ptr(out))
     return out
 
 

@@ -63,6 +63,7 @@ __global__ void __launch_bounds__(kThreads) noalloc_triple_kernel(TripleTerms t,
 }
 
 struct DeviceScratch {
+    unsigned long long context_id = 0;  // driver context the addresses belong to
     Fp2* partials = nullptr;
     unsigned* counter = nullptr;
 };
@@ -71,7 +72,37 @@ constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
 DeviceScratch g_scratch[kMaxDevices];
 
-// Resolve the scratch addresses for the current device (once per device).
+// The unique id of the current driver context (cuCtxGetCurrent + cuCtxGetId,
+// reached through the runtime's driver entry points so the library does not
+// link libcuda).  0 when no context is current yet or the query is missing.
+unsigned long long current_context_id() {
+    using GetCurrent = int (*)(void**);
+    using GetId = int (*)(void*, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static bool looked_up = false;
+    if (!looked_up) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(f);
+        looked_up = true;
+    }
+    void* ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != 0 || !ctx || get_id(ctx, &id) != 0) return 0;
+    return id;
+}
+
+// Resolve the scratch addresses for the current device: once per device and
+// driver context, with that device current.  A context created after the
+// previous one was destroyed (cudaDeviceReset) has a new id, so its
+// addresses are resolved again instead of reusing stale ones.
 cudaError_t scratch_for_current_device(DeviceScratch* out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -79,15 +110,17 @@ cudaError_t scratch_for_current_device(DeviceScratch* out) {
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     DeviceScratch& s = g_scratch[dev];
-    if (!s.partials) {
+    const unsigned long long ctx = current_context_id();
+    if (!s.partials || ctx == 0 || ctx != s.context_id) {
         void* p = nullptr;
         void* q = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+        e = cudaGetSymbolAddress(&p, g_noalloc_partials);  // makes the device's primary context current
         if (e != cudaSuccess) return e;
         e = cudaGetSymbolAddress(&q, g_noalloc_counter);
         if (e != cudaSuccess) return e;
         s.partials = static_cast<Fp2*>(p);
         s.counter = static_cast<unsigned*>(q);
+        s.context_id = current_context_id();
     }
     *out = s;
     return cudaSuccess;

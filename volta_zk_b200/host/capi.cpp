@@ -292,6 +292,13 @@ void vzh_fpstream_fp2(const uint8_t* seed, uint64_t domain, size_t n, vz_fp2* ou
     for (size_t i = 0; i < n; ++i) out[i] = s.next_fp2();
 }
 
+// The first n Fp draws (rejection-sampled next_fp) of FpStream(seed, domain):
+// row `domain` of the ChaCha8 prover-secret rows (input synthesis).
+void vzh_fpstream_fp(const uint8_t* seed, uint64_t domain, size_t n, uint64_t* out) {
+    FpStream s(seed, domain);
+    for (size_t i = 0; i < n; ++i) out[i] = s.next_fp();
+}
+
 // Raw u64 draws of FpStream(seed, domain) (input synthesis for benches).
 void vzh_fpstream_u64(const uint8_t* seed, uint64_t domain, size_t n, uint64_t* out) {
     FpStream s(seed, domain);
