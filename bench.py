@@ -72,13 +72,12 @@ def parse():
 # workload synthesis (shared by both arms; host side, untimed)
 # ---------------------------------------------------------------------------
 
-def gelu_table(scale_log2: int = 10) -> np.ndarray:
-    """luts.rs:133-150: gelu[u] for the i16 bit pattern u (tanh approximation)."""
-    x = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16).view(np.int16).astype(np.float64)
-    s = float(1 << scale_log2)
-    xr = x / s
-    g = 0.5 * xr * (1.0 + np.tanh(0.7978845608028654 * (xr + 0.044715 * xr * xr * xr)))
-    return np.clip(np.round(g * s), -32768, 32767).astype(np.int16)
+def gelu_table() -> np.ndarray:
+    """The 2^16-entry int16 GELU table of luts.rs build_luts (LutParams
+    defaults), indexed by the input's u16 bit pattern."""
+    from volta_zk_b200.gpt2 import build_luts
+
+    return build_luts()["gelu"]
 
 
 def embed_i16(v: np.ndarray) -> np.ndarray:

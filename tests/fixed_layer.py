@@ -61,10 +61,11 @@ def digest(a) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
 
-def forward_layer(ops, x, w, luts, t):
+def forward_layer(ops, x, w, luts, t, row_shift=0):
     """forward_layer from the seam primitives; `ops` provides layer_norm,
     gemm, qkv_split, scores, softmax, av, lookup with the oracle's
-    signatures.  Returns {name: array} with the reference's names."""
+    signatures.  row_shift = 1 selects the P5 stable softmax.  Returns
+    {name: array} with the reference's names."""
     r = {}
     ln1 = ops.layer_norm(x, w["ln1_gain"], w["ln1_bias"], luts["ln_rsqrt"], t, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
     r.update(ln1_mean=ln1[0], ln1_var=ln1[1], ln1_rsqrt_in=ln1[2], ln1_rsqrt_out=ln1[3], ln1_out=ln1[5])
@@ -77,10 +78,10 @@ def forward_layer(ops, x, w, luts, t):
     s_acc, s_q, e = ops.scores(q, k, t, t, 0, H, DH, SHIFT_SCORES)
     errs.append(e)
     r.update(scores_acc=s_acc, scores_q=s_q)
-    _, exp_out, denoms, recips, wts, e = ops.softmax(s_q, luts["exp"], luts["softmax_recip"], t, 0, H,
-                                                     RECIP_DEN_SHIFT, RECIP_LOG2, SHIFT_SOFTMAX_NORM, 0)
+    rs, exp_out, denoms, recips, wts, e = ops.softmax(s_q, luts["exp"], luts["softmax_recip"], t, 0, H,
+                                                      RECIP_DEN_SHIFT, RECIP_LOG2, SHIFT_SOFTMAX_NORM, row_shift)
     errs.append(e)
-    r.update(exp_out=exp_out, denoms=denoms, recips=recips)
+    r.update(row_shift=rs, exp_out=exp_out, denoms=denoms, recips=recips)
     av_acc, av_q, e = ops.av(wts, v, t, t, 0, D, H, SHIFT_AV)
     errs.append(e)
     r.update(av_acc=av_acc, av_q=av_q)
@@ -100,6 +101,27 @@ def forward_layer(ops, x, w, luts, t):
     r.update(ffn_down_acc=dn_acc, ffn_down_q=dn_q, ffn_block_out=out)
     r["errors"] = errs
     return r
+
+
+def forward_model(ops, tokens, model, luts, row_shift=1):
+    """gpt2_fixed.py forward_model (688-760) from the same primitives: embed
+    (shift 0), every layer, final LN of the last row, its logits against the
+    tied wte.  `model` is a volta_zk_b200.gpt2.Gpt2Model."""
+    t = len(tokens)
+    vocab = model.wte.shape[0]
+    acc, x, e = ops.embed(tokens, model.wte, model.wpe, t, D, vocab, model.wpe.shape[0], 0, 0)
+    out = {"embed_out": x, "errors": [e], "layers": []}
+    for lw in model.layers:
+        r = forward_layer(ops, x, lw, luts, t, row_shift)
+        out["layers"].append(r)
+        out["errors"] += r["errors"]
+        x = r["ffn_block_out"]
+    fin = ops.layer_norm(np.ascontiguousarray(x[-D:]), model.lnf_gain, model.lnf_bias, luts["ln_rsqrt"], 1, D,
+                         LN_VAR_SHIFT, SHIFT_LN_NORM)
+    out["errors"].append(fin[6])
+    out["final_ln_out"] = fin[5]
+    out["logits"] = ops.logits(fin[5], model.wte, 1, D, vocab)
+    return out
 
 
 class OracleOps:
@@ -126,6 +148,12 @@ class OracleOps:
 
     def lookup(self, x, lut):
         return self.o.fixed_lookup(x, lut)
+
+    def embed(self, tokens, wte, wpe, rows, d, vocab, positions, pos0, shift):
+        return self.o.fixed_embed(tokens, wte, wpe, rows, d, vocab, positions, pos0, shift)
+
+    def logits(self, x, w, rows, d, vocab):
+        return self.o.fixed_logits(x, w, rows, d, vocab)
 
 
 def check_against_golden(result):

@@ -1,0 +1,96 @@
+"""GPT-2 small synthetic model (config 0/3): the package's input synthesis
+and the oracle's whole-model forward against the reference's own NumPy
+mirror (scripts/gpt2_fixed.py forward_model), through the digests that
+tests/golden/make_model_golden.py recorded from it."""
+
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+from tests.fixed_layer import OracleOps, forward_model
+
+GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+LAYER_KEYS = ["row_shift", "ln1_out", "qkv_acc", "q", "k", "v", "scores_acc", "scores_q", "exp_out", "denoms",
+              "recips", "av_acc", "av_q", "proj_acc", "attn_proj_q", "attn_block_out", "ln2_out", "ffn_up_acc",
+              "ffn_up_q", "gelu_out", "ffn_down_acc", "ffn_down_q", "ffn_block_out"]
+DTYPES = {"row_shift": np.int64, "denoms": np.int64, "recips": np.int16, "logits": np.int64}
+
+
+def digest(a) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def golden(t):
+    return np.load(os.path.join(GOLDEN_DIR, f"gpt2_model_t{t}.npz"))
+
+
+def mismatches(g, embed_out, layers, final_ln_out, logits):
+    """Names whose digest differs from the fixture.  `layers` maps a layer
+    index to a callable name -> array (int64 accumulators, int16 wires)."""
+    bad = []
+    if digest(np.asarray(embed_out, np.int16)) != str(g["embed_out"]):
+        bad.append("embed_out")
+    n_layers = sum(1 for k in g.files if k.endswith("_ffn_block_out"))
+    for layer in range(n_layers):
+        keys = LAYER_KEYS if f"l{layer}_ln1_out" in g.files else ["attn_block_out", "ffn_block_out"]
+        for k in keys:
+            a = layers(layer, k)
+            dt = DTYPES.get(k, np.int64 if k.endswith("_acc") else np.int16)
+            if digest(np.asarray(a).astype(dt)) != str(g[f"l{layer}_{k}"]):
+                bad.append(f"l{layer}_{k}")
+    if digest(np.asarray(final_ln_out, np.int16)) != str(g["final_ln_out"]):
+        bad.append("final_ln_out")
+    if digest(np.asarray(logits, np.int64)) != str(g["logits"]):
+        bad.append("logits")
+    return bad
+
+
+@pytest.fixture(scope="module")
+def model():
+    from volta_zk_b200 import gpt2
+
+    return gpt2.synthetic_model()
+
+
+def test_synthetic_model_matches_reference_generators(model, package_built):
+    from volta_zk_b200 import gpt2
+
+    g = golden(16)
+    cat = np.concatenate([np.concatenate([lw[k].ravel() for k in ("c_attn", "attn_proj", "ffn_up", "ffn_down",
+                                                                   "ln1_gain", "ln1_bias", "ln2_gain", "ln2_bias")])
+                          for lw in model.layers])
+    assert digest(cat) == str(g["weights_digest"])
+    assert digest(model.wte) == str(g["wte_digest"])
+    assert digest(model.wpe) == str(g["wpe_digest"])
+    assert digest(gpt2.prefill_tokens(16)) == str(g["tokens_digest"])
+    assert digest(gpt2.prefill_tokens(1024)) == str(golden(1024)["tokens_digest"])
+
+
+def test_luts_match_reference_tables():
+    from volta_zk_b200 import gpt2
+
+    fx = np.load(os.path.join(GOLDEN_DIR, "fixed_layer_t8.npz"))
+    luts = gpt2.build_luts()
+    for k in ("exp", "gelu", "ln_rsqrt", "softmax_recip"):
+        assert np.array_equal(luts[k], fx[k]), k
+
+
+def test_reference_needs_the_stable_softmax_at_1024():
+    """The recorded mirror run at T = 1024 is strict-clean with the P5 stable
+    softmax; with LutParams::default the reference stops there (layer.rs:782)."""
+    g = golden(1024)
+    assert bool(g["strict_ok"]) and bool(g["softmax_row_shift"])
+
+
+def test_oracle_forward_matches_reference_mirror_t16(oracle, model, package_built):
+    from volta_zk_b200 import gpt2
+
+    t = 16
+    tokens = gpt2.prefill_tokens(t)
+    res = forward_model(OracleOps(oracle), tokens, model, gpt2.build_luts(), row_shift=1)
+    assert all(e == 0 for e in res["errors"])
+    bad = mismatches(golden(t), res["embed_out"], lambda l, k: res["layers"][l][k], res["final_ln_out"],
+                     res["logits"])
+    assert not bad, bad

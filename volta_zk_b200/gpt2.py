@@ -1,0 +1,262 @@
+"""GPT-2 small int16 fixed-point model: synthetic weights, lookup tables and
+the whole-model device session (config 3's witness forward).
+
+Input synthesis restates the reference's generators:
+  * synthetic_model (rust/volta-gpt2/src/model.rs:504-600): layer l's weights
+    from synthetic_weights_for_config(seed + l * 0x9E3779B9)
+    (layer.rs:283-309, one splitmix64 stream per layer: c_attn, attn_proj,
+    ffn_up, ffn_down, ln1/ln2 gains, ln1/ln2 biases), zero GEMM biases, wte
+    then wpe from one LCG, final LN gain 64 / bias 0, tied output;
+  * build_luts (rust/volta-gpt2/src/luts.rs:133-173, mirrored by
+    scripts/gpt2_fixed.py:112-166): the exp, gelu, ln_rsqrt and
+    softmax_recip tables, f64 math with round-half-away-from-zero.
+The session runs the forward on the device (libvolta_accel.so
+vzh_gpt2_*, over the seam's volta_cuda_fixed_*_device entry points).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+VOCAB, POSITIONS, D, HEADS, HEAD_DIM, DFF, LAYERS = 50257, 1024, 768, 12, 64, 3072, 12
+TOKEN_SEED = bytes([0x70] * 32)
+MODEL_SEED = 0x1234
+TABLE_LEN = 1 << 16
+I16_MIN, I16_MAX = -32768, 32767
+
+
+@dataclass
+class LutParams:
+    """luts.rs LutParams::default, with the P5 stable softmax switch."""
+    ln_var_shift: int = 7
+    ln_rsqrt_log2: int = 18
+    shift_ln_norm: int = 16
+    exp_in_log2: int = 10
+    exp_out_log2: int = 12
+    recip_den_shift: int = 6
+    recip_log2: int = 26
+    gelu_scale_log2: int = 10
+    shift_qkv: int = 10
+    shift_scores: int = 10
+    shift_softmax_norm: int = 14
+    shift_av: int = 12
+    shift_attn_proj: int = 10
+    shift_ffn_up: int = 10
+    shift_ffn_down: int = 10
+    softmax_row_shift: bool = True
+    shift_embed: int = 0
+
+
+def _round_away(v: float) -> int:
+    """f64::round (half away from zero)."""
+    return math.floor(v + 0.5) if v >= 0 else math.ceil(v - 0.5)
+
+
+def build_luts(p: LutParams | None = None) -> dict:
+    """The four int16 tables of luts.rs build_luts (65536 entries each; exp
+    and gelu indexed by the i16 input's u16 bit pattern)."""
+    p = p or LutParams()
+    exp_in, exp_out, gelu_s = float(1 << p.exp_in_log2), float(1 << p.exp_out_log2), float(1 << p.gelu_scale_log2)
+    exp_tab = np.zeros(TABLE_LEN, dtype=np.int16)
+    gelu_tab = np.zeros(TABLE_LEN, dtype=np.int16)
+    rsqrt_tab = np.zeros(TABLE_LEN, dtype=np.int16)
+    recip_tab = np.zeros(TABLE_LEN, dtype=np.int16)
+    for u in range(TABLE_LEN):
+        x = u - 65536 if u >= 32768 else u
+        exp_tab[u] = min(_round_away(exp_out * (2.0 ** (x / exp_in))), I16_MAX)
+        xr = x / gelu_s
+        g = 0.5 * xr * (1.0 + math.tanh(0.7978845608028654 * (xr + 0.044715 * xr * xr * xr)))
+        gelu_tab[u] = max(I16_MIN, min(I16_MAX, _round_away(g * gelu_s)))
+        s = math.isqrt((u + 1) << p.ln_var_shift)
+        rsqrt_tab[u] = min(((1 << p.ln_rsqrt_log2) + s // 2) // s, I16_MAX)
+        den = (u << p.recip_den_shift) + (1 << (p.recip_den_shift - 1))
+        recip_tab[u] = min(((1 << p.recip_log2) + den // 2) // den, I16_MAX)
+    return {"exp": exp_tab, "gelu": gelu_tab, "ln_rsqrt": rsqrt_tab, "softmax_recip": recip_tab}
+
+
+_U64 = np.uint64
+
+
+def splitmix64_stream(seed: int, n: int, start: int = 0) -> np.ndarray:
+    """Outputs start..start+n of splitmix64 from `seed` (state +=
+    0x9E3779B97F4A7C15, then the xor-shift-multiply finaliser), vectorised."""
+    with np.errstate(over="ignore"):
+        idx = np.arange(start + 1, start + n + 1, dtype=_U64)
+        z = _U64(seed & 0xFFFFFFFFFFFFFFFF) + idx * _U64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> _U64(30))) * _U64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> _U64(27))) * _U64(0x94D049BB133111EB)
+        return z ^ (z >> _U64(31))
+
+
+def lcg_values(state: int, n: int, radius: int):
+    """n draws of x <- x * 6364136223846793005 + 1442695040888963407 (mod 2^64)
+    mapped to x mod (2r+1) - r; returns (values, state after the last draw).
+    Vectorised through the closed form x_k = a^k x_0 + c (1 + a + ... +
+    a^(k-1)), whose powers and sums numpy accumulates mod 2^64."""
+    a, c = _U64(6364136223846793005), _U64(1442695040888963407)
+    with np.errstate(over="ignore"):
+        ak = np.cumprod(np.full(n, a, dtype=_U64), dtype=_U64)       # a^1 .. a^n
+        geo = np.empty(n, dtype=_U64)                                 # 1 + a + ... + a^(k-1)
+        geo[0] = _U64(1)
+        if n > 1:
+            geo[1:] = ak[:-1]
+        geo = np.cumsum(geo, dtype=_U64)
+        x = ak * _U64(state & 0xFFFFFFFFFFFFFFFF) + c * geo
+    vals = (x % _U64(2 * radius + 1)).astype(np.int64) - radius
+    return vals.astype(np.int16), int(x[-1])
+
+
+@dataclass
+class Gpt2Model:
+    layers: list = field(default_factory=list)   # dicts of int16 arrays (k x n GEMM weights)
+    wte: np.ndarray = None
+    wpe: np.ndarray = None
+    lnf_gain: np.ndarray = None
+    lnf_bias: np.ndarray = None
+
+
+def synthetic_layer_weights(seed: int) -> dict:
+    """layer.rs synthetic_weights_for_config for GPT-2 small shapes."""
+    sizes = [D * 3 * D, D * D, D * DFF, DFF * D]
+    shapes = [(D, 3 * D), (D, D), (D, DFF), (DFF, D)]
+    pos, mats = 0, []
+    for n, shp in zip(sizes, shapes):
+        mats.append(((splitmix64_stream(seed, n, pos) % _U64(127)).astype(np.int64) - 63).astype(np.int16)
+                    .reshape(shp))
+        pos += n
+    vec = []
+    for mod, off in ((33, 48), (33, 48), (256, -128), (256, -128)):
+        vec.append(((splitmix64_stream(seed, D, pos) % _U64(mod)).astype(np.int64) + off).astype(np.int16))
+        pos += D
+    return dict(c_attn=mats[0], attn_proj=mats[1], ffn_up=mats[2], ffn_down=mats[3], ln1_gain=vec[0],
+                ln2_gain=vec[1], ln1_bias=vec[2], ln2_bias=vec[3])
+
+
+def synthetic_model(seed: int = MODEL_SEED, n_layers: int = LAYERS) -> Gpt2Model:
+    layers = [synthetic_layer_weights((seed + l * 0x9E3779B9) & 0xFFFFFFFFFFFFFFFF) for l in range(n_layers)]
+    wte, state = lcg_values(seed ^ 0xD1B54A32D192ED03, VOCAB * D, 15)
+    wpe, _ = lcg_values(state, POSITIONS * D, 7)
+    return Gpt2Model(layers=layers, wte=wte.reshape(VOCAB, D), wpe=wpe.reshape(POSITIONS, D),
+                     lnf_gain=np.full(D, 64, dtype=np.int16), lnf_bias=np.zeros(D, dtype=np.int16))
+
+
+def prefill_tokens(t: int) -> np.ndarray:
+    """FpStream::domain_separated([0x70; 32], 0).next_fp() mod 50257, t ids (u32)."""
+    from .accel import fpstream_fp_rows
+
+    return (fpstream_fp_rows(TOKEN_SEED, 0, t) % _U64(VOCAB)).astype(np.uint32)
+
+
+# wire names, in the order of gpt2.hpp's Gpt2Wire
+WIRES = ["x_in", "ln1_mean", "ln1_var", "ln1_rsqrt_in", "ln1_rsqrt_out", "ln1_acc", "ln1_out", "qkv_acc", "qkv_q",
+         "q", "k", "v", "scores_acc", "scores_q", "row_shift", "exp_out", "denoms", "recips", "weights", "av_acc",
+         "av_q", "proj_acc", "attn_proj_q", "attn_block_out", "ln2_mean", "ln2_var", "ln2_rsqrt_in", "ln2_rsqrt_out",
+         "ln2_acc", "ln2_out", "ffn_up_acc", "ffn_up_q", "gelu_out", "ffn_down_acc", "ffn_down_q", "ffn_block_out",
+         "error"]
+
+
+def wire_dtype_count(name: str, t: int):
+    td, n, ht = t * D, HEADS * (t * (t + 1) // 2), HEADS * t
+    i16, i64 = np.int16, np.int64
+    table = {"ln1_mean": (i64, t), "ln1_var": (i64, t), "ln1_rsqrt_in": (i64, t), "ln1_rsqrt_out": (i16, t),
+             "ln2_mean": (i64, t), "ln2_var": (i64, t), "ln2_rsqrt_in": (i64, t), "ln2_rsqrt_out": (i16, t),
+             "ln1_acc": (i64, td), "ln2_acc": (i64, td), "av_acc": (i64, td), "proj_acc": (i64, td),
+             "ffn_down_acc": (i64, td), "qkv_acc": (i64, 3 * td), "qkv_q": (i16, 3 * td), "scores_acc": (i64, n),
+             "scores_q": (i16, n), "exp_out": (i16, n), "weights": (i16, n), "row_shift": (i16, ht),
+             "recips": (i16, ht), "denoms": (i64, ht), "ffn_up_acc": (i64, t * DFF), "ffn_up_q": (i16, t * DFF),
+             "gelu_out": (i16, t * DFF), "error": (np.uint32, 1)}
+    return table.get(name, (i16, td))
+
+
+class Gpt2Session:
+    """The whole model resident on one device context (weights uploaded
+    once); forward() enqueues embed -> 12 layers -> final LN -> logits."""
+
+    def __init__(self, prover, model: Gpt2Model, t: int, luts: dict | None = None, params: LutParams | None = None):
+        from . import accel
+
+        self.prover, self.be, self.t = prover, prover.backend, t
+        self.params = params or LutParams()
+        self.luts = luts or build_luts(self.params)
+        self.host = accel.load_host_library()
+        L = self.host
+        L.vzh_gpt2_open.restype = C.c_void_p
+        L.vzh_gpt2_open.argtypes = [C.c_void_p] + [C.c_void_p] * 10 + [C.c_char_p, C.c_size_t]
+        L.vzh_gpt2_close.argtypes = [C.c_void_p]
+        L.vzh_gpt2_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+        L.vzh_gpt2_buffer.restype = C.c_uint64
+        L.vzh_gpt2_buffer.argtypes = [C.c_void_p, C.c_size_t, C.c_int]
+        p = self.params
+        self._keep = []
+        dims = np.array([len(model.layers), D, HEADS, HEAD_DIM, DFF, VOCAB, POSITIONS, t], dtype=np.uint64)
+        shifts = np.array([p.ln_var_shift, p.shift_ln_norm, p.recip_den_shift, p.recip_log2, p.shift_qkv,
+                           p.shift_scores, p.shift_softmax_norm, p.shift_av, p.shift_attn_proj, p.shift_ffn_up,
+                           p.shift_ffn_down, p.shift_embed & 0xFFFFFFFF, int(p.softmax_row_shift)], dtype=np.uint32)
+        ptrs = []
+        for lw in model.layers:
+            for k in ("c_attn", "attn_proj", "ffn_up", "ffn_down", "ln1_gain", "ln1_bias", "ln2_gain", "ln2_bias"):
+                a = np.ascontiguousarray(lw[k], dtype=np.int16)
+                self._keep.append(a)
+                ptrs.append(a.ctypes.data)
+        wptr = (C.c_void_p * len(ptrs))(*ptrs)
+        lut_arrays = [np.ascontiguousarray(self.luts[k], dtype=np.int16)
+                      for k in ("ln_rsqrt", "exp", "softmax_recip", "gelu")]
+        lptr = (C.c_void_p * 4)(*[a.ctypes.data for a in lut_arrays])
+        llen = np.array([a.size for a in lut_arrays], dtype=np.uint64)
+        host = [np.ascontiguousarray(x, dtype=np.int16) for x in (model.wte, model.wpe, model.lnf_gain, model.lnf_bias)]
+        err = C.create_string_buffer(1024)
+        self.h = L.vzh_gpt2_open(prover.h, dims.ctypes.data, shifts.ctypes.data, C.cast(wptr, C.c_void_p),
+                                 *[x.ctypes.data for x in host], C.cast(lptr, C.c_void_p), llen.ctypes.data, err, 1024)
+        if not self.h:
+            raise accel.AccelError(err.value.decode())
+
+    def close(self):
+        if self.h:
+            self.host.vzh_gpt2_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def forward(self, tokens: np.ndarray | None = None):
+        """Enqueue the forward (tokens: t u32 ids from host memory, else the
+        resident token buffer); nothing is downloaded."""
+        from . import accel
+
+        err = C.create_string_buffer(1024)
+        ptr = None
+        if tokens is not None:
+            tokens = np.ascontiguousarray(tokens, dtype=np.uint32)
+            assert tokens.size == self.t
+            ptr = tokens.ctypes.data
+        if self.host.vzh_gpt2_forward(self.h, ptr, err, 1024) != 0:
+            raise accel.AccelError(err.value.decode())
+
+    def buffer(self, layer, which: int) -> int:
+        return int(self.host.vzh_gpt2_buffer(self.h, C.c_size_t(layer if layer is not None else 2**64 - 1), which))
+
+    def wire(self, layer: int, name: str) -> np.ndarray:
+        dtype, count = wire_dtype_count(name, self.t)
+        return self.be.download(self.buffer(layer, WIRES.index(name)), count * np.dtype(dtype).itemsize, dtype=dtype)
+
+    def logits(self) -> np.ndarray:
+        return self.be.download(self.buffer(None, 2), VOCAB * 8, dtype=np.int64)
+
+    def embed_out(self) -> np.ndarray:
+        return self.wire(0, "x_in")
+
+    def final_ln_out(self) -> np.ndarray:
+        return self.be.download(self.buffer(None, 9), D * 2, dtype=np.int16)
+
+    def error_word(self) -> int:
+        return int(self.be.download(self.buffer(None, 3), 4, dtype=np.uint32)[0])
+
+    def layer_errors(self):
+        return [int(self.wire(l, "error")[0]) for l in range(LAYERS)]

@@ -7,6 +7,7 @@
 
 #include "accel.hpp"
 #include "api.hpp"
+#include "gpt2.hpp"
 #include "protocol.hpp"
 
 using namespace vzh;
@@ -290,6 +291,90 @@ int vzh_logup_finish(const vz_fp2* parts, size_t shards, size_t words_per_shard,
 void vzh_fpstream_fp2(const uint8_t* seed, uint64_t domain, size_t n, vz_fp2* out) {
     FpStream s(seed, domain);
     for (size_t i = 0; i < n; ++i) out[i] = s.next_fp2();
+}
+
+// ---- whole-model GPT-2 session (gpt2.hpp) ----------------------------------
+// dims: layers, d, heads, head_dim, dff, vocab, positions, t.
+// shifts: ln_var, ln_norm, recip_den, recip_log2, qkv, scores, softmax_norm,
+// av, attn_proj, ffn_up, ffn_down, embed (two's complement), row_shift flag.
+// layer_weights: layers x 8 pointers (c_attn, attn_proj, ffn_up, ffn_down,
+// ln1_gain, ln1_bias, ln2_gain, ln2_bias); luts: ln_rsqrt, exp,
+// softmax_recip, gelu with their lengths.
+void* vzh_gpt2_open(void* h, const size_t* dims, const uint32_t* shifts, const int16_t* const* layer_weights,
+                    const int16_t* wte, const int16_t* wpe, const int16_t* lnf_gain, const int16_t* lnf_bias,
+                    const int16_t* const* luts, const size_t* lut_lens, char* err, size_t len) {
+    try {
+        Gpt2Shape s;
+        s.layers = dims[0];
+        s.d = dims[1];
+        s.heads = dims[2];
+        s.head_dim = dims[3];
+        s.dff = dims[4];
+        s.vocab = dims[5];
+        s.positions = dims[6];
+        s.t = dims[7];
+        Gpt2Shifts& f = s.shifts;
+        f.ln_var = shifts[0];
+        f.ln_norm = shifts[1];
+        f.recip_den = shifts[2];
+        f.recip_log2 = shifts[3];
+        f.qkv = shifts[4];
+        f.scores = shifts[5];
+        f.softmax_norm = shifts[6];
+        f.av = shifts[7];
+        f.attn_proj = shifts[8];
+        f.ffn_up = shifts[9];
+        f.ffn_down = shifts[10];
+        f.embed = static_cast<int32_t>(shifts[11]);
+        f.row_shift = shifts[12] != 0;
+        std::vector<Gpt2LayerHost> lw(s.layers);
+        for (size_t l = 0; l < s.layers; ++l) {
+            const int16_t* const* p = layer_weights + 8 * l;
+            lw[l] = Gpt2LayerHost{p[0], p[1], p[2], p[3], p[4], p[5], p[6], p[7]};
+        }
+        return new Gpt2Session(*static_cast<Backend*>(h), s, lw, wte, wpe, lnf_gain, lnf_bias,
+                               {luts[0], luts[1], luts[2], luts[3]},
+                               {lut_lens[0], lut_lens[1], lut_lens[2], lut_lens[3]});
+    } catch (const std::exception& e) {
+        fail(err, len, e.what());
+    } catch (...) {
+        fail(err, len, "unknown C++ exception");
+    }
+    return nullptr;
+}
+
+void vzh_gpt2_close(void* s) { delete static_cast<Gpt2Session*>(s); }
+
+// Enqueue the whole forward; tokens (t u32 ids) are uploaded first when given,
+// else the session's resident token buffer is used.
+int vzh_gpt2_forward(void* s, const uint32_t* tokens, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        Gpt2Session& g = *static_cast<Gpt2Session*>(s);
+        if (tokens) g.upload_tokens(tokens);
+        g.forward(g.tokens_id());
+    });
+}
+
+// Arena id of one resident buffer: wire w of layer l (w < kWireCount), or for
+// l == SIZE_MAX: 0 tokens, 1 embed acc, 2 logits, 3 error word, 4..9 final
+// LN (mean, var, rin, rout, acc, out), 10..13 luts, 14 wte.
+uint64_t vzh_gpt2_buffer(void* s, size_t layer, int which) {
+    const Gpt2Session& g = *static_cast<Gpt2Session*>(s);
+    if (layer != SIZE_MAX) {
+        if (layer >= g.shape().layers || which < 0 || which >= kWireCount) return 0;
+        return g.wire(layer, which);
+    }
+    switch (which) {
+        case 0: return g.tokens_id();
+        case 1: return g.embed_acc();
+        case 2: return g.logits();
+        case 3: return g.error_word();
+        case 14: return g.wte();
+        default:
+            if (which >= 4 && which <= 9) return g.final_ln(which - 4);
+            if (which >= 10 && which <= 13) return g.lut(which - 10);
+            return 0;
+    }
 }
 
 // The first n Fp draws (rejection-sampled next_fp) of FpStream(seed, domain):

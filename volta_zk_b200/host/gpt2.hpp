@@ -1,0 +1,107 @@
+// Whole-model int16 fixed-point GPT-2 forward (the witness of a prefill
+// proof) over the seam's resident fixed-point entry points, and the per-layer
+// proof schedule that consumes it.
+//
+//   forward   rust/volta-gpt2/src/resident.rs:1106-1300
+//             (forward_model_tokens_resident / build_resident_forward),
+//             value-for-value the reference NumPy mirror
+//             scripts/gpt2_fixed.py:427-645 forward_layer and 688-760
+//             forward_model: embed -> L x (LN1, QKV, scores, softmax, A.V,
+//             projection + residual, LN2, FFN up, GELU, FFN down + residual)
+//             -> final LN of the last position -> logits of that position.
+//   model     rust/volta-gpt2/src/model.rs:504-600 synthetic_model is built by
+//             the caller; this session only uploads the weights it is given.
+#pragma once
+
+#include <array>
+#include <cstddef>
+#include <cstdint>
+#include <vector>
+
+#include "accel.hpp"
+
+namespace vzh {
+
+// LutParams defaults (rust/volta-gpt2/src/luts.rs; gpt2_fixed.py:94-110).
+struct Gpt2Shifts {
+    uint32_t ln_var = 7, ln_norm = 16, recip_den = 6, recip_log2 = 26;
+    uint32_t qkv = 10, scores = 10, softmax_norm = 14, av = 12, attn_proj = 10, ffn_up = 10, ffn_down = 10;
+    int32_t embed = 0;
+    bool row_shift = true;  // P5 stable softmax (luts.rs:57-59); needed past T ~ 300 (u16 recip domain)
+};
+
+struct Gpt2Shape {
+    size_t layers = 12, d = 768, heads = 12, head_dim = 64, dff = 3072, vocab = 50257, positions = 1024;
+    size_t t = 0;  // tokens of the prefill this session proves
+    Gpt2Shifts shifts;
+    size_t packed() const { return heads * (t * (t + 1) / 2); }  // causal-packed attention entries
+};
+
+// Per-layer wires of the forward, kept resident for the proof (arena ids).
+enum Gpt2Wire : int {
+    kXin = 0, kLn1Mean, kLn1Var, kLn1Rin, kLn1Rout, kLn1Acc, kLn1Out, kQkvAcc, kQkvQ, kQ, kK, kV, kScoresAcc,
+    kScoresQ, kRowShift, kExpOut, kDenoms, kRecips, kWeights, kAvAcc, kAvQ, kProjAcc, kProjQ, kAttnOut, kLn2Mean,
+    kLn2Var, kLn2Rin, kLn2Rout, kLn2Acc, kLn2Out, kUpAcc, kUpQ, kGelu, kDownAcc, kDownQ, kFfnOut, kLayerError,
+    kWireCount
+};
+
+// Element size and count of one wire at this shape.
+struct WireSpec {
+    size_t elem, count;
+};
+WireSpec gpt2_wire_spec(const Gpt2Shape& s, int wire);
+
+// The weights of one layer, host side, row-major (k x n for GEMM weights).
+struct Gpt2LayerHost {
+    const int16_t *c_attn, *attn_proj, *ffn_up, *ffn_down, *ln1_gain, *ln1_bias, *ln2_gain, *ln2_bias;
+};
+
+class Gpt2Session {
+   public:
+    // Uploads every weight and the four int16 lookup tables (ln_rsqrt, exp,
+    // softmax_recip, gelu; lengths in lut_lens) once, and allocates every
+    // wire for `shape.t` tokens.
+    Gpt2Session(Backend& b, const Gpt2Shape& shape, const std::vector<Gpt2LayerHost>& layers, const int16_t* wte,
+                const int16_t* wpe, const int16_t* lnf_gain, const int16_t* lnf_bias,
+                const std::array<const int16_t*, 4>& luts, const std::array<size_t, 4>& lut_lens);
+    ~Gpt2Session();
+    Gpt2Session(const Gpt2Session&) = delete;
+    Gpt2Session& operator=(const Gpt2Session&) = delete;
+
+    // Enqueue the whole forward for the resident token ids (u32, t entries):
+    // every wire of every layer, the final LN of the last row and its logits.
+    // Nothing is downloaded and nothing waits on the device.
+    void forward(uint64_t tokens_id);
+    // Upload t token ids from host memory into the session's token buffer.
+    void upload_tokens(const uint32_t* tokens);
+    uint64_t tokens_id() const { return tokens_; }
+
+    const Gpt2Shape& shape() const { return s_; }
+    Backend& backend() { return b_; }
+    uint64_t wire(size_t layer, int w) const { return wires_[layer][w]; }
+    uint64_t weight(size_t layer, int which) const { return lw_[layer][which]; }  // 0..7 as in Gpt2LayerHost
+    uint64_t embed_acc() const { return embed_acc_; }
+    uint64_t final_ln(int which) const { return fin_[which]; }  // 0 mean 1 var 2 rin 3 rout 4 acc 5 out
+    uint64_t logits() const { return logits_; }
+    uint64_t error_word() const { return err_; }  // sticky u32 of the embed, final LN and every layer
+    uint64_t lut(int which) const { return luts_[which]; }
+    size_t lut_len(int which) const { return lut_lens_[which]; }
+    uint64_t wte() const { return wte_; }
+
+   private:
+    Backend& b_;
+    Gpt2Shape s_;
+    std::vector<std::array<uint64_t, 8>> lw_;
+    std::vector<std::array<uint64_t, kWireCount>> wires_;
+    uint64_t wte_ = 0, wpe_ = 0, lnf_gain_ = 0, lnf_bias_ = 0, tokens_ = 0, embed_acc_ = 0, logits_ = 0, err_ = 0;
+    std::array<uint64_t, 6> fin_{};
+    std::array<uint64_t, 4> luts_{};
+    std::array<size_t, 4> lut_lens_{};
+    std::vector<uint64_t> owned_;
+    uint64_t own(uint64_t id) {
+        owned_.push_back(id);
+        return id;
+    }
+};
+
+}  // namespace vzh
