@@ -88,6 +88,9 @@ void or_triple_sumcheck(ofp2* a, ofp2* b, ofp2* c, size_t n, const uint8_t chal_
 /* logup_prove (logup.rs:1760-1771) over i16 queries/table; writes the
  * proof in a flat layout: alpha, then per side root_p, root_q, then per layer
  * [rounds x (h0,h2)], p0,p1,q0,q1.  Returns number of Fp2 written. */
+size_t or_logup_prove_fp(const uint64_t* f, size_t n_f, const uint64_t* table, size_t n_t,
+                         const uint32_t* mult, const uint8_t chal_seed[32], uint64_t chal_domain,
+                         ofp2* out, size_t out_cap);
 size_t or_logup_prove(const int16_t* f, size_t n_f, const int16_t* table, size_t n_t,
                       const uint32_t* mult, const uint8_t chal_seed[32], uint64_t chal_domain,
                       ofp2* out, size_t out_cap);

@@ -111,6 +111,8 @@ def _declare(L):
     L.or_triple_sumcheck.argtypes = [_vp, _vp, _vp, _sz, C.c_char_p, _vp, _vp]
     L.or_logup_prove.restype = _sz
     L.or_logup_prove.argtypes = [_vp, _sz, _vp, _sz, _vp, C.c_char_p, _u64, _vp, _sz]
+    L.or_logup_prove_fp.restype = _sz
+    L.or_logup_prove_fp.argtypes = [_vp, _sz, _vp, _sz, _vp, C.c_char_p, _u64, _vp, _sz]
     L.or_ntt_batch.argtypes = [_vp, _sz, _sz, _sz, _vp]
     L.or_ntt_fp2_batch.argtypes = [_vp, _sz, _sz, _sz, _vp]
     L.or_blake3.argtypes = [_vp, _sz, _vp]
@@ -322,6 +324,19 @@ def logup_prove(f: np.ndarray, table: np.ndarray, mult: np.ndarray, chal_seed: b
     out = fp2_array(cap)
     w = lib().or_logup_prove(_p(f), f.size, _p(table), table.size, _p(mult), chal_seed,
                              chal_domain, _p(out), cap)
+    assert w == cap, (w, cap)
+    return out
+
+
+def logup_prove_fp(f: np.ndarray, table: np.ndarray, mult: np.ndarray, chal_seed: bytes, chal_domain: int):
+    """logup_prove over canonical Fp query and table columns (u64 < p)."""
+    f = np.ascontiguousarray(f, dtype=np.uint64)
+    table = np.ascontiguousarray(table, dtype=np.uint64)
+    mult = np.ascontiguousarray(mult, dtype=np.uint32)
+    cap = logup_prove_words(f.size, table.size)
+    out = fp2_array(cap)
+    w = lib().or_logup_prove_fp(_p(f), f.size, _p(table), table.size, _p(mult), chal_seed,
+                                chal_domain & 0xFFFFFFFFFFFFFFFF, _p(out), cap)
     assert w == cap, (w, cap)
     return out
 

@@ -426,3 +426,25 @@ size_t or_logup_prove(const int16_t* f, size_t n_f, const int16_t* table, size_t
     free(a);
     return w;
 }
+
+/* The same proof over canonical Fp query and table columns (packed pair
+ * values in + 2^k out, range remainders): logup.rs:1760-1771 with the
+ * columns already embedded in Fp (rust/volta-proto/src/block_proof.rs
+ * range_table / pair_table, range_cols_padded / pair_cols_padded). */
+size_t or_logup_prove_fp(const uint64_t* f, size_t n_f, const uint64_t* table, size_t n_t,
+                         const uint32_t* mult, const uint8_t chal_seed[32], uint64_t chal_domain,
+                         ofp2* out, size_t out_cap) {
+    (void)out_cap;
+    or_stream chal;
+    or_stream_init(&chal, chal_seed, chal_domain);
+    ofp2 alpha = or_stream_next_fp2(&chal);
+    size_t w = 0;
+    out[w++] = alpha;
+    uint64_t* a = (uint64_t*)malloc(sizeof(uint64_t) * (n_f > n_t ? n_f : n_t));
+    for (size_t i = 0; i < n_f; ++i) a[i] = or_fp_sub(alpha.c0, f[i]);
+    w += prove_frac_tree(a, NULL, n_f, alpha.c1, &chal, out + w);
+    for (size_t i = 0; i < n_t; ++i) a[i] = or_fp_sub(alpha.c0, table[i]);
+    w += prove_frac_tree(a, mult, n_t, alpha.c1, &chal, out + w);
+    free(a);
+    return w;
+}

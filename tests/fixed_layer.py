@@ -66,13 +66,14 @@ def forward_layer(ops, x, w, luts, t, row_shift=0):
     gemm, qkv_split, scores, softmax, av, lookup with the oracle's
     signatures.  row_shift = 1 selects the P5 stable softmax.  Returns
     {name: array} with the reference's names."""
-    r = {}
+    r = {"x_in": x}
     ln1 = ops.layer_norm(x, w["ln1_gain"], w["ln1_bias"], luts["ln_rsqrt"], t, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
-    r.update(ln1_mean=ln1[0], ln1_var=ln1[1], ln1_rsqrt_in=ln1[2], ln1_rsqrt_out=ln1[3], ln1_out=ln1[5])
+    r.update(ln1_mean=ln1[0], ln1_var=ln1[1], ln1_rsqrt_in=ln1[2], ln1_rsqrt_out=ln1[3], ln1_acc=ln1[4],
+             ln1_out=ln1[5])
     errs = [ln1[6]]
     qkv_acc, qkv_q, _, e = ops.gemm(ln1[5], w["c_attn"], None, None, t, D, 3 * D, SHIFT_QKV)
     errs.append(e)
-    r["qkv_acc"] = qkv_acc
+    r.update(qkv_acc=qkv_acc, qkv_q=qkv_q)
     q, k, v = ops.qkv_split(qkv_q, t, D)
     r.update(q=q, k=k, v=v)
     s_acc, s_q, e = ops.scores(q, k, t, t, 0, H, DH, SHIFT_SCORES)
@@ -81,7 +82,7 @@ def forward_layer(ops, x, w, luts, t, row_shift=0):
     rs, exp_out, denoms, recips, wts, e = ops.softmax(s_q, luts["exp"], luts["softmax_recip"], t, 0, H,
                                                       RECIP_DEN_SHIFT, RECIP_LOG2, SHIFT_SOFTMAX_NORM, row_shift)
     errs.append(e)
-    r.update(row_shift=rs, exp_out=exp_out, denoms=denoms, recips=recips)
+    r.update(row_shift=rs, exp_out=exp_out, denoms=denoms, recips=recips, weights=wts)
     av_acc, av_q, e = ops.av(wts, v, t, t, 0, D, H, SHIFT_AV)
     errs.append(e)
     r.update(av_acc=av_acc, av_q=av_q)
@@ -90,7 +91,8 @@ def forward_layer(ops, x, w, luts, t, row_shift=0):
     r.update(proj_acc=proj_acc, attn_proj_q=proj_q, attn_block_out=attn_out)
     ln2 = ops.layer_norm(attn_out, w["ln2_gain"], w["ln2_bias"], luts["ln_rsqrt"], t, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
     errs.append(ln2[6])
-    r.update(ln2_mean=ln2[0], ln2_var=ln2[1], ln2_rsqrt_in=ln2[2], ln2_rsqrt_out=ln2[3], ln2_out=ln2[5])
+    r.update(ln2_mean=ln2[0], ln2_var=ln2[1], ln2_rsqrt_in=ln2[2], ln2_rsqrt_out=ln2[3], ln2_acc=ln2[4],
+             ln2_out=ln2[5])
     up_acc, up_q, _, e = ops.gemm(ln2[5], w["ffn_up"], None, None, t, D, DFF, SHIFT_FFN_UP)
     errs.append(e)
     r.update(ffn_up_acc=up_acc, ffn_up_q=up_q)

@@ -1,0 +1,301 @@
+"""CPU composition of the GPT-2 prefill proof schedule (the checker of
+libvolta_accel.so's Gpt2Prover, volta_zk_b200/host/gpt2_proof.cpp) from the
+oracle's restated primitives: LogUp over Fp columns (logup.rs:1760-1771),
+the clear product and triple-product sumchecks (sumcheck_clear.rs:23-70,
+hadamard.rs:222-240), matrix folds and eq tables (mle.rs:7-30), ChaCha8
+VOLE-MAC masks (corr.rs:234-255) and the Ligero commitment
+(ligero.rs:465-505, ntt.rs, merkle.rs).  The lookup columns restate
+block_proof.rs range_cols_padded / range_mult / pair_cols_padded /
+pair_table (2359-2520) in numpy.
+
+Test infrastructure only.
+"""
+
+import numpy as np
+
+P = 0xFFFFFFFF00000001
+HEAD_PAD = 16
+RECIP_BITS = 18
+RECIP_PAD_INPUT = 256
+PCS_ROWS, PCS_COL_BITS, PCS_PAD, PCS_CODE_BITS = 8192, 14, 512, 15
+SITES = dict(down_range=1, gelu=2, up_range=3, ln2_norm=4, ln2_rsqrt=5, proj_range=6, av_range=7, norm_range=8,
+             exp=9, recip=10, scores_range=11, qkv_range=12, ln1_norm=13, ln1_rsqrt=14, gemm_down=16, gemm_up=17,
+             ln2_had=18, gemm_proj=19, av=20, norm_had=21, qk=22, gemm_qkv=23, ln1_had=24)
+
+
+def site_domain(layer, site):
+    return 0x7000000000000000 | (layer << 16) | (SITES[site] << 8)
+
+
+def pow2(n):
+    p = 1
+    while p < n:
+        p <<= 1
+    return p
+
+
+def emb(v):
+    v = np.asarray(v).astype(np.int64)
+    return np.where(v >= 0, v.astype(np.uint64), np.uint64(P) - (-v).astype(np.uint64)).astype(np.uint64)
+
+
+def fp_sub(a, b):
+    """(a - b) mod p for canonical u64 arrays."""
+    return np.where(a >= b, a - b, a + (np.uint64(P) - b)).astype(np.uint64)
+
+
+def pack_pair(inp, out, k):
+    """Canonical Fp of in + 2^k out for small signed integers (exact in int64)."""
+    return emb(np.asarray(inp, np.int64) + (np.asarray(out, np.int64) << k))
+
+
+def fp2_mul(a, b):
+    a0, a1, b0, b1 = (int(x) for x in (a[0], a[1], b[0], b[1]))
+    return ((a0 * b0 + 7 * a1 * b1) % P, (a0 * b1 + a1 * b0) % P)
+
+
+def lift(col):
+    x = np.zeros((col.size, 2), dtype=np.uint64)
+    x[:, 0] = col
+    return x
+
+
+class Schedule:
+    def __init__(self, o, luts, t):
+        self.o, self.luts, self.t = o, luts, t
+        self.tp = pow2(t)
+        self.rect = HEAD_PAD * self.tp * self.tp
+        exp = luts["exp"]
+        assert exp[0x8000] == 0
+        u = np.arange(1 << 16)
+        self.gap_exp = np.where(u <= 0x8000, exp[((-u) & 0xFFFF)], 0).astype(np.int64)
+        r = np.arange(1 << RECIP_BITS, dtype=np.int64)
+        den = (r << 6) + 32
+        hi = np.minimum(((1 << 26) + den // 2) // den, 32767)
+        self.recip18 = np.where(r < (1 << 16), luts["softmax_recip"][np.minimum(r, 65535)], hi).astype(np.int64)
+
+    # ---- lookup instances -------------------------------------------------
+    def logup(self, f, table, mult, seed, layer, site):
+        return self.o.logup_prove_fp(f, table, mult, seed, site_domain(layer, site))
+
+    def range_site(self, acc, out, rows, cols, row_pad, col_pad, shift, seed, layer, site):
+        half = 1 << (shift - 1)
+        acc = np.asarray(acc, np.int64).reshape(rows, cols)
+        out = np.asarray(out, np.int64).reshape(rows, cols)
+        rem = np.full((row_pad, col_pad), half, dtype=np.int64)
+        rem[:rows, :cols] = acc + half - (out << shift)
+        assert rem.min() >= 0 and rem.max() < (1 << shift)
+        rem = rem.reshape(-1)
+        mult = np.bincount(rem, minlength=1 << shift).astype(np.uint32)
+        return self.logup(rem.astype(np.uint64), np.arange(1 << shift, dtype=np.uint64), mult, seed, layer, site)
+
+    def pair_site(self, inp, out, rows, cols, row_pad, col_pad, pad_in, pad_out, lut, signed, seed, layer, site):
+        ic = np.full((row_pad, col_pad), pad_in, dtype=np.int64)
+        oc = np.full((row_pad, col_pad), pad_out, dtype=np.int64)
+        ic[:rows, :cols] = np.asarray(inp, np.int64).reshape(rows, cols)
+        oc[:rows, :cols] = np.asarray(out, np.int64).reshape(rows, cols)
+        ic, oc = ic.reshape(-1), oc.reshape(-1)
+        f = pack_pair(ic, oc, 16)
+        idx = (ic & 0xFFFF) if signed else ic
+        mult = np.bincount(idx, minlength=1 << 16).astype(np.uint32)
+        u = np.arange(1 << 16, dtype=np.int64)
+        tin = u.astype(np.uint16).view(np.int16).astype(np.int64) if signed else u
+        table = pack_pair(tin, lut, 16)
+        return self.logup(f, table, mult, seed, layer, site)
+
+    # ---- sumchecks ------------------------------------------------------------
+    def product(self, a, b, tx):
+        o = self.o
+        n = a.shape[0]
+        k = n.bit_length() - 1
+        r = [tx.next_fp2() for _ in range(k)]
+        words = []
+        for j in range(k):
+            words.append(o.product_round(a, b, a.shape[0] // 2))
+            a = o.fold_rows(a, 1, a.shape[0], r[j])
+            b = o.fold_rows(b, 1, b.shape[0], r[j])
+        words.append(np.concatenate([a, b]))
+        return np.concatenate(words)
+
+    def triple(self, a, b, c, tx):
+        o = self.o
+        n = a.shape[0]
+        k = n.bit_length() - 1
+        r = [tx.next_fp2() for _ in range(k)]
+        words = []
+        for j in range(k):
+            words.append(o.triple_product_round(a, b, c, a.shape[0] // 2))
+            a, b, c = (o.fold_rows(x, 1, x.shape[0], r[j]) for x in (a, b, c))
+        words.append(np.concatenate([a, b, c]))
+        return np.concatenate(words)
+
+    def eq(self, pt):
+        pts = np.array(pt, dtype=np.uint64).reshape(-1, 2)
+        return self.o.eq_rows(np.ascontiguousarray(pts), 1, len(pt)) if len(pt) else np.array([[1, 0]], np.uint64)
+
+    def gemm(self, x, w, acc, m, k, n, seed, layer, site):
+        o = self.o
+        tx = o.FpStream(seed, site_domain(layer, site))
+        m_pad, n_pad, k_pad = pow2(m), pow2(n), pow2(k)
+        rj = [tx.next_fp2() for _ in range(n_pad.bit_length() - 1)]
+        ri = [tx.next_fp2() for _ in range(m_pad.bit_length() - 1)]
+        eq_j, eq_i = self.eq(rj), self.eq(ri)
+        acc_r = o.matrix_fold(np.ascontiguousarray(acc, np.int64).reshape(-1), eq_i, m, n, 0, n, n_pad, 1, 0)
+        claim = (0, 0)
+        for j in range(n_pad):
+            t = fp2_mul(acc_r[j], eq_j[j])
+            claim = ((claim[0] + t[0]) % P, (claim[1] + t[1]) % P)
+        a = o.matrix_fold(np.ascontiguousarray(x, np.int16).reshape(-1), eq_i, m, k, 0, k, k_pad, 0, 0)
+        b = o.matrix_fold(np.ascontiguousarray(w, np.int16).reshape(-1), eq_j, k, n, 0, n, k_pad, 0, 1)
+        return np.concatenate([np.array([claim], np.uint64), self.product(a, b, tx)])
+
+    def ln_product(self, x, mean, rout, gain, seed, layer, site):
+        t, tp, d = self.t, self.tp, 768
+        tx = self.o.FpStream(seed, site_domain(layer, site))
+        dp = 1024
+        xx = np.zeros((tp, dp), np.int64)
+        xx[:t, :d] = np.asarray(x, np.int64).reshape(t, d)
+        cen = np.zeros((tp, dp), np.int64)
+        cen[:t] = xx[:t] - np.asarray(mean, np.int64)[:, None]
+        rs = np.zeros(tp, np.int64)
+        rs[:t] = np.asarray(rout, np.int64)
+        g = np.zeros(dp, np.int64)
+        g[:d] = np.asarray(gain, np.int64)
+        return self.product(lift(emb(cen.reshape(-1))), lift(emb((rs[:, None] * g[None, :]).reshape(-1))), tx)
+
+    # ---- one layer --------------------------------------------------------------
+    def layer(self, r, lw, seed, layer):
+        """The words of one layer from the forward's wires r (forward_layer names)."""
+        t, tp, rect = self.t, self.tp, self.rect
+        d, dff, h = 768, 3072, 12
+        lut = self.luts
+        words = []
+        words.append(self.range_site(r["ffn_down_acc"], r["ffn_down_q"], t, d, tp, 1024, 10, seed, layer, "down_range"))
+        words.append(self.pair_site(r["ffn_up_q"], r["gelu_out"], t, dff, tp, 4096, 0, int(lut["gelu"][0]),
+                                    lut["gelu"], True, seed, layer, "gelu"))
+        words.append(self.range_site(r["ffn_up_acc"], r["ffn_up_q"], t, dff, tp, 4096, 10, seed, layer, "up_range"))
+        words.append(self.range_site(r["ln2_acc"], r["ln2_out"], t, d, tp, 1024, 16, seed, layer, "ln2_norm"))
+        words.append(self.pair_site(r["ln2_rsqrt_in"], r["ln2_rsqrt_out"], 1, t, 1, tp, 0, int(lut["ln_rsqrt"][0]),
+                                    lut["ln_rsqrt"], False, seed, layer, "ln2_rsqrt"))
+        words.append(self.range_site(r["proj_acc"], r["attn_proj_q"], t, d, tp, 1024, 10, seed, layer, "proj_range"))
+        words.append(self.range_site(r["av_acc"], r["av_q"], t, d, tp, 1024, 12, seed, layer, "av_range"))
+        # softmax columns over the padded packed rectangle
+        packed = h * t * (t + 1) // 2
+        rs = np.asarray(r["row_shift"], np.int64).reshape(h, t)
+        rc = np.asarray(r["recips"], np.int64).reshape(h, t)
+        heads = np.repeat(np.arange(h), t * (t + 1) // 2)
+        rows = np.concatenate([np.repeat(np.arange(t), np.arange(1, t + 1))] * h)
+        sq = np.asarray(r["scores_q"], np.int64)
+        ex = np.asarray(r["exp_out"], np.int64)
+        wt = np.asarray(r["weights"], np.int64)
+        gap = np.zeros(rect, np.int64)
+        gap[:packed] = rs[heads, rows] - sq
+        exc = np.full(rect, self.gap_exp[0], np.int64)
+        exc[:packed] = ex
+        rem = np.full(rect, 1 << 13, np.int64)
+        rem[:packed] = ex * rc[heads, rows] + (1 << 13) - (wt << 14)
+        rcc = np.zeros(rect, np.int64)
+        rcc[:packed] = rc[heads, rows]
+        mask = np.zeros(rect, np.uint64)
+        mask[:packed] = 1
+        assert gap.min() >= 0 and gap.max() < 65536 and rem.min() >= 0 and rem.max() < (1 << 14)
+        words.append(self.logup(rem.astype(np.uint64), np.arange(1 << 14, dtype=np.uint64),
+                                np.bincount(rem, minlength=1 << 14).astype(np.uint32), seed, layer, "norm_range"))
+        u = np.arange(1 << 16, dtype=np.int64)
+        words.append(self.logup(pack_pair(gap, exc, 16), pack_pair(u, self.gap_exp, 16),
+                                np.bincount(gap, minlength=1 << 16).astype(np.uint32), seed, layer, "exp"))
+        rin = np.full((HEAD_PAD, tp), RECIP_PAD_INPUT, np.int64)
+        rout = np.full((HEAD_PAD, tp), self.recip18[RECIP_PAD_INPUT], np.int64)
+        rin[:h, :t] = np.asarray(r["denoms"], np.int64).reshape(h, t) >> 6
+        rout[:h, :t] = rc
+        rin, rout = rin.reshape(-1), rout.reshape(-1)
+        v = np.arange(1 << RECIP_BITS, dtype=np.int64)
+        words.append(self.logup(pack_pair(rin, rout, RECIP_BITS), pack_pair(v, self.recip18, RECIP_BITS),
+                                np.bincount(rin, minlength=1 << RECIP_BITS).astype(np.uint32), seed, layer, "recip"))
+        words.append(self.range_site(r["scores_acc"], r["scores_q"], 1, packed, 1, rect, 10, seed, layer,
+                                     "scores_range"))
+        words.append(self.range_site(r["qkv_acc"], np.asarray(r["qkv_q"]), t, 3 * d, tp, 4096, 10, seed, layer,
+                                     "qkv_range"))
+        words.append(self.range_site(r["ln1_acc"], r["ln1_out"], t, d, tp, 1024, 16, seed, layer, "ln1_norm"))
+        words.append(self.pair_site(r["ln1_rsqrt_in"], r["ln1_rsqrt_out"], 1, t, 1, tp, 0, int(lut["ln_rsqrt"][0]),
+                                    lut["ln_rsqrt"], False, seed, layer, "ln1_rsqrt"))
+        # sumchecks
+        o = self.o
+        words.append(self.gemm(r["gelu_out"], lw["ffn_down"], r["ffn_down_acc"], t, dff, d, seed, layer, "gemm_down"))
+        words.append(self.gemm(r["ln2_out"], lw["ffn_up"], r["ffn_up_acc"], t, d, dff, seed, layer, "gemm_up"))
+        words.append(self.ln_product(r["attn_block_out"], r["ln2_mean"], r["ln2_rsqrt_out"], lw["ln2_gain"], seed, layer,
+                                     "ln2_had"))
+        words.append(self.gemm(r["av_q"], lw["attn_proj"], r["proj_acc"], t, d, d, seed, layer, "gemm_proj"))
+        tx = o.FpStream(seed, site_domain(layer, "av"))
+        rcp = [tx.next_fp2() for _ in range(6)]
+        rh = [tx.next_fp2() for _ in range(4)]
+        ri = [tx.next_fp2() for _ in range(tp.bit_length() - 1)]
+        eq_c, eq_h, eq_i = self.eq(rcp), self.eq(rh), self.eq(ri)
+        A = np.zeros((HEAD_PAD * tp, 2), np.uint64)
+        B = np.zeros((HEAD_PAD * tp, 2), np.uint64)
+        C = np.zeros((HEAD_PAD * tp, 2), np.uint64)
+        per_head = t * (t + 1) // 2
+        vv = np.asarray(r["v"], np.int64).reshape(t, d)
+        for hh in range(HEAD_PAD):
+            C[hh * tp:(hh + 1) * tp] = eq_h[hh]
+            if hh >= h:
+                continue
+            wh = wt[hh * per_head:(hh + 1) * per_head]
+            for j in range(t):
+                ia = np.arange(j, t)
+                A[hh * tp + j] = _dot_base(eq_i[ia], wh[ia * (ia + 1) // 2 + j])
+                B[hh * tp + j] = _dot_base(eq_c[:64], vv[j, hh * 64:(hh + 1) * 64])
+        words.append(self.triple(A, B, C, tx))
+        tx = o.FpStream(seed, site_domain(layer, "norm_had"))
+        words.append(self.triple(lift(emb(exc)), lift(emb(rcc)), lift(mask), tx))
+        tx = o.FpStream(seed, site_domain(layer, "qk"))
+        rj = [tx.next_fp2() for _ in range(tp.bit_length() - 1)]
+        ri = [tx.next_fp2() for _ in range(tp.bit_length() - 1)]
+        rh = [tx.next_fp2() for _ in range(4)]
+        eq_i, eq_j, eq_h = self.eq(ri), self.eq(rj), self.eq(rh)
+        qr = o.matrix_fold(np.ascontiguousarray(r["q"], np.int16).reshape(-1), eq_i, t, d, 0, d, 1024, 0, 0)
+        kr = o.matrix_fold(np.ascontiguousarray(r["k"], np.int16).reshape(-1), eq_j, t, d, 0, d, 1024, 0, 0)
+        cc = np.ascontiguousarray(eq_h[np.arange(1024) // 64])
+        words.append(self.triple(qr, kr, cc, tx))
+        words.append(self.gemm(r["ln1_out"], lw["c_attn"], r["qkv_acc"], t, d, 3 * d, seed, layer, "gemm_qkv"))
+        words.append(self.ln_product(r["x_in"], r["ln1_mean"], r["ln1_rsqrt_out"], lw["ln1_gain"], seed, layer,
+                                     "ln1_had"))
+        return np.concatenate([np.asarray(w, np.uint64).reshape(-1, 2) for w in words])
+
+    def corrections(self, r, mac_seed, layer):
+        out = []
+        for w, name in enumerate(("x_in", "k", "v", "attn_block_out", "ffn_block_out")):
+            masks = self.o.chacha_fp_rows(mac_seed, (layer * 8 + w) << 32, self.t, 768).reshape(-1)
+            out.append(fp_sub(emb(np.asarray(r[name]).reshape(-1)), masks))
+        return out
+
+
+def _dot_base(eqs, vals):
+    s0 = s1 = 0
+    for e, v in zip(eqs, vals):
+        v = int(v) % P
+        if v:
+            s0 += int(e[0]) * v
+            s1 += int(e[1]) * v
+    return (s0 % P, s1 % P)
+
+
+def pcs_root(o, model, pad_seed):
+    """The weight commitment: every layer's weights, then wte, wpe, final LN,
+    row-major into 8192 rows of 2^14 int16, 512 ChaCha8 pads per row, RS code
+    2^15, BLAKE3 column tree."""
+    cols, code_len = 1 << PCS_COL_BITS, 1 << PCS_CODE_BITS
+    parts = []
+    for lw in model.layers:
+        parts += [lw[k].reshape(-1) for k in ("c_attn", "attn_proj", "ffn_up", "ffn_down", "ln1_gain", "ln1_bias",
+                                              "ln2_gain", "ln2_bias")]
+    parts += [model.wte.reshape(-1), model.wpe.reshape(-1), model.lnf_gain, model.lnf_bias]
+    flat = np.concatenate(parts).astype(np.int16)
+    w = np.zeros(PCS_ROWS * cols, np.int16)
+    w[:flat.size] = flat
+    pads = o.chacha_fp_rows(pad_seed, 0, PCS_ROWS, PCS_PAD)
+    msgs = o.pcs_messages(w, np.ascontiguousarray(pads), PCS_ROWS, cols, PCS_PAD, code_len)
+    code = o.ntt_batch(msgs.reshape(PCS_ROWS, code_len)[:, :cols + PCS_PAD].copy(), PCS_ROWS, cols + PCS_PAD,
+                       code_len)
+    tree = o.merkle_tree(o.hash_fp_columns(code, PCS_ROWS, code_len))
+    return bytes(tree[-1])

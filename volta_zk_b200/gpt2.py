@@ -260,3 +260,58 @@ class Gpt2Session:
 
     def layer_errors(self):
         return [int(self.wire(l, "error")[0]) for l in range(LAYERS)]
+
+
+class Gpt2Prover:
+    """The prefill proof schedule over a Gpt2Session's witness
+    (libvolta_accel.so vzh_gpt2_prove; volta_zk_b200/host/gpt2_proof.cpp)."""
+
+    def __init__(self, session: Gpt2Session):
+        from . import accel
+
+        self.s, self.host = session, session.host
+        L = self.host
+        L.vzh_gpt2_prover_open.restype = C.c_void_p
+        L.vzh_gpt2_prover_open.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
+        L.vzh_gpt2_prover_close.argtypes = [C.c_void_p]
+        L.vzh_gpt2_prove.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_char_p, C.c_void_p, C.c_size_t,
+                                     C.POINTER(C.c_size_t), C.POINTER(C.c_size_t), C.c_void_p, C.c_char_p,
+                                     C.c_size_t]
+        L.vzh_gpt2_correction.restype = C.c_uint64
+        L.vzh_gpt2_correction.argtypes = [C.c_void_p, C.c_size_t, C.c_int]
+        err = C.create_string_buffer(1024)
+        self.h = L.vzh_gpt2_prover_open(session.h, err, 1024)
+        if not self.h:
+            raise accel.AccelError(err.value.decode())
+        self.cap = 1 << 22
+
+    def close(self):
+        if self.h:
+            self.host.vzh_gpt2_prover_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def prove(self, seed: bytes, mac_seed: bytes, pad_seed: bytes):
+        """Returns (words as an (n, 2) u64 array, words per layer, 32-byte PCS root)."""
+        from . import accel
+
+        out = np.zeros((self.cap, 2), dtype=np.uint64)
+        written, per_layer = C.c_size_t(0), C.c_size_t(0)
+        root = (C.c_uint8 * 32)()
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_gpt2_prove(self.h, seed, mac_seed, pad_seed, out.ctypes.data, self.cap, C.byref(written),
+                                      C.byref(per_layer), root, err, 1024)
+        if rc != 0:
+            raise accel.AccelError(err.value.decode())
+        return out[:written.value].copy(), per_layer.value, bytes(root)
+
+    def correction(self, layer: int, wire: int) -> np.ndarray:
+        """Boundary corrections x - mask of wire (0 x_in, 1 k, 2 v, 3
+        attn_block_out, 4 ffn_block_out) of `layer`, t x d u64."""
+        buf = int(self.host.vzh_gpt2_correction(self.h, layer, wire))
+        return self.s.be.download(buf, self.s.t * D * 8, dtype=np.uint64)

@@ -137,6 +137,10 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         dlsym(handle_, "volta_b200_triple_local_device"));
     ext_loaded_->triple_flush = reinterpret_cast<decltype(ext_loaded_->triple_flush)>(
         dlsym(handle_, "volta_b200_triple_flush_device"));
+    ext_loaded_->softmax_lookup_columns = reinterpret_cast<decltype(ext_loaded_->softmax_lookup_columns)>(
+        dlsym(handle_, "volta_b200_softmax_lookup_columns_device"));
+    ext_loaded_->av_factors =
+        reinterpret_cast<decltype(ext_loaded_->av_factors)>(dlsym(handle_, "volta_b200_av_factors_device"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

@@ -35,6 +35,8 @@ struct ExtApi {
     decltype(&::volta_b200_logup_tree_column_device) logup_tree_column = nullptr;
     decltype(&::volta_b200_triple_local_device) triple_local = nullptr;
     decltype(&::volta_b200_triple_flush_device) triple_flush = nullptr;
+    decltype(&::volta_b200_softmax_lookup_columns_device) softmax_lookup_columns = nullptr;
+    decltype(&::volta_b200_av_factors_device) av_factors = nullptr;
 };
 
 }  // namespace vzh

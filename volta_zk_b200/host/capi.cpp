@@ -377,6 +377,50 @@ uint64_t vzh_gpt2_buffer(void* s, size_t layer, int which) {
     }
 }
 
+// The prefill proof schedule over a session's witness (gpt2_proof.cpp).
+void* vzh_gpt2_prover_open(void* session, char* err, size_t len) {
+    try {
+        return new Gpt2Prover(*static_cast<Gpt2Session*>(session));
+    } catch (const std::exception& e) {
+        fail(err, len, e.what());
+    } catch (...) {
+        fail(err, len, "unknown C++ exception");
+    }
+    return nullptr;
+}
+
+void vzh_gpt2_prover_close(void* p) { delete static_cast<Gpt2Prover*>(p); }
+
+// Prove the session's last forward.  words: every layer's words in order
+// (cap Fp2 at most; *written gets the total and *per_layer the count of
+// one layer); root: the 32-byte PCS commitment.
+int vzh_gpt2_prove(void* p, const uint8_t* seed, const uint8_t* mac_seed, const uint8_t* pad_seed, vz_fp2* words,
+                   size_t cap, size_t* written, size_t* per_layer, uint8_t* root, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        const Gpt2Proof pr = static_cast<Gpt2Prover*>(p)->prove(seed, mac_seed, pad_seed);
+        size_t total = 0;
+        for (const auto& w : pr.layer_words) total += w.size();
+        if (total > cap) throw AccelError("GPT-2 proof buffer too small");
+        size_t at = 0;
+        for (const auto& w : pr.layer_words) {
+            std::memcpy(words + at, w.data(), w.size() * sizeof(vz_fp2));
+            at += w.size();
+        }
+        *written = total;
+        *per_layer = pr.layer_words.empty() ? 0 : pr.layer_words[0].size();
+        std::memcpy(root, pr.pcs_root, 32);
+    });
+}
+
+// Arena id of the boundary corrections of wire w (0..4) of layer l.
+uint64_t vzh_gpt2_correction(void* p, size_t layer, int w) {
+    try {
+        return static_cast<Gpt2Prover*>(p)->correction(layer, w);
+    } catch (...) {
+        return 0;
+    }
+}
+
 // The first n Fp draws (rejection-sampled next_fp) of FpStream(seed, domain):
 // row `domain` of the ChaCha8 prover-secret rows (input synthesis).
 void vzh_fpstream_fp(const uint8_t* seed, uint64_t domain, size_t n, uint64_t* out) {

@@ -65,7 +65,10 @@ Gpt2Session::Gpt2Session(Backend& b, const Gpt2Shape& shape, const std::vector<G
         wpe_ = up(wpe, s_.positions * d);
         lnf_gain_ = up(lnf_gain, d);
         lnf_bias_ = up(lnf_bias, d);
-        for (int k = 0; k < 4; ++k) luts_[k] = up(luts[k], lut_lens[k]);
+        for (int k = 0; k < 4; ++k) {
+            luts_[k] = up(luts[k], lut_lens[k]);
+            luts_host_[k].assign(luts[k], luts[k] + lut_lens[k]);
+        }
         tokens_ = own(b_.alloc(s_.t * sizeof(uint32_t)));
         embed_acc_ = own(b_.alloc(s_.t * d * sizeof(int64_t)));
         wires_.resize(s_.layers);

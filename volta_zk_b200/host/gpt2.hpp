@@ -16,6 +16,8 @@
 #include <array>
 #include <cstddef>
 #include <cstdint>
+#include <map>
+#include <memory>
 #include <vector>
 
 #include "accel.hpp"
@@ -86,7 +88,10 @@ class Gpt2Session {
     uint64_t error_word() const { return err_; }  // sticky u32 of the embed, final LN and every layer
     uint64_t lut(int which) const { return luts_[which]; }
     size_t lut_len(int which) const { return lut_lens_[which]; }
+    const std::vector<int16_t>& lut_host(int which) const { return luts_host_[which]; }
     uint64_t wte() const { return wte_; }
+    uint64_t wpe() const { return wpe_; }
+    uint64_t lnf(int which) const { return which ? lnf_bias_ : lnf_gain_; }
 
    private:
     Backend& b_;
@@ -97,7 +102,73 @@ class Gpt2Session {
     std::array<uint64_t, 6> fin_{};
     std::array<uint64_t, 4> luts_{};
     std::array<size_t, 4> lut_lens_{};
+    std::array<std::vector<int16_t>, 4> luts_host_;
     std::vector<uint64_t> owned_;
+    uint64_t own(uint64_t id) {
+        owned_.push_back(id);
+        return id;
+    }
+};
+
+// ---- the prefill proof schedule (gpt2_proof.cpp) -----------------------------
+
+// Sub-proof sites of one layer, in proof order; each draws from its own
+// private transcript FpStream(seed, gpt2_site_domain(layer, site)).
+enum Gpt2Site : int {
+    kSiteDownRange = 1, kSiteGelu, kSiteUpRange, kSiteLn2Norm, kSiteLn2Rsqrt, kSiteProjRange, kSiteAvRange,
+    kSiteNormRange, kSiteExp, kSiteRecip, kSiteScoresRange, kSiteQkvRange, kSiteLn1Norm, kSiteLn1Rsqrt,
+    kSiteGemmDown = 16, kSiteGemmUp, kSiteLn2Had, kSiteGemmProj, kSiteAv, kSiteNormHad, kSiteQk, kSiteGemmQkv,
+    kSiteLn1Had
+};
+uint64_t gpt2_site_domain(size_t layer, int site);
+
+struct Gpt2Proof {
+    std::vector<std::vector<Fp2>> layer_words;  // per layer, the sub-proofs' words in site order
+    uint8_t pcs_root[32];
+};
+
+struct Owned;
+struct PendingLogup;
+
+class Gpt2Prover {
+   public:
+    // Ligero shape of the weight commitment (GPT2_FULL, ligero.rs:59-60)
+    static constexpr size_t kPcsRows = 8192, kPcsColBits = 14, kPcsPad = 512, kPcsCodeBits = 15;
+
+    // Builds the lookup tables and the committed weight matrix once.
+    explicit Gpt2Prover(Gpt2Session& s);
+    ~Gpt2Prover();
+    Gpt2Prover(const Gpt2Prover&) = delete;
+    Gpt2Prover& operator=(const Gpt2Prover&) = delete;
+
+    // Prove the witness of the session's last forward.  seed: the
+    // sub-proofs' transcripts; mac_seed: the VOLE-MAC mask stream; pad_seed:
+    // the PCS row pads.  The boundary corrections stay resident
+    // (correction()).
+    Gpt2Proof prove(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32]);
+    // Corrections x - mask of boundary wire w (0 x_in, 1 k, 2 v, 3
+    // attn_block_out, 4 ffn_block_out) of layer l: t x d u64.
+    uint64_t correction(size_t layer, int w) const { return corrections_.at(layer).at(w); }
+
+   private:
+    struct Slot {
+        PendingLogup* logup = nullptr;  // a LogUp instance, else `words` message slots at msgs
+        uint64_t msgs = 0;
+        size_t words = 0;
+        size_t at = 0;  // offset of its raw messages in the layer's buffer
+    };
+    std::vector<Slot> enqueue_layer(size_t l, Owned& own, const uint8_t seed[32], const uint8_t mac_seed[32]);
+
+    Gpt2Session& s_;
+    Backend& b_;
+    size_t t_pad_ = 0, rect_ = 0;
+    std::map<uint32_t, uint64_t> range_;
+    uint64_t gelu_pairs_ = 0, rsqrt_pairs_ = 0, expgap_pairs_ = 0, recip_pairs_ = 0, shifts_ = 0;
+    uint64_t exp_pad_out_ = 0, recip_pad_out_ = 0;
+    uint64_t wmat_ = 0, pads_ = 0, code_ = 0, tree_ = 0, err_ = 0;
+    std::vector<uint64_t> owned_;
+    std::vector<std::vector<uint64_t>> corrections_;
+    std::vector<std::vector<std::unique_ptr<PendingLogup>>> pending_logups_;
     uint64_t own(uint64_t id) {
         owned_.push_back(id);
         return id;

@@ -95,6 +95,8 @@ PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mu
 // one-CTA jobs.
 void launch_side_work(Backend& b, const std::vector<PendingSide*>& sides);
 LocalSide frac_side_collect(Backend& b, const PendingSide& ps);
+// The same from the side's raw message slots already on the host.
+LocalSide frac_side_parse(const PendingSide& ps, const Fp2* raw);
 // Both sides of a (sharded) LogUp proof: the words of vzh_logup_local.
 struct PendingLogup {
     Fp2 alpha;
@@ -104,6 +106,10 @@ struct PendingLogup {
 PendingLogup logup_local_enqueue(Backend& b, Owned& own, uint64_t f_col, size_t n_f_local, uint64_t t_col,
                                  size_t n_t_local, uint64_t mult, size_t shard_bits, FpStream& chal);
 std::vector<Fp2> logup_local_collect(Backend& b, const PendingLogup& pl);
+// The proof words of a whole (unsharded) LogUp proof from both sides' raw
+// message slots on the host (raw0: the query side, raw1: the table side):
+// alpha, then per side its root and round messages, as logup_prove_resident.
+void logup_proof_words(const PendingLogup& pl, const Fp2* raw0, const Fp2* raw1, std::vector<Fp2>& out);
 // The whole LogUp proof (both sides' batches sharing launches, one download
 // per side after everything is enqueued); words as logup_prove_resident.
 std::vector<Fp2> logup_prove_scheduled(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col, size_t n_t,

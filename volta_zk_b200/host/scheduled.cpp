@@ -584,16 +584,20 @@ void launch_side_work(Backend& b, const std::vector<PendingSide*>& sides) {
 }
 
 LocalSide frac_side_collect(Backend& b, const PendingSide& ps) {
-    LocalSide out;
-    out.shard_bits = ps.shard_bits;
     std::vector<Fp2> m(ps.msg_total);
     b.download(ps.msgs, 0, m.data(), ps.msg_total * sizeof(Fp2));
+    return frac_side_parse(ps, m.data());
+}
+
+LocalSide frac_side_parse(const PendingSide& ps, const Fp2* m) {
+    LocalSide out;
+    out.shard_bits = ps.shard_bits;
     out.root_p = m[0];
     out.root_q = m[1];
     for (size_t l = ps.shard_bits; l < ps.depth; ++l) {
         const size_t L = l - ps.shard_bits;
-        out.accs.emplace_back(m.begin() + ps.moff[l], m.begin() + ps.moff[l] + 4 * L);
-        out.leftover.emplace_back(m.begin() + ps.moff[l] + 4 * L, m.begin() + ps.moff[l] + 4 * L + 4);
+        out.accs.emplace_back(m + ps.moff[l], m + ps.moff[l] + 4 * L);
+        out.leftover.emplace_back(m + ps.moff[l] + 4 * L, m + ps.moff[l] + 4 * L + 4);
     }
     return out;
 }
@@ -667,6 +671,12 @@ static void append_side_proof(const SideSchedule& sch, const LocalSide& loc, std
         }
         for (int k = 0; k < 4; ++k) proof.push_back(loc.leftover[l][k]);
     }
+}
+
+void logup_proof_words(const PendingLogup& pl, const Fp2* raw0, const Fp2* raw1, std::vector<Fp2>& out) {
+    out.push_back(pl.alpha);
+    append_side_proof(pl.sch[0], frac_side_parse(pl.side[0], raw0), out);
+    append_side_proof(pl.sch[1], frac_side_parse(pl.side[1], raw1), out);
 }
 
 std::vector<Fp2> logup_prove_scheduled(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col, size_t n_t,
