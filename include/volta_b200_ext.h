@@ -305,43 +305,43 @@ int volta_b200_embed_i16_device(void* ctx, uint64_t in_id, size_t in_offset, uin
  * Softmax witness columns of the GPT-2 layer proof, from the forward's
  * causal-packed wires (scores_q, exp_out, weights: heads * rows(rows+1)/2
  * int16; row_shift, recips: heads * rows int16; denoms: heads * rows int64).
- * Writes five u64 columns of n_pad >= packed entries each at cols: the score
- * gap c_row - s (the ExpGap lookup input, rust/volta-gpt2/src/luts.rs:
- * 188-206), the exp value (Fp), the softmax-norm requant remainder
- * exp*rc + 2^(s-1) - w*2^s (Range(s) lookup, s = norm_shift), the row's
- * reciprocal (Fp) and a 0/1 real-entry mask; entries past the packed length
- * hold the pads (0, exp_pad, 2^(s-1), 0, 0).  At recip_cols, two columns of
- * h_pad * t_pad entries (index head * t_pad + row): the reciprocal lookup
- * pair (denom >> recip_den_shift, rc) over the 18-bit reciprocal domain
- * (luts.rs:208-226), (recip_pad_in, recip_pad_out) outside the real heads
- * and rows.  An out-of-domain gap, remainder or reciprocal input sets
- * *error to 1.  Replaces the host-side column builders of the reference's
- * softmax sites (rust/volta-proto/src/block_proof.rs: build_attn_wires,
- * prove_range_site, c62_softmax_recip_wires).
+ * Writes u64 columns of n_pad >= packed entries into the buffers out_ids[0..4]
+ * (offset 0): [0] the score gap c_row - s followed by the exp value (2 x
+ * n_pad: the ExpGap lookup pair, rust/volta-gpt2/src/luts.rs:188-206), [1]
+ * the exp value (Fp) again, [2] the softmax-norm requant remainder
+ * exp*rc + 2^(s-1) - w*2^s (Range(s) lookup, s = norm_shift), [3] the row's
+ * reciprocal (Fp), [4] a 0/1 real-entry mask; entries past the packed length
+ * hold the pads (gap 0, exp_pad, 2^(s-1), 0, 0).  At recip_cols, two
+ * columns of h_pad * t_pad entries (index head * t_pad + row): the
+ * reciprocal lookup pair (denom >> recip_den_shift, rc) over the 18-bit
+ * reciprocal domain (luts.rs:208-226), (recip_pad_in, recip_pad_out)
+ * outside the real heads and rows.  An out-of-domain gap, remainder or
+ * reciprocal input sets *error to 1.  Replaces the host-side column builders
+ * of the reference's softmax sites (rust/volta-proto/src/block_proof.rs:
+ * build_attn_wires, prove_range_site, c62_softmax_recip_wires).
  */
 int volta_b200_softmax_lookup_columns_device(void* ctx, uint64_t scores_id, size_t scores_offset,
                                             uint64_t row_shift_id, size_t row_shift_offset, uint64_t exp_id,
                                             size_t exp_offset, uint64_t denoms_id, size_t denoms_offset,
                                             uint64_t recips_id, size_t recips_offset, uint64_t weights_id,
-                                            size_t weights_offset, uint64_t cols_id, size_t cols_offset,
-                                            uint64_t recip_cols_id, size_t recip_cols_offset, uint64_t error_id,
-                                            size_t error_offset, size_t rows, size_t heads, size_t n_pad,
-                                            size_t h_pad, size_t t_pad, uint64_t exp_pad, uint32_t norm_shift,
-                                            uint32_t recip_den_shift, uint64_t recip_pad_in,
-                                            uint64_t recip_pad_out);
+                                            size_t weights_offset, const uint64_t* out_ids, uint64_t recip_cols_id,
+                                            size_t recip_cols_offset, uint64_t error_id, size_t error_offset,
+                                            size_t rows, size_t heads, size_t n_pad, size_t h_pad, size_t t_pad,
+                                            uint64_t exp_pad, uint32_t norm_shift, uint32_t recip_den_shift,
+                                            uint64_t recip_pad_in, uint64_t recip_pad_out);
 
 /*
  * Factors of the A.V contraction sumcheck (the attention-value GEMM of
  * rust/volta-proto/src/block_proof.rs prove_attn_block): over index
  * h * t_pad + j, A = sum_i eq_rows[i] w[h,i,j] (causal-packed weights),
  * B = sum_c eq_dim[c] v[j, h*head_dim + c] (v: rows x heads*head_dim int16),
- * C = eq_head[h]; three Fp2 vectors of h_pad * t_pad entries at out (A, B,
- * C), zero past the real heads and rows.
+ * C = eq_head[h]; three Fp2 vectors of h_pad * t_pad entries into the buffers
+ * out_ids[0..2] (offset 0), zero past the real heads and rows.
  */
 int volta_b200_av_factors_device(void* ctx, uint64_t weights_id, size_t weights_offset, uint64_t v_id,
                                 size_t v_offset, uint64_t eq_rows_id, size_t eq_rows_offset, uint64_t eq_dim_id,
-                                size_t eq_dim_offset, uint64_t eq_head_id, size_t eq_head_offset, uint64_t out_id,
-                                size_t out_offset, size_t rows, size_t heads, size_t head_dim, size_t h_pad,
+                                size_t eq_dim_offset, uint64_t eq_head_id, size_t eq_head_offset,
+                                const uint64_t* out_ids, size_t rows, size_t heads, size_t head_dim, size_t h_pad,
                                 size_t t_pad);
 
 #ifdef __cplusplus

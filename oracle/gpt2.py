@@ -1,17 +1,130 @@
-"""CPU composition of the GPT-2 prefill proof schedule (the checker of
-libvolta_accel.so's Gpt2Prover, volta_zk_b200/host/gpt2_proof.cpp) from the
-oracle's restated primitives: LogUp over Fp columns (logup.rs:1760-1771),
-the clear product and triple-product sumchecks (sumcheck_clear.rs:23-70,
-hadamard.rs:222-240), matrix folds and eq tables (mle.rs:7-30), ChaCha8
-VOLE-MAC masks (corr.rs:234-255) and the Ligero commitment
-(ligero.rs:465-505, ntt.rs, merkle.rs).  The lookup columns restate
-block_proof.rs range_cols_padded / range_mult / pair_cols_padded /
-pair_table (2359-2520) in numpy.
+"""Oracle (test infrastructure only) for the GPT-2 small prefill path.
 
-Test infrastructure only.
+Whole-model forward: forward_layer / forward_model compose the oracle's
+fixed-point primitives (oracle/fixed.c) in the order of the reference's NumPy
+mirror scripts/gpt2_fixed.py:427-645 (forward_layer) and 688-760
+(forward_model); OracleOps binds them.
+
+Prefill proof schedule: Schedule / pcs_root compose the oracle's restated
+primitives into the checker of libvolta_accel.so's Gpt2Prover
+(volta_zk_b200/host/gpt2_proof.cpp): LogUp over Fp columns
+(logup.rs:1760-1771), the clear product and triple-product sumchecks
+(sumcheck_clear.rs:23-70, hadamard.rs:222-240), matrix folds and eq tables
+(mle.rs:7-30), ChaCha8 VOLE-MAC masks (corr.rs:234-255) and the Ligero
+commitment (ligero.rs:465-505, ntt.rs, merkle.rs); the lookup columns restate
+block_proof.rs range_cols_padded / range_mult / pair_cols_padded / pair_table
+(2359-2520) in numpy.
+
+Imported by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline and
+reference legs only, as the checker; the shipped library never imports it.
 """
 
 import numpy as np
+
+D, H, DH, DFF = 768, 12, 64, 3072
+# P4 LutParams defaults (gpt2_fixed.py LutParams / luts.rs)
+LN_VAR_SHIFT, SHIFT_LN_NORM, RECIP_DEN_SHIFT, RECIP_LOG2 = 7, 16, 6, 26
+SHIFT_QKV, SHIFT_SCORES, SHIFT_SOFTMAX_NORM, SHIFT_AV = 10, 10, 14, 12
+SHIFT_ATTN_PROJ, SHIFT_FFN_UP, SHIFT_FFN_DOWN = 10, 10, 10
+
+
+def forward_layer(ops, x, w, luts, t, row_shift=0):
+    """forward_layer from the seam primitives; `ops` provides layer_norm,
+    gemm, qkv_split, scores, softmax, av, lookup with the oracle's
+    signatures.  row_shift = 1 selects the P5 stable softmax.  Returns
+    {name: array} with the reference's names."""
+    r = {"x_in": x}
+    ln1 = ops.layer_norm(x, w["ln1_gain"], w["ln1_bias"], luts["ln_rsqrt"], t, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
+    r.update(ln1_mean=ln1[0], ln1_var=ln1[1], ln1_rsqrt_in=ln1[2], ln1_rsqrt_out=ln1[3], ln1_acc=ln1[4],
+             ln1_out=ln1[5])
+    errs = [ln1[6]]
+    qkv_acc, qkv_q, _, e = ops.gemm(ln1[5], w["c_attn"], None, None, t, D, 3 * D, SHIFT_QKV)
+    errs.append(e)
+    r.update(qkv_acc=qkv_acc, qkv_q=qkv_q)
+    q, k, v = ops.qkv_split(qkv_q, t, D)
+    r.update(q=q, k=k, v=v)
+    s_acc, s_q, e = ops.scores(q, k, t, t, 0, H, DH, SHIFT_SCORES)
+    errs.append(e)
+    r.update(scores_acc=s_acc, scores_q=s_q)
+    rs, exp_out, denoms, recips, wts, e = ops.softmax(s_q, luts["exp"], luts["softmax_recip"], t, 0, H,
+                                                      RECIP_DEN_SHIFT, RECIP_LOG2, SHIFT_SOFTMAX_NORM, row_shift)
+    errs.append(e)
+    r.update(row_shift=rs, exp_out=exp_out, denoms=denoms, recips=recips, weights=wts)
+    av_acc, av_q, e = ops.av(wts, v, t, t, 0, D, H, SHIFT_AV)
+    errs.append(e)
+    r.update(av_acc=av_acc, av_q=av_q)
+    proj_acc, proj_q, attn_out, e = ops.gemm(av_q, w["attn_proj"], None, x.reshape(-1), t, D, D, SHIFT_ATTN_PROJ)
+    errs.append(e)
+    r.update(proj_acc=proj_acc, attn_proj_q=proj_q, attn_block_out=attn_out)
+    ln2 = ops.layer_norm(attn_out, w["ln2_gain"], w["ln2_bias"], luts["ln_rsqrt"], t, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
+    errs.append(ln2[6])
+    r.update(ln2_mean=ln2[0], ln2_var=ln2[1], ln2_rsqrt_in=ln2[2], ln2_rsqrt_out=ln2[3], ln2_acc=ln2[4],
+             ln2_out=ln2[5])
+    up_acc, up_q, _, e = ops.gemm(ln2[5], w["ffn_up"], None, None, t, D, DFF, SHIFT_FFN_UP)
+    errs.append(e)
+    r.update(ffn_up_acc=up_acc, ffn_up_q=up_q)
+    gelu = ops.lookup(up_q, luts["gelu"])
+    r["gelu_out"] = gelu
+    dn_acc, dn_q, out, e = ops.gemm(gelu, w["ffn_down"], None, attn_out, t, DFF, D, SHIFT_FFN_DOWN)
+    errs.append(e)
+    r.update(ffn_down_acc=dn_acc, ffn_down_q=dn_q, ffn_block_out=out)
+    r["errors"] = errs
+    return r
+
+
+def forward_model(ops, tokens, model, luts, row_shift=1):
+    """gpt2_fixed.py forward_model (688-760) from the same primitives: embed
+    (shift 0), every layer, final LN of the last row, its logits against the
+    tied wte.  `model` is a volta_zk_b200.gpt2.Gpt2Model."""
+    t = len(tokens)
+    vocab = model.wte.shape[0]
+    acc, x, e = ops.embed(tokens, model.wte, model.wpe, t, D, vocab, model.wpe.shape[0], 0, 0)
+    out = {"embed_out": x, "errors": [e], "layers": []}
+    for lw in model.layers:
+        r = forward_layer(ops, x, lw, luts, t, row_shift)
+        out["layers"].append(r)
+        out["errors"] += r["errors"]
+        x = r["ffn_block_out"]
+    fin = ops.layer_norm(np.ascontiguousarray(x[-D:]), model.lnf_gain, model.lnf_bias, luts["ln_rsqrt"], 1, D,
+                         LN_VAR_SHIFT, SHIFT_LN_NORM)
+    out["errors"].append(fin[6])
+    out["final_ln_out"] = fin[5]
+    out["logits"] = ops.logits(fin[5], model.wte, 1, D, vocab)
+    return out
+
+
+class OracleOps:
+    def __init__(self, o):
+        self.o = o
+
+    def layer_norm(self, *a):
+        return self.o.fixed_layer_norm(*a)
+
+    def gemm(self, *a):
+        return self.o.fixed_gemm(*a)
+
+    def qkv_split(self, *a):
+        return self.o.fixed_qkv_split(*a)
+
+    def scores(self, *a):
+        return self.o.fixed_attention_scores(*a)
+
+    def softmax(self, *a):
+        return self.o.fixed_softmax(*a)
+
+    def av(self, *a):
+        return self.o.fixed_av(*a)
+
+    def lookup(self, x, lut):
+        return self.o.fixed_lookup(x, lut)
+
+    def embed(self, tokens, wte, wpe, rows, d, vocab, positions, pos0, shift):
+        return self.o.fixed_embed(tokens, wte, wpe, rows, d, vocab, positions, pos0, shift)
+
+    def logits(self, x, w, rows, d, vocab):
+        return self.o.fixed_logits(x, w, rows, d, vocab)
+
+
 
 P = 0xFFFFFFFF00000001
 HEAD_PAD = 16

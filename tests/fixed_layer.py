@@ -1,13 +1,16 @@
 """Shared driver for the fixed-point layer parity tests: regenerates the
 synthetic layer (rust/volta-gpt2/src/layer.rs synthetic_weights /
-synthetic_input: one splitmix64 stream) and composes forward_layer
-(scripts/gpt2_fixed.py forward_layer, layer.rs) from the seam primitives of
-a backend (the CPU oracle or the device), returning every intermediate."""
+synthetic_input: one splitmix64 stream) and binds the device's seam
+primitives (DeviceOps) for the oracle's forward_layer composition
+(oracle/gpt2.py, restating scripts/gpt2_fixed.py forward_layer), which
+returns every intermediate."""
 
 import hashlib
 import os
 
 import numpy as np
+
+from oracle.gpt2 import OracleOps, forward_layer, forward_model  # noqa: F401  (the oracle's compositions)
 
 D, H, DH, DFF = 768, 12, 64, 3072
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "fixed_layer_t8.npz")
@@ -59,103 +62,6 @@ def weights_digest(w) -> str:
 
 def digest(a) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
-
-
-def forward_layer(ops, x, w, luts, t, row_shift=0):
-    """forward_layer from the seam primitives; `ops` provides layer_norm,
-    gemm, qkv_split, scores, softmax, av, lookup with the oracle's
-    signatures.  row_shift = 1 selects the P5 stable softmax.  Returns
-    {name: array} with the reference's names."""
-    r = {"x_in": x}
-    ln1 = ops.layer_norm(x, w["ln1_gain"], w["ln1_bias"], luts["ln_rsqrt"], t, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
-    r.update(ln1_mean=ln1[0], ln1_var=ln1[1], ln1_rsqrt_in=ln1[2], ln1_rsqrt_out=ln1[3], ln1_acc=ln1[4],
-             ln1_out=ln1[5])
-    errs = [ln1[6]]
-    qkv_acc, qkv_q, _, e = ops.gemm(ln1[5], w["c_attn"], None, None, t, D, 3 * D, SHIFT_QKV)
-    errs.append(e)
-    r.update(qkv_acc=qkv_acc, qkv_q=qkv_q)
-    q, k, v = ops.qkv_split(qkv_q, t, D)
-    r.update(q=q, k=k, v=v)
-    s_acc, s_q, e = ops.scores(q, k, t, t, 0, H, DH, SHIFT_SCORES)
-    errs.append(e)
-    r.update(scores_acc=s_acc, scores_q=s_q)
-    rs, exp_out, denoms, recips, wts, e = ops.softmax(s_q, luts["exp"], luts["softmax_recip"], t, 0, H,
-                                                      RECIP_DEN_SHIFT, RECIP_LOG2, SHIFT_SOFTMAX_NORM, row_shift)
-    errs.append(e)
-    r.update(row_shift=rs, exp_out=exp_out, denoms=denoms, recips=recips, weights=wts)
-    av_acc, av_q, e = ops.av(wts, v, t, t, 0, D, H, SHIFT_AV)
-    errs.append(e)
-    r.update(av_acc=av_acc, av_q=av_q)
-    proj_acc, proj_q, attn_out, e = ops.gemm(av_q, w["attn_proj"], None, x.reshape(-1), t, D, D, SHIFT_ATTN_PROJ)
-    errs.append(e)
-    r.update(proj_acc=proj_acc, attn_proj_q=proj_q, attn_block_out=attn_out)
-    ln2 = ops.layer_norm(attn_out, w["ln2_gain"], w["ln2_bias"], luts["ln_rsqrt"], t, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
-    errs.append(ln2[6])
-    r.update(ln2_mean=ln2[0], ln2_var=ln2[1], ln2_rsqrt_in=ln2[2], ln2_rsqrt_out=ln2[3], ln2_acc=ln2[4],
-             ln2_out=ln2[5])
-    up_acc, up_q, _, e = ops.gemm(ln2[5], w["ffn_up"], None, None, t, D, DFF, SHIFT_FFN_UP)
-    errs.append(e)
-    r.update(ffn_up_acc=up_acc, ffn_up_q=up_q)
-    gelu = ops.lookup(up_q, luts["gelu"])
-    r["gelu_out"] = gelu
-    dn_acc, dn_q, out, e = ops.gemm(gelu, w["ffn_down"], None, attn_out, t, DFF, D, SHIFT_FFN_DOWN)
-    errs.append(e)
-    r.update(ffn_down_acc=dn_acc, ffn_down_q=dn_q, ffn_block_out=out)
-    r["errors"] = errs
-    return r
-
-
-def forward_model(ops, tokens, model, luts, row_shift=1):
-    """gpt2_fixed.py forward_model (688-760) from the same primitives: embed
-    (shift 0), every layer, final LN of the last row, its logits against the
-    tied wte.  `model` is a volta_zk_b200.gpt2.Gpt2Model."""
-    t = len(tokens)
-    vocab = model.wte.shape[0]
-    acc, x, e = ops.embed(tokens, model.wte, model.wpe, t, D, vocab, model.wpe.shape[0], 0, 0)
-    out = {"embed_out": x, "errors": [e], "layers": []}
-    for lw in model.layers:
-        r = forward_layer(ops, x, lw, luts, t, row_shift)
-        out["layers"].append(r)
-        out["errors"] += r["errors"]
-        x = r["ffn_block_out"]
-    fin = ops.layer_norm(np.ascontiguousarray(x[-D:]), model.lnf_gain, model.lnf_bias, luts["ln_rsqrt"], 1, D,
-                         LN_VAR_SHIFT, SHIFT_LN_NORM)
-    out["errors"].append(fin[6])
-    out["final_ln_out"] = fin[5]
-    out["logits"] = ops.logits(fin[5], model.wte, 1, D, vocab)
-    return out
-
-
-class OracleOps:
-    def __init__(self, o):
-        self.o = o
-
-    def layer_norm(self, *a):
-        return self.o.fixed_layer_norm(*a)
-
-    def gemm(self, *a):
-        return self.o.fixed_gemm(*a)
-
-    def qkv_split(self, *a):
-        return self.o.fixed_qkv_split(*a)
-
-    def scores(self, *a):
-        return self.o.fixed_attention_scores(*a)
-
-    def softmax(self, *a):
-        return self.o.fixed_softmax(*a)
-
-    def av(self, *a):
-        return self.o.fixed_av(*a)
-
-    def lookup(self, x, lut):
-        return self.o.fixed_lookup(x, lut)
-
-    def embed(self, tokens, wte, wpe, rows, d, vocab, positions, pos0, shift):
-        return self.o.fixed_embed(tokens, wte, wpe, rows, d, vocab, positions, pos0, shift)
-
-    def logits(self, x, w, rows, d, vocab):
-        return self.o.fixed_logits(x, w, rows, d, vocab)
 
 
 def check_against_golden(result):

@@ -9,7 +9,7 @@ import os
 import numpy as np
 import pytest
 
-from tests.fixed_layer import OracleOps, forward_model
+from oracle.gpt2 import OracleOps, forward_model
 
 GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 LAYER_KEYS = ["row_shift", "ln1_out", "qkv_acc", "q", "k", "v", "scores_acc", "scores_q", "exp_out", "denoms",

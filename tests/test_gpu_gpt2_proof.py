@@ -1,6 +1,6 @@
 """The GPT-2 prefill proof schedule on the device (Gpt2Prover over a
 Gpt2Session's witness) against its CPU oracle composition
-(tests/gpt2_proof_oracle.py) on the same model and tokens, word for word:
+(oracle/gpt2.py) on the same model and tokens, word for word:
 every layer's 14 LogUp instances, four GEMM sumchecks, the A.V, softmax-norm
 and Q.K^T sumchecks and the two LayerNorm products; the boundary
 corrections; the weight commitment's root.  A power-of-two prefill (T = 16)
@@ -9,8 +9,7 @@ and the reference's measured prefill length (T = 100, padded to 128)."""
 import numpy as np
 import pytest
 
-from tests.fixed_layer import OracleOps, forward_model
-from tests.gpt2_proof_oracle import Schedule, pcs_root
+from oracle.gpt2 import OracleOps, Schedule, forward_model, pcs_root
 
 pytestmark = pytest.mark.gpu
 SEED, MAC_SEED, PAD_SEED = bytes([0x50] * 32), bytes([0x4D] * 32), bytes([0x11] * 32)

@@ -131,30 +131,85 @@ __global__ void pair_columns_kernel(const void* in, const void* outs, uint64_t* 
     }
 }
 
-// Multiplicity histograms with a shared-memory privatised 2^16-bin table
-// would need 256 KB; bins are privatised per warp-slice in L2 via atomics.
-__global__ void histogram_fp_kernel(const uint64_t* in, uint32_t* out, size_t n, size_t bins) {
-    VZB_GRID_LOOP(i, n) {
-        const uint64_t v = in[i];
-        if (v < bins) atomicAdd(out + v, 1u);
+// Multiplicity histograms.  Lookup columns are dominated by a few values
+// (every pad entry holds the same value, and remainders and table indices
+// cluster), so one global atomic per element serialises on the hot bins.
+// A warp whose 32 elements share one bin (a run of pads) adds them with one
+// atomic; other warps add per lane.  Tables of at most kSmemBins bins are
+// counted in a per-block shared-memory copy that is added to the global
+// table once per block (blocks are sized so that this flush stays small
+// against the column).  Each warp walks 32 consecutive elements per step.
+constexpr size_t kSmemBins = 16384;  // 64 KB of u32 counters
+
+__device__ __forceinline__ uint32_t lut_bin(uint64_t v, int signed_input, bool& ok) {
+    ok = true;
+    if (!signed_input) {
+        ok = v < (uint64_t{1} << 16);
+        return static_cast<uint32_t>(v);
+    }
+    if (v <= 32767) return static_cast<uint32_t>(v);
+    ok = v >= kP - (uint64_t{1} << 15);
+    return static_cast<uint32_t>((uint64_t{1} << 16) - (kP - v));
+}
+
+// mode 0: bins = values below `bins`; mode 1: u16 table index (signed_input)
+template <bool kShared>
+__global__ void histogram_kernel(const uint64_t* in, uint32_t* out, size_t n, size_t bins, int mode,
+                                 int signed_input) {
+    extern __shared__ uint32_t sm_hist[];
+    if (kShared) {
+        for (size_t b = threadIdx.x; b < bins; b += blockDim.x) sm_hist[b] = 0;
+        __syncthreads();
+    }
+    uint32_t* target = kShared ? sm_hist : out;
+    const unsigned lane = threadIdx.x & 31;
+    const size_t warp = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const size_t warps = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
+    for (size_t base = warp * 32; base < n; base += warps * 32) {
+        const size_t i = base + lane;
+        bool ok = i < n;
+        uint32_t bin = 0;
+        if (ok) {
+            const uint64_t v = __ldcs(in + i);
+            if (mode == 0) {
+                ok = v < bins;
+                bin = static_cast<uint32_t>(v);
+            } else {
+                bin = lut_bin(v, signed_input, ok);
+            }
+        }
+        const uint32_t first = __shfl_sync(0xffffffffu, bin, 0);
+        if (__all_sync(0xffffffffu, ok && bin == first)) {
+            if (lane == 0) atomicAdd(target + first, 32u);
+        } else if (ok) {
+            atomicAdd(target + bin, 1u);
+        }
+    }
+    if (kShared) {
+        __syncthreads();
+        for (size_t b = threadIdx.x; b < bins; b += blockDim.x)
+            if (sm_hist[b]) atomicAdd(out + b, sm_hist[b]);
     }
 }
 
-__global__ void histogram_lut_kernel(const uint64_t* in, uint32_t* out, size_t n, int signed_input) {
-    VZB_GRID_LOOP(i, n) {
-        const uint64_t v = in[i];
-        uint32_t idx;
-        if (!signed_input) {
-            if (v >= (uint64_t{1} << 16)) continue;
-            idx = static_cast<uint32_t>(v);
-        } else if (v <= 32767) {
-            idx = static_cast<uint32_t>(v);
-        } else {
-            if (v < kP - (uint64_t{1} << 15)) continue;
-            idx = static_cast<uint32_t>((uint64_t{1} << 16) - (kP - v));
-        }
-        atomicAdd(out + idx, 1u);
+int launch_histogram(Context* c, const uint64_t* in, uint32_t* out, size_t n, size_t bins, int mode,
+                     int signed_input) {
+    if (bins <= kSmemBins) {
+        // one flush of `bins` atomics per block: at most one block per 8 x
+        // bins elements, up to two 1024-thread blocks per SM
+        const size_t want = n / (8 * bins);
+        const unsigned blocks = static_cast<unsigned>(
+            std::max<size_t>(1, std::min<size_t>(want, static_cast<size_t>(c->sm_count) * 2)));
+        const size_t smem = bins * sizeof(uint32_t);
+        if (smem > 48 * 1024)
+            VZB_CUDA(c, cudaFuncSetAttribute(histogram_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem)));
+        histogram_kernel<true><<<blocks, 1024, smem, c->stream>>>(in, out, n, bins, mode, signed_input);
+    } else {
+        histogram_kernel<false><<<grid_for(c, n, 256), 256, 0, c->stream>>>(in, out, n, bins, mode, signed_input);
     }
+    VZB_LAUNCHED(c);
+    return 0;
 }
 
 // out[i] = in[i % len] for elements of 2, 4, 8 or 16 bytes
@@ -489,9 +544,10 @@ extern "C" int volta_cuda_histogram_lut_device(void* raw, uint64_t in_id, size_t
         return -1;
     VZB_OP_BEGIN(c);
     VZB_CUDA(c, cudaMemsetAsync(out, 0, (size_t{1} << 16) * 4, c->stream));
-    histogram_lut_kernel<<<grid_for(c, n, 256), 256, 0, c->stream>>>(static_cast<const uint64_t*>(in),
-                                                                     static_cast<uint32_t*>(out), n, signed_input);
-    VZB_OP_END(c, kOpLogup);
+    if (launch_histogram(c, static_cast<const uint64_t*>(in), static_cast<uint32_t*>(out), n, size_t{1} << 16, 1,
+                         signed_input))
+        return -1;
+    VZB_OP_END_COPY(c, kOpLogup);  // launch_histogram counted the launch
 }
 
 extern "C" int volta_cuda_histogram_fp_device(void* raw, uint64_t in_id, size_t in_off, uint64_t out_id,
@@ -502,9 +558,8 @@ extern "C" int volta_cuda_histogram_fp_device(void* raw, uint64_t in_id, size_t 
     if (region_elems(c, in_id, in_off, n, 8, &in) || region_elems(c, out_id, out_off, bins, 4, &out)) return -1;
     VZB_OP_BEGIN(c);
     VZB_CUDA(c, cudaMemsetAsync(out, 0, bins * 4, c->stream));
-    histogram_fp_kernel<<<grid_for(c, n, 256), 256, 0, c->stream>>>(static_cast<const uint64_t*>(in),
-                                                                    static_cast<uint32_t*>(out), n, bins);
-    VZB_OP_END(c, kOpLogup);
+    if (launch_histogram(c, static_cast<const uint64_t*>(in), static_cast<uint32_t*>(out), n, bins, 0, 0)) return -1;
+    VZB_OP_END_COPY(c, kOpLogup);  // launch_histogram counted the launch
 }
 
 extern "C" int volta_cuda_u32_add_inplace_device(void* raw, uint64_t t_id, size_t t_off, uint64_t a_id,

@@ -28,17 +28,22 @@
 namespace vzb {
 namespace {
 
+struct SoftmaxCols {
+    uint64_t *gap, *exp_pair, *exp, *rem, *rc, *mask;  // gap and exp_pair are one 2 x n_pad buffer
+};
+
 __global__ void softmax_columns_kernel(const int16_t* scores, const int16_t* row_shift, const int16_t* exp_out,
                                        const int64_t* denoms, const int16_t* recips, const int16_t* weights,
-                                       uint64_t* cols, uint64_t* recip_cols, uint32_t* error, size_t rows,
+                                       SoftmaxCols cols, uint64_t* recip_cols, uint32_t* error, size_t rows,
                                        size_t heads, size_t packed, size_t n_pad, size_t h_pad, size_t t_pad,
                                        uint64_t exp_pad, uint32_t norm_shift, uint32_t den_shift,
                                        uint64_t recip_pad_in, uint64_t recip_pad_out) {
-    uint64_t* gap_c = cols;
-    uint64_t* exp_c = cols + n_pad;
-    uint64_t* rem_c = cols + 2 * n_pad;
-    uint64_t* rc_c = cols + 3 * n_pad;
-    uint64_t* mask_c = cols + 4 * n_pad;
+    uint64_t* gap_c = cols.gap;
+    uint64_t* exp_c = cols.exp;
+    uint64_t* exp_pair_c = cols.exp_pair;
+    uint64_t* rem_c = cols.rem;
+    uint64_t* rc_c = cols.rc;
+    uint64_t* mask_c = cols.mask;
     const size_t warp = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const size_t warps = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -65,6 +70,7 @@ __global__ void softmax_columns_kernel(const int16_t* scores, const int16_t* row
             if (gap < 0 || gap > 0xFFFF || rem < 0 || rem >= (int64_t{1} << norm_shift)) bad = true;
             gap_c[e] = static_cast<uint64_t>(gap & 0xFFFF);
             exp_c[e] = ffrom_i64(ex);
+            exp_pair_c[e] = ffrom_i64(ex);
             rem_c[e] = static_cast<uint64_t>(rem & ((int64_t{1} << norm_shift) - 1));
             rc_c[e] = ffrom_i64(rc);
             mask_c[e] = 1;
@@ -75,6 +81,7 @@ __global__ void softmax_columns_kernel(const int16_t* scores, const int16_t* row
          e += static_cast<size_t>(gridDim.x) * blockDim.x) {
         gap_c[e] = 0;
         exp_c[e] = exp_pad;
+        exp_pair_c[e] = exp_pad;
         rem_c[e] = static_cast<uint64_t>(half);
         rc_c[e] = 0;
         mask_c[e] = 0;
@@ -90,32 +97,44 @@ __global__ void softmax_columns_kernel(const int16_t* scores, const int16_t* row
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(error, 1u);
 }
 
-__global__ void av_factors_kernel(const int16_t* weights, const int16_t* v, const Fp2* eq_i, const Fp2* eq_c,
-                                  const Fp2* eq_h, Fp2* out, size_t rows, size_t heads, size_t head_dim,
-                                  size_t h_pad, size_t t_pad) {
-    const size_t total = h_pad * t_pad;
+// One block per (head, tile of 32 key positions): lane j of each of the 8
+// warps takes key position j0 + lane, and the warps split the query rows
+// i >= j (row i's 32 entries are contiguous in the packed layout); the
+// partial sums meet in shared memory.  B and C come from warp 0.
+__global__ void __launch_bounds__(256) av_factors_kernel(const int16_t* weights, const int16_t* v,
+                                                         const Fp2* eq_i, const Fp2* eq_c, const Fp2* eq_h,
+                                                         Fp2* out_a, Fp2* out_b, Fp2* out_c, size_t rows,
+                                                         size_t heads, size_t head_dim, size_t h_pad,
+                                                         size_t t_pad) {
+    __shared__ Fp2 part[8][32];
+    const size_t tiles = (t_pad + 31) / 32;
+    const size_t h = blockIdx.x / tiles, j = (blockIdx.x % tiles) * 32 + (threadIdx.x & 31);
+    const unsigned w = threadIdx.x >> 5;
     const size_t per_head = rows * (rows + 1) / 2;
-    const size_t d = heads * head_dim;
-    for (size_t z = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; z < total;
-         z += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const size_t h = z / t_pad, j = z - h * t_pad;
-        Fp2 a{0, 0}, b{0, 0};
+    Fp2 a{0, 0};
+    if (h < heads && j < rows) {
+        const int16_t* wh = weights + h * per_head;
+        for (size_t i = j + w; i < rows; i += 8) {
+            const int16_t x = wh[i * (i + 1) / 2 + j];
+            if (x) a = f2add(a, f2mul_base(ldg2(eq_i + i), ffrom_i64(x)));
+        }
+    }
+    part[w][threadIdx.x & 31] = a;
+    __syncthreads();
+    if (w == 0 && j < t_pad) {
+        for (int k = 1; k < 8; ++k) a = f2add(a, part[k][threadIdx.x]);
+        Fp2 b{0, 0};
         if (h < heads && j < rows) {
-            // consecutive threads take consecutive j: row i's entries j are contiguous
-            const int16_t* wh = weights + h * per_head;
-            for (size_t i = j; i < rows; ++i) {
-                const int16_t w = wh[i * (i + 1) / 2 + j];
-                if (w) a = f2add(a, f2mul_base(ldg2(eq_i + i), ffrom_i64(w)));
-            }
-            const int16_t* vr = v + j * d + h * head_dim;
+            const int16_t* vr = v + j * heads * head_dim + h * head_dim;
             for (size_t c = 0; c < head_dim; ++c) {
                 const int16_t x = vr[c];
                 if (x) b = f2add(b, f2mul_base(ldg2(eq_c + c), ffrom_i64(x)));
             }
         }
-        st2(out + z, a);
-        st2(out + total + z, b);
-        st2(out + 2 * total + z, ldg2(eq_h + h));
+        const size_t z = h * t_pad + j;
+        st2(out_a + z, a);
+        st2(out_b + z, b);
+        st2(out_c + z, ldg2(eq_h + h));
     }
 }
 
@@ -127,33 +146,43 @@ using namespace vzb;
 extern "C" int volta_b200_softmax_lookup_columns_device(
     void* raw, uint64_t scores_id, size_t scores_offset, uint64_t row_shift_id, size_t row_shift_offset,
     uint64_t exp_id, size_t exp_offset, uint64_t denoms_id, size_t denoms_offset, uint64_t recips_id,
-    size_t recips_offset, uint64_t weights_id, size_t weights_offset, uint64_t cols_id, size_t cols_offset,
+    size_t recips_offset, uint64_t weights_id, size_t weights_offset, const uint64_t* out_ids,
     uint64_t recip_cols_id, size_t recip_cols_offset, uint64_t error_id, size_t error_offset, size_t rows,
     size_t heads, size_t n_pad, size_t h_pad, size_t t_pad, uint64_t exp_pad, uint32_t norm_shift,
     uint32_t recip_den_shift, uint64_t recip_pad_in, uint64_t recip_pad_out) {
     Context* c = static_cast<Context*>(raw);
     const size_t packed = heads * (rows * (rows + 1) / 2);
-    if (!c || !rows || !heads || n_pad < packed || h_pad < heads || t_pad < rows || !norm_shift ||
+    if (!c || !out_ids || !rows || !heads || n_pad < packed || h_pad < heads || t_pad < rows || !norm_shift ||
         norm_shift > 30 || !recip_den_shift || recip_den_shift > 30)
         return fail_message(c, "invalid softmax lookup column geometry");
-    void *sc = nullptr, *rs = nullptr, *ex = nullptr, *dn = nullptr, *rc = nullptr, *w = nullptr, *cols = nullptr,
-         *rcols = nullptr, *err = nullptr;
+    void *sc = nullptr, *rs = nullptr, *ex = nullptr, *dn = nullptr, *rc = nullptr, *w = nullptr, *rcols = nullptr,
+         *err = nullptr;
+    void* outs[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
     if (region_elems(c, scores_id, scores_offset, packed, 2, &sc) ||
         region_elems(c, row_shift_id, row_shift_offset, heads * rows, 2, &rs) ||
         region_elems(c, exp_id, exp_offset, packed, 2, &ex) ||
         region_elems(c, denoms_id, denoms_offset, heads * rows, 8, &dn) ||
         region_elems(c, recips_id, recips_offset, heads * rows, 2, &rc) ||
         region_elems(c, weights_id, weights_offset, packed, 2, &w) ||
-        region_elems(c, cols_id, cols_offset, 5 * n_pad, 8, &cols) ||
+        region_elems(c, out_ids[0], 0, 2 * n_pad, 8, &outs[0]) ||
         region_elems(c, recip_cols_id, recip_cols_offset, 2 * h_pad * t_pad, 8, &rcols) ||
         region_elems(c, error_id, error_offset, 1, 4, &err))
         return -1;
+    for (int k = 1; k < 5; ++k)
+        if (region_elems(c, out_ids[k], 0, n_pad, 8, &outs[k])) return -1;
+    SoftmaxCols cols;
+    cols.gap = static_cast<uint64_t*>(outs[0]);
+    cols.exp_pair = cols.gap + n_pad;
+    cols.exp = static_cast<uint64_t*>(outs[1]);
+    cols.rem = static_cast<uint64_t*>(outs[2]);
+    cols.rc = static_cast<uint64_t*>(outs[3]);
+    cols.mask = static_cast<uint64_t*>(outs[4]);
     if (op_begin(c) || op_mark(c, 1)) return -1;
     softmax_columns_kernel<<<grid_for(c, n_pad, 256), 256, 0, c->stream>>>(
         static_cast<const int16_t*>(sc), static_cast<const int16_t*>(rs), static_cast<const int16_t*>(ex),
-        static_cast<const int64_t*>(dn), static_cast<const int16_t*>(rc), static_cast<const int16_t*>(w),
-        static_cast<uint64_t*>(cols), static_cast<uint64_t*>(rcols), static_cast<uint32_t*>(err), rows, heads,
-        packed, n_pad, h_pad, t_pad, exp_pad, norm_shift, recip_den_shift, recip_pad_in, recip_pad_out);
+        static_cast<const int64_t*>(dn), static_cast<const int16_t*>(rc), static_cast<const int16_t*>(w), cols,
+        static_cast<uint64_t*>(rcols), static_cast<uint32_t*>(err), rows, heads, packed, n_pad, h_pad, t_pad,
+        exp_pad, norm_shift, recip_den_shift, recip_pad_in, recip_pad_out);
     VZB_LAUNCHED(c);
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpLogup, 0, 0);
@@ -162,25 +191,27 @@ extern "C" int volta_b200_softmax_lookup_columns_device(
 extern "C" int volta_b200_av_factors_device(void* raw, uint64_t weights_id, size_t weights_offset, uint64_t v_id,
                                            size_t v_offset, uint64_t eq_rows_id, size_t eq_rows_offset,
                                            uint64_t eq_dim_id, size_t eq_dim_offset, uint64_t eq_head_id,
-                                           size_t eq_head_offset, uint64_t out_id, size_t out_offset, size_t rows,
-                                           size_t heads, size_t head_dim, size_t h_pad, size_t t_pad) {
+                                           size_t eq_head_offset, const uint64_t* out_ids, size_t rows, size_t heads,
+                                           size_t head_dim, size_t h_pad, size_t t_pad) {
     Context* c = static_cast<Context*>(raw);
-    if (!c || !rows || !heads || !head_dim || h_pad < heads || t_pad < rows)
+    if (!c || !out_ids || !rows || !heads || !head_dim || h_pad < heads || t_pad < rows)
         return fail_message(c, "invalid A.V factor geometry");
     const size_t packed = heads * (rows * (rows + 1) / 2);
-    void *w = nullptr, *v = nullptr, *ei = nullptr, *ec = nullptr, *eh = nullptr, *out = nullptr;
+    void *w = nullptr, *v = nullptr, *ei = nullptr, *ec = nullptr, *eh = nullptr;
+    void* outs[3] = {nullptr, nullptr, nullptr};
     if (region_elems(c, weights_id, weights_offset, packed, 2, &w) ||
         region_elems(c, v_id, v_offset, rows * heads * head_dim, 2, &v) ||
         region_elems(c, eq_rows_id, eq_rows_offset, t_pad, sizeof(Fp2), &ei) ||
         region_elems(c, eq_dim_id, eq_dim_offset, head_dim, sizeof(Fp2), &ec) ||
-        region_elems(c, eq_head_id, eq_head_offset, h_pad, sizeof(Fp2), &eh) ||
-        region_elems(c, out_id, out_offset, 3 * h_pad * t_pad, sizeof(Fp2), &out))
+        region_elems(c, eq_head_id, eq_head_offset, h_pad, sizeof(Fp2), &eh))
         return -1;
+    for (int k = 0; k < 3; ++k)
+        if (region_elems(c, out_ids[k], 0, h_pad * t_pad, sizeof(Fp2), &outs[k])) return -1;
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    av_factors_kernel<<<grid_for(c, h_pad * t_pad, 128), 128, 0, c->stream>>>(
+    av_factors_kernel<<<static_cast<unsigned>(h_pad * ((t_pad + 31) / 32)), 256, 0, c->stream>>>(
         static_cast<const int16_t*>(w), static_cast<const int16_t*>(v), static_cast<const Fp2*>(ei),
-        static_cast<const Fp2*>(ec), static_cast<const Fp2*>(eh), static_cast<Fp2*>(out), rows, heads, head_dim,
-        h_pad, t_pad);
+        static_cast<const Fp2*>(ec), static_cast<const Fp2*>(eh), static_cast<Fp2*>(outs[0]),
+        static_cast<Fp2*>(outs[1]), static_cast<Fp2*>(outs[2]), rows, heads, head_dim, h_pad, t_pad);
     VZB_LAUNCHED(c);
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpGemm, 0, 0);

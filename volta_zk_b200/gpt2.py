@@ -185,7 +185,7 @@ class Gpt2Session:
         self.host = accel.load_host_library()
         L = self.host
         L.vzh_gpt2_open.restype = C.c_void_p
-        L.vzh_gpt2_open.argtypes = [C.c_void_p] + [C.c_void_p] * 10 + [C.c_char_p, C.c_size_t]
+        L.vzh_gpt2_open.argtypes = [C.c_void_p] * 10 + [C.c_char_p, C.c_size_t]
         L.vzh_gpt2_close.argtypes = [C.c_void_p]
         L.vzh_gpt2_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
         L.vzh_gpt2_buffer.restype = C.c_uint64
@@ -277,13 +277,17 @@ class Gpt2Prover:
         L.vzh_gpt2_prove.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_char_p, C.c_void_p, C.c_size_t,
                                      C.POINTER(C.c_size_t), C.POINTER(C.c_size_t), C.c_void_p, C.c_char_p,
                                      C.c_size_t]
+        L.vzh_gpt2_prove_layers.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_char_p, C.c_size_t, C.c_size_t,
+                                            C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t),
+                                            C.POINTER(C.c_size_t), C.c_void_p, C.c_char_p, C.c_size_t]
         L.vzh_gpt2_correction.restype = C.c_uint64
         L.vzh_gpt2_correction.argtypes = [C.c_void_p, C.c_size_t, C.c_int]
         err = C.create_string_buffer(1024)
         self.h = L.vzh_gpt2_prover_open(session.h, err, 1024)
         if not self.h:
             raise accel.AccelError(err.value.decode())
-        self.cap = 1 << 22
+        self.cap = 1 << 20  # words (12 layers at T = 1024 take about 121 k)
+        self._out = np.zeros((self.cap, 2), dtype=np.uint64)
 
     def close(self):
         if self.h:
@@ -296,16 +300,21 @@ class Gpt2Prover:
     def __exit__(self, *exc):
         self.close()
 
-    def prove(self, seed: bytes, mac_seed: bytes, pad_seed: bytes):
-        """Returns (words as an (n, 2) u64 array, words per layer, 32-byte PCS root)."""
+    def prove(self, seed: bytes, mac_seed: bytes, pad_seed: bytes, first: int = 0, stride: int = 1,
+              with_pcs: bool = True):
+        """Returns (words as an (n, 2) u64 array, words per layer, 32-byte PCS
+        root).  first/stride: prove layers first, first + stride, ... only
+        (one GPU's share of a proof split by layers); with_pcs: also the
+        weight commitment (root all zero otherwise)."""
         from . import accel
 
-        out = np.zeros((self.cap, 2), dtype=np.uint64)
+        out = self._out
         written, per_layer = C.c_size_t(0), C.c_size_t(0)
         root = (C.c_uint8 * 32)()
         err = C.create_string_buffer(1024)
-        rc = self.host.vzh_gpt2_prove(self.h, seed, mac_seed, pad_seed, out.ctypes.data, self.cap, C.byref(written),
-                                      C.byref(per_layer), root, err, 1024)
+        rc = self.host.vzh_gpt2_prove_layers(self.h, seed, mac_seed, pad_seed, first, stride, int(with_pcs),
+                                             out.ctypes.data, self.cap, C.byref(written), C.byref(per_layer), root,
+                                             err, 1024)
         if rc != 0:
             raise accel.AccelError(err.value.decode())
         return out[:written.value].copy(), per_layer.value, bytes(root)

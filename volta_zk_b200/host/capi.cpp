@@ -391,13 +391,27 @@ void* vzh_gpt2_prover_open(void* session, char* err, size_t len) {
 
 void vzh_gpt2_prover_close(void* p) { delete static_cast<Gpt2Prover*>(p); }
 
+int vzh_gpt2_prove_layers(void* p, const uint8_t* seed, const uint8_t* mac_seed, const uint8_t* pad_seed,
+                          size_t first, size_t stride, int with_pcs, vz_fp2* words, size_t cap, size_t* written,
+                          size_t* per_layer, uint8_t* root, char* err, size_t len);
+
 // Prove the session's last forward.  words: every layer's words in order
 // (cap Fp2 at most; *written gets the total and *per_layer the count of
 // one layer); root: the 32-byte PCS commitment.
 int vzh_gpt2_prove(void* p, const uint8_t* seed, const uint8_t* mac_seed, const uint8_t* pad_seed, vz_fp2* words,
                    size_t cap, size_t* written, size_t* per_layer, uint8_t* root, char* err, size_t len) {
+    return vzh_gpt2_prove_layers(p, seed, mac_seed, pad_seed, 0, 1, 1, words, cap, written, per_layer, root, err,
+                                 len);
+}
+
+// Layers first, first + stride, ... only (with_pcs: also the weight
+// commitment); words of the proved layers in layer order.
+int vzh_gpt2_prove_layers(void* p, const uint8_t* seed, const uint8_t* mac_seed, const uint8_t* pad_seed,
+                          size_t first, size_t stride, int with_pcs, vz_fp2* words, size_t cap, size_t* written,
+                          size_t* per_layer, uint8_t* root, char* err, size_t len) {
     return guarded(err, len, [&] {
-        const Gpt2Proof pr = static_cast<Gpt2Prover*>(p)->prove(seed, mac_seed, pad_seed);
+        const Gpt2Proof pr =
+            static_cast<Gpt2Prover*>(p)->prove_layers(seed, mac_seed, pad_seed, first, stride, with_pcs != 0);
         size_t total = 0;
         for (const auto& w : pr.layer_words) total += w.size();
         if (total > cap) throw AccelError("GPT-2 proof buffer too small");

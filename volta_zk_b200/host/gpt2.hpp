@@ -123,8 +123,8 @@ enum Gpt2Site : int {
 uint64_t gpt2_site_domain(size_t layer, int site);
 
 struct Gpt2Proof {
-    std::vector<std::vector<Fp2>> layer_words;  // per layer, the sub-proofs' words in site order
-    uint8_t pcs_root[32];
+    std::vector<std::vector<Fp2>> layer_words;  // per proved layer, the sub-proofs' words in site order
+    uint8_t pcs_root[32] = {0};
 };
 
 struct Owned;
@@ -146,6 +146,11 @@ class Gpt2Prover {
     // the PCS row pads.  The boundary corrections stay resident
     // (correction()).
     Gpt2Proof prove(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32]);
+    // The same for layers first, first + stride, ... only (one GPU's share
+    // of a proof split by layers; the sub-proofs of different layers are
+    // independent), with the weight commitment when with_pcs.
+    Gpt2Proof prove_layers(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
+                           size_t first, size_t stride, bool with_pcs);
     // Corrections x - mask of boundary wire w (0 x_in, 1 k, 2 v, 3
     // attn_block_out, 4 ffn_block_out) of layer l: t x d u64.
     uint64_t correction(size_t layer, int w) const { return corrections_.at(layer).at(w); }
@@ -167,7 +172,7 @@ class Gpt2Prover {
     uint64_t exp_pad_out_ = 0, recip_pad_out_ = 0;
     uint64_t wmat_ = 0, pads_ = 0, code_ = 0, tree_ = 0, err_ = 0;
     std::vector<uint64_t> owned_;
-    std::vector<std::vector<uint64_t>> corrections_;
+    std::map<size_t, std::vector<uint64_t>> corrections_;  // per proved layer
     std::vector<std::vector<std::unique_ptr<PendingLogup>>> pending_logups_;
     uint64_t own(uint64_t id) {
         owned_.push_back(id);

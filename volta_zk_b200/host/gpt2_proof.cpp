@@ -183,7 +183,7 @@ Gpt2Prover::Gpt2Prover(Gpt2Session& s) : s_(s), b_(s.backend()) {
 Gpt2Prover::~Gpt2Prover() {
     for (uint64_t id : owned_) b_.api().volta_cuda_resident_free(b_.ctx(), id);
     for (const auto& l : corrections_)
-        for (uint64_t id : l) b_.api().volta_cuda_resident_free(b_.ctx(), id);
+        for (uint64_t id : l.second) b_.api().volta_cuda_resident_free(b_.ctx(), id);
 }
 
 namespace {
@@ -268,9 +268,6 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     const size_t packed = sh.packed();
     auto W = [&](int w) { return s_.wire(l, w); };
     auto alloc = [&](size_t bytes) { return own.add(b_.alloc(bytes)); };
-    auto zero = [&](uint64_t id, size_t bytes) {
-        b_.check(A.volta_cuda_resident_zero(ctx, id, 0, bytes), "resident_zero");
-    };
     std::vector<Slot> slots;
 
     // ---- boundary authentication --------------------------------------------
@@ -285,7 +282,7 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         b_.check(A.volta_cuda_subfield_corrections_device(ctx, W(boundary[w]), 0, masks, 0, corr[w], 0, t * d, 0),
                  "subfield_corrections_device");
     }
-    corrections_.push_back(corr);
+    corrections_[l] = corr;
 
     // ---- the 14 lookup instances --------------------------------------------
     std::vector<PendingSide*> sides;
@@ -309,8 +306,7 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         b_.check(A.volta_cuda_requant_columns_device(ctx, acc, 0, out, 0, cc, 0, err_, 0, rows, cols, row_pad,
                                                      col_pad, 1, shift),
                  "requant_columns_device");
-        const uint64_t mult = alloc((size_t{1} << shift) * sizeof(uint32_t));
-        zero(mult, (size_t{1} << shift) * sizeof(uint32_t));
+        const uint64_t mult = alloc((size_t{1} << shift) * sizeof(uint32_t));  // the histograms clear it
         b_.check(A.volta_cuda_histogram_fp_device(ctx, cc, 0, mult, 0, n, size_t{1} << shift),
                  "histogram_fp_device");
         add_logup(site, cc, 1, 0, n, range_.at(shift), size_t{1} << shift, mult);
@@ -325,7 +321,6 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
                                                   pad_out, in_kind, 0),
                  "pair_columns_device");
         const uint64_t mult = alloc((size_t{1} << 16) * sizeof(uint32_t));
-        zero(mult, (size_t{1} << 16) * sizeof(uint32_t));
         if (signed_in)
             b_.check(A.volta_cuda_histogram_lut_device(ctx, cc, 0, mult, 0, n, 1), "histogram_lut_device");
         else
@@ -344,33 +339,31 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     // attention chain
     range_site(kSiteProjRange, W(kProjAcc), W(kProjQ), t, d, tp, d_pad, f.attn_proj);
     range_site(kSiteAvRange, W(kAvAcc), W(kAvQ), t, d, tp, d_pad, f.av);
-    const uint64_t sm = alloc(5 * rect_ * sizeof(uint64_t));
+    // softmax columns: [0] (gap, exp) pairs, [1] exp, [2] norm remainders, [3] reciprocals, [4] mask
+    uint64_t sm[5];
+    sm[0] = alloc(2 * rect_ * sizeof(uint64_t));
+    for (int k = 1; k < 5; ++k) sm[k] = alloc(rect_ * sizeof(uint64_t));
     const uint64_t rcols = alloc(2 * kHeadPad * tp * sizeof(uint64_t));
     b_.check(b_.ext().softmax_lookup_columns(ctx, W(kScoresQ), 0, W(kRowShift), 0, W(kExpOut), 0, W(kDenoms), 0,
-                                             W(kRecips), 0, W(kWeights), 0, sm, 0, rcols, 0, err_, 0, t, h, rect_,
+                                             W(kRecips), 0, W(kWeights), 0, sm, rcols, 0, err_, 0, t, h, rect_,
                                              kHeadPad, tp, exp_pad_out_, f.softmax_norm, f.recip_den,
                                              kRecipPadInput, recip_pad_out_),
              "volta_b200_softmax_lookup_columns_device");
     {   // softmax norm remainders on Range(14)
         const uint64_t mult = alloc((size_t{1} << f.softmax_norm) * sizeof(uint32_t));
-        zero(mult, (size_t{1} << f.softmax_norm) * sizeof(uint32_t));
-        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm, 2 * rect_, mult, 0, rect_, size_t{1} << f.softmax_norm),
+        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[2], 0, mult, 0, rect_, size_t{1} << f.softmax_norm),
                  "histogram_fp_device");
-        const uint64_t col = alloc(rect_ * sizeof(uint64_t));
-        b_.check(A.volta_cuda_resident_copy_rows(ctx, sm, 2 * rect_ * 8, rect_ * 8, col, 0, rect_ * 8, 1, rect_ * 8),
-                 "resident_copy_rows");
-        add_logup(kSiteNormRange, col, 1, 0, rect_, range_.at(f.softmax_norm), size_t{1} << f.softmax_norm, mult);
+        add_logup(kSiteNormRange, sm[2], 1, 0, rect_, range_.at(f.softmax_norm), size_t{1} << f.softmax_norm, mult);
     }
     {   // (gap, exp) pairs on the ExpGap table
         const uint64_t mult = alloc((size_t{1} << 16) * sizeof(uint32_t));
-        zero(mult, (size_t{1} << 16) * sizeof(uint32_t));
-        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm, 0, mult, 0, rect_, size_t{1} << 16), "histogram_fp_device");
-        add_logup(kSiteExp, sm, 2, 0, rect_, expgap_pairs_, size_t{1} << 16, mult);
+        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[0], 0, mult, 0, rect_, size_t{1} << 16),
+                 "histogram_fp_device");
+        add_logup(kSiteExp, sm[0], 2, 0, rect_, expgap_pairs_, size_t{1} << 16, mult);
     }
     {   // (denom >> den_shift, rc) pairs on the 18-bit reciprocal table
         const size_t n = kHeadPad * tp;
         const uint64_t mult = alloc((size_t{1} << kRecipBits) * sizeof(uint32_t));
-        zero(mult, (size_t{1} << kRecipBits) * sizeof(uint32_t));
         b_.check(A.volta_cuda_histogram_fp_device(ctx, rcols, 0, mult, 0, n, size_t{1} << kRecipBits),
                  "histogram_fp_device");
         add_logup(kSiteRecip, rcols, 2, 2, n, recip_pairs_, size_t{1} << kRecipBits, mult);
@@ -448,28 +441,15 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         const std::vector<Fp2> rc = draw(tx, log2_exact(sh.head_dim)), rh = draw(tx, 4), ri = draw(tx, log2_exact(tp));
         const uint64_t eq_c = eq_table(rc), eq_h = eq_table(rh), eq_i = eq_table(ri);
         const size_t n = kHeadPad * tp;
-        const uint64_t fac = alloc(3 * n * sizeof(Fp2));
-        b_.check(b_.ext().av_factors(ctx, W(kWeights), 0, W(kV), 0, eq_i, 0, eq_c, 0, eq_h, 0, fac, 0, t, h,
+        const uint64_t parts[3] = {alloc(n * sizeof(Fp2)), alloc(n * sizeof(Fp2)), alloc(n * sizeof(Fp2))};
+        b_.check(b_.ext().av_factors(ctx, W(kWeights), 0, W(kV), 0, eq_i, 0, eq_c, 0, eq_h, 0, parts, t, h,
                                      sh.head_dim, kHeadPad, tp),
                  "volta_b200_av_factors_device");
-        const uint64_t parts[3] = {alloc(n * sizeof(Fp2)), alloc(n * sizeof(Fp2)), alloc(n * sizeof(Fp2))};
-        for (int k = 0; k < 3; ++k)
-            b_.check(A.volta_cuda_resident_copy_rows(ctx, fac, k * n * sizeof(Fp2), n * sizeof(Fp2), parts[k], 0,
-                                                     n * sizeof(Fp2), 1, n * sizeof(Fp2)),
-                     "resident_copy_rows");
         triple(parts[0], parts[1], parts[2], n, tx, false);
     }
-    {   // softmax norm product over the attention rectangle (Fp columns)
+    {   // softmax norm product over the attention rectangle (Fp columns: exp, reciprocal, mask)
         FpStream tx(seed, gpt2_site_domain(l, kSiteNormHad));
-        uint64_t col[3];
-        const size_t which[3] = {1, 3, 4};  // exp, reciprocal, real-entry mask
-        for (int k = 0; k < 3; ++k) {
-            col[k] = alloc(rect_ * sizeof(uint64_t));
-            b_.check(A.volta_cuda_resident_copy_rows(ctx, sm, which[k] * rect_ * 8, rect_ * 8, col[k], 0, rect_ * 8,
-                                                     1, rect_ * 8),
-                     "resident_copy_rows");
-        }
-        triple(col[0], col[1], col[2], rect_, tx, true);
+        triple(sm[1], sm[3], sm[4], rect_, tx, true);
     }
     {   // Q.K^T over (head, dimension)
         FpStream tx(seed, gpt2_site_domain(l, kSiteQk));
@@ -493,11 +473,17 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
 }
 
 Gpt2Proof Gpt2Prover::prove(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32]) {
+    return prove_layers(seed, mac_seed, pad_seed, 0, 1, true);
+}
+
+Gpt2Proof Gpt2Prover::prove_layers(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
+                                   size_t first, size_t stride, bool with_pcs) {
     const Api& A = b_.api();
     void* ctx = b_.ctx();
     const Gpt2Shape& sh = s_.shape();
+    if (!stride) throw AccelError("GPT-2 proof layer stride must be positive");
     for (const auto& l : corrections_)
-        for (uint64_t id : l) A.volta_cuda_resident_free(ctx, id);
+        for (uint64_t id : l.second) A.volta_cuda_resident_free(ctx, id);
     corrections_.clear();
     pending_logups_.clear();
     b_.check(A.volta_cuda_resident_zero(ctx, err_, 0, sizeof(uint32_t)), "resident_zero");
@@ -511,10 +497,11 @@ Gpt2Proof Gpt2Prover::prove(const uint8_t seed[32], const uint8_t mac_seed[32], 
         size_t total = 0;
         std::vector<Slot> slots;
     };
-    std::vector<LayerRaw> raw(sh.layers);
-    for (size_t l = 0; l < sh.layers; ++l) {
+    std::vector<LayerRaw> raw;
+    for (size_t l = first; l < sh.layers; l += stride) {
         Owned lay(b_);
-        LayerRaw& lr = raw[l];
+        raw.emplace_back();
+        LayerRaw& lr = raw.back();
         lr.slots = enqueue_layer(l, lay, seed, mac_seed);
         for (Slot& sl : lr.slots) {
             sl.at = lr.total;
@@ -537,12 +524,16 @@ Gpt2Proof Gpt2Prover::prove(const uint8_t seed[32], const uint8_t mac_seed[32], 
     }
     // Ligero commitment of the weights
     const size_t code_len = size_t{1} << kPcsCodeBits, cols = size_t{1} << kPcsColBits;
-    b_.check(A.volta_cuda_chacha8_prover_secret_fp_rows_device(ctx, pads_, 0, pad_seed, 0, kPcsRows, kPcsPad),
-             "chacha8_prover_secret_fp_rows_device");
-    b_.check(A.volta_cuda_pcs_messages_device(ctx, wmat_, 0, pads_, 0, kPcsRows, cols, kPcsPad, code_len, code_, 0),
-             "pcs_messages_device");
-    b_.check(A.volta_cuda_ntt_fp_batch_device(ctx, code_, 0, kPcsRows, code_len, code_, 0), "ntt_fp_batch_device");
-    b_.check(A.volta_cuda_hash_fp_tree_device(ctx, code_, 0, kPcsRows, code_len, tree_, 0), "hash_fp_tree_device");
+    if (with_pcs) {
+        b_.check(A.volta_cuda_chacha8_prover_secret_fp_rows_device(ctx, pads_, 0, pad_seed, 0, kPcsRows, kPcsPad),
+                 "chacha8_prover_secret_fp_rows_device");
+        b_.check(A.volta_cuda_pcs_messages_device(ctx, wmat_, 0, pads_, 0, kPcsRows, cols, kPcsPad, code_len, code_,
+                                                  0),
+                 "pcs_messages_device");
+        b_.check(A.volta_cuda_ntt_fp_batch_device(ctx, code_, 0, kPcsRows, code_len, code_, 0), "ntt_fp_batch_device");
+        b_.check(A.volta_cuda_hash_fp_tree_device(ctx, code_, 0, kPcsRows, code_len, tree_, 0),
+                 "hash_fp_tree_device");
+    }
     // the words: one download per layer, LogUp accumulators turned into
     // round messages exactly as the resident LogUp driver does
     Gpt2Proof out;
@@ -560,7 +551,7 @@ Gpt2Proof Gpt2Prover::prove(const uint8_t seed[32], const uint8_t mac_seed[32], 
         out.layer_words.push_back(std::move(words));
     }
     pending_logups_.clear();
-    b_.download(tree_, (2 * code_len - 2) * 32, out.pcs_root, 32);
+    if (with_pcs) b_.download(tree_, (2 * code_len - 2) * 32, out.pcs_root, 32);
     uint32_t e = 0;
     b_.download(err_, 0, &e, sizeof(e));
     if (e) throw AccelError("GPT-2 proof witness columns out of their lookup domains");

@@ -566,9 +566,24 @@ void launch_side_work(Backend& b, const std::vector<PendingSide*>& sides) {
         jobs.insert(jobs.end(), ps->jobs.begin(), ps->jobs.end());
         for (const auto& st : ps->plan) steps_max = std::max(steps_max, st.size());
     }
-    if (!suffix_jobs.empty())
-        b.check(X.logup_suffix_eq_batch(ctx, suffix_jobs.data(), suffix_jobs.size()),
+    // one suffix-table batch per group of jobs whose large tables fit one
+    // outer-product launch: a job of point length L has min(11, L - 12)
+    // tables of 2^12 .. 2^22 entries in the first band, and no later band
+    // has more
+    constexpr size_t kOuterJobsPerLaunch = 256, kEqTileBits = 11;
+    for (size_t at = 0; at < suffix_jobs.size();) {
+        size_t end = at, large = 0;
+        while (end < suffix_jobs.size()) {
+            const size_t L = suffix_jobs[end].point_len;
+            const size_t k = L > kEqTileBits + 1 ? std::min(kEqTileBits, L - kEqTileBits - 1) : 0;
+            if (end > at && large + k > kOuterJobsPerLaunch) break;
+            large += k;
+            ++end;
+        }
+        b.check(X.logup_suffix_eq_batch(ctx, suffix_jobs.data() + at, end - at),
                 "volta_b200_logup_suffix_eq_batch_device");
+        at = end;
+    }
     // step t of every large layer of every side in one launch (chunks of kRoundBatchMax)
     std::vector<vzb_round_job> batch;
     for (size_t t = 0; t < steps_max; ++t) {
