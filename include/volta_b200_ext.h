@@ -1,7 +1,9 @@
 /*
  * Extensions of libvolta_cuda_backend.so that have no counterpart in the
- * reference seam.  They serve measurement only and never touch the RawStats
- * counters or any buffer: a caller of the reference ABI can ignore them.
+ * reference seam: timing markers, fused and batched forms of the seam's
+ * round kernels used by the scheduled drivers, the column builders of the
+ * GPT-2 proof schedule, and the allocation-free round.  A caller of the
+ * reference ABI can ignore them.
  */
 #ifndef VOLTA_B200_EXT_H
 #define VOLTA_B200_EXT_H
@@ -199,6 +201,24 @@ int volta_b200_logup_suffix_eq_batch_device(void* ctx, const vzb_suffix_job* job
  * 3 messages per round, then the 3 final values. */
 int volta_b200_triple_tail_device(void* ctx, uint64_t a_id, uint64_t b_id, uint64_t c_id, size_t len,
                                   uint64_t r_id, size_t r_offset, uint64_t out_id, size_t out_offset);
+
+/*
+ * Product sumchecks (two factors, the GEMM and LayerNorm claims of the GPT-2
+ * layer proof), the counterparts of the triple-product extensions above:
+ *   product_fold_round_into: fold resident a, b (len entries, a multiple of
+ *     4) with r into a_out, b_out (len/2 entries) exactly as
+ *     volta_cuda_fp2_fold_rows_device, and write the next round's [g(0), g(2)]
+ *     (as volta_cuda_fp2_product_round_into_device on the folded vectors) to
+ *     (out_id, out_offset): one pass and one launch instead of three;
+ *   product_tail: all rounds on two resident vectors of len (<= 2^11, a power
+ *     of two) entries in one CTA, challenges at (r_id, r_offset); output: 2
+ *     messages per round, then the 2 final values.
+ */
+int volta_b200_product_fold_round_into_device(void* ctx, uint64_t a_id, uint64_t b_id, size_t len, vz_fp2 r,
+                                              uint64_t a_out_id, uint64_t b_out_id, uint64_t out_id,
+                                              size_t out_offset);
+int volta_b200_product_tail_device(void* ctx, uint64_t a_id, uint64_t b_id, size_t len, uint64_t r_id,
+                                   size_t r_offset, uint64_t out_id, size_t out_offset);
 
 /*
  * Triple-product round message without any device allocation.

@@ -135,7 +135,9 @@ __global__ void pair_columns_kernel(const void* in, const void* outs, uint64_t* 
 // (every pad entry holds the same value, and remainders and table indices
 // cluster), so one global atomic per element serialises on the hot bins.
 // A warp whose 32 elements share one bin (a run of pads) adds them with one
-// atomic; other warps add per lane.  Tables of at most kSmemBins bins are
+// atomic; in other warps the lanes holding the same bin (softmax remainders
+// of rows where most exp values underflow to 0, small table indices) add
+// once with their count.  Tables of at most kSmemBins bins are
 // counted in a per-block shared-memory copy that is added to the global
 // table once per block (blocks are sized so that this flush stays small
 // against the column).  Each warp walks 32 consecutive elements per step.
@@ -179,10 +181,13 @@ __global__ void histogram_kernel(const uint64_t* in, uint32_t* out, size_t n, si
             }
         }
         const uint32_t first = __shfl_sync(0xffffffffu, bin, 0);
+        const unsigned ok_mask = __ballot_sync(0xffffffffu, ok);
         if (__all_sync(0xffffffffu, ok && bin == first)) {
             if (lane == 0) atomicAdd(target + first, 32u);
         } else if (ok) {
-            atomicAdd(target + bin, 1u);
+            // lanes holding the same bin add once, with their count
+            const unsigned peers = __match_any_sync(ok_mask, bin);
+            if (lane == static_cast<unsigned>(__ffs(peers) - 1)) atomicAdd(target + bin, __popc(peers));
         }
     }
     if (kShared) {

@@ -120,6 +120,21 @@ struct TripleFoldEval {
     }
 };
 
+// Fused fold + next product round: fold a, b (len entries) with r into
+// half-length vectors and accumulate the next round's [g(0), g(2)].
+struct ProductFoldEval {
+    const Fp2 *a, *b;
+    Fp2 *ao, *bo;
+    Fp2 r;
+    __device__ __forceinline__ void operator()(size_t i, Fp2W* w) const {
+        Fp2 a0, a1, b0, b1;
+        fold4_pair(a, ao, i, r, a0, a1);
+        fold4_pair(b, bo, i, r, b0, b1);
+        f2w_mac(w[0], a0, b0);
+        f2w_mac(w[1], d2add_weak(a1, d2sub(a1, a0)), d2add_weak(b1, d2sub(b1, b0)));
+    }
+};
+
 // Round 0 of a triple product over base-field tables (Fp values, i.e. Fp2
 // values with c1 = 0): the products stay in Fp (two base products per point
 // instead of two Fp2 products) and the message has c1 = 0.
@@ -1528,6 +1543,24 @@ extern "C" int volta_b200_triple_fold_round_into_device(void* raw, uint64_t a_id
                                                         uint64_t co_id, uint64_t out_id, size_t out_offset) {
     return triple_fold_round(static_cast<Context*>(raw), a_id, b_id, c_id, len, r, ao_id, bo_id, co_id, nullptr,
                              out_id, out_offset);
+}
+
+extern "C" int volta_b200_product_fold_round_into_device(void* raw, uint64_t a_id, uint64_t b_id, size_t len, Fp2 r,
+                                                         uint64_t ao_id, uint64_t bo_id, uint64_t out_id,
+                                                         size_t out_offset) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !out_id || len < 4 || (len & 3)) return fail_message(c, "invalid fused product fold-round geometry");
+    void *a = nullptr, *b = nullptr, *ao = nullptr, *bo = nullptr, *dev = nullptr;
+    if (region_elems(c, a_id, 0, len, sizeof(Fp2), &a) || region_elems(c, b_id, 0, len, sizeof(Fp2), &b) ||
+        region_elems(c, ao_id, 0, len / 2, sizeof(Fp2), &ao) || region_elems(c, bo_id, 0, len / 2, sizeof(Fp2), &bo) ||
+        region_elems(c, out_id, out_offset, 2, sizeof(Fp2), &dev))
+        return -1;
+    const MsgOut o = msg_out(c, static_cast<Fp2*>(dev), nullptr, 2);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    ProductFoldEval ev{static_cast<const Fp2*>(a), static_cast<const Fp2*>(b), static_cast<Fp2*>(ao),
+                       static_cast<Fp2*>(bo), r};
+    if (launch_reduce_wide<2>(c, ev, len / 4, store_epi<2>(o), 8)) return -1;
+    return finish_msg(c, kOpGemm, o);
 }
 
 // Triple-product rounds on base-field tables (extensions).

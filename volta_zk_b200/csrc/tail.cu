@@ -197,6 +197,60 @@ int typed_region(Context* c, uint64_t id, size_t off, size_t count, P*& out) {
     return 0;
 }
 
+// All rounds of a product sumcheck on two vectors of 2^L <= 2^11 entries:
+// per round [g(0), g(2)] of a*b (as fp2_product_round) then the fold with
+// that round's challenge; out: 2 per round, then the two final values.
+__global__ void __launch_bounds__(kTailThreads) product_tail_kernel(const Fp2* a, const Fp2* b, int L, const Fp2* rs,
+                                                                    Fp2* out) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int n = 1 << L;
+    Fp2* v[2];
+    Fp2* base = reinterpret_cast<Fp2*>(smem_raw);
+    for (int k = 0; k < 2; ++k) v[k] = base + k * n;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        v[0][i] = ldg2(a + i);
+        v[1][i] = ldg2(b + i);
+    }
+    __syncthreads();
+    int len = n;
+    for (int j = 0; j < L; ++j) {
+        const int half = len >> 1;
+        const Fp2 r = ldg2(rs + j);
+        Fp2W w[2];
+        f2w_zero(w[0]);
+        f2w_zero(w[1]);
+        Fp2 folded[2][kTailPer];
+#pragma unroll
+        for (int m = 0; m < kTailPer; ++m) {
+            const int i = threadIdx.x + m * kTailThreads;
+            if (i >= half) break;
+            const Fp2 a0 = v[0][2 * i], a1 = v[0][2 * i + 1], b0 = v[1][2 * i], b1 = v[1][2 * i + 1];
+            f2w_mac(w[0], a0, b0);
+            f2w_mac(w[1], d2add_weak(a1, d2sub(a1, a0)), d2add_weak(b1, d2sub(b1, b0)));
+            folded[0][m] = d2fold(a0, a1, r);
+            folded[1][m] = d2fold(b0, b1, r);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < kTailPer; ++m) {
+            const int i = threadIdx.x + m * kTailThreads;
+            if (i >= half) break;
+            v[0][i] = folded[0][m];
+            v[1][i] = folded[1][m];
+        }
+        Acc<2> acc;
+        acc.v[0] = f2w_reduce(w[0]);
+        acc.v[1] = f2w_reduce(w[1]);
+        acc = block_sum<2>(acc);
+        if (threadIdx.x == 0) {
+            st2(out + 2 * j, acc.v[0]);
+            st2(out + 2 * j + 1, acc.v[1]);
+        }
+        len = half;
+    }
+    if (threadIdx.x < 2) st2(out + 2 * L + threadIdx.x, v[threadIdx.x][0]);
+}
+
 }  // namespace
 }  // namespace vzb
 
@@ -258,6 +312,29 @@ extern "C" int volta_b200_triple_tail_device(void* raw, uint64_t a_id, uint64_t 
                                      static_cast<int>(smem)));
     if (op_begin(c) || op_mark(c, 1)) return -1;
     triple_tail_kernel<<<1, kTailThreads, smem, c->stream>>>(a, b, cc, L, r, out);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpGemm, 0, 0);
+}
+
+extern "C" int volta_b200_product_tail_device(void* raw, uint64_t a_id, uint64_t b_id, size_t len, uint64_t r_id,
+                                              size_t r_offset, uint64_t out_id, size_t out_offset) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !len || (len & (len - 1)) || len > (size_t{1} << kTailMaxLog))
+        return fail_message(c, "invalid product tail geometry");
+    int L = 0;
+    while ((size_t{1} << L) < len) ++L;
+    const Fp2 *a = nullptr, *b = nullptr, *r = nullptr;
+    Fp2* out = nullptr;
+    if (typed_region(c, a_id, 0, len, a) || typed_region(c, b_id, 0, len, b) ||
+        (L && typed_region(c, r_id, r_offset, L, r)) || typed_region(c, out_id, out_offset, 2 * L + 2, out))
+        return -1;
+    const size_t smem = 2 * len * sizeof(Fp2);
+    if (smem > 48 * 1024)
+        VZB_CUDA(c, cudaFuncSetAttribute(product_tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    product_tail_kernel<<<1, kTailThreads, smem, c->stream>>>(a, b, L, r, out);
     VZB_LAUNCHED(c);
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpGemm, 0, 0);

@@ -192,38 +192,51 @@ namespace {
 
 // Product sumcheck of two resident Fp2 vectors of n = 2^k entries
 // (sumcheck_clear.rs:23-70 / hadamard.rs:190-260 with two factors): per round
-// the seam's [g(0), g(2)] (fp2_product_round_into_device) at
-// msgs[off + 2 j], then the fold with r_j; the two final values at
-// msgs[off + 2 k], msgs[off + 2 k + 1].  Challenges: the next k draws of tx.
+// the seam's [g(0), g(2)] at msgs[off + 2 j], then the fold with r_j; the two
+// final values at msgs[off + 2 k], msgs[off + 2 k + 1].  Challenges: the
+// next k draws of tx.  Rounds on more than 2^11 entries run as one fused
+// fold + next-round launch each; the rest run in one CTA.
+constexpr size_t kProductTail = 2048;
+
 void product_rounds(Backend& b, Owned& own, uint64_t a, uint64_t bb, size_t n, FpStream& tx, uint64_t msgs,
                     size_t off) {
     const Api& A = b.api();
+    const ExtApi& X = b.ext();
     void* ctx = b.ctx();
     const size_t k = log2_exact(n);
     const std::vector<Fp2> r = draw(tx, k);
-    uint64_t cur[2] = {a, bb};
-    size_t len = n;
-    for (size_t j = 0; j < k; ++j) {
-        b.check(A.volta_cuda_fp2_product_round_into_device(ctx, cur[0], 0, cur[1], 0, len / 2, msgs, off + 2 * j),
-                "fp2_product_round_into_device");
-        const vz_fp2 rj{r[j].c0, r[j].c1};
-        if (len == 2) {
-            for (int t = 0; t < 2; ++t)
-                b.check(A.volta_cuda_fp2_fold_rows_device(ctx, cur[t], 0, 1, 2, rj, msgs, off + 2 * k + t),
-                        "fp2_fold_rows_device");
-            return;
-        }
-        for (int t = 0; t < 2; ++t) {
-            const uint64_t nxt = own.add(b.alloc((len / 2) * sizeof(Fp2)));
-            b.check(A.volta_cuda_fp2_fold_rows_device(ctx, cur[t], 0, 1, len, rj, nxt, 0), "fp2_fold_rows_device");
-            cur[t] = nxt;
-        }
-        len /= 2;
+    if (!k) {
+        for (int t = 0; t < 2; ++t)
+            b.check(A.volta_cuda_resident_copy_rows(ctx, t ? bb : a, 0, sizeof(Fp2), msgs, (off + t) * sizeof(Fp2),
+                                                    sizeof(Fp2), 1, sizeof(Fp2)),
+                    "resident_copy_rows");
+        return;
     }
-    for (int t = 0; t < 2; ++t)  // n == 1
-        b.check(A.volta_cuda_resident_copy_rows(ctx, cur[t], 0, sizeof(Fp2), msgs, (off + t) * sizeof(Fp2),
-                                                sizeof(Fp2), 1, sizeof(Fp2)),
-                "resident_copy_rows");
+    const uint64_t rdev = own.add(b.alloc(k * sizeof(Fp2)));
+    b.upload(rdev, 0, r.data(), k * sizeof(Fp2));
+    uint64_t cur[2] = {a, bb};
+    size_t len = n, j = 0;
+    if (len > kProductTail)
+        b.check(A.volta_cuda_fp2_product_round_into_device(ctx, a, 0, bb, 0, len / 2, msgs, off),
+                "fp2_product_round_into_device");
+    while (len > kProductTail) {
+        uint64_t nxt[2];
+        for (int t = 0; t < 2; ++t) nxt[t] = own.add(b.alloc((len / 2) * sizeof(Fp2)));
+        const vz_fp2 rj{r[j].c0, r[j].c1};
+        if (len / 2 > kProductTail) {  // fold with r_j and round j + 1's message in one pass
+            b.check(X.product_fold_round(ctx, cur[0], cur[1], len, rj, nxt[0], nxt[1], msgs, off + 2 * (j + 1)),
+                    "volta_b200_product_fold_round_into_device");
+        } else {  // the tail computes round j + 1 itself
+            for (int t = 0; t < 2; ++t)
+                b.check(A.volta_cuda_fp2_fold_rows_device(ctx, cur[t], 0, 1, len, rj, nxt[t], 0),
+                        "fp2_fold_rows_device");
+        }
+        cur[0] = nxt[0];
+        cur[1] = nxt[1];
+        len /= 2;
+        ++j;
+    }
+    b.check(X.product_tail(ctx, cur[0], cur[1], len, rdev, j, msgs, off + 2 * j), "volta_b200_product_tail_device");
 }
 
 // LogUp proof of one lookup instance: query side from `qcols` (one Fp
