@@ -325,30 +325,39 @@ int volta_b200_embed_i16_device(void* ctx, uint64_t in_id, size_t in_offset, uin
  * Softmax witness columns of the GPT-2 layer proof, from the forward's
  * causal-packed wires (scores_q, exp_out, weights: heads * rows(rows+1)/2
  * int16; row_shift, recips: heads * rows int16; denoms: heads * rows int64).
- * Writes u64 columns of n_pad >= packed entries into the buffers out_ids[0..4]
- * (offset 0): [0] the score gap c_row - s followed by the exp value (2 x
- * n_pad: the ExpGap lookup pair, rust/volta-gpt2/src/luts.rs:188-206), [1]
- * the exp value (Fp) again, [2] the softmax-norm requant remainder
- * exp*rc + 2^(s-1) - w*2^s (Range(s) lookup, s = norm_shift), [3] the row's
- * reciprocal (Fp), [4] a 0/1 real-entry mask; entries past the packed length
- * hold the pads (gap 0, exp_pad, 2^(s-1), 0, 0).  At recip_cols, two
- * columns of h_pad * t_pad entries (index head * t_pad + row): the
- * reciprocal lookup pair (denom >> recip_den_shift, rc) over the 18-bit
- * reciprocal domain (luts.rs:208-226), (recip_pad_in, recip_pad_out)
- * outside the real heads and rows.  An out-of-domain gap, remainder or
- * reciprocal input sets *error to 1.  Replaces the host-side column builders
- * of the reference's softmax sites (rust/volta-proto/src/block_proof.rs:
- * build_attn_wires, prove_range_site, c62_softmax_recip_wires).
+ * Writes u64 columns into the buffers out_ids[0..7] (offset 0), [0..5] of
+ * n_pad >= packed entries: [0] the score gap c_row - s (the ExpGap table
+ * index, rust/volta-gpt2/src/luts.rs:188-206), [1] the exp lookup's packed
+ * query gap + 2^16 exp, [2] the exp value (Fp), [3] the softmax-norm requant
+ * remainder exp*rc + 2^(s-1) - w*2^s (Range(s) lookup, s = norm_shift), [4]
+ * the row's reciprocal (Fp), [5] a 0/1 real-entry mask, the entries past the
+ * packed length holding the pads (gap 0, exp = exp_pad, 2^(s-1), 0, 0); and
+ * [6..7] of h_pad * t_pad entries (index head * t_pad + row): the reciprocal
+ * lookup's input denom >> recip_den_shift (table index over the 18-bit
+ * domain, luts.rs:208-226) and its packed query input + 2^18 rc,
+ * (recip_pad_in, recip_pad_out) outside the real heads and rows.  An
+ * out-of-domain gap, remainder or reciprocal input sets *error to 1.
+ * Replaces the host-side column builders of the reference's softmax sites
+ * (rust/volta-proto/src/block_proof.rs: build_attn_wires, prove_range_site,
+ * c62_softmax_recip_wires).
  */
 int volta_b200_softmax_lookup_columns_device(void* ctx, uint64_t scores_id, size_t scores_offset,
                                             uint64_t row_shift_id, size_t row_shift_offset, uint64_t exp_id,
                                             size_t exp_offset, uint64_t denoms_id, size_t denoms_offset,
                                             uint64_t recips_id, size_t recips_offset, uint64_t weights_id,
-                                            size_t weights_offset, const uint64_t* out_ids, uint64_t recip_cols_id,
-                                            size_t recip_cols_offset, uint64_t error_id, size_t error_offset,
-                                            size_t rows, size_t heads, size_t n_pad, size_t h_pad, size_t t_pad,
-                                            uint64_t exp_pad, uint32_t norm_shift, uint32_t recip_den_shift,
-                                            uint64_t recip_pad_in, uint64_t recip_pad_out);
+                                            size_t weights_offset, const uint64_t* out_ids, uint64_t error_id,
+                                            size_t error_offset, size_t rows, size_t heads, size_t n_pad,
+                                            size_t h_pad, size_t t_pad, uint64_t exp_pad, uint32_t norm_shift,
+                                            uint32_t recip_den_shift, uint64_t recip_pad_in, uint64_t recip_pad_out);
+
+/*
+ * A pair lookup's query column: out[i] = cols[i] + 2^shift cols[n + i]
+ * (mod p) for the two canonical columns at cols (input, then output), as
+ * the reference packs pairs (rust/volta-proto/src/block_proof.rs:2511-2520
+ * pair_table).
+ */
+int volta_b200_pack_pair_column_device(void* ctx, uint64_t cols_id, size_t cols_offset, size_t n, uint32_t shift,
+                                       uint64_t out_id, size_t out_offset);
 
 /*
  * Factors of the A.V contraction sumcheck (the attention-value GEMM of

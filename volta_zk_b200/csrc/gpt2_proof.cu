@@ -12,11 +12,14 @@
 //       row's reciprocal and a 0/1 real-entry mask.  Entries past the packed
 //       length up to the padded length get the pad values (gap 0, exp =
 //       ExpGap[0], rem 2^(s-1), rc 0, mask 0), so every column is a
-//       complete lookup / sumcheck table.  Lane 0 of each row also writes
-//       the row's reciprocal lookup pair (denom >> den_shift, rc) at
-//       head * t_pad + row (the "softmax_recip" instance over the 18-bit
-//       domain, luts.rs:208-226); the other (head, row) slots hold the pad
-//       pair.
+//       complete lookup / sumcheck table.  The exp lookup's query column is
+//       written packed (gap + 2^16 exp) beside the gap (its table index).
+//       Lane 0 of each row also writes the row's reciprocal lookup input
+//       denom >> den_shift and its packed pair input + 2^18 rc at head *
+//       t_pad + row (the "softmax_recip" instance over the 18-bit domain,
+//       luts.rs:208-226); the other (head, row) slots hold the pad pair.
+//   pack_pair_column  a + 2^k b of two canonical columns (a pair lookup's
+//       query column).
 //   av_factors  the three factors of the A.V contraction sumcheck over
 //       (head, key position): A[h,j] = sum_i eq_i[i] w[h,i,j] (packed
 //       causal weights, i >= j), B[h,j] = sum_c eq_c[c] v[j, h*dh + c],
@@ -29,18 +32,18 @@ namespace vzb {
 namespace {
 
 struct SoftmaxCols {
-    uint64_t *gap, *exp_pair, *exp, *rem, *rc, *mask;  // gap and exp_pair are one 2 x n_pad buffer
+    uint64_t *gap, *packed, *exp, *rem, *rc, *mask, *rin, *rpacked;
 };
 
 __global__ void softmax_columns_kernel(const int16_t* scores, const int16_t* row_shift, const int16_t* exp_out,
                                        const int64_t* denoms, const int16_t* recips, const int16_t* weights,
-                                       SoftmaxCols cols, uint64_t* recip_cols, uint32_t* error, size_t rows,
+                                       SoftmaxCols cols, uint32_t* error, size_t rows,
                                        size_t heads, size_t packed, size_t n_pad, size_t h_pad, size_t t_pad,
-                                       uint64_t exp_pad, uint32_t norm_shift, uint32_t den_shift,
-                                       uint64_t recip_pad_in, uint64_t recip_pad_out) {
+                                       uint64_t exp_pad, uint64_t packed_pad, uint32_t norm_shift,
+                                       uint32_t den_shift, uint64_t recip_pad_in, uint64_t recip_pad_packed) {
     uint64_t* gap_c = cols.gap;
     uint64_t* exp_c = cols.exp;
-    uint64_t* exp_pair_c = cols.exp_pair;
+    uint64_t* packed_c = cols.packed;
     uint64_t* rem_c = cols.rem;
     uint64_t* rc_c = cols.rc;
     uint64_t* mask_c = cols.mask;
@@ -59,8 +62,9 @@ __global__ void softmax_columns_kernel(const int16_t* scores, const int16_t* row
         if (lane == 0) {
             const int64_t rin = denoms[head * rows + row] >> den_shift;
             if (rin < 0 || rin >= (int64_t{1} << 18)) bad = true;
-            recip_cols[head * t_pad + row] = static_cast<uint64_t>(rin & ((int64_t{1} << 18) - 1));
-            recip_cols[h_pad * t_pad + head * t_pad + row] = ffrom_i64(rc);
+            const int64_t ri = rin & ((int64_t{1} << 18) - 1);
+            cols.rin[head * t_pad + row] = static_cast<uint64_t>(ri);
+            cols.rpacked[head * t_pad + row] = ffrom_i64(ri + rc * (int64_t{1} << 18));
         }
         for (size_t j = lane; j <= row; j += 32) {
             const size_t e = start + j;
@@ -70,7 +74,7 @@ __global__ void softmax_columns_kernel(const int16_t* scores, const int16_t* row
             if (gap < 0 || gap > 0xFFFF || rem < 0 || rem >= (int64_t{1} << norm_shift)) bad = true;
             gap_c[e] = static_cast<uint64_t>(gap & 0xFFFF);
             exp_c[e] = ffrom_i64(ex);
-            exp_pair_c[e] = ffrom_i64(ex);
+            packed_c[e] = ffrom_i64((gap & 0xFFFF) + ex * 65536);
             rem_c[e] = static_cast<uint64_t>(rem & ((int64_t{1} << norm_shift) - 1));
             rc_c[e] = ffrom_i64(rc);
             mask_c[e] = 1;
@@ -81,7 +85,7 @@ __global__ void softmax_columns_kernel(const int16_t* scores, const int16_t* row
          e += static_cast<size_t>(gridDim.x) * blockDim.x) {
         gap_c[e] = 0;
         exp_c[e] = exp_pad;
-        exp_pair_c[e] = exp_pad;
+        packed_c[e] = packed_pad;
         rem_c[e] = static_cast<uint64_t>(half);
         rc_c[e] = 0;
         mask_c[e] = 0;
@@ -91,10 +95,18 @@ __global__ void softmax_columns_kernel(const int16_t* scores, const int16_t* row
          z += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const size_t head = z / t_pad, row = z - head * t_pad;
         if (head < heads && row < rows) continue;
-        recip_cols[z] = recip_pad_in;
-        recip_cols[h_pad * t_pad + z] = recip_pad_out;
+        cols.rin[z] = recip_pad_in;
+        cols.rpacked[z] = recip_pad_packed;
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(error, 1u);
+}
+
+// out[i] = a[i] + 2^shift b[i] (mod p) for canonical a, b: a packed lookup
+// pair as one query column
+__global__ void pack_pair_kernel(const uint64_t* a, const uint64_t* b, uint64_t* out, size_t n, uint64_t scale) {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        out[i] = dadd(__ldcs(a + i), dmul(__ldcs(b + i), scale));
 }
 
 // One block per (head, tile of 32 key positions): lane j of each of the 8
@@ -146,43 +158,55 @@ using namespace vzb;
 extern "C" int volta_b200_softmax_lookup_columns_device(
     void* raw, uint64_t scores_id, size_t scores_offset, uint64_t row_shift_id, size_t row_shift_offset,
     uint64_t exp_id, size_t exp_offset, uint64_t denoms_id, size_t denoms_offset, uint64_t recips_id,
-    size_t recips_offset, uint64_t weights_id, size_t weights_offset, const uint64_t* out_ids,
-    uint64_t recip_cols_id, size_t recip_cols_offset, uint64_t error_id, size_t error_offset, size_t rows,
-    size_t heads, size_t n_pad, size_t h_pad, size_t t_pad, uint64_t exp_pad, uint32_t norm_shift,
-    uint32_t recip_den_shift, uint64_t recip_pad_in, uint64_t recip_pad_out) {
+    size_t recips_offset, uint64_t weights_id, size_t weights_offset, const uint64_t* out_ids, uint64_t error_id,
+    size_t error_offset, size_t rows, size_t heads, size_t n_pad, size_t h_pad, size_t t_pad, uint64_t exp_pad,
+    uint32_t norm_shift, uint32_t recip_den_shift, uint64_t recip_pad_in, uint64_t recip_pad_out) {
     Context* c = static_cast<Context*>(raw);
     const size_t packed = heads * (rows * (rows + 1) / 2);
     if (!c || !out_ids || !rows || !heads || n_pad < packed || h_pad < heads || t_pad < rows || !norm_shift ||
-        norm_shift > 30 || !recip_den_shift || recip_den_shift > 30)
+        norm_shift > 30 || !recip_den_shift || recip_den_shift > 30 || exp_pad >= kP || recip_pad_in >= (1u << 18) ||
+        recip_pad_out >= kP)
         return fail_message(c, "invalid softmax lookup column geometry");
-    void *sc = nullptr, *rs = nullptr, *ex = nullptr, *dn = nullptr, *rc = nullptr, *w = nullptr, *rcols = nullptr,
-         *err = nullptr;
-    void* outs[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    void *sc = nullptr, *rs = nullptr, *ex = nullptr, *dn = nullptr, *rc = nullptr, *w = nullptr, *err = nullptr;
+    void* outs[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     if (region_elems(c, scores_id, scores_offset, packed, 2, &sc) ||
         region_elems(c, row_shift_id, row_shift_offset, heads * rows, 2, &rs) ||
         region_elems(c, exp_id, exp_offset, packed, 2, &ex) ||
         region_elems(c, denoms_id, denoms_offset, heads * rows, 8, &dn) ||
         region_elems(c, recips_id, recips_offset, heads * rows, 2, &rc) ||
         region_elems(c, weights_id, weights_offset, packed, 2, &w) ||
-        region_elems(c, out_ids[0], 0, 2 * n_pad, 8, &outs[0]) ||
-        region_elems(c, recip_cols_id, recip_cols_offset, 2 * h_pad * t_pad, 8, &rcols) ||
         region_elems(c, error_id, error_offset, 1, 4, &err))
         return -1;
-    for (int k = 1; k < 5; ++k)
-        if (region_elems(c, out_ids[k], 0, n_pad, 8, &outs[k])) return -1;
+    for (int k = 0; k < 8; ++k)
+        if (region_elems(c, out_ids[k], 0, k < 6 ? n_pad : h_pad * t_pad, 8, &outs[k])) return -1;
     SoftmaxCols cols;
-    cols.gap = static_cast<uint64_t*>(outs[0]);
-    cols.exp_pair = cols.gap + n_pad;
-    cols.exp = static_cast<uint64_t*>(outs[1]);
-    cols.rem = static_cast<uint64_t*>(outs[2]);
-    cols.rc = static_cast<uint64_t*>(outs[3]);
-    cols.mask = static_cast<uint64_t*>(outs[4]);
+    uint64_t** dst[8] = {&cols.gap, &cols.packed, &cols.exp, &cols.rem, &cols.rc, &cols.mask, &cols.rin, &cols.rpacked};
+    for (int k = 0; k < 8; ++k) *dst[k] = static_cast<uint64_t*>(outs[k]);
+    // pads: gap 0 with ExpGap[0]; the reciprocal pad pair, packed
+    const uint64_t packed_pad = fmul(exp_pad, uint64_t{1} << 16);
+    const uint64_t recip_pad_packed = fadd(recip_pad_in, fmul(recip_pad_out, uint64_t{1} << 18));
     if (op_begin(c) || op_mark(c, 1)) return -1;
     softmax_columns_kernel<<<grid_for(c, n_pad, 256), 256, 0, c->stream>>>(
         static_cast<const int16_t*>(sc), static_cast<const int16_t*>(rs), static_cast<const int16_t*>(ex),
         static_cast<const int64_t*>(dn), static_cast<const int16_t*>(rc), static_cast<const int16_t*>(w), cols,
-        static_cast<uint64_t*>(rcols), static_cast<uint32_t*>(err), rows, heads, packed, n_pad, h_pad, t_pad,
-        exp_pad, norm_shift, recip_den_shift, recip_pad_in, recip_pad_out);
+        static_cast<uint32_t*>(err), rows, heads, packed, n_pad, h_pad, t_pad, exp_pad, packed_pad, norm_shift,
+        recip_den_shift, recip_pad_in, recip_pad_packed);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpLogup, 0, 0);
+}
+
+extern "C" int volta_b200_pack_pair_column_device(void* raw, uint64_t cols_id, size_t cols_offset, size_t n,
+                                                  uint32_t shift, uint64_t out_id, size_t out_offset) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !n || shift >= 64) return fail_message(c, "invalid pair-column packing geometry");
+    void *cols = nullptr, *out = nullptr;
+    if (region_elems(c, cols_id, cols_offset, 2 * n, 8, &cols) || region_elems(c, out_id, out_offset, n, 8, &out))
+        return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    const uint64_t* a = static_cast<const uint64_t*>(cols);
+    pack_pair_kernel<<<grid_for(c, n, 256), 256, 0, c->stream>>>(a, a + n, static_cast<uint64_t*>(out), n,
+                                                                 uint64_t{1} << shift);
     VZB_LAUNCHED(c);
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpLogup, 0, 0);

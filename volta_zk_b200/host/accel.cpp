@@ -145,6 +145,8 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         dlsym(handle_, "volta_b200_product_fold_round_into_device"));
     ext_loaded_->product_tail =
         reinterpret_cast<decltype(ext_loaded_->product_tail)>(dlsym(handle_, "volta_b200_product_tail_device"));
+    ext_loaded_->pack_pair_column = reinterpret_cast<decltype(ext_loaded_->pack_pair_column)>(
+        dlsym(handle_, "volta_b200_pack_pair_column_device"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

@@ -339,7 +339,10 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         else
             b_.check(A.volta_cuda_histogram_fp_device(ctx, cc, 0, mult, 0, n, size_t{1} << 16),
                      "histogram_fp_device");
-        add_logup(site, cc, 2, 0, n, table, size_t{1} << 16, mult);
+        // one query column in + 2^16 out: the column path of the LogUp driver
+        const uint64_t q = alloc(n * sizeof(uint64_t));
+        b_.check(b_.ext().pack_pair_column(ctx, cc, 0, n, 16, q, 0), "volta_b200_pack_pair_column_device");
+        add_logup(site, q, 1, 0, n, table, size_t{1} << 16, mult);
     };
     const std::vector<int16_t>& gelu = s_.lut_host(3);
     const std::vector<int16_t>& rsqrt = s_.lut_host(0);
@@ -352,34 +355,34 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     // attention chain
     range_site(kSiteProjRange, W(kProjAcc), W(kProjQ), t, d, tp, d_pad, f.attn_proj);
     range_site(kSiteAvRange, W(kAvAcc), W(kAvQ), t, d, tp, d_pad, f.av);
-    // softmax columns: [0] (gap, exp) pairs, [1] exp, [2] norm remainders, [3] reciprocals, [4] mask
-    uint64_t sm[5];
-    sm[0] = alloc(2 * rect_ * sizeof(uint64_t));
-    for (int k = 1; k < 5; ++k) sm[k] = alloc(rect_ * sizeof(uint64_t));
-    const uint64_t rcols = alloc(2 * kHeadPad * tp * sizeof(uint64_t));
+    // softmax columns: [0] gap, [1] packed (gap, exp), [2] exp, [3] norm
+    // remainders, [4] reciprocals, [5] mask; [6] reciprocal inputs, [7] packed
+    // (input, reciprocal)
+    uint64_t sm[8];
+    for (int k = 0; k < 8; ++k) sm[k] = alloc((k < 6 ? rect_ : kHeadPad * tp) * sizeof(uint64_t));
     b_.check(b_.ext().softmax_lookup_columns(ctx, W(kScoresQ), 0, W(kRowShift), 0, W(kExpOut), 0, W(kDenoms), 0,
-                                             W(kRecips), 0, W(kWeights), 0, sm, rcols, 0, err_, 0, t, h, rect_,
-                                             kHeadPad, tp, exp_pad_out_, f.softmax_norm, f.recip_den,
-                                             kRecipPadInput, recip_pad_out_),
+                                             W(kRecips), 0, W(kWeights), 0, sm, err_, 0, t, h, rect_, kHeadPad, tp,
+                                             exp_pad_out_, f.softmax_norm, f.recip_den, kRecipPadInput,
+                                             recip_pad_out_),
              "volta_b200_softmax_lookup_columns_device");
     {   // softmax norm remainders on Range(14)
         const uint64_t mult = alloc((size_t{1} << f.softmax_norm) * sizeof(uint32_t));
-        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[2], 0, mult, 0, rect_, size_t{1} << f.softmax_norm),
+        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[3], 0, mult, 0, rect_, size_t{1} << f.softmax_norm),
                  "histogram_fp_device");
-        add_logup(kSiteNormRange, sm[2], 1, 0, rect_, range_.at(f.softmax_norm), size_t{1} << f.softmax_norm, mult);
+        add_logup(kSiteNormRange, sm[3], 1, 0, rect_, range_.at(f.softmax_norm), size_t{1} << f.softmax_norm, mult);
     }
     {   // (gap, exp) pairs on the ExpGap table
         const uint64_t mult = alloc((size_t{1} << 16) * sizeof(uint32_t));
         b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[0], 0, mult, 0, rect_, size_t{1} << 16),
                  "histogram_fp_device");
-        add_logup(kSiteExp, sm[0], 2, 0, rect_, expgap_pairs_, size_t{1} << 16, mult);
+        add_logup(kSiteExp, sm[1], 1, 0, rect_, expgap_pairs_, size_t{1} << 16, mult);
     }
     {   // (denom >> den_shift, rc) pairs on the 18-bit reciprocal table
         const size_t n = kHeadPad * tp;
         const uint64_t mult = alloc((size_t{1} << kRecipBits) * sizeof(uint32_t));
-        b_.check(A.volta_cuda_histogram_fp_device(ctx, rcols, 0, mult, 0, n, size_t{1} << kRecipBits),
+        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[6], 0, mult, 0, n, size_t{1} << kRecipBits),
                  "histogram_fp_device");
-        add_logup(kSiteRecip, rcols, 2, 2, n, recip_pairs_, size_t{1} << kRecipBits, mult);
+        add_logup(kSiteRecip, sm[7], 1, 0, n, recip_pairs_, size_t{1} << kRecipBits, mult);
     }
     range_site(kSiteScoresRange, W(kScoresAcc), W(kScoresQ), 1, packed, 1, rect_, f.scores);
     range_site(kSiteQkvRange, W(kQkvAcc), W(kQkvQ), t, 3 * d, tp, q_pad, f.qkv);
@@ -462,7 +465,7 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     }
     {   // softmax norm product over the attention rectangle (Fp columns: exp, reciprocal, mask)
         FpStream tx(seed, gpt2_site_domain(l, kSiteNormHad));
-        triple(sm[1], sm[3], sm[4], rect_, tx, true);
+        triple(sm[2], sm[4], sm[5], rect_, tx, true);
     }
     {   // Q.K^T over (head, dimension)
         FpStream tx(seed, gpt2_site_domain(l, kSiteQk));
