@@ -53,6 +53,54 @@ int volta_b200_logup_fold_round_into_device(void* ctx, uint64_t p0_id, uint64_t 
                                             size_t suffix_offset, uint64_t out_id, size_t out_offset);
 
 /*
+ * Every round of a general LogUp sumcheck on four resident vectors p0, p1,
+ * q0, q1 of len = 2^L entries (L >= 1), challenges r[0..L) known in advance
+ * (replaces the reference's per-round volta_cuda_logup_general_round_device
+ * + volta_cuda_logup_fold4_device loop, rust/volta-proto/src/logup.rs:427-471,
+ * and its blind-rounds benchmark loop cuda/p7_logup_blind_rounds.cu:403-431).
+ * Round j's message reads the suffix table's first len >> (j+1) entries at
+ * (suffix_id, suffix_offset).  The folded levels 1 .. L-1 of vector k go to
+ * ladder k (len - 2 entries; level j at offset len - 2 (len >> j); unused
+ * when len == 2).  Output at (out_id, out_offset): 4 L accumulators (pq0,
+ * pq2, qq0, qq2 of each round, as volta_cuda_logup_general_round_device
+ * returns them), then the four final values p0, p1, q0, q1.  L + 1 launches,
+ * no host wait.
+ */
+int volta_b200_logup_rounds_device(void* ctx, uint64_t p0_id, uint64_t p1_id, uint64_t q0_id, uint64_t q1_id,
+                                   size_t len, uint64_t suffix_id, size_t suffix_offset, const vz_fp2* r,
+                                   uint64_t ladder0_id, uint64_t ladder1_id, uint64_t ladder2_id,
+                                   uint64_t ladder3_id, uint64_t out_id, size_t out_offset);
+
+/*
+ * Blind LogUp corrections (rust/volta-proto/src/logup.rs:1903-2000
+ * BlindSink::root / round / splits; cuda/p7_logup_blind_rounds.cu:180-214):
+ * per job, one fraction-tree layer whose raw round output is resident in the
+ * layout above (4 accumulators per round, then the four split values).
+ * Output, in proof order, each value minus the mask at the same index:
+ *   [root p, root q]       only when root_id != 0
+ *   h0_j, h2_j per round   h = cpref (lambda pq + qq), cpref *= 2 pt r + 1 - pt - r
+ *   p0, p1, q0, q1         the split values
+ *   p0 q1, p1 q0, q0 q1    the layer-end products
+ * sched holds the rounds claim-point coordinates and then the rounds
+ * challenges.  Any number of jobs (rounds <= 64 each); one launch per 64.
+ */
+typedef struct vzb_blind_job {
+    uint64_t raw_id;
+    size_t raw_offset;
+    uint64_t root_id;
+    size_t root_offset;
+    uint64_t sched_id;
+    size_t sched_offset;
+    uint64_t mask_id;
+    size_t mask_offset;
+    uint64_t out_id;
+    size_t out_offset;
+    vz_fp2 lambda;
+    size_t rounds;
+} vzb_blind_job;
+int volta_b200_logup_blind_corrections_device(void* ctx, const vzb_blind_job* jobs, size_t count);
+
+/*
  * LogUp layer rounds read straight from a fraction-tree level: the layer's
  * vectors p0, p1, q0, q1 (vector_len entries each) are the even/odd children
  * p[child_offset + 2k], p[child_offset + 2k + 1], q[...] of the level.

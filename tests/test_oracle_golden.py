@@ -199,14 +199,24 @@ def rounds_inputs(log2n):
     return cols, s, chals
 
 
-@pytest.mark.parametrize("log2n,checksum", [(16, 0x7eaefbd02661f35b), (22, 0x26139daf10dc7707)])
-def test_logup_rounds_golden(oracle, log2n, checksum):
+@pytest.mark.parametrize("log2n,checksum,blind_checksum", [
+    (16, 0x7eaefbd02661f35b, 0xa0cd787a9d565b4d),
+    (22, 0x26139daf10dc7707, 0x232b3848930c2f15),
+])
+def test_logup_rounds_golden(oracle, log2n, checksum, blind_checksum):
+    """The clear rounds checksum (p7-gpu-logup-rounds*.json) and, over the
+    same rounds, the blind one (cuda/p7_logup_blind_rounds.cu:505-551,
+    p7-gpu-logup-blind-rounds*.json): the blind sink's root / round / split /
+    product corrections hashed after the round messages and folds."""
+    from oracle import blind
     cols, s, chals = rounds_inputs(log2n)
     h = FNV0
     length = 1 << log2n
+    accs = []
     for rnd in range(log2n):
         pairs = length // 2
         acc = oracle.logup_general_round(*cols, s, pairs)
+        accs.append([tuple(int(v) for v in a) for a in acc.reshape(4, 2)])
         h = oracle.fnv_u64(acc.reshape(-1), h)
         nxt = []
         for col in range(4):
@@ -216,6 +226,9 @@ def test_logup_rounds_golden(oracle, log2n, checksum):
         cols = nxt
         length = pairs
     assert h == checksum
+    splits = [tuple(int(v) for v in cols[col][0]) for col in range(4)]
+    art = blind.blind_artifacts(accs, splits, blind.golden_inputs(log2n))
+    assert blind.hash_artifacts(h, art) == blind_checksum
 
 
 # --------------------------------------------------------------------------

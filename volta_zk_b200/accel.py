@@ -48,6 +48,18 @@ def fp2(v) -> Fp2:
     return Fp2(int(v[0]), int(v[1]))
 
 
+class BlindJob(C.Structure):
+    """vzb_blind_job (include/volta_b200_ext.h): one LogUp layer's blind
+    corrections; 112 bytes, lambda 16-byte aligned as vz_fp2 is."""
+
+    _fields_ = [(n, C.c_uint64) for n in (
+        "raw_id raw_offset root_id root_offset sched_id sched_offset mask_id mask_offset out_id "
+        "out_offset").split()] + [("lambda_", Fp2), ("rounds", C.c_uint64), ("_pad", C.c_uint64)]
+
+
+assert C.sizeof(BlindJob) == 112
+
+
 class RawStats(C.Structure):
     _fields_ = (
         [("calls", C.c_uint64 * 7), ("kernel_ns", C.c_uint64 * 7)]
@@ -82,7 +94,7 @@ _CTYPES = {
     "vz_raw_stats*": C.c_void_p, "vz_raw_pinned_stats*": C.c_void_p,
     "vz_raw_control_state*": C.c_void_p, "const vz_attention_wires_args*": C.c_void_p,
     "float*": C.POINTER(C.c_float), "const vzb_layer_job*": C.c_void_p, "const vzb_round_job*": C.c_void_p,
-    "const vzb_suffix_job*": C.c_void_p,
+    "const vzb_suffix_job*": C.c_void_p, "const vzb_blind_job*": C.c_void_p,
 }
 _RESTYPES = {"int": C.c_int, "uint32_t": C.c_uint32, "void": None, "const char*": C.c_char_p}
 

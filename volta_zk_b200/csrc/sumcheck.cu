@@ -1622,6 +1622,63 @@ extern "C" int volta_b200_logup_fold_round_into_device(void* raw, uint64_t p0_id
                             out_offset);
 }
 
+// Every round of a general LogUp sumcheck with the challenges known in
+// advance (the rounds of logup.rs:427-471 run_general_rounds; the GPU loop
+// of cuda/p7_logup_blind_rounds.cu:403-431): round 0's message over the
+// inputs, then per round j >= 1 one fused pass that folds level j-1 with
+// r[j-1] into level j of the caller's ladder and reduces round j's message,
+// and a last plain fold of the two-entry level into the four final values.
+// log2(len) + 1 launches, no host wait; the message of round j reads the
+// suffix table's first len >> (j + 1) entries.
+extern "C" int volta_b200_logup_rounds_device(void* raw, uint64_t p0_id, uint64_t p1_id, uint64_t q0_id,
+                                              uint64_t q1_id, size_t len, uint64_t s_id, size_t s_off,
+                                              const Fp2* r, uint64_t l0_id, uint64_t l1_id, uint64_t l2_id,
+                                              uint64_t l3_id, uint64_t out_id, size_t out_offset) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !r || len < 2 || (len & (len - 1))) return fail_message(c, "invalid LogUp rounds geometry");
+    int L = 0;
+    while ((size_t{1} << L) < len) ++L;
+    for (int j = 0; j < L; ++j)
+        if (r[j].c0 >= kP || r[j].c1 >= kP) return fail_message(c, "LogUp rounds challenge is not canonical");
+    const uint64_t in_ids[4] = {p0_id, p1_id, q0_id, q1_id}, lad_ids[4] = {l0_id, l1_id, l2_id, l3_id};
+    const Fp2* in[4];
+    Fp2* lad[4] = {nullptr, nullptr, nullptr, nullptr};
+    void *p = nullptr, *s = nullptr, *out = nullptr;
+    for (int k = 0; k < 4; ++k) {
+        if (region_elems(c, in_ids[k], 0, len, sizeof(Fp2), &p)) return -1;
+        in[k] = static_cast<const Fp2*>(p);
+        if (len > 2) {
+            if (region_elems(c, lad_ids[k], 0, len - 2, sizeof(Fp2), &p)) return -1;
+            lad[k] = static_cast<Fp2*>(p);
+        }
+    }
+    if (region_elems(c, s_id, s_off, len / 2, sizeof(Fp2), &s) ||
+        region_elems(c, out_id, out_offset, 4 * size_t(L) + 4, sizeof(Fp2), &out))
+        return -1;
+    Fp2* msg = static_cast<Fp2*>(out);
+    const Fp2* suffix = static_cast<const Fp2*>(s);
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    if (logup_round(c, in[0], in[1], in[2], in[3], suffix, len / 2, msg_out(c, msg, nullptr, 4))) return -1;
+    const Fp2* src[4] = {in[0], in[1], in[2], in[3]};
+    for (int j = 1; j < L; ++j) {
+        const size_t cur = len >> (j - 1), at = len - 2 * (len >> j);  // level j at ladder offset `at`
+        Fp2* dst[4];
+        for (int k = 0; k < 4; ++k) dst[k] = lad[k] + at;
+        LogupFoldEval ev{src[0], src[1], src[2], src[3], suffix, dst[0], dst[1], dst[2], dst[3], r[j - 1]};
+        if (launch_reduce_wide<4>(c, ev, cur / 4, store_epi<4>(msg_out(c, msg + 4 * j, nullptr, 4)))) return -1;
+        for (int k = 0; k < 4; ++k) src[k] = dst[k];
+    }
+    Quad q{};
+    for (int k = 0; k < 4; ++k) {
+        q.in[k] = src[k];
+        q.out[k] = msg + 4 * L + k;
+    }
+    fold4_kernel<<<1, 32, 0, c->stream>>>(q, 1, r[L - 1]);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpLogup, 0, 0);
+}
+
 // ===========================================================================
 // Extensions: LogUp layer rounds straight from interleaved tree children
 // ===========================================================================
