@@ -104,3 +104,37 @@ def test_gemm_rejects_bad_geometry(be):
     assert be.lib.volta_cuda_gemm_i64_device(be.ctx, buf, 0, buf, 0, buf, 0, 4, 4, 4) != 0  # beyond the buffers
     assert be.lib.volta_cuda_gemm_requant_auth_device(be.ctx, buf, 0, buf, 0, buf, 0, buf, 0, buf, 0, 1, 1, 1, 0) != 0
     be.free(buf)
+
+
+def test_epilogue_output_is_mac_authenticated(be, oracle):
+    """End to end through the VOLE-MAC: the device expands the mock sub masks
+    of a tensor (domain (tag << 32) | row, corr.rs:1896-1915), the fused GEMM
+    epilogue publishes corrections out - mask, and the verifier half
+    (auth_verifier_from_epilogue, auth.rs:56-69) with the prover's lazily
+    expanded tags (prover_tags_from_epilogue, auth.rs:71-95) accepts every
+    output: k = m + delta out."""
+    from oracle import blind as ob
+
+    m, k, n, shift, tag = 6, 768, 96, 10, 0x0102_0304
+    seed = bytes([0x4D] * 32)
+    delta = (0x0DDC_0FFE_E123_4567, 0x0BAD_CAFE_7654_3210)
+    rng = np.random.default_rng(21)
+    a, b = rand_i16(rng, m * k), rand_i16(rng, k * n)
+    ids = [be.upload_new(x) for x in (a, b)]
+    mid, oid, cid = be.alloc(8 * m * n), be.alloc(2 * m * n), be.alloc(8 * m * n)
+    be.call("mock_correlation_sub_masks_device", mid, 0, seed, tag << 32, m, n)
+    be.call("gemm_requant_auth_device", ids[0], 0, ids[1], 0, mid, 0, oid, 0, cid, 0, m, k, n, shift)
+    out = be.download(oid, 2 * m * n, dtype=np.int16).reshape(m, n)
+    corr = be.download(cid, 8 * m * n).reshape(m, n)
+    exp_out, _ = oracle.gemm_requant_auth(a, b, np.zeros(m * n, dtype=np.uint64), m, k, n, shift)
+    assert np.array_equal(out.reshape(-1), exp_out)
+    for row in range(m):
+        dom = (tag << 32) | row
+        tags = ob.sub_tags(oracle, seed, dom, n)
+        keys = ob.auth_verifier(oracle, seed, dom, [int(c) for c in corr[row]], delta)
+        assert ob.mac_holds(tags, keys, [int(v) for v in out[row]], delta), row
+    # a corrupted correction is rejected
+    keys = ob.auth_verifier(oracle, seed, tag << 32, [int(c) + 1 for c in corr[0]], delta)
+    assert not ob.mac_holds(ob.sub_tags(oracle, seed, tag << 32, n), keys, [int(v) for v in out[0]], delta)
+    for i in ids + [mid, oid, cid]:
+        be.free(i)

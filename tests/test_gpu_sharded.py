@@ -150,3 +150,31 @@ def test_sharded_proof_local_matches_oracle(prover, oracle, log2n, log2f, log2t,
     assert np.array_equal(finals, em_finals)
     got = sh.logup_finish([p[kt:] for p in parts], nf, nt, lseed, domain)
     assert np.array_equal(got, oracle.logup_prove(f, table, mult, lseed, domain))
+
+
+@pytest.mark.parametrize("m,k,n,G", [(1024, 768, 768, 4), (100, 768, 2304, 3), (5, 3072, 768, 8)])
+def test_auth_rows_shards_match_single_gpu_and_oracle(prover, oracle, m, k, n, G):
+    """The VOLE-MAC epilogue split by row blocks (G shards taking turns on
+    one GPU): each block's device masks and fused GEMM epilogue equal the
+    single-call output and corrections rows, and the oracle's."""
+    be = prover.backend
+    rng = np.random.default_rng(m + n + G)
+    a = rng.integers(-900, 900, size=m * k).astype(np.int16)
+    b = rng.integers(-900, 900, size=k * n).astype(np.int16)
+    seed, tag, shift = bytes([0x4D] * 32), 0x0A0B0C, 10
+    ai, bi = be.upload_new(a), be.upload_new(b)
+    _, _, wy, wc = sh.auth_gemm_rows_shard(be, 0, 1, ai, bi, m, k, n, shift, seed, tag)
+    whole_y = be.download(wy, 2 * m * n, dtype=np.int16)
+    whole_c = be.download(wc, 8 * m * n)
+    ey, ec = oracle.gemm_requant_auth(a, b, oracle.chacha_fp_rows(seed, tag << 32, m, n).reshape(-1), m, k, n, shift)
+    assert np.array_equal(whole_y, ey) and np.array_equal(whole_c, ec)
+    for g in range(G):
+        row0, rows, out, corr = sh.auth_gemm_rows_shard(be, g, G, ai, bi, m, k, n, shift, seed, tag)
+        if not rows:
+            continue
+        assert np.array_equal(be.download(out, 2 * rows * n, dtype=np.int16), whole_y[row0 * n:(row0 + rows) * n])
+        assert np.array_equal(be.download(corr, 8 * rows * n), whole_c[row0 * n:(row0 + rows) * n])
+        be.free(out)
+        be.free(corr)
+    for i in (ai, bi, wy, wc):
+        be.free(i)

@@ -215,3 +215,128 @@ def test_concurrently_lane_semantics():
         sh.concurrently(lambda: {}["missing"], slow)
     assert done == [True]  # the lane's work completed before the error surfaced
     assert sh.concurrently(lambda: 5, lambda: 6) == (5, 6)
+
+
+# ---- VOLE-MAC epilogue rows split over shards ----------------------------------
+
+class _EmuBackend:
+    """The two device calls of sh.auth_gemm_rows_shard, by the oracle, on
+    byte buffers registered under integer ids (element offsets as the C ABI)."""
+
+    def __init__(self, oracle):
+        self.o, self.store, self.next = oracle, {}, 1
+
+    def alloc(self, nbytes):
+        self.store[self.next] = np.zeros(nbytes, dtype=np.uint8)
+        self.next += 1
+        return self.next - 1
+
+    def free(self, buf):
+        del self.store[buf]
+
+    def upload_new(self, a):
+        buf = self.alloc(a.nbytes)
+        self.store[buf][:] = np.ascontiguousarray(a).view(np.uint8).reshape(-1)
+        return buf
+
+    def view(self, buf, dtype):
+        return self.store[buf].view(dtype)
+
+    def call(self, name, *args):
+        if name == "mock_correlation_sub_masks_device":
+            out, off_bytes, seed, base, rows, cols = args
+            rows_ = self.o.chacha_fp_rows(seed, base, rows, cols).reshape(-1)
+            self.view(out, np.uint64)[off_bytes // 8:off_bytes // 8 + rows * cols] = rows_
+        elif name == "gemm_requant_auth_device":
+            a, ao, b, bo, mk, mo, out, oo, corr, co, m, k, n, shift = args
+            av = self.view(a, np.int16)[ao:ao + m * k]
+            bv = self.view(b, np.int16)[bo:bo + k * n]
+            y, c = self.o.gemm_requant_auth(av, bv, self.view(mk, np.uint64)[mo:mo + m * n], m, k, n, shift)
+            self.view(out, np.int16)[oo:oo + m * n] = y
+            self.view(corr, np.uint64)[co:co + m * n] = c
+        else:
+            raise AssertionError(name)
+
+
+@pytest.mark.parametrize("m,world", [(1, 1), (7, 2), (12, 4), (5, 8), (1024, 3)])
+def test_row_blocks_partition_the_rows(m, world):
+    blocks = [sh.row_block(m, g, world) for g in range(world)]
+    assert blocks[0][0] == 0 and sum(r for _, r in blocks) == m
+    assert all(blocks[g][0] + blocks[g][1] == blocks[g + 1][0] for g in range(world - 1))
+    assert max(r for _, r in blocks) - min(r for _, r in blocks) <= 1
+    with pytest.raises(Exception):
+        sh.row_block(m, world, world)
+
+
+def _auth_case(rng, m, k, n):
+    a = rng.integers(-600, 600, size=m * k).astype(np.int16)
+    b = rng.integers(-600, 600, size=k * n).astype(np.int16)
+    return a, b
+
+
+@pytest.mark.parametrize("m,world", [(9, 2), (10, 3), (3, 4)])
+def test_auth_rows_shards_concatenate_to_the_whole(oracle, m, world):
+    k, n, shift, tag, seed = 40, 24, 6, 0x33, bytes([0x4D] * 32)
+    a, b = _auth_case(np.random.default_rng(m), m, k, n)
+    whole_y, whole_c = oracle.gemm_requant_auth(a, b, oracle.chacha_fp_rows(seed, tag << 32, m, n).reshape(-1),
+                                                m, k, n, shift)
+    be = _EmuBackend(oracle)
+    ai, bi = be.upload_new(a), be.upload_new(b)
+    ys, cs = [], []
+    for g in range(world):
+        row0, rows, out, corr = sh.auth_gemm_rows_shard(be, g, world, ai, bi, m, k, n, shift, seed, tag)
+        if rows:
+            ys.append(be.view(out, np.int16)[:rows * n].copy())
+            cs.append(be.view(corr, np.uint64)[:rows * n].copy())
+            be.free(out)
+            be.free(corr)
+    assert np.array_equal(np.concatenate(ys), whole_y) and np.array_equal(np.concatenate(cs), whole_c)
+    assert set(be.store) == {ai, bi}  # the shard freed its masks
+
+
+def _rank_auth(rank, world, port, q):
+    """Each gloo rank authenticates its row block; one all-gather of the
+    (padded) blocks rebuilds the single-process output and corrections."""
+    import torch.distributed as dist
+
+    from oracle import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        m, k, n, shift, tag, seed = 11, 32, 16, 5, 0x21, bytes([0x4D] * 32)
+        a, b = _auth_case(np.random.default_rng(4), m, k, n)
+        be = _EmuBackend(oracle)
+        ai, bi = be.upload_new(a), be.upload_new(b)
+        row0, rows, out, corr = sh.auth_gemm_rows_shard(be, rank, world, ai, bi, m, k, n, shift, seed, tag)
+        cap = -(-m // world)
+        mine = np.zeros((cap, n, 2), dtype=np.uint64)
+        mine[:rows, :, 0] = be.view(out, np.int16)[:rows * n].astype(np.int64).view(np.uint64).reshape(rows, n)
+        mine[:rows, :, 1] = be.view(corr, np.uint64)[:rows * n].reshape(rows, n)
+        parts = sh.torch_all_gather()(mine)
+        got = np.concatenate([parts[g][:sh.row_block(m, g, world)[1]] for g in range(world)])
+        y, c = oracle.gemm_requant_auth(a, b, oracle.chacha_fp_rows(seed, tag << 32, m, n).reshape(-1), m, k, n,
+                                        shift)
+        ok = np.array_equal(got[:, :, 0].view(np.int64).reshape(-1), y.astype(np.int64))
+        q.put((rank, bool(ok and np.array_equal(got[:, :, 1].reshape(-1), c))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_auth_rows():
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_auth, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    results = dict(q.get(timeout=5) for _ in range(2))
+    assert results == {0: True, 1: True}
+    assert all(p.exitcode == 0 for p in procs)

@@ -363,3 +363,48 @@ def ligero_commit_open_sharded(be, rank: int, world: int, all_gather: AllGather,
     be.free(tree)
     columns, full_paths = ligero_assemble(all_cols, all_paths, top, idx, slab)
     return top[-1].tobytes(), idx, columns, full_paths
+
+
+# ---------------------------------------------------------------------------
+# VOLE-MAC epilogue rows over G GPUs.  Row i of an authenticated tensor draws
+# its masks from its own correlation domain (tag << 32) | i
+# (rust/volta-gpt2/src/gemm.rs:120-154; corr.rs:234-255), so a row block is
+# independent work: shard g expands the masks of its rows on its GPU and runs
+# the fused GEMM epilogue on its block of A with the whole B.  Nothing is
+# exchanged; the blocks concatenate to the single-GPU output and corrections.
+# ---------------------------------------------------------------------------
+
+def row_block(m: int, rank: int, world: int):
+    """(first row, rows) of shard `rank`: contiguous blocks, the first m % world
+    one row longer."""
+    if world < 1 or not 0 <= rank < world:
+        raise AccelError(f"invalid shard {rank} of {world}")
+    base, extra = divmod(m, world)
+    row0 = rank * base + min(rank, extra)
+    return row0, base + (1 if rank < extra else 0)
+
+
+def auth_gemm_rows_shard(be, rank: int, world: int, a_id: int, b_id: int, m: int, k: int, n: int, shift: int,
+                         mac_seed: bytes, tag: int):
+    """This shard's rows of out = requant(A B) and its corrections out - mask
+    (volta_cuda_gemm_requant_auth_device on rows [row0, row0 + rows) of the
+    resident i16 A (m x k) and the resident B (k x n)).  Returns (row0, rows,
+    out id (i16), correction id (u64)); ids are 0 for an empty block."""
+    if not 0 <= tag < (1 << 29):
+        raise AccelError("tensor tag must leave the reserved domain bits clear")
+    row0, rows = row_block(m, rank, world)
+    if rows == 0:
+        return row0, 0, 0, 0
+    masks = be.alloc(8 * rows * n)
+    out, corr = be.alloc(2 * rows * n), be.alloc(8 * rows * n)
+    try:
+        be.call("mock_correlation_sub_masks_device", masks, 0, mac_seed, (tag << 32) | row0, rows, n)
+        be.call("gemm_requant_auth_device", a_id, row0 * k, b_id, 0, masks, 0, out, 0, corr, 0, rows, k, n,
+                shift)
+    except Exception:
+        be.free(out)
+        be.free(corr)
+        raise
+    finally:
+        be.free(masks)
+    return row0, rows, out, corr
