@@ -148,3 +148,120 @@ def mac_holds(tags, keys, values, delta) -> bool:
     """k = m + delta x for every authenticated value x (canonical Fp)."""
     d = f2(delta)
     return all(k == add(f2(m), (d[0] * int(x) % P, d[1] * int(x) % P)) for m, k, x in zip(tags, keys, values))
+
+
+# ---- the blind LogUp prover, its transcript and its wire format ---------------
+
+TX_CONTEXT = "volta-zk/transcript/canonical-moves/v1"
+U64_MAX = (1 << 64) - 1
+
+
+class Transcript:
+    """Private seeded transcript (rust/volta-mac/src/transcript.rs): challenges
+    from FpStream(seed, u64::MAX) (84-110); every message charged to a label
+    (account, 358-361) and bound as kind || u16 label length || label || u64
+    length || message into the canonical move stream (append_message
+    215-233; challenge requests 3 || 2 for Fp2, 3 || 1 for Fp, 3 || 3 || width
+    for bits, 362-380), whose BLAKE3 derive-key hash with the context
+    "volta-zk/transcript/canonical-moves/v1" is the binding digest (654-667)."""
+
+    def __init__(self, o, seed: bytes):
+        self.o, self.chal, self.moves, self.ledger = o, o.FpStream(seed, U64_MAX), bytearray(), {}
+
+    def append_message(self, label: str, msg: bytes):
+        self.ledger[label] = self.ledger.get(label, 0) + len(msg)
+        lb = label.encode()
+        self.moves += bytes([1]) + len(lb).to_bytes(2, "little") + lb + len(msg).to_bytes(8, "little") + msg
+
+    def append_fp2s(self, label: str, values):
+        self.append_message(label, b"".join(wire_fp2(v) for v in values))
+
+    def challenge_fp2(self):
+        self.moves += bytes([3, 2])
+        return self.chal.next_fp2()
+
+    def digest(self) -> bytes:
+        return self.o.blake3_derive_key(TX_CONTEXT, bytes(self.moves))
+
+    def total_bytes(self) -> int:
+        return sum(self.ledger.values())
+
+
+def wire_fp2(v) -> bytes:
+    return int(v[0]).to_bytes(8, "little") + int(v[1]).to_bytes(8, "little")
+
+
+def encode_blind_frac(root_corrs, layers) -> bytes:
+    """BlindFracProof { root_corrs: [Fp2; 2], layers: Vec<BlindLayerProof>,
+    aux: Option<BlindAuxPart> } under model_proof_codec.rs's Wire rules
+    (rust/volta-proto/src/model_proof_codec.rs:202-320, 362-364): fixed arrays
+    without a length, Vec as u32 LE length + items, Option None as byte 0."""
+    out = b"".join(wire_fp2(x) for x in root_corrs) + len(layers).to_bytes(4, "little")
+    for rounds, split, z in layers:
+        out += len(rounds).to_bytes(4, "little") + b"".join(wire_fp2(a) + wire_fp2(b) for a, b in rounds)
+        out += b"".join(wire_fp2(x) for x in split) + b"".join(wire_fp2(x) for x in z)
+    return out + b"\x00"
+
+
+def blind_logup_prove(o, f, table, mult, tx_seed: bytes, corr_seed: bytes, dom_base: int):
+    """blind_logup_prove (rust/volta-proto/src/logup.rs:3184-3225) with a fresh
+    Transcript::new(tx_seed) and the mock CorrelationStream::new(corr_seed):
+    the clear messages are the oracle's clear LogUp proof under the same
+    private challenge stream (the sinks draw alpha, then per layer lambda, the
+    round challenges and the split challenge in the same order); BlindSink
+    (1927-2004) publishes each as its correction against the full-field masks
+    of one fresh domain per root / round / split / product group, and
+    cross_prover (2526-2556) the corrections of p_f q_t, p_t q_f, 1/q_f, 1/q_t.
+    Returns (BlindLogupProof wire bytes, transcript digest, transcript bytes,
+    the domain cursor after the proof)."""
+    words = o.logup_prove(f, table, mult, tx_seed, U64_MAX)
+    w = [tuple(int(x) for x in row) for row in words]
+    tx = Transcript(o, tx_seed)
+    assert tx.challenge_fp2() == w[0]
+    dom = dom_base
+    pos = 1
+    out, roots = b"", []
+    for n in (len(f), len(table)):
+        depth = n.bit_length() - 1
+        root = (w[pos], w[pos + 1])
+        pos += 2
+        roots.append(root)
+        m = [x for x, _ in full_corrs(o, corr_seed, dom, 2)]
+        dom += 1
+        root_corrs = [sub(root[0], m[0]), sub(root[1], m[1])]
+        tx.append_fp2s("logup_root_corrections", root_corrs)
+        layers = []
+        for layer in range(depth):
+            tx.challenge_fp2()  # lambda
+            rounds = []
+            for _ in range(layer):
+                m = [x for x, _ in full_corrs(o, corr_seed, dom, 2)]
+                dom += 1
+                c = (sub(w[pos], m[0]), sub(w[pos + 1], m[1]))
+                pos += 2
+                tx.append_fp2s("logup_round_corrections", c)
+                rounds.append(c)
+                tx.challenge_fp2()  # round challenge
+            s = w[pos:pos + 4]
+            pos += 4
+            m = [x for x, _ in full_corrs(o, corr_seed, dom, 4)]
+            dom += 1
+            split = [sub(s[k], m[k]) for k in range(4)]
+            tx.append_fp2s("logup_split_corrections", split)
+            zx = [mul(s[0], s[3]), mul(s[1], s[2]), mul(s[2], s[3])]
+            m = [x for x, _ in full_corrs(o, corr_seed, dom, 3)]
+            dom += 1
+            z = [sub(zx[k], m[k]) for k in range(3)]
+            tx.append_fp2s("logup_prod_corrections", z)
+            tx.challenge_fp2()  # split challenge
+            layers.append((rounds, split, z))
+        out += encode_blind_frac(root_corrs, layers)
+    assert pos == len(w)
+    (pf, qf), (pt, qt) = roots
+    zx = [mul(pf, qt), mul(pt, qf), f2(o.fp2_inv(qf)), f2(o.fp2_inv(qt))]
+    m = [x for x, _ in full_corrs(o, corr_seed, dom, 4)]
+    dom += 1
+    cross = [sub(zx[k], m[k]) for k in range(4)]
+    tx.append_fp2s("logup_cross_corrections", cross)
+    out += b"".join(wire_fp2(x) for x in cross)
+    return out, tx.digest(), tx.total_bytes(), dom

@@ -101,6 +101,8 @@ void or_ntt_fp2_batch(const ofp2* in, size_t rows, size_t msg_len, size_t n, ofp
 
 /* ---- BLAKE3 (third-party blake3 1.8.5, restated from the published spec) ---- */
 void or_blake3(const uint8_t* data, size_t len, uint8_t out[32]);
+void or_blake3_derive_key(const uint8_t* context, size_t context_len, const uint8_t* data, size_t len,
+                          uint8_t out[32]);
 /* Column leaves (ligero.rs:351-359, 595-616) and merkle levels (merkle.rs:27-36) */
 void or_hash_fp_columns(const uint64_t* m, size_t rows, size_t cols, uint8_t* leaves);
 void or_hash_fp2_columns(const ofp2* m, size_t rows, size_t cols, uint8_t* leaves);

@@ -116,6 +116,7 @@ def _declare(L):
     L.or_ntt_batch.argtypes = [_vp, _sz, _sz, _sz, _vp]
     L.or_ntt_fp2_batch.argtypes = [_vp, _sz, _sz, _sz, _vp]
     L.or_blake3.argtypes = [_vp, _sz, _vp]
+    L.or_blake3_derive_key.argtypes = [_vp, _sz, _vp, _sz, _vp]
     L.or_hash_fp_columns.argtypes = [_vp, _sz, _sz, _vp]
     L.or_hash_fp2_columns.argtypes = [_vp, _sz, _sz, _vp]
     L.or_merkle_tree.argtypes = [_vp, _sz, _vp]
@@ -361,6 +362,16 @@ def blake3(data: bytes) -> bytes:
     buf = np.frombuffer(data, dtype=np.uint8).copy() if data else np.zeros(1, np.uint8)
     out = np.zeros(32, dtype=np.uint8)
     lib().or_blake3(_p(buf), len(data), _p(out))
+    return out.tobytes()
+
+
+def blake3_derive_key(context: str, data: bytes) -> bytes:
+    """BLAKE3 derive_key mode (blake3::Hasher::new_derive_key(context))."""
+    ctx = context.encode()
+    cbuf = np.frombuffer(ctx, dtype=np.uint8).copy() if ctx else np.zeros(1, np.uint8)
+    buf = np.frombuffer(data, dtype=np.uint8).copy() if data else np.zeros(1, np.uint8)
+    out = np.zeros(32, dtype=np.uint8)
+    lib().or_blake3_derive_key(_p(cbuf), len(ctx), _p(buf), len(data), _p(out))
     return out.tobytes()
 
 

@@ -155,17 +155,20 @@ static void b3_compress(const uint32_t cv[8], const uint8_t block[64], uint64_t 
     for (int i = 0; i < 8; ++i) out[i] = s[i] ^ s[i + 8];
 }
 
-/* Chaining value of one chunk (<= 1024 bytes); root flag when it is the only chunk. */
+/* Chaining value of one chunk (<= 1024 bytes); root flag when it is the only chunk.
+ * key: the 8 key words (the IV for plain hashing); mode: the mode flag added to
+ * every compression (0 hash, 16 keyed hash, 32 key-derivation context, 64
+ * key-derivation material). */
 static void b3_chunk_cv(const uint8_t* data, size_t len, uint64_t chunk_index, int is_root,
-                        uint32_t out[8]) {
+                        const uint32_t key[8], uint32_t mode, uint32_t out[8]) {
     uint32_t cv[8];
-    memcpy(cv, B3_IV, sizeof cv);
+    memcpy(cv, key, sizeof cv);
     size_t nblocks = len == 0 ? 1 : (len + 63) / 64;
     for (size_t b = 0; b < nblocks; ++b) {
         uint8_t block[64] = {0};
         size_t take = len - b * 64 < 64 ? len - b * 64 : 64;
         if (len) memcpy(block, data + b * 64, take);
-        uint32_t flags = 0;
+        uint32_t flags = mode;
         if (b == 0) flags |= 1;
         if (b + 1 == nblocks) {
             flags |= 2;
@@ -176,7 +179,8 @@ static void b3_chunk_cv(const uint8_t* data, size_t len, uint64_t chunk_index, i
     memcpy(out, cv, sizeof cv);
 }
 
-static void b3_parent(const uint32_t l[8], const uint32_t r[8], int is_root, uint32_t out[8]) {
+static void b3_parent(const uint32_t l[8], const uint32_t r[8], int is_root, const uint32_t key[8],
+                      uint32_t mode, uint32_t out[8]) {
     uint8_t block[64];
     for (int i = 0; i < 8; ++i) {
         for (int k = 0; k < 4; ++k) {
@@ -184,32 +188,47 @@ static void b3_parent(const uint32_t l[8], const uint32_t r[8], int is_root, uin
             block[32 + 4 * i + k] = (uint8_t)(r[i] >> (8 * k));
         }
     }
-    b3_compress(B3_IV, block, 0, 64, 4 | (is_root ? 8 : 0), out);
+    b3_compress(key, block, 0, 64, mode | 4 | (is_root ? 8 : 0), out);
 }
 
 /* Subtree over chunks [first, first+count) of the input. */
 static void b3_subtree(const uint8_t* data, size_t len, size_t first, size_t count, int is_root,
-                       uint32_t out[8]) {
+                       const uint32_t key[8], uint32_t mode, uint32_t out[8]) {
     if (count == 1) {
         size_t off = first * 1024;
         size_t take = len - off < 1024 ? len - off : 1024;
-        b3_chunk_cv(data + off, take, first, is_root, out);
+        b3_chunk_cv(data + off, take, first, is_root, key, mode, out);
         return;
     }
     size_t left = 1;
     while (left * 2 < count) left *= 2;
     uint32_t lcv[8], rcv[8];
-    b3_subtree(data, len, first, left, 0, lcv);
-    b3_subtree(data, len, first + left, count - left, 0, rcv);
-    b3_parent(lcv, rcv, is_root, out);
+    b3_subtree(data, len, first, left, 0, key, mode, lcv);
+    b3_subtree(data, len, first + left, count - left, 0, key, mode, rcv);
+    b3_parent(lcv, rcv, is_root, key, mode, out);
 }
 
-void or_blake3(const uint8_t* data, size_t len, uint8_t out[32]) {
+static void b3_root(const uint8_t* data, size_t len, const uint32_t key[8], uint32_t mode, uint8_t out[32]) {
     size_t chunks = len == 0 ? 1 : (len + 1023) / 1024;
     uint32_t cv[8];
-    b3_subtree(data, len, 0, chunks, 1, cv);
+    b3_subtree(data, len, 0, chunks, 1, key, mode, cv);
     for (int i = 0; i < 8; ++i)
         for (int k = 0; k < 4; ++k) out[4 * i + k] = (uint8_t)(cv[i] >> (8 * k));
+}
+
+void or_blake3(const uint8_t* data, size_t len, uint8_t out[32]) { b3_root(data, len, B3_IV, 0, out); }
+
+/* derive_key mode: the context string hashed with the context flag gives
+ * the key with which the material is hashed (material flag). */
+void or_blake3_derive_key(const uint8_t* context, size_t context_len, const uint8_t* data, size_t len,
+                          uint8_t out[32]) {
+    uint8_t k[32];
+    uint32_t key[8];
+    b3_root(context, context_len, B3_IV, 32, k);
+    for (int i = 0; i < 8; ++i)
+        key[i] = (uint32_t)k[4 * i] | ((uint32_t)k[4 * i + 1] << 8) | ((uint32_t)k[4 * i + 2] << 16) |
+                 ((uint32_t)k[4 * i + 3] << 24);
+    b3_root(data, len, key, 64, out);
 }
 
 void or_hash_fp_columns(const uint64_t* m, size_t rows, size_t cols, uint8_t* leaves) {

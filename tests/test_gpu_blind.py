@@ -219,3 +219,44 @@ def test_blind_entry_points_reject_bad_geometry(be):
     assert be.lib.volta_b200_logup_blind_corrections_device(be.ctx, arr, 1) != 0
     for i in ids + [sid, out]:
         be.free(i)
+
+
+@pytest.fixture(scope="module")
+def prover():
+    from volta_zk_b200 import accel
+
+    p = accel.Prover(policy=1)
+    yield p
+    p.close()
+
+
+def embed_i16(x):
+    v = np.asarray(x, dtype=np.int64)
+    out = v.astype(np.uint64)
+    out[v < 0] -= np.uint64(0xFFFFFFFF)  # 2^64 + v - (2^32 - 1) = p + v
+    return out
+
+
+@pytest.mark.parametrize("log2f,log2t", [(1, 1), (4, 3), (10, 8), (14, 10), (16, 13)])
+def test_blind_logup_prove_matches_oracle(prover, oracle, log2f, log2t):
+    """The whole blind LogUp proof (logup.rs:3184-3225) on the device's
+    scheduled rounds: the BlindLogupProof wire bytes, the transcript's
+    canonical binding digest, its charged bytes and the correlation-domain
+    cursor equal the oracle's blind prover."""
+    from oracle import blind as ob
+
+    rng = np.random.default_rng(log2f * 100 + log2t)
+    nf, nt = 1 << log2f, 1 << log2t
+    table = rng.integers(-32768, 32768, size=nt).astype(np.int16)
+    idx = rng.integers(0, nt, size=nf)
+    f = table[idx]
+    mult = np.bincount(idx, minlength=nt).astype(np.uint32)
+    be = prover.backend
+    ids = [be.upload_new(x) for x in (embed_i16(f), embed_i16(table), mult)]
+    tx_seed, corr_seed, base = bytes([0x5A] * 32), bytes([0x4D] * 32), 0x3_0000
+    got = prover.blind_logup_prove(ids[0], nf, ids[1], nt, ids[2], tx_seed, corr_seed, base)
+    exp = ob.blind_logup_prove(oracle, f, table, mult, tx_seed, corr_seed, base)
+    assert got[0] == exp[0]
+    assert got[1:] == exp[1:]
+    for i in ids:
+        be.free(i)

@@ -211,3 +211,47 @@ def test_chacha_rows_with_rejected_draw(be, oracle):
     assert np.array_equal(got, exp)
     assert got[2215 - base, 45451] == raw[45452]
     be.free(out)
+
+
+@pytest.mark.parametrize("n,bins,dist", [
+    (1 << 22, 1 << 16, "skewed"), (1 << 22, 40000, "uniform"), ((1 << 20) + 12345, 1 << 16, "one-bin"),
+    (300000, 20000, "uniform"), (1 << 24, 1 << 16, "skewed")])
+def test_histogram_fp_large_tables(be, n, bins, dist):
+    """Tables of 16385 .. 2^16 bins over long columns (the packed 16-bit
+    shared-memory counters, flushed every 64512 elements of a CTA's slice):
+    exact counts, values at or above `bins` ignored, a single hot bin past
+    65535 per CTA."""
+    rng = np.random.default_rng(n + bins)
+    if dist == "uniform":
+        v = rng.integers(0, bins + 500, size=n, dtype=np.uint64)
+    elif dist == "one-bin":
+        v = np.full(n, bins - 1, dtype=np.uint64)
+    else:
+        v = np.minimum(rng.geometric(0.01, size=n), bins + 10).astype(np.uint64)
+    iv, hist = be.upload_new(v), be.alloc(4 * bins)
+    be.call("resident_zero", hist, 0, 4 * bins)
+    be.call("histogram_fp_device", iv, 0, hist, 0, n, bins)
+    exp = np.bincount(v[v < bins].astype(np.int64), minlength=bins).astype(np.uint32)
+    assert np.array_equal(be.download(hist, 4 * bins, dtype=np.uint32), exp)
+    be.free(iv)
+    be.free(hist)
+
+
+def test_histogram_lut_large_signed_column(be):
+    """u16 lookup indices of a signed column through the packed path: values
+    in [-32768, 32767] embedded in Fp, out-of-domain values ignored."""
+    rng = np.random.default_rng(77)
+    n = (1 << 21) + 3
+    f = np.clip(np.round(rng.normal(0, 300, size=n)), -32768, 32767).astype(np.int64)
+    col = f.astype(np.uint64)
+    col[f < 0] -= np.uint64(0xFFFFFFFF)  # 2^64 + f - (2^32 - 1) = p + f
+    col[::1000] = np.uint64(1 << 20)  # outside the i16 domain: not counted
+    ic, hist = be.upload_new(col), be.alloc(4 << 16)
+    be.call("resident_zero", hist, 0, 4 << 16)
+    be.call("histogram_lut_device", ic, 0, hist, 0, n, 1)
+    keep = np.ones(n, dtype=bool)
+    keep[::1000] = False
+    exp = np.bincount(f[keep] & 0xFFFF, minlength=1 << 16).astype(np.uint32)
+    assert np.array_equal(be.download(hist, 4 << 16, dtype=np.uint32), exp)
+    be.free(ic)
+    be.free(hist)

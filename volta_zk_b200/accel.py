@@ -190,6 +190,12 @@ def load_host_library():
         L.vzh_fpstream_fp2.argtypes = [C.c_char_p, u64, sz, vp]
         L.vzh_fpstream_u64.argtypes = [C.c_char_p, u64, sz, vp]
         L.vzh_fpstream_fp.argtypes = [C.c_char_p, u64, sz, vp]
+        L.vzh_blake3.argtypes = [C.c_char_p, C.c_char_p, sz, vp]
+        L.vzh_blake3.restype = None
+        L.vzh_blind_logup_prove.argtypes = [vp, u64, sz, u64, sz, u64, C.c_char_p, C.c_char_p, u64, vp, sz,
+                                            C.POINTER(C.c_size_t), vp, C.POINTER(C.c_uint64),
+                                            C.POINTER(C.c_uint64), C.c_char_p, sz]
+        L.vzh_blind_logup_check.argtypes = [C.c_char_p, sz, vp, sz, C.POINTER(C.c_size_t), C.c_char_p, sz]
         _host_lib = L
     return _host_lib
 
@@ -197,6 +203,27 @@ def load_host_library():
 def _ptr(a: np.ndarray):
     assert a.flags["C_CONTIGUOUS"]
     return a.ctypes.data_as(C.c_void_p)
+
+
+def blake3(data: bytes, derive_key_context: str | None = None) -> bytes:
+    """BLAKE3 of `data` through the host library (derive-key mode with a context)."""
+    out = np.zeros(32, dtype=np.uint8)
+    ctx = derive_key_context.encode() if derive_key_context is not None else None
+    load_host_library().vzh_blake3(ctx, data, len(data), _ptr(out))
+    return out.tobytes()
+
+
+def blind_logup_check(data: bytes, max_layers: int = 256):
+    """Strict decode + re-encode of BlindLogupProof wire bytes; returns the
+    per-layer round counts (lookup side, then table side)."""
+    rounds = np.zeros(max_layers, dtype=np.uint32)
+    layers = C.c_size_t()
+    err = C.create_string_buffer(1024)
+    rc = load_host_library().vzh_blind_logup_check(data, len(data), _ptr(rounds), max_layers, C.byref(layers), err,
+                                                   1024)
+    if rc != 0:
+        raise AccelError(err.value.decode())
+    return [int(x) for x in rounds[: layers.value]]
 
 
 class CudaBackend:
@@ -404,6 +431,23 @@ class Prover:
                                        C.byref(written), err, 1024)
         self._err(rc, err)
         return out[: written.value]
+
+    def blind_logup_prove(self, f_col: int, n_f: int, t_col: int, n_t: int, mult: int, tx_seed: bytes,
+                          corr_seed: bytes, dom_base: int):
+        """Blind LogUp proof (rust/volta-proto/src/logup.rs:3184-3225) with a
+        fresh private transcript and the mock correlation stream: (proof wire
+        bytes, transcript binding digest, transcript bytes, next domain)."""
+        d_f, d_t = n_f.bit_length() - 1, n_t.bit_length() - 1
+        cap = 4096 + 16 * 2 * (d_f * d_f + d_t * d_t + 8 * (d_f + d_t))
+        out = np.zeros(cap, dtype=np.uint8)
+        digest = np.zeros(32, dtype=np.uint8)
+        written, tx_bytes, next_dom = C.c_size_t(), C.c_uint64(), C.c_uint64()
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_blind_logup_prove(self.h, f_col, n_f, t_col, n_t, mult, tx_seed, corr_seed, dom_base,
+                                             _ptr(out), cap, C.byref(written), _ptr(digest), C.byref(tx_bytes),
+                                             C.byref(next_dom), err, 1024)
+        self._err(rc, err)
+        return out[: written.value].tobytes(), digest.tobytes(), tx_bytes.value, next_dom.value
 
     def ligero_commit_open(self, row_seed: bytes, rows: int, msg_len: int, code_len: int, queries: int,
                            chal_seed: bytes):

@@ -9,6 +9,7 @@
 #include "api.hpp"
 #include "gpt2.hpp"
 #include "protocol.hpp"
+#include "transcript.hpp"
 
 using namespace vzh;
 
@@ -446,6 +447,59 @@ void vzh_fpstream_fp(const uint8_t* seed, uint64_t domain, size_t n, uint64_t* o
 void vzh_fpstream_u64(const uint8_t* seed, uint64_t domain, size_t n, uint64_t* out) {
     FpStream s(seed, domain);
     for (size_t i = 0; i < n; ++i) out[i] = s.next_u64();
+}
+
+// BLAKE3 of `len` bytes: plain hash (context null) or derive-key mode with
+// the given context string (the transcript's binding hash).
+void vzh_blake3(const char* context, const uint8_t* data, size_t len, uint8_t* out) {
+    if (context)
+        blake3_derive_key(context, data, len, out);
+    else
+        blake3_hash(data, len, out);
+}
+
+// Blind LogUp proof (logup.rs:3184-3225 blind_logup_prove) of the resident
+// query column f_col (n_f canonical Fp values), table column t_col (n_t) and
+// u32 multiplicities mult, with a fresh transcript Transcript::new(tx_seed)
+// and the mock correlation stream seeded with corr_seed, domains from
+// dom_base.  Writes the BlindLogupProof wire bytes (model_proof_codec.rs
+// rules) to out (cap bytes; *written), the transcript's canonical binding
+// digest (32 bytes), its charged bytes and the domain cursor after the proof.
+int vzh_blind_logup_prove(void* h, uint64_t f_col, size_t n_f, uint64_t t_col, size_t n_t, uint64_t mult,
+                          const uint8_t* tx_seed, const uint8_t* corr_seed, uint64_t dom_base, uint8_t* out,
+                          size_t cap, size_t* written, uint8_t* digest, uint64_t* tx_bytes, uint64_t* next_dom,
+                          char* err, size_t len) {
+    return guarded(err, len, [&] {
+        Transcript tx(tx_seed);
+        const BlindLogupResult r =
+            blind_logup_prove(*static_cast<Backend*>(h), f_col, n_f, t_col, n_t, mult, corr_seed, dom_base, tx);
+        const std::vector<uint8_t> bytes = encode_blind_logup(r.proof);
+        if (bytes.size() > cap) throw AccelError("blind LogUp proof buffer too small");
+        std::memcpy(out, bytes.data(), bytes.size());
+        *written = bytes.size();
+        tx.binding_digest(digest);
+        *tx_bytes = tx.total_bytes();
+        *next_dom = r.next_domain;
+    });
+}
+
+// Decode and re-encode BlindLogupProof wire bytes (strict: canonical field
+// elements, collection caps, option tags, no trailing bytes); writes the
+// per-layer round counts of both sides (lookup side first) to rounds.
+int vzh_blind_logup_check(const uint8_t* data, size_t n, uint32_t* rounds, size_t rounds_cap, size_t* layers,
+                          char* err, size_t len) {
+    return guarded(err, len, [&] {
+        const BlindLogupProof p = decode_blind_logup(data, n);
+        size_t k = 0;
+        for (const BlindFracProof* side : {&p.lookup, &p.table})
+            for (const BlindLayerProof& l : side->layers) {
+                if (k == rounds_cap) throw AccelError("rounds buffer too small");
+                rounds[k++] = static_cast<uint32_t>(l.round_corrs.size());
+            }
+        *layers = k;
+        if (encode_blind_logup(p) != std::vector<uint8_t>(data, data + n))
+            throw AccelError("blind LogUp proof does not re-encode to its bytes");
+    });
 }
 
 }  // extern "C"

@@ -110,6 +110,8 @@ std::vector<Fp2> logup_local_collect(Backend& b, const PendingLogup& pl);
 // message slots on the host (raw0: the query side, raw1: the table side):
 // alpha, then per side its root and round messages, as logup_prove_resident.
 void logup_proof_words(const PendingLogup& pl, const Fp2* raw0, const Fp2* raw1, std::vector<Fp2>& out);
+// The same, downloading both sides' messages of an enqueued, unsharded proof.
+std::vector<Fp2> logup_local_proof_words(Backend& b, const PendingLogup& pl);
 // The whole LogUp proof (both sides' batches sharing launches, one download
 // per side after everything is enqueued); words as logup_prove_resident.
 std::vector<Fp2> logup_prove_scheduled(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col, size_t n_t,

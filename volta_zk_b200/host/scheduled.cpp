@@ -694,6 +694,13 @@ void logup_proof_words(const PendingLogup& pl, const Fp2* raw0, const Fp2* raw1,
     append_side_proof(pl.sch[1], frac_side_parse(pl.side[1], raw1), out);
 }
 
+std::vector<Fp2> logup_local_proof_words(Backend& b, const PendingLogup& pl) {
+    std::vector<Fp2> proof;
+    proof.push_back(pl.alpha);
+    for (int side = 0; side < 2; ++side) append_side_proof(pl.sch[side], frac_side_collect(b, pl.side[side]), proof);
+    return proof;
+}
+
 std::vector<Fp2> logup_prove_scheduled(Backend& b, uint64_t f_col, size_t n_f, uint64_t t_col, size_t n_t,
                                        uint64_t mult, FpStream& chal) {
     Owned own(b);
