@@ -390,7 +390,8 @@ def logup_step0_replica(be, log2_queries: int, reps: int = 10):
     shapes: step 0 of the query side's cross-layer round batch, i.e. round 0
     on the interleaved children of every layer with more than 2^11 entries
     per vector (layer L: 2 x 2^L children of P and Q, a 2^(L-1)-entry suffix
-    table); the leaf layer's numerators are all 1 and its children are read
+    table, and its parent level, whose even entries are the round's t = 0
+    terms); the leaf layer's numerators are all 1 and its children are read
     from the 8-byte query column.  Returns (average launch ms, algorithmic
     bytes per launch, jobs)."""
     import ctypes as C
@@ -403,20 +404,28 @@ def logup_step0_replica(be, log2_queries: int, reps: int = 10):
         leaf = L == log2_queries - 1
         q = be.alloc((8 if leaf else 16) * 2 * vlen)
         be.call("chacha8_prover_secret_fp_rows_device", q, 0, SUMCHECK_SEED, 100 + L, 1, (2 if leaf else 4) * vlen)
-        p = 0
+        p = pp = pq = 0
         if not leaf:
             p = be.alloc(16 * 2 * vlen)
             be.call("chacha8_prover_secret_fp_rows_device", p, 0, SUMCHECK_SEED, 200 + L, 1, 4 * vlen)
+            pp, pq = be.alloc(16 * vlen), be.alloc(16 * vlen)
+            be.call("chacha8_prover_secret_fp_rows_device", pp, 0, SUMCHECK_SEED, 400 + L, 1, 2 * vlen)
+            be.call("chacha8_prover_secret_fp_rows_device", pq, 0, SUMCHECK_SEED, 500 + L, 1, 2 * vlen)
         s = be.alloc(16 * (vlen // 2))
         be.call("chacha8_prover_secret_fp_rows_device", s, 0, SUMCHECK_SEED, 300 + L, 1, vlen)
-        bufs += [x for x in (p, q, s) if x]
+        bufs += [x for x in (p, q, s, pp, pq) if x]
         j = RoundJob()
-        j.kind, j.flags, j.len = 0, 3 if leaf else 0, vlen
+        # leaf: all-one numerators, children from the query column; else parents given
+        j.kind, j.flags, j.len = 0, 3 if leaf else 4, vlen
         j.q_alpha[0], j.q_alpha[1] = 5, 7
         j.in_id[0], j.in_id[1] = p, q
+        if not leaf:
+            j.out_id[0], j.out_id[1] = pp, pq
         j.s_id, j.msg_id, j.msg_offset = s, msg, 4 * len(jobs)
         jobs.append(j)
-        nbytes += (16 * vlen if leaf else 64 * vlen) + 16 * (vlen // 2)
+        # children (P and Q: 64 B per pair; the leaf column: 16 B), the even
+        # parents (2 x 16 B per pair) and the suffix table (16 B per pair)
+        nbytes += (16 * vlen if leaf else 64 * vlen + 16 * vlen) + 16 * (vlen // 2)
     arr = (RoundJob * len(jobs))(*jobs)
     call = lambda: be.check(be.lib.volta_b200_logup_round_batch_device(be.ctx, C.cast(arr, C.c_void_p), len(jobs)),
                             "logup_round_batch")  # noqa: E731

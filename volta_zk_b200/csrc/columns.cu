@@ -197,8 +197,73 @@ __global__ void histogram_kernel(const uint64_t* in, uint32_t* out, size_t n, si
     }
 }
 
+// Tables of up to 2^16 bins (the u16 lookup tables and 16-bit ranges): two
+// 16-bit counters per shared-memory word, 128 KB for 2^16 bins.  A CTA
+// counts a contiguous slice of the column in chunks of kPackedChunk
+// elements and adds its nonzero counters to the global table after each
+// chunk, so no counter can pass 65535 and wrap.
+constexpr size_t kPackedBins = size_t{1} << 16;
+constexpr unsigned kPackedThreads = 1024;
+constexpr size_t kPackedChunk = 63 * kPackedThreads;  // <= 65535 elements per flush
+
+__global__ void __launch_bounds__(kPackedThreads) histogram_packed_kernel(const uint64_t* in, uint32_t* out, size_t n,
+                                                                         size_t bins, int mode, int signed_input) {
+    extern __shared__ uint32_t sm_pair[];
+    const size_t words = (bins + 1) / 2;
+    for (size_t w = threadIdx.x; w < words; w += blockDim.x) sm_pair[w] = 0;
+    const size_t per = (n + gridDim.x - 1) / gridDim.x;
+    const size_t begin = min(n, per * blockIdx.x), end = min(n, begin + per);
+    const unsigned lane = threadIdx.x & 31;
+    for (size_t chunk = begin; chunk < end; chunk += kPackedChunk) {
+        __syncthreads();  // counters zeroed (first chunk) or flushed
+        const size_t stop = min(end, chunk + kPackedChunk);
+        for (size_t base = chunk + (threadIdx.x & ~31u); base < stop; base += blockDim.x) {
+            const size_t i = base + lane;
+            bool ok = i < stop;
+            uint32_t bin = 0;
+            if (ok) {
+                const uint64_t v = __ldcs(in + i);
+                if (mode == 0) {
+                    ok = v < bins;
+                    bin = static_cast<uint32_t>(v);
+                } else {
+                    bin = lut_bin(v, signed_input, ok);
+                }
+            }
+            const uint32_t first = __shfl_sync(0xffffffffu, bin, 0);
+            const unsigned ok_mask = __ballot_sync(0xffffffffu, ok);
+            if (__all_sync(0xffffffffu, ok && bin == first)) {
+                if (lane == 0) atomicAdd(sm_pair + (first >> 1), 32u << (16 * (first & 1)));
+            } else if (ok) {
+                const unsigned peers = __match_any_sync(ok_mask, bin);
+                if (lane == static_cast<unsigned>(__ffs(peers) - 1))
+                    atomicAdd(sm_pair + (bin >> 1), static_cast<uint32_t>(__popc(peers)) << (16 * (bin & 1)));
+            }
+        }
+        __syncthreads();
+        for (size_t w = threadIdx.x; w < words; w += blockDim.x) {
+            const uint32_t v = sm_pair[w];
+            if (!v) continue;
+            sm_pair[w] = 0;
+            if (v & 0xFFFFu) atomicAdd(out + 2 * w, v & 0xFFFFu);
+            if (v >> 16) atomicAdd(out + 2 * w + 1, v >> 16);
+        }
+    }
+}
+
 int launch_histogram(Context* c, const uint64_t* in, uint32_t* out, size_t n, size_t bins, int mode,
                      int signed_input) {
+    if (bins > kSmemBins && bins <= kPackedBins && n >= 4 * kPackedChunk) {
+        // one CTA per SM (128 KB of counters), each a contiguous slice
+        const size_t smem = (bins + 1) / 2 * sizeof(uint32_t);
+        VZB_CUDA(c, cudaFuncSetAttribute(histogram_packed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+        const unsigned blocks = static_cast<unsigned>(
+            std::max<size_t>(1, std::min<size_t>(static_cast<size_t>(c->sm_count), n / kPackedChunk)));
+        histogram_packed_kernel<<<blocks, kPackedThreads, smem, c->stream>>>(in, out, n, bins, mode, signed_input);
+        VZB_LAUNCHED(c);
+        return 0;
+    }
     if (bins <= kSmemBins) {
         // one flush of `bins` atomics per block: at most one block per 8 x
         // bins elements, up to two 1024-thread blocks per SM

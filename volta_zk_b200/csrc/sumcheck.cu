@@ -1936,16 +1936,23 @@ struct MsgStoreEpi {
 
 // CTA b runs the job whose range holds b: a grid-stride loop over that
 // job's items with the job's own CTA count as the stride, then the job's
-// grid reduction.  Fold-only jobs skip the reduction.
-__global__ void __launch_bounds__(kReduceThreads, 2) logup_round_batch_kernel(const __grid_constant__ RoundBatch batch,
-                                                                          Fp2* partials, unsigned* counters) {
+// grid reduction.  Fold-only jobs skip the reduction.  kRound0: every job
+// is a round-0 step (kind 0), whose evaluators fit 96 registers: five
+// 128-thread CTAs (20 warps) share an SM instead of the 16 warps that the
+// fold evaluators' 128 registers allow.
+constexpr unsigned kRound0Threads = 128;
+constexpr unsigned kRound0Ctas = 5;
+
+template <bool kRound0>
+__global__ void __launch_bounds__(kRound0 ? kRound0Threads : kReduceThreads, kRound0 ? kRound0Ctas : 2)
+    logup_round_batch_kernel(const __grid_constant__ RoundBatch batch, Fp2* partials, unsigned* counters) {
     unsigned j = 0;
     while (j + 1 < batch.count && blockIdx.x >= batch.job[j + 1].block0) ++j;
     const BatchJob& jb = batch.job[j];
     const unsigned bidx = blockIdx.x - jb.block0;
     const size_t stride = static_cast<size_t>(jb.blocks) * blockDim.x;
     const size_t first = static_cast<size_t>(bidx) * blockDim.x + threadIdx.x;
-    if (jb.kind == kBatchFold) {
+    if (!kRound0 && jb.kind == kBatchFold) {
         for (size_t i = first; i < jb.items; i += stride) {
             Fp2 x0, x1;
             if (jb.p_one) {
@@ -1966,7 +1973,21 @@ __global__ void __launch_bounds__(kReduceThreads, 2) logup_round_batch_kernel(co
     Fp2W w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) f2w_zero(w[k]);
-    if (jb.q_col) {
+    if (kRound0) {
+        if (jb.q_col) {
+            const QColEvalIL ev{jb.col, jb.s, jb.a0, jb.a1, jb.w7a1sq};
+            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+        } else if (jb.p_one) {
+            const QEvalIL ev{jb.in1, jb.s};
+            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+        } else if (jb.parents) {
+            const LogupEvalILPar ev{jb.in0, jb.in1, jb.s, jb.pp, jb.pq};
+            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+        } else {
+            const LogupEvalIL ev{jb.in0, jb.in1, jb.s};
+            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
+        }
+    } else if (jb.q_col) {
         if (jb.kind == kBatchRoundIL) {
             const QColEvalIL ev{jb.col, jb.s, jb.a0, jb.a1, jb.w7a1sq};
             for (size_t i = first; i < jb.items; i += stride) ev(i, w);
@@ -2089,12 +2110,15 @@ extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_jo
         total += d.items;
     }
     // CTAs in proportion to the items (at least one per job, at most one
-    // per kReduceThreads items), about 4 per SM in all
-    const size_t target = static_cast<size_t>(c->sm_count) * 4;
+    // per thread block of items), two waves of the resident CTAs in all
+    bool round0 = true;
+    for (size_t j = 0; j < count; ++j) round0 = round0 && batch.job[j].kind == kBatchRoundIL;
+    const unsigned threads = round0 ? kRound0Threads : kReduceThreads;
+    const size_t target = static_cast<size_t>(c->sm_count) * (round0 ? 2 * kRound0Ctas : 4);
     uint32_t next = 0;
     for (size_t j = 0; j < count; ++j) {
         BatchJob& d = batch.job[j];
-        const size_t need = (d.items + kReduceThreads - 1) / kReduceThreads;
+        const size_t need = (d.items + threads - 1) / threads;
         size_t share = (target * d.items + total - 1) / total;
         if (share < 1) share = 1;
         d.block0 = next;
@@ -2105,8 +2129,12 @@ extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_jo
     if (static_cast<size_t>(next) * 4 > static_cast<size_t>(c->sm_count) * 8 * 9)
         return fail_message(c, "LogUp round batch exceeds the reduction workspace");
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    logup_round_batch_kernel<<<next, kReduceThreads, 0, c->stream>>>(batch, ws<Fp2>(c, kWsPartials),
-                                                                     ws<unsigned>(c, kWsCounter) + kBatchCounterBase);
+    if (round0)
+        logup_round_batch_kernel<true><<<next, kRound0Threads, 0, c->stream>>>(
+            batch, ws<Fp2>(c, kWsPartials), ws<unsigned>(c, kWsCounter) + kBatchCounterBase);
+    else
+        logup_round_batch_kernel<false><<<next, kReduceThreads, 0, c->stream>>>(
+            batch, ws<Fp2>(c, kWsPartials), ws<unsigned>(c, kWsCounter) + kBatchCounterBase);
     VZB_LAUNCHED(c);
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpLogup, 0, 0);
