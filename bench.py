@@ -385,6 +385,13 @@ class RoundJob(__import__("ctypes").Structure):
                 ("q_alpha", _C.c_uint64 * 2)]
 
 
+# DRAM read + write bytes per algorithmic byte of the step-0 replica, from an
+# ncu capture of the 2^22-query replica (mean of its 13 launches: 268,123,077 B
+# read + 1,230,021 B written for 234,520,576 algorithmic bytes; the parents
+# are read at stride 2, so their whole level crosses DRAM)
+LOGUP_REPLICA_TRAFFIC = (268123077 + 1230021) / 234520576
+
+
 def logup_step0_replica(be, log2_queries: int, reps: int = 10):
     """The proof's largest launch, replicated on seeded data of the same
     shapes: step 0 of the query side's cross-layer round batch, i.e. round 0
@@ -399,7 +406,7 @@ def logup_step0_replica(be, log2_queries: int, reps: int = 10):
     jobs, bufs, nbytes = [], [], 0
     msg = be.alloc(16 * 4 * 32)
     bufs.append(msg)
-    for L in range(12, log2_queries):
+    for L in range(min(12, log2_queries - 1), log2_queries):  # at least the leaf layer on small cases
         vlen = 1 << L
         leaf = L == log2_queries - 1
         q = be.alloc((8 if leaf else 16) * 2 * vlen)
@@ -608,9 +615,7 @@ def config1_leg(args, rank, world, local_rank, dist, prover, peaks, timed_steps=
     peak = peaks.get("hbm_gbs", 6650.0)
     batch_ms, batch_bytes, batch_jobs = logup_step0_replica(be, args.log2_queries)
     achieved = batch_bytes / (batch_ms / 1e3) / 1e9
-    # DRAM read + write bytes per algorithmic byte of this launch, from the ncu
-    # capture of the 2^22-query replica of the same launch
-    traffic_ratio = (201.150720e6 + 3.792640e6) / 201031680
+    traffic_ratio = LOGUP_REPLICA_TRAFFIC
     roofline = {"bound": "hbm",
                 "kernel": f"logup_round_batch_kernel: step 0 of the 2^{args.log2_queries}-query side "
                           f"({batch_jobs} layers in one launch, the proof's largest launch)",
@@ -843,7 +848,7 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
     peak = peaks.get("hbm_gbs", 6650.0)
     batch_ms, batch_bytes, batch_jobs = logup_step0_replica(be, 24)
     achieved = batch_bytes / (batch_ms / 1e3) / 1e9
-    traffic_ratio = (201.150720e6 + 3.792640e6) / 201031680
+    traffic_ratio = LOGUP_REPLICA_TRAFFIC
     roofline = {"bound": "hbm",
                 "kernel": f"logup_round_batch_kernel: step 0 of a 2^24-query side ({batch_jobs} layers in one launch, "
                           "the shape of the attention-rectangle lookup instances)",

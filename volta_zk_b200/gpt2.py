@@ -324,3 +324,32 @@ class Gpt2Prover:
         attn_block_out, 4 ffn_block_out) of `layer`, t x d u64."""
         buf = int(self.host.vzh_gpt2_correction(self.h, layer, wire))
         return self.s.be.download(buf, self.s.t * D * 8, dtype=np.uint64)
+
+
+def main(argv=None):
+    """One GPT-2 small prefill proof on the first GPU: the synthetic model, the
+    witness forward of `--tokens` prefill tokens and the proof of every layer
+    plus the weight commitment (`--proofs` times); prints the proof digest."""
+    import argparse
+    import hashlib
+
+    from . import accel
+
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("--tokens", type=int, default=1024)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--proofs", type=int, default=1)
+    args = ap.parse_args(argv)
+    model = synthetic_model(n_layers=args.layers)
+    seeds = bytes([0x50] * 32), bytes([0x4D] * 32), bytes([0x11] * 32)
+    with accel.Prover(policy=1) as prover, Gpt2Session(prover, model, args.tokens) as s, Gpt2Prover(s) as gp:
+        s.forward(prefill_tokens(args.tokens))
+        for _ in range(args.proofs):
+            s.forward()
+            words, per_layer, root = gp.prove(*seeds)
+    print(f"proof words {words.shape[0]} ({per_layer} per layer), sha256 "
+          f"{hashlib.sha256(words.tobytes() + root).hexdigest()[:16]}")
+
+
+if __name__ == "__main__":
+    main()
