@@ -370,6 +370,16 @@ int volta_b200_embed_i16_device(void* ctx, uint64_t in_id, size_t in_offset, uin
                                 size_t n);
 
 /*
+ * Greedy token selection of KV-cached decoding (rust/volta-gpt2/src/decode.rs:
+ * 270-272 argmax): the index of the largest of n i64 values, the last one
+ * among equal maxima (Iterator::max_by_key), written as a u32 token id at
+ * (out_id, out_offset) so the next decode step embeds it without a host
+ * round trip.
+ */
+int volta_b200_argmax_i64_device(void* ctx, uint64_t in_id, size_t in_offset, size_t n, uint64_t out_id,
+                                 size_t out_offset);
+
+/*
  * Softmax witness columns of the GPT-2 layer proof, from the forward's
  * causal-packed wires (scores_q, exp_out, weights: heads * rows(rows+1)/2
  * int16; row_shift, recips: heads * rows int16; denoms: heads * rows int64).

@@ -93,6 +93,99 @@ def forward_model(ops, tokens, model, luts, row_shift=1):
     return out
 
 
+def _tri(x):
+    return x * (x + 1) // 2
+
+
+def band_witness(ops, full, model, luts, t0):
+    """band_model_witness (rust/volta-gpt2/src/band.rs:77-196) from a
+    forward_model result over t rows: row-local wires sliced to rows t0 .. t-1,
+    the per-head causal-packed wires repacked to the band (head h keeps rows
+    t0 .. t-1 with their windows t0 + i + 1), the per-head row tables cut to
+    h x q, the final LayerNorm over every band row of the last layer's output
+    and the logits of every band row."""
+    t = np.asarray(full["embed_out"]).size // D
+    q = t - t0
+    vocab = model.wte.shape[0]
+
+    def rows(a):
+        a = np.asarray(a).reshape(-1)
+        width = a.size // t
+        return a[t0 * width:t * width]
+
+    layers = []
+    for r in full["layers"]:
+        b = {}
+        for name, v in r.items():
+            if name == "errors":
+                continue
+            if name in ("scores_acc", "scores_q", "exp_out", "weights"):
+                b[name] = np.asarray(v).reshape(H, _tri(t))[:, _tri(t0):].reshape(-1)
+            elif name in ("row_shift", "denoms", "recips"):
+                b[name] = np.asarray(v).reshape(H, t)[:, t0:].reshape(-1)
+            else:
+                b[name] = rows(v)
+        layers.append(b)
+    x_fin = np.ascontiguousarray(rows(full["layers"][-1]["ffn_block_out"]))
+    fin = ops.layer_norm(x_fin, model.lnf_gain, model.lnf_bias, luts["ln_rsqrt"], q, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
+    logits = ops.logits(fin[5], model.wte, q, D, vocab)
+    return {"layers": layers, "fin": fin[:6], "fin_error": fin[6], "logits": np.asarray(logits).reshape(q, vocab),
+            "embed_out": rows(full["embed_out"])}
+
+
+def argmax_last(x):
+    """decode.rs:270-272: Iterator::max_by_key returns the last of equal maxima."""
+    x = np.asarray(x)
+    return int(x.size - 1 - int(np.argmax(x[::-1])))
+
+
+def decode_step(ops, model, luts, cache, token, pos, row_shift=1):
+    """decode_step (rust/volta-gpt2/src/decode.rs:137-268) on the oracle's
+    primitives: one new row at position pos; its K/V rows are appended to
+    `cache` ({"k": [per layer], "v": [per layer]}, pos rows each) before the
+    attention over rows 0 .. pos.  Returns (logits row, error flags)."""
+    vocab = model.wte.shape[0]
+    _, x, e = ops.embed(np.array([token], np.uint32), model.wte, model.wpe, 1, D, vocab, model.wpe.shape[0], pos, 0)
+    errs = [e]
+    for l, lw in enumerate(model.layers):
+        ln1 = ops.layer_norm(x, lw["ln1_gain"], lw["ln1_bias"], luts["ln_rsqrt"], 1, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
+        _, qkv_q, _, e1 = ops.gemm(ln1[5], lw["c_attn"], None, None, 1, D, 3 * D, SHIFT_QKV)
+        q, k, v = ops.qkv_split(qkv_q, 1, D)
+        cache["k"][l] = np.concatenate([cache["k"][l], k])
+        cache["v"][l] = np.concatenate([cache["v"][l], v])
+        _, s_q, e2 = ops.scores(q, cache["k"][l], 1, pos + 1, pos, H, DH, SHIFT_SCORES)
+        _, _, _, _, wts, e3 = ops.softmax(s_q, luts["exp"], luts["softmax_recip"], 1, pos, H, RECIP_DEN_SHIFT,
+                                          RECIP_LOG2, SHIFT_SOFTMAX_NORM, row_shift)
+        _, av_q, e4 = ops.av(wts, cache["v"][l], 1, pos + 1, pos, D, H, SHIFT_AV)
+        _, _, attn_out, e5 = ops.gemm(av_q, lw["attn_proj"], None, x, 1, D, D, SHIFT_ATTN_PROJ)
+        ln2 = ops.layer_norm(attn_out, lw["ln2_gain"], lw["ln2_bias"], luts["ln_rsqrt"], 1, D, LN_VAR_SHIFT,
+                             SHIFT_LN_NORM)
+        _, up_q, _, e6 = ops.gemm(ln2[5], lw["ffn_up"], None, None, 1, D, DFF, SHIFT_FFN_UP)
+        gelu = ops.lookup(up_q, luts["gelu"])
+        _, _, x, e7 = ops.gemm(gelu, lw["ffn_down"], None, attn_out, 1, DFF, D, SHIFT_FFN_DOWN)
+        errs += [ln1[6], e1, e2, e3, e4, e5, ln2[6], e6, e7]
+    fin = ops.layer_norm(x, model.lnf_gain, model.lnf_bias, luts["ln_rsqrt"], 1, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
+    errs.append(fin[6])
+    return np.asarray(ops.logits(fin[5], model.wte, 1, D, vocab)).reshape(-1), errs
+
+
+def generate(ops, model, luts, k_rows, v_rows, t0, logits_t0, n, row_shift=1):
+    """generate (decode.rs:278-300): greedy steps after a prefill of t0 rows
+    whose per-layer K/V (t0 x D) and last-position logits are given.  Returns
+    (tokens, logits rows, cache)."""
+    cache = {"k": [np.asarray(k).reshape(-1)[:t0 * D].copy() for k in k_rows],
+             "v": [np.asarray(v).reshape(-1)[:t0 * D].copy() for v in v_rows]}
+    tokens, rows, errs = [], [], []
+    nxt = argmax_last(logits_t0)
+    for i in range(n):
+        tokens.append(nxt)
+        lg, e = decode_step(ops, model, luts, cache, nxt, t0 + i, row_shift)
+        rows.append(lg)
+        errs += e
+        nxt = argmax_last(lg)
+    return tokens, np.stack(rows), cache, errs
+
+
 class OracleOps:
     def __init__(self, o):
         self.o = o

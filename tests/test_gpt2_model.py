@@ -94,3 +94,62 @@ def test_oracle_forward_matches_reference_mirror_t16(oracle, model, package_buil
     bad = mismatches(golden(t), res["embed_out"], lambda l, k: res["layers"][l][k], res["final_ln_out"],
                      res["logits"])
     assert not bad, bad
+
+
+@pytest.fixture(scope="module")
+def model2():
+    from volta_zk_b200 import gpt2
+
+    return gpt2.synthetic_model(n_layers=2)
+
+
+def test_oracle_decode_equals_the_full_forward(oracle, model2, package_built):
+    """decode.rs's own invariant (decode_matches_full_forward) on the oracle:
+    greedy KV-cached steps after a prefill give the same logits rows and K/V
+    rows as full forwards over the growing sequence (2-layer synthetic model)."""
+    from oracle.gpt2 import argmax_last, generate
+    from volta_zk_b200 import gpt2
+
+    ops, luts = OracleOps(oracle), gpt2.build_luts()
+    t0, n = 6, 3
+    tokens = list(gpt2.prefill_tokens(t0))
+    pre = forward_model(ops, np.array(tokens, np.uint32), model2, luts, row_shift=1)
+    gen, rows, cache, errs = generate(ops, model2, luts, [r["k"] for r in pre["layers"]],
+                                      [r["v"] for r in pre["layers"]], t0, pre["logits"], n)
+    assert all(e == 0 for e in errs)
+    assert gen[0] == argmax_last(pre["logits"])
+    seq = tokens
+    for i in range(n):
+        seq = seq + [gen[i]]
+        full = forward_model(ops, np.array(seq, np.uint32), model2, luts, row_shift=1)
+        assert np.array_equal(np.asarray(full["logits"]).reshape(-1), rows[i]), i
+        for l in range(2):
+            assert np.array_equal(cache["k"][l][:len(seq) * 768], np.asarray(full["layers"][l]["k"]).reshape(-1))
+            assert np.array_equal(cache["v"][l][:len(seq) * 768], np.asarray(full["layers"][l]["v"]).reshape(-1))
+        if i + 1 < n:
+            assert gen[i + 1] == argmax_last(rows[i])
+
+
+def test_oracle_band_witness_invariants(oracle, model2, package_built):
+    """band.rs's band_extraction_consistency on the oracle: band windows, and
+    the band's last logits / final-LN row equal the full forward's."""
+    from oracle.gpt2 import band_witness
+    from volta_zk_b200 import gpt2
+
+    ops, luts = OracleOps(oracle), gpt2.build_luts()
+    t, t0 = 9, 5
+    full = forward_model(ops, gpt2.prefill_tokens(t), model2, luts, row_shift=1)
+    band = band_witness(ops, full, model2, luts, t0)
+    q = t - t0
+    assert band["layers"][0]["scores_q"].size == 12 * sum(t0 + r + 1 for r in range(q))
+    assert np.array_equal(band["logits"][-1], np.asarray(full["logits"]).reshape(-1))
+    assert np.array_equal(band["fin"][5][-768:], np.asarray(full["final_ln_out"]).reshape(-1))
+    assert np.array_equal(band["layers"][1]["k"], np.asarray(full["layers"][1]["k"]).reshape(-1)[t0 * 768:])
+
+
+def test_argmax_keeps_the_last_maximum():
+    from oracle.gpt2 import argmax_last
+
+    assert argmax_last([1, 5, 3, 5, 2]) == 3
+    assert argmax_last([7]) == 0
+    assert argmax_last([-4, -4]) == 1

@@ -608,3 +608,77 @@ extern "C" int volta_cuda_fixed_logits_device(void* raw, uint64_t input_id, size
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpGemm, 0, 0);
 }
+
+// ---------------------------------------------------------------------------
+// Extension: greedy token selection (rust/volta-gpt2/src/decode.rs:270-272,
+// argmax by Iterator::max_by_key, which returns the LAST of equal maxima)
+// ---------------------------------------------------------------------------
+
+namespace vzb {
+namespace {
+
+// One CTA: (value, index) pairs reduced with "greater value, or equal value
+// and larger index" wins.
+__global__ void __launch_bounds__(1024) argmax_last_kernel(const int64_t* __restrict__ x, size_t n,
+                                                           uint32_t* __restrict__ out) {
+    __shared__ int64_t sv[32];
+    __shared__ uint32_t si[32];
+    int64_t bv = INT64_MIN;
+    uint32_t bi = 0;
+    for (size_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const int64_t v = x[i];
+        if (v >= bv) {  // indices grow along a thread's walk: >= keeps the last
+            bv = v;
+            bi = static_cast<uint32_t>(i);
+        }
+    }
+    auto better = [](int64_t va, uint32_t ia, int64_t vb, uint32_t ib) { return vb > va || (vb == va && ib > ia); };
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+        const int64_t ov = __shfl_down_sync(0xffffffffu, bv, d);
+        const uint32_t oi = __shfl_down_sync(0xffffffffu, bi, d);
+        if (better(bv, bi, ov, oi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int warps = (blockDim.x + 31) >> 5;
+        bv = lane < warps ? sv[lane] : INT64_MIN;
+        bi = lane < warps ? si[lane] : 0;
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            const int64_t ov = __shfl_down_sync(0xffffffffu, bv, d);
+            const uint32_t oi = __shfl_down_sync(0xffffffffu, bi, d);
+            if (better(bv, bi, ov, oi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) *out = bi;
+    }
+}
+
+}  // namespace
+}  // namespace vzb
+
+extern "C" int volta_b200_argmax_i64_device(void* raw, uint64_t in_id, size_t in_off, size_t n, uint64_t out_id,
+                                            size_t out_off) {
+    using namespace vzb;
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !n || n > 0xFFFFFFFFull) return fail_message(c, "invalid argmax geometry");
+    const int64_t* x = nullptr;
+    uint32_t* out = nullptr;
+    if (VZB_REGION(in_id, in_off, n, int64_t, x) || VZB_REGION(out_id, out_off, 1, uint32_t, out)) return -1;
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    argmax_last_kernel<<<1, 1024, 0, c->stream>>>(x, n, out);
+    VZB_LAUNCHED(c);
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpGemm, 0, 0);
+}

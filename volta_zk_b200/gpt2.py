@@ -261,6 +261,162 @@ class Gpt2Session:
     def layer_errors(self):
         return [int(self.wire(l, "error")[0]) for l in range(LAYERS)]
 
+    def band(self, t0: int) -> "Gpt2Band":
+        """The band witness of rows t0 .. t-1 of the last forward (built)."""
+        return Gpt2Band(self, t0)
+
+    def decoder(self, max_steps: int = 0) -> "Gpt2Decoder":
+        """KV-cached greedy decoding after the last forward (at most max_steps
+        steps; 0: up to the last position)."""
+        return Gpt2Decoder(self, max_steps)
+
+
+def _bind_decode(L):
+    vp, sz, u64 = C.c_void_p, C.c_size_t, C.c_uint64
+    L.vzh_gpt2_band_open.restype = vp
+    L.vzh_gpt2_band_open.argtypes = [vp, sz, C.c_char_p, sz]
+    L.vzh_gpt2_band_close.argtypes = [vp]
+    L.vzh_gpt2_band_build.argtypes = [vp, C.c_char_p, sz]
+    L.vzh_gpt2_band_buffer.argtypes = [vp, sz, C.c_int, C.POINTER(u64), C.POINTER(sz), C.c_char_p, sz]
+    L.vzh_gpt2_decoder_open.restype = vp
+    L.vzh_gpt2_decoder_open.argtypes = [vp, sz, C.c_char_p, sz]
+    L.vzh_gpt2_decoder_close.argtypes = [vp]
+    L.vzh_gpt2_decode.argtypes = [vp, sz, C.c_char_p, sz]
+    L.vzh_gpt2_decoder_buffer.restype = u64
+    L.vzh_gpt2_decoder_buffer.argtypes = [vp, sz, C.c_int]
+
+
+def band_dtype_count(name: str, t0: int, q: int):
+    """Element type and count of a band wire (band.rs:112-150 layouts)."""
+    bc = HEADS * (q * t0 + q * (q + 1) // 2)
+    packed = {"scores_acc": np.int64, "scores_q": np.int16, "exp_out": np.int16, "weights": np.int16}
+    tables = {"row_shift": np.int16, "denoms": np.int64, "recips": np.int16}
+    if name in packed:
+        return packed[name], bc
+    if name in tables:
+        return tables[name], HEADS * q
+    return wire_dtype_count(name, q)
+
+
+class Gpt2Band:
+    """Band witness (rust/volta-gpt2/src/band.rs:77-196): rows t0 .. t-1 of a
+    session's forward, the per-head packed wires in band packing, the final
+    LayerNorm and the logits of every band row."""
+
+    def __init__(self, session: Gpt2Session, t0: int):
+        from . import accel
+
+        self.s, self.t0, self.q = session, t0, session.t - t0
+        self.L = session.host
+        _bind_decode(self.L)
+        err = C.create_string_buffer(1024)
+        self.h = self.L.vzh_gpt2_band_open(session.h, t0, err, 1024)
+        if not self.h:
+            raise accel.AccelError(err.value.decode())
+        self._check(self.L.vzh_gpt2_band_build(self.h, err, 1024), err)
+
+    @staticmethod
+    def _check(rc, err):
+        from . import accel
+
+        if rc != 0:
+            raise accel.AccelError(err.value.decode())
+
+    def close(self):
+        if self.h:
+            self.L.vzh_gpt2_band_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _buffer(self, layer, which):
+        bid, off = C.c_uint64(), C.c_size_t()
+        err = C.create_string_buffer(1024)
+        self._check(self.L.vzh_gpt2_band_buffer(self.h, C.c_size_t(layer if layer is not None else 2**64 - 1), which,
+                                                C.byref(bid), C.byref(off), err, 1024), err)
+        return bid.value, off.value
+
+    def wire(self, layer: int, name: str) -> np.ndarray:
+        dtype, count = band_dtype_count(name, self.t0, self.q)
+        bid, off = self._buffer(layer, WIRES.index(name))
+        size = np.dtype(dtype).itemsize
+        return self.s.be.download(bid, count * size, dtype=dtype, offset_bytes=off * size)
+
+    def final_ln(self, which: int) -> np.ndarray:
+        """0 mean, 1 var, 2 rsqrt input, 3 rsqrt output, 4 acc, 5 out, over the q rows."""
+        q = self.q
+        dt, n = [(np.int64, q), (np.int64, q), (np.int64, q), (np.int16, q), (np.int64, q * D), (np.int16, q * D)][which]
+        bid, _ = self._buffer(None, which)
+        return self.s.be.download(bid, n * np.dtype(dt).itemsize, dtype=dt)
+
+    def logits(self) -> np.ndarray:
+        bid, _ = self._buffer(None, 6)
+        return self.s.be.download(bid, self.q * VOCAB * 8, dtype=np.int64).reshape(self.q, VOCAB)
+
+    def error_word(self) -> int:
+        bid, _ = self._buffer(None, 7)
+        return int(self.s.be.download(bid, 4, dtype=np.uint32)[0])
+
+
+class Gpt2Decoder:
+    """KV-cached greedy decoding (rust/volta-gpt2/src/decode.rs:80-300) on
+    the device: the caches start from the session's K/V rows, every step runs
+    the model on one new row and picks the next token on the device."""
+
+    def __init__(self, session: Gpt2Session, max_steps: int = 0):
+        from . import accel
+
+        self.s = session
+        self.L = session.host
+        _bind_decode(self.L)
+        err = C.create_string_buffer(1024)
+        self.h = self.L.vzh_gpt2_decoder_open(session.h, max_steps, err, 1024)
+        if not self.h:
+            raise accel.AccelError(err.value.decode())
+        self.generated = 0
+
+    def close(self):
+        if self.h:
+            self.L.vzh_gpt2_decoder_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def generate(self, n: int):
+        """Enqueue n more greedy steps (nothing is downloaded)."""
+        from . import accel
+
+        err = C.create_string_buffer(1024)
+        if self.L.vzh_gpt2_decode(self.h, n, err, 1024) != 0:
+            raise accel.AccelError(err.value.decode())
+        self.generated += n
+
+    def tokens(self) -> np.ndarray:
+        """The generated tokens so far (token i was fed to step i)."""
+        buf = int(self.L.vzh_gpt2_decoder_buffer(self.h, 0, 0))
+        return self.s.be.download(buf, 4 * self.generated, dtype=np.uint32)
+
+    def logits(self) -> np.ndarray:
+        """Step i's logits row (the row that sampled token i + 1)."""
+        buf = int(self.L.vzh_gpt2_decoder_buffer(self.h, 0, 1))
+        return self.s.be.download(buf, 8 * self.generated * VOCAB, dtype=np.int64).reshape(self.generated, VOCAB)
+
+    def cache(self, layer: int, kv: int, rows: int) -> np.ndarray:
+        buf = int(self.L.vzh_gpt2_decoder_buffer(self.h, layer, 3 + kv))
+        return self.s.be.download(buf, 2 * rows * D, dtype=np.int16)
+
+    def error_word(self) -> int:
+        buf = int(self.L.vzh_gpt2_decoder_buffer(self.h, 0, 2))
+        return int(self.s.be.download(buf, 4, dtype=np.uint32)[0])
+
 
 class Gpt2Prover:
     """The prefill proof schedule over a Gpt2Session's witness

@@ -147,6 +147,8 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         reinterpret_cast<decltype(ext_loaded_->product_tail)>(dlsym(handle_, "volta_b200_product_tail_device"));
     ext_loaded_->pack_pair_column = reinterpret_cast<decltype(ext_loaded_->pack_pair_column)>(
         dlsym(handle_, "volta_b200_pack_pair_column_device"));
+    ext_loaded_->argmax_i64 =
+        reinterpret_cast<decltype(ext_loaded_->argmax_i64)>(dlsym(handle_, "volta_b200_argmax_i64_device"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

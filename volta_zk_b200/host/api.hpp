@@ -40,6 +40,7 @@ struct ExtApi {
     decltype(&::volta_b200_pack_pair_column_device) pack_pair_column = nullptr;
     decltype(&::volta_b200_product_fold_round_into_device) product_fold_round = nullptr;
     decltype(&::volta_b200_product_tail_device) product_tail = nullptr;
+    decltype(&::volta_b200_argmax_i64_device) argmax_i64 = nullptr;
 };
 
 }  // namespace vzh

@@ -427,6 +427,80 @@ int vzh_gpt2_prove_layers(void* p, const uint8_t* seed, const uint8_t* mac_seed,
     });
 }
 
+// Band witness of rows t0 .. t-1 of a session's last forward (band.rs).
+void* vzh_gpt2_band_open(void* session, size_t t0, char* err, size_t len) {
+    try {
+        return new Gpt2Band(*static_cast<Gpt2Session*>(session), t0);
+    } catch (const std::exception& e) {
+        fail(err, len, e.what());
+    } catch (...) {
+        fail(err, len, "unknown C++ exception");
+    }
+    return nullptr;
+}
+
+void vzh_gpt2_band_close(void* b) { delete static_cast<Gpt2Band*>(b); }
+
+int vzh_gpt2_band_build(void* b, char* err, size_t len) {
+    return guarded(err, len, [&] { static_cast<Gpt2Band*>(b)->build(); });
+}
+
+// Buffer id and element offset of band wire w of layer l; for l == SIZE_MAX:
+// 0..5 final LN (mean, var, rin, rout, acc, out), 6 logits (q x vocab), 7 the
+// band's error word (offset 0).
+int vzh_gpt2_band_buffer(void* b, size_t layer, int which, uint64_t* id, size_t* offset, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        const Gpt2Band& g = *static_cast<Gpt2Band*>(b);
+        *offset = 0;
+        if (layer != SIZE_MAX) {
+            const auto w = g.wire(layer, which);
+            *id = w.first;
+            *offset = w.second;
+        } else if (which >= 0 && which <= 5) {
+            *id = g.final_ln(which);
+        } else if (which == 6) {
+            *id = g.logits();
+        } else if (which == 7) {
+            *id = g.error_word();
+        } else {
+            throw AccelError("unknown band buffer");
+        }
+    });
+}
+
+// KV-cached greedy decoding after a session's forward (decode.rs).
+void* vzh_gpt2_decoder_open(void* session, size_t max_steps, char* err, size_t len) {
+    try {
+        return new Gpt2Decoder(*static_cast<Gpt2Session*>(session), max_steps);
+    } catch (const std::exception& e) {
+        fail(err, len, e.what());
+    } catch (...) {
+        fail(err, len, "unknown C++ exception");
+    }
+    return nullptr;
+}
+
+void vzh_gpt2_decoder_close(void* d) { delete static_cast<Gpt2Decoder*>(d); }
+
+int vzh_gpt2_decode(void* d, size_t n, char* err, size_t len) {
+    return guarded(err, len, [&] { static_cast<Gpt2Decoder*>(d)->generate(n); });
+}
+
+// 0 tokens (u32), 1 logits rows (i64), 2 error word, 3 K cache of `layer`,
+// 4 V cache of `layer`; 5 the next position (not an id).
+uint64_t vzh_gpt2_decoder_buffer(void* d, size_t layer, int which) {
+    const Gpt2Decoder& g = *static_cast<Gpt2Decoder*>(d);
+    switch (which) {
+        case 0: return g.tokens();
+        case 1: return g.logits();
+        case 2: return g.error_word();
+        case 3: return g.cache(layer, 0);
+        case 4: return g.cache(layer, 1);
+        case 5: return g.position();
+        default: return 0;
+    }
+}
+
 // Arena id of the boundary corrections of wire w (0..4) of layer l.
 uint64_t vzh_gpt2_correction(void* p, size_t layer, int w) {
     try {

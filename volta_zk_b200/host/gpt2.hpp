@@ -18,6 +18,7 @@
 #include <cstdint>
 #include <map>
 #include <memory>
+#include <utility>
 #include <vector>
 
 #include "accel.hpp"
@@ -108,6 +109,80 @@ class Gpt2Session {
         owned_.push_back(id);
         return id;
     }
+};
+
+// ---- decode bands and KV-cached decoding (gpt2_decode.cpp) ------------------
+
+// The band witness of rows t0 .. t-1 of the session's last forward
+// (rust/volta-gpt2/src/band.rs:77-196, resident.rs:335-455 and 941-1030):
+// row-local wires are the session's rows from t0 on; the causal-packed
+// per-head wires (scores, exp, weights) are compacted to the band packing
+// (head h: rows t0 .. t-1, windows t0 + i + 1) and the per-head row tables
+// (row shift, denominators, reciprocals) cut to h x q; the final LayerNorm
+// runs over every band row of the last layer's output and the logits over
+// every band row (each decode position's sampled token is checkable).
+class Gpt2Band {
+   public:
+    Gpt2Band(Gpt2Session& s, size_t t0);
+    ~Gpt2Band();
+    Gpt2Band(const Gpt2Band&) = delete;
+    Gpt2Band& operator=(const Gpt2Band&) = delete;
+    // Enqueue the compaction, the final LN and the logits (no wait).
+    void build();
+    size_t t0() const { return t0_; }
+    size_t q() const { return q_; }
+    // Buffer and element offset of a band wire of `layer` (Gpt2Wire).
+    std::pair<uint64_t, size_t> wire(size_t layer, int w) const;
+    uint64_t final_ln(int which) const { return fin_[which]; }  // 0 mean 1 var 2 rin 3 rout 4 acc 5 out
+    uint64_t logits() const { return logits_; }                  // q x vocab i64
+    uint64_t error_word() const { return err_; }
+
+   private:
+    Gpt2Session& s_;
+    size_t t0_, q_;
+    std::vector<std::array<uint64_t, 7>> derived_;  // scores_acc, scores_q, row_shift, exp, denoms, recips, weights
+    std::array<uint64_t, 6> fin_{};
+    uint64_t logits_ = 0, err_ = 0;
+    std::vector<uint64_t> owned_;
+};
+
+// KV-cached greedy decoding (rust/volta-gpt2/src/decode.rs:80-300): caches
+// seeded with the session's K/V rows of its t tokens (KvCache::from_prefill),
+// then one row per step at position pos: embed, every layer on the new row
+// with attention over cache rows 0 .. pos (the new K/V row appended first),
+// final LN, the logits row, and the next token as the argmax of that row (the
+// last of equal maxima), kept on the device for the next step's embed.
+class Gpt2Decoder {
+   public:
+    // max_steps: the most steps this decoder will run (0: every position left)
+    Gpt2Decoder(Gpt2Session& s, size_t max_steps);
+    ~Gpt2Decoder();
+    Gpt2Decoder(const Gpt2Decoder&) = delete;
+    Gpt2Decoder& operator=(const Gpt2Decoder&) = delete;
+    // Enqueue n greedy steps; the first token is the argmax of the session's
+    // last-position logits.  Step i writes its token to tokens()[i] and its
+    // logits row to logits() row i.  Throws when the positions run out.
+    void generate(size_t n);
+    size_t position() const { return pos_; }
+    uint64_t tokens() const { return tokens_; }  // u32, one per generated token
+    uint64_t logits() const { return logits_; }  // i64, n_max x vocab
+    uint64_t cache(size_t layer, int kv) const {
+        return layer >= kcache_.size() ? 0 : (kv ? vcache_[layer] : kcache_[layer]);
+    }
+    uint64_t error_word() const { return err_; }
+    size_t capacity() const { return cap_; }
+
+   private:
+    void step(size_t i);
+    Gpt2Session& s_;
+    Backend& b_;
+    size_t pos_ = 0, cap_ = 0, gen_max_ = 0, done_ = 0;
+    std::vector<uint64_t> kcache_, vcache_;
+    uint64_t xalt_ = 0;  // second layer-input row (inputs and outputs alternate)
+    std::array<uint64_t, kWireCount> w_{};  // one-row wires of the current step
+    std::array<uint64_t, 6> fin_{};
+    uint64_t tokens_ = 0, logits_ = 0, embed_acc_ = 0, err_ = 0;
+    std::vector<uint64_t> owned_;
 };
 
 // ---- the prefill proof schedule (gpt2_proof.cpp) -----------------------------
