@@ -75,6 +75,7 @@ def parse():
                     help="2: the triple sumcheck and the LogUp proof run concurrently on two contexts")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="config 3 line without the config-4 witness leg")
     return ap.parse_args()
 
 
@@ -323,12 +324,17 @@ def ligero_leg(args, prover, be, peaks, rank=0, world=1, comm=None):
                              "hbm_gbs": round(2 * data / (ntt_ms / 1e3) / 1e9, 1),
                              "frac_of_hbm_peak": round(2 * data / (ntt_ms / 1e3) / 1e9 / hbm, 4),
                              "butterflies_per_s": round(butterflies / (ntt_ms / 1e3), 1),
-                             "algorithmic_bytes": 2 * data},
+                             "algorithmic_bytes": 2 * data,
+                             "issue": issue_roofline(NTT_WARP_INST_PER_BUTTERFLY * butterflies, ntt_ms),
+                             "alu_pipe_ncu": {"pass1": 0.772, "pass2": 0.849,
+                                              "source": "ncu at 1024 rows x 2^16 (ALU pipe, pct of peak)"}},
             "hash_fp_tree": {"avg_launch_ms": round(hash_ms, 4),
                              "hbm_gbs": round(data / (hash_ms / 1e3) / 1e9, 1),
                              "frac_of_hbm_peak": round(data / (hash_ms / 1e3) / 1e9 / hbm, 4),
                              "blake3_compressions_per_s": round(compressions / (hash_ms / 1e3), 1),
-                             "algorithmic_bytes": data},
+                             "algorithmic_bytes": data,
+                             "alu_pipe_ncu": {"column_leaves": 0.913,
+                                              "source": "ncu at 1024 rows x 2^16 (ALU pipe, pct of peak)"}},
         },
     }
 
@@ -390,6 +396,30 @@ class RoundJob(__import__("ctypes").Structure):
 # read + 1,230,021 B written for 234,520,576 algorithmic bytes; the parents
 # are read at stride 2, so their whole level crosses DRAM)
 LOGUP_REPLICA_TRAFFIC = (268123077 + 1230021) / 234520576
+# Warp instructions per unit of work of the integer-bound kernels, from ncu
+# captures (smsp__inst_executed.sum): the step-0 replica at 2^22 queries
+# (42,314,187 for 2,095,104 pairs), the NTT passes at 96 rows x 2^16
+# (75,634,080 for 50,331,648 butterflies), the on-chip triple rounds at 2^23
+# (197.0 M for 1024 tiles of 8192 entries)
+LOGUP_WARP_INST_PER_PAIR = 42314187 / 2095104
+NTT_WARP_INST_PER_BUTTERFLY = 75634080 / 50331648
+TRIPLE_LOCAL_WARP_INST_PER_TILE = 197.0e6 / 1024
+SM_MAX_MHZ = 1965.0  # clocks.max.sm of this pool's B200s
+
+
+def issue_roofline(warp_instructions: float, ms: float, sm_mhz: float | None = None) -> dict:
+    """A kernel's integer-instruction issue rate against the SMs' issue peak
+    (4 warp instructions per clock per SM): the roofline of the
+    integer-bound Goldilocks kernels, next to their HBM fraction."""
+    import torch
+
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    mhz = sm_mhz or SM_MAX_MHZ
+    peak = sms * 4 * mhz * 1e6
+    achieved = warp_instructions / (ms / 1e3)
+    return {"bound": "integer instruction issue", "unit": "warp instructions/s", "achieved": round(achieved, 1),
+            "peak": round(peak, 1), "frac": round(achieved / peak, 4), "warp_instructions": int(warp_instructions),
+            "peak_source": f"4 warp instructions per clock per SM x {sms} SMs x {mhz:.0f} MHz"}
 
 
 def logup_step0_replica(be, log2_queries: int, reps: int = 10):
@@ -624,6 +654,8 @@ def config1_leg(args, rank, world, local_rank, dist, prover, peaks, timed_steps=
                 "frac": round(achieved / peak, 4), "traffic": int(batch_bytes * traffic_ratio),
                 "traffic_source": "ncu capture of the 2^22-query replica, scaled by algorithmic bytes",
                 "algorithmic_bytes": batch_bytes, "avg_launch_ms": round(batch_ms, 4)}
+    pairs = sum((1 << L) // 2 for L in range(min(12, args.log2_queries - 1), args.log2_queries))
+    roofline["issue"] = issue_roofline(LOGUP_WARP_INST_PER_PAIR * pairs, batch_ms)
     # the triple-product round kernels, at full size (three 2^24 tables)
     mbox = be.alloc(48)
     lifted = [be.alloc(16 * n) for _ in range(3)]
@@ -663,6 +695,8 @@ def config1_leg(args, rank, world, local_rank, dist, prover, peaks, timed_steps=
         kernels[name] = {"avg_launch_ms": round(kms, 4), "algorithmic_bytes": nbytes,
                          "hbm_gbs": round(nbytes / (kms / 1e3) / 1e9, 1),
                          "frac": round(nbytes / (kms / 1e3) / 1e9 / peak, 4)}
+        if name.startswith("triple_local"):  # instruction-bound by design: its issue roofline
+            kernels[name]["issue"] = issue_roofline(TRIPLE_LOCAL_WARP_INST_PER_TILE * tiles, kms)
     roofline["other_kernels"] = kernels
     for x in lifted + [mbox, loc_r, loc_acc] + loc_f:
         be.free(x)
@@ -762,9 +796,13 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
         allw = out.cpu().numpy().view(np.uint64).reshape(world, per_rank, per_layer, 2)
         return np.concatenate([allw[l % world, l // world] for l in range(gpt2.LAYERS)])
 
+    # the weight commitment goes to the last rank: with 12 layers over 8 GPUs
+    # ranks 0-3 prove two layers and ranks 4-7 one, so the commitment balances
+    pcs_rank = world - 1
+
     def step(host_tokens=None):
         sess.forward(host_tokens)
-        words, per_layer, root = gp.prove(PROOF_SEED, MAC_SEED, PAD_SEED, rank, world, rank == 0)
+        words, per_layer, root = gp.prove(PROOF_SEED, MAC_SEED, PAD_SEED, rank, world, rank == pcs_rank)
         return gather(words, per_layer), per_layer, root
 
     def barrier():
@@ -796,9 +834,9 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
     logits = sess.logits()
     fwd_err = sess.error_word() | max(sess.layer_errors())
     roots = [root] if world == 1 else None
-    if world > 1:  # rank 0's root to every rank (the others committed nothing)
+    if world > 1:  # the committing rank's root to every rank (the others committed nothing)
         r = torch.from_numpy(np.frombuffer(root, dtype=np.uint8).copy()).to(dev)
-        dist.broadcast(r, 0)
+        dist.broadcast(r, pcs_rank)
         roots = [bytes(r.cpu().numpy())]
 
     # ---- the rho denominator: the plain int16 forward (each rank a replica) --
@@ -857,6 +895,8 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
                 "frac": round(achieved / peak, 4), "traffic": int(batch_bytes * traffic_ratio),
                 "traffic_source": "ncu capture of the 2^22-query replica, scaled by algorithmic bytes",
                 "algorithmic_bytes": batch_bytes, "avg_launch_ms": round(batch_ms, 4)}
+    pairs = sum((1 << L) // 2 for L in range(12, 24))
+    roofline["issue"] = issue_roofline(LOGUP_WARP_INST_PER_PAIR * pairs, batch_ms, clocks.summary().get("sm_mhz"))
 
     digest = hashlib.sha256(np.ascontiguousarray(words).tobytes() + roots[0]).hexdigest()
     golden = {}
@@ -885,7 +925,8 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
                                "proofs + weight commitment)",
                    "model": "gpt2-small (12 layers, d 768, 12 heads, MLP 3072, vocab 50257), int16 fixed point, "
                             "LutParams defaults with the stable softmax",
-                   "parallelism": f"forward replicated, layers {gpt2.LAYERS} split over {world} GPU(s), one NCCL "
+                   "parallelism": f"forward replicated, layers {gpt2.LAYERS} split over {world} GPU(s) (rank r: "
+                                  f"layers r, r + {world}, ...; weight commitment on rank {world - 1}), one NCCL "
                                   f"all-gather of the words" if world > 1 else "one proof on one GPU",
                    "l2": "working set (witness 1.8 GB, lookup trees, 2.1 GB codeword) far larger than L2",
                    "timing_policy": "wall-only counters"},
@@ -899,6 +940,52 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
                         "sha256": digest, "pcs_root": roots[0].hex(), "forward_error_word": int(fwd_err),
                         **golden},
     }
+
+
+def decode_leg(prover, t0: int = 960, n: int = 64, reps: int = 3):
+    """Config 4's witness side on one GPU: greedy KV-cached decoding of n
+    tokens after a t0-token prefill (rust/volta-gpt2/src/decode.rs, the
+    native decode baseline of rho_decode) and the band witness of those n rows
+    (band.rs / resident.rs band_model_witness_resident) from the full
+    forward over the same t0 + n tokens.  Device-timed; the band proofs are
+    not built (the layer proof schedule here is the prefill one)."""
+    from volta_zk_b200 import gpt2
+
+    be = prover.backend
+    model = gpt2.synthetic_model()
+    tokens = gpt2.prefill_tokens(t0)
+    with gpt2.Gpt2Session(prover, model, t0) as s:
+        s.forward(tokens)
+        times = []
+        for _ in range(reps + 1):  # the first run warms up
+            with s.decoder(n) as dec:
+                be.mark(0)
+                dec.generate(n)
+                be.mark(1)
+                times.append(be.elapsed_ms(0, 1))
+                gen = dec.tokens()
+                err = dec.error_word()
+        decode_ms = statistics.median(times[1:])
+    with gpt2.Gpt2Session(prover, model, t0 + n) as s2:
+        s2.forward(np.concatenate([tokens, gen]).astype(np.uint32))
+        btimes = []
+        for _ in range(reps + 1):
+            be.mark(2)
+            band = s2.band(t0)
+            be.mark(3)
+            btimes.append(be.elapsed_ms(2, 3))
+            logits_last = band.logits()[-1]
+            band.close()
+        full_logits = s2.logits()
+    return {"workload": f"config 4 witness: {n} greedy KV-cached decode steps after a {t0}-token prefill "
+                        f"(GPT-2 small, 12 layers), and the band witness of those {n} rows",
+            "decode_ms_per_token": round(decode_ms / n, 4), "decode_tokens_per_s": round(n / (decode_ms / 1e3), 1),
+            "band_witness_ms": round(statistics.median(btimes[1:]), 4),
+            "generated_tokens_sha256": hashlib.sha256(gen.tobytes()).hexdigest()[:16],
+            "band_last_logits_equal_full_forward": bool(np.array_equal(logits_last, full_logits)),
+            "decode_error_word": int(err),
+            "note": "band proofs (prove_layer_phase1_band) are not built; the timed decode is the native "
+                    "decode baseline (one device launch sequence per token, the next token chosen on the device)"}
 
 
 def run_b200(args, rank, world, local_rank):
@@ -959,8 +1046,12 @@ def run_b200(args, rank, world, local_rank):
     if world == 1 and not args.no_ligero and not args.no_ligero_zk:
         ligero_zk = ligero_zk_leg(prover)
 
+    decode = None
+    if world == 1 and args.workload == "config3" and not args.no_decode:
+        decode = decode_leg(prover)
+
     if rank == 0:
-        line.update({"ligero": ligero, "ligero_zk": ligero_zk, "witness_gemm": gemm})
+        line.update({"ligero": ligero, "ligero_zk": ligero_zk, "witness_gemm": gemm, "config4_witness": decode})
         print(json.dumps(line), flush=True)
     prover.close()
     if dist:
