@@ -370,6 +370,23 @@ int volta_b200_embed_i16_device(void* ctx, uint64_t in_id, size_t in_offset, uin
                                 size_t n);
 
 /*
+ * Many small device-to-device copies in one call (the counterpart of one
+ * volta_cuda_resident_copy_rows call per segment with rows = 1): segment k
+ * copies bytes from (src_id, src_offset) to (dst_id, dst_offset), offsets in
+ * bytes.  Segments must not overlap one another's destinations.  Every
+ * segment is bounds-checked before anything is launched; one launch per 96
+ * segments.
+ */
+typedef struct vzb_copy_seg {
+    uint64_t src_id;
+    size_t src_offset;
+    uint64_t dst_id;
+    size_t dst_offset;
+    size_t bytes;
+} vzb_copy_seg;
+int volta_b200_copy_segments_device(void* ctx, const vzb_copy_seg* segs, size_t count);
+
+/*
  * Greedy token selection of KV-cached decoding (rust/volta-gpt2/src/decode.rs:
  * 270-272 argmax): the index of the largest of n i64 values, the last one
  * among equal maxima (Iterator::max_by_key), written as a u32 token id at

@@ -1385,6 +1385,54 @@ extern "C" int volta_cuda_resident_mailbox_copy_rows(void* raw, uint64_t src_id,
                      dst_stride, rows, row_bytes, kOpMailbox);
 }
 
+// Many small device-to-device copies in one launch (extension): one CTA per
+// segment, 16-byte units when both ends and the length allow it.
+struct CopySeg {
+    const unsigned char* src;
+    unsigned char* dst;
+    size_t bytes;
+};
+constexpr int kSegsPerLaunch = 96;
+struct CopySegs {
+    CopySeg s[kSegsPerLaunch];
+};
+
+__global__ void copy_segments_kernel(const __grid_constant__ CopySegs segs) {
+    const CopySeg& g = segs.s[blockIdx.x];
+    const bool wide = ((reinterpret_cast<uintptr_t>(g.src) | reinterpret_cast<uintptr_t>(g.dst) | g.bytes) & 15) == 0;
+    if (wide) {
+        for (size_t i = threadIdx.x; i < g.bytes / 16; i += blockDim.x)
+            reinterpret_cast<uint4*>(g.dst)[i] = reinterpret_cast<const uint4*>(g.src)[i];
+    } else {
+        for (size_t i = threadIdx.x; i < g.bytes; i += blockDim.x) g.dst[i] = g.src[i];
+    }
+}
+
+extern "C" int volta_b200_copy_segments_device(void* raw, const vzb_copy_seg* segs, size_t count) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || (count && !segs)) return fail_message(c, "invalid copy segments");
+    std::vector<CopySeg> resolved(count);  // every segment checked before anything is launched
+    size_t total = 0;
+    for (size_t i = 0; i < count; ++i) {
+        void *src = nullptr, *dst = nullptr;
+        if (region_elems(c, segs[i].src_id, segs[i].src_offset, segs[i].bytes, 1, &src) ||
+            region_elems(c, segs[i].dst_id, segs[i].dst_offset, segs[i].bytes, 1, &dst))
+            return -1;
+        resolved[i] = CopySeg{static_cast<const unsigned char*>(src), static_cast<unsigned char*>(dst), segs[i].bytes};
+        total += segs[i].bytes;
+    }
+    if (op_begin(c) || op_mark(c, 1)) return -1;
+    for (size_t base = 0; base < count; base += kSegsPerLaunch) {
+        const size_t n = std::min(count - base, static_cast<size_t>(kSegsPerLaunch));
+        CopySegs batch{};
+        for (size_t i = 0; i < n; ++i) batch.s[i] = resolved[base + i];
+        copy_segments_kernel<<<static_cast<unsigned>(n), 256, 0, c->stream>>>(batch);
+        VZB_LAUNCHED(c);
+    }
+    if (op_mark(c, 2)) return -1;
+    return op_finish(c, kOpPcsRows, 0, 0, total, 0, 0);
+}
+
 // ===========================================================================
 // Extensions (include/volta_b200_ext.h): measurement markers, launch count
 // ===========================================================================

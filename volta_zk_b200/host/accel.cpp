@@ -149,6 +149,8 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         dlsym(handle_, "volta_b200_pack_pair_column_device"));
     ext_loaded_->argmax_i64 =
         reinterpret_cast<decltype(ext_loaded_->argmax_i64)>(dlsym(handle_, "volta_b200_argmax_i64_device"));
+    ext_loaded_->copy_segments =
+        reinterpret_cast<decltype(ext_loaded_->copy_segments)>(dlsym(handle_, "volta_b200_copy_segments_device"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

@@ -41,6 +41,7 @@ struct ExtApi {
     decltype(&::volta_b200_product_fold_round_into_device) product_fold_round = nullptr;
     decltype(&::volta_b200_product_tail_device) product_tail = nullptr;
     decltype(&::volta_b200_argmax_i64_device) argmax_i64 = nullptr;
+    decltype(&::volta_b200_copy_segments_device) copy_segments = nullptr;
 };
 
 }  // namespace vzh

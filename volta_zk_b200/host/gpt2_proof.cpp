@@ -524,18 +524,25 @@ Gpt2Proof Gpt2Prover::prove_layers(const uint8_t seed[32], const uint8_t mac_see
             lr.total += sl.logup ? sl.logup->side[0].msg_total + sl.logup->side[1].msg_total : sl.words;
         }
         lr.buf = keep.add(b_.alloc(lr.total * sizeof(Fp2)));
+        std::vector<vzb_copy_seg> segs;  // every slot's messages into the layer buffer, one batched copy
+        auto copy = [&](uint64_t src, size_t words, size_t at) {
+            segs.push_back(vzb_copy_seg{src, 0, lr.buf, at * sizeof(Fp2), words * sizeof(Fp2)});
+        };
         for (const Slot& sl : lr.slots) {
-            auto copy = [&](uint64_t src, size_t words, size_t at) {
-                b_.check(A.volta_cuda_resident_copy_rows(ctx, src, 0, words * sizeof(Fp2), lr.buf, at * sizeof(Fp2),
-                                                         words * sizeof(Fp2), 1, words * sizeof(Fp2)),
-                         "resident_copy_rows");
-            };
             if (sl.logup) {
                 copy(sl.logup->side[0].msgs, sl.logup->side[0].msg_total, sl.at);
                 copy(sl.logup->side[1].msgs, sl.logup->side[1].msg_total, sl.at + sl.logup->side[0].msg_total);
             } else {
                 copy(sl.msgs, sl.words, sl.at);
             }
+        }
+        if (b_.ext().copy_segments) {
+            b_.check(b_.ext().copy_segments(ctx, segs.data(), segs.size()), "copy_segments_device");
+        } else {
+            for (const vzb_copy_seg& g : segs)
+                b_.check(A.volta_cuda_resident_copy_rows(ctx, g.src_id, 0, g.bytes, g.dst_id, g.dst_offset, g.bytes, 1,
+                                                         g.bytes),
+                         "resident_copy_rows");
         }
     }
     // Ligero commitment of the weights
