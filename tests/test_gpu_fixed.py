@@ -43,7 +43,12 @@ def test_layer_matches_reference_mirror(dev, oracle):
 @pytest.mark.parametrize("m,k,n,shift,with_bias,with_res", [(1, 1, 1, 1, False, False), (5, 70, 9, 10, True, True),
                                                             (64, 768, 128, 10, True, False),
                                                             (33, 3072, 65, 20, False, True),
-                                                            (7, 100, 300, 3, True, True)])
+                                                            (7, 100, 300, 3, True, True),
+                                                            # decode rows (the few-row path)
+                                                            (1, 768, 2304, 10, False, False),
+                                                            (2, 3072, 768, 10, True, True),
+                                                            (4, 768, 3072, 17, True, False),
+                                                            (3, 100, 1000, 5, False, True)])
 def test_fixed_gemm(dev, oracle, m, k, n, shift, with_bias, with_res):
     rng = np.random.default_rng(m + k + n)
     x, w = i16(rng, m * k, -600, 600), i16(rng, k * n, -600, 600)
@@ -58,6 +63,28 @@ def test_fixed_gemm(dev, oracle, m, k, n, shift, with_bias, with_res):
             assert g_ == e_
         else:
             assert np.array_equal(g_, e_)
+
+
+def test_fixed_gemm_few_rows_extremes(dev, oracle):
+    """The few-row path at the int16 extremes over k = 3072 (exact int64 sums)
+    and for a width that is not a multiple of its 32-column blocks."""
+    for m, k, n in ((1, 3072, 777), (4, 3072, 33)):
+        x = np.where(np.arange(m * k) % 3 == 0, -32768, 32767).astype(np.int16)
+        w = np.where(np.arange(k * n) % 5 == 0, -32768, 32767).astype(np.int16)
+        got = dev.gemm(x, w, None, None, m, k, n, 30)
+        exp = oracle.fixed_gemm(x, w, None, None, m, k, n, 30)
+        assert np.array_equal(got[0], exp[0]) and np.array_equal(got[1], exp[1]) and got[3] == exp[3]
+
+
+def test_logits_one_row_full_vocabulary(be, oracle):
+    rng = np.random.default_rng(5)
+    rows, d, vocab = 1, 768, 50257
+    xin, w = i16(rng, rows * d, -3000, 3000), i16(rng, vocab * d, -3000, 3000)
+    a, b, o = be.upload_new(xin), be.upload_new(w), be.alloc(8 * rows * vocab)
+    be.call("fixed_logits_device", a, 0, b, 0, o, 0, rows, d, vocab)
+    assert np.array_equal(be.download(o, 8 * rows * vocab, dtype=np.int64), oracle.fixed_logits(xin, w, rows, d, vocab))
+    for i in (a, b, o):
+        be.free(i)
 
 
 def test_fixed_gemm_error_word(dev, oracle):

@@ -308,6 +308,141 @@ struct LogitsEpi {
     __device__ __forceinline__ void operator()(size_t, size_t i, size_t j, int64_t v) const { out[i * vocab + j] = v; }
 };
 
+// Few-row products (KV-cached decoding: one row per step).  The tensor-core
+// path splits the whole weight matrix into byte planes per call, which for a
+// single row costs more than the product; here the weights are read once,
+// straight from HBM, and the sums are exact in int64 (|x w| < 2^30, k <=
+// 2^16).  The epilogues are the tensor-core path's.
+constexpr size_t kSmallRows = 4;
+
+// out[i][j] = sum_t x[i][t] w[t][j] for w row-major (k x n), split over k so
+// that enough bytes are in flight to stream the weights at HBM speed: CTA
+// (cx, s) covers columns [256 cx, 256 cx + 256) (8 per thread, one 16-byte
+// load per row) over rows [16 s, 16 s + 16) (2 per warp); the 8 warps' sums
+// meet in shared memory and the CTA writes its slice's partial sums; a
+// second kernel adds the slices and applies the epilogue.  Needs n % 8 == 0
+// and 16-byte aligned rows.
+constexpr size_t kSliceRows = 16;
+
+__global__ void __launch_bounds__(256) small_rows_kn_kernel(const int16_t* __restrict__ x, size_t m, size_t k,
+                                                            const int16_t* __restrict__ w, size_t n,
+                                                            int64_t* __restrict__ part) {
+    extern __shared__ int64_t red[];  // [warp][row < m][column in the CTA], 16 KB per row
+    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const size_t c0 = static_cast<size_t>(blockIdx.x) * 256 + lane * 8, slice = blockIdx.y;
+    int64_t acc[kSmallRows][8];
+#pragma unroll
+    for (size_t i = 0; i < kSmallRows; ++i)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[i][c] = 0;
+    if (c0 < n) {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            const size_t r = slice * kSliceRows + warp * 2 + rr;
+            if (r < k) {
+                const uint4 v = __ldcs(reinterpret_cast<const uint4*>(w + r * n + c0));
+                const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (size_t i = 0; i < kSmallRows; ++i) {
+                    if (i >= m) break;
+                    const int32_t xv = x[i * k + r];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const int32_t wv = static_cast<int16_t>(words[c >> 1] >> (16 * (c & 1)));
+                        acc[i][c] += static_cast<int64_t>(xv * wv);
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (size_t i = 0; i < kSmallRows; ++i) {
+        if (i >= m) break;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) red[(warp * m + i) * 256 + lane * 8 + c] = acc[i][c];
+    }
+    __syncthreads();
+    // thread t sums column t of the CTA over the warps, row by row
+    const size_t col = static_cast<size_t>(blockIdx.x) * 256 + threadIdx.x;
+    if (col < n)
+        for (size_t i = 0; i < m; ++i) {
+            int64_t a = 0;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) a += red[(q * m + i) * 256 + threadIdx.x];
+            part[(slice * m + i) * n + col] = a;
+        }
+}
+
+template <class Epi>
+__global__ void small_rows_finish_kernel(const int64_t* __restrict__ part, size_t slices, size_t m, size_t n, Epi epi) {
+    const size_t z = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (z >= m * n) return;
+    int64_t a = 0;
+    for (size_t s = 0; s < slices; ++s) a += part[s * m * n + z];
+    epi(0, z / n, z % n, a);
+}
+
+// out[i][v] = sum_t x[i][t] w[v][t] for w stored n x k (the tied wte of the
+// logits): one warp per output column v, lanes along t, a shuffle sum.
+template <class Epi>
+__global__ void __launch_bounds__(256) small_rows_nk_kernel(const int16_t* __restrict__ x, size_t m, size_t k,
+                                                            const int16_t* __restrict__ w, size_t n, Epi epi) {
+    extern __shared__ int16_t xs[];
+    for (size_t t = threadIdx.x; t < m * k; t += blockDim.x) xs[t] = x[t];
+    __syncthreads();
+    const size_t v = static_cast<size_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    const unsigned lane = threadIdx.x & 31;
+    if (v >= n) return;
+    int64_t acc[kSmallRows] = {0, 0, 0, 0};
+    for (size_t t = lane; t < k; t += 32) {
+        const int32_t wv = __ldcs(w + v * k + t);
+#pragma unroll
+        for (size_t i = 0; i < kSmallRows; ++i)
+            if (i < m) acc[i] += static_cast<int64_t>(static_cast<int32_t>(xs[i * k + t]) * wv);
+    }
+#pragma unroll
+    for (size_t i = 0; i < kSmallRows; ++i) {
+        int64_t a = acc[i];
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) a += __shfl_down_sync(0xffffffffu, a, d);
+        if (i < m && lane == 0) epi(0, i, v, a);
+    }
+}
+
+// Whether the few-row path applies: the row-major form wants 16-byte rows.
+bool small_rows_ok(size_t m, size_t k, const int16_t* w, size_t n, bool w_nk) {
+    if (m > kSmallRows || k > 16384) return false;
+    return w_nk || ((n % 8) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0);
+}
+
+template <class Epi>
+int launch_small_rows(Context* c, const int16_t* x, size_t m, size_t k, const int16_t* w, size_t n, bool w_nk,
+                      const Epi& epi) {
+    if (w_nk) {
+        const size_t smem = m * k * sizeof(int16_t);
+        if (smem > 48 * 1024)
+            VZB_CUDA(c, cudaFuncSetAttribute(small_rows_nk_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem)));
+        small_rows_nk_kernel<Epi><<<static_cast<unsigned>((n + 7) / 8), 256, smem, c->stream>>>(x, m, k, w, n, epi);
+        VZB_LAUNCHED(c);
+        return 0;
+    }
+    const size_t slices = (k + kSliceRows - 1) / kSliceRows;
+    if (ensure_ws(c, kWsScratch3, slices * m * n * sizeof(int64_t))) return -1;
+    int64_t* part = ws<int64_t>(c, kWsScratch3);
+    const dim3 grid(static_cast<unsigned>((n + 255) / 256), static_cast<unsigned>(slices));
+    const size_t smem = 8 * m * 256 * sizeof(int64_t);
+    if (smem > 48 * 1024)
+        VZB_CUDA(c, cudaFuncSetAttribute(small_rows_kn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+    small_rows_kn_kernel<<<grid, 256, smem, c->stream>>>(x, m, k, w, n, part);
+    VZB_LAUNCHED(c);
+    small_rows_finish_kernel<Epi><<<static_cast<unsigned>((m * n + 255) / 256), 256, 0, c->stream>>>(part, slices, m,
+                                                                                                     n, epi);
+    VZB_LAUNCHED(c);
+    return 0;
+}
+
 // Byte planes of the packed causal attention weights as dense rows (rpad per
 // head, zero beyond each row's width pos0 + row + 1 and beyond `rows`); one
 // thread per 16-byte chunk of the planes.
@@ -432,9 +567,14 @@ extern "C" int volta_cuda_fixed_gemm_device(void* raw, uint64_t input_id, size_t
         VZB_REGION(error_id, error_off, 1, uint32_t, err))
         return -1;
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    GemmPlanes g;
-    if (gemm_prepare(c, in, m, k, k, w, n, n, false, &g)) return -1;
-    if (gemm_launch(c, g, FixedGemmEpi{bias, res, acc, req, res_out, err, n, shift})) return -1;
+    const FixedGemmEpi epi{bias, res, acc, req, res_out, err, n, shift};
+    if (small_rows_ok(m, k, w, n, false)) {
+        if (launch_small_rows(c, in, m, k, w, n, false, epi)) return -1;
+    } else {
+        GemmPlanes g;
+        if (gemm_prepare(c, in, m, k, k, w, n, n, false, &g)) return -1;
+        if (gemm_launch(c, g, epi)) return -1;
+    }
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpGemm, 0, 0);
 }
@@ -602,9 +742,13 @@ extern "C" int volta_cuda_fixed_logits_device(void* raw, uint64_t input_id, size
         return -1;
     if (op_begin(c) || op_mark(c, 1)) return -1;
     // x (rows x d) times wte^T: wte (vocab x d) is already the n x k layout
-    GemmPlanes g;
-    if (gemm_prepare(c, in, rows, d, d, w, vocab, d, true, &g)) return -1;
-    if (gemm_launch(c, g, LogitsEpi{out, vocab})) return -1;
+    if (small_rows_ok(rows, d, w, vocab, true)) {
+        if (launch_small_rows(c, in, rows, d, w, vocab, true, LogitsEpi{out, vocab})) return -1;
+    } else {
+        GemmPlanes g;
+        if (gemm_prepare(c, in, rows, d, d, w, vocab, d, true, &g)) return -1;
+        if (gemm_launch(c, g, LogitsEpi{out, vocab})) return -1;
+    }
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpGemm, 0, 0);
 }

@@ -117,7 +117,8 @@ enum WorkspaceSlot : int {
     kWsScratch = 12,   // miscellaneous scratch
     kWsScratch2 = 13,
     kWsGemm = 14,      // byte planes of the GEMM operands
-    kWsCount = 15,
+    kWsScratch3 = 15,  // split-k partial sums of the few-row products
+    kWsCount = 16,
 };
 
 constexpr size_t kStageSlotBytes = size_t{64} << 10;
