@@ -370,6 +370,22 @@ int volta_b200_embed_i16_device(void* ctx, uint64_t in_id, size_t in_offset, uin
                                 size_t n);
 
 /*
+ * Many small host-to-device uploads in one call (the counterpart of one
+ * volta_cuda_resident_upload per item): item k copies bytes (1 .. 64 KiB)
+ * from host memory src to (dst_id, dst_offset bytes), ordered on the
+ * context's stream like any upload.  The items are packed into the pinned
+ * staging ring and copied by one launch per filled staging slot.  Every
+ * destination is bounds-checked before anything is staged.
+ */
+typedef struct vzb_upload {
+    uint64_t dst_id;
+    size_t dst_offset;
+    const void* src;
+    size_t bytes;
+} vzb_upload;
+int volta_b200_upload_batch(void* ctx, const vzb_upload* items, size_t count);
+
+/*
  * Many small device-to-device copies in one call (the counterpart of one
  * volta_cuda_resident_copy_rows call per segment with rows = 1): segment k
  * copies bytes from (src_id, src_offset) to (dst_id, dst_offset), offsets in

@@ -94,7 +94,7 @@ _CTYPES = {
     "vz_raw_stats*": C.c_void_p, "vz_raw_pinned_stats*": C.c_void_p,
     "vz_raw_control_state*": C.c_void_p, "const vz_attention_wires_args*": C.c_void_p,
     "float*": C.POINTER(C.c_float), "const vzb_layer_job*": C.c_void_p, "const vzb_round_job*": C.c_void_p,
-    "const vzb_suffix_job*": C.c_void_p, "const vzb_blind_job*": C.c_void_p, "const vzb_copy_seg*": C.c_void_p,
+    "const vzb_suffix_job*": C.c_void_p, "const vzb_blind_job*": C.c_void_p, "const vzb_copy_seg*": C.c_void_p, "const vzb_upload*": C.c_void_p,
 }
 _RESTYPES = {"int": C.c_int, "uint32_t": C.c_uint32, "void": None, "const char*": C.c_char_p}
 

@@ -1281,6 +1281,69 @@ extern "C" int volta_cuda_resident_upload(void* raw, uint64_t id, size_t offset,
     return xfer_finish(c, bytes, true);
 }
 
+// Many small uploads at once (extension): the host buffers are packed into
+// staging slots (16-byte aligned pieces) and each slot's pieces are copied to
+// their destinations by one launch, one CTA per piece.
+struct StagePiece {
+    unsigned char* dst;
+    size_t src_at;  // offset in the mapped staging ring
+    size_t bytes;
+};
+constexpr int kPiecesPerLaunch = 96;
+struct StagePieces {
+    StagePiece p[kPiecesPerLaunch];
+};
+
+__global__ void stage_pieces_kernel(const __grid_constant__ StagePieces pieces, const unsigned char* __restrict__ stage) {
+    const StagePiece& g = pieces.p[blockIdx.x];
+    const unsigned char* src = stage + g.src_at;
+    if (((reinterpret_cast<uintptr_t>(g.dst) | g.bytes) & 15) == 0) {
+        for (size_t i = 16 * threadIdx.x; i < g.bytes; i += 16 * blockDim.x)
+            *reinterpret_cast<uint4*>(g.dst + i) = *reinterpret_cast<const uint4*>(src + i);
+    } else {
+        for (size_t i = threadIdx.x; i < g.bytes; i += blockDim.x) g.dst[i] = src[i];
+    }
+}
+
+extern "C" int volta_b200_upload_batch(void* raw, const vzb_upload* items, size_t count) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || (count && !items)) return fail_message(c, "invalid upload batch");
+    if (!c->stage) return fail_message(c, "upload batch needs the staging ring");
+    std::vector<void*> dsts(count);
+    for (size_t i = 0; i < count; ++i) {  // every destination checked before anything is staged
+        if (!items[i].src || !items[i].bytes || items[i].bytes > kStageSlotBytes)
+            return fail_message(c, "invalid upload batch item (1 byte .. 64 KiB each)");
+        if (region(c, items[i].dst_id, items[i].dst_offset, items[i].bytes, &dsts[i])) return -1;
+    }
+    if (xfer_begin(c)) return -1;
+    size_t total = 0, i = 0;
+    while (i < count) {  // fill one slot, launch its copies
+        const int slot = c->stage_next;
+        c->stage_next = (slot + 1) % kStageSlots;
+        if (c->stage_used[slot]) VZB_CUDA(c, cudaEventSynchronize(c->stage_ev[slot]));
+        const size_t base = static_cast<size_t>(slot) * kStageSlotBytes;
+        StagePieces batch{};
+        int n = 0;
+        size_t used = 0;
+        while (i < count && n < kPiecesPerLaunch && used + items[i].bytes <= kStageSlotBytes) {
+            std::memcpy(static_cast<char*>(c->stage) + base + used, items[i].src, items[i].bytes);
+            batch.p[n++] = StagePiece{static_cast<unsigned char*>(dsts[i]), base + used, items[i].bytes};
+            used += (items[i].bytes + 15) & ~size_t{15};
+            total += items[i].bytes;
+            ++i;
+        }
+        stage_pieces_kernel<<<static_cast<unsigned>(n), 128, 0, c->stream>>>(
+            batch, static_cast<const unsigned char*>(c->stage_dev));
+        cudaError_t e = cudaGetLastError();
+        ++c->launches;
+        if (e == cudaSuccess) e = cudaEventRecord(c->stage_ev[slot], c->stream);
+        if (e != cudaSuccess) return fail_cuda(c, "upload batch", e);
+        c->stage_used[slot] = true;
+    }
+    ++c->stats.resident_h2d_host_calls;
+    return xfer_finish(c, total, true);
+}
+
 extern "C" int volta_cuda_resident_download(void* raw, uint64_t id, size_t offset, void* dst,
                                             size_t bytes) {
     Context* c = static_cast<Context*>(raw);

@@ -151,6 +151,8 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         reinterpret_cast<decltype(ext_loaded_->argmax_i64)>(dlsym(handle_, "volta_b200_argmax_i64_device"));
     ext_loaded_->copy_segments =
         reinterpret_cast<decltype(ext_loaded_->copy_segments)>(dlsym(handle_, "volta_b200_copy_segments_device"));
+    ext_loaded_->upload_batch =
+        reinterpret_cast<decltype(ext_loaded_->upload_batch)>(dlsym(handle_, "volta_b200_upload_batch"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

@@ -84,6 +84,10 @@ struct PendingSide {
     std::vector<vzb_suffix_job> suffix_jobs;
     std::vector<std::vector<vzb_round_job>> plan;
     std::vector<vzb_layer_job> jobs;
+    std::vector<vzb_copy_seg> copies;  // the root into the message slots
+    // claim points and challenges read only by the batched launches, uploaded
+    // together by launch_side_work
+    std::vector<std::pair<uint64_t, std::vector<Fp2>>> uploads;
 };
 // leaf: the packed leaf column, or 0 with `col` and `alpha0` given (a side
 // without multiplicities; leaf j = alpha0 - col_j).

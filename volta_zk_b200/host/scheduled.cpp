@@ -243,10 +243,18 @@ PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mu
         const size_t Lp = l - shard_bits;
         flat.insert(flat.end(), sch.point[l].begin(), sch.point[l].begin() + Lp);
     }
+    // With the cross-layer batches, the points and the jobs' challenges are
+    // read only by launch_side_work's launches: their uploads go with it
+    const bool defer = X.logup_layers && X.logup_round_batch && X.logup_suffix_eq_batch && X.upload_batch &&
+                       b.batched() && flat.size() * sizeof(Fp2) <= (size_t{64} << 10);
+    std::vector<std::pair<uint64_t, std::vector<Fp2>>> deferred;
     uint64_t pts = 0;
     if (!flat.empty()) {
         pts = own.add(b.alloc(flat.size() * sizeof(Fp2)));
-        b.upload(pts, 0, flat.data(), flat.size() * sizeof(Fp2));
+        if (defer)
+            deferred.emplace_back(pts, flat);
+        else
+            b.upload(pts, 0, flat.data(), flat.size() * sizeof(Fp2));
     }
     // message slots: local root, then per sharded layer its local round
     // accumulators (4 Fp2 each) and its 4 left-over values
@@ -280,11 +288,10 @@ PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mu
         b.check(A.volta_cuda_logup_tree_device(ctx, leaf, 0, mult, 0, n_local, alpha1, mult ? 1 : 0, tp, 0, tq, 0),
                 "logup_tree_device");
     }
-    b.check(A.volta_cuda_resident_copy_rows(ctx, tp, 0, sizeof(Fp2), msgs, 0, sizeof(Fp2), 1, sizeof(Fp2)),
-            "resident_copy_rows");
-    b.check(A.volta_cuda_resident_copy_rows(ctx, tq, 0, sizeof(Fp2), msgs, sizeof(Fp2), sizeof(Fp2), 1,
-                                            sizeof(Fp2)),
-            "resident_copy_rows");
+    // the side's root (p, q) into its first message slots: gathered with the
+    // other sides' roots into one batched copy by launch_side_work
+    std::vector<vzb_copy_seg> root_copies = {vzb_copy_seg{tp, 0, msgs, 0, sizeof(Fp2)},
+                                             vzb_copy_seg{tq, 0, msgs, sizeof(Fp2), sizeof(Fp2)}};
     // round challenges of the local rounds, for the one-CTA layer jobs
     const bool jobs_on = X.logup_layers != nullptr;
     std::vector<size_t> r_off(depth, 0);
@@ -297,7 +304,10 @@ PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mu
         }
         if (!rflat.empty()) {
             rbuf = own.add(b.alloc(rflat.size() * sizeof(Fp2)));
-            b.upload(rbuf, 0, rflat.data(), rflat.size() * sizeof(Fp2));
+            if (defer && rflat.size() * sizeof(Fp2) <= (size_t{64} << 10))
+                deferred.emplace_back(rbuf, std::move(rflat));
+            else
+                b.upload(rbuf, 0, rflat.data(), rflat.size() * sizeof(Fp2));
         }
     }
     std::vector<vzb_layer_job> jobs;  // launched together after every large round is enqueued
@@ -552,12 +562,33 @@ PendingSide frac_side_enqueue(Backend& b, Owned& own, uint64_t leaf, uint64_t mu
     ps.suffix_jobs = std::move(suffix_jobs);
     ps.plan = std::move(plan);
     ps.jobs = std::move(jobs);
+    ps.copies = std::move(root_copies);
+    ps.uploads = std::move(deferred);
     return ps;
 }
 
 void launch_side_work(Backend& b, const std::vector<PendingSide*>& sides) {
     const ExtApi& X = b.ext();
     void* ctx = b.ctx();
+    {   // every side's deferred uploads, before the launches that read them
+        std::vector<vzb_upload> items;
+        for (const PendingSide* ps : sides)
+            for (const auto& u : ps->uploads)
+                items.push_back(vzb_upload{u.first, 0, u.second.data(), u.second.size() * sizeof(Fp2)});
+        if (!items.empty()) b.check(X.upload_batch(ctx, items.data(), items.size()), "upload_batch");
+    }
+    {   // every side's root copies (its tree is already enqueued)
+        std::vector<vzb_copy_seg> copies;
+        for (const PendingSide* ps : sides) copies.insert(copies.end(), ps->copies.begin(), ps->copies.end());
+        if (X.copy_segments) {
+            b.check(X.copy_segments(ctx, copies.data(), copies.size()), "copy_segments_device");
+        } else {
+            for (const vzb_copy_seg& g : copies)
+                b.check(b.api().volta_cuda_resident_copy_rows(ctx, g.src_id, g.src_offset, g.bytes, g.dst_id,
+                                                              g.dst_offset, g.bytes, 1, g.bytes),
+                        "resident_copy_rows");
+        }
+    }
     std::vector<vzb_suffix_job> suffix_jobs;
     std::vector<vzb_layer_job> jobs;
     size_t steps_max = 0;
