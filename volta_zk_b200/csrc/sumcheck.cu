@@ -1936,15 +1936,24 @@ struct MsgStoreEpi {
 
 // CTA b runs the job whose range holds b: a grid-stride loop over that
 // job's items with the job's own CTA count as the stride, then the job's
-// grid reduction.  Fold-only jobs skip the reduction.  kRound0: every job
-// is a round-0 step (kind 0), whose evaluators fit 96 registers: five
-// 128-thread CTAs (20 warps) share an SM instead of the 16 warps that the
-// fold evaluators' 128 registers allow.
+// grid reduction.  Fold-only jobs skip the reduction.  One instantiation per
+// job class, so that each class gets its own register allocation:
+//   kBatchRound0   kind 0 (round 0 on interleaved children); its evaluators
+//                  fit 96 registers, so five 128-thread CTAs (20 warps)
+//                  share an SM;
+//   kBatchFoldIL   kind 1 (fold 0 + round 1 on interleaved children);
+//   kBatchFoldRun  kinds 2 and 3 (fold j + round j + 1, fold only).
+enum BatchClass : int { kBatchRound0 = 0, kBatchFoldIL = 1, kBatchFoldRun = 2 };
 constexpr unsigned kRound0Threads = 128;
 constexpr unsigned kRound0Ctas = 5;
 
-template <bool kRound0>
-__global__ void __launch_bounds__(kRound0 ? kRound0Threads : kReduceThreads, kRound0 ? kRound0Ctas : 2)
+__host__ __device__ constexpr int batch_class(uint32_t kind) {
+    return kind == kBatchRoundIL ? kBatchRound0 : kind == kBatchFoldRoundIL ? kBatchFoldIL : kBatchFoldRun;
+}
+
+template <int kClass>
+__global__ void __launch_bounds__(kClass == kBatchRound0 ? kRound0Threads : kReduceThreads,
+                                  kClass == kBatchRound0 ? kRound0Ctas : 2)
     logup_round_batch_kernel(const __grid_constant__ RoundBatch batch, Fp2* partials, unsigned* counters) {
     unsigned j = 0;
     while (j + 1 < batch.count && blockIdx.x >= batch.job[j + 1].block0) ++j;
@@ -1952,7 +1961,7 @@ __global__ void __launch_bounds__(kRound0 ? kRound0Threads : kReduceThreads, kRo
     const unsigned bidx = blockIdx.x - jb.block0;
     const size_t stride = static_cast<size_t>(jb.blocks) * blockDim.x;
     const size_t first = static_cast<size_t>(bidx) * blockDim.x + threadIdx.x;
-    if (!kRound0 && jb.kind == kBatchFold) {
+    if (kClass == kBatchFoldRun && jb.kind == kBatchFold) {
         for (size_t i = first; i < jb.items; i += stride) {
             Fp2 x0, x1;
             if (jb.p_one) {
@@ -1973,7 +1982,7 @@ __global__ void __launch_bounds__(kRound0 ? kRound0Threads : kReduceThreads, kRo
     Fp2W w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) f2w_zero(w[k]);
-    if (kRound0) {
+    if (kClass == kBatchRound0) {
         if (jb.q_col) {
             const QColEvalIL ev{jb.col, jb.s, jb.a0, jb.a1, jb.w7a1sq};
             for (size_t i = first; i < jb.items; i += stride) ev(i, w);
@@ -1987,33 +1996,19 @@ __global__ void __launch_bounds__(kRound0 ? kRound0Threads : kReduceThreads, kRo
             const LogupEvalIL ev{jb.in0, jb.in1, jb.s};
             for (size_t i = first; i < jb.items; i += stride) ev(i, w);
         }
-    } else if (jb.q_col) {
-        if (jb.kind == kBatchRoundIL) {
-            const QColEvalIL ev{jb.col, jb.s, jb.a0, jb.a1, jb.w7a1sq};
-            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
-        } else {
+    } else if (kClass == kBatchFoldIL) {
+        if (jb.q_col) {
             const QColFoldEvalIL ev{jb.col, jb.s, jb.out2, jb.out3, jb.r, jb.a0, jb.a1};
             for (size_t i = first; i < jb.items; i += stride) ev(i, w);
-        }
-    } else if (jb.p_one) {
-        if (jb.kind == kBatchRoundIL) {
-            const QEvalIL ev{jb.in1, jb.s};
-            for (size_t i = first; i < jb.items; i += stride) ev(i, w);
-        } else if (jb.kind == kBatchFoldRoundIL) {
+        } else if (jb.p_one) {
             const QFoldEvalIL ev{jb.in1, jb.s, jb.out2, jb.out3, jb.r};
             for (size_t i = first; i < jb.items; i += stride) ev(i, w);
         } else {
-            const QFoldEval ev{jb.in2, jb.in3, jb.s, jb.out2, jb.out3, jb.r};
+            const LogupFoldEvalIL ev{jb.in0, jb.in1, jb.s, jb.out0, jb.out1, jb.out2, jb.out3, jb.r};
             for (size_t i = first; i < jb.items; i += stride) ev(i, w);
         }
-    } else if (jb.kind == kBatchRoundIL && jb.parents) {
-        const LogupEvalILPar ev{jb.in0, jb.in1, jb.s, jb.pp, jb.pq};
-        for (size_t i = first; i < jb.items; i += stride) ev(i, w);
-    } else if (jb.kind == kBatchRoundIL) {
-        const LogupEvalIL ev{jb.in0, jb.in1, jb.s};
-        for (size_t i = first; i < jb.items; i += stride) ev(i, w);
-    } else if (jb.kind == kBatchFoldRoundIL) {
-        const LogupFoldEvalIL ev{jb.in0, jb.in1, jb.s, jb.out0, jb.out1, jb.out2, jb.out3, jb.r};
+    } else if (jb.p_one) {
+        const QFoldEval ev{jb.in2, jb.in3, jb.s, jb.out2, jb.out3, jb.r};
         for (size_t i = first; i < jb.items; i += stride) ev(i, w);
     } else {
         const LogupFoldEval ev{jb.in0, jb.in1, jb.in2, jb.in3, jb.s, jb.out0, jb.out1, jb.out2, jb.out3, jb.r};
@@ -2026,6 +2021,39 @@ __global__ void __launch_bounds__(kRound0 ? kRound0Threads : kReduceThreads, kRo
                   MsgStoreEpi{jb.msg});
 }
 
+// One launch of the jobs of one class: CTAs in proportion to the items (at
+// least one per job, at most one per thread block of items), two waves of
+// the resident CTAs in all.
+int launch_round_batch(Context* c, RoundBatch& batch, int cls) {
+    size_t total = 0;
+    for (uint32_t j = 0; j < batch.count; ++j) total += batch.job[j].items;
+    const unsigned threads = cls == kBatchRound0 ? kRound0Threads : kReduceThreads;
+    const size_t target = static_cast<size_t>(c->sm_count) * (cls == kBatchRound0 ? 2 * kRound0Ctas : 4);
+    uint32_t next = 0;
+    for (uint32_t j = 0; j < batch.count; ++j) {
+        BatchJob& d = batch.job[j];
+        const size_t need = (d.items + threads - 1) / threads;
+        size_t share = (target * d.items + total - 1) / total;
+        if (share < 1) share = 1;
+        d.block0 = next;
+        d.blocks = static_cast<uint32_t>(need < share ? need : share);
+        next += d.blocks;
+    }
+    // partials: 4 Fp2 per CTA within the workspace (SMs x 8 CTAs x 9 Fp2)
+    if (static_cast<size_t>(next) * 4 > static_cast<size_t>(c->sm_count) * 8 * 9)
+        return fail_message(c, "LogUp round batch exceeds the reduction workspace");
+    Fp2* partials = ws<Fp2>(c, kWsPartials);
+    unsigned* counters = ws<unsigned>(c, kWsCounter) + kBatchCounterBase;
+    if (cls == kBatchRound0)
+        logup_round_batch_kernel<kBatchRound0><<<next, threads, 0, c->stream>>>(batch, partials, counters);
+    else if (cls == kBatchFoldIL)
+        logup_round_batch_kernel<kBatchFoldIL><<<next, threads, 0, c->stream>>>(batch, partials, counters);
+    else
+        logup_round_batch_kernel<kBatchFoldRun><<<next, threads, 0, c->stream>>>(batch, partials, counters);
+    VZB_LAUNCHED(c);
+    return 0;
+}
+
 }  // namespace
 
 extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_job* jobs, size_t count) {
@@ -2034,7 +2062,6 @@ extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_jo
         return fail_message(c, "invalid LogUp round batch (1 to 24 jobs)");
     RoundBatch batch{};
     batch.count = static_cast<uint32_t>(count);
-    size_t total = 0;
     for (size_t j = 0; j < count; ++j) {
         const vzb_round_job& q = jobs[j];
         BatchJob& d = batch.job[j];
@@ -2107,35 +2134,17 @@ extern "C" int volta_b200_logup_round_batch_device(void* raw, const vzb_round_jo
             d.s = static_cast<const Fp2*>(sv);
             d.msg = static_cast<Fp2*>(mv);
         }
-        total += d.items;
     }
-    // CTAs in proportion to the items (at least one per job, at most one
-    // per thread block of items), two waves of the resident CTAs in all
-    bool round0 = true;
-    for (size_t j = 0; j < count; ++j) round0 = round0 && batch.job[j].kind == kBatchRoundIL;
-    const unsigned threads = round0 ? kRound0Threads : kReduceThreads;
-    const size_t target = static_cast<size_t>(c->sm_count) * (round0 ? 2 * kRound0Ctas : 4);
-    uint32_t next = 0;
-    for (size_t j = 0; j < count; ++j) {
-        BatchJob& d = batch.job[j];
-        const size_t need = (d.items + threads - 1) / threads;
-        size_t share = (target * d.items + total - 1) / total;
-        if (share < 1) share = 1;
-        d.block0 = next;
-        d.blocks = static_cast<uint32_t>(need < share ? need : share);
-        next += d.blocks;
-    }
-    // partials: 4 Fp2 per CTA within the workspace (SMs x 8 CTAs x 9 Fp2)
-    if (static_cast<size_t>(next) * 4 > static_cast<size_t>(c->sm_count) * 8 * 9)
-        return fail_message(c, "LogUp round batch exceeds the reduction workspace");
+    // one launch per job class present, in class order (a step of the
+    // scheduled drivers holds one class, or kinds 2 and 3 together); the
+    // launches run in stream order, so they share the partials and counters
     if (op_begin(c) || op_mark(c, 1)) return -1;
-    if (round0)
-        logup_round_batch_kernel<true><<<next, kRound0Threads, 0, c->stream>>>(
-            batch, ws<Fp2>(c, kWsPartials), ws<unsigned>(c, kWsCounter) + kBatchCounterBase);
-    else
-        logup_round_batch_kernel<false><<<next, kReduceThreads, 0, c->stream>>>(
-            batch, ws<Fp2>(c, kWsPartials), ws<unsigned>(c, kWsCounter) + kBatchCounterBase);
-    VZB_LAUNCHED(c);
+    for (int cls = kBatchRound0; cls <= kBatchFoldRun; ++cls) {
+        RoundBatch sub{};
+        for (uint32_t j = 0; j < batch.count; ++j)
+            if (batch_class(batch.job[j].kind) == cls) sub.job[sub.count++] = batch.job[j];
+        if (sub.count && launch_round_batch(c, sub, cls)) return -1;
+    }
     if (op_mark(c, 2)) return -1;
     return op_finish(c, kOpLogup, 0, 0);
 }
