@@ -442,6 +442,21 @@ int volta_b200_softmax_lookup_columns_device(void* ctx, uint64_t scores_id, size
                                             uint32_t recip_den_shift, uint64_t recip_pad_in, uint64_t recip_pad_out);
 
 /*
+ * The same columns for a band of `rows` query rows at positions t0 .. t0 +
+ * rows - 1 attending over t0 + rows keys (rust/volta-proto/src/block_proof.rs
+ * BandShape, build_attn_wires_band): row i of head h holds t0 + i + 1 packed
+ * entries at h * caus + i * t0 + i (i + 1) / 2, caus = rows * t0 +
+ * rows (rows + 1) / 2 (band.rs band packing); the row tables are heads x
+ * rows and t_pad pads the rows.  t0 = 0 is the entry point above.
+ */
+int volta_b200_softmax_lookup_columns_band_device(
+    void* ctx, uint64_t scores_id, size_t scores_offset, uint64_t row_shift_id, size_t row_shift_offset,
+    uint64_t exp_id, size_t exp_offset, uint64_t denoms_id, size_t denoms_offset, uint64_t recips_id,
+    size_t recips_offset, uint64_t weights_id, size_t weights_offset, const uint64_t* out_ids, uint64_t error_id,
+    size_t error_offset, size_t rows, size_t t0, size_t heads, size_t n_pad, size_t h_pad, size_t t_pad,
+    uint64_t exp_pad, uint32_t norm_shift, uint32_t recip_den_shift, uint64_t recip_pad_in, uint64_t recip_pad_out);
+
+/*
  * A pair lookup's query column: out[i] = cols[i] + 2^shift cols[n + i]
  * (mod p) for the two canonical columns at cols (input, then output), as
  * the reference packs pairs (rust/volta-proto/src/block_proof.rs:2511-2520
@@ -463,6 +478,20 @@ int volta_b200_av_factors_device(void* ctx, uint64_t weights_id, size_t weights_
                                 size_t eq_dim_offset, uint64_t eq_head_id, size_t eq_head_offset,
                                 const uint64_t* out_ids, size_t rows, size_t heads, size_t head_dim, size_t h_pad,
                                 size_t t_pad);
+
+/*
+ * The A.V factors of a band (rows query rows at positions t0 .. t0 + rows -
+ * 1, band-packed weights as above): over index h * s_pad + j for the t0 +
+ * rows keys j, A = sum over the rows i with t0 + i >= j of eq_rows[i]
+ * w[h,i,j] (eq_rows: q_pad entries), B = sum_c eq_dim[c] v[j, h*head_dim + c]
+ * (v: the t0 + rows cached V rows), C = eq_head[h]; h_pad * s_pad entries
+ * each.  t0 = 0, q_pad = s_pad = t_pad is the entry point above.
+ */
+int volta_b200_av_factors_band_device(void* ctx, uint64_t weights_id, size_t weights_offset, uint64_t v_id,
+                                     size_t v_offset, uint64_t eq_rows_id, size_t eq_rows_offset,
+                                     uint64_t eq_dim_id, size_t eq_dim_offset, uint64_t eq_head_id,
+                                     size_t eq_head_offset, const uint64_t* out_ids, size_t rows, size_t t0,
+                                     size_t heads, size_t head_dim, size_t h_pad, size_t q_pad, size_t s_pad);
 
 #ifdef __cplusplus
 }

@@ -229,8 +229,10 @@ SITES = dict(down_range=1, gelu=2, up_range=3, ln2_norm=4, ln2_rsqrt=5, proj_ran
              ln2_had=18, gemm_proj=19, av=20, norm_had=21, qk=22, gemm_qkv=23, ln1_had=24)
 
 
-def site_domain(layer, site):
-    return 0x7000000000000000 | (layer << 16) | (SITES[site] << 8)
+def site_domain(layer, site, chunk=0):
+    """Transcript domain of a sub-proof site; chunk 0 is the prefill, c >= 1
+    the c-th decode band of a response."""
+    return 0x7000000000000000 | (chunk << 32) | (layer << 16) | (SITES[site] << 8)
 
 
 def pow2(n):
@@ -267,10 +269,16 @@ def lift(col):
 
 
 class Schedule:
-    def __init__(self, o, luts, t):
-        self.o, self.luts, self.t = o, luts, t
-        self.tp = pow2(t)
-        self.rect = HEAD_PAD * self.tp * self.tp
+    """The layer schedule over t proof rows at positions t0 .. t0 + t - 1
+    attending over s = t0 + t keys (block_proof.rs BandShape: q = t; the
+    prefill is the square band t0 = 0, a decode band has t0 > 0 and its own
+    transcript and mask domains, chunk >= 1)."""
+
+    def __init__(self, o, luts, t, t0=0, chunk=0):
+        self.o, self.luts, self.t, self.t0, self.chunk = o, luts, t, t0, chunk
+        self.s = t0 + t
+        self.tp, self.sp = pow2(t), pow2(self.s)
+        self.rect = HEAD_PAD * self.tp * self.sp
         exp = luts["exp"]
         assert exp[0x8000] == 0
         u = np.arange(1 << 16)
@@ -281,8 +289,11 @@ class Schedule:
         self.recip18 = np.where(r < (1 << 16), luts["softmax_recip"][np.minimum(r, 65535)], hi).astype(np.int64)
 
     # ---- lookup instances -------------------------------------------------
+    def dom(self, layer, site):
+        return site_domain(layer, site, self.chunk)
+
     def logup(self, f, table, mult, seed, layer, site):
-        return self.o.logup_prove_fp(f, table, mult, seed, site_domain(layer, site))
+        return self.o.logup_prove_fp(f, table, mult, seed, self.dom(layer, site))
 
     def range_site(self, acc, out, rows, cols, row_pad, col_pad, shift, seed, layer, site):
         half = 1 << (shift - 1)
@@ -341,7 +352,7 @@ class Schedule:
 
     def gemm(self, x, w, acc, m, k, n, seed, layer, site):
         o = self.o
-        tx = o.FpStream(seed, site_domain(layer, site))
+        tx = o.FpStream(seed, self.dom(layer, site))
         m_pad, n_pad, k_pad = pow2(m), pow2(n), pow2(k)
         rj = [tx.next_fp2() for _ in range(n_pad.bit_length() - 1)]
         ri = [tx.next_fp2() for _ in range(m_pad.bit_length() - 1)]
@@ -357,7 +368,7 @@ class Schedule:
 
     def ln_product(self, x, mean, rout, gain, seed, layer, site):
         t, tp, d = self.t, self.tp, 768
-        tx = self.o.FpStream(seed, site_domain(layer, site))
+        tx = self.o.FpStream(seed, self.dom(layer, site))
         dp = 1024
         xx = np.zeros((tp, dp), np.int64)
         xx[:t, :d] = np.asarray(x, np.int64).reshape(t, d)
@@ -370,9 +381,12 @@ class Schedule:
         return self.product(lift(emb(cen.reshape(-1))), lift(emb((rs[:, None] * g[None, :]).reshape(-1))), tx)
 
     # ---- one layer --------------------------------------------------------------
-    def layer(self, r, lw, seed, layer):
-        """The words of one layer from the forward's wires r (forward_layer names)."""
-        t, tp, rect = self.t, self.tp, self.rect
+    def layer(self, r, lw, seed, layer, kv=None):
+        """The words of one layer from the wires r (forward_layer names; a
+        band_witness layer for a band) and, for a band, kv = (K, V) of all s
+        cached rows (the prefill uses r's own K and V)."""
+        t, tp, rect, t0, s, sp = self.t, self.tp, self.rect, self.t0, self.s, self.sp
+        k_all, v_all = kv if kv is not None else (r["k"], r["v"])
         d, dff, h = 768, 3072, 12
         lut = self.luts
         words = []
@@ -385,12 +399,13 @@ class Schedule:
                                     lut["ln_rsqrt"], False, seed, layer, "ln2_rsqrt"))
         words.append(self.range_site(r["proj_acc"], r["attn_proj_q"], t, d, tp, 1024, 10, seed, layer, "proj_range"))
         words.append(self.range_site(r["av_acc"], r["av_q"], t, d, tp, 1024, 12, seed, layer, "av_range"))
-        # softmax columns over the padded packed rectangle
-        packed = h * t * (t + 1) // 2
+        # softmax columns over the padded packed rectangle (row i: window t0 + i + 1)
+        caus = t * t0 + t * (t + 1) // 2
+        packed = h * caus
         rs = np.asarray(r["row_shift"], np.int64).reshape(h, t)
         rc = np.asarray(r["recips"], np.int64).reshape(h, t)
-        heads = np.repeat(np.arange(h), t * (t + 1) // 2)
-        rows = np.concatenate([np.repeat(np.arange(t), np.arange(1, t + 1))] * h)
+        heads = np.repeat(np.arange(h), caus)
+        rows = np.concatenate([np.repeat(np.arange(t), t0 + np.arange(1, t + 1))] * h)
         sq = np.asarray(r["scores_q"], np.int64)
         ex = np.asarray(r["exp_out"], np.int64)
         wt = np.asarray(r["weights"], np.int64)
@@ -432,35 +447,23 @@ class Schedule:
         words.append(self.ln_product(r["attn_block_out"], r["ln2_mean"], r["ln2_rsqrt_out"], lw["ln2_gain"], seed, layer,
                                      "ln2_had"))
         words.append(self.gemm(r["av_q"], lw["attn_proj"], r["proj_acc"], t, d, d, seed, layer, "gemm_proj"))
-        tx = o.FpStream(seed, site_domain(layer, "av"))
+        # A.V over (head, key position j < s): rows i with t0 + i >= j
+        tx = o.FpStream(seed, self.dom(layer, "av"))
         rcp = [tx.next_fp2() for _ in range(6)]
         rh = [tx.next_fp2() for _ in range(4)]
         ri = [tx.next_fp2() for _ in range(tp.bit_length() - 1)]
         eq_c, eq_h, eq_i = self.eq(rcp), self.eq(rh), self.eq(ri)
-        A = np.zeros((HEAD_PAD * tp, 2), np.uint64)
-        B = np.zeros((HEAD_PAD * tp, 2), np.uint64)
-        C = np.zeros((HEAD_PAD * tp, 2), np.uint64)
-        per_head = t * (t + 1) // 2
-        vv = np.asarray(r["v"], np.int64).reshape(t, d)
-        for hh in range(HEAD_PAD):
-            C[hh * tp:(hh + 1) * tp] = eq_h[hh]
-            if hh >= h:
-                continue
-            wh = wt[hh * per_head:(hh + 1) * per_head]
-            for j in range(t):
-                ia = np.arange(j, t)
-                A[hh * tp + j] = _dot_base(eq_i[ia], wh[ia * (ia + 1) // 2 + j])
-                B[hh * tp + j] = _dot_base(eq_c[:64], vv[j, hh * 64:(hh + 1) * 64])
-        words.append(self.triple(A, B, C, tx))
-        tx = o.FpStream(seed, site_domain(layer, "norm_had"))
+        words.append(self.triple(*self.av_factors(wt, v_all, eq_i, eq_c, eq_h), tx))
+        tx = o.FpStream(seed, self.dom(layer, "norm_had"))
         words.append(self.triple(lift(emb(exc)), lift(emb(rcc)), lift(mask), tx))
-        tx = o.FpStream(seed, site_domain(layer, "qk"))
-        rj = [tx.next_fp2() for _ in range(tp.bit_length() - 1)]
+        # Q.K^T: the band's Q rows against all s cached K rows
+        tx = o.FpStream(seed, self.dom(layer, "qk"))
+        rj = [tx.next_fp2() for _ in range(sp.bit_length() - 1)]
         ri = [tx.next_fp2() for _ in range(tp.bit_length() - 1)]
         rh = [tx.next_fp2() for _ in range(4)]
         eq_i, eq_j, eq_h = self.eq(ri), self.eq(rj), self.eq(rh)
         qr = o.matrix_fold(np.ascontiguousarray(r["q"], np.int16).reshape(-1), eq_i, t, d, 0, d, 1024, 0, 0)
-        kr = o.matrix_fold(np.ascontiguousarray(r["k"], np.int16).reshape(-1), eq_j, t, d, 0, d, 1024, 0, 0)
+        kr = o.matrix_fold(np.ascontiguousarray(k_all, np.int16).reshape(-1), eq_j, s, d, 0, d, 1024, 0, 0)
         cc = np.ascontiguousarray(eq_h[np.arange(1024) // 64])
         words.append(self.triple(qr, kr, cc, tx))
         words.append(self.gemm(r["ln1_out"], lw["c_attn"], r["qkv_acc"], t, d, 3 * d, seed, layer, "gemm_qkv"))
@@ -468,10 +471,35 @@ class Schedule:
                                      "ln1_had"))
         return np.concatenate([np.asarray(w, np.uint64).reshape(-1, 2) for w in words])
 
+    def av_factors(self, wt, v_all, eq_i, eq_c, eq_h):
+        """The A.V contraction's factors over (head, key position j < s):
+        A = sum over the rows i with t0 + i >= j of eq_i[i] w[h,i,j] (band
+        packing), B = sum_c eq_c[c] v[j, h*64 + c], C = eq_h[h]."""
+        t, t0, s, sp, h, d = self.t, self.t0, self.s, self.sp, 12, 768
+        caus = t * t0 + t * (t + 1) // 2
+        wt = np.asarray(wt, np.int64)
+        A = np.zeros((HEAD_PAD * sp, 2), np.uint64)
+        B = np.zeros((HEAD_PAD * sp, 2), np.uint64)
+        C = np.zeros((HEAD_PAD * sp, 2), np.uint64)
+        vv = np.asarray(v_all, np.int64).reshape(s, d)
+        for hh in range(HEAD_PAD):
+            C[hh * sp:(hh + 1) * sp] = eq_h[hh]
+            if hh >= h:
+                continue
+            wh = wt[hh * caus:(hh + 1) * caus]
+            for j in range(s):
+                ia = np.arange(max(0, j - t0), t)
+                A[hh * sp + j] = _dot_base(eq_i[ia], wh[ia * t0 + ia * (ia + 1) // 2 + j])
+                B[hh * sp + j] = _dot_base(eq_c[:64], vv[j, hh * 64:(hh + 1) * 64])
+        return A, B, C
+
     def corrections(self, r, mac_seed, layer):
+        """x - mask of the boundary wires (the proof's t rows); one mask domain
+        per (chunk, layer, wire), row i at (tag << 32) | i."""
         out = []
         for w, name in enumerate(("x_in", "k", "v", "attn_block_out", "ffn_block_out")):
-            masks = self.o.chacha_fp_rows(mac_seed, (layer * 8 + w) << 32, self.t, 768).reshape(-1)
+            tag = (self.chunk << 16) | (layer * 8 + w)
+            masks = self.o.chacha_fp_rows(mac_seed, tag << 32, self.t, 768).reshape(-1)
             out.append(fp_sub(emb(np.asarray(r[name]).reshape(-1)), masks))
         return out
 

@@ -153,3 +153,41 @@ def test_argmax_keeps_the_last_maximum():
     assert argmax_last([1, 5, 3, 5, 2]) == 3
     assert argmax_last([7]) == 0
     assert argmax_last([-4, -4]) == 1
+
+
+def test_oracle_band_av_factors_evaluate_the_band_contraction(oracle, model2, package_built):
+    """The band schedule's A.V factors: sum over (head, key) of A B C equals
+    the multilinear value of the band's attention-value accumulators
+    av_acc(r_i, r_h, r_c) (band rows i, heads h, head dimensions c), so the
+    band packing (row i: window t0 + i + 1 at i t0 + i (i + 1) / 2) and the
+    key range (all t0 + q cached V rows) are consistent with the forward."""
+    from oracle.gpt2 import P, Schedule, band_witness, fp2_mul
+    from volta_zk_b200 import gpt2
+
+    ops, luts = OracleOps(oracle), gpt2.build_luts()
+    t, t0 = 11, 6
+    full = forward_model(ops, gpt2.prefill_tokens(t), model2, luts, row_shift=1)
+    band = band_witness(ops, full, model2, luts, t0)
+    q = t - t0
+    sch = Schedule(oracle, luts, q, t0, chunk=1)
+    assert (sch.tp, sch.sp, sch.rect) == (8, 16, 16 * 8 * 16)
+    stream = oracle.FpStream(bytes([0x33] * 32), 7)
+    rc = [stream.next_fp2() for _ in range(6)]
+    rh = [stream.next_fp2() for _ in range(4)]
+    ri = [stream.next_fp2() for _ in range(3)]
+    eq_c, eq_h, eq_i = sch.eq(rc), sch.eq(rh), sch.eq(ri)
+    lay = band["layers"][1]
+    A, B, C = sch.av_factors(lay["weights"], full["layers"][1]["v"], eq_i, eq_c, eq_h)
+    total = (0, 0)
+    for a, b, c in zip(A, B, C):
+        x = fp2_mul(fp2_mul(a, b), c)
+        total = ((total[0] + x[0]) % P, (total[1] + x[1]) % P)
+    acc = np.asarray(lay["av_acc"], np.int64).reshape(q, 768)
+    want = (0, 0)
+    for i in range(q):
+        for h in range(12):
+            for c in range(64):
+                v = int(acc[i, h * 64 + c]) % P
+                e = fp2_mul(fp2_mul(eq_i[i], eq_h[h]), eq_c[c])
+                want = ((want[0] + e[0] * v) % P, (want[1] + e[1] * v) % P)
+    assert total == want

@@ -59,3 +59,60 @@ def test_proof_needs_the_stable_softmax(prover):
     with gpt2.Gpt2Session(prover, model, 8, params=gpt2.LutParams(softmax_row_shift=False)) as s:
         with pytest.raises(accel.AccelError):
             gpt2.Gpt2Prover(s)
+
+
+@pytest.mark.parametrize("t,t0,chunk", [(16, 10, 1), (100, 93, 3)])
+def test_band_proof_matches_oracle_composition(prover, oracle, t, t0, chunk):
+    """A decode band's proof (rows t0 .. t-1 of a t-token forward, attention
+    over all t keys) against the oracle's band schedule over the oracle's
+    band witness, with the full forward's K and V as the cache: every word
+    and every boundary correction.  Non-power-of-two q and s included."""
+    from oracle.gpt2 import band_witness
+    from volta_zk_b200 import gpt2
+
+    layers = 2
+    model = gpt2.synthetic_model(n_layers=layers)
+    luts = gpt2.build_luts()
+    tokens = gpt2.prefill_tokens(t)
+    with gpt2.Gpt2Session(prover, model, t) as s, gpt2.Gpt2Prover(s) as gp:
+        s.forward(tokens)
+        pre, _, root = gp.prove(SEED, MAC_SEED, PAD_SEED)
+        with s.band(t0) as band:
+            words, per_layer = gp.prove_band(band, chunk, SEED, MAC_SEED)
+            corr = [[gp.correction(l, w) for w in range(5)] for l in range(layers)]
+            other, _ = gp.prove_band(band, chunk + 1, SEED, MAC_SEED)
+            half, _ = gp.prove_band(band, chunk, SEED, MAC_SEED, first=1, stride=2)
+        # the prefill proof is untouched by the band proofs
+        again, _, root2 = gp.prove(SEED, MAC_SEED, PAD_SEED)
+        assert np.array_equal(again, pre) and root2 == root
+    assert not np.array_equal(other, words)  # chunks have their own transcripts
+    assert np.array_equal(half, words[per_layer:2 * per_layer])
+    ops = OracleOps(oracle)
+    full = forward_model(ops, tokens, model, luts, row_shift=1)
+    bw = band_witness(ops, full, model, luts, t0)
+    sch = Schedule(oracle, luts, t - t0, t0, chunk)
+    assert per_layer * layers == words.shape[0]
+    for l in range(layers):
+        kv = (full["layers"][l]["k"], full["layers"][l]["v"])
+        exp = sch.layer(bw["layers"][l], model.layers[l], SEED, l, kv=kv)
+        got = words[l * per_layer:(l + 1) * per_layer]
+        assert got.shape == exp.shape, (l, got.shape, exp.shape)
+        bad = np.nonzero(np.any(got != exp, axis=1))[0]
+        assert bad.size == 0, f"layer {l}: first differing word {bad[:8]}"
+        for w, e in enumerate(sch.corrections(bw["layers"][l], MAC_SEED, l)):
+            assert np.array_equal(corr[l][w], e), (l, w)
+
+
+def test_band_proof_rejects_bad_chunk_and_foreign_band(prover):
+    from volta_zk_b200 import accel, gpt2
+
+    model = gpt2.synthetic_model(n_layers=1)
+    with gpt2.Gpt2Session(prover, model, 8) as s, gpt2.Gpt2Session(prover, model, 8) as s2, \
+            gpt2.Gpt2Prover(s) as gp:
+        s.forward(gpt2.prefill_tokens(8))
+        s2.forward(gpt2.prefill_tokens(8))
+        with s.band(4) as band, s2.band(4) as foreign:
+            with pytest.raises(accel.AccelError, match="chunk"):
+                gp.prove_band(band, 0, SEED, MAC_SEED)
+            with pytest.raises(accel.AccelError, match="session"):
+                gp.prove_band(foreign, 1, SEED, MAC_SEED)

@@ -419,8 +419,9 @@ class Gpt2Decoder:
 
 
 class Gpt2Prover:
-    """The prefill proof schedule over a Gpt2Session's witness
-    (libvolta_accel.so vzh_gpt2_prove; volta_zk_b200/host/gpt2_proof.cpp)."""
+    """The prefill proof schedule over a Gpt2Session's witness, and the band
+    proofs of decode chunks over the same session (libvolta_accel.so
+    vzh_gpt2_prove / vzh_gpt2_prove_band; volta_zk_b200/host/gpt2_proof.cpp)."""
 
     def __init__(self, session: Gpt2Session):
         from . import accel
@@ -436,8 +437,12 @@ class Gpt2Prover:
         L.vzh_gpt2_prove_layers.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_char_p, C.c_size_t, C.c_size_t,
                                             C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t),
                                             C.POINTER(C.c_size_t), C.c_void_p, C.c_char_p, C.c_size_t]
+        L.vzh_gpt2_prove_band.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_char_p, C.c_char_p, C.c_size_t,
+                                          C.c_size_t, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t),
+                                          C.POINTER(C.c_size_t), C.c_char_p, C.c_size_t]
         L.vzh_gpt2_correction.restype = C.c_uint64
         L.vzh_gpt2_correction.argtypes = [C.c_void_p, C.c_size_t, C.c_int]
+        self._rows = session.t  # rows of the last proof (the corrections' height)
         err = C.create_string_buffer(1024)
         self.h = L.vzh_gpt2_prover_open(session.h, err, 1024)
         if not self.h:
@@ -473,13 +478,36 @@ class Gpt2Prover:
                                              err, 1024)
         if rc != 0:
             raise accel.AccelError(err.value.decode())
+        self._rows = self.s.t
         return out[:written.value].copy(), per_layer.value, bytes(root)
+
+    def prove_band(self, band: "Gpt2Band", chunk: int, seed: bytes, mac_seed: bytes, first: int = 0,
+                   stride: int = 1):
+        """Proof of a decode band (rows t0 .. t-1 of the session's forward;
+        block_proof.rs prove_layer_phase1_band, model_proof.rs prove_response
+        chunks): the layer schedule over the band's q rows with attention over
+        all t0 + q keys, transcripts and mask domains of chunk (>= 1).
+        Returns (words as an (n, 2) u64 array, words per layer)."""
+        from . import accel
+
+        if band.s is not self.s:
+            raise accel.AccelError("the band is not of this prover's session")
+        out = self._out
+        written, per_layer = C.c_size_t(0), C.c_size_t(0)
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_gpt2_prove_band(self.h, band.h, chunk, seed, mac_seed, first, stride, out.ctypes.data,
+                                           self.cap, C.byref(written), C.byref(per_layer), err, 1024)
+        if rc != 0:
+            raise accel.AccelError(err.value.decode())
+        self._rows = band.q
+        return out[:written.value].copy(), per_layer.value
 
     def correction(self, layer: int, wire: int) -> np.ndarray:
         """Boundary corrections x - mask of wire (0 x_in, 1 k, 2 v, 3
-        attn_block_out, 4 ffn_block_out) of `layer`, t x d u64."""
+        attn_block_out, 4 ffn_block_out) of `layer` from the last proof: rows
+        x d u64 (t rows, or the band's q)."""
         buf = int(self.host.vzh_gpt2_correction(self.h, layer, wire))
-        return self.s.be.download(buf, self.s.t * D * 8, dtype=np.uint64)
+        return self.s.be.download(buf, self._rows * D * 8, dtype=np.uint64)
 
 
 def main(argv=None):

@@ -141,6 +141,10 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         dlsym(handle_, "volta_b200_softmax_lookup_columns_device"));
     ext_loaded_->av_factors =
         reinterpret_cast<decltype(ext_loaded_->av_factors)>(dlsym(handle_, "volta_b200_av_factors_device"));
+    ext_loaded_->softmax_lookup_columns_band = reinterpret_cast<decltype(ext_loaded_->softmax_lookup_columns_band)>(
+        dlsym(handle_, "volta_b200_softmax_lookup_columns_band_device"));
+    ext_loaded_->av_factors_band = reinterpret_cast<decltype(ext_loaded_->av_factors_band)>(
+        dlsym(handle_, "volta_b200_av_factors_band_device"));
     ext_loaded_->product_fold_round = reinterpret_cast<decltype(ext_loaded_->product_fold_round)>(
         dlsym(handle_, "volta_b200_product_fold_round_into_device"));
     ext_loaded_->product_tail =

@@ -37,6 +37,8 @@ struct ExtApi {
     decltype(&::volta_b200_triple_flush_device) triple_flush = nullptr;
     decltype(&::volta_b200_softmax_lookup_columns_device) softmax_lookup_columns = nullptr;
     decltype(&::volta_b200_av_factors_device) av_factors = nullptr;
+    decltype(&::volta_b200_softmax_lookup_columns_band_device) softmax_lookup_columns_band = nullptr;
+    decltype(&::volta_b200_av_factors_band_device) av_factors_band = nullptr;
     decltype(&::volta_b200_pack_pair_column_device) pack_pair_column = nullptr;
     decltype(&::volta_b200_product_fold_round_into_device) product_fold_round = nullptr;
     decltype(&::volta_b200_product_tail_device) product_tail = nullptr;

@@ -427,6 +427,28 @@ int vzh_gpt2_prove_layers(void* p, const uint8_t* seed, const uint8_t* mac_seed,
     });
 }
 
+// A decode band's proof (chunk >= 1) over the prover's session: layers first,
+// first + stride, ... in layer order; no weight commitment.
+int vzh_gpt2_prove_band(void* p, void* band, size_t chunk, const uint8_t* seed, const uint8_t* mac_seed,
+                        size_t first, size_t stride, vz_fp2* words, size_t cap, size_t* written, size_t* per_layer,
+                        char* err, size_t len) {
+    return guarded(err, len, [&] {
+        if (!band) throw AccelError("no band");
+        const Gpt2Proof pr = static_cast<Gpt2Prover*>(p)->prove_band(*static_cast<Gpt2Band*>(band), chunk, seed,
+                                                                     mac_seed, first, stride);
+        size_t total = 0;
+        for (const auto& w : pr.layer_words) total += w.size();
+        if (total > cap) throw AccelError("GPT-2 proof buffer too small");
+        size_t at = 0;
+        for (const auto& w : pr.layer_words) {
+            std::memcpy(words + at, w.data(), w.size() * sizeof(vz_fp2));
+            at += w.size();
+        }
+        *written = total;
+        *per_layer = pr.layer_words.empty() ? 0 : pr.layer_words[0].size();
+    });
+}
+
 // Band witness of rows t0 .. t-1 of a session's last forward (band.rs).
 void* vzh_gpt2_band_open(void* session, size_t t0, char* err, size_t len) {
     try {

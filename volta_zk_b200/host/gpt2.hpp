@@ -131,6 +131,7 @@ class Gpt2Band {
     void build();
     size_t t0() const { return t0_; }
     size_t q() const { return q_; }
+    const Gpt2Session& session() const { return s_; }
     // Buffer and element offset of a band wire of `layer` (Gpt2Wire).
     std::pair<uint64_t, size_t> wire(size_t layer, int w) const;
     uint64_t final_ln(int which) const { return fin_[which]; }  // 0 mean 1 var 2 rin 3 rout 4 acc 5 out
@@ -188,14 +189,15 @@ class Gpt2Decoder {
 // ---- the prefill proof schedule (gpt2_proof.cpp) -----------------------------
 
 // Sub-proof sites of one layer, in proof order; each draws from its own
-// private transcript FpStream(seed, gpt2_site_domain(layer, site)).
+// private transcript FpStream(seed, gpt2_site_domain(layer, site, chunk)),
+// chunk 0 for the prefill and c >= 1 for the c-th decode band of a response.
 enum Gpt2Site : int {
     kSiteDownRange = 1, kSiteGelu, kSiteUpRange, kSiteLn2Norm, kSiteLn2Rsqrt, kSiteProjRange, kSiteAvRange,
     kSiteNormRange, kSiteExp, kSiteRecip, kSiteScoresRange, kSiteQkvRange, kSiteLn1Norm, kSiteLn1Rsqrt,
     kSiteGemmDown = 16, kSiteGemmUp, kSiteLn2Had, kSiteGemmProj, kSiteAv, kSiteNormHad, kSiteQk, kSiteGemmQkv,
     kSiteLn1Had
 };
-uint64_t gpt2_site_domain(size_t layer, int site);
+uint64_t gpt2_site_domain(size_t layer, int site, size_t chunk = 0);
 
 struct Gpt2Proof {
     std::vector<std::vector<Fp2>> layer_words;  // per proved layer, the sub-proofs' words in site order
@@ -226,8 +228,20 @@ class Gpt2Prover {
     // independent), with the weight commitment when with_pcs.
     Gpt2Proof prove_layers(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
                            size_t first, size_t stride, bool with_pcs);
+    // Prove a decode band of the same session (rust/volta-proto/src/
+    // block_proof.rs:10112-10125 prove_layer_phase1_band; model_proof.rs:2710
+    // prove_response's deferred chunks): the layer schedule over the band's q
+    // rows, with the attention sites over q_pad x s_pad rectangles (s = t0 + q
+    // keys, the session's K/V rows 0 .. s - 1: the earlier rows are the cache
+    // segments, the band's own rows its new ones).  `band` must be built from
+    // this prover's session; chunk >= 1 separates the band's transcripts and
+    // mask domains from the prefill's and from other chunks'.  No weight
+    // commitment (one per response, with the prefill).
+    Gpt2Proof prove_band(const Gpt2Band& band, size_t chunk, const uint8_t seed[32], const uint8_t mac_seed[32],
+                         size_t first, size_t stride);
     // Corrections x - mask of boundary wire w (0 x_in, 1 k, 2 v, 3
-    // attn_block_out, 4 ffn_block_out) of layer l: t x d u64.
+    // attn_block_out, 4 ffn_block_out) of layer l: rows x d u64 (the last
+    // proof's rows: t, or the band's q).
     uint64_t correction(size_t layer, int w) const { return corrections_.at(layer).at(w); }
 
    private:
@@ -237,11 +251,13 @@ class Gpt2Prover {
         size_t words = 0;
         size_t at = 0;  // offset of its raw messages in the layer's buffer
     };
-    std::vector<Slot> enqueue_layer(size_t l, Owned& own, const uint8_t seed[32], const uint8_t mac_seed[32]);
+    std::vector<Slot> enqueue_layer(size_t l, Owned& own, const uint8_t seed[32], const uint8_t mac_seed[32],
+                                    const Gpt2Band* band, size_t chunk);
+    Gpt2Proof run(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32], size_t first,
+                  size_t stride, bool with_pcs, const Gpt2Band* band, size_t chunk);
 
     Gpt2Session& s_;
     Backend& b_;
-    size_t t_pad_ = 0, rect_ = 0;
     std::map<uint32_t, uint64_t> range_;
     uint64_t gelu_pairs_ = 0, rsqrt_pairs_ = 0, expgap_pairs_ = 0, recip_pairs_ = 0, shifts_ = 0;
     uint64_t exp_pad_out_ = 0, recip_pad_out_ = 0;

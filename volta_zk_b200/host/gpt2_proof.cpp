@@ -87,15 +87,14 @@ std::vector<Fp2> draw(FpStream& tx, size_t n) {
 
 }  // namespace
 
-uint64_t gpt2_site_domain(size_t layer, int site) {
-    return 0x7000000000000000ull | (static_cast<uint64_t>(layer) << 16) | (static_cast<uint64_t>(site) << 8);
+uint64_t gpt2_site_domain(size_t layer, int site, size_t chunk) {
+    return 0x7000000000000000ull | (static_cast<uint64_t>(chunk) << 32) | (static_cast<uint64_t>(layer) << 16) |
+           (static_cast<uint64_t>(site) << 8);
 }
 
 Gpt2Prover::Gpt2Prover(Gpt2Session& s) : s_(s), b_(s.backend()) {
     const Gpt2Shape& sh = s.shape();
     if (!sh.shifts.row_shift) throw AccelError("the GPT-2 proof needs the row-shifted (stable) softmax");
-    t_pad_ = pow2_at_least(sh.t);
-    rect_ = kHeadPad * t_pad_ * t_pad_;
     try {
         auto up = [&](const void* src, size_t bytes) {
             const uint64_t id = own(b_.alloc(bytes));
@@ -271,15 +270,29 @@ PendingLogup lookup_enqueue(Backend& b, Owned& own, uint64_t qcols, size_t qcoun
 // One layer: enqueue every sub-proof (nothing is downloaded); returns the
 // pending message slots in proof order.
 std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, const uint8_t seed[32],
-                                                        const uint8_t mac_seed[32]) {
+                                                        const uint8_t mac_seed[32], const Gpt2Band* band,
+                                                        size_t chunk) {
     const Api& A = b_.api();
     void* ctx = b_.ctx();
     const Gpt2Shape& sh = s_.shape();
     const Gpt2Shifts& f = sh.shifts;
-    const size_t t = sh.t, d = sh.d, dff = sh.dff, h = sh.heads, tp = t_pad_;
+    // rows t of the proof (the band's q, or the prefill's t) at positions
+    // t0 .. t0 + t - 1, attending over the session's `keys` = t0 + t rows
+    // (BandShape: q, s = t0 + q; the prefill is the square band t0 = 0)
+    const size_t keys = sh.t, t0 = band ? band->t0() : 0, t = keys - t0;
+    const size_t d = sh.d, dff = sh.dff, h = sh.heads;
+    const size_t tp = pow2_at_least(t), sp = pow2_at_least(keys), rect = kHeadPad * tp * sp;
     const size_t d_pad = pow2_at_least(d), q_pad = pow2_at_least(3 * d), f_pad = pow2_at_least(dff);
-    const size_t packed = sh.packed();
-    auto W = [&](int w) { return s_.wire(l, w); };
+    const size_t packed = h * (t * t0 + t * (t + 1) / 2);  // causal-packed attention entries (band packing)
+    struct Wire {
+        uint64_t id;
+        size_t off;  // elements
+    };
+    auto W = [&](int w) -> Wire {
+        if (!band) return Wire{s_.wire(l, w), 0};
+        const auto bw = band->wire(l, w);
+        return Wire{bw.first, bw.second};
+    };
     auto alloc = [&](size_t bytes) { return own.add(b_.alloc(bytes)); };
     std::vector<Slot> slots;
 
@@ -287,12 +300,14 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     const int boundary[5] = {kXin, kK, kV, kAttnOut, kFfnOut};
     std::vector<uint64_t> corr(5);
     for (int w = 0; w < 5; ++w) {
+        // one mask domain per (chunk, layer, wire), row r at (tag << 32) | r
+        const uint64_t tag = (static_cast<uint64_t>(chunk) << 16) | (l * 8 + w);
         const uint64_t masks = alloc(t * d * sizeof(uint64_t));
-        b_.check(A.volta_cuda_mock_correlation_sub_masks_device(ctx, masks, 0, mac_seed,
-                                                                static_cast<uint64_t>(l * 8 + w) << 32, t, d),
+        b_.check(A.volta_cuda_mock_correlation_sub_masks_device(ctx, masks, 0, mac_seed, tag << 32, t, d),
                  "mock_correlation_sub_masks_device");
         corr[w] = b_.alloc(t * d * sizeof(uint64_t));
-        b_.check(A.volta_cuda_subfield_corrections_device(ctx, W(boundary[w]), 0, masks, 0, corr[w], 0, t * d, 0),
+        const Wire x = W(boundary[w]);
+        b_.check(A.volta_cuda_subfield_corrections_device(ctx, x.id, x.off, masks, 0, corr[w], 0, t * d, 0),
                  "subfield_corrections_device");
     }
     corrections_[l] = corr;
@@ -302,7 +317,7 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     std::vector<std::unique_ptr<PendingLogup>> logups;
     auto add_logup = [&](int site, uint64_t qcols, size_t qcount, size_t shifts_off, size_t n_f, uint64_t t_col,
                          size_t n_t, uint64_t mult) {
-        FpStream chal(seed, gpt2_site_domain(l, site));
+        FpStream chal(seed, gpt2_site_domain(l, site, chunk));
         logups.push_back(std::make_unique<PendingLogup>(
             lookup_enqueue(b_, own, qcols, qcount, shifts_, shifts_off, n_f, t_col, n_t, mult, chal)));
         sides.push_back(&logups.back()->side[0]);
@@ -312,12 +327,12 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         slots.push_back(sl);
     };
     // a requant site: remainders of (acc, out) padded to row_pad x col_pad
-    auto range_site = [&](int site, uint64_t acc, uint64_t out, size_t rows, size_t cols, size_t row_pad,
-                          size_t col_pad, uint32_t shift) {
+    auto range_site = [&](int site, Wire acc, Wire out, size_t rows, size_t cols, size_t row_pad, size_t col_pad,
+                          uint32_t shift) {
         const size_t n = row_pad * col_pad;
         const uint64_t cc = alloc(2 * n * sizeof(uint64_t));
-        b_.check(A.volta_cuda_requant_columns_device(ctx, acc, 0, out, 0, cc, 0, err_, 0, rows, cols, row_pad,
-                                                     col_pad, 1, shift),
+        b_.check(A.volta_cuda_requant_columns_device(ctx, acc.id, acc.off, out.id, out.off, cc, 0, err_, 0, rows,
+                                                     cols, row_pad, col_pad, 1, shift),
                  "requant_columns_device");
         const uint64_t mult = alloc((size_t{1} << shift) * sizeof(uint32_t));  // the histograms clear it
         b_.check(A.volta_cuda_histogram_fp_device(ctx, cc, 0, mult, 0, n, size_t{1} << shift),
@@ -325,13 +340,12 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         add_logup(site, cc, 1, 0, n, range_.at(shift), size_t{1} << shift, mult);
     };
     // a pair site: (in, out) padded, packed in + 2^16 out
-    auto pair_site = [&](int site, uint64_t in, int in_kind, uint64_t out, size_t rows, size_t cols,
-                         size_t row_pad, size_t col_pad, uint64_t pad_in, uint64_t pad_out, uint64_t table,
-                         bool signed_in) {
+    auto pair_site = [&](int site, Wire in, int in_kind, Wire out, size_t rows, size_t cols, size_t row_pad,
+                         size_t col_pad, uint64_t pad_in, uint64_t pad_out, uint64_t table, bool signed_in) {
         const size_t n = row_pad * col_pad;
         const uint64_t cc = alloc(2 * n * sizeof(uint64_t));
-        b_.check(A.volta_cuda_pair_columns_device(ctx, in, 0, out, 0, cc, 0, rows, cols, row_pad, col_pad, pad_in,
-                                                  pad_out, in_kind, 0),
+        b_.check(A.volta_cuda_pair_columns_device(ctx, in.id, in.off, out.id, out.off, cc, 0, rows, cols, row_pad,
+                                                  col_pad, pad_in, pad_out, in_kind, 0),
                  "pair_columns_device");
         const uint64_t mult = alloc((size_t{1} << 16) * sizeof(uint32_t));
         if (signed_in)
@@ -359,23 +373,28 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     // remainders, [4] reciprocals, [5] mask; [6] reciprocal inputs, [7] packed
     // (input, reciprocal)
     uint64_t sm[8];
-    for (int k = 0; k < 8; ++k) sm[k] = alloc((k < 6 ? rect_ : kHeadPad * tp) * sizeof(uint64_t));
-    b_.check(b_.ext().softmax_lookup_columns(ctx, W(kScoresQ), 0, W(kRowShift), 0, W(kExpOut), 0, W(kDenoms), 0,
-                                             W(kRecips), 0, W(kWeights), 0, sm, err_, 0, t, h, rect_, kHeadPad, tp,
-                                             exp_pad_out_, f.softmax_norm, f.recip_den, kRecipPadInput,
-                                             recip_pad_out_),
-             "volta_b200_softmax_lookup_columns_device");
+    for (int k = 0; k < 8; ++k) sm[k] = alloc((k < 6 ? rect : kHeadPad * tp) * sizeof(uint64_t));
+    {
+        const Wire sq = W(kScoresQ), rs = W(kRowShift), ex = W(kExpOut), dn = W(kDenoms), rc = W(kRecips),
+                   wt = W(kWeights);
+        if (!b_.ext().softmax_lookup_columns_band) throw AccelError("backend lacks the band softmax columns");
+        b_.check(b_.ext().softmax_lookup_columns_band(ctx, sq.id, sq.off, rs.id, rs.off, ex.id, ex.off, dn.id, dn.off,
+                                                      rc.id, rc.off, wt.id, wt.off, sm, err_, 0, t, t0, h, rect,
+                                                      kHeadPad, tp, exp_pad_out_, f.softmax_norm, f.recip_den,
+                                                      kRecipPadInput, recip_pad_out_),
+                 "volta_b200_softmax_lookup_columns_band_device");
+    }
     {   // softmax norm remainders on Range(14)
         const uint64_t mult = alloc((size_t{1} << f.softmax_norm) * sizeof(uint32_t));
-        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[3], 0, mult, 0, rect_, size_t{1} << f.softmax_norm),
+        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[3], 0, mult, 0, rect, size_t{1} << f.softmax_norm),
                  "histogram_fp_device");
-        add_logup(kSiteNormRange, sm[3], 1, 0, rect_, range_.at(f.softmax_norm), size_t{1} << f.softmax_norm, mult);
+        add_logup(kSiteNormRange, sm[3], 1, 0, rect, range_.at(f.softmax_norm), size_t{1} << f.softmax_norm, mult);
     }
     {   // (gap, exp) pairs on the ExpGap table
         const uint64_t mult = alloc((size_t{1} << 16) * sizeof(uint32_t));
-        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[0], 0, mult, 0, rect_, size_t{1} << 16),
+        b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[0], 0, mult, 0, rect, size_t{1} << 16),
                  "histogram_fp_device");
-        add_logup(kSiteExp, sm[1], 1, 0, rect_, expgap_pairs_, size_t{1} << 16, mult);
+        add_logup(kSiteExp, sm[1], 1, 0, rect, expgap_pairs_, size_t{1} << 16, mult);
     }
     {   // (denom >> den_shift, rc) pairs on the 18-bit reciprocal table
         const size_t n = kHeadPad * tp;
@@ -384,7 +403,7 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
                  "histogram_fp_device");
         add_logup(kSiteRecip, sm[7], 1, 0, n, recip_pairs_, size_t{1} << kRecipBits, mult);
     }
-    range_site(kSiteScoresRange, W(kScoresAcc), W(kScoresQ), 1, packed, 1, rect_, f.scores);
+    range_site(kSiteScoresRange, W(kScoresAcc), W(kScoresQ), 1, packed, 1, rect, f.scores);
     range_site(kSiteQkvRange, W(kQkvAcc), W(kQkvQ), t, 3 * d, tp, q_pad, f.qkv);
     range_site(kSiteLn1Norm, W(kLn1Acc), W(kLn1Out), t, d, tp, d_pad, f.ln_norm);
     pair_site(kSiteLn1Rsqrt, W(kLn1Rin), 1, W(kLn1Rout), 1, t, 1, tp, 0, fp_from_i64(rsqrt[0]), rsqrt_pairs_, false);
@@ -408,20 +427,20 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         return eq;
     };
     // weight GEMM: claim acc~(r_i, r_j), folds, product sumcheck over k
-    auto gemm = [&](int site, uint64_t x, uint64_t w, uint64_t acc, size_t m, size_t k, size_t n) {
-        FpStream tx(seed, gpt2_site_domain(l, site));
+    auto gemm = [&](int site, Wire x, uint64_t w, Wire acc, size_t m, size_t k, size_t n) {
+        FpStream tx(seed, gpt2_site_domain(l, site, chunk));
         const size_t m_pad = pow2_at_least(m), n_pad = pow2_at_least(n), k_pad = pow2_at_least(k);
         const std::vector<Fp2> rj = draw(tx, log2_exact(n_pad)), ri = draw(tx, log2_exact(m_pad));
         const uint64_t eq_j = eq_table(rj), eq_i = eq_table(ri);
         const size_t kb = log2_exact(k_pad);
         const uint64_t msgs = slot_buffer(1 + 2 * kb + 2);
         const uint64_t acc_r = alloc(n_pad * sizeof(Fp2));
-        b_.check(A.volta_cuda_matrix_fold_device(ctx, acc, 0, eq_i, 0, acc_r, 0, m, n, 0, n, n_pad, 1, 0),
+        b_.check(A.volta_cuda_matrix_fold_device(ctx, acc.id, acc.off, eq_i, 0, acc_r, 0, m, n, 0, n, n_pad, 1, 0),
                  "matrix_fold_device");
         b_.check(A.volta_cuda_fp2_row_dots_device(ctx, acc_r, 0, n_pad, eq_j, 0, n_pad, msgs, 0, 1, n_pad),
                  "fp2_row_dots_device");
         const uint64_t av = alloc(k_pad * sizeof(Fp2)), bv = alloc(k_pad * sizeof(Fp2));
-        b_.check(A.volta_cuda_matrix_fold_device(ctx, x, 0, eq_i, 0, av, 0, m, k, 0, k, k_pad, 0, 0),
+        b_.check(A.volta_cuda_matrix_fold_device(ctx, x.id, x.off, eq_i, 0, av, 0, m, k, 0, k, k_pad, 0, 0),
                  "matrix_fold_device");
         b_.check(A.volta_cuda_matrix_fold_device(ctx, w, 0, eq_j, 0, bv, 0, k, n, 0, n, k_pad, 0, 1),
                  "matrix_fold_device");
@@ -429,14 +448,15 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     };
     // LayerNorm product (x - mu) * (r g) over t_pad x d_pad
     auto ln_product = [&](int site, int x, int mean, int rout, int gain) {
-        FpStream tx(seed, gpt2_site_domain(l, site));
+        FpStream tx(seed, gpt2_site_domain(l, site, chunk));
         const uint64_t mu = alloc(tp * sizeof(uint64_t)), rs = alloc(tp * sizeof(uint64_t));
-        b_.check(A.volta_cuda_pad_base_vector_device(ctx, W(mean), 0, mu, 0, t, tp, 0, 1), "pad_base_vector_device");
-        b_.check(A.volta_cuda_pad_base_vector_device(ctx, W(rout), 0, rs, 0, t, tp, 0, 0), "pad_base_vector_device");
+        const Wire wm = W(mean), wr = W(rout), wx = W(x);
+        b_.check(A.volta_cuda_pad_base_vector_device(ctx, wm.id, wm.off, mu, 0, t, tp, 0, 1), "pad_base_vector_device");
+        b_.check(A.volta_cuda_pad_base_vector_device(ctx, wr.id, wr.off, rs, 0, t, tp, 0, 0), "pad_base_vector_device");
         const size_t n = tp * d_pad;
         const uint64_t cen = alloc(n * sizeof(Fp2)), sc = alloc(n * sizeof(Fp2));
-        b_.check(A.volta_cuda_ln_hadamard_factors_device(ctx, W(x), 0, mu, 0, rs, 0, s_.weight(l, gain), 0, cen, 0,
-                                                         sc, 0, t, d, tp, d_pad),
+        b_.check(A.volta_cuda_ln_hadamard_factors_device(ctx, wx.id, wx.off, mu, 0, rs, 0, s_.weight(l, gain), 0, cen,
+                                                         0, sc, 0, t, d, tp, d_pad),
                  "ln_hadamard_factors_device");
         const uint64_t msgs = slot_buffer(2 * log2_exact(n) + 2);
         product_rounds(b_, own, cen, sc, n, tx, msgs, 0);
@@ -453,23 +473,26 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     ln_product(kSiteLn2Had, kAttnOut, kLn2Mean, kLn2Rout, 6);
     gemm(kSiteGemmProj, W(kAvQ), s_.weight(l, 1), W(kProjAcc), t, d, d);
     {   // A.V over (head, key position)
-        FpStream tx(seed, gpt2_site_domain(l, kSiteAv));
+        FpStream tx(seed, gpt2_site_domain(l, kSiteAv, chunk));
         const std::vector<Fp2> rc = draw(tx, log2_exact(sh.head_dim)), rh = draw(tx, 4), ri = draw(tx, log2_exact(tp));
         const uint64_t eq_c = eq_table(rc), eq_h = eq_table(rh), eq_i = eq_table(ri);
-        const size_t n = kHeadPad * tp;
+        const size_t n = kHeadPad * sp;  // (head, key position)
         const uint64_t parts[3] = {alloc(n * sizeof(Fp2)), alloc(n * sizeof(Fp2)), alloc(n * sizeof(Fp2))};
-        b_.check(b_.ext().av_factors(ctx, W(kWeights), 0, W(kV), 0, eq_i, 0, eq_c, 0, eq_h, 0, parts, t, h,
-                                     sh.head_dim, kHeadPad, tp),
-                 "volta_b200_av_factors_device");
+        const Wire wt = W(kWeights);
+        if (!b_.ext().av_factors_band) throw AccelError("backend lacks the band A.V factors");
+        // V over every cached row 0 .. keys - 1 (the session's rows)
+        b_.check(b_.ext().av_factors_band(ctx, wt.id, wt.off, s_.wire(l, kV), 0, eq_i, 0, eq_c, 0, eq_h, 0, parts, t,
+                                          t0, h, sh.head_dim, kHeadPad, tp, sp),
+                 "volta_b200_av_factors_band_device");
         triple(parts[0], parts[1], parts[2], n, tx, false);
     }
     {   // softmax norm product over the attention rectangle (Fp columns: exp, reciprocal, mask)
-        FpStream tx(seed, gpt2_site_domain(l, kSiteNormHad));
-        triple(sm[2], sm[4], sm[5], rect_, tx, true);
+        FpStream tx(seed, gpt2_site_domain(l, kSiteNormHad, chunk));
+        triple(sm[2], sm[4], sm[5], rect, tx, true);
     }
     {   // Q.K^T over (head, dimension)
-        FpStream tx(seed, gpt2_site_domain(l, kSiteQk));
-        const std::vector<Fp2> rj = draw(tx, log2_exact(tp)), ri = draw(tx, log2_exact(tp)), rh = draw(tx, 4);
+        FpStream tx(seed, gpt2_site_domain(l, kSiteQk, chunk));
+        const std::vector<Fp2> rj = draw(tx, log2_exact(sp)), ri = draw(tx, log2_exact(tp)), rh = draw(tx, 4);
         const uint64_t eq_i = eq_table(ri), eq_j = eq_table(rj);
         const std::vector<Fp2> eh = eq_host(rh);
         std::vector<Fp2> c(d_pad, Fp2{0, 0});
@@ -477,9 +500,11 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         const uint64_t cid = alloc(d_pad * sizeof(Fp2));
         b_.upload(cid, 0, c.data(), d_pad * sizeof(Fp2));
         const uint64_t qr = alloc(d_pad * sizeof(Fp2)), kr = alloc(d_pad * sizeof(Fp2));
-        b_.check(A.volta_cuda_matrix_fold_device(ctx, W(kQ), 0, eq_i, 0, qr, 0, t, d, 0, d, d_pad, 0, 0),
+        const Wire wq = W(kQ);
+        b_.check(A.volta_cuda_matrix_fold_device(ctx, wq.id, wq.off, eq_i, 0, qr, 0, t, d, 0, d, d_pad, 0, 0),
                  "matrix_fold_device");
-        b_.check(A.volta_cuda_matrix_fold_device(ctx, W(kK), 0, eq_j, 0, kr, 0, t, d, 0, d, d_pad, 0, 0),
+        // K over every cached row 0 .. keys - 1
+        b_.check(A.volta_cuda_matrix_fold_device(ctx, s_.wire(l, kK), 0, eq_j, 0, kr, 0, keys, d, 0, d, d_pad, 0, 0),
                  "matrix_fold_device");
         triple(qr, kr, cid, d_pad, tx, false);
     }
@@ -489,11 +514,23 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
 }
 
 Gpt2Proof Gpt2Prover::prove(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32]) {
-    return prove_layers(seed, mac_seed, pad_seed, 0, 1, true);
+    return run(seed, mac_seed, pad_seed, 0, 1, true, nullptr, 0);
 }
 
 Gpt2Proof Gpt2Prover::prove_layers(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
                                    size_t first, size_t stride, bool with_pcs) {
+    return run(seed, mac_seed, pad_seed, first, stride, with_pcs, nullptr, 0);
+}
+
+Gpt2Proof Gpt2Prover::prove_band(const Gpt2Band& band, size_t chunk, const uint8_t seed[32],
+                                 const uint8_t mac_seed[32], size_t first, size_t stride) {
+    if (&band.session() != &s_) throw AccelError("the band is not of this prover's session");
+    if (!chunk || chunk >= (size_t{1} << 14)) throw AccelError("band chunk index must be in 1 .. 2^14 - 1");
+    return run(seed, mac_seed, nullptr, first, stride, false, &band, chunk);
+}
+
+Gpt2Proof Gpt2Prover::run(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
+                          size_t first, size_t stride, bool with_pcs, const Gpt2Band* band, size_t chunk) {
     const Api& A = b_.api();
     void* ctx = b_.ctx();
     const Gpt2Shape& sh = s_.shape();
@@ -518,7 +555,7 @@ Gpt2Proof Gpt2Prover::prove_layers(const uint8_t seed[32], const uint8_t mac_see
         Owned lay(b_);
         raw.emplace_back();
         LayerRaw& lr = raw.back();
-        lr.slots = enqueue_layer(l, lay, seed, mac_seed);
+        lr.slots = enqueue_layer(l, lay, seed, mac_seed, band, chunk);
         for (Slot& sl : lr.slots) {
             sl.at = lr.total;
             lr.total += sl.logup ? sl.logup->side[0].msg_total + sl.logup->side[1].msg_total : sl.words;
