@@ -767,8 +767,12 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
     layer: 14 LogUp lookup instances, the weight-GEMM, attention and
     LayerNorm/softmax product sumchecks, VOLE-MAC boundary corrections) +
     the Ligero commitment of the weights.  With N GPUs every rank runs the
-    forward (replicas) and proves layers rank, rank + N, ...; rank 0 also
-    commits; the words meet in one NCCL all-gather."""
+    forward (replicas) and proves its share: the (layer, site) sub-proofs
+    are independent over the same witness, so gpt2.split_sites deals whole
+    layers (or layer parts) and the commitment out by measured costs,
+    largest first onto the least-loaded GPU; the words meet in two NCCL
+    all-gathers (word counts per site, then the words) and are assembled in
+    layer and site order, identical to the one-GPU proof."""
     import torch
 
     from volta_zk_b200 import gpt2
@@ -780,30 +784,40 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
     sess = gpt2.Gpt2Session(prover, model, t)
     sess.forward(tokens)  # uploads the tokens: resident from here on
     gp = gpt2.Gpt2Prover(sess)
-    mine = list(range(rank, gpt2.LAYERS, world))
-    per_rank = (gpt2.LAYERS + world - 1) // world
+    split, pcs_rank = gpt2.split_sites(world)
+    units = split[rank]
+    mine = [l for l, m in units if m & (1 << gpt2.SITE_CORRECTIONS)]  # layers whose corrections this rank makes
     dev = torch.device("cuda", local_rank)
 
-    def gather(words, per_layer):
-        """Every rank's words -> all layers in order (on every rank)."""
+    def gather(words, sites):
+        """Every rank's words -> the proof in layer and site order (on every rank)."""
         if world == 1:
             return words
-        buf = np.zeros((per_rank * per_layer, 2), dtype=np.uint64)
+        counts = np.zeros((gpt2.LAYERS, 25), np.int64)  # words of (layer, site), 0 where another rank proves it
+        for (layer, _), us in zip(units, sites):
+            for site, n in us:
+                counts[layer, site] = n
+        c = torch.from_numpy(counts).to(dev)
+        call = torch.empty((world,) + tuple(c.shape), dtype=c.dtype, device=dev)
+        dist.all_gather_into_tensor(call, c)
+        counts_all = call.cpu().numpy()
+        totals = counts_all.reshape(world, -1).sum(axis=1)
+        buf = np.zeros((int(totals.max()), 2), dtype=np.uint64)
         buf[:words.shape[0]] = words
         src = torch.from_numpy(buf.view(np.int64)).to(dev)
         out = torch.empty((world,) + tuple(src.shape), dtype=src.dtype, device=dev)
         dist.all_gather_into_tensor(out, src)
-        allw = out.cpu().numpy().view(np.uint64).reshape(world, per_rank, per_layer, 2)
-        return np.concatenate([allw[l % world, l // world] for l in range(gpt2.LAYERS)])
-
-    # the weight commitment goes to the last rank: with 12 layers over 8 GPUs
-    # ranks 0-3 prove two layers and ranks 4-7 one, so the commitment balances
-    pcs_rank = world - 1
+        allw = out.cpu().numpy().view(np.uint64)
+        pieces = []
+        for g in range(world):
+            sites_g = [[(k, int(counts_all[g, l, k])) for k in gpt2.SITE_ORDER if (m >> k) & 1] for l, m in split[g]]
+            pieces.append((split[g], allw[g, :int(totals[g])], sites_g))
+        return gpt2.assemble_units(pieces)
 
     def step(host_tokens=None):
         sess.forward(host_tokens)
-        words, per_layer, root = gp.prove(PROOF_SEED, MAC_SEED, PAD_SEED, rank, world, rank == pcs_rank)
-        return gather(words, per_layer), per_layer, root
+        words, sites, root = gp.prove_units(PROOF_SEED, MAC_SEED, PAD_SEED, units, rank == pcs_rank)
+        return gather(words, sites), None, root
 
     def barrier():
         torch.cuda.synchronize()
@@ -874,7 +888,7 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
         barrier()
         corr_bytes = gpt2.LAYERS * 5 * t * gpt2.D * 8
         e2e = {"value": round(e2e_s, 6), "unit": "s/proof", "h2d_bytes_per_step": 4 * t * world,
-               "d2h_bytes_per_step": int(ew.shape[0]) * 16 * world + 8 * gpt2.VOCAB + 32 + corr_bytes,
+               "d2h_bytes_per_step": int(ew.shape[0]) * 16 + 8 * gpt2.VOCAB + 32 + corr_bytes,
                "inputs": "token ids from pinned host memory; out: proof words, PCS root, logits of the last "
                          "position and every boundary correction (the proof's VOLE-MAC payload)",
                "proof_matches_resident": bool(np.array_equal(ew, words)),
@@ -925,9 +939,10 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
                                "proofs + weight commitment)",
                    "model": "gpt2-small (12 layers, d 768, 12 heads, MLP 3072, vocab 50257), int16 fixed point, "
                             "LutParams defaults with the stable softmax",
-                   "parallelism": f"forward replicated, layers {gpt2.LAYERS} split over {world} GPU(s) (rank r: "
-                                  f"layers r, r + {world}, ...; weight commitment on rank {world - 1}), one NCCL "
-                                  f"all-gather of the words" if world > 1 else "one proof on one GPU",
+                   "parallelism": f"forward replicated; the {gpt2.LAYERS} layer proofs (or layer parts) and the "
+                                  f"weight commitment dealt over {world} GPUs largest first onto the least-loaded "
+                                  f"GPU (commitment on rank {pcs_rank}); NCCL all-gathers of the per-site word "
+                                  f"counts and the words" if world > 1 else "one proof on one GPU",
                    "l2": "working set (witness 1.8 GB, lookup trees, 2.1 GB codeword) far larger than L2",
                    "timing_policy": "wall-only counters"},
         "rho": round(step_s / fwd_s, 2), "forward_s": round(fwd_s, 6),

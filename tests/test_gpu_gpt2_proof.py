@@ -116,3 +116,39 @@ def test_band_proof_rejects_bad_chunk_and_foreign_band(prover):
                 gp.prove_band(band, 0, SEED, MAC_SEED)
             with pytest.raises(accel.AccelError, match="session"):
                 gp.prove_band(foreign, 1, SEED, MAC_SEED)
+
+
+@pytest.mark.parametrize("split", ["world2", "world8", "parts", "sites"])
+def test_site_units_reassemble_the_proof(prover, split):
+    """A proof split over GPUs by (layer, site) units (the ranks taking turns
+    on one device): gpt2.split_sites' splits, a split into layer parts and
+    one into single sites.  The units' words reassemble to the one-GPU proof,
+    the committing rank's root is the one-GPU root, and each layer's
+    corrections come from the rank holding its site 0."""
+    from volta_zk_b200 import gpt2
+
+    t, layers = 16, 2
+    model = gpt2.synthetic_model(n_layers=layers)
+    with gpt2.Gpt2Session(prover, model, t) as s, gpt2.Gpt2Prover(s) as gp:
+        s.forward(gpt2.prefill_tokens(t))
+        full, _, root = gp.prove(SEED, MAC_SEED, PAD_SEED)
+        corr = [[gp.correction(l, w) for w in range(5)] for l in range(layers)]
+        if split.startswith("world"):
+            per_rank, commit = gpt2.split_sites(int(split[5:]), t, layers=layers)
+        elif split == "parts":
+            per_rank = [[(0, gpt2.ALL_SITES), (1, gpt2.PART_REST)], [(1, gpt2.PART_ATTENTION)], []]
+            commit = 2
+        else:  # every site of layer 1 its own unit on its own rank, layer 0 whole
+            per_rank = [[(0, gpt2.ALL_SITES)]] + [[(1, 1 << k)] for k in [0] + gpt2.SITE_ORDER]
+            commit = 1
+        pieces = []
+        for g, units in enumerate(per_rank):
+            words, sites, r = gp.prove_units(SEED, MAC_SEED, PAD_SEED, units, g == commit)
+            if g == commit:
+                assert r == root
+            pieces.append((units, words, sites))
+            for l, m in units:
+                if m & 1:
+                    for w in range(5):
+                        assert np.array_equal(gp.correction(l, w), corr[l][w])
+    assert np.array_equal(gpt2.assemble_units(pieces, layers=layers), full)

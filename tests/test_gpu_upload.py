@@ -188,3 +188,47 @@ def test_two_contexts_concurrently(prover, oracle):
             be_b.free(i)
     finally:
         other.close()
+
+
+def test_resident_arena_best_fit_reuse_and_trim():
+    """The arena's free list: a request reuses the smallest free buffer that
+    fits (the lowest slot among equal capacities), a stale id is rejected,
+    and a trim releases every free buffer (later requests allocate anew)."""
+    from volta_zk_b200 import accel
+
+    be = accel.CudaBackend(policy=0)
+    try:
+        s0 = be.stats()
+        sizes = [4096, 1 << 20, 65536, 65536, 1 << 16 | 16]
+        ids = [be.alloc(n) for n in sizes]
+        slot = lambda i: i & 0xFFFFFFFF
+        for i in ids:
+            be.free(i)
+        s1 = be.stats()
+        assert s1.allocation_calls - s0.allocation_calls == len(sizes)
+        a = be.alloc(60000)  # best fit: a 65536 buffer, the lower slot of the two
+        assert slot(a) == min(slot(ids[2]), slot(ids[3]))
+        b = be.alloc(65536)  # the other 65536 buffer
+        assert slot(b) == max(slot(ids[2]), slot(ids[3]))
+        c = be.alloc(65540)  # 65552 fits before 1 MiB
+        assert slot(c) == slot(ids[4])
+        d = be.alloc(100)  # the 4 KiB buffer
+        assert slot(d) == slot(ids[0])
+        s2 = be.stats()
+        assert s2.resident_reuse_hits - s1.resident_reuse_hits == 4
+        assert s2.allocation_calls == s1.allocation_calls
+        with pytest.raises(accel.AccelError):
+            be.free(ids[0])  # stale generation
+        x = be.upload_new(np.arange(8192, dtype=np.uint64))  # the 1 MiB buffer (64 KiB requested)
+        assert np.array_equal(be.download(x, 8 * 8192), np.arange(8192, dtype=np.uint64))
+        for i in (a, b, c, d, x):
+            be.free(i)
+        be.call("trim_resident_cache")
+        s3 = be.stats()
+        assert s3.physical_free_calls - s2.physical_free_calls == len(sizes)
+        y = be.alloc(4096)  # nothing free with memory: a fresh allocation in a trimmed slot
+        assert be.stats().allocation_calls == s3.allocation_calls + 1
+        assert slot(y) in {slot(i) for i in ids}
+        be.free(y)
+    finally:
+        be.close()

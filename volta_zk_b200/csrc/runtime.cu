@@ -609,20 +609,28 @@ static int pinned_ready(Context* c, PinnedSlot* p, bool* ready) {
 }
 
 static int trim_resident(Context* c) {
-    bool any = false;
-    for (size_t s : c->free_slots)
-        if (!c->slots[s].active && c->slots[s].ptr) any = true;
-    if (!any) return 0;
+    if (c->free_fit.empty() && c->free_retired.empty()) return 0;
     if (sync_for_reclaim(c)) return -1;
-    for (size_t s : c->free_slots) {
+    auto release = [&](size_t s) -> int {
         Slot& b = c->slots[s];
-        if (b.active || !b.ptr) continue;
         VZB_CUDA(c, cudaFree(b.ptr));
         ++c->stats.physical_free_calls;
         c->stats.live_device_bytes -= b.capacity;
         b.ptr = nullptr;
         b.capacity = 0;
         b.logical = 0;
+        return 0;
+    };
+    while (!c->free_fit.empty()) {
+        const size_t s = c->free_fit.begin()->second;
+        c->free_fit.erase(c->free_fit.begin());
+        if (release(s)) return -1;
+        c->free_empty.push_back(s);
+    }
+    while (!c->free_retired.empty()) {  // retired slots are never handed out again
+        const size_t s = c->free_retired.back();
+        c->free_retired.pop_back();
+        if (release(s)) return -1;
     }
     return 0;
 }
@@ -1153,20 +1161,11 @@ extern "C" int volta_cuda_resident_alloc(void* raw, size_t bytes, uint64_t* out_
     if (bind_device(c)) return fail_message(c, "cannot select the context's device");
     try {
         ++c->stats.resident_alloc_requests;
-        size_t best_pos = SIZE_MAX, best_slot = SIZE_MAX, best_cap = SIZE_MAX;
-        for (size_t pos = 0; pos < c->free_slots.size(); ++pos) {
-            const size_t s = c->free_slots[pos];
-            const Slot& b = c->slots[s];
-            if (b.active || !b.ptr || b.generation == kGenerationMax || b.capacity < bytes) continue;
-            if (b.capacity < best_cap || (b.capacity == best_cap && s < best_slot)) {
-                best_pos = pos;
-                best_cap = b.capacity;
-                best_slot = s;
-            }
-        }
-        if (best_pos != SIZE_MAX) {
-            c->free_slots[best_pos] = c->free_slots.back();
-            c->free_slots.pop_back();
+        // best fit: the smallest free capacity >= bytes, the lowest slot among equals
+        const auto fit = c->free_fit.lower_bound({bytes, 0});
+        if (fit != c->free_fit.end()) {
+            const size_t best_slot = fit->second;
+            c->free_fit.erase(fit);
             Slot& b = c->slots[best_slot];
             ++b.generation;
             b.logical = bytes;
@@ -1187,15 +1186,9 @@ extern "C" int volta_cuda_resident_alloc(void* raw, size_t bytes, uint64_t* out_
         c->stats.live_device_bytes += bytes;
         c->stats.peak_device_bytes = std::max(c->stats.peak_device_bytes, c->stats.live_device_bytes);
         size_t slot = SIZE_MAX;
-        for (size_t pos = 0; pos < c->free_slots.size(); ++pos) {
-            const size_t s = c->free_slots[pos];
-            const Slot& b = c->slots[s];
-            if (!b.active && !b.ptr && b.generation != kGenerationMax) {
-                slot = s;
-                c->free_slots[pos] = c->free_slots.back();
-                c->free_slots.pop_back();
-                break;
-            }
+        if (!c->free_empty.empty()) {  // a trimmed slot's id
+            slot = c->free_empty.back();
+            c->free_empty.pop_back();
         }
         if (slot == SIZE_MAX) {
             if (c->slots.size() >= kSlotMask) {
@@ -1227,7 +1220,11 @@ extern "C" int volta_cuda_resident_free(void* raw, uint64_t id) {
     Slot* b = find_slot(c, id);
     if (!b) return fail_message(c, "unknown or stale resident buffer id");
     try {
-        c->free_slots.push_back(static_cast<size_t>((id & kSlotMask) - 1));
+        const size_t s = static_cast<size_t>((id & kSlotMask) - 1);
+        if (b->generation == kGenerationMax)
+            c->free_retired.push_back(s);
+        else
+            c->free_fit.insert({b->capacity, s});
     } catch (...) {
         return fail_message(c, "resident free threw a C++ exception");
     }

@@ -16,6 +16,7 @@
 #include <cstdint>
 #include <cstring>
 #include <limits>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -135,7 +136,11 @@ struct Context {
     void* host_mailbox_dev = nullptr;
 
     std::vector<Slot> slots;
-    std::vector<size_t> free_slots;
+    // Free slots: with memory, ordered by (capacity, slot) for the best fit
+    // in O(log n); without memory (trimmed); retired (generation exhausted)
+    // but still holding memory until the next trim.
+    std::set<std::pair<size_t, size_t>> free_fit;
+    std::vector<size_t> free_empty, free_retired;
     std::vector<PinnedSlot> pinned;
     std::vector<size_t> free_pinned;
 

@@ -151,6 +151,22 @@ def prefill_tokens(t: int) -> np.ndarray:
     return (fpstream_fp_rows(TOKEN_SEED, 0, t) % _U64(VOCAB)).astype(np.uint32)
 
 
+# Proof sites of one layer in word order (host/gpt2.hpp Gpt2Site): the 14
+# lookup instances, then the GEMM, attention and LayerNorm sumchecks; site 0
+# (the VOLE-MAC boundary corrections) has no words.  A unit's mask has bit k
+# for site k.
+SITE_ORDER = list(range(1, 15)) + list(range(16, 25))
+SITE_CORRECTIONS = 0
+ALL_SITES = 0x1FF7FFF
+# The two parts a layer's proof splits into when a GPU split needs finer
+# units: the attention-rectangle sites (the three 16 x T_pad^2 lookups, the
+# reciprocal lookup and the A.V, softmax-norm and Q.K^T sumchecks) and the
+# rest.  Their device times at T = 1024 on a B200 (ms, in a sequence of
+# 12): a whole layer 10.9, the parts 6.55 and 4.4, the weight commitment 6.8.
+PART_ATTENTION = sum(1 << k for k in (8, 9, 10, 11, 20, 21, 22))
+PART_REST = ALL_SITES & ~PART_ATTENTION
+LAYER_COST, PART_COSTS, COMMIT_COST = 10.9, {PART_ATTENTION: 6.55, PART_REST: 4.4}, 6.8
+
 # wire names, in the order of gpt2.hpp's Gpt2Wire
 WIRES = ["x_in", "ln1_mean", "ln1_var", "ln1_rsqrt_in", "ln1_rsqrt_out", "ln1_acc", "ln1_out", "qkv_acc", "qkv_q",
          "q", "k", "v", "scores_acc", "scores_q", "row_shift", "exp_out", "denoms", "recips", "weights", "av_acc",
@@ -440,6 +456,10 @@ class Gpt2Prover:
         L.vzh_gpt2_prove_band.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_char_p, C.c_char_p, C.c_size_t,
                                           C.c_size_t, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t),
                                           C.POINTER(C.c_size_t), C.c_char_p, C.c_size_t]
+        L.vzh_gpt2_prove_units.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_char_p, C.c_void_p, C.c_void_p,
+                                           C.c_size_t, C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t),
+                                           C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t), C.c_void_p,
+                                           C.c_void_p, C.c_char_p, C.c_size_t]
         L.vzh_gpt2_correction.restype = C.c_uint64
         L.vzh_gpt2_correction.argtypes = [C.c_void_p, C.c_size_t, C.c_int]
         self._rows = session.t  # rows of the last proof (the corrections' height)
@@ -481,6 +501,38 @@ class Gpt2Prover:
         self._rows = self.s.t
         return out[:written.value].copy(), per_layer.value, bytes(root)
 
+    def prove_units(self, seed: bytes, mac_seed: bytes, pad_seed: bytes, units, with_pcs: bool = False):
+        """Prove the units [(layer, site mask)] only, in that order (one GPU's
+        share of a proof split by sites; bit k of a mask is site k, bit 0 the
+        layer's boundary corrections, SITE_ORDER the rest).  Returns (words as
+        an (n, 2) u64 array, per unit the list of (site, word count) in word
+        order, 32-byte PCS root or zeros)."""
+        from . import accel
+
+        units = list(units)
+        layers = np.array([u[0] for u in units], dtype=np.uint64)
+        masks = np.array([u[1] for u in units], dtype=np.uint32)
+        site_cap = 32 * max(1, len(units))
+        sid, swords = np.zeros(site_cap, np.uint32), np.zeros(site_cap, np.uint64)
+        per_unit = np.zeros(max(1, len(units)), np.uint64)
+        out = self._out
+        written, n_sites = C.c_size_t(0), C.c_size_t(0)
+        root = (C.c_uint8 * 32)()
+        err = C.create_string_buffer(1024)
+        rc = self.host.vzh_gpt2_prove_units(self.h, seed, mac_seed, pad_seed, layers.ctypes.data, masks.ctypes.data,
+                                            len(units), int(with_pcs), out.ctypes.data, self.cap, C.byref(written),
+                                            sid.ctypes.data, swords.ctypes.data, site_cap, C.byref(n_sites),
+                                            per_unit.ctypes.data, root, err, 1024)
+        if rc != 0:
+            raise accel.AccelError(err.value.decode())
+        self._rows = self.s.t
+        sites, k = [], 0
+        for u in range(len(units)):
+            n = int(per_unit[u])
+            sites.append([(int(sid[k + i]), int(swords[k + i])) for i in range(n)])
+            k += n
+        return out[:written.value].copy(), sites, bytes(root)
+
     def prove_band(self, band: "Gpt2Band", chunk: int, seed: bytes, mac_seed: bytes, first: int = 0,
                    stride: int = 1):
         """Proof of a decode band (rows t0 .. t-1 of the session's forward;
@@ -502,12 +554,75 @@ class Gpt2Prover:
         self._rows = band.q
         return out[:written.value].copy(), per_layer.value
 
+    def host_timing(self):
+        """(enqueue ms, total ms): host wall time of the last proof spent
+        enqueueing its launches, and in all (the device finishes within the
+        total: the downloads wait for it)."""
+        e, t = C.c_double(0), C.c_double(0)
+        self.host.vzh_gpt2_prover_timing.argtypes = [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_double)]
+        self.host.vzh_gpt2_prover_timing(self.h, C.byref(e), C.byref(t))
+        return e.value, t.value
+
     def correction(self, layer: int, wire: int) -> np.ndarray:
         """Boundary corrections x - mask of wire (0 x_in, 1 k, 2 v, 3
         attn_block_out, 4 ffn_block_out) of `layer` from the last proof: rows
         x d u64 (t rows, or the band's q)."""
         buf = int(self.host.vzh_gpt2_correction(self.h, layer, wire))
         return self.s.be.download(buf, self._rows * D * 8, dtype=np.uint64)
+
+def _lpt(items, world):
+    """Largest first onto the least-loaded GPU: items [(cost, key)] ->
+    (per GPU the keys, makespan)."""
+    load = [0.0] * world
+    keys = [[] for _ in range(world)]
+    for c, key in sorted(items, key=lambda x: (-x[0], x[1])):
+        g = min(range(world), key=lambda r: (load[r], r))
+        load[g] += c
+        keys[g].append(key)
+    return keys, max(load)
+
+
+def split_sites(world: int, t: int = None, layers: int = LAYERS):
+    """Deterministic split of a proof over `world` GPUs: whole layers, the
+    weight commitment and, where finer units shorten the slowest GPU, the
+    last k layers as their two parts (PART_ATTENTION, PART_REST), dealt
+    largest first onto the least-loaded GPU with the measured costs
+    (LAYER_COST, PART_COSTS, COMMIT_COST); the k with the shortest slowest
+    GPU wins, fewer splits on a tie.  Returns (per rank the units
+    [(layer, site mask)] in layer order, the rank that commits)."""
+    best = None
+    for k in range(layers + 1):
+        items = [(COMMIT_COST, (-1, 0))]
+        items += [(LAYER_COST, (l, ALL_SITES)) for l in range(layers - k)]
+        items += [(PART_COSTS[m], (l, m)) for l in range(layers - k, layers) for m in (PART_ATTENTION, PART_REST)]
+        keys, span = _lpt(items, world)
+        if best is None or span < best[0] - 1e-9:
+            best = (span, keys)
+    per_rank, commit = [], 0
+    for g, ks in enumerate(best[1]):
+        masks = {}
+        for l, m in ks:
+            if l < 0:
+                commit = g
+            else:
+                masks[l] = masks.get(l, 0) | m
+        per_rank.append(sorted(masks.items()))
+    return per_rank, commit
+
+
+def assemble_units(pieces, layers: int = LAYERS):
+    """The proof words of every layer in site order from the units' words:
+    pieces = [(units [(layer, mask)], words, per-unit [(site, count)])] from
+    every GPU.  Returns the (n, 2) u64 words in layer order."""
+    by_site = {}
+    for units, words, sites in pieces:
+        at = 0
+        for (layer, _), us in zip(units, sites):
+            for site, n in us:
+                by_site[(layer, site)] = words[at:at + n]
+                at += n
+    out = [by_site[(l, k)] for l in range(layers) for k in SITE_ORDER]
+    return np.concatenate(out) if out else np.zeros((0, 2), np.uint64)
 
 
 def main(argv=None):

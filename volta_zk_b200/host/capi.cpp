@@ -427,6 +427,42 @@ int vzh_gpt2_prove_layers(void* p, const uint8_t* seed, const uint8_t* mac_seed,
     });
 }
 
+// The units (layers[u], sites[u]) of a proof only, in that order (one GPU's
+// share of a proof split by sites; site k = bit k, 0 the boundary
+// corrections): words of every unit in order; per proved site, in order, its
+// id and word count (site_ids / site_words, site_cap entries at most,
+// *n_sites written) and per unit its site count (unit_sites, n_units).
+int vzh_gpt2_prove_units(void* p, const uint8_t* seed, const uint8_t* mac_seed, const uint8_t* pad_seed,
+                         const size_t* layers, const uint32_t* sites, size_t n_units, int with_pcs, vz_fp2* words,
+                         size_t cap, size_t* written, uint32_t* site_ids, size_t* site_words, size_t site_cap,
+                         size_t* n_sites, size_t* unit_sites, uint8_t* root, char* err, size_t len) {
+    return guarded(err, len, [&] {
+        std::vector<Gpt2Unit> units(n_units);
+        for (size_t u = 0; u < n_units; ++u) units[u] = Gpt2Unit{layers[u], sites[u]};
+        const Gpt2Proof pr = static_cast<Gpt2Prover*>(p)->prove_units(seed, mac_seed, pad_seed, units, with_pcs != 0);
+        size_t total = 0, ns = 0;
+        for (size_t u = 0; u < pr.layer_words.size(); ++u) {
+            total += pr.layer_words[u].size();
+            ns += pr.unit_sites[u].size();
+        }
+        if (total > cap) throw AccelError("GPT-2 proof buffer too small");
+        if (ns > site_cap) throw AccelError("GPT-2 proof site buffer too small");
+        size_t at = 0, k = 0;
+        for (size_t u = 0; u < pr.layer_words.size(); ++u) {
+            std::memcpy(words + at, pr.layer_words[u].data(), pr.layer_words[u].size() * sizeof(vz_fp2));
+            at += pr.layer_words[u].size();
+            unit_sites[u] = pr.unit_sites[u].size();
+            for (const auto& st : pr.unit_sites[u]) {
+                site_ids[k] = static_cast<uint32_t>(st.first);
+                site_words[k++] = st.second;
+            }
+        }
+        *written = total;
+        *n_sites = ns;
+        std::memcpy(root, pr.pcs_root, 32);
+    });
+}
+
 // A decode band's proof (chunk >= 1) over the prover's session: layers first,
 // first + stride, ... in layer order; no weight commitment.
 int vzh_gpt2_prove_band(void* p, void* band, size_t chunk, const uint8_t* seed, const uint8_t* mac_seed,
@@ -521,6 +557,13 @@ uint64_t vzh_gpt2_decoder_buffer(void* d, size_t layer, int which) {
         case 5: return g.position();
         default: return 0;
     }
+}
+
+// Host wall time of the prover's last proof: enqueueing its launches, and in all.
+void vzh_gpt2_prover_timing(void* p, double* enqueue_ms, double* total_ms) {
+    const Gpt2Prover& g = *static_cast<Gpt2Prover*>(p);
+    *enqueue_ms = g.host_enqueue_ms();
+    *total_ms = g.host_total_ms();
 }
 
 // Arena id of the boundary corrections of wire w (0..4) of layer l.

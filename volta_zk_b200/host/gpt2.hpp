@@ -198,9 +198,21 @@ enum Gpt2Site : int {
     kSiteLn1Had
 };
 uint64_t gpt2_site_domain(size_t layer, int site, size_t chunk = 0);
+// Site 0 of a unit's mask: the layer's VOLE-MAC boundary corrections.
+constexpr int kSiteCorrections = 0;
+constexpr uint32_t kGpt2AllSites = 0x1FF7FFFu;  // bits 0 .. 14 and 16 .. 24
+
+// A unit of proof work: the sites (bit k = site k) of one layer.  The sites of
+// a layer are independent sub-proofs over the same witness, so a proof can be
+// split over GPUs by units as well as by layers.
+struct Gpt2Unit {
+    size_t layer;
+    uint32_t sites;
+};
 
 struct Gpt2Proof {
-    std::vector<std::vector<Fp2>> layer_words;  // per proved layer, the sub-proofs' words in site order
+    std::vector<std::vector<Fp2>> layer_words;  // per proved unit (layer), its sites' words in site order
+    std::vector<std::vector<std::pair<int, size_t>>> unit_sites;  // per unit: (site, words) in order
     uint8_t pcs_root[32] = {0};
 };
 
@@ -239,26 +251,36 @@ class Gpt2Prover {
     // commitment (one per response, with the prefill).
     Gpt2Proof prove_band(const Gpt2Band& band, size_t chunk, const uint8_t seed[32], const uint8_t mac_seed[32],
                          size_t first, size_t stride);
+    // The given units only, in the given order (one GPU's share of a proof
+    // split by sites), with the weight commitment when with_pcs.
+    Gpt2Proof prove_units(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
+                          const std::vector<Gpt2Unit>& units, bool with_pcs);
     // Corrections x - mask of boundary wire w (0 x_in, 1 k, 2 v, 3
     // attn_block_out, 4 ffn_block_out) of layer l: rows x d u64 (the last
     // proof's rows: t, or the band's q).
     uint64_t correction(size_t layer, int w) const { return corrections_.at(layer).at(w); }
+    // Host wall time of the last proof: enqueueing every launch, and in all
+    // (the enqueue, then the downloads that wait for the device).
+    double host_enqueue_ms() const { return host_enqueue_ms_; }
+    double host_total_ms() const { return host_total_ms_; }
 
    private:
     struct Slot {
         PendingLogup* logup = nullptr;  // a LogUp instance, else `words` message slots at msgs
+        int site = 0;
         uint64_t msgs = 0;
         size_t words = 0;
         size_t at = 0;  // offset of its raw messages in the layer's buffer
     };
     std::vector<Slot> enqueue_layer(size_t l, Owned& own, const uint8_t seed[32], const uint8_t mac_seed[32],
-                                    const Gpt2Band* band, size_t chunk);
-    Gpt2Proof run(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32], size_t first,
-                  size_t stride, bool with_pcs, const Gpt2Band* band, size_t chunk);
+                                    const Gpt2Band* band, size_t chunk, uint32_t mask);
+    Gpt2Proof run(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
+                  const std::vector<Gpt2Unit>& units, bool with_pcs, const Gpt2Band* band, size_t chunk);
 
     Gpt2Session& s_;
     Backend& b_;
     std::map<uint32_t, uint64_t> range_;
+    double host_enqueue_ms_ = 0, host_total_ms_ = 0;
     uint64_t gelu_pairs_ = 0, rsqrt_pairs_ = 0, expgap_pairs_ = 0, recip_pairs_ = 0, shifts_ = 0;
     uint64_t exp_pad_out_ = 0, recip_pad_out_ = 0;
     uint64_t wmat_ = 0, pads_ = 0, code_ = 0, tree_ = 0, err_ = 0;

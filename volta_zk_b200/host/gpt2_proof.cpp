@@ -38,6 +38,7 @@
 // enqueued with device-side message slots and nothing waits on the device
 // until the words of all layers come home at the end.
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 
 #include "gpt2.hpp"
@@ -271,7 +272,7 @@ PendingLogup lookup_enqueue(Backend& b, Owned& own, uint64_t qcols, size_t qcoun
 // pending message slots in proof order.
 std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, const uint8_t seed[32],
                                                         const uint8_t mac_seed[32], const Gpt2Band* band,
-                                                        size_t chunk) {
+                                                        size_t chunk, uint32_t mask) {
     const Api& A = b_.api();
     void* ctx = b_.ctx();
     const Gpt2Shape& sh = s_.shape();
@@ -294,12 +295,13 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         return Wire{bw.first, bw.second};
     };
     auto alloc = [&](size_t bytes) { return own.add(b_.alloc(bytes)); };
+    auto on = [&](int site) { return ((mask >> site) & 1u) != 0; };  // this unit proves the site
     std::vector<Slot> slots;
 
     // ---- boundary authentication --------------------------------------------
     const int boundary[5] = {kXin, kK, kV, kAttnOut, kFfnOut};
     std::vector<uint64_t> corr(5);
-    for (int w = 0; w < 5; ++w) {
+    for (int w = 0; w < 5 && on(kSiteCorrections); ++w) {
         // one mask domain per (chunk, layer, wire), row r at (tag << 32) | r
         const uint64_t tag = (static_cast<uint64_t>(chunk) << 16) | (l * 8 + w);
         const uint64_t masks = alloc(t * d * sizeof(uint64_t));
@@ -310,7 +312,7 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         b_.check(A.volta_cuda_subfield_corrections_device(ctx, x.id, x.off, masks, 0, corr[w], 0, t * d, 0),
                  "subfield_corrections_device");
     }
-    corrections_[l] = corr;
+    if (on(kSiteCorrections)) corrections_[l] = corr;
 
     // ---- the 14 lookup instances --------------------------------------------
     std::vector<PendingSide*> sides;
@@ -324,11 +326,13 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         sides.push_back(&logups.back()->side[1]);
         Slot sl;
         sl.logup = logups.back().get();
+        sl.site = site;
         slots.push_back(sl);
     };
     // a requant site: remainders of (acc, out) padded to row_pad x col_pad
     auto range_site = [&](int site, Wire acc, Wire out, size_t rows, size_t cols, size_t row_pad, size_t col_pad,
                           uint32_t shift) {
+        if (!on(site)) return;
         const size_t n = row_pad * col_pad;
         const uint64_t cc = alloc(2 * n * sizeof(uint64_t));
         b_.check(A.volta_cuda_requant_columns_device(ctx, acc.id, acc.off, out.id, out.off, cc, 0, err_, 0, rows,
@@ -342,6 +346,7 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     // a pair site: (in, out) padded, packed in + 2^16 out
     auto pair_site = [&](int site, Wire in, int in_kind, Wire out, size_t rows, size_t cols, size_t row_pad,
                          size_t col_pad, uint64_t pad_in, uint64_t pad_out, uint64_t table, bool signed_in) {
+        if (!on(site)) return;
         const size_t n = row_pad * col_pad;
         const uint64_t cc = alloc(2 * n * sizeof(uint64_t));
         b_.check(A.volta_cuda_pair_columns_device(ctx, in.id, in.off, out.id, out.off, cc, 0, rows, cols, row_pad,
@@ -372,9 +377,9 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     // softmax columns: [0] gap, [1] packed (gap, exp), [2] exp, [3] norm
     // remainders, [4] reciprocals, [5] mask; [6] reciprocal inputs, [7] packed
     // (input, reciprocal)
-    uint64_t sm[8];
-    for (int k = 0; k < 8; ++k) sm[k] = alloc((k < 6 ? rect : kHeadPad * tp) * sizeof(uint64_t));
-    {
+    uint64_t sm[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (on(kSiteNormRange) || on(kSiteExp) || on(kSiteRecip) || on(kSiteNormHad)) {
+        for (int k = 0; k < 8; ++k) sm[k] = alloc((k < 6 ? rect : kHeadPad * tp) * sizeof(uint64_t));
         const Wire sq = W(kScoresQ), rs = W(kRowShift), ex = W(kExpOut), dn = W(kDenoms), rc = W(kRecips),
                    wt = W(kWeights);
         if (!b_.ext().softmax_lookup_columns_band) throw AccelError("backend lacks the band softmax columns");
@@ -384,19 +389,19 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
                                                       kRecipPadInput, recip_pad_out_),
                  "volta_b200_softmax_lookup_columns_band_device");
     }
-    {   // softmax norm remainders on Range(14)
+    if (on(kSiteNormRange)) {  // softmax norm remainders on Range(14)
         const uint64_t mult = alloc((size_t{1} << f.softmax_norm) * sizeof(uint32_t));
         b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[3], 0, mult, 0, rect, size_t{1} << f.softmax_norm),
                  "histogram_fp_device");
         add_logup(kSiteNormRange, sm[3], 1, 0, rect, range_.at(f.softmax_norm), size_t{1} << f.softmax_norm, mult);
     }
-    {   // (gap, exp) pairs on the ExpGap table
+    if (on(kSiteExp)) {  // (gap, exp) pairs on the ExpGap table
         const uint64_t mult = alloc((size_t{1} << 16) * sizeof(uint32_t));
         b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[0], 0, mult, 0, rect, size_t{1} << 16),
                  "histogram_fp_device");
         add_logup(kSiteExp, sm[1], 1, 0, rect, expgap_pairs_, size_t{1} << 16, mult);
     }
-    {   // (denom >> den_shift, rc) pairs on the 18-bit reciprocal table
+    if (on(kSiteRecip)) {  // (denom >> den_shift, rc) pairs on the 18-bit reciprocal table
         const size_t n = kHeadPad * tp;
         const uint64_t mult = alloc((size_t{1} << kRecipBits) * sizeof(uint32_t));
         b_.check(A.volta_cuda_histogram_fp_device(ctx, sm[6], 0, mult, 0, n, size_t{1} << kRecipBits),
@@ -408,14 +413,15 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     range_site(kSiteLn1Norm, W(kLn1Acc), W(kLn1Out), t, d, tp, d_pad, f.ln_norm);
     pair_site(kSiteLn1Rsqrt, W(kLn1Rin), 1, W(kLn1Rout), 1, t, 1, tp, 0, fp_from_i64(rsqrt[0]), rsqrt_pairs_, false);
     // every instance's batched rounds share launches
-    launch_side_work(b_, sides);
+    if (!sides.empty()) launch_side_work(b_, sides);
     pending_logups_.push_back(std::move(logups));
 
     // ---- sumchecks ------------------------------------------------------------
-    auto slot_buffer = [&](size_t words) {
+    auto slot_buffer = [&](int site, size_t words) {
         Slot sl;
         sl.msgs = alloc(words * sizeof(Fp2));
         sl.words = words;
+        sl.site = site;
         slots.push_back(sl);
         return sl.msgs;
     };
@@ -428,12 +434,13 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     };
     // weight GEMM: claim acc~(r_i, r_j), folds, product sumcheck over k
     auto gemm = [&](int site, Wire x, uint64_t w, Wire acc, size_t m, size_t k, size_t n) {
+        if (!on(site)) return;
         FpStream tx(seed, gpt2_site_domain(l, site, chunk));
         const size_t m_pad = pow2_at_least(m), n_pad = pow2_at_least(n), k_pad = pow2_at_least(k);
         const std::vector<Fp2> rj = draw(tx, log2_exact(n_pad)), ri = draw(tx, log2_exact(m_pad));
         const uint64_t eq_j = eq_table(rj), eq_i = eq_table(ri);
         const size_t kb = log2_exact(k_pad);
-        const uint64_t msgs = slot_buffer(1 + 2 * kb + 2);
+        const uint64_t msgs = slot_buffer(site, 1 + 2 * kb + 2);
         const uint64_t acc_r = alloc(n_pad * sizeof(Fp2));
         b_.check(A.volta_cuda_matrix_fold_device(ctx, acc.id, acc.off, eq_i, 0, acc_r, 0, m, n, 0, n, n_pad, 1, 0),
                  "matrix_fold_device");
@@ -448,6 +455,7 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     };
     // LayerNorm product (x - mu) * (r g) over t_pad x d_pad
     auto ln_product = [&](int site, int x, int mean, int rout, int gain) {
+        if (!on(site)) return;
         FpStream tx(seed, gpt2_site_domain(l, site, chunk));
         const uint64_t mu = alloc(tp * sizeof(uint64_t)), rs = alloc(tp * sizeof(uint64_t));
         const Wire wm = W(mean), wr = W(rout), wx = W(x);
@@ -458,12 +466,13 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         b_.check(A.volta_cuda_ln_hadamard_factors_device(ctx, wx.id, wx.off, mu, 0, rs, 0, s_.weight(l, gain), 0, cen,
                                                          0, sc, 0, t, d, tp, d_pad),
                  "ln_hadamard_factors_device");
-        const uint64_t msgs = slot_buffer(2 * log2_exact(n) + 2);
+        const uint64_t msgs = slot_buffer(site, 2 * log2_exact(n) + 2);
         product_rounds(b_, own, cen, sc, n, tx, msgs, 0);
     };
-    auto triple = [&](uint64_t a, uint64_t bb, uint64_t c, size_t n, FpStream& tx, bool base) {
+    auto triple = [&](int site, uint64_t a, uint64_t bb, uint64_t c, size_t n, FpStream& tx, bool base) {
         size_t k = 0;
         Slot sl;
+        sl.site = site;
         sl.msgs = triple_enqueue(b_, own, a, bb, c, n, tx, base, k);
         sl.words = 3 * k + 3;
         slots.push_back(sl);
@@ -472,7 +481,7 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
     gemm(kSiteGemmUp, W(kLn2Out), s_.weight(l, 2), W(kUpAcc), t, d, dff);
     ln_product(kSiteLn2Had, kAttnOut, kLn2Mean, kLn2Rout, 6);
     gemm(kSiteGemmProj, W(kAvQ), s_.weight(l, 1), W(kProjAcc), t, d, d);
-    {   // A.V over (head, key position)
+    if (on(kSiteAv)) {  // A.V over (head, key position)
         FpStream tx(seed, gpt2_site_domain(l, kSiteAv, chunk));
         const std::vector<Fp2> rc = draw(tx, log2_exact(sh.head_dim)), rh = draw(tx, 4), ri = draw(tx, log2_exact(tp));
         const uint64_t eq_c = eq_table(rc), eq_h = eq_table(rh), eq_i = eq_table(ri);
@@ -484,13 +493,13 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         b_.check(b_.ext().av_factors_band(ctx, wt.id, wt.off, s_.wire(l, kV), 0, eq_i, 0, eq_c, 0, eq_h, 0, parts, t,
                                           t0, h, sh.head_dim, kHeadPad, tp, sp),
                  "volta_b200_av_factors_band_device");
-        triple(parts[0], parts[1], parts[2], n, tx, false);
+        triple(kSiteAv, parts[0], parts[1], parts[2], n, tx, false);
     }
-    {   // softmax norm product over the attention rectangle (Fp columns: exp, reciprocal, mask)
+    if (on(kSiteNormHad)) {  // softmax norm product over the attention rectangle (Fp columns: exp, reciprocal, mask)
         FpStream tx(seed, gpt2_site_domain(l, kSiteNormHad, chunk));
-        triple(sm[2], sm[4], sm[5], rect, tx, true);
+        triple(kSiteNormHad, sm[2], sm[4], sm[5], rect, tx, true);
     }
-    {   // Q.K^T over (head, dimension)
+    if (on(kSiteQk)) {  // Q.K^T over (head, dimension)
         FpStream tx(seed, gpt2_site_domain(l, kSiteQk, chunk));
         const std::vector<Fp2> rj = draw(tx, log2_exact(sp)), ri = draw(tx, log2_exact(tp)), rh = draw(tx, 4);
         const uint64_t eq_i = eq_table(ri), eq_j = eq_table(rj);
@@ -506,7 +515,7 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         // K over every cached row 0 .. keys - 1
         b_.check(A.volta_cuda_matrix_fold_device(ctx, s_.wire(l, kK), 0, eq_j, 0, kr, 0, keys, d, 0, d, d_pad, 0, 0),
                  "matrix_fold_device");
-        triple(qr, kr, cid, d_pad, tx, false);
+        triple(kSiteQk, qr, kr, cid, d_pad, tx, false);
     }
     gemm(kSiteGemmQkv, W(kLn1Out), s_.weight(l, 0), W(kQkvAcc), t, d, 3 * d);
     ln_product(kSiteLn1Had, kXin, kLn1Mean, kLn1Rout, 4);
@@ -514,27 +523,44 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
 }
 
 Gpt2Proof Gpt2Prover::prove(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32]) {
-    return run(seed, mac_seed, pad_seed, 0, 1, true, nullptr, 0);
+    return prove_layers(seed, mac_seed, pad_seed, 0, 1, true);
 }
+
+namespace {
+std::vector<Gpt2Unit> layer_units(size_t layers, size_t first, size_t stride) {
+    if (!stride) throw AccelError("GPT-2 proof layer stride must be positive");
+    std::vector<Gpt2Unit> u;
+    for (size_t l = first; l < layers; l += stride) u.push_back(Gpt2Unit{l, kGpt2AllSites});
+    return u;
+}
+}  // namespace
 
 Gpt2Proof Gpt2Prover::prove_layers(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
                                    size_t first, size_t stride, bool with_pcs) {
-    return run(seed, mac_seed, pad_seed, first, stride, with_pcs, nullptr, 0);
+    return run(seed, mac_seed, pad_seed, layer_units(s_.shape().layers, first, stride), with_pcs, nullptr, 0);
+}
+
+Gpt2Proof Gpt2Prover::prove_units(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
+                                  const std::vector<Gpt2Unit>& units, bool with_pcs) {
+    return run(seed, mac_seed, pad_seed, units, with_pcs, nullptr, 0);
 }
 
 Gpt2Proof Gpt2Prover::prove_band(const Gpt2Band& band, size_t chunk, const uint8_t seed[32],
                                  const uint8_t mac_seed[32], size_t first, size_t stride) {
     if (&band.session() != &s_) throw AccelError("the band is not of this prover's session");
     if (!chunk || chunk >= (size_t{1} << 14)) throw AccelError("band chunk index must be in 1 .. 2^14 - 1");
-    return run(seed, mac_seed, nullptr, first, stride, false, &band, chunk);
+    return run(seed, mac_seed, nullptr, layer_units(s_.shape().layers, first, stride), false, &band, chunk);
 }
 
 Gpt2Proof Gpt2Prover::run(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
-                          size_t first, size_t stride, bool with_pcs, const Gpt2Band* band, size_t chunk) {
+                          const std::vector<Gpt2Unit>& units, bool with_pcs, const Gpt2Band* band, size_t chunk) {
     const Api& A = b_.api();
     void* ctx = b_.ctx();
     const Gpt2Shape& sh = s_.shape();
-    if (!stride) throw AccelError("GPT-2 proof layer stride must be positive");
+    for (const Gpt2Unit& u : units)
+        if (u.layer >= sh.layers || !u.sites || (u.sites & ~kGpt2AllSites))
+            throw AccelError("invalid GPT-2 proof unit (layer out of range or unknown sites)");
+    const auto t_start = std::chrono::steady_clock::now();
     for (const auto& l : corrections_)
         for (uint64_t id : l.second) A.volta_cuda_resident_free(ctx, id);
     corrections_.clear();
@@ -551,16 +577,16 @@ Gpt2Proof Gpt2Prover::run(const uint8_t seed[32], const uint8_t mac_seed[32], co
         std::vector<Slot> slots;
     };
     std::vector<LayerRaw> raw;
-    for (size_t l = first; l < sh.layers; l += stride) {
+    for (const Gpt2Unit& u : units) {
         Owned lay(b_);
         raw.emplace_back();
         LayerRaw& lr = raw.back();
-        lr.slots = enqueue_layer(l, lay, seed, mac_seed, band, chunk);
+        lr.slots = enqueue_layer(u.layer, lay, seed, mac_seed, band, chunk, u.sites);
         for (Slot& sl : lr.slots) {
             sl.at = lr.total;
             lr.total += sl.logup ? sl.logup->side[0].msg_total + sl.logup->side[1].msg_total : sl.words;
         }
-        lr.buf = keep.add(b_.alloc(lr.total * sizeof(Fp2)));
+        lr.buf = keep.add(b_.alloc(std::max<size_t>(lr.total, 1) * sizeof(Fp2)));  // (a corrections-only unit has no words)
         std::vector<vzb_copy_seg> segs;  // every slot's messages into the layer buffer, one batched copy
         auto copy = [&](uint64_t src, size_t words, size_t at) {
             segs.push_back(vzb_copy_seg{src, 0, lr.buf, at * sizeof(Fp2), words * sizeof(Fp2)});
@@ -573,7 +599,7 @@ Gpt2Proof Gpt2Prover::run(const uint8_t seed[32], const uint8_t mac_seed[32], co
                 copy(sl.msgs, sl.words, sl.at);
             }
         }
-        if (b_.ext().copy_segments) {
+        if (b_.ext().copy_segments && !segs.empty()) {
             b_.check(b_.ext().copy_segments(ctx, segs.data(), segs.size()), "copy_segments_device");
         } else {
             for (const vzb_copy_seg& g : segs)
@@ -594,26 +620,34 @@ Gpt2Proof Gpt2Prover::run(const uint8_t seed[32], const uint8_t mac_seed[32], co
         b_.check(A.volta_cuda_hash_fp_tree_device(ctx, code_, 0, kPcsRows, code_len, tree_, 0),
                  "hash_fp_tree_device");
     }
+    const auto t_enqueued = std::chrono::steady_clock::now();
     // the words: one download per layer, LogUp accumulators turned into
     // round messages exactly as the resident LogUp driver does
     Gpt2Proof out;
     for (const LayerRaw& lr : raw) {
         std::vector<Fp2> host(lr.total);
-        b_.download(lr.buf, 0, host.data(), lr.total * sizeof(Fp2));
+        if (lr.total) b_.download(lr.buf, 0, host.data(), lr.total * sizeof(Fp2));
         std::vector<Fp2> words;
+        std::vector<std::pair<int, size_t>> sites;
         for (const Slot& sl : lr.slots) {
+            const size_t before = words.size();
             if (sl.logup)
                 logup_proof_words(*sl.logup, host.data() + sl.at, host.data() + sl.at + sl.logup->side[0].msg_total,
                                   words);
             else
                 words.insert(words.end(), host.begin() + sl.at, host.begin() + sl.at + sl.words);
+            sites.emplace_back(sl.site, words.size() - before);
         }
         out.layer_words.push_back(std::move(words));
+        out.unit_sites.push_back(std::move(sites));
     }
     pending_logups_.clear();
     if (with_pcs) b_.download(tree_, (2 * code_len - 2) * 32, out.pcs_root, 32);
     uint32_t e = 0;
     b_.download(err_, 0, &e, sizeof(e));
+    const auto t_done = std::chrono::steady_clock::now();
+    host_enqueue_ms_ = std::chrono::duration<double, std::milli>(t_enqueued - t_start).count();
+    host_total_ms_ = std::chrono::duration<double, std::milli>(t_done - t_start).count();
     if (e) throw AccelError("GPT-2 proof witness columns out of their lookup domains");
     return out;
 }
