@@ -76,6 +76,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="config 3 line without the config-4 witness leg")
+    ap.add_argument("--no-scaled", action="store_true", help="config 3 line without the config-4 scaled-shape leg")
     return ap.parse_args()
 
 
@@ -760,6 +761,26 @@ def config3_cpu(t: int, layer: int = 0):
     return {"forward_s": t1 - t0, "layer_s": t2 - t1, "pcs_s": t3 - t2, "threads": threads, "root": root}, words
 
 
+def split_commitment(be, gp, rank, world, dev, pcs_rank):
+    """The weight commitment's share of a proof step on this rank: with
+    pcs_rank None every rank encodes its row block and the root comes from
+    the all-to-all of column chaining values (sharded.gpt2_commit_sharded);
+    otherwise the committing rank's prove_units call commits (returns None)."""
+    if pcs_rank is not None:
+        return lambda: None
+    from volta_zk_b200 import sharded
+
+    gather, a2a = sharded.torch_all_gather(dev), sharded.torch_all_to_all(dev)
+    return lambda: sharded.gpt2_commit_sharded(be, gp, PAD_SEED, rank, world, gather, a2a)
+
+
+def commit_note(pcs_rank, world) -> str:
+    if pcs_rank is None:
+        return (f"the weight commitment split by rows over the {world} GPUs (NCCL all-to-all of the column "
+                f"chaining values, all-gather of the slab roots)")
+    return f"the weight commitment on rank {pcs_rank}"
+
+
 def config3(args, rank, world, local_rank, dist, prover, peaks):
     """BASELINE config 3 (the metric): GPT-2 small prefill of T = 1024
     tokens through the drop-in ABI.  One step = the witness forward (embed,
@@ -768,14 +789,16 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
     LayerNorm/softmax product sumchecks, VOLE-MAC boundary corrections) +
     the Ligero commitment of the weights.  With N GPUs every rank runs the
     forward (replicas) and proves its share: the (layer, site) sub-proofs
-    are independent over the same witness, so gpt2.split_sites deals whole
-    layers (or layer parts) and the commitment out by measured costs,
-    largest first onto the least-loaded GPU; the words meet in two NCCL
-    all-gathers (word counts per site, then the words) and are assembled in
-    layer and site order, identical to the one-GPU proof."""
+    are independent over the same witness, so gpt2.split_plan deals whole
+    layers (or layer parts) out by measured costs, largest first onto the
+    least-loaded GPU, and gives the commitment to one GPU or splits it by
+    rows (an all-to-all of column chaining values) where the cost model
+    says that is faster; the words meet in two NCCL all-gathers (word
+    counts per site, then the words) and are assembled in layer and site
+    order, identical to the one-GPU proof."""
     import torch
 
-    from volta_zk_b200 import gpt2
+    from volta_zk_b200 import gpt2, sharded
 
     t = args.tokens
     be = prover.backend
@@ -784,40 +807,17 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
     sess = gpt2.Gpt2Session(prover, model, t)
     sess.forward(tokens)  # uploads the tokens: resident from here on
     gp = gpt2.Gpt2Prover(sess)
-    split, pcs_rank = gpt2.split_sites(world)
+    split, pcs_rank = gpt2.split_plan(world)
     units = split[rank]
     mine = [l for l, m in units if m & (1 << gpt2.SITE_CORRECTIONS)]  # layers whose corrections this rank makes
     dev = torch.device("cuda", local_rank)
-
-    def gather(words, sites):
-        """Every rank's words -> the proof in layer and site order (on every rank)."""
-        if world == 1:
-            return words
-        counts = np.zeros((gpt2.LAYERS, 25), np.int64)  # words of (layer, site), 0 where another rank proves it
-        for (layer, _), us in zip(units, sites):
-            for site, n in us:
-                counts[layer, site] = n
-        c = torch.from_numpy(counts).to(dev)
-        call = torch.empty((world,) + tuple(c.shape), dtype=c.dtype, device=dev)
-        dist.all_gather_into_tensor(call, c)
-        counts_all = call.cpu().numpy()
-        totals = counts_all.reshape(world, -1).sum(axis=1)
-        buf = np.zeros((int(totals.max()), 2), dtype=np.uint64)
-        buf[:words.shape[0]] = words
-        src = torch.from_numpy(buf.view(np.int64)).to(dev)
-        out = torch.empty((world,) + tuple(src.shape), dtype=src.dtype, device=dev)
-        dist.all_gather_into_tensor(out, src)
-        allw = out.cpu().numpy().view(np.uint64)
-        pieces = []
-        for g in range(world):
-            sites_g = [[(k, int(counts_all[g, l, k])) for k in gpt2.SITE_ORDER if (m >> k) & 1] for l, m in split[g]]
-            pieces.append((split[g], allw[g, :int(totals[g])], sites_g))
-        return gpt2.assemble_units(pieces)
+    commit = split_commitment(be, gp, rank, world, dev, pcs_rank)
 
     def step(host_tokens=None):
         sess.forward(host_tokens)
-        words, sites, root = gp.prove_units(PROOF_SEED, MAC_SEED, PAD_SEED, units, rank == pcs_rank)
-        return gather(words, sites), None, root
+        root = commit()
+        words, sites, r = gp.prove_units(PROOF_SEED, MAC_SEED, PAD_SEED, units, rank == pcs_rank)
+        return sharded.gather_units(words, sites, split, rank, world, dist, dev, gpt2.LAYERS), None, root or r
 
     def barrier():
         torch.cuda.synchronize()
@@ -847,8 +847,8 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
     step_s = max_over_ranks(ms / 1e3 / args.steps)
     logits = sess.logits()
     fwd_err = sess.error_word() | max(sess.layer_errors())
-    roots = [root] if world == 1 else None
-    if world > 1:  # the committing rank's root to every rank (the others committed nothing)
+    roots = [root]
+    if world > 1 and pcs_rank is not None:  # the committing rank's root to every rank
         r = torch.from_numpy(np.frombuffer(root, dtype=np.uint8).copy()).to(dev)
         dist.broadcast(r, pcs_rank)
         roots = [bytes(r.cpu().numpy())]
@@ -939,10 +939,10 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
                                "proofs + weight commitment)",
                    "model": "gpt2-small (12 layers, d 768, 12 heads, MLP 3072, vocab 50257), int16 fixed point, "
                             "LutParams defaults with the stable softmax",
-                   "parallelism": f"forward replicated; the {gpt2.LAYERS} layer proofs (or layer parts) and the "
-                                  f"weight commitment dealt over {world} GPUs largest first onto the least-loaded "
-                                  f"GPU (commitment on rank {pcs_rank}); NCCL all-gathers of the per-site word "
-                                  f"counts and the words" if world > 1 else "one proof on one GPU",
+                   "parallelism": f"forward replicated; the {gpt2.LAYERS} layer proofs (or layer parts) dealt "
+                                  f"over {world} GPUs largest first onto the least-loaded GPU; "
+                                  f"{commit_note(pcs_rank, world)}; NCCL all-gathers of the per-site word counts "
+                                  f"and the words" if world > 1 else "one proof on one GPU",
                    "l2": "working set (witness 1.8 GB, lookup trees, 2.1 GB codeword) far larger than L2",
                    "timing_policy": "wall-only counters"},
         "rho": round(step_s / fwd_s, 2), "forward_s": round(fwd_s, 6),
@@ -955,6 +955,89 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
                         "sha256": digest, "pcs_root": roots[0].hex(), "forward_error_word": int(fwd_err),
                         **golden},
     }
+
+
+def scaled_leg(args, rank, world, local_rank, dist, prover, steps: int = 3, warmup: int = 2):
+    """The scaled synthetic shape of config 4 (24 layers, d_model 1024, 16
+    heads of 64, MLP 4096; gpt2.GPT2_SCALED) at a 512-token prefill: the
+    witness forward, the 24 layer proofs and the weight commitment (355 M
+    weights: 2^15 rows of 2^14), with the same split over N GPUs as config 3
+    (replicated forward, layers / layer parts dealt by gpt2.split_plan with
+    this shape's measured costs, the commitment on one GPU or split by rows
+    with the all-to-all of column chaining values, two NCCL all-gathers of
+    the words).  Device-timed, max over ranks."""
+    import torch
+
+    from volta_zk_b200 import gpt2, sharded
+
+    t, layers = 512, gpt2.GPT2_SCALED.layers
+    be = prover.backend
+    dev = torch.device("cuda", local_rank)
+    model = gpt2.synthetic_model(shape=gpt2.GPT2_SCALED)
+    tokens = gpt2.prefill_tokens(t)
+    split, pcs_rank = gpt2.split_plan(world, layers, gpt2.SCALED_COSTS)
+    units = split[rank]
+
+    def max_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        v = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        return float(v.item())
+
+    with gpt2.Gpt2Session(prover, model, t) as sess, gpt2.Gpt2Prover(sess) as gp:
+        sess.forward(tokens)
+        commit = split_commitment(be, gp, rank, world, dev, pcs_rank)
+
+        def step():
+            sess.forward()
+            root = commit()
+            words, sites, r = gp.prove_units(PROOF_SEED, MAC_SEED, PAD_SEED, units, rank == pcs_rank)
+            return sharded.gather_units(words, sites, split, rank, world, dist, dev, layers), root or r
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        be.mark(0)
+        for _ in range(steps):
+            words, root = step()
+        be.mark(1)
+        step_s = max_over_ranks(be.elapsed_ms(0, 1) / 1e3 / steps)
+        reps = 5
+        be.mark(2)
+        for _ in range(reps):
+            sess.forward()
+        be.mark(3)
+        fwd_s = max_over_ranks(be.elapsed_ms(2, 3) / 1e3 / reps)
+        fwd_err = sess.error_word() | max(sess.layer_errors())
+        logits = sess.logits()
+        pcs_rows = gp.pcs_rows()
+    if world > 1 and pcs_rank is not None:
+        r = torch.from_numpy(np.frombuffer(root, dtype=np.uint8).copy()).to(dev)
+        dist.broadcast(r, pcs_rank)
+        root = bytes(r.cpu().numpy())
+    golden = {}
+    try:
+        g = np.load(os.path.join(ROOT, "tests", "golden", "gpt2_scaled_t512.npz"))
+        golden = {"logits_match_reference_mirror": hashlib.sha256(np.ascontiguousarray(logits).tobytes()).hexdigest()
+                  == str(g["logits"])}
+    except FileNotFoundError:
+        pass
+    return {"workload": f"config 4, scaled shape: {layers} layers, d_model 1024, 16 heads of 64, MLP 4096, "
+                        f"vocab 50257; {t}-token prefill proof (witness forward + {layers} layer proofs + weight "
+                        f"commitment of {pcs_rows} x 2^14 weights)",
+            "value": round(step_s, 6), "unit": "s/proof", "steps": steps, "warmup": warmup,
+            "ms_per_step": round(step_s * 1e3, 3), "rho": round(step_s / fwd_s, 2), "forward_s": round(fwd_s, 6),
+            "parallelism": f"forward replicated; layers / layer parts dealt over {world} GPUs; "
+                           f"{commit_note(pcs_rank, world)}" if world > 1 else "one proof on one GPU",
+            "proof_words": int(words.shape[0]),
+            "sha256": hashlib.sha256(np.ascontiguousarray(words).tobytes() + root).hexdigest(),
+            "pcs_root": root.hex(), "forward_error_word": int(fwd_err), **golden,
+            "note": "parity of this shape's forward, proof, corrections and commitment is pinned against the "
+                    "oracle at T = 16 and 100 over 2 layers and for an 8-layer commitment of 16384 rows "
+                    "(tests/test_gpu_gpt2_scaled.py); compare sha256 across N"}
 
 
 def decode_leg(prover, t0: int = 960, n: int = 64, reps: int = 3, curve_chunk: int = 16):
@@ -1097,8 +1180,13 @@ def run_b200(args, rank, world, local_rank):
     if world == 1 and args.workload == "config3" and not args.no_decode:
         decode = decode_leg(prover)
 
+    scaled = None
+    if args.workload == "config3" and not args.no_scaled:
+        scaled = scaled_leg(args, rank, world, local_rank, dist, prover)
+
     if rank == 0:
-        line.update({"ligero": ligero, "ligero_zk": ligero_zk, "witness_gemm": gemm, "config4": decode})
+        line.update({"ligero": ligero, "ligero_zk": ligero_zk, "witness_gemm": gemm, "config4": decode,
+                     "config4_scaled": scaled})
         print(json.dumps(line), flush=True)
     prover.close()
     if dist:

@@ -21,6 +21,10 @@ reference legs only, as the checker; the shipped library never imports it.
 
 import numpy as np
 
+# GPT-2 small.  Every function below takes its dimensions from the weights
+# it is given (d = ln1_gain's length, dff = ffn_up's size / d, heads =
+# d / 64; flat arrays work), so the same code checks other shapes such as
+# the 24-layer d-1024 one.
 D, H, DH, DFF = 768, 12, 64, 3072
 # P4 LutParams defaults (gpt2_fixed.py LutParams / luts.rs)
 LN_VAR_SHIFT, SHIFT_LN_NORM, RECIP_DEN_SHIFT, RECIP_LOG2 = 7, 16, 6, 26
@@ -33,6 +37,8 @@ def forward_layer(ops, x, w, luts, t, row_shift=0):
     gemm, qkv_split, scores, softmax, av, lookup with the oracle's
     signatures.  row_shift = 1 selects the P5 stable softmax.  Returns
     {name: array} with the reference's names."""
+    D = np.asarray(w["ln1_gain"]).size
+    DFF, H = np.asarray(w["ffn_up"]).size // D, D // DH
     r = {"x_in": x}
     ln1 = ops.layer_norm(x, w["ln1_gain"], w["ln1_bias"], luts["ln_rsqrt"], t, D, LN_VAR_SHIFT, SHIFT_LN_NORM)
     r.update(ln1_mean=ln1[0], ln1_var=ln1[1], ln1_rsqrt_in=ln1[2], ln1_rsqrt_out=ln1[3], ln1_acc=ln1[4],
@@ -77,7 +83,7 @@ def forward_model(ops, tokens, model, luts, row_shift=1):
     (shift 0), every layer, final LN of the last row, its logits against the
     tied wte.  `model` is a volta_zk_b200.gpt2.Gpt2Model."""
     t = len(tokens)
-    vocab = model.wte.shape[0]
+    vocab, D = model.wte.shape
     acc, x, e = ops.embed(tokens, model.wte, model.wpe, t, D, vocab, model.wpe.shape[0], 0, 0)
     out = {"embed_out": x, "errors": [e], "layers": []}
     for lw in model.layers:
@@ -104,9 +110,10 @@ def band_witness(ops, full, model, luts, t0):
     t0 .. t-1 with their windows t0 + i + 1), the per-head row tables cut to
     h x q, the final LayerNorm over every band row of the last layer's output
     and the logits of every band row."""
+    vocab, D = model.wte.shape
+    H = D // DH
     t = np.asarray(full["embed_out"]).size // D
     q = t - t0
-    vocab = model.wte.shape[0]
 
     def rows(a):
         a = np.asarray(a).reshape(-1)
@@ -144,7 +151,8 @@ def decode_step(ops, model, luts, cache, token, pos, row_shift=1):
     primitives: one new row at position pos; its K/V rows are appended to
     `cache` ({"k": [per layer], "v": [per layer]}, pos rows each) before the
     attention over rows 0 .. pos.  Returns (logits row, error flags)."""
-    vocab = model.wte.shape[0]
+    vocab, D = model.wte.shape
+    H, DFF = D // DH, np.asarray(model.layers[0]["ffn_up"]).size // D
     _, x, e = ops.embed(np.array([token], np.uint32), model.wte, model.wpe, 1, D, vocab, model.wpe.shape[0], pos, 0)
     errs = [e]
     for l, lw in enumerate(model.layers):
@@ -173,6 +181,7 @@ def generate(ops, model, luts, k_rows, v_rows, t0, logits_t0, n, row_shift=1):
     """generate (decode.rs:278-300): greedy steps after a prefill of t0 rows
     whose per-layer K/V (t0 x D) and last-position logits are given.  Returns
     (tokens, logits rows, cache)."""
+    D = model.wte.shape[1]
     cache = {"k": [np.asarray(k).reshape(-1)[:t0 * D].copy() for k in k_rows],
              "v": [np.asarray(v).reshape(-1)[:t0 * D].copy() for v in v_rows]}
     tokens, rows, errs = [], [], []
@@ -367,9 +376,9 @@ class Schedule:
         return np.concatenate([np.array([claim], np.uint64), self.product(a, b, tx)])
 
     def ln_product(self, x, mean, rout, gain, seed, layer, site):
-        t, tp, d = self.t, self.tp, 768
+        t, tp, d = self.t, self.tp, np.asarray(gain).size
         tx = self.o.FpStream(seed, self.dom(layer, site))
-        dp = 1024
+        dp = pow2(d)
         xx = np.zeros((tp, dp), np.int64)
         xx[:t, :d] = np.asarray(x, np.int64).reshape(t, d)
         cen = np.zeros((tp, dp), np.int64)
@@ -387,18 +396,21 @@ class Schedule:
         cached rows (the prefill uses r's own K and V)."""
         t, tp, rect, t0, s, sp = self.t, self.tp, self.rect, self.t0, self.s, self.sp
         k_all, v_all = kv if kv is not None else (r["k"], r["v"])
-        d, dff, h = 768, 3072, 12
+        d = np.asarray(lw["ln1_gain"]).size
+        dff, h = np.asarray(lw["ffn_up"]).size // d, d // DH
+        assert h <= HEAD_PAD
+        dp, fp, qp = pow2(d), pow2(dff), pow2(3 * d)
         lut = self.luts
         words = []
-        words.append(self.range_site(r["ffn_down_acc"], r["ffn_down_q"], t, d, tp, 1024, 10, seed, layer, "down_range"))
-        words.append(self.pair_site(r["ffn_up_q"], r["gelu_out"], t, dff, tp, 4096, 0, int(lut["gelu"][0]),
+        words.append(self.range_site(r["ffn_down_acc"], r["ffn_down_q"], t, d, tp, dp, 10, seed, layer, "down_range"))
+        words.append(self.pair_site(r["ffn_up_q"], r["gelu_out"], t, dff, tp, fp, 0, int(lut["gelu"][0]),
                                     lut["gelu"], True, seed, layer, "gelu"))
-        words.append(self.range_site(r["ffn_up_acc"], r["ffn_up_q"], t, dff, tp, 4096, 10, seed, layer, "up_range"))
-        words.append(self.range_site(r["ln2_acc"], r["ln2_out"], t, d, tp, 1024, 16, seed, layer, "ln2_norm"))
+        words.append(self.range_site(r["ffn_up_acc"], r["ffn_up_q"], t, dff, tp, fp, 10, seed, layer, "up_range"))
+        words.append(self.range_site(r["ln2_acc"], r["ln2_out"], t, d, tp, dp, 16, seed, layer, "ln2_norm"))
         words.append(self.pair_site(r["ln2_rsqrt_in"], r["ln2_rsqrt_out"], 1, t, 1, tp, 0, int(lut["ln_rsqrt"][0]),
                                     lut["ln_rsqrt"], False, seed, layer, "ln2_rsqrt"))
-        words.append(self.range_site(r["proj_acc"], r["attn_proj_q"], t, d, tp, 1024, 10, seed, layer, "proj_range"))
-        words.append(self.range_site(r["av_acc"], r["av_q"], t, d, tp, 1024, 12, seed, layer, "av_range"))
+        words.append(self.range_site(r["proj_acc"], r["attn_proj_q"], t, d, tp, dp, 10, seed, layer, "proj_range"))
+        words.append(self.range_site(r["av_acc"], r["av_q"], t, d, tp, dp, 12, seed, layer, "av_range"))
         # softmax columns over the padded packed rectangle (row i: window t0 + i + 1)
         caus = t * t0 + t * (t + 1) // 2
         packed = h * caus
@@ -435,9 +447,9 @@ class Schedule:
                                 np.bincount(rin, minlength=1 << RECIP_BITS).astype(np.uint32), seed, layer, "recip"))
         words.append(self.range_site(r["scores_acc"], r["scores_q"], 1, packed, 1, rect, 10, seed, layer,
                                      "scores_range"))
-        words.append(self.range_site(r["qkv_acc"], np.asarray(r["qkv_q"]), t, 3 * d, tp, 4096, 10, seed, layer,
+        words.append(self.range_site(r["qkv_acc"], np.asarray(r["qkv_q"]), t, 3 * d, tp, qp, 10, seed, layer,
                                      "qkv_range"))
-        words.append(self.range_site(r["ln1_acc"], r["ln1_out"], t, d, tp, 1024, 16, seed, layer, "ln1_norm"))
+        words.append(self.range_site(r["ln1_acc"], r["ln1_out"], t, d, tp, dp, 16, seed, layer, "ln1_norm"))
         words.append(self.pair_site(r["ln1_rsqrt_in"], r["ln1_rsqrt_out"], 1, t, 1, tp, 0, int(lut["ln_rsqrt"][0]),
                                     lut["ln_rsqrt"], False, seed, layer, "ln1_rsqrt"))
         # sumchecks
@@ -453,7 +465,7 @@ class Schedule:
         rh = [tx.next_fp2() for _ in range(4)]
         ri = [tx.next_fp2() for _ in range(tp.bit_length() - 1)]
         eq_c, eq_h, eq_i = self.eq(rcp), self.eq(rh), self.eq(ri)
-        words.append(self.triple(*self.av_factors(wt, v_all, eq_i, eq_c, eq_h), tx))
+        words.append(self.triple(*self.av_factors(wt, v_all, eq_i, eq_c, eq_h, h, d), tx))
         tx = o.FpStream(seed, self.dom(layer, "norm_had"))
         words.append(self.triple(lift(emb(exc)), lift(emb(rcc)), lift(mask), tx))
         # Q.K^T: the band's Q rows against all s cached K rows
@@ -462,20 +474,20 @@ class Schedule:
         ri = [tx.next_fp2() for _ in range(tp.bit_length() - 1)]
         rh = [tx.next_fp2() for _ in range(4)]
         eq_i, eq_j, eq_h = self.eq(ri), self.eq(rj), self.eq(rh)
-        qr = o.matrix_fold(np.ascontiguousarray(r["q"], np.int16).reshape(-1), eq_i, t, d, 0, d, 1024, 0, 0)
-        kr = o.matrix_fold(np.ascontiguousarray(k_all, np.int16).reshape(-1), eq_j, s, d, 0, d, 1024, 0, 0)
-        cc = np.ascontiguousarray(eq_h[np.arange(1024) // 64])
+        qr = o.matrix_fold(np.ascontiguousarray(r["q"], np.int16).reshape(-1), eq_i, t, d, 0, d, dp, 0, 0)
+        kr = o.matrix_fold(np.ascontiguousarray(k_all, np.int16).reshape(-1), eq_j, s, d, 0, d, dp, 0, 0)
+        cc = np.ascontiguousarray(eq_h[np.arange(dp) // DH])
         words.append(self.triple(qr, kr, cc, tx))
         words.append(self.gemm(r["ln1_out"], lw["c_attn"], r["qkv_acc"], t, d, 3 * d, seed, layer, "gemm_qkv"))
         words.append(self.ln_product(r["x_in"], r["ln1_mean"], r["ln1_rsqrt_out"], lw["ln1_gain"], seed, layer,
                                      "ln1_had"))
         return np.concatenate([np.asarray(w, np.uint64).reshape(-1, 2) for w in words])
 
-    def av_factors(self, wt, v_all, eq_i, eq_c, eq_h):
+    def av_factors(self, wt, v_all, eq_i, eq_c, eq_h, h=H, d=D):
         """The A.V contraction's factors over (head, key position j < s):
         A = sum over the rows i with t0 + i >= j of eq_i[i] w[h,i,j] (band
         packing), B = sum_c eq_c[c] v[j, h*64 + c], C = eq_h[h]."""
-        t, t0, s, sp, h, d = self.t, self.t0, self.s, self.sp, 12, 768
+        t, t0, s, sp = self.t, self.t0, self.s, self.sp
         caus = t * t0 + t * (t + 1) // 2
         wt = np.asarray(wt, np.int64)
         A = np.zeros((HEAD_PAD * sp, 2), np.uint64)
@@ -497,9 +509,10 @@ class Schedule:
         """x - mask of the boundary wires (the proof's t rows); one mask domain
         per (chunk, layer, wire), row i at (tag << 32) | i."""
         out = []
+        d = np.asarray(r["x_in"]).size // self.t
         for w, name in enumerate(("x_in", "k", "v", "attn_block_out", "ffn_block_out")):
             tag = (self.chunk << 16) | (layer * 8 + w)
-            masks = self.o.chacha_fp_rows(mac_seed, tag << 32, self.t, 768).reshape(-1)
+            masks = self.o.chacha_fp_rows(mac_seed, tag << 32, self.t, d).reshape(-1)
             out.append(fp_sub(emb(np.asarray(r[name]).reshape(-1)), masks))
         return out
 
@@ -514,10 +527,19 @@ def _dot_base(eqs, vals):
     return (s0 % P, s1 % P)
 
 
+def pcs_rows(total):
+    """Rows of the weight matrix: 8192 (GPT2_FULL, ligero.rs:59-60) while the
+    weights fit, else the power of two the weights fill (the MLE row
+    variables are ceil(log2 rows) either way, ligero.rs:47-50, 66-68)."""
+    cols = 1 << PCS_COL_BITS
+    need = -(-total // cols)
+    return max(PCS_ROWS, pow2(need))
+
+
 def pcs_root(o, model, pad_seed):
     """The weight commitment: every layer's weights, then wte, wpe, final LN,
-    row-major into 8192 rows of 2^14 int16, 512 ChaCha8 pads per row, RS code
-    2^15, BLAKE3 column tree."""
+    row-major into pcs_rows rows of 2^14 int16 (8192 for GPT-2 small), 512
+    ChaCha8 pads per row, RS code 2^15, BLAKE3 column tree."""
     cols, code_len = 1 << PCS_COL_BITS, 1 << PCS_CODE_BITS
     parts = []
     for lw in model.layers:
@@ -525,11 +547,11 @@ def pcs_root(o, model, pad_seed):
                                               "ln2_gain", "ln2_bias")]
     parts += [model.wte.reshape(-1), model.wpe.reshape(-1), model.lnf_gain, model.lnf_bias]
     flat = np.concatenate(parts).astype(np.int16)
-    w = np.zeros(PCS_ROWS * cols, np.int16)
+    rows = pcs_rows(flat.size)
+    w = np.zeros(rows * cols, np.int16)
     w[:flat.size] = flat
-    pads = o.chacha_fp_rows(pad_seed, 0, PCS_ROWS, PCS_PAD)
-    msgs = o.pcs_messages(w, np.ascontiguousarray(pads), PCS_ROWS, cols, PCS_PAD, code_len)
-    code = o.ntt_batch(msgs.reshape(PCS_ROWS, code_len)[:, :cols + PCS_PAD].copy(), PCS_ROWS, cols + PCS_PAD,
-                       code_len)
-    tree = o.merkle_tree(o.hash_fp_columns(code, PCS_ROWS, code_len))
+    pads = o.chacha_fp_rows(pad_seed, 0, rows, PCS_PAD)
+    msgs = o.pcs_messages(w, np.ascontiguousarray(pads), rows, cols, PCS_PAD, code_len)
+    code = o.ntt_batch(msgs.reshape(rows, code_len)[:, :cols + PCS_PAD].copy(), rows, cols + PCS_PAD, code_len)
+    tree = o.merkle_tree(o.hash_fp_columns(code, rows, code_len))
     return bytes(tree[-1])

@@ -5,6 +5,12 @@ stated bit-exact with rust/volta-gpt2's forward).
 
 Run once in a checkout that has the reference tree:
     python tests/golden/make_model_golden.py /path/to/reference [T ...]
+    python tests/golden/make_model_golden.py --scaled /path/to/reference [T ...]
+
+--scaled writes gpt2_scaled_t{T}.npz instead: the first 2 layers of the
+scaled synthetic shape (24 layers, d_model 1024, 16 heads of 64, MLP 4096),
+from the same mirror with its shape constants (D, H, DFF) set to that shape
+(every mirror function reads them at call time), every wire of both layers.
 
 The model is the reference's synthetic GPT-2 small
 (rust/volta-gpt2/src/model.rs:504-600 synthetic_model, seed 0x1234 as in its
@@ -42,7 +48,7 @@ sys.path.insert(0, ROOT)
 
 SEED = 0x1234
 TOKEN_SEED = bytes([0x70] * 32)
-VOCAB, POS, D, L = 50257, 1024, 768, 12
+VOCAB, POS = 50257, 1024
 LAYER_KEYS = ["row_shift", "ln1_out", "qkv_acc", "q", "k", "v", "scores_acc", "scores_q", "exp_out", "denoms", "recips", "av_acc",
               "av_q", "proj_acc", "attn_proj_q", "attn_block_out", "ln2_out", "ffn_up_acc", "ffn_up_q", "gelu_out",
               "ffn_down_acc", "ffn_down_q", "ffn_block_out"]
@@ -64,11 +70,16 @@ def lcg_values(state: int, n: int, radius: int):
     return out, state
 
 
-def main(ref_root: str, ts):
+def main(ref_root: str, ts, scaled: bool = False):
     sys.path.insert(0, os.path.join(ref_root, "scripts"))
     import gpt2_fixed as g
 
     from oracle import oracle as o
+
+    D, L = 768, 12
+    if scaled:
+        D, L = 1024, 2
+        g.D, g.H, g.DFF = D, D // g.DH, 4096
 
     t0 = time.time()
     layers = []
@@ -113,12 +124,16 @@ def main(ref_root: str, ts):
             if layer in (0, L - 1):
                 for k in LAYER_KEYS:
                     out[f"l{layer}_{k}"] = np.array(digest(lr[k]))
-        path = os.path.join(os.path.dirname(os.path.abspath(__file__)), f"gpt2_model_t{t}.npz")
+        name = f"gpt2_scaled_t{t}.npz" if scaled else f"gpt2_model_t{t}.npz"
+        path = os.path.join(os.path.dirname(os.path.abspath(__file__)), name)
         np.savez_compressed(path, **out)
         print("wrote", path, os.path.getsize(path), "bytes", flush=True)
 
 
 if __name__ == "__main__":
-    if len(sys.argv) < 2:
-        sys.exit("usage: make_model_golden.py <reference checkout> [T ...]")
-    main(sys.argv[1], [int(x) for x in sys.argv[2:]] or [16, 1024])
+    argv = sys.argv[1:]
+    scaled = bool(argv) and argv[0] == "--scaled"
+    argv = argv[1:] if scaled else argv
+    if not argv:
+        sys.exit("usage: make_model_golden.py [--scaled] <reference checkout> [T ...]")
+    main(argv[0], [int(x) for x in argv[1:]] or ([16] if scaled else [16, 1024]), scaled)

@@ -118,9 +118,38 @@ class Gpt2Model:
     lnf_gain: np.ndarray = None
     lnf_bias: np.ndarray = None
 
+    @property
+    def shape(self) -> "Gpt2Shape":
+        """The shape the weights carry (heads of 64)."""
+        vocab, d = self.wte.shape
+        return Gpt2Shape(layers=len(self.layers), d=d, heads=d // HEAD_DIM, head_dim=HEAD_DIM,
+                         dff=self.layers[0]["ffn_up"].shape[1], vocab=vocab, positions=self.wpe.shape[0])
 
-def synthetic_layer_weights(seed: int) -> dict:
-    """layer.rs synthetic_weights_for_config for GPT-2 small shapes."""
+
+@dataclass(frozen=True)
+class Gpt2Shape:
+    """A dense GPT-2 shape (ModelConfig's fields for a full-causal
+    LayerNorm/GELU model with n_kv_heads = n_q_heads, model.rs)."""
+    layers: int = LAYERS
+    d: int = D
+    heads: int = HEADS
+    head_dim: int = HEAD_DIM
+    dff: int = DFF
+    vocab: int = VOCAB
+    positions: int = POSITIONS
+
+
+GPT2_SMALL = Gpt2Shape()
+# The scaled synthetic shape of the decode/scaling configuration: 24 layers,
+# d_model 1024, 16 heads of 64, MLP 4096 (a ModelConfig with the GPT-2 small
+# vocabulary and context), proved at 512 tokens.
+GPT2_SCALED = Gpt2Shape(layers=24, d=1024, heads=16, dff=4096)
+
+
+def synthetic_layer_weights(seed: int, d: int = D, dff: int = DFF) -> dict:
+    """layer.rs synthetic_weights_for_config (283-309) for a dense shape
+    (qkv_dim = 3 d)."""
+    D, DFF = d, dff
     sizes = [D * 3 * D, D * D, D * DFF, DFF * D]
     shapes = [(D, 3 * D), (D, D), (D, DFF), (DFF, D)]
     pos, mats = 0, []
@@ -136,8 +165,15 @@ def synthetic_layer_weights(seed: int) -> dict:
                 ln2_gain=vec[1], ln1_bias=vec[2], ln2_bias=vec[3])
 
 
-def synthetic_model(seed: int = MODEL_SEED, n_layers: int = LAYERS) -> Gpt2Model:
-    layers = [synthetic_layer_weights((seed + l * 0x9E3779B9) & 0xFFFFFFFFFFFFFFFF) for l in range(n_layers)]
+def synthetic_model(seed: int = MODEL_SEED, n_layers: int | None = None, shape: Gpt2Shape = GPT2_SMALL) -> Gpt2Model:
+    """model.rs synthetic_model (504-585): per-layer synthetic weights at
+    seed + layer * 0x9E3779B9, zero GEMM biases, then wte (radius 15), wpe
+    (radius 7) from one LCG, final LN gain 64 and bias 0.  n_layers
+    overrides shape.layers (a model cut short for tests)."""
+    n_layers = shape.layers if n_layers is None else n_layers
+    D, VOCAB, POSITIONS = shape.d, shape.vocab, shape.positions
+    layers = [synthetic_layer_weights((seed + l * 0x9E3779B9) & 0xFFFFFFFFFFFFFFFF, D, shape.dff)
+              for l in range(n_layers)]
     wte, state = lcg_values(seed ^ 0xD1B54A32D192ED03, VOCAB * D, 15)
     wpe, _ = lcg_values(state, POSITIONS * D, 7)
     return Gpt2Model(layers=layers, wte=wte.reshape(VOCAB, D), wpe=wpe.reshape(POSITIONS, D),
@@ -166,6 +202,10 @@ ALL_SITES = 0x1FF7FFF
 PART_ATTENTION = sum(1 << k for k in (8, 9, 10, 11, 20, 21, 22))
 PART_REST = ALL_SITES & ~PART_ATTENTION
 LAYER_COST, PART_COSTS, COMMIT_COST = 10.9, {PART_ATTENTION: 6.55, PART_REST: 4.4}, 6.8
+# The same costs for the scaled shape (GPT2_SCALED) at T = 512, measured the
+# same way (24 in a row): a layer 6.06, its parts 2.63 and 3.49, the 2^15-row
+# weight commitment 27.55 (ms on a B200).
+SCALED_COSTS = (6.06, {PART_ATTENTION: 2.63, PART_REST: 3.49}, 27.55)
 
 # wire names, in the order of gpt2.hpp's Gpt2Wire
 WIRES = ["x_in", "ln1_mean", "ln1_var", "ln1_rsqrt_in", "ln1_rsqrt_out", "ln1_acc", "ln1_out", "qkv_acc", "qkv_q",
@@ -175,7 +215,9 @@ WIRES = ["x_in", "ln1_mean", "ln1_var", "ln1_rsqrt_in", "ln1_rsqrt_out", "ln1_ac
          "error"]
 
 
-def wire_dtype_count(name: str, t: int):
+def wire_dtype_count(name: str, t: int, shape: "Gpt2Shape" = None):
+    shape = shape or GPT2_SMALL
+    D, HEADS, DFF = shape.d, shape.heads, shape.dff
     td, n, ht = t * D, HEADS * (t * (t + 1) // 2), HEADS * t
     i16, i64 = np.int16, np.int64
     table = {"ln1_mean": (i64, t), "ln1_var": (i64, t), "ln1_rsqrt_in": (i64, t), "ln1_rsqrt_out": (i16, t),
@@ -208,7 +250,8 @@ class Gpt2Session:
         L.vzh_gpt2_buffer.argtypes = [C.c_void_p, C.c_size_t, C.c_int]
         p = self.params
         self._keep = []
-        dims = np.array([len(model.layers), D, HEADS, HEAD_DIM, DFF, VOCAB, POSITIONS, t], dtype=np.uint64)
+        self.shape = sh = model.shape
+        dims = np.array([sh.layers, sh.d, sh.heads, sh.head_dim, sh.dff, sh.vocab, sh.positions, t], dtype=np.uint64)
         shifts = np.array([p.ln_var_shift, p.shift_ln_norm, p.recip_den_shift, p.recip_log2, p.shift_qkv,
                            p.shift_scores, p.shift_softmax_norm, p.shift_av, p.shift_attn_proj, p.shift_ffn_up,
                            p.shift_ffn_down, p.shift_embed & 0xFFFFFFFF, int(p.softmax_row_shift)], dtype=np.uint32)
@@ -259,23 +302,23 @@ class Gpt2Session:
         return int(self.host.vzh_gpt2_buffer(self.h, C.c_size_t(layer if layer is not None else 2**64 - 1), which))
 
     def wire(self, layer: int, name: str) -> np.ndarray:
-        dtype, count = wire_dtype_count(name, self.t)
+        dtype, count = wire_dtype_count(name, self.t, self.shape)
         return self.be.download(self.buffer(layer, WIRES.index(name)), count * np.dtype(dtype).itemsize, dtype=dtype)
 
     def logits(self) -> np.ndarray:
-        return self.be.download(self.buffer(None, 2), VOCAB * 8, dtype=np.int64)
+        return self.be.download(self.buffer(None, 2), self.shape.vocab * 8, dtype=np.int64)
 
     def embed_out(self) -> np.ndarray:
         return self.wire(0, "x_in")
 
     def final_ln_out(self) -> np.ndarray:
-        return self.be.download(self.buffer(None, 9), D * 2, dtype=np.int16)
+        return self.be.download(self.buffer(None, 9), self.shape.d * 2, dtype=np.int16)
 
     def error_word(self) -> int:
         return int(self.be.download(self.buffer(None, 3), 4, dtype=np.uint32)[0])
 
     def layer_errors(self):
-        return [int(self.wire(l, "error")[0]) for l in range(LAYERS)]
+        return [int(self.wire(l, "error")[0]) for l in range(self.shape.layers)]
 
     def band(self, t0: int) -> "Gpt2Band":
         """The band witness of rows t0 .. t-1 of the last forward (built)."""
@@ -302,8 +345,10 @@ def _bind_decode(L):
     L.vzh_gpt2_decoder_buffer.argtypes = [vp, sz, C.c_int]
 
 
-def band_dtype_count(name: str, t0: int, q: int):
+def band_dtype_count(name: str, t0: int, q: int, shape: "Gpt2Shape" = None):
     """Element type and count of a band wire (band.rs:112-150 layouts)."""
+    shape = shape or GPT2_SMALL
+    HEADS = shape.heads
     bc = HEADS * (q * t0 + q * (q + 1) // 2)
     packed = {"scores_acc": np.int64, "scores_q": np.int16, "exp_out": np.int16, "weights": np.int16}
     tables = {"row_shift": np.int16, "denoms": np.int64, "recips": np.int16}
@@ -311,7 +356,7 @@ def band_dtype_count(name: str, t0: int, q: int):
         return packed[name], bc
     if name in tables:
         return tables[name], HEADS * q
-    return wire_dtype_count(name, q)
+    return wire_dtype_count(name, q, shape)
 
 
 class Gpt2Band:
@@ -357,21 +402,22 @@ class Gpt2Band:
         return bid.value, off.value
 
     def wire(self, layer: int, name: str) -> np.ndarray:
-        dtype, count = band_dtype_count(name, self.t0, self.q)
+        dtype, count = band_dtype_count(name, self.t0, self.q, self.s.shape)
         bid, off = self._buffer(layer, WIRES.index(name))
         size = np.dtype(dtype).itemsize
         return self.s.be.download(bid, count * size, dtype=dtype, offset_bytes=off * size)
 
     def final_ln(self, which: int) -> np.ndarray:
         """0 mean, 1 var, 2 rsqrt input, 3 rsqrt output, 4 acc, 5 out, over the q rows."""
-        q = self.q
-        dt, n = [(np.int64, q), (np.int64, q), (np.int64, q), (np.int16, q), (np.int64, q * D), (np.int16, q * D)][which]
+        q, qd = self.q, self.q * self.s.shape.d
+        dt, n = [(np.int64, q), (np.int64, q), (np.int64, q), (np.int16, q), (np.int64, qd), (np.int16, qd)][which]
         bid, _ = self._buffer(None, which)
         return self.s.be.download(bid, n * np.dtype(dt).itemsize, dtype=dt)
 
     def logits(self) -> np.ndarray:
         bid, _ = self._buffer(None, 6)
-        return self.s.be.download(bid, self.q * VOCAB * 8, dtype=np.int64).reshape(self.q, VOCAB)
+        vocab = self.s.shape.vocab
+        return self.s.be.download(bid, self.q * vocab * 8, dtype=np.int64).reshape(self.q, vocab)
 
     def error_word(self) -> int:
         bid, _ = self._buffer(None, 7)
@@ -423,11 +469,12 @@ class Gpt2Decoder:
     def logits(self) -> np.ndarray:
         """Step i's logits row (the row that sampled token i + 1)."""
         buf = int(self.L.vzh_gpt2_decoder_buffer(self.h, 0, 1))
-        return self.s.be.download(buf, 8 * self.generated * VOCAB, dtype=np.int64).reshape(self.generated, VOCAB)
+        vocab = self.s.shape.vocab
+        return self.s.be.download(buf, 8 * self.generated * vocab, dtype=np.int64).reshape(self.generated, vocab)
 
     def cache(self, layer: int, kv: int, rows: int) -> np.ndarray:
         buf = int(self.L.vzh_gpt2_decoder_buffer(self.h, layer, 3 + kv))
-        return self.s.be.download(buf, 2 * rows * D, dtype=np.int16)
+        return self.s.be.download(buf, 2 * rows * self.s.shape.d, dtype=np.int16)
 
     def error_word(self) -> int:
         buf = int(self.L.vzh_gpt2_decoder_buffer(self.h, 0, 2))
@@ -554,6 +601,30 @@ class Gpt2Prover:
         self._rows = band.q
         return out[:written.value].copy(), per_layer.value
 
+    def commit_rows(self, pad_seed: bytes, row0: int, rows: int) -> np.ndarray:
+        """One GPU's row block of the weight commitment (rows = 128 * 2^k at
+        a multiple of rows): each code column's BLAKE3 chaining value over
+        those rows, (2^15, 32) uint8.  The blocks of all GPUs, exchanged so
+        that each GPU holds a column slab (all-to-all), give the whole
+        commitment's tree (sharded.ligero_shard_tree / ligero_top_tree)."""
+        from . import accel
+
+        L = self.host
+        L.vzh_gpt2_commit_rows.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_char_p,
+                                           C.c_size_t]
+        out = np.zeros((1 << 15, 32), np.uint8)
+        err = C.create_string_buffer(1024)
+        if L.vzh_gpt2_commit_rows(self.h, pad_seed, row0, rows, out.ctypes.data, err, 1024) != 0:
+            raise accel.AccelError(err.value.decode())
+        return out
+
+    def pcs_rows(self) -> int:
+        """Rows of the weight commitment: 8192 while the weights fit, else
+        the power of two they fill."""
+        self.host.vzh_gpt2_prover_pcs_rows.restype = C.c_size_t
+        self.host.vzh_gpt2_prover_pcs_rows.argtypes = [C.c_void_p]
+        return int(self.host.vzh_gpt2_prover_pcs_rows(self.h))
+
     def host_timing(self):
         """(enqueue ms, total ms): host wall time of the last proof spent
         enqueueing its launches, and in all (the device finishes within the
@@ -568,7 +639,7 @@ class Gpt2Prover:
         attn_block_out, 4 ffn_block_out) of `layer` from the last proof: rows
         x d u64 (t rows, or the band's q)."""
         buf = int(self.host.vzh_gpt2_correction(self.h, layer, wire))
-        return self.s.be.download(buf, self._rows * D * 8, dtype=np.uint64)
+        return self.s.be.download(buf, self._rows * self.s.shape.d * 8, dtype=np.uint64)
 
 def _lpt(items, world):
     """Largest first onto the least-loaded GPU: items [(cost, key)] ->
@@ -582,19 +653,22 @@ def _lpt(items, world):
     return keys, max(load)
 
 
-def split_sites(world: int, t: int = None, layers: int = LAYERS):
+def split_sites(world: int, t: int = None, layers: int = LAYERS, costs=None):
     """Deterministic split of a proof over `world` GPUs: whole layers, the
     weight commitment and, where finer units shorten the slowest GPU, the
     last k layers as their two parts (PART_ATTENTION, PART_REST), dealt
     largest first onto the least-loaded GPU with the measured costs
-    (LAYER_COST, PART_COSTS, COMMIT_COST); the k with the shortest slowest
-    GPU wins, fewer splits on a tie.  Returns (per rank the units
-    [(layer, site mask)] in layer order, the rank that commits)."""
+    (LAYER_COST, PART_COSTS, COMMIT_COST, or costs = (layer, {part: cost},
+    commitment) for another shape; a commitment cost of 0 leaves it out);
+    the k with the shortest slowest GPU wins, fewer splits on a tie.
+    Returns (per rank the units [(layer, site mask)] in layer order, the
+    rank that commits)."""
+    layer_cost, part_costs, commit_cost = costs or (LAYER_COST, PART_COSTS, COMMIT_COST)
     best = None
     for k in range(layers + 1):
-        items = [(COMMIT_COST, (-1, 0))]
-        items += [(LAYER_COST, (l, ALL_SITES)) for l in range(layers - k)]
-        items += [(PART_COSTS[m], (l, m)) for l in range(layers - k, layers) for m in (PART_ATTENTION, PART_REST)]
+        items = [(commit_cost, (-1, 0))] if commit_cost else []
+        items += [(layer_cost, (l, ALL_SITES)) for l in range(layers - k)]
+        items += [(part_costs[m], (l, m)) for l in range(layers - k, layers) for m in (PART_ATTENTION, PART_REST)]
         keys, span = _lpt(items, world)
         if best is None or span < best[0] - 1e-9:
             best = (span, keys)
@@ -608,6 +682,33 @@ def split_sites(world: int, t: int = None, layers: int = LAYERS):
                 masks[l] = masks.get(l, 0) | m
         per_rank.append(sorted(masks.items()))
     return per_rank, commit
+
+
+def split_span(per_rank, commit, costs=None) -> float:
+    """The slowest GPU's cost of a split by the cost model (a rank holding
+    both parts of a layer pays the parts); commit None: no commitment unit."""
+    layer_cost, part_costs, commit_cost = costs or (LAYER_COST, PART_COSTS, COMMIT_COST)
+    cost = {ALL_SITES: layer_cost, **part_costs}
+    return max(sum(cost[m] for _, m in units) + (commit_cost if g == commit else 0.0)
+               for g, units in enumerate(per_rank))
+
+
+def split_plan(world: int, layers: int = LAYERS, costs=None, exchange_ms: float = 1.0):
+    """The split of a proof over `world` GPUs with the weight commitment
+    either as one GPU's unit (split_sites) or, where that is faster by the
+    cost model, split by rows over every GPU (each pays 1/world of it plus
+    exchange_ms for the chaining-value all-to-all and the root gather; world
+    a power of two).  Returns (per rank the units, the committing rank or
+    None when every rank commits its row block)."""
+    costs = costs or (LAYER_COST, PART_COSTS, COMMIT_COST)
+    whole, commit = split_sites(world, layers=layers, costs=costs)
+    if world == 1 or world & (world - 1):
+        return whole, commit
+    rows_split, _ = split_sites(world, layers=layers, costs=(costs[0], costs[1], 0))
+    sharded = split_span(rows_split, None, costs) + costs[2] / world + exchange_ms
+    if sharded < split_span(whole, commit, costs) - 1e-9:
+        return rows_split, None
+    return whole, commit
 
 
 def assemble_units(pieces, layers: int = LAYERS):
@@ -626,7 +727,7 @@ def assemble_units(pieces, layers: int = LAYERS):
 
 
 def main(argv=None):
-    """One GPT-2 small prefill proof on the first GPU: the synthetic model, the
+    """One GPT-2 prefill proof on the first GPU: the synthetic model, the
     witness forward of `--tokens` prefill tokens and the proof of every layer
     plus the weight commitment (`--proofs` times); prints the proof digest."""
     import argparse
@@ -636,10 +737,11 @@ def main(argv=None):
 
     ap = argparse.ArgumentParser(description=main.__doc__)
     ap.add_argument("--tokens", type=int, default=1024)
-    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--layers", type=int, default=None, help="default: the shape's layer count")
     ap.add_argument("--proofs", type=int, default=1)
+    ap.add_argument("--scaled", action="store_true", help="the 24-layer d-1024 shape instead of GPT-2 small")
     args = ap.parse_args(argv)
-    model = synthetic_model(n_layers=args.layers)
+    model = synthetic_model(n_layers=args.layers, shape=GPT2_SCALED if args.scaled else GPT2_SMALL)
     seeds = bytes([0x50] * 32), bytes([0x4D] * 32), bytes([0x11] * 32)
     with accel.Prover(policy=1) as prover, Gpt2Session(prover, model, args.tokens) as s, Gpt2Prover(s) as gp:
         s.forward(prefill_tokens(args.tokens))

@@ -157,6 +157,8 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         reinterpret_cast<decltype(ext_loaded_->copy_segments)>(dlsym(handle_, "volta_b200_copy_segments_device"));
     ext_loaded_->upload_batch =
         reinterpret_cast<decltype(ext_loaded_->upload_batch)>(dlsym(handle_, "volta_b200_upload_batch"));
+    ext_loaded_->hash_fp_column_cvs = reinterpret_cast<decltype(ext_loaded_->hash_fp_column_cvs)>(
+        dlsym(handle_, "volta_b200_hash_fp_column_cvs_device"));
     ext_ = ext_loaded_;
     void* ctx = nullptr;
     if (api_->volta_cuda_create(&ctx) != 0) {

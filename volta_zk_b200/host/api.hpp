@@ -44,6 +44,7 @@ struct ExtApi {
     decltype(&::volta_b200_product_tail_device) product_tail = nullptr;
     decltype(&::volta_b200_argmax_i64_device) argmax_i64 = nullptr;
     decltype(&::volta_b200_copy_segments_device) copy_segments = nullptr;
+    decltype(&::volta_b200_hash_fp_column_cvs_device) hash_fp_column_cvs = nullptr;
     decltype(&::volta_b200_upload_batch) upload_batch = nullptr;
 };
 

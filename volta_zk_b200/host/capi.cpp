@@ -566,6 +566,16 @@ void vzh_gpt2_prover_timing(void* p, double* enqueue_ms, double* total_ms) {
     *total_ms = g.host_total_ms();
 }
 
+// One GPU's row block of the weight commitment: the column chaining values
+// of rows row0 .. row0 + rows - 1 (code_len x 32 bytes into cvs).
+int vzh_gpt2_commit_rows(void* p, const uint8_t* pad_seed, size_t row0, size_t rows, uint8_t* cvs, char* err,
+                         size_t len) {
+    return guarded(err, len, [&] { static_cast<Gpt2Prover*>(p)->commit_rows(pad_seed, row0, rows, cvs); });
+}
+
+// Rows of the prover's weight commitment (8192 for GPT-2 small).
+size_t vzh_gpt2_prover_pcs_rows(void* p) { return static_cast<Gpt2Prover*>(p)->pcs_rows(); }
+
 // Arena id of the boundary corrections of wire w (0..4) of layer l.
 uint64_t vzh_gpt2_correction(void* p, size_t layer, int w) {
     try {

@@ -221,8 +221,18 @@ struct PendingLogup;
 
 class Gpt2Prover {
    public:
-    // Ligero shape of the weight commitment (GPT2_FULL, ligero.rs:59-60)
+    // Ligero shape of the weight commitment (GPT2_FULL, ligero.rs:59-60).
+    // kPcsRows is the row count while the weights fit (GPT-2 small); larger
+    // models take the power of two their weights fill (the MLE row
+    // variables are ceil(log2 rows) either way, ligero.rs:47-50, 66-68).
     static constexpr size_t kPcsRows = 8192, kPcsColBits = 14, kPcsPad = 512, kPcsCodeBits = 15;
+    static size_t pcs_rows_for(size_t weights) {
+        const size_t need = (weights + (size_t{1} << kPcsColBits) - 1) >> kPcsColBits;
+        size_t rows = kPcsRows;
+        while (rows < need) rows <<= 1;
+        return rows;
+    }
+    size_t pcs_rows() const { return pcs_rows_; }
 
     // Builds the lookup tables and the committed weight matrix once.
     explicit Gpt2Prover(Gpt2Session& s);
@@ -255,6 +265,13 @@ class Gpt2Prover {
     // split by sites), with the weight commitment when with_pcs.
     Gpt2Proof prove_units(const uint8_t seed[32], const uint8_t mac_seed[32], const uint8_t pad_seed[32],
                           const std::vector<Gpt2Unit>& units, bool with_pcs);
+    // One GPU's row block of the weight commitment, for a commitment split
+    // by rows over GPUs (ligero.rs commit_impl rows are independent until
+    // the column hash): the pads, messages and RS code of rows row0 ..
+    // row0 + rows - 1, then each code column's BLAKE3 chaining value over
+    // those rows (chunk counters from row0 / 128).  rows = 128 * 2^k and
+    // row0 a multiple of rows.  Writes code_len x 32 bytes to cvs (host).
+    void commit_rows(const uint8_t pad_seed[32], size_t row0, size_t rows, uint8_t* cvs);
     // Corrections x - mask of boundary wire w (0 x_in, 1 k, 2 v, 3
     // attn_block_out, 4 ffn_block_out) of layer l: rows x d u64 (the last
     // proof's rows: t, or the band's q).
@@ -283,7 +300,8 @@ class Gpt2Prover {
     double host_enqueue_ms_ = 0, host_total_ms_ = 0;
     uint64_t gelu_pairs_ = 0, rsqrt_pairs_ = 0, expgap_pairs_ = 0, recip_pairs_ = 0, shifts_ = 0;
     uint64_t exp_pad_out_ = 0, recip_pad_out_ = 0;
-    uint64_t wmat_ = 0, pads_ = 0, code_ = 0, tree_ = 0, err_ = 0;
+    uint64_t wmat_ = 0, pads_ = 0, code_ = 0, tree_ = 0, err_ = 0, cvs_ = 0;
+    size_t pcs_rows_ = kPcsRows;
     std::vector<uint64_t> owned_;
     std::map<size_t, std::vector<uint64_t>> corrections_;  // per proved layer
     std::vector<std::vector<std::unique_ptr<PendingLogup>>> pending_logups_;

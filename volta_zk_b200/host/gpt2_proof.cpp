@@ -96,6 +96,9 @@ uint64_t gpt2_site_domain(size_t layer, int site, size_t chunk) {
 Gpt2Prover::Gpt2Prover(Gpt2Session& s) : s_(s), b_(s.backend()) {
     const Gpt2Shape& sh = s.shape();
     if (!sh.shifts.row_shift) throw AccelError("the GPT-2 proof needs the row-shifted (stable) softmax");
+    // the attention sumchecks pad heads to 16 and draw 4 head variables
+    if (sh.heads > kHeadPad || pow2_at_least(sh.d) / sh.head_dim > kHeadPad)
+        throw AccelError("the GPT-2 proof supports at most 16 heads (padded model width / head_dim <= 16)");
     try {
         auto up = [&](const void* src, size_t bytes) {
             const uint64_t id = own(b_.alloc(bytes));
@@ -159,9 +162,9 @@ Gpt2Prover::Gpt2Prover(Gpt2Session& s) : s_(s), b_(s.backend()) {
         parts.emplace_back(s.lnf(0), d);
         parts.emplace_back(s.lnf(1), d);
         for (const auto& p : parts) total += p.second;
-        if (total > kPcsRows * cols) throw AccelError("weights exceed the PCS matrix");
-        wmat_ = own(b_.alloc(kPcsRows * cols * sizeof(int16_t)));
-        b_.check(b_.api().volta_cuda_resident_zero(b_.ctx(), wmat_, 0, kPcsRows * cols * sizeof(int16_t)),
+        pcs_rows_ = pcs_rows_for(total);
+        wmat_ = own(b_.alloc(pcs_rows_ * cols * sizeof(int16_t)));
+        b_.check(b_.api().volta_cuda_resident_zero(b_.ctx(), wmat_, 0, pcs_rows_ * cols * sizeof(int16_t)),
                  "resident_zero");
         size_t at = 0;
         for (const auto& p : parts) {
@@ -170,8 +173,8 @@ Gpt2Prover::Gpt2Prover(Gpt2Session& s) : s_(s), b_(s.backend()) {
                      "resident_copy_rows");
             at += p.second;
         }
-        pads_ = own(b_.alloc(kPcsRows * kPcsPad * sizeof(uint64_t)));
-        code_ = own(b_.alloc(kPcsRows * (size_t{1} << kPcsCodeBits) * sizeof(uint64_t)));
+        pads_ = own(b_.alloc(pcs_rows_ * kPcsPad * sizeof(uint64_t)));
+        code_ = own(b_.alloc(pcs_rows_ * (size_t{1} << kPcsCodeBits) * sizeof(uint64_t)));
         tree_ = own(b_.alloc(((size_t{2} << kPcsCodeBits) - 1) * 32));
         err_ = own(b_.alloc(sizeof(uint32_t)));
     } catch (...) {
@@ -545,6 +548,26 @@ Gpt2Proof Gpt2Prover::prove_units(const uint8_t seed[32], const uint8_t mac_seed
     return run(seed, mac_seed, pad_seed, units, with_pcs, nullptr, 0);
 }
 
+void Gpt2Prover::commit_rows(const uint8_t pad_seed[32], size_t row0, size_t rows, uint8_t* cvs) {
+    const Api& A = b_.api();
+    void* ctx = b_.ctx();
+    const size_t code_len = size_t{1} << kPcsCodeBits, cols = size_t{1} << kPcsColBits;
+    if (!rows || rows % 128 || ((rows / 128) & (rows / 128 - 1)) || row0 % rows || row0 + rows > pcs_rows_)
+        throw AccelError("commitment row block must be 128 * 2^k rows at a multiple of its size inside the matrix");
+    if (!cvs_) cvs_ = own(b_.alloc(code_len * 32));
+    // row r's pads come from ChaCha8 stream r, as in the whole commitment
+    b_.check(A.volta_cuda_chacha8_prover_secret_fp_rows_device(ctx, pads_, 0, pad_seed, row0, rows, kPcsPad),
+             "chacha8_prover_secret_fp_rows_device");
+    b_.check(A.volta_cuda_pcs_messages_device(ctx, wmat_, row0 * cols, pads_, 0, rows, cols, kPcsPad, code_len, code_,
+                                              0),
+             "pcs_messages_device");
+    b_.check(A.volta_cuda_ntt_fp_batch_device(ctx, code_, 0, rows, code_len, code_, 0), "ntt_fp_batch_device");
+    if (!b_.ext().hash_fp_column_cvs) throw AccelError("backend lacks the column chaining values");
+    b_.check(b_.ext().hash_fp_column_cvs(ctx, code_, 0, rows, code_len, row0 / 128, cvs_, 0),
+             "volta_b200_hash_fp_column_cvs_device");
+    b_.download(cvs_, 0, cvs, code_len * 32);
+}
+
 Gpt2Proof Gpt2Prover::prove_band(const Gpt2Band& band, size_t chunk, const uint8_t seed[32],
                                  const uint8_t mac_seed[32], size_t first, size_t stride) {
     if (&band.session() != &s_) throw AccelError("the band is not of this prover's session");
@@ -611,13 +634,13 @@ Gpt2Proof Gpt2Prover::run(const uint8_t seed[32], const uint8_t mac_seed[32], co
     // Ligero commitment of the weights
     const size_t code_len = size_t{1} << kPcsCodeBits, cols = size_t{1} << kPcsColBits;
     if (with_pcs) {
-        b_.check(A.volta_cuda_chacha8_prover_secret_fp_rows_device(ctx, pads_, 0, pad_seed, 0, kPcsRows, kPcsPad),
+        b_.check(A.volta_cuda_chacha8_prover_secret_fp_rows_device(ctx, pads_, 0, pad_seed, 0, pcs_rows_, kPcsPad),
                  "chacha8_prover_secret_fp_rows_device");
-        b_.check(A.volta_cuda_pcs_messages_device(ctx, wmat_, 0, pads_, 0, kPcsRows, cols, kPcsPad, code_len, code_,
+        b_.check(A.volta_cuda_pcs_messages_device(ctx, wmat_, 0, pads_, 0, pcs_rows_, cols, kPcsPad, code_len, code_,
                                                   0),
                  "pcs_messages_device");
-        b_.check(A.volta_cuda_ntt_fp_batch_device(ctx, code_, 0, kPcsRows, code_len, code_, 0), "ntt_fp_batch_device");
-        b_.check(A.volta_cuda_hash_fp_tree_device(ctx, code_, 0, kPcsRows, code_len, tree_, 0),
+        b_.check(A.volta_cuda_ntt_fp_batch_device(ctx, code_, 0, pcs_rows_, code_len, code_, 0), "ntt_fp_batch_device");
+        b_.check(A.volta_cuda_hash_fp_tree_device(ctx, code_, 0, pcs_rows_, code_len, tree_, 0),
                  "hash_fp_tree_device");
     }
     const auto t_enqueued = std::chrono::steady_clock::now();

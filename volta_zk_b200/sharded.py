@@ -365,6 +365,64 @@ def ligero_commit_open_sharded(be, rank: int, world: int, all_gather: AllGather,
     return top[-1].tobytes(), idx, columns, full_paths
 
 
+def gather_units(words, sites, split, rank, world, dist, dev, layers):
+    """Every rank's GPT-2 proof words (Gpt2Prover.prove_units over its units
+    split[rank]) -> the whole proof in layer and site order, on every rank:
+    one all-gather of the word counts per (layer, site)
+    (0 where another rank proves it), one of the words (padded to the
+    longest rank), then gpt2.assemble_units."""
+    import torch
+
+    from . import gpt2
+
+    if world == 1:
+        return words
+    counts = np.zeros((layers, 25), np.int64)
+    for (layer, _), us in zip(split[rank], sites):
+        for site, n in us:
+            counts[layer, site] = n
+    # outputs concatenated along dim 0 (the form every backend takes)
+    c = torch.from_numpy(counts).to(dev)
+    call = torch.empty((world * layers, 25), dtype=c.dtype, device=dev)
+    dist.all_gather_into_tensor(call, c)
+    counts_all = call.cpu().numpy().reshape(world, layers, 25)
+    totals = counts_all.reshape(world, -1).sum(axis=1)
+    longest = int(totals.max())
+    buf = np.zeros((longest, 2), dtype=np.uint64)
+    buf[:words.shape[0]] = words
+    src = torch.from_numpy(buf.view(np.int64)).to(dev)
+    out = torch.empty((world * longest, 2), dtype=src.dtype, device=dev)
+    dist.all_gather_into_tensor(out, src)
+    allw = out.cpu().numpy().view(np.uint64).reshape(world, longest, 2)
+    pieces = []
+    for g in range(world):
+        sites_g = [[(k, int(counts_all[g, l, k])) for k in gpt2.SITE_ORDER if (m >> k) & 1] for l, m in split[g]]
+        pieces.append((split[g], allw[g, :int(totals[g])], sites_g))
+    return gpt2.assemble_units(pieces, layers=layers)
+
+
+def gpt2_commit_sharded(be, gp, pad_seed: bytes, rank: int, world: int, all_gather: AllGather, all_to_all) -> bytes:
+    """The GPT-2 weight commitment (Gpt2Prover's Ligero matrix: pcs_rows x
+    2^14 int16 + 512 ChaCha8 pads per row, RS code 2^15, BLAKE3 column tree)
+    over `world` GPUs by rows, like ligero_commit_open_sharded: rank g
+    encodes rows g * R / G .. (g + 1) * R / G - 1 and hashes their column
+    chaining values (Gpt2Prover.commit_rows), one all-to-all hands every rank
+    its column slab's values from all row blocks, each rank builds its slab
+    subtree, and the G slab roots meet in an all-gather for the top levels.
+    Every rank returns the root, equal to the one-GPU commitment's."""
+    rows, code_len = gp.pcs_rows(), 1 << 15
+    rl, slab = rows // world, code_len // world
+    if rows % (128 * world) or (rl // 128) & (rl // 128 - 1) or code_len % world:
+        raise ValueError("sharded weight commitment needs rows / world = 128 * 2^k")
+    cvs = gp.commit_rows(pad_seed, rank * rl, rl)
+    recv = all_to_all(cvs.reshape(world, slab, H))
+    tree, root = ligero_shard_tree(be, recv, world, slab)
+    be.free(tree)
+    roots = np.stack(all_gather(np.frombuffer(root.tobytes(), dtype=np.uint64).copy()))
+    top = ligero_top_tree(be, roots.view(np.uint8).reshape(world, H))
+    return top[-1].tobytes()
+
+
 # ---------------------------------------------------------------------------
 # VOLE-MAC epilogue rows over G GPUs.  Row i of an authenticated tensor draws
 # its masks from its own correlation domain (tag << 32) | i
