@@ -77,6 +77,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="config 3 line without the config-4 witness leg")
     ap.add_argument("--no-scaled", action="store_true", help="config 3 line without the config-4 scaled-shape leg")
+    ap.add_argument("--commit", choices=["auto", "unit", "rows"], default="auto",
+                    help="weight commitment at N > 1: by the cost model, on one GPU, or split by rows")
     return ap.parse_args()
 
 
@@ -291,6 +293,21 @@ def ligero_leg(args, prover, be, peaks, rank=0, world=1, comm=None):
                             f"{world} GPUs (all-to-all of 32-byte column chaining values)",
                 "value": round(commit_s, 6), "unit": "s/commitment", "higher_is_better": False,
                 "root": out[0].hex()}
+    e2e = None if args.no_e2e else ligero_e2e(args, be, out[0])
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle as o  # checker / baseline only
+
+        o.build()
+        threads = o.set_threads(o.host_threads())
+        t0 = time.perf_counter()
+        ref = o.ligero_commit_open(LIGERO_ROW_SEED, rows, msg, code, q, TRANSCRIPT_SEED)
+        cpu_s = time.perf_counter() - t0
+        cpu = {"value": round(cpu_s, 3), "unit": "s/commitment", "cores": threads, "kind": "port",
+               "sample": f"one whole config-2 commitment with its {q} openings at full size (oracle: C/OpenMP "
+                         f"restatement of ligero.rs commit + open)",
+               "parity": bool(ref[0] == out[0] and np.array_equal(ref[1], out[1]) and np.array_equal(ref[2], out[2])
+                              and np.array_equal(ref[3], out[3]))}
     # dominant kernels alone on a resident codeword (in place, inputs >> L2)
     buf = be.alloc(8 * rows * code)
     be.call("chacha8_prover_secret_fp_rows_device", buf, 0, LIGERO_ROW_SEED, 0, rows, code)
@@ -319,7 +336,7 @@ def ligero_leg(args, prover, be, peaks, rank=0, world=1, comm=None):
         "workload": f"config 2: Ligero commit {rows} rows x 2^{args.ligero_log2_msg} msg -> 2^{args.ligero_log2_code} "
                     f"code, BLAKE3 column Merkle, {q} openings",
         "value": round(commit_s, 6), "unit": "s/commitment", "higher_is_better": False,
-        "root": out[0].hex(),
+        "root": out[0].hex(), "e2e": e2e, "cpu_baseline": cpu,
         "kernels": {
             "ntt_fp_batch": {"avg_launch_ms": round(ntt_ms, 4),
                              "hbm_gbs": round(2 * data / (ntt_ms / 1e3) / 1e9, 1),
@@ -338,6 +355,56 @@ def ligero_leg(args, prover, be, peaks, rank=0, world=1, comm=None):
                                               "source": "ncu at 1024 rows x 2^16 (ALU pipe, pct of peak)"}},
         },
     }
+
+
+def ligero_e2e(args, be, root_resident: bytes, steps: int = 3):
+    """Config 2 end to end through the seam with host buffers: the message
+    rows (rows x 2^msg Fp, the same seeded rows) from pinned host memory to
+    the device each step, zero-padded to the code length on the device, the
+    batched NTT, the BLAKE3 column tree, the openings' columns and paths
+    gathered on the device, and the root, columns and paths back to the
+    host.  Returns the e2e object (its root must equal the resident run's)."""
+    import torch
+
+    from volta_zk_b200.sharded import ligero_query_indices
+
+    rows, msg, code, q = args.ligero_rows, 1 << args.ligero_log2_msg, 1 << args.ligero_log2_code, args.ligero_queries
+    bits = code.bit_length() - 1
+    stage = be.alloc(8 * rows * msg)
+    be.call("chacha8_prover_secret_fp_rows_device", stage, 0, LIGERO_ROW_SEED, 0, rows, msg)
+    pinned = torch.empty(rows * msg, dtype=torch.int64).pin_memory()
+    host = pinned.numpy().view(np.uint64)
+    host[:] = be.download(stage, 8 * rows * msg)
+    codeword = be.alloc(8 * rows * code)
+    tree = be.alloc(32 * (2 * code - 1))
+    idx = ligero_query_indices(TRANSCRIPT_SEED, q, code)
+    ids = be.upload_new(idx)
+    cols = be.alloc(8 * q * rows)
+    paths = be.alloc(32 * q * bits)
+
+    def step():
+        be.upload(stage, host)
+        be.call("resident_zero", codeword, 0, 8 * rows * code)
+        be.call("resident_copy_rows", stage, 0, 8 * msg, codeword, 0, 8 * code, rows, 8 * msg)
+        be.call("ntt_fp_batch_device", codeword, 0, rows, code, codeword, 0)
+        be.call("hash_fp_tree_device", codeword, 0, rows, code, tree, 0)
+        be.call("pcs_gather_columns_device", codeword, 0, rows, code, ids, 0, q, cols, 0, 0)
+        be.call("merkle_paths_device", tree, 0, code, ids, 0, q, paths, 0)
+        root = be.download(tree, 32, dtype=np.uint8, offset_bytes=32 * (2 * code - 2)).tobytes()
+        return root, be.download(cols, 8 * q * rows), be.download(paths, 32 * q * bits, dtype=np.uint8)
+
+    step()
+    be.mark(12)
+    for _ in range(steps):
+        root, _, _ = step()
+    be.mark(13)
+    e2e_s = be.elapsed_ms(12, 13) / 1e3 / steps
+    for b in (stage, codeword, tree, ids, cols, paths):
+        be.free(b)
+    return {"value": round(e2e_s, 6), "unit": "s/commitment", "h2d_bytes_per_step": 8 * rows * msg,
+            "d2h_bytes_per_step": 32 + 8 * q * rows + 32 * q * bits,
+            "inputs": "message rows (Fp) from pinned host memory; out: root, opened columns and their paths",
+            "root_matches_resident": root == root_resident}
 
 
 # GPT-2 small at 1024 tokens: QKV, attention projection, MLP up and down, logits (m, k, n)
@@ -761,6 +828,19 @@ def config3_cpu(t: int, layer: int = 0):
     return {"forward_s": t1 - t0, "layer_s": t2 - t1, "pcs_s": t3 - t2, "threads": threads, "root": root}, words
 
 
+def plan_split(args, world, layers, costs):
+    """gpt2.split_plan, or with --commit unit / rows the commitment forced
+    onto one GPU / split by rows (rows needs a power-of-two world)."""
+    from volta_zk_b200 import gpt2
+
+    if args.commit == "auto" or world == 1:
+        return gpt2.split_plan(world, layers, costs)
+    if args.commit == "unit" or world & (world - 1):
+        return gpt2.split_sites(world, layers=layers, costs=costs)
+    c = costs or (gpt2.LAYER_COST, gpt2.PART_COSTS, gpt2.COMMIT_COST)
+    return gpt2.split_sites(world, layers=layers, costs=(c[0], c[1], 0))[0], None
+
+
 def split_commitment(be, gp, rank, world, dev, pcs_rank):
     """The weight commitment's share of a proof step on this rank: with
     pcs_rank None every rank encodes its row block and the root comes from
@@ -807,7 +887,7 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
     sess = gpt2.Gpt2Session(prover, model, t)
     sess.forward(tokens)  # uploads the tokens: resident from here on
     gp = gpt2.Gpt2Prover(sess)
-    split, pcs_rank = gpt2.split_plan(world)
+    split, pcs_rank = plan_split(args, world, gpt2.LAYERS, None)
     units = split[rank]
     mine = [l for l, m in units if m & (1 << gpt2.SITE_CORRECTIONS)]  # layers whose corrections this rank makes
     dev = torch.device("cuda", local_rank)
@@ -975,7 +1055,7 @@ def scaled_leg(args, rank, world, local_rank, dist, prover, steps: int = 3, warm
     dev = torch.device("cuda", local_rank)
     model = gpt2.synthetic_model(shape=gpt2.GPT2_SCALED)
     tokens = gpt2.prefill_tokens(t)
-    split, pcs_rank = gpt2.split_plan(world, layers, gpt2.SCALED_COSTS)
+    split, pcs_rank = plan_split(args, world, layers, gpt2.SCALED_COSTS)
     units = split[rank]
 
     def max_over_ranks(x: float) -> float:
