@@ -695,8 +695,8 @@ def split_span(per_rank, commit, costs=None) -> float:
 
 def split_plan(world: int, layers: int = LAYERS, costs=None, exchange_ms: float = 1.0):
     """The split of a proof over `world` GPUs with the weight commitment
-    either as one GPU's unit (split_sites) or, where that is faster by the
-    cost model, split by rows over every GPU (each pays 1/world of it plus
+    either as one GPU's unit (split_sites) or, where that is not slower by
+    the cost model, split by rows over every GPU (each pays 1/world of it plus
     exchange_ms for the chaining-value all-to-all and the root gather; world
     a power of two).  Returns (per rank the units, the committing rank or
     None when every rank commits its row block)."""
@@ -706,7 +706,7 @@ def split_plan(world: int, layers: int = LAYERS, costs=None, exchange_ms: float 
         return whole, commit
     rows_split, _ = split_sites(world, layers=layers, costs=(costs[0], costs[1], 0))
     sharded = split_span(rows_split, None, costs) + costs[2] / world + exchange_ms
-    if sharded < split_span(whole, commit, costs) - 1e-9:
+    if sharded <= split_span(whole, commit, costs) + 1e-9:  # a tie goes to the row split (measured faster)
         return rows_split, None
     return whole, commit
 
