@@ -975,7 +975,7 @@ def config3(args, rank, world, local_rank, dist, prover, peaks):
                "corrections_downloaded_per_rank": n_corr}
 
     # ---- roofline: the proof's dominant kernel (logup_round_batch_kernel,
-    # 37 % of a proof in the launch list): its largest launch shape, step 0
+    # 42 % of a proof in the launch list): its largest launch shape, step 0
     # of a 2^24-query side's 12 large layers, replicated on seeded data
     peak = peaks.get("hbm_gbs", 6650.0)
     batch_ms, batch_bytes, batch_jobs = logup_step0_replica(be, 24)
