@@ -362,6 +362,19 @@ int volta_b200_upload_async(void* ctx, uint64_t id, size_t offset_bytes, const v
 int volta_b200_wait_uploads(void* ctx);
 
 /*
+ * Asynchronous downloads (no counterpart in the reference's ABI, which
+ * downloads synchronously): download_async copies `bytes` from (id, offset)
+ * to host memory `dst` (pinned for a truly asynchronous copy) on a second
+ * copy stream, after every kernel enqueued on the context's stream so far,
+ * and returns at once, so that the copy overlaps the kernels enqueued after
+ * it.  wait_downloads blocks until every such copy has landed; `dst` must
+ * stay valid until then.  A buffer freed while a copy is pending may be
+ * reused at once: later work on the context's stream waits for the copies.
+ */
+int volta_b200_download_async(void* ctx, uint64_t id, size_t offset_bytes, void* dst, size_t bytes);
+int volta_b200_wait_downloads(void* ctx);
+
+/*
  * int16 column to canonical Fp values (v >= 0 -> v, v < 0 -> p + v), so that
  * int16 witness columns (lookup queries and tables) travel as 2 bytes per
  * entry and are embedded on the device.

@@ -152,3 +152,30 @@ def test_site_units_reassemble_the_proof(prover, split):
                     for w in range(5):
                         assert np.array_equal(gp.correction(l, w), corr[l][w])
     assert np.array_equal(gpt2.assemble_units(pieces, layers=layers), full)
+
+
+def test_correction_sink_receives_every_correction(prover):
+    """With a correction sink the proof copies every boundary correction to
+    pinned host memory while later layers compute (download_async on the
+    second copy stream); after prove returns the sink equals the resident
+    corrections, proof after proof, and the words are unchanged."""
+    import torch
+
+    from volta_zk_b200 import gpt2
+
+    t, layers = 16, 2
+    model = gpt2.synthetic_model(n_layers=layers)
+    with gpt2.Gpt2Session(prover, model, t) as s, gpt2.Gpt2Prover(s) as gp:
+        s.forward(gpt2.prefill_tokens(t))
+        plain, _, _ = gp.prove(SEED, MAC_SEED, PAD_SEED)
+        sink = torch.zeros(layers * 5 * t * gpt2.D, dtype=torch.int64).pin_memory().numpy().view(np.uint64)
+        gp.set_correction_sink(sink)
+        for mac in (MAC_SEED, bytes([0x4E] * 32)):
+            sink[:] = 0
+            words, _, _ = gp.prove(SEED, mac, PAD_SEED)
+            assert np.array_equal(words, plain)
+            got = sink.reshape(layers, 5, -1)
+            for l in range(layers):
+                for w in range(5):
+                    assert np.array_equal(got[l, w], gp.correction(l, w)), (l, w)
+        gp.set_correction_sink(None)

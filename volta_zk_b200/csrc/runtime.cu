@@ -733,6 +733,10 @@ extern "C" void volta_cuda_destroy(void* raw) {
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
     if (c->copy_ev) cudaEventDestroy(c->copy_ev);
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+    if (c->dl_stream) cudaStreamSynchronize(c->dl_stream);
+    if (c->dl_ev) cudaEventDestroy(c->dl_ev);
+    if (c->dl_done_ev) cudaEventDestroy(c->dl_done_ev);
+    if (c->dl_stream) cudaStreamDestroy(c->dl_stream);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -1219,6 +1223,10 @@ extern "C" int volta_cuda_resident_free(void* raw, uint64_t id) {
     ++c->stats.resident_free_requests;
     Slot* b = find_slot(c, id);
     if (!b) return fail_message(c, "unknown or stale resident buffer id");
+    if (c->dl_pending) {  // a later owner of this memory writes only after the pending downloads read it
+        VZB_CUDA(c, cudaEventRecord(c->dl_done_ev, c->dl_stream));
+        VZB_CUDA(c, cudaStreamWaitEvent(c->stream, c->dl_done_ev, 0));
+    }
     try {
         const size_t s = static_cast<size_t>((id & kSlotMask) - 1);
         if (b->generation == kGenerationMax)
@@ -1539,6 +1547,34 @@ extern "C" int volta_b200_upload_async(void* raw, uint64_t id, size_t offset, co
     }
     VZB_CUDA(c, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->copy_stream));
     VZB_CUDA(c, cudaEventRecord(c->copy_ev, c->copy_stream));
+    return 0;
+}
+
+extern "C" int volta_b200_download_async(void* raw, uint64_t id, size_t offset, void* dst, size_t bytes) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c || !dst || !bytes) return fail_message(c, "invalid asynchronous download");
+    if (bind_device(c)) return fail_message(c, "cannot select the context's device");
+    void* src = nullptr;
+    if (region(c, id, offset, bytes, &src)) return -1;
+    if (!c->dl_stream) {
+        VZB_CUDA(c, cudaStreamCreateWithFlags(&c->dl_stream, cudaStreamNonBlocking));
+        VZB_CUDA(c, cudaEventCreateWithFlags(&c->dl_ev, cudaEventDisableTiming));
+        VZB_CUDA(c, cudaEventCreateWithFlags(&c->dl_done_ev, cudaEventDisableTiming));
+    }
+    // the copy sees everything enqueued on the compute stream so far
+    VZB_CUDA(c, cudaEventRecord(c->dl_ev, c->stream));
+    VZB_CUDA(c, cudaStreamWaitEvent(c->dl_stream, c->dl_ev, 0));
+    VZB_CUDA(c, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c->dl_stream));
+    c->dl_pending = true;
+    return 0;
+}
+
+extern "C" int volta_b200_wait_downloads(void* raw) {
+    Context* c = static_cast<Context*>(raw);
+    if (!c) return -1;
+    if (bind_device(c)) return fail_message(c, "cannot select the context's device");
+    if (c->dl_stream) VZB_CUDA(c, cudaStreamSynchronize(c->dl_stream));
+    c->dl_pending = false;
     return 0;
 }
 

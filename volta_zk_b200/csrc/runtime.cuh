@@ -181,6 +181,12 @@ struct Context {
     // last copy, which volta_b200_wait_uploads makes the compute stream wait on
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t copy_ev = nullptr;
+    // asynchronous downloads (extension): a second copy stream; dl_ev orders
+    // each copy after the compute work enqueued before it, dl_done_ev orders
+    // later compute work (which may reuse a freed buffer) after the copies
+    cudaStream_t dl_stream = nullptr;
+    cudaEvent_t dl_ev = nullptr, dl_done_ev = nullptr;
+    bool dl_pending = false;
     std::string error;
 };
 

@@ -618,6 +618,16 @@ class Gpt2Prover:
             raise accel.AccelError(err.value.decode())
         return out
 
+    def set_correction_sink(self, host) -> None:
+        """Every later proof copies its boundary corrections into `host`
+        (a contiguous u64 array of layers x 5 x rows x d, pinned for the
+        copies to overlap the proof; wire w of layer l at [l, w]) while its
+        later layers compute; they have landed when prove returns.  None
+        stops the copies.  The array must outlive the proofs that fill it."""
+        self.host.vzh_gpt2_set_correction_sink.argtypes = [C.c_void_p, C.c_void_p]
+        self._sink = host
+        self.host.vzh_gpt2_set_correction_sink(self.h, None if host is None else host.ctypes.data)
+
     def pcs_rows(self) -> int:
         """Rows of the weight commitment: 8192 while the weights fit, else
         the power of two they fill."""

@@ -131,6 +131,10 @@ Backend::Backend(const std::string& library, TimingPolicy policy) {
         reinterpret_cast<decltype(ext_loaded_->wait_uploads)>(dlsym(handle_, "volta_b200_wait_uploads"));
     ext_loaded_->upload_async =
         reinterpret_cast<decltype(ext_loaded_->upload_async)>(dlsym(handle_, "volta_b200_upload_async"));
+    ext_loaded_->download_async =
+        reinterpret_cast<decltype(ext_loaded_->download_async)>(dlsym(handle_, "volta_b200_download_async"));
+    ext_loaded_->wait_downloads =
+        reinterpret_cast<decltype(ext_loaded_->wait_downloads)>(dlsym(handle_, "volta_b200_wait_downloads"));
     ext_loaded_->logup_tree_column = reinterpret_cast<decltype(ext_loaded_->logup_tree_column)>(
         dlsym(handle_, "volta_b200_logup_tree_column_device"));
     ext_loaded_->triple_local = reinterpret_cast<decltype(ext_loaded_->triple_local)>(

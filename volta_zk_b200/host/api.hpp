@@ -32,6 +32,8 @@ struct ExtApi {
     decltype(&::volta_b200_triple_fold_round_fp_into_device) triple_fold_round_fp = nullptr;
     decltype(&::volta_b200_wait_uploads) wait_uploads = nullptr;
     decltype(&::volta_b200_upload_async) upload_async = nullptr;
+    decltype(&::volta_b200_download_async) download_async = nullptr;
+    decltype(&::volta_b200_wait_downloads) wait_downloads = nullptr;
     decltype(&::volta_b200_logup_tree_column_device) logup_tree_column = nullptr;
     decltype(&::volta_b200_triple_local_device) triple_local = nullptr;
     decltype(&::volta_b200_triple_flush_device) triple_flush = nullptr;

@@ -573,6 +573,9 @@ int vzh_gpt2_commit_rows(void* p, const uint8_t* pad_seed, size_t row0, size_t r
     return guarded(err, len, [&] { static_cast<Gpt2Prover*>(p)->commit_rows(pad_seed, row0, rows, cvs); });
 }
 
+// Host destination of every later proof's boundary corrections (nullptr: none).
+void vzh_gpt2_set_correction_sink(void* p, uint64_t* host) { static_cast<Gpt2Prover*>(p)->set_correction_sink(host); }
+
 // Rows of the prover's weight commitment (8192 for GPT-2 small).
 size_t vzh_gpt2_prover_pcs_rows(void* p) { return static_cast<Gpt2Prover*>(p)->pcs_rows(); }
 

@@ -272,6 +272,12 @@ class Gpt2Prover {
     // those rows (chunk counters from row0 / 128).  rows = 128 * 2^k and
     // row0 a multiple of rows.  Writes code_len x 32 bytes to cvs (host).
     void commit_rows(const uint8_t pad_seed[32], size_t row0, size_t rows, uint8_t* cvs);
+    // Host destination of the boundary corrections (nullptr: none): wire w
+    // of layer l goes to host + (l * 5 + w) * rows * d (rows: the proof's t
+    // or the band's q), copied asynchronously while the later layers
+    // compute; every copy has landed when the proof call returns.  Pinned
+    // memory makes the copies overlap; host must hold layers * 5 * rows * d.
+    void set_correction_sink(uint64_t* host) { sink_ = host; }
     // Corrections x - mask of boundary wire w (0 x_in, 1 k, 2 v, 3
     // attn_block_out, 4 ffn_block_out) of layer l: rows x d u64 (the last
     // proof's rows: t, or the band's q).
@@ -302,6 +308,7 @@ class Gpt2Prover {
     uint64_t exp_pad_out_ = 0, recip_pad_out_ = 0;
     uint64_t wmat_ = 0, pads_ = 0, code_ = 0, tree_ = 0, err_ = 0, cvs_ = 0;
     size_t pcs_rows_ = kPcsRows;
+    uint64_t* sink_ = nullptr;
     std::vector<uint64_t> owned_;
     std::map<size_t, std::vector<uint64_t>> corrections_;  // per proved layer
     std::vector<std::vector<std::unique_ptr<PendingLogup>>> pending_logups_;

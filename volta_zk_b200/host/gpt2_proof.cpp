@@ -315,7 +315,16 @@ std::vector<Gpt2Prover::Slot> Gpt2Prover::enqueue_layer(size_t l, Owned& own, co
         b_.check(A.volta_cuda_subfield_corrections_device(ctx, x.id, x.off, masks, 0, corr[w], 0, t * d, 0),
                  "subfield_corrections_device");
     }
-    if (on(kSiteCorrections)) corrections_[l] = corr;
+    if (on(kSiteCorrections)) {
+        corrections_[l] = corr;
+        if (sink_) {
+            if (!b_.ext().download_async) throw AccelError("backend lacks asynchronous downloads");
+            for (int w = 0; w < 5; ++w)
+                b_.check(b_.ext().download_async(ctx, corr[w], 0, sink_ + (l * 5 + w) * t * d,
+                                                 t * d * sizeof(uint64_t)),
+                         "volta_b200_download_async");
+        }
+    }
 
     // ---- the 14 lookup instances --------------------------------------------
     std::vector<PendingSide*> sides;
@@ -668,6 +677,7 @@ Gpt2Proof Gpt2Prover::run(const uint8_t seed[32], const uint8_t mac_seed[32], co
     if (with_pcs) b_.download(tree_, (2 * code_len - 2) * 32, out.pcs_root, 32);
     uint32_t e = 0;
     b_.download(err_, 0, &e, sizeof(e));
+    if (sink_) b_.check(b_.ext().wait_downloads(ctx), "volta_b200_wait_downloads");
     const auto t_done = std::chrono::steady_clock::now();
     host_enqueue_ms_ = std::chrono::duration<double, std::milli>(t_enqueued - t_start).count();
     host_total_ms_ = std::chrono::duration<double, std::milli>(t_done - t_start).count();
